@@ -1,0 +1,135 @@
+/* h3sa — B200 (sm_100a) streaming audio-video attention: the C ABI.
+ *
+ * Plain pointers, sizes and a CUDA stream handle (cudaStream_t passed as void*); no
+ * framework types. Every entry point validates its arguments on the host, enqueues work on
+ * `stream` and returns without synchronising. Return value: H3SA_OK or an H3SA_ERR_* code;
+ * h3sa_last_error() gives a message for the calling thread's most recent failure.
+ *
+ * Device-side failures (a page index outside its pool, a bounded wait that gave up) are
+ * OR-ed into the optional `device_error` word (int32 in device memory) as H3SA_DEVERR_*
+ * bits; the caller reads it when it next synchronises.
+ *
+ * Tensor layouts (row-major, contiguous, 16-byte aligned base pointers):
+ *   packed rows  [rows, heads, head_dim]              the post-Ulysses q/k/v layout
+ *   paged pool   [heads, pool_pages * 128, head_dim]  page p of head h = rows [128p, 128p+128)
+ *   page table   int32 [table_blocks]: logical KV block b (rows [128b, 128b+128)) -> page
+ * head_dim is 128 for the attention kernels.
+ */
+#ifndef H3SA_H_
+#define H3SA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define H3SA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define H3SA_API __attribute__((visibility("default")))
+#else
+#define H3SA_API
+#endif
+
+enum {
+  H3SA_OK = 0,
+  H3SA_ERR_INVALID = 1,     /* bad shape, size, pointer or alignment */
+  H3SA_ERR_UNSUPPORTED = 2, /* valid request this build does not implement */
+  H3SA_ERR_CUDA = 3         /* a CUDA runtime/driver call failed */
+};
+
+enum {
+  H3SA_DEVERR_WAIT_TIMEOUT = 1, /* a pipeline wait gave up; outputs are invalid */
+  H3SA_DEVERR_BAD_PAGE = 2,     /* page-table entry outside the pool */
+  H3SA_DEVERR_BAD_INDEX = 4     /* row or block index outside its range */
+};
+
+/* One attention problem of a launch: queries [q_lo, q_hi) of the packed query tensor attend
+ * to logical KV rows [kv_lo, kv_hi) of the page sequence; the result goes to the same rows
+ * of the output. sparse != 0 restricts each 128-row query block to the KV blocks listed for
+ * it (flex BlockMask layout, see h3sa_attention_fwd). */
+typedef struct h3sa_problem {
+  int32_t q_lo, q_hi;
+  int32_t kv_lo, kv_hi;
+  int32_t sparse;
+  int32_t reserved[3];
+} h3sa_problem;
+
+/* A row space for the KV copy kernels: packed rows or a paged pool. */
+typedef struct h3sa_rows {
+  void* base;
+  int32_t paged;              /* 0: packed [extent, heads, head_dim]; 1: paged pool */
+  int32_t extent;             /* packed: rows; paged: pool_pages */
+  const int32_t* page_table;  /* paged only */
+  int32_t table_blocks;       /* paged only */
+  int32_t reserved;
+} h3sa_rows;
+
+H3SA_API int h3sa_abi_version(void);
+H3SA_API const char* h3sa_last_error(void);
+H3SA_API size_t h3sa_attention_smem_bytes(int fp8);
+
+/* Non-causal softmax(Q K^T * softmax_scale) V in bf16 with fp32 accumulation.
+ * query/out: packed [rows, heads, 128] bf16. key_pool/value_pool: paged [heads, pool_pages*128,
+ * 128] bf16. Up to 4 problems per launch. Block-sparse problems read kv_num_blocks
+ * [heads, q_blocks] and kv_indices [heads, q_blocks, kv_index_stride] (int32, device; each
+ * list sorted ascending, absolute logical block indices); q-block j of a problem covers query
+ * rows [q_lo + 128j, q_lo + 128j + 128). Dense-only launches pass NULL lists.
+ *
+ * Replaces: the FlashAttention-3 calls of the streaming hook and the K/V concatenation in
+ * front of them (T/streaming/attention_hook.py:77-92; F/streaming/attention_hook.py:288-316,
+ * 1068-1110), and the compiled flex_attention block-sparse call
+ * (F/inference/dynamic_block_sparse.py:127-172). */
+H3SA_API int h3sa_attention_fwd(const void* query, void* out, int32_t rows, int32_t heads,
+                       int32_t head_dim, const void* key_pool, const void* value_pool,
+                       int32_t pool_pages, const int32_t* page_table, int32_t table_blocks,
+                       const h3sa_problem* problems, int32_t num_problems, float softmax_scale,
+                       const int32_t* kv_num_blocks, const int32_t* kv_indices,
+                       int32_t q_blocks, int32_t kv_index_stride, int32_t* device_error,
+                       void* stream);
+
+/* The same attention on e4m3 query and KV pools with per-head dequantisation scales
+ * (q_scale, k_scale, v_scale: fp32 [heads], device), bf16 output: the FP8 FlashAttention-3
+ * call with q/k/v_descale (F/streaming/attention_hook.py:1081-1107). */
+H3SA_API int h3sa_attention_fwd_fp8(const void* query, void* out, int32_t rows, int32_t heads,
+                           int32_t head_dim, const void* key_pool, const void* value_pool,
+                           int32_t pool_pages, const int32_t* page_table, int32_t table_blocks,
+                           const h3sa_problem* problems, int32_t num_problems,
+                           float softmax_scale, const float* q_scale, const float* k_scale,
+                           const float* v_scale, const int32_t* kv_num_blocks,
+                           const int32_t* kv_indices, int32_t q_blocks, int32_t kv_index_stride,
+                           int32_t* device_error, void* stream);
+
+/* Row copies between packed tensors and paged pools (num_tensors pairs, same indexing):
+ * for i < count and every head, src row (src_index ? src_index[i] : src_start + i) goes to
+ * dst row (dst_index ? dst_index[i] : dst_start + i). row_bytes = head_dim * element size
+ * (a multiple of 16). Replaces the index_select / torch.cat traffic of the clean KV cache
+ * (T/streaming/cache.py:156-171 stage, 188-199 commit, 246-284 retention). */
+H3SA_API int h3sa_kv_copy_rows(const h3sa_rows* src, const h3sa_rows* dst, int32_t num_tensors,
+                      const int32_t* src_index, int32_t src_start, const int32_t* dst_index,
+                      int32_t dst_start, int32_t count, int32_t heads, int32_t row_bytes,
+                      int32_t* device_error, void* stream);
+
+/* Per-(batch, head) absmax e4m3 quantiser: x [batch, seq, heads, dim] bf16 -> y e4m3 of the
+ * same shape and scale fp32 [batch, heads], scale = max(amax / 448, 1e-12),
+ * y = RTNE(clamp(x / scale, -448, 448)). Uses a device scratch of
+ * batch * heads * ceil(seq / 256) floats taken from the stream-ordered allocator.
+ * Replaces quantize_fp8_e4m3_per_head (F/inference/fused_kernels.py:823-877). */
+H3SA_API int h3sa_quantize_fp8_per_head(const void* x, void* y, float* scale, int32_t batch,
+                               int32_t seq, int32_t heads, int32_t dim, void* stream);
+
+/* The same quantiser over logical KV rows [0, rows) of a paged bf16 pool, written to an e4m3
+ * pool through the same page table: one scale per head over the whole logical sequence, as
+ * the FP8 dynamic backend quantises the concatenated K (or V) parts
+ * (F/streaming/attention_hook.py:1081-1098). */
+H3SA_API int h3sa_quantize_fp8_pool(const void* pool, void* pool_fp8, float* scale, int32_t heads,
+                           int32_t pool_pages, const int32_t* page_table, int32_t table_blocks,
+                           int32_t rows, int32_t* device_error, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3SA_H_ */

@@ -1,0 +1,544 @@
+// Streaming chunk attention (dense / block-sparse, bf16 / e4m3) for sm_100a.
+// Kernel layout and warp roles are described in h3sa_attention.cuh.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <climits>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "h3sa_attention.cuh"
+#include "h3sa_host.h"
+
+namespace h3sa {
+
+template <bool kFp8>
+struct AttnCfg {
+  static constexpr int kElem = kFp8 ? 1 : 2;
+  static constexpr int kTileBytes = kBlockM * kHeadDim * kElem;  // 32 KB bf16, 16 KB e4m3
+  static constexpr int kAtoms = kHeadDim * kElem / 128;          // 128-byte swizzle atoms per row
+  static constexpr int kAtomBytes = kBlockM * 128;               // 16 KB
+  static constexpr int kKSteps = kFp8 ? 4 : 8;                   // MMA K steps over d (QK^T)
+  static constexpr int kKStepBytes = 32;                         // bytes of K per MMA step
+  static constexpr int kPvRowsPerStep = kFp8 ? 32 : 16;          // kv rows per PV MMA step
+  static constexpr int kPCols = kBlockN * kElem / 4;             // TMEM columns of packed P
+  static constexpr uint32_t kIdescQK = kFp8 ? idesc_e4m3(kBlockM, kBlockN, false)
+                                            : idesc_bf16(kBlockM, kBlockN, false);
+  static constexpr uint32_t kIdescPV = kFp8 ? idesc_e4m3(kBlockM, kHeadDim, true)
+                                            : idesc_bf16(kBlockM, kHeadDim, true);
+};
+
+template <bool kFp8>
+struct alignas(1024) AttnSmem {
+  uint8_t q[2][AttnCfg<kFp8>::kTileBytes];
+  uint8_t k[kKVStages][AttnCfg<kFp8>::kTileBytes];
+  uint8_t v[kKVStages][AttnCfg<kFp8>::kTileBytes];
+  uint64_t q_full;
+  uint64_t k_full[kKVStages], k_empty[kKVStages];
+  uint64_t v_full[kKVStages], v_empty[kKVStages];
+  uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int n_blocks;
+  int16_t blk[kMaxUnionBlocks];
+  uint8_t blk_mask[kMaxUnionBlocks];
+  uint8_t present[kMaxUnionBlocks];
+};
+
+template <bool kFp8>
+constexpr size_t attn_smem_bytes() {
+  return sizeof(AttnSmem<kFp8>) + 1024;  // + slack for 1024-byte alignment of the base
+}
+
+// Union of the two per-q-block KV block lists of a CTA, with a per-block tile mask
+// (bit 0: tile 0 attends to the block, bit 1: tile 1). Blocks are marked in a presence
+// map over [b_lo, b_hi) and compacted in ascending order by one warp.
+__device__ void build_union(const int* A, int na, const int* B, int nb, int b_lo, int b_hi,
+                            uint8_t* present, int16_t* blk, uint8_t* blk_mask, int* n_out,
+                            int* err, volatile int* abort_flag) {
+  const int lane = threadIdx.x & 31;
+  const int range = b_hi - b_lo;
+  if (range > kMaxUnionBlocks) {
+    if (lane == 0) {
+      if (err) atomicOr(err, kErrBadIndex);
+      *abort_flag = 1;
+      *n_out = 0;
+    }
+    return;
+  }
+  for (int i = lane; i < range; i += 32) present[i] = 0;
+  __syncwarp();
+  for (int i = lane; i < na; i += 32) {
+    const int v = __ldg(A + i) - b_lo;
+    if (v >= 0 && v < range) present[v] = 1;
+    else { if (err) atomicOr(err, kErrBadIndex); *abort_flag = 1; }
+  }
+  __syncwarp();
+  for (int i = lane; i < nb; i += 32) {
+    const int v = __ldg(B + i) - b_lo;
+    if (v >= 0 && v < range) present[v] |= 2;
+    else { if (err) atomicOr(err, kErrBadIndex); *abort_flag = 1; }
+  }
+  __syncwarp();
+  const int chunk = (range + 31) / 32;
+  const int beg = min(lane * chunk, range);
+  const int end = min(beg + chunk, range);
+  int cnt = 0;
+  for (int i = beg; i < end; ++i) cnt += present[i] ? 1 : 0;
+  int incl = cnt;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  int pos = incl - cnt;
+  for (int i = beg; i < end; ++i) {
+    if (present[i]) {
+      blk[pos] = static_cast<int16_t>(i + b_lo);
+      blk_mask[pos] = present[i];
+      ++pos;
+    }
+  }
+  if (lane == 31) *n_out = incl;
+  __syncwarp();
+}
+
+template <bool kFp8>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using Cfg = AttnCfg<kFp8>;
+  extern __shared__ uint8_t smem_raw[];
+  AttnSmem<kFp8>& sm = *reinterpret_cast<AttnSmem<kFp8>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort_flag = &sm.abort_flag;
+
+  // ---- locate this CTA's work: problem, head, pair of query tiles
+  int pi = 0;
+  while (pi + 1 < p.n_prob && static_cast<int>(blockIdx.x) >= p.prob[pi + 1].cta_begin) ++pi;
+  const AttnProblemDev pr = p.prob[pi];
+  const int local = static_cast<int>(blockIdx.x) - pr.cta_begin;
+  const int head = local / pr.pairs;
+  const int pair = local - head * pr.pairs;
+  const int n_tiles = min(2, pr.tiles - pair * 2);
+  const int q_row0 = pr.q_lo + pair * 2 * kBlockM;
+  const int b_lo = pr.kv_lo / kBlockN;
+  const int b_hi = (pr.kv_hi + kBlockN - 1) / kBlockN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&sm.q_full), 1);
+    for (int s = 0; s < kKVStages; ++s) {
+      mbar_init(smem_u32(&sm.k_full[s]), 1);
+      mbar_init(smem_u32(&sm.k_empty[s]), 1);
+      mbar_init(smem_u32(&sm.v_full[s]), 1);
+      mbar_init(smem_u32(&sm.v_empty[s]), 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(smem_u32(&sm.s_full[t]), 1);
+      mbar_init(smem_u32(&sm.p_full[t]), 128);
+      mbar_init(smem_u32(&sm.o_done[t]), 1);
+    }
+    mbar_init(smem_u32(&sm.drain), 1);
+    sm.abort_flag = 0;
+    sm.n_blocks = b_hi - b_lo;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), 512);
+    tmem_relinquish();
+  }
+  __syncthreads();
+  if (pr.sparse && warp == 2) {
+    const int qb = (q_row0 - pr.q_lo) / kBlockM;
+    const int* nums = p.kv_num_blocks + static_cast<size_t>(head) * p.q_blocks;
+    const int* A = p.kv_indices + (static_cast<size_t>(head) * p.q_blocks + qb) * p.kv_stride;
+    const int na = min(__ldg(nums + qb), p.kv_stride);
+    const int nb = (n_tiles > 1) ? min(__ldg(nums + qb + 1), p.kv_stride) : 0;
+    build_union(A, na, A + p.kv_stride, nb, b_lo, b_hi, sm.present, sm.blk, sm.blk_mask,
+                &sm.n_blocks, p.err, abort_flag);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tbase = sm.tmem_base;
+  const int nblk = sm.n_blocks;
+  const int dense_mask = (n_tiles > 1) ? 3 : 1;
+  auto block_at = [&](int i, int& b, int& m) {
+    if (pr.sparse) { b = sm.blk[i]; m = sm.blk_mask[i]; }
+    else { b = b_lo + i; m = dense_mask; }
+  };
+
+  if (warp == 0) {
+    // ================================================================ TMA producer
+    if (lane == 0 && !*abort_flag) {
+      tma_prefetch_desc(&tmQ);
+      tma_prefetch_desc(&tmK);
+      tma_prefetch_desc(&tmV);
+      const uint32_t qbar = smem_u32(&sm.q_full);
+      mbar_expect_tx(qbar, n_tiles * Cfg::kTileBytes);
+      for (int t = 0; t < n_tiles; ++t)
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_3d(smem_u32(sm.q[t]) + a * Cfg::kAtomBytes, &tmQ, qbar, a * (128 / Cfg::kElem),
+                      head, q_row0 + t * kBlockM);
+      for (int i = 0; i < nblk; ++i) {
+        const int s = i % kKVStages;
+        const uint32_t ph = (i / kKVStages) & 1;
+        int b, m;
+        block_at(i, b, m);
+        int page = (b >= 0 && b < p.table_blocks) ? __ldg(p.page_table + b) : -1;
+        if (page < 0 || page >= p.pool_pages) {
+          if (p.err) atomicOr(p.err, kErrBadPage);
+          *abort_flag = 1;
+          break;
+        }
+        if (!mbar_wait(smem_u32(&sm.k_empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        const uint32_t kb = smem_u32(&sm.k_full[s]);
+        mbar_expect_tx(kb, Cfg::kTileBytes);
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_3d(smem_u32(sm.k[s]) + a * Cfg::kAtomBytes, &tmK, kb, a * (128 / Cfg::kElem),
+                      page * kBlockN, head);
+        if (!mbar_wait(smem_u32(&sm.v_empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        const uint32_t vb = smem_u32(&sm.v_full[s]);
+        mbar_expect_tx(vb, Cfg::kTileBytes);
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_3d(smem_u32(sm.v[s]) + a * Cfg::kAtomBytes, &tmV, vb, a * (128 / Cfg::kElem),
+                      page * kBlockN, head);
+      }
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      const uint32_t tS[2] = {tbase + 0u, tbase + 128u};
+      const uint32_t tO[2] = {tbase + 256u, tbase + 384u};
+      int cnt[2] = {0, 0};       // QK MMAs issued per tile (== softmax rounds requested)
+      int pv_started[2] = {0, 0};
+      int pend = 0;              // tiles whose PV for block i-1 is still to be issued
+      bool ok = mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err);
+      tc_fence_after();
+      auto issue_pv = [&](int t, int vs) {
+        const uint32_t vaddr = smem_u32(sm.v[vs]);
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
+          const uint64_t bdesc =
+              sdesc_sw128(vaddr + kk * Cfg::kPvRowsPerStep * 128, Cfg::kAtomBytes, 1024);
+          const uint32_t a_tmem = tS[t] + 64u + kk * 8u;
+          if constexpr (kFp8)
+            mma_ts_f8(tO[t], a_tmem, bdesc, Cfg::kIdescPV, (pv_started[t] | kk) ? 1u : 0u);
+          else
+            mma_ts(tO[t], a_tmem, bdesc, Cfg::kIdescPV, (pv_started[t] | kk) ? 1u : 0u);
+        }
+        pv_started[t] = 1;
+      };
+      auto issue_qk = [&](int t, int ks) {
+        const uint32_t qaddr = smem_u32(sm.q[t]);
+        const uint32_t kaddr = smem_u32(sm.k[ks]);
+#pragma unroll
+        for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
+          const uint32_t off = (kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
+                               (kk * Cfg::kKStepBytes) % 128;
+          const uint64_t adesc = sdesc_sw128(qaddr + off, 16, 1024);
+          const uint64_t bdesc = sdesc_sw128(kaddr + off, 16, 1024);
+          if constexpr (kFp8)
+            mma_ss_f8(tS[t], adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
+          else
+            mma_ss(tS[t], adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
+        }
+      };
+      for (int i = 0; ok && i < nblk; ++i) {
+        const int s = i % kKVStages;
+        const uint32_t ph = (i / kKVStages) & 1;
+        const int ps = (i + kKVStages - 1) % kKVStages;
+        const uint32_t pph = ((i - 1) / kKVStages) & 1;
+        int b, m;
+        block_at(i, b, m);
+        if (!(ok = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err))) break;
+        if (pend) {
+          if (!(ok = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err))) break;
+        }
+        tc_fence_after();
+        for (int t = 0; t < 2 && ok; ++t) {
+          if ((pend >> t) & 1) {
+            if (!(ok = mbar_wait(smem_u32(&sm.p_full[t]), (cnt[t] - 1) & 1, abort_flag, p.err)))
+              break;
+            tc_fence_after();
+            issue_pv(t, ps);
+          }
+          if ((m >> t) & 1) {
+            issue_qk(t, s);
+            tc_commit(smem_u32(&sm.s_full[t]));
+            ++cnt[t];
+          }
+        }
+        if (!ok) break;
+        if (pend) tc_commit(smem_u32(&sm.v_empty[ps]));
+        tc_commit(smem_u32(&sm.k_empty[s]));
+        pend = m;
+      }
+      if (ok && pend) {
+        const int ps = (nblk - 1) % kKVStages;
+        const uint32_t pph = ((nblk - 1) / kKVStages) & 1;
+        ok = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
+        tc_fence_after();
+        for (int t = 0; t < 2 && ok; ++t) {
+          if ((pend >> t) & 1) {
+            if (!(ok = mbar_wait(smem_u32(&sm.p_full[t]), (cnt[t] - 1) & 1, abort_flag, p.err)))
+              break;
+            tc_fence_after();
+            issue_pv(t, ps);
+          }
+        }
+      }
+      if (ok) {
+        for (int t = 0; t < n_tiles; ++t) tc_commit(smem_u32(&sm.o_done[t]));
+      }
+      // Whatever happened, do not leave tensor-core work in flight past the teardown.
+      tc_commit(smem_u32(&sm.drain));
+      const unsigned long long t0 = global_ns();
+      while (!mbar_try_wait(smem_u32(&sm.drain), 0)) {
+        if (global_ns() - t0 > kWaitTimeoutNs) {
+          if (p.err) atomicOr(p.err, kErrWaitTimeout);
+          break;
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ================================================================ softmax / epilogue
+    const int t = (warp - 4) >> 2;
+    if (t < n_tiles) {
+      const int row = (warp & 3) * 32 + lane;
+      const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
+      const uint32_t tS = tbase + static_cast<uint32_t>(t) * 128u + lane_off;
+      const uint32_t tP = tS + 64u;
+      const uint32_t tO = tbase + 256u + static_cast<uint32_t>(t) * 128u + lane_off;
+      float scale_log2;
+      if constexpr (kFp8)
+        scale_log2 = __ldg(p.q_scale + head) * __ldg(p.k_scale + head) * p.softmax_scale_log2;
+      else
+        scale_log2 = p.scale_log2;
+      float m_used = -INFINITY;
+      float l_sum = 0.f;
+      int c = 0;
+      bool ok = true;
+      for (int i = 0; i < nblk; ++i) {
+        int b, m;
+        block_at(i, b, m);
+        if (!((m >> t) & 1)) continue;
+        if (!(ok = mbar_wait(smem_u32(&sm.s_full[t]), c & 1, abort_flag, p.err))) break;
+        tc_fence_after();
+        float s[kBlockN];
+        {
+          uint32_t r[32];
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            tmem_ld32(tS + ch * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) s[ch * 32 + j] = __uint_as_float(r[j]);
+          }
+        }
+        const int col0 = b * kBlockN;
+        const int lo = pr.kv_lo - col0;  // valid columns [lo, hi)
+        const int hi = pr.kv_hi - col0;
+        if (lo > 0 || hi < kBlockN) {
+#pragma unroll
+          for (int j = 0; j < kBlockN; ++j)
+            if (j < lo || j >= hi) s[j] = -INFINITY;
+        }
+        float mx = s[0];
+#pragma unroll
+        for (int j = 1; j < kBlockN; ++j) mx = fmaxf(mx, s[j]);
+        const float m_blk = mx * scale_log2;
+        const bool need = m_blk > m_used + 8.0f;
+        const float m_new = need ? m_blk : m_used;
+        if (c > 0 && __any_sync(0xffffffffu, need)) {
+          const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
+          l_sum *= alpha;
+          uint32_t r[32];
+#pragma unroll
+          for (int ch = 0; ch < 4; ++ch) {
+            tmem_ld32(tO + ch * 32, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
+            tmem_st32(tO + ch * 32, r);
+          }
+          tmem_wait_st();
+        }
+        m_used = m_new;
+        float sum = 0.f;
+        if constexpr (kFp8) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float p0 = fast_exp2(fmaf(s[4 * j + 0], scale_log2, -m_used));
+            const float p1 = fast_exp2(fmaf(s[4 * j + 1], scale_log2, -m_used));
+            const float p2 = fast_exp2(fmaf(s[4 * j + 2], scale_log2, -m_used));
+            const float p3 = fast_exp2(fmaf(s[4 * j + 3], scale_log2, -m_used));
+            sum += (p0 + p1) + (p2 + p3);
+            uint16_t lo16, hi16;
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo16) : "f"(p1), "f"(p0));
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi16) : "f"(p3), "f"(p2));
+            pk[j] = static_cast<uint32_t>(lo16) | (static_cast<uint32_t>(hi16) << 16);
+          }
+          tmem_st32(tP, pk);
+        } else {
+          uint32_t pk[32];
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float p0 = fast_exp2(fmaf(s[64 * half + 2 * j], scale_log2, -m_used));
+              const float p1 = fast_exp2(fmaf(s[64 * half + 2 * j + 1], scale_log2, -m_used));
+              sum += p0 + p1;
+              pk[j] = pack_bf16x2(p0, p1);
+            }
+            tmem_st32(tP + half * 32, pk);
+          }
+        }
+        l_sum += sum;
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(smem_u32(&sm.p_full[t]));
+        ++c;
+      }
+      if (ok) ok = mbar_wait(smem_u32(&sm.o_done[t]), 0, abort_flag, p.err);
+      if (ok) {
+        tc_fence_after();
+        float out_scale = 1.0f / l_sum;
+        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        const int qrow = q_row0 + t * kBlockM + row;
+        const bool valid = qrow < pr.q_hi;
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
+                             (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim;
+        uint32_t r[32];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          tmem_ld32(tO + ch * 32, r);
+          tmem_wait_ld();
+          uint32_t o[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j)
+            o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * out_scale,
+                               __uint_as_float(r[2 * j + 1]) * out_scale);
+          if (valid) {
+            uint4* d4 = reinterpret_cast<uint4*>(dst + ch * 32);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              d4[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// ------------------------------------------------------------------------ host side
+
+template <bool kFp8>
+static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
+  using Cfg = AttnCfg<kFp8>;
+  const CUtensorMapDataType dt =
+      kFp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint32_t box_inner = 128 / Cfg::kElem;  // one 128-byte swizzle atom of d
+  CUtensorMap tmQ, tmK, tmV;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim), static_cast<uint64_t>(L.heads),
+                              static_cast<uint64_t>(L.rows)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(kHeadDim) * Cfg::kElem,
+                                 static_cast<uint64_t>(L.heads) * kHeadDim * Cfg::kElem};
+    const uint32_t box[3] = {box_inner, 1, static_cast<uint32_t>(kBlockM)};
+    int rc = encode_tiled_3d(&tmQ, dt, L.query, dims, strides, box);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(kHeadDim),
+                              static_cast<uint64_t>(L.pool_pages) * kBlockN,
+                              static_cast<uint64_t>(L.heads)};
+    const uint64_t strides[2] = {
+        static_cast<uint64_t>(kHeadDim) * Cfg::kElem,
+        static_cast<uint64_t>(L.pool_pages) * kBlockN * kHeadDim * Cfg::kElem};
+    const uint32_t box[3] = {box_inner, static_cast<uint32_t>(kBlockN), 1};
+    int rc = encode_tiled_3d(&tmK, dt, L.key_pool, dims, strides, box);
+    if (rc) return rc;
+    rc = encode_tiled_3d(&tmV, dt, L.value_pool, dims, strides, box);
+    if (rc) return rc;
+  }
+  AttnParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.out = L.out;
+  prm.rows = L.rows;
+  prm.heads = L.heads;
+  prm.page_table = L.page_table;
+  prm.table_blocks = L.table_blocks;
+  prm.pool_pages = L.pool_pages;
+  prm.scale_log2 = L.softmax_scale * 1.4426950408889634f;
+  prm.softmax_scale_log2 = prm.scale_log2;
+  prm.q_scale = L.q_scale;
+  prm.k_scale = L.k_scale;
+  prm.v_scale = L.v_scale;
+  prm.kv_num_blocks = L.kv_num_blocks;
+  prm.kv_indices = L.kv_indices;
+  prm.q_blocks = L.q_blocks;
+  prm.kv_stride = L.kv_stride;
+  prm.err = L.device_error;
+  int ctas = 0;
+  int n = 0;
+  for (int i = 0; i < L.num_problems; ++i) {
+    const auto& src = L.problems[i];
+    if (src.q_hi <= src.q_lo) continue;
+    AttnProblemDev& d = prm.prob[n++];
+    d.q_lo = src.q_lo;
+    d.q_hi = src.q_hi;
+    d.kv_lo = src.kv_lo;
+    d.kv_hi = src.kv_hi;
+    d.sparse = src.sparse ? 1 : 0;
+    d.tiles = (src.q_hi - src.q_lo + kBlockM - 1) / kBlockM;
+    d.pairs = (d.tiles + 1) / 2;
+    d.cta_begin = ctas;
+    ctas += d.pairs * L.heads;
+  }
+  prm.n_prob = n;
+  if (ctas == 0) return H3SA_OK;
+  const size_t smem = attn_smem_bytes<kFp8>();
+  static std::mutex mu;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<kFp8>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(smem));
+      if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute", e);
+      configured[dev] = true;
+    }
+  }
+  attn_fwd_kernel<kFp8><<<ctas, kAttnThreads, smem, stream>>>(tmQ, tmK, tmV, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("attn_fwd_kernel launch", e);
+  return H3SA_OK;
+}
+
+int attention_launch(const AttnLaunch& L, bool fp8, cudaStream_t stream) {
+  return fp8 ? launch_attention<true>(L, stream) : launch_attention<false>(L, stream);
+}
+
+size_t attention_smem_bytes(bool fp8) {
+  return fp8 ? attn_smem_bytes<true>() : attn_smem_bytes<false>();
+}
+
+}  // namespace h3sa

@@ -1,0 +1,48 @@
+// Host-side helpers shared by the C-ABI translation units (not part of the public ABI).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "../../include/h3sa.h"
+
+namespace h3sa {
+
+// Record a message for h3sa_last_error() and return `code`.
+int set_error(int code, const char* fmt, ...);
+int set_cuda_error(const char* what, cudaError_t e);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda needed),
+// 128-byte swizzle, zero fill out of bounds.
+int encode_tiled_3d(CUtensorMap* map, CUtensorMapDataType dt, const void* base,
+                    const uint64_t dims[3], const uint64_t strides_bytes[2], const uint32_t box[3]);
+
+struct AttnLaunch {
+  const void* query;  // [rows, heads, 128] bf16 or e4m3
+  void* out;          // [rows, heads, 128] bf16
+  int rows;
+  int heads;
+  const void* key_pool;    // [heads, pool_pages * 128, 128]
+  const void* value_pool;  // [heads, pool_pages * 128, 128]
+  int pool_pages;
+  const int32_t* page_table;
+  int table_blocks;
+  const h3sa_problem* problems;
+  int num_problems;
+  float softmax_scale;
+  const float* q_scale;  // e4m3 path only, [heads]
+  const float* k_scale;
+  const float* v_scale;
+  const int32_t* kv_num_blocks;
+  const int32_t* kv_indices;
+  int q_blocks;
+  int kv_stride;
+  int32_t* device_error;
+};
+
+int attention_launch(const AttnLaunch& L, bool fp8, cudaStream_t stream);
+size_t attention_smem_bytes(bool fp8);
+
+}  // namespace h3sa

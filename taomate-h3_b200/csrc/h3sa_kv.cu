@@ -1,0 +1,333 @@
+// Paged KV cache row movement and the per-head e4m3 quantiser.
+//
+// Row copies move 16-byte chunks: consecutive threads cover one (row, head) record, then the
+// next head, then the next row, so reads from the packed [rows, heads, d] layout and writes
+// into a page's head plane are both full 128-byte lines.
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+
+#include <cstring>
+
+#include "h3sa_attention.cuh"
+#include "h3sa_host.h"
+
+namespace h3sa {
+
+struct RowsDev {
+  uint8_t* base;
+  int paged;
+  int extent;
+  const int* page_table;
+  int table_blocks;
+};
+
+struct CopyParams {
+  RowsDev src[2];
+  RowsDev dst[2];
+  int ntensors;
+  const int* src_index;
+  int src_start;
+  const int* dst_index;
+  int dst_start;
+  int count;
+  int heads;
+  int row_bytes;
+  int* err;
+};
+
+__device__ __forceinline__ uint8_t* row_address(const RowsDev& r, int row, int head, int heads,
+                                                int row_bytes) {
+  if (row < 0) return nullptr;
+  if (!r.paged) {
+    if (row >= r.extent) return nullptr;
+    return r.base + (static_cast<size_t>(row) * heads + head) * row_bytes;
+  }
+  const int blk = row >> 7;
+  if (blk >= r.table_blocks) return nullptr;
+  const int page = __ldg(r.page_table + blk);
+  if (page < 0 || page >= r.extent) return nullptr;
+  return r.base +
+         ((static_cast<size_t>(head) * r.extent + page) * kBlockN + (row & 127)) * row_bytes;
+}
+
+__global__ void __launch_bounds__(256) kv_copy_kernel(const CopyParams p) {
+  const int cpr = p.row_bytes >> 4;
+  const long long total = static_cast<long long>(p.count) * p.heads * cpr;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % cpr);
+    const long long rh = idx / cpr;
+    const int h = static_cast<int>(rh % p.heads);
+    const int i = static_cast<int>(rh / p.heads);
+    const int sr = p.src_index ? __ldg(p.src_index + i) : p.src_start + i;
+    const int dr = p.dst_index ? __ldg(p.dst_index + i) : p.dst_start + i;
+    for (int t = 0; t < p.ntensors; ++t) {
+      const uint8_t* s = row_address(p.src[t], sr, h, p.heads, p.row_bytes);
+      uint8_t* d = row_address(p.dst[t], dr, h, p.heads, p.row_bytes);
+      if (!s || !d) {
+        if (p.err) atomicOr(p.err, kErrBadIndex);
+        continue;
+      }
+      reinterpret_cast<uint4*>(d)[c] = __ldg(reinterpret_cast<const uint4*>(s) + c);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ e4m3 quantiser
+constexpr int kQuantChunkRows = 256;
+constexpr float kFp8Max = 448.0f;
+
+struct QuantSpace {
+  const __nv_bfloat16* src;
+  uint8_t* dst;
+  int paged;
+  int batch;
+  int seq;  // rows per (batch, head)
+  int heads;
+  int pool_pages;
+  const int* page_table;
+  int table_blocks;
+};
+
+// Element offset of (b, s, h, 0); -1 when a page lookup fails.
+__device__ __forceinline__ long long quant_offset(const QuantSpace& q, int b, int s, int h) {
+  if (!q.paged) return ((static_cast<long long>(b) * q.seq + s) * q.heads + h) * kHeadDim;
+  const int blk = s >> 7;
+  if (blk >= q.table_blocks) return -1;
+  const int page = __ldg(q.page_table + blk);
+  if (page < 0 || page >= q.pool_pages) return -1;
+  return ((static_cast<long long>(h) * q.pool_pages + page) * kBlockN + (s & 127)) * kHeadDim;
+}
+
+__device__ __forceinline__ float bf16_bits_abs_max8(uint4 v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  float m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m = fmaxf(m, fabsf(__uint_as_float(w[i] << 16)));
+    m = fmaxf(m, fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
+  }
+  return m;
+}
+
+// grid (batch*heads, chunks): max |x| over kQuantChunkRows rows of one (batch, head).
+__global__ void __launch_bounds__(256) quant_amax_partial_kernel(const QuantSpace q, float* partial,
+                                                                 int chunks, int* err) {
+  const int bh = blockIdx.x;
+  const int b = bh / q.heads;
+  const int h = bh - b * q.heads;
+  const int chunk = blockIdx.y;
+  const int lane16 = threadIdx.x & 15;   // 16-byte column chunk of the 256-byte row
+  const int rsub = threadIdx.x >> 4;     // 16 rows per pass
+  float m = 0.f;
+  const int row_end = min(q.seq, (chunk + 1) * kQuantChunkRows);
+  for (int s = chunk * kQuantChunkRows + rsub; s < row_end; s += 16) {
+    const long long off = quant_offset(q, b, s, h);
+    if (off < 0) {
+      if (err) atomicOr(err, kErrBadPage);
+      continue;
+    }
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(q.src + off) + lane16);
+    m = fmaxf(m, bf16_bits_abs_max8(v));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = red[0];
+    for (int i = 1; i < 8; ++i) r = fmaxf(r, red[i]);
+    partial[static_cast<size_t>(bh) * chunks + chunk] = r;
+  }
+}
+
+// grid (batch*heads): scale = max(amax / 448, 1e-12) with IEEE division.
+__global__ void __launch_bounds__(256) quant_finalize_kernel(const float* partial, int chunks,
+                                                             float* scale) {
+  float m = 0.f;
+  for (int i = threadIdx.x; i < chunks; i += blockDim.x)
+    m = fmaxf(m, partial[static_cast<size_t>(blockIdx.x) * chunks + i]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = red[0];
+    for (int i = 1; i < (blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
+    scale[blockIdx.x] = fmaxf(__fdiv_rn(r, kFp8Max), 1.0e-12f);
+  }
+}
+
+__device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s) {
+  a = fminf(fmaxf(__fdiv_rn(a, s), -kFp8Max), kFp8Max);
+  b = fminf(fmaxf(__fdiv_rn(b, s), -kFp8Max), kFp8Max);
+  c = fminf(fmaxf(__fdiv_rn(c, s), -kFp8Max), kFp8Max);
+  d = fminf(fmaxf(__fdiv_rn(d, s), -kFp8Max), kFp8Max);
+  uint16_t lo, hi;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
+  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+}
+
+// One thread per 16 input bytes (8 values) -> 8 output bytes.
+__global__ void __launch_bounds__(256) quant_apply_kernel(const QuantSpace q, const float* scale,
+                                                          int* err) {
+  const long long total = static_cast<long long>(q.batch) * q.seq * q.heads * (kHeadDim / 8);
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % (kHeadDim / 8));
+    long long r = idx / (kHeadDim / 8);
+    int h, s, b;
+    if (q.paged) {  // head-major walk keeps page reads contiguous
+      s = static_cast<int>(r % q.seq);
+      r /= q.seq;
+      h = static_cast<int>(r % q.heads);
+      b = static_cast<int>(r / q.heads);
+    } else {
+      h = static_cast<int>(r % q.heads);
+      r /= q.heads;
+      s = static_cast<int>(r % q.seq);
+      b = static_cast<int>(r / q.seq);
+    }
+    const long long off = quant_offset(q, b, s, h);
+    if (off < 0) {
+      if (err) atomicOr(err, kErrBadPage);
+      continue;
+    }
+    const float sc = __ldg(scale + b * q.heads + h);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(q.src + off) + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+    uint2 o;
+    o.x = quant4(f[0], f[1], f[2], f[3], sc);
+    o.y = quant4(f[4], f[5], f[6], f[7], sc);
+    reinterpret_cast<uint2*>(q.dst + off)[c] = o;
+  }
+}
+
+static int grid_for(long long work, int threads) {
+  long long g = (work + threads - 1) / threads;
+  const long long cap = 148LL * 16;
+  if (g > cap) g = cap;
+  return static_cast<int>(g < 1 ? 1 : g);
+}
+
+int quantize_launch(const QuantSpace& q, float* scale, float* partial, int chunks, int* err,
+                    cudaStream_t stream) {
+  quant_amax_partial_kernel<<<dim3(q.batch * q.heads, chunks), 256, 0, stream>>>(q, partial,
+                                                                                 chunks, err);
+  quant_finalize_kernel<<<q.batch * q.heads, 256, 0, stream>>>(partial, chunks, scale);
+  const long long work = static_cast<long long>(q.batch) * q.seq * q.heads * (kHeadDim / 8);
+  quant_apply_kernel<<<grid_for(work, 256), 256, 0, stream>>>(q, scale, err);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("fp8 quantiser launch", e);
+  return H3SA_OK;
+}
+
+static int quantize_with_scratch(const QuantSpace& q, float* scale, int* err,
+                                 cudaStream_t stream) {
+  const int chunks = (q.seq + kQuantChunkRows - 1) / kQuantChunkRows;
+  const size_t bytes = static_cast<size_t>(q.batch) * q.heads * chunks * sizeof(float);
+  void* partial = nullptr;
+  cudaError_t e = cudaMallocAsync(&partial, bytes, stream);
+  if (e != cudaSuccess) return set_cuda_error("cudaMallocAsync(fp8 amax scratch)", e);
+  int rc = quantize_launch(q, scale, static_cast<float*>(partial), chunks, err, stream);
+  e = cudaFreeAsync(partial, stream);
+  if (rc == H3SA_OK && e != cudaSuccess) return set_cuda_error("cudaFreeAsync", e);
+  return rc;
+}
+
+}  // namespace h3sa
+
+using namespace h3sa;
+
+extern "C" {
+
+int h3sa_kv_copy_rows(const h3sa_rows* src, const h3sa_rows* dst, int32_t num_tensors,
+                      const int32_t* src_index, int32_t src_start, const int32_t* dst_index,
+                      int32_t dst_start, int32_t count, int32_t heads, int32_t row_bytes,
+                      int32_t* device_error, void* stream) {
+  if (num_tensors < 1 || num_tensors > 2 || !src || !dst)
+    return set_error(H3SA_ERR_INVALID, "kv_copy_rows: 1 or 2 tensor pairs, got %d", num_tensors);
+  if (count < 0 || heads <= 0 || row_bytes <= 0 || (row_bytes & 15))
+    return set_error(H3SA_ERR_INVALID, "kv_copy_rows: count=%d heads=%d row_bytes=%d", count,
+                     heads, row_bytes);
+  if (count == 0) return H3SA_OK;
+  CopyParams p;
+  memset(&p, 0, sizeof(p));
+  for (int t = 0; t < num_tensors; ++t) {
+    const h3sa_rows* rs[2] = {&src[t], &dst[t]};
+    RowsDev* rd[2] = {&p.src[t], &p.dst[t]};
+    for (int k = 0; k < 2; ++k) {
+      if (!rs[k]->base || (reinterpret_cast<uintptr_t>(rs[k]->base) & 15))
+        return set_error(H3SA_ERR_INVALID, "kv_copy_rows: null or unaligned base");
+      if (rs[k]->extent <= 0 || (rs[k]->paged && (!rs[k]->page_table || rs[k]->table_blocks <= 0)))
+        return set_error(H3SA_ERR_INVALID, "kv_copy_rows: bad row space");
+      rd[k]->base = static_cast<uint8_t*>(rs[k]->base);
+      rd[k]->paged = rs[k]->paged ? 1 : 0;
+      rd[k]->extent = rs[k]->extent;
+      rd[k]->page_table = rs[k]->page_table;
+      rd[k]->table_blocks = rs[k]->table_blocks;
+    }
+  }
+  p.ntensors = num_tensors;
+  p.src_index = src_index;
+  p.src_start = src_start;
+  p.dst_index = dst_index;
+  p.dst_start = dst_start;
+  p.count = count;
+  p.heads = heads;
+  p.row_bytes = row_bytes;
+  p.err = device_error;
+  const long long work = static_cast<long long>(count) * heads * (row_bytes / 16);
+  kv_copy_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("kv_copy_kernel launch", e);
+  return H3SA_OK;
+}
+
+int h3sa_quantize_fp8_per_head(const void* x, void* y, float* scale, int32_t batch,
+                               int32_t seq, int32_t heads, int32_t dim, void* stream) {
+  if (dim != kHeadDim)
+    return set_error(H3SA_ERR_UNSUPPORTED, "quantize_fp8_per_head: dim must be 128, got %d", dim);
+  if (batch <= 0 || seq <= 0 || heads <= 0 || !x || !y || !scale)
+    return set_error(H3SA_ERR_INVALID, "quantize_fp8_per_head: invalid arguments");
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
+    return set_error(H3SA_ERR_INVALID, "quantize_fp8_per_head: tensors must be 16-byte aligned");
+  QuantSpace q{};
+  q.src = static_cast<const __nv_bfloat16*>(x);
+  q.dst = static_cast<uint8_t*>(y);
+  q.paged = 0;
+  q.batch = batch;
+  q.seq = seq;
+  q.heads = heads;
+  return quantize_with_scratch(q, scale, nullptr, static_cast<cudaStream_t>(stream));
+}
+
+int h3sa_quantize_fp8_pool(const void* pool, void* pool_fp8, float* scale, int32_t heads,
+                           int32_t pool_pages, const int32_t* page_table, int32_t table_blocks,
+                           int32_t rows, int32_t* device_error, void* stream) {
+  if (heads <= 0 || pool_pages <= 0 || rows <= 0 || !pool || !pool_fp8 || !scale || !page_table ||
+      table_blocks <= 0 || static_cast<long long>(rows) > static_cast<long long>(table_blocks) * 128)
+    return set_error(H3SA_ERR_INVALID, "quantize_fp8_pool: invalid arguments");
+  QuantSpace q{};
+  q.src = static_cast<const __nv_bfloat16*>(pool);
+  q.dst = static_cast<uint8_t*>(pool_fp8);
+  q.paged = 1;
+  q.batch = 1;
+  q.seq = rows;
+  q.heads = heads;
+  q.pool_pages = pool_pages;
+  q.page_table = page_table;
+  q.table_blocks = table_blocks;
+  return quantize_with_scratch(q, scale, device_error, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

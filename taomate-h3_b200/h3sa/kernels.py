@@ -1,0 +1,198 @@
+"""Tensor-level wrappers over the C ABI: attention, KV row copies, e4m3 quantisation.
+
+Shapes follow the reference's post-Ulysses layout: packed rows ``[rows, heads, 128]``.
+KV pools are head-major and paged: ``[heads, pages * 128, 128]``; a page table (int32,
+device) maps logical 128-row blocks to pages.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Sequence
+
+import torch
+
+from . import _lib
+from ._lib import Problem, Rows, call, ptr, stream_handle
+
+PAGE_ROWS = 128
+HEAD_DIM = 128
+
+
+@dataclass(frozen=True)
+class AttentionProblem:
+    """Queries ``[q_lo, q_hi)`` attend to logical KV rows ``[kv_lo, kv_hi)``."""
+
+    q_lo: int
+    q_hi: int
+    kv_lo: int
+    kv_hi: int
+    sparse: bool = False
+
+
+def _problems(problems: Sequence[AttentionProblem]) -> ctypes.Array:
+    if not 1 <= len(problems) <= _lib.MAX_PROBLEMS:
+        raise ValueError(f"1..{_lib.MAX_PROBLEMS} attention problems per launch")
+    arr = (Problem * len(problems))()
+    for dst, src in zip(arr, problems):
+        dst.q_lo, dst.q_hi = int(src.q_lo), int(src.q_hi)
+        dst.kv_lo, dst.kv_hi = int(src.kv_lo), int(src.kv_hi)
+        dst.sparse = 1 if src.sparse else 0
+    return arr
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("h3sa kernels require CUDA tensors")
+        if t is not None and not t.is_contiguous():
+            raise RuntimeError("h3sa kernels require contiguous tensors")
+
+
+def attention_fwd(
+    query: torch.Tensor,
+    out: torch.Tensor,
+    key_pool: torch.Tensor,
+    value_pool: torch.Tensor,
+    page_table: torch.Tensor,
+    problems: Sequence[AttentionProblem],
+    softmax_scale: float,
+    *,
+    kv_num_blocks: torch.Tensor | None = None,
+    kv_indices: torch.Tensor | None = None,
+    q_scale: torch.Tensor | None = None,
+    k_scale: torch.Tensor | None = None,
+    v_scale: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> torch.Tensor:
+    """Launch the sm_100a attention kernel (bf16, or e4m3 when scales are given)."""
+
+    _require_cuda(query, out, key_pool, value_pool, page_table, kv_num_blocks, kv_indices)
+    rows, heads, head_dim = (int(s) for s in query.shape)
+    if out.shape != query.shape or out.dtype != torch.bfloat16:
+        raise RuntimeError("attention output must be bf16 with the query's shape")
+    if key_pool.shape != value_pool.shape or key_pool.ndim != 3 or key_pool.shape[0] != heads:
+        raise RuntimeError("KV pools must be [heads, pages*128, head_dim] with matching shapes")
+    if page_table.dtype != torch.int32:
+        raise RuntimeError("page table must be int32")
+    pool_pages = int(key_pool.shape[1]) // PAGE_ROWS
+    q_blocks = stride = 0
+    if kv_num_blocks is not None:
+        if kv_indices is None or kv_num_blocks.dtype != torch.int32 or kv_indices.dtype != torch.int32:
+            raise RuntimeError("block lists must be int32 kv_num_blocks and kv_indices")
+        q_blocks = int(kv_num_blocks.shape[-1])
+        stride = int(kv_indices.shape[-1])
+    probs = _problems(problems)
+    fp8 = q_scale is not None
+    common = (
+        ptr(query), ptr(out), rows, heads, head_dim, ptr(key_pool), ptr(value_pool), pool_pages,
+        ptr(page_table), int(page_table.numel()), probs, len(problems), float(softmax_scale),
+    )
+    tail = (ptr(kv_num_blocks), ptr(kv_indices), q_blocks, stride, ptr(device_error),
+            stream_handle(stream))
+    if fp8:
+        if query.dtype != torch.float8_e4m3fn or key_pool.dtype != torch.float8_e4m3fn:
+            raise RuntimeError("fp8 attention takes e4m3 query and KV pools")
+        _require_cuda(q_scale, k_scale, v_scale)
+        call("h3sa_attention_fwd_fp8", *common, ptr(q_scale), ptr(k_scale), ptr(v_scale), *tail)
+    else:
+        if query.dtype != torch.bfloat16 or key_pool.dtype != torch.bfloat16:
+            raise RuntimeError("attention takes bf16 query and KV pools")
+        call("h3sa_attention_fwd", *common, *tail)
+    return out
+
+
+def _rows(t: torch.Tensor, page_table: torch.Tensor | None) -> Rows:
+    r = Rows()
+    r.base = ptr(t)
+    if page_table is None:
+        r.paged = 0
+        r.extent = int(t.shape[0])
+        r.page_table = None
+        r.table_blocks = 0
+    else:
+        r.paged = 1
+        r.extent = int(t.shape[1]) // PAGE_ROWS
+        r.page_table = ptr(page_table)
+        r.table_blocks = int(page_table.numel())
+    return r
+
+
+def kv_copy_rows(
+    src: Sequence[torch.Tensor],
+    dst: Sequence[torch.Tensor],
+    *,
+    count: int,
+    src_table: torch.Tensor | None = None,
+    dst_table: torch.Tensor | None = None,
+    src_index: torch.Tensor | None = None,
+    src_start: int = 0,
+    dst_index: torch.Tensor | None = None,
+    dst_start: int = 0,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """Copy ``count`` rows (all heads) from each src tensor to the matching dst tensor.
+
+    A tensor is paged (``[heads, pages*128, d]``) when its side has a page table, else
+    packed (``[rows, heads, d]``). Row i goes from ``src_index[i]`` (or ``src_start + i``)
+    to ``dst_index[i]`` (or ``dst_start + i``).
+    """
+
+    if len(src) != len(dst) or not 1 <= len(src) <= 2:
+        raise ValueError("one or two src/dst tensor pairs")
+    _require_cuda(*src, *dst, src_table, dst_table, src_index, dst_index)
+    if count == 0:
+        return
+    heads = int(src[0].shape[0] if src_table is not None else src[0].shape[1])
+    row_bytes = int(src[0].shape[-1]) * src[0].element_size()
+    s_arr = (Rows * len(src))(*[_rows(t, src_table) for t in src])
+    d_arr = (Rows * len(dst))(*[_rows(t, dst_table) for t in dst])
+    for idx in (src_index, dst_index):
+        if idx is not None and idx.dtype != torch.int32:
+            raise RuntimeError("row indices must be int32")
+    call(
+        "h3sa_kv_copy_rows", s_arr, d_arr, len(src), ptr(src_index), int(src_start),
+        ptr(dst_index), int(dst_start), int(count), heads, row_bytes, ptr(device_error),
+        stream_handle(stream),
+    )
+
+
+def quantize_fp8_e4m3_per_head(value: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """``[B, S, H, D]`` bf16 -> (e4m3 of the same shape, fp32 scales ``[B, H]``).
+
+    Drop-in for ``quantize_fp8_e4m3_per_head`` (F/inference/fused_kernels.py:823-877):
+    scale = max(amax over (S, D) / 448, 1e-12); q = RTNE(clamp(x / scale, +-448)).
+    """
+
+    if value.ndim != 4 or value.dtype != torch.bfloat16:
+        raise ValueError("quantize_fp8_e4m3_per_head expects [B, S, H, D] bf16")
+    _require_cuda(value)
+    x = value.contiguous()
+    b, s, h, d = (int(v) for v in x.shape)
+    out = torch.empty_like(x, dtype=torch.float8_e4m3fn)
+    scale = torch.empty((b, h), dtype=torch.float32, device=x.device)
+    call("h3sa_quantize_fp8_per_head", ptr(x), ptr(out), ptr(scale), b, s, h, d,
+         stream_handle(None))
+    return out, scale
+
+
+def quantize_fp8_pool(
+    pool: torch.Tensor,
+    pool_fp8: torch.Tensor,
+    scale: torch.Tensor,
+    page_table: torch.Tensor,
+    rows: int,
+    *,
+    device_error: torch.Tensor | None = None,
+) -> None:
+    """Per-head e4m3 quantisation of logical rows ``[0, rows)`` of a paged bf16 pool."""
+
+    _require_cuda(pool, pool_fp8, scale, page_table)
+    heads = int(pool.shape[0])
+    pages = int(pool.shape[1]) // PAGE_ROWS
+    call("h3sa_quantize_fp8_pool", ptr(pool), ptr(pool_fp8), ptr(scale), heads, pages,
+         ptr(page_table), int(page_table.numel()), int(rows), ptr(device_error),
+         stream_handle(None))
