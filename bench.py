@@ -1,0 +1,480 @@
+#!/usr/bin/env python
+"""Benchmark: 768p streaming chunk attention (TaoMate-H3 hot path) on B200.
+
+One step = one streaming-hook layer call of the 768p chunk on this rank: (SP > 1) pack the
+local merged QKV shard, NCCL all-to-all seq->heads, unpack; write the current chunk's K/V
+rows into the paged cache after the 16384-row history; attention of the 12509 media queries
+over [history | current] (plus the pad document over itself); (SP > 1) all-to-all of O back
+and unpack. Ulysses SP = number of GPUs, heads 24 / SP per GPU.
+
+Prints one JSON line (rank 0). ``value`` = total attention TFLOP/s of the whole job
+(4 * Nq * Nk * d * H per step / max-over-ranks device time). ``e2e`` repeats the step
+through the public API with pinned host inputs and outputs copied inside the timed region.
+``--impl reference`` times the reference's CPU attention (its PyTorch path restated in
+oracle/) on this host's cores on a bounded query sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "taomate-h3_b200"))
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+CFG = {
+    "heads": 24,
+    "head_dim": 128,
+    "video": 12384,   # 3 latent frames x 48 x 86
+    "audio": 125,
+    "history": 16384,
+    "align": 64,      # packed-sequence alignment (T/model/architecture.py:12)
+}
+METRIC = "chunk attention TFLOP/s (768p, Ulysses SP=N, bf16, 16k KV cache)"
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"bf16": float(data["bf16_tflops"]), "bf16_sustained": float(data["bf16_tflops_sustained"]),
+                "hbm": float(data["hbm_gbs"]), "source": "measured"}
+    return {"bf16": 1590.0, "bf16_sustained": 1400.0, "hbm": 6650.0, "source": "fallback"}
+
+
+def _ncu_traffic() -> float | None:
+    """DRAM bytes per attention launch from the committed ncu summary, if present."""
+
+    path = ROOT / "profiles" / "attention_768p_sp1_ncu.md"
+    if not path.exists():
+        return None
+    for line in path.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc: subprocess.Popen | None = None
+
+    def __enter__(self) -> "ClockSampler":
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc: object) -> None:
+        self.lines: list[str] = []
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def _dist() -> tuple[int, int, int]:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not torch.distributed.is_initialized():
+        import datetime
+
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def _geometry(world: int) -> dict:
+    nq = CFG["video"] + CFG["audio"]
+    align = CFG["align"] * world // _gcd(CFG["align"], world)
+    rows = (nq + align - 1) // align * align
+    return {"nq": nq, "rows": rows, "pad": rows - nq, "tokens": rows // world,
+            "heads_local": CFG["heads"] // world, "nk": CFG["history"] + nq}
+
+
+def _gcd(a: int, b: int) -> int:
+    while b:
+        a, b = b, a % b
+    return a
+
+
+def _cpu_baseline(seconds: float = 12.0) -> dict:
+    """Oracle (reference CPU attention math) on a bounded query sample, all host threads."""
+
+    from oracle.attention import attention_flops, time_cpu_attention
+
+    threads = len(os.sched_getaffinity(0))
+    g = torch.Generator().manual_seed(7)
+    nk = CFG["history"] + CFG["video"] + CFG["audio"]
+    heads, d = CFG["heads"], CFG["head_dim"]
+    k = torch.randn(nk, heads, d, generator=g)
+    v = torch.randn(nk, heads, d, generator=g)
+    nq = 64
+    total_t = total_f = 0.0
+    calls = 0
+    while total_t < seconds and calls < 64:
+        q = torch.randn(nq, heads, d, generator=g)
+        t = time_cpu_attention(q, k, v, d ** -0.5, threads)
+        total_t += t
+        total_f += attention_flops(nq, nk, heads, d)
+        calls += 1
+        if t < 0.5 and nq < 4096:
+            nq *= 2
+    return {"value": total_f / total_t / 1e12, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+            "sample": f"{calls} calls, up to {nq} query rows x {heads} heads x {nk} keys, fp32 "
+                      f"torch CPU (oracle.attention.sdpa_from_kv_parts), {total_t:.1f} s"}
+
+
+def run_reference(args: argparse.Namespace) -> None:
+    world, rank, _ = (int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0)
+    if rank != 0:
+        return
+    from oracle.attention import attention_flops, sdpa_from_kv_parts
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    geo = _geometry(world)
+    heads, d, nk = CFG["heads"], CFG["head_dim"], geo["nk"]
+    k = torch.randn(nk, heads, d, generator=g)
+    v = torch.randn(nk, heads, d, generator=g)
+    sample_q = 256
+    q = torch.randn(sample_q, heads, d, generator=g)
+    for _ in range(args.warmup):
+        sdpa_from_kv_parts(q, [(k, v)], d ** -0.5)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        sdpa_from_kv_parts(q, [(k, v)], d ** -0.5)
+        times.append(time.perf_counter() - t0)
+    flops = attention_flops(sample_q, nk, heads, d)
+    value = flops * len(times) / sum(times) / 1e12
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "768p chunk attention, reference CPU path on a bounded sample",
+                   "heads": heads, "head_dim": d, "queries": geo["nq"], "keys": nk,
+                   "sample_queries_per_step": sample_q},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample_q} query rows x {heads} heads x {nk} keys per step, "
+                                   "fp32 torch CPU (oracle restatement of the reference "
+                                   "_sdpa_from_kv_parts; FlashAttention-3 is sm_90a-only)"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+class Step:
+    """Device buffers and launches of one benchmark step on this rank."""
+
+    def __init__(self, world: int, rank: int, device: torch.device) -> None:
+        import h3sa
+        from h3sa.kernels import PAGE_ROWS
+
+        self.h3sa = h3sa
+        self.world, self.rank, self.device = world, rank, device
+        geo = _geometry(world)
+        self.geo = geo
+        heads, d = CFG["heads"], CFG["head_dim"]
+        hl = geo["heads_local"]
+        self.hl = hl
+        g = torch.Generator(device=device).manual_seed(1000 + rank)
+        # this rank's post-prologue merged QKV shard [T, 3*H*d] (q, k RMS-normalised ~ N(0,1))
+        self.merged = torch.randn(geo["tokens"], 3 * heads * d, device=device, generator=g).to(torch.bfloat16)
+        nh = CFG["history"]
+        self.n_hist = nh
+        total_rows = nh + geo["rows"]
+        pages = (total_rows + PAGE_ROWS - 1) // PAGE_ROWS
+        self.table = torch.arange(pages, dtype=torch.int32, device=device)
+        self.kpool = torch.zeros(hl, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=device)
+        self.vpool = torch.zeros_like(self.kpool)
+        hist = torch.randn(nh, hl, d, device=device, generator=g).to(torch.bfloat16)
+        h3sa.kv_copy_rows([hist, hist], [self.kpool, self.vpool], count=nh, dst_table=self.table)
+        rows, tokens = geo["rows"], geo["tokens"]
+        if world > 1:
+            self.send = torch.empty(world, 3, tokens, hl, d, dtype=torch.bfloat16, device=device)
+            self.recv = torch.empty_like(self.send)
+            self.qkv = torch.empty(3, rows, hl, d, dtype=torch.bfloat16, device=device)
+            self.orecv = torch.empty(world, tokens, hl, d, dtype=torch.bfloat16, device=device)
+            self.final = torch.empty(tokens, heads, d, dtype=torch.bfloat16, device=device)
+        else:
+            self.qkv = self.merged.view(rows, 3, heads, d).permute(1, 0, 2, 3).contiguous()
+        self.out = torch.empty(rows, hl, d, dtype=torch.bfloat16, device=device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        P = h3sa.AttentionProblem
+        nq, pad = geo["nq"], geo["pad"]
+        self.problems = [P(0, nq, 0, nh + nq)]
+        if pad:
+            self.problems.append(P(nq, rows, nh + nq, nh + rows))
+        self.scale = d ** -0.5
+        self.flops = 4.0 * nq * (nh + nq) * d * hl  # this rank's algorithmic FLOPs
+        self.launches_per_step = 2 + (4 if world > 1 else 0)
+
+    def run(self, attn_events: tuple[torch.cuda.Event, torch.cuda.Event] | None = None,
+            merged: torch.Tensor | None = None) -> torch.Tensor:
+        from h3sa.ulysses import pack_qkv_send, unpack_o_recv, unpack_qkv_recv
+
+        h3sa, geo, hl = self.h3sa, self.geo, self.hl
+        d, heads = CFG["head_dim"], CFG["heads"]
+        src = self.merged if merged is None else merged
+        if self.world > 1:
+            pack_qkv_send(src, self.send, world=self.world, num_heads=heads, head_dim=d)
+            torch.distributed.all_to_all_single(self.recv, self.send)
+            unpack_qkv_recv(self.recv, self.qkv, world=self.world, tokens=geo["tokens"],
+                            local_heads=hl, head_dim=d)
+        elif merged is not None:
+            self.qkv.copy_(merged.view(geo["rows"], 3, heads, d).permute(1, 0, 2, 3))
+        q, k, v = self.qkv[0], self.qkv[1], self.qkv[2]
+        # current chunk's K/V rows (media + pad document) after the history
+        h3sa.kv_copy_rows([k, v], [self.kpool, self.vpool], count=geo["rows"], dst_table=self.table,
+                          dst_start=self.n_hist, device_error=self.err)
+        if attn_events is not None:
+            attn_events[0].record()
+        h3sa.attention_fwd(q, self.out, self.kpool, self.vpool, self.table, self.problems,
+                           self.scale, device_error=self.err)
+        if attn_events is not None:
+            attn_events[1].record()
+        if self.world > 1:
+            torch.distributed.all_to_all_single(self.orecv, self.out)
+            unpack_o_recv(self.orecv, self.final, world=self.world, tokens=geo["tokens"],
+                          local_heads=hl, head_dim=d)
+            return self.final
+        return self.out
+
+
+def _max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+
+def _comparator_sdpa(step: Step, iters: int = 5) -> dict:
+    """The reference FL2VA `sdpa` backend on this GPU: torch.cat of the K/V parts then
+    torch SDPA (F/streaming/attention_hook.py:288-316), same shapes, one rank."""
+
+    geo, hl, d = step.geo, step.hl, CFG["head_dim"]
+    nh, nq = step.n_hist, geo["nq"]
+    q = step.qkv[0][:nq]
+    hist_k = step.kpool[:, :nh].transpose(0, 1).contiguous()
+    hist_v = step.vpool[:, :nh].transpose(0, 1).contiguous()
+    cur_k, cur_v = step.qkv[1][:nq], step.qkv[2][:nq]
+
+    def call() -> torch.Tensor:
+        key = torch.cat((hist_k, cur_k), dim=0)
+        value = torch.cat((hist_v, cur_v), dim=0)
+        out = torch.nn.functional.scaled_dot_product_attention(
+            q.transpose(0, 1).unsqueeze(0), key.transpose(0, 1).unsqueeze(0),
+            value.transpose(0, 1).unsqueeze(0), dropout_p=0.0, is_causal=False, scale=step.scale)
+        return out.squeeze(0).transpose(0, 1)
+
+    for _ in range(2):
+        call()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for _ in range(iters):
+        a.record()
+        call()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return {"impl": "torch SDPA on this GPU via the reference's sdpa-backend call pattern "
+                    "(cat K/V parts + F.scaled_dot_product_attention)",
+            "ms_p50": statistics.median(times)}
+
+
+def run_h3sa(args: argparse.Namespace) -> None:
+    world, rank, local = _dist()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    step = Step(world, rank, device)
+    peaks = _peaks()
+
+    for _ in range(args.warmup):
+        step.run()
+    _barrier(world)
+    attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+    step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        _barrier(world)
+        start.record()
+        for i in range(args.steps):
+            step_ev[i][0].record()
+            step.run(attn_ev[i])
+            step_ev[i][1].record()
+        stop.record()
+        _barrier(world)
+    total_ms = _max_over_ranks(start.elapsed_time(stop), world)
+    attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
+    step_ms = [a.elapsed_time(b) for a, b in step_ev]
+    attn_avg = _max_over_ranks(sum(attn_ms) / len(attn_ms), world)
+    p50 = _max_over_ranks(statistics.median(step_ms), world)
+    p90 = _max_over_ranks(sorted(step_ms)[int(0.9 * (len(step_ms) - 1))], world)
+    err = int(step.err.item())
+
+    # e2e: public API with pinned host input / output each step
+    e2e = None
+    if not args.no_e2e:
+        host_in = step.merged.cpu().pin_memory()
+        dev_in = torch.empty_like(step.merged)
+        out_shape = step.final.shape if world > 1 else step.out.shape
+        host_out = torch.empty(out_shape, dtype=torch.bfloat16).pin_memory()
+        for _ in range(2):
+            dev_in.copy_(host_in, non_blocking=True)
+            host_out.copy_(step.run(merged=dev_in), non_blocking=True)
+        _barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            dev_in.copy_(host_in, non_blocking=True)
+            host_out.copy_(step.run(merged=dev_in), non_blocking=True)
+        b.record()
+        _barrier(world)
+        e2e_ms = _max_over_ranks(a.elapsed_time(b), world) / args.steps
+        total_flops = 4.0 * step.geo["nq"] * step.geo["nk"] * CFG["head_dim"] * CFG["heads"]
+        e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+               "ms_per_step": e2e_ms, "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+               "d2h_bytes_per_step": host_out.numel() * host_out.element_size(),
+               "api": "h3sa.ulysses + h3sa.kv_copy_rows + h3sa.attention_fwd (C ABI via ctypes)"}
+
+    extra = {}
+    if rank == 0 and world == 1 and not args.no_comparator:
+        extra["comparator"] = _comparator_sdpa(step)
+        extra["comparator"]["speedup_p50"] = extra["comparator"]["ms_p50"] / attn_avg
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = _cpu_baseline()
+
+    if rank != 0:
+        return
+    geo = step.geo
+    total_flops = 4.0 * geo["nq"] * geo["nk"] * CFG["head_dim"] * CFG["heads"]
+    value = total_flops * args.steps / (total_ms * 1e-3) / 1e12
+    achieved = step.flops / (attn_avg * 1e-3) / 1e12
+    traffic = _ncu_traffic()
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": total_ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {
+            "workload": "768p chunk: 12384 video + 125 audio queries x [16384 history + 12509 "
+                        "current] keys, H=24, d=128, dense non-causal",
+            "ulysses_sp": world, "heads_per_gpu": step.hl, "packed_rows": geo["rows"],
+            "pad_rows": geo["pad"], "parallelism": f"sp{world}",
+            "l2": "inputs larger than L2 (Q 77 MB + K/V pool 355 MB at SP=1)",
+        },
+        "per_gpu_tflops": value / world,
+        "tokens_per_s": geo["nq"] * args.steps / (total_ms * 1e-3),
+        "latency_ms": {"p50": p50, "p90": p90, "attention_kernel_avg": attn_avg},
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"],
+                     "unit": "TFLOP/s", "frac": achieved / peaks["bf16"],
+                     "frac_of_sustained": achieved / peaks["bf16_sustained"],
+                     "peak_source": peaks["source"] + " bf16 burst (MEASURED_PEAKS.json)",
+                     "traffic": traffic},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": step.launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+        "device_error": err,
+        **extra,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["h3sa", "reference"], default="h3sa")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-comparator", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "h3sa":
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_h3sa(args)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

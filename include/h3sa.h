@@ -128,6 +128,16 @@ H3SA_API int h3sa_quantize_fp8_pool(const void* pool, void* pool_fp8, float* sca
                            int32_t pool_pages, const int32_t* page_table, int32_t table_blocks,
                            int32_t rows, int32_t* device_error, void* stream);
 
+/* Generic layout permute of 16-byte-aligned records: for every index (i0, i1, i2, i3) of
+ * the row-major space dims[4], copy row_bytes from src + sum(i_k * src_strides[k]) to
+ * dst + sum(i_k * dst_strides[k]) (strides in bytes, multiples of 16). Serves the Ulysses
+ * send/receive layouts: [T, 3, W, H/W, d] -> [W, 3, T, H/W, d] before the QKV all-to-all and
+ * the inverse moves around the output all-to-all (T/distributed/ulysses.py:10-55, 103-132;
+ * F/distributed/ulysses_layout.py:8-60). */
+H3SA_API int h3sa_permute_rows(const void* src, void* dst, const int64_t* dims,
+                               const int64_t* src_strides, const int64_t* dst_strides,
+                               int32_t row_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

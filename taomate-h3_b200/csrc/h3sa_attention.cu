@@ -174,8 +174,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     else { b = b_lo + i; m = dense_mask; }
   };
 
+  // Register split (every warp of a warpgroup executes the same setmaxnreg at the top of its
+  // role): the producer/MMA warpgroup gives registers to the two softmax warpgroups.
   if (warp == 0) {
     // ================================================================ TMA producer
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     if (lane == 0 && !*abort_flag) {
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -213,29 +216,29 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == 1) {
     // ================================================================ MMA issuer
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     if (lane == 0) {
-      const uint32_t tS[2] = {tbase + 0u, tbase + 128u};
-      const uint32_t tO[2] = {tbase + 256u, tbase + 384u};
-      int cnt[2] = {0, 0};       // QK MMAs issued per tile (== softmax rounds requested)
-      int pv_started[2] = {0, 0};
-      int pend = 0;              // tiles whose PV for block i-1 is still to be issued
+      const uint32_t tS0 = tbase + 0u, tS1 = tbase + 128u;
+      const uint32_t tO0 = tbase + 256u, tO1 = tbase + 384u;
+      int cnt0 = 0, cnt1 = 0;       // QK MMAs issued per tile (softmax rounds requested)
+      int pv0 = 0, pv1 = 0;         // PV issued at least once per tile
+      int pend = 0;                 // tiles whose PV for block i-1 is still to be issued
       bool ok = mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err);
       tc_fence_after();
-      auto issue_pv = [&](int t, int vs) {
+      auto issue_pv = [&](uint32_t tS, uint32_t tO, int started, int vs) {
         const uint32_t vaddr = smem_u32(sm.v[vs]);
 #pragma unroll
         for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
           const uint64_t bdesc =
               sdesc_sw128(vaddr + kk * Cfg::kPvRowsPerStep * 128, Cfg::kAtomBytes, 1024);
-          const uint32_t a_tmem = tS[t] + 64u + kk * 8u;
+          const uint32_t a_tmem = tS + 64u + kk * 8u;
           if constexpr (kFp8)
-            mma_ts_f8(tO[t], a_tmem, bdesc, Cfg::kIdescPV, (pv_started[t] | kk) ? 1u : 0u);
+            mma_ts_f8(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
           else
-            mma_ts(tO[t], a_tmem, bdesc, Cfg::kIdescPV, (pv_started[t] | kk) ? 1u : 0u);
+            mma_ts(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
         }
-        pv_started[t] = 1;
       };
-      auto issue_qk = [&](int t, int ks) {
+      auto issue_qk = [&](uint32_t tS, int t, int ks) {
         const uint32_t qaddr = smem_u32(sm.q[t]);
         const uint32_t kaddr = smem_u32(sm.k[ks]);
 #pragma unroll
@@ -245,57 +248,58 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const uint64_t adesc = sdesc_sw128(qaddr + off, 16, 1024);
           const uint64_t bdesc = sdesc_sw128(kaddr + off, 16, 1024);
           if constexpr (kFp8)
-            mma_ss_f8(tS[t], adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
+            mma_ss_f8(tS, adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
           else
-            mma_ss(tS[t], adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
+            mma_ss(tS, adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
         }
       };
-      for (int i = 0; ok && i < nblk; ++i) {
+      for (int i = 0; ok && i <= nblk; ++i) {
+        const bool last = (i == nblk);
         const int s = i % kKVStages;
         const uint32_t ph = (i / kKVStages) & 1;
         const int ps = (i + kKVStages - 1) % kKVStages;
         const uint32_t pph = ((i - 1) / kKVStages) & 1;
-        int b, m;
-        block_at(i, b, m);
-        if (!(ok = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err))) break;
-        if (pend) {
-          if (!(ok = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err))) break;
+        int b = 0, m = 0;
+        if (!last) {
+          block_at(i, b, m);
+          ok = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err);
         }
-        tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          if ((pend >> t) & 1) {
-            if (!(ok = mbar_wait(smem_u32(&sm.p_full[t]), (cnt[t] - 1) & 1, abort_flag, p.err)))
-              break;
-            tc_fence_after();
-            issue_pv(t, ps);
-          }
-          if ((m >> t) & 1) {
-            issue_qk(t, s);
-            tc_commit(smem_u32(&sm.s_full[t]));
-            ++cnt[t];
-          }
-        }
+        if (ok && pend) ok = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
         if (!ok) break;
+        tc_fence_after();
+        // tile 0: PV for the previous block, then QK for this one (same TMEM columns)
+        if (pend & 1) {
+          ok = mbar_wait(smem_u32(&sm.p_full[0]), (cnt0 - 1) & 1, abort_flag, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(tS0, tO0, pv0, ps);
+          pv0 = 1;
+        }
+        if (m & 1) {
+          issue_qk(tS0, 0, s);
+          tc_commit(smem_u32(&sm.s_full[0]));
+          ++cnt0;
+        }
+        // tile 1
+        if (pend & 2) {
+          ok = mbar_wait(smem_u32(&sm.p_full[1]), (cnt1 - 1) & 1, abort_flag, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(tS1, tO1, pv1, ps);
+          pv1 = 1;
+        }
+        if (m & 2) {
+          issue_qk(tS1, 1, s);
+          tc_commit(smem_u32(&sm.s_full[1]));
+          ++cnt1;
+        }
         if (pend) tc_commit(smem_u32(&sm.v_empty[ps]));
-        tc_commit(smem_u32(&sm.k_empty[s]));
+        if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
         pend = m;
       }
-      if (ok && pend) {
-        const int ps = (nblk - 1) % kKVStages;
-        const uint32_t pph = ((nblk - 1) / kKVStages) & 1;
-        ok = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
-        tc_fence_after();
-        for (int t = 0; t < 2 && ok; ++t) {
-          if ((pend >> t) & 1) {
-            if (!(ok = mbar_wait(smem_u32(&sm.p_full[t]), (cnt[t] - 1) & 1, abort_flag, p.err)))
-              break;
-            tc_fence_after();
-            issue_pv(t, ps);
-          }
-        }
-      }
       if (ok) {
-        for (int t = 0; t < n_tiles; ++t) tc_commit(smem_u32(&sm.o_done[t]));
+        tc_commit(smem_u32(&sm.o_done[0]));
+        if (n_tiles > 1) tc_commit(smem_u32(&sm.o_done[1]));
       }
       // Whatever happened, do not leave tensor-core work in flight past the teardown.
       tc_commit(smem_u32(&sm.drain));
@@ -307,8 +311,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
       }
     }
-  } else if (warp >= 4) {
+  } else if (warp < 4) {
+    // ================================================================ idle warps 2-3
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+  } else {
     // ================================================================ softmax / epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
     const int t = (warp - 4) >> 2;
     if (t < n_tiles) {
       const int row = (warp & 3) * 32 + lane;
@@ -321,87 +329,119 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         scale_log2 = __ldg(p.q_scale + head) * __ldg(p.k_scale + head) * p.softmax_scale_log2;
       else
         scale_log2 = p.scale_log2;
+      // Lazy rescaling: O and l are rescaled only when a row maximum grows by more than
+      // kRescaleThreshold (log2 units); P is then bounded by 2^(threshold + boost).
+      constexpr float kRescaleThreshold = kFp8 ? 2.0f : 8.0f;
+      constexpr float kBoost = kFp8 ? 6.0f : 0.0f;  // e4m3 P: keep the bulk above 2^-6
       float m_used = -INFINITY;
       float l_sum = 0.f;
       int c = 0;
       bool ok = true;
+      const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
       for (int i = 0; i < nblk; ++i) {
         int b, m;
         block_at(i, b, m);
         if (!((m >> t) & 1)) continue;
         if (!(ok = mbar_wait(smem_u32(&sm.s_full[t]), c & 1, abort_flag, p.err))) break;
         tc_fence_after();
+        uint32_t r0[32], r1[32], r2[32], r3[32];
+        tmem_ld32(tS + 0, r0);
+        tmem_ld32(tS + 32, r1);
+        tmem_ld32(tS + 64, r2);
+        tmem_ld32(tS + 96, r3);
+        tmem_wait_ld();
+        reg_fence32(r0);
+        reg_fence32(r1);
+        reg_fence32(r2);
+        reg_fence32(r3);
         float s[kBlockN];
-        {
-          uint32_t r[32];
 #pragma unroll
-          for (int ch = 0; ch < 4; ++ch) {
-            tmem_ld32(tS + ch * 32, r);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) s[ch * 32 + j] = __uint_as_float(r[j]);
-          }
+        for (int j = 0; j < 32; ++j) {
+          s[j] = __uint_as_float(r0[j]);
+          s[32 + j] = __uint_as_float(r1[j]);
+          s[64 + j] = __uint_as_float(r2[j]);
+          s[96 + j] = __uint_as_float(r3[j]);
         }
         const int col0 = b * kBlockN;
         const int lo = pr.kv_lo - col0;  // valid columns [lo, hi)
         const int hi = pr.kv_hi - col0;
-        if (lo > 0 || hi < kBlockN) {
+        const bool partial = (lo > 0 || hi < kBlockN);
+        if (partial) {
 #pragma unroll
           for (int j = 0; j < kBlockN; ++j)
             if (j < lo || j >= hi) s[j] = -INFINITY;
         }
-        float mx = s[0];
+        float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
 #pragma unroll
-        for (int j = 1; j < kBlockN; ++j) mx = fmaxf(mx, s[j]);
+        for (int j = 4; j < kBlockN; j += 8) {
+          mx0 = fmax3(mx0, s[j], s[j + 4]);
+          mx1 = fmax3(mx1, s[j + 1], s[j + 5]);
+          mx2 = fmax3(mx2, s[j + 2], s[j + 6]);
+          mx3 = fmax3(mx3, s[j + 3], s[j + 7]);
+        }
+        const float mx = fmaxf(fmax3(mx0, mx1, mx2), mx3);
         const float m_blk = mx * scale_log2;
-        const bool need = m_blk > m_used + 8.0f;
+        const bool need = m_blk > m_used + kRescaleThreshold;
         const float m_new = need ? m_blk : m_used;
         if (c > 0 && __any_sync(0xffffffffu, need)) {
           const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
           l_sum *= alpha;
-          uint32_t r[32];
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
-            tmem_ld32(tO + ch * 32, r);
+            uint32_t o[32];
+            tmem_ld32(tO + ch * 32, o);
             tmem_wait_ld();
+            reg_fence32(o);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(__uint_as_float(r[j]) * alpha);
-            tmem_st32(tO + ch * 32, r);
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+            tmem_st32(tO + ch * 32, o);
           }
           tmem_wait_st();
         }
         m_used = m_new;
-        float sum = 0.f;
+        // x = s * scale_log2 - (m_used - boost), in packed pairs
+        const float bias = kBoost - m_used;
+        const uint64_t bias2 = f2_pack(bias, bias);
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < kBlockN; j += 4) {
+          float x0, x1, x2, x3;
+          f2_unpack(f2_fma(f2_pack(s[j], s[j + 1]), scale2, bias2), x0, x1);
+          f2_unpack(f2_fma(f2_pack(s[j + 2], s[j + 3]), scale2, bias2), x2, x3);
+          // half of the exponentials on the MUFU, half on the FMA pipe
+          s[j] = fast_exp2(x0);
+          s[j + 1] = fast_exp2(x1);
+          exp2_poly_pair(x2, x3, s[j + 2], s[j + 3]);
+          if (partial) {
+            const int jj = j;
+            if (jj + 2 < lo || jj + 2 >= hi) s[j + 2] = 0.f;
+            if (jj + 3 < lo || jj + 3 >= hi) s[j + 3] = 0.f;
+          }
+          sum2 = f2_add(sum2, f2_add(f2_pack(s[j], s[j + 1]), f2_pack(s[j + 2], s[j + 3])));
+        }
+        float sa, sb;
+        f2_unpack(sum2, sa, sb);
+        l_sum += sa + sb;
         if constexpr (kFp8) {
           uint32_t pk[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const float p0 = fast_exp2(fmaf(s[4 * j + 0], scale_log2, -m_used));
-            const float p1 = fast_exp2(fmaf(s[4 * j + 1], scale_log2, -m_used));
-            const float p2 = fast_exp2(fmaf(s[4 * j + 2], scale_log2, -m_used));
-            const float p3 = fast_exp2(fmaf(s[4 * j + 3], scale_log2, -m_used));
-            sum += (p0 + p1) + (p2 + p3);
             uint16_t lo16, hi16;
-            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo16) : "f"(p1), "f"(p0));
-            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi16) : "f"(p3), "f"(p2));
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo16) : "f"(s[4 * j + 1]), "f"(s[4 * j]));
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi16) : "f"(s[4 * j + 3]), "f"(s[4 * j + 2]));
             pk[j] = static_cast<uint32_t>(lo16) | (static_cast<uint32_t>(hi16) << 16);
           }
           tmem_st32(tP, pk);
         } else {
-          uint32_t pk[32];
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
+            uint32_t pk[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const float p0 = fast_exp2(fmaf(s[64 * half + 2 * j], scale_log2, -m_used));
-              const float p1 = fast_exp2(fmaf(s[64 * half + 2 * j + 1], scale_log2, -m_used));
-              sum += p0 + p1;
-              pk[j] = pack_bf16x2(p0, p1);
-            }
+            for (int j = 0; j < 32; ++j)
+              pk[j] = pack_bf16x2(s[64 * half + 2 * j], s[64 * half + 2 * j + 1]);
             tmem_st32(tP + half * 32, pk);
           }
         }
-        l_sum += sum;
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(smem_u32(&sm.p_full[t]));
@@ -416,11 +456,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const bool valid = qrow < pr.q_hi;
         __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
                              (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim;
-        uint32_t r[32];
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
+          uint32_t r[32];
           tmem_ld32(tO + ch * 32, r);
           tmem_wait_ld();
+          reg_fence32(r);
           uint32_t o[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)
@@ -525,6 +566,21 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
                                            static_cast<int>(smem));
       if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute", e);
       configured[dev] = true;
+    }
+  }
+  {
+    // setmaxnreg.inc waits until the registers it asks for are free in the block's launch
+    // allocation; refuse to launch a build whose register count cannot fund the split.
+    static int checked[2] = {0, 0};
+    if (!checked[kFp8 ? 1 : 0]) {
+      cudaFuncAttributes attr;
+      cudaError_t e = cudaFuncGetAttributes(&attr, attn_fwd_kernel<kFp8>);
+      if (e != cudaSuccess) return set_cuda_error("cudaFuncGetAttributes", e);
+      if (attr.numRegs * kAttnThreads < kRegSplitTotal)
+        return set_error(H3SA_ERR_UNSUPPORTED, "attention build has %d registers per thread; the "
+                         "warp-role register split needs %d", attr.numRegs,
+                         (kRegSplitTotal + kAttnThreads - 1) / kAttnThreads);
+      checked[kFp8 ? 1 : 0] = 1;
     }
   }
   attn_fwd_kernel<kFp8><<<ctas, kAttnThreads, smem, stream>>>(tmQ, tmK, tmV, prm);

@@ -6,7 +6,9 @@
 //   warp 0      TMA producer: Q tiles once, then K and V blocks through 2-stage rings.
 //   warp 1      TMEM owner and MMA issuer (one thread): S_t = Q_t K^T (smem x smem),
 //               O_t += P_t V (P from TMEM x V from smem), fp32 accumulators in TMEM.
-//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1 (one thread per query row):
+//   warps 2-3   idle (warp 2 builds the block-sparse union list before the roles start)
+//   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1 (one thread per query row;
+//               warp w reads TMEM lanes 32*(w%4) .. +31):
 //               online max / sum, lazy O rescale, P written back to TMEM as bf16, and the
 //               final normalise + bf16 store.
 // TMEM columns: S0 [0,128) with P0 aliased at [64,128), S1 [128,256) with P1 at
@@ -26,6 +28,12 @@ constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
 constexpr int kKVStages = 2;
 constexpr int kAttnThreads = 384;
+// setmaxnreg split: warps 0-3 (producer, MMA, two idle) keep kRegsControl registers, the two
+// softmax warpgroups get kRegsSoftmax. The sum must fit the launch allocation
+// (threads x registers per thread at launch, 168 under these launch bounds).
+constexpr int kRegsControl = 56;
+constexpr int kRegsSoftmax = 216;
+constexpr int kRegSplitTotal = 128 * kRegsControl + 256 * kRegsSoftmax;
 constexpr int kMaxProblems = 4;
 constexpr int kMaxUnionBlocks = 2048;
 

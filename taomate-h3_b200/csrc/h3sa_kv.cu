@@ -212,6 +212,36 @@ __global__ void __launch_bounds__(256) quant_apply_kernel(const QuantSpace q, co
   }
 }
 
+
+// ------------------------------------------------------------------ layout permutes
+struct PermuteParams {
+  const uint8_t* src;
+  uint8_t* dst;
+  long long dims[4];         // outer index space, row-major
+  long long src_stride[4];   // bytes
+  long long dst_stride[4];   // bytes
+  int row_bytes;             // contiguous inner record, multiple of 16
+};
+
+__global__ void __launch_bounds__(256) permute_rows_kernel(const PermuteParams p) {
+  const int cpr = p.row_bytes >> 4;
+  const long long total = p.dims[0] * p.dims[1] * p.dims[2] * p.dims[3] * cpr;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % cpr);
+    long long r = idx / cpr;
+    long long so = 0, dof = 0;
+#pragma unroll
+    for (int k = 3; k >= 0; --k) {
+      const long long i = r % p.dims[k];
+      r /= p.dims[k];
+      so += i * p.src_stride[k];
+      dof += i * p.dst_stride[k];
+    }
+    reinterpret_cast<uint4*>(p.dst + dof)[c] = __ldg(reinterpret_cast<const uint4*>(p.src + so) + c);
+  }
+}
+
 static int grid_for(long long work, int threads) {
   long long g = (work + threads - 1) / threads;
   const long long cap = 148LL * 16;
@@ -328,6 +358,32 @@ int h3sa_quantize_fp8_pool(const void* pool, void* pool_fp8, float* scale, int32
   q.page_table = page_table;
   q.table_blocks = table_blocks;
   return quantize_with_scratch(q, scale, device_error, static_cast<cudaStream_t>(stream));
+}
+
+int h3sa_permute_rows(const void* src, void* dst, const int64_t* dims, const int64_t* src_strides,
+                      const int64_t* dst_strides, int32_t row_bytes, void* stream) {
+  if (!src || !dst || !dims || !src_strides || !dst_strides || row_bytes <= 0 || (row_bytes & 15))
+    return set_error(H3SA_ERR_INVALID, "permute_rows: invalid arguments");
+  if ((reinterpret_cast<uintptr_t>(src) & 15) || (reinterpret_cast<uintptr_t>(dst) & 15))
+    return set_error(H3SA_ERR_INVALID, "permute_rows: tensors must be 16-byte aligned");
+  PermuteParams p;
+  p.src = static_cast<const uint8_t*>(src);
+  p.dst = static_cast<uint8_t*>(dst);
+  long long work = row_bytes / 16;
+  for (int k = 0; k < 4; ++k) {
+    if (dims[k] < 0 || (src_strides[k] & 15) || (dst_strides[k] & 15))
+      return set_error(H3SA_ERR_INVALID, "permute_rows: dims must be >= 0, strides 16-byte multiples");
+    p.dims[k] = dims[k];
+    p.src_stride[k] = src_strides[k];
+    p.dst_stride[k] = dst_strides[k];
+    work *= dims[k];
+  }
+  p.row_bytes = row_bytes;
+  if (work == 0) return H3SA_OK;
+  permute_rows_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("permute_rows_kernel launch", e);
+  return H3SA_OK;
 }
 
 }  // extern "C"

@@ -73,6 +73,11 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "h3sa_quantize_fp8_per_head": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "h3sa_quantize_fp8_pool": (ctypes.c_int, [_P, _P, _P, _I, _I, _P, _I, _I, _P, _P]),
+    "h3sa_permute_rows": (
+        ctypes.c_int,
+        [_P, _P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),
+         ctypes.POINTER(ctypes.c_int64), _I, _P],
+    ),
 }
 
 

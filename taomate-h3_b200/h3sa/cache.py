@@ -1,0 +1,433 @@
+"""Paged, head-major clean audio/video KV cache with the CleanAVKVCache interface.
+
+Mirrors ``CleanAVKVCache`` (T/streaming/cache.py:77-294): the same transactional
+stage -> commit protocol, the same retention and audio-drop row selection and the same
+error messages, but the storage is a per-layer pool of 128-row pages laid out
+``[heads, pages * 128, head_dim]`` plus a page table, instead of one dense tensor that
+``torch.cat`` re-allocates on every commit.
+
+Logical layout of one layer's page sequence::
+
+    [ history (committed clean rows, logical commit order) | tail ]
+
+The streaming hook writes the current chunk's media rows straight after the history
+(the tail), so a clean commit only advances the history length: staged rows are already
+in place. Retention and audio drop gather the selected rows into fresh pages in one
+kernel launch per layer (T/streaming/cache.py:246-284 selects the same rows).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .kernels import PAGE_ROWS, kv_copy_rows
+
+MAIN_LAYER_NAMES = tuple(f"blocks.{index}.attn" for index in range(50))
+VIDEO_TOKEN_TAG = 0
+AUDIO_TOKEN_TAG = 2
+
+
+@dataclass(frozen=True)
+class KVContract:
+    """Shape contract for the local attention shard (T/streaming/cache.py:16-23)."""
+
+    local_heads: int = 14
+    head_dim: int = 128
+    dtype: torch.dtype = torch.bfloat16
+    device_type: str = "cuda"
+
+
+def kv_contract_from_model(model: object) -> KVContract:
+    """Build the KV shape contract from an installed model (T/streaming/cache.py:26-48)."""
+
+    blocks = getattr(model, "blocks", None)
+    if blocks is None:
+        raise RuntimeError("model does not expose transformer blocks")
+    layers = len(blocks)
+    if layers != len(MAIN_LAYER_NAMES):
+        raise RuntimeError(f"expected {len(MAIN_LAYER_NAMES)} transformer layers, got {layers}")
+    architecture = getattr(model, "arch", None)
+    context = getattr(model, "parallel_context", None)
+    total_heads = int(getattr(architecture, "num_attention_heads", 0))
+    head_dim = int(getattr(architecture, "attention_head_dim", 0))
+    tp_size = int(getattr(context, "tp_world_size", 0))
+    ulysses_size = int(getattr(context, "ulysses_world_size", 0))
+    parallel_size = tp_size * ulysses_size
+    if total_heads <= 0 or head_dim <= 0 or parallel_size <= 0 or total_heads % parallel_size:
+        raise RuntimeError("model topology cannot resolve post-Ulysses local KV heads")
+    return KVContract(local_heads=total_heads // parallel_size, head_dim=head_dim)
+
+
+@dataclass(frozen=True)
+class AVKV:
+    """Dense clean audio/video keys and values for one attention layer."""
+
+    key: torch.Tensor
+    value: torch.Tensor
+
+
+class PagedLayerKV:
+    """Page pool and page sequence of one layer.
+
+    ``key``/``value`` are ``[heads, capacity_pages * 128, head_dim]``; ``pages`` lists the
+    physical page of each logical 128-row block; ``table`` is its int32 device copy
+    (length = capacity, unused entries 0). Pages are recycled through a free list; a
+    fresh or grown pool is zero-filled, so rows beyond a sequence's end are always finite.
+    """
+
+    def __init__(self, heads: int, head_dim: int, dtype: torch.dtype, device: torch.device,
+                 initial_pages: int = 8) -> None:
+        self.heads = heads
+        self.head_dim = head_dim
+        self.dtype = dtype
+        self.device = device
+        self.capacity = 0
+        self.key = torch.empty(0, device=device, dtype=dtype)
+        self.value = torch.empty(0, device=device, dtype=dtype)
+        self.free: list[int] = []
+        self.pages: list[int] = []
+        self.table = torch.zeros(0, dtype=torch.int32, device=device)
+        self.history_rows = 0
+        self._grow(max(1, initial_pages))
+
+    def _grow(self, capacity: int) -> None:
+        key = torch.zeros(self.heads, capacity * PAGE_ROWS, self.head_dim, dtype=self.dtype,
+                          device=self.device)
+        value = torch.zeros_like(key)
+        if self.capacity:
+            rows = self.capacity * PAGE_ROWS
+            key[:, :rows].copy_(self.key)
+            value[:, :rows].copy_(self.value)
+        self.free.extend(range(capacity - 1, self.capacity - 1, -1))
+        self.key, self.value = key, value
+        self.capacity = capacity
+        table = torch.zeros(capacity, dtype=torch.int32, device=self.device)
+        if self.pages:
+            table[: len(self.pages)] = torch.tensor(self.pages, dtype=torch.int32)
+        self.table = table
+
+    def _take(self, count: int) -> list[int]:
+        if count > len(self.free):
+            self._grow(max(2 * self.capacity, self.capacity + count - len(self.free)))
+        taken = [self.free.pop() for _ in range(count)]
+        return taken
+
+    def _sync_table(self) -> None:
+        n = len(self.pages)
+        if n:
+            self.table[:n].copy_(torch.tensor(self.pages, dtype=torch.int32), non_blocking=False)
+
+    def reserve(self, rows: int) -> None:
+        """Make the page sequence cover logical rows [0, rows)."""
+
+        need = (rows + PAGE_ROWS - 1) // PAGE_ROWS
+        if need > len(self.pages):
+            self.pages.extend(self._take(need - len(self.pages)))
+            self._sync_table()
+
+    def write(self, key: torch.Tensor, value: torch.Tensor, *, start: int, count: int,
+              src_start: int = 0, src_index: torch.Tensor | None = None) -> None:
+        """Copy ``count`` packed rows of key/value into logical rows [start, start+count)."""
+
+        self.reserve(start + count)
+        kv_copy_rows([key, value], [self.key, self.value], count=count, dst_table=self.table,
+                     src_start=src_start, src_index=src_index, dst_start=start)
+
+    def gather(self, rows: torch.Tensor) -> "PagedLayerKV":
+        """Build the sequence made of the given logical rows, in order, in fresh pages."""
+
+        count = int(rows.numel())
+        new_pages = self._take((count + PAGE_ROWS - 1) // PAGE_ROWS)
+        table = torch.zeros(self.capacity, dtype=torch.int32, device=self.device)
+        if new_pages:
+            table[: len(new_pages)] = torch.tensor(new_pages, dtype=torch.int32)
+        if count:
+            kv_copy_rows([self.key, self.value], [self.key, self.value], count=count,
+                         src_table=self.table, dst_table=table,
+                         src_index=rows.to(device=self.device, dtype=torch.int32))
+        self.free.extend(reversed(self.pages))
+        self.pages = new_pages
+        self.table = table
+        self.history_rows = count
+        return self
+
+    def materialize(self, rows: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Dense ``[rows, heads, head_dim]`` copies of logical rows [0, rows)."""
+
+        key = torch.empty(rows, self.heads, self.head_dim, dtype=self.dtype, device=self.device)
+        value = torch.empty_like(key)
+        if rows:
+            kv_copy_rows([self.key, self.value], [key, value], count=rows, src_table=self.table)
+        return key, value
+
+    def release(self) -> None:
+        self.free.extend(reversed(self.pages))
+        self.pages = []
+        self.history_rows = 0
+
+
+def _validate_layer_name(layer_name: str, names: tuple[str, ...]) -> None:
+    if layer_name not in names:
+        raise KeyError(f"unexpected transformer layer: {layer_name}")
+
+
+class CleanAVKVCache:
+    """Transactional persistent cache containing clean media KV only.
+
+    Clean commits append one streaming chunk. Retention preserves the first video's rows
+    as a long-term sink and the two most recent clean chunks.
+    """
+
+    def __init__(self, contract: KVContract, *, layer_names: tuple[str, ...] = MAIN_LAYER_NAMES,
+                 device: torch.device | str | None = None, initial_pages: int = 8) -> None:
+        self.contract = contract
+        self.layer_names = tuple(layer_names)
+        self._device = torch.device(device) if device is not None else None
+        self._initial_pages = initial_pages
+        self._layers: dict[str, PagedLayerKV] = {}
+        self._staged: dict[str, int] = {}
+        self._staged_block: int | None = None
+        self._staged_tags: tuple[int, ...] | None = None
+        self._staged_indices: torch.Tensor | None = None
+        self._block_index = 0
+        self._commit_token_counts: list[int] = []
+        self._commit_token_tags: list[tuple[int, ...]] = []
+
+    # ------------------------------------------------------------------ properties
+    @property
+    def committed_blocks(self) -> int:
+        """Logical number of clean chunks committed since the last clear."""
+
+        return self._block_index
+
+    @property
+    def history_tokens(self) -> int:
+        return sum(self._commit_token_counts)
+
+    @property
+    def history_audio_tokens(self) -> int:
+        return sum(tag == AUDIO_TOKEN_TAG for tags in self._commit_token_tags for tag in tags)
+
+    @property
+    def history_video_tokens(self) -> int:
+        return sum(tag == VIDEO_TOKEN_TAG for tags in self._commit_token_tags for tag in tags)
+
+    @property
+    def clean_commit_active(self) -> bool:
+        return self._staged_block is not None
+
+    def commit_token_tags(self) -> list[tuple[int, ...]]:
+        return list(self._commit_token_tags)
+
+    # ------------------------------------------------------------------ paged access
+    def layer(self, layer_name: str, device: torch.device | None = None) -> PagedLayerKV:
+        """The layer's page sequence, created on first use."""
+
+        _validate_layer_name(layer_name, self.layer_names)
+        paged = self._layers.get(layer_name)
+        if paged is None:
+            dev = device or self._device or torch.device("cuda", torch.cuda.current_device())
+            paged = PagedLayerKV(self.contract.local_heads, self.contract.head_dim,
+                                 self.contract.dtype, dev, self._initial_pages)
+            self._layers[layer_name] = paged
+        return paged
+
+    def history_rows(self, layer_name: str) -> int:
+        _validate_layer_name(layer_name, self.layer_names)
+        paged = self._layers.get(layer_name)
+        return 0 if paged is None else paged.history_rows
+
+    def history(self, layer_name: str) -> AVKV | None:
+        """Dense copies of the layer's committed rows (None when empty)."""
+
+        _validate_layer_name(layer_name, self.layer_names)
+        paged = self._layers.get(layer_name)
+        if paged is None or paged.history_rows == 0:
+            return None
+        key, value = paged.materialize(paged.history_rows)
+        return AVKV(key=key, value=value)
+
+    # ------------------------------------------------------------------ transactions
+    def begin_clean_commit(self, block_index: int) -> None:
+        if self.clean_commit_active:
+            raise RuntimeError("a clean KV commit is already active")
+        if block_index != self._block_index:
+            raise RuntimeError(f"expected clean chunk {self._block_index}, got {block_index}")
+        self._staged_block = block_index
+        self._staged.clear()
+        self._staged_tags = None
+        self._staged_indices = None
+
+    def _resolve_stage(self, token_tags: torch.Tensor, commit_mask: torch.Tensor) -> torch.Tensor:
+        if self._staged_indices is None:
+            indices = torch.nonzero(commit_mask.to(torch.bool), as_tuple=False).flatten()
+            if indices.numel() == 0:
+                raise RuntimeError("clean commit did not contain audio/video rows")
+            selected_tags = token_tags.index_select(0, indices)
+            tags = tuple(int(tag) for tag in selected_tags.detach().cpu().tolist())
+            if frozenset(tags) != frozenset((VIDEO_TOKEN_TAG, AUDIO_TOKEN_TAG)):
+                raise RuntimeError("each clean chunk must contain both video and audio KV")
+            self._staged_indices = indices
+            self._staged_tags = tags
+        return self._staged_indices
+
+    def _check_stage_args(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,
+                          token_tags: torch.Tensor, commit_mask: torch.Tensor) -> None:
+        if not self.clean_commit_active:
+            raise RuntimeError("begin_clean_commit() must be called before stage()")
+        _validate_layer_name(layer_name, self.layer_names)
+        if layer_name in self._staged:
+            raise RuntimeError(f"{layer_name}: KV was staged more than once")
+        if key.shape != value.shape or key.ndim != 3:
+            raise RuntimeError(f"{layer_name}: key/value must have matching rank-3 shapes")
+        if token_tags.ndim != 1 or commit_mask.ndim != 1:
+            raise RuntimeError("token_tags and commit_mask must be rank-1")
+        if token_tags.shape[0] != key.shape[0] or commit_mask.shape[0] != key.shape[0]:
+            raise RuntimeError(f"{layer_name}: packed metadata length does not match KV rows")
+        expected_tail = (self.contract.local_heads, self.contract.head_dim)
+        if tuple(key.shape[1:]) != expected_tail:
+            raise RuntimeError(
+                f"{layer_name}: expected key shape [tokens, {expected_tail[0]}, {expected_tail[1]}], "
+                f"got {tuple(key.shape)}"
+            )
+        if key.dtype != self.contract.dtype or value.dtype != self.contract.dtype:
+            raise RuntimeError(f"{layer_name}: persistent KV must be {self.contract.dtype}")
+        if key.device.type != self.contract.device_type or value.device.type != self.contract.device_type:
+            raise RuntimeError(f"{layer_name}: persistent KV must reside on {self.contract.device_type}")
+
+    def stage(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,
+              token_tags: torch.Tensor, commit_mask: torch.Tensor) -> None:
+        """Stage clean audio/video rows produced by one transformer layer.
+
+        The committed rows (``nonzero(commit_mask)`` in packed order) are written into the
+        layer's tail, directly after its history.
+        """
+
+        self._check_stage_args(layer_name, key, value, token_tags, commit_mask)
+        indices = self._resolve_stage(token_tags, commit_mask)
+        paged = self.layer(layer_name, key.device)
+        paged.write(key.contiguous(), value.contiguous(), start=paged.history_rows,
+                    count=int(indices.numel()), src_index=indices.to(torch.int32))
+        self._staged[layer_name] = int(indices.numel())
+
+    def stage_in_place(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,
+                       token_tags: torch.Tensor, commit_mask: torch.Tensor) -> None:
+        """Stage rows the streaming hook already wrote to the tail, in commit order."""
+
+        self._check_stage_args(layer_name, key, value, token_tags, commit_mask)
+        indices = self._resolve_stage(token_tags, commit_mask)
+        self._staged[layer_name] = int(indices.numel())
+
+    def commit(self) -> None:
+        """Atomically append all staged layers to persistent history."""
+
+        if not self.clean_commit_active:
+            raise RuntimeError("no clean KV commit is active")
+        missing = [name for name in self.layer_names if name not in self._staged]
+        if missing:
+            raise RuntimeError(f"clean KV commit is missing {len(missing)} transformer layers")
+        assert self._staged_tags is not None
+        token_count = len(self._staged_tags)
+        for layer_name in self.layer_names:
+            staged = self._staged.pop(layer_name)
+            if staged != token_count:
+                raise RuntimeError(f"{layer_name}: staged {staged} rows, expected {token_count}")
+            self._layers[layer_name].history_rows += token_count
+        self._commit_token_counts.append(token_count)
+        self._commit_token_tags.append(self._staged_tags)
+        self._block_index += 1
+        self._clear_staging()
+
+    def retain_sink_and_recent_commits(self) -> None:
+        """Keep the first chunk's video sink and the most recent clean chunks."""
+
+        if self.clean_commit_active:
+            raise RuntimeError("cannot trim persistent KV during an active clean commit")
+        block_count = len(self._commit_token_counts)
+        if block_count <= 2:
+            return
+        recent_start = max(1, block_count - 2)
+        selection = [(0, True)] + [(index, False) for index in range(recent_start, block_count)]
+        self._retain_commit_rows(selection)
+
+    def drop_audio_history(self) -> int:
+        """Remove audio rows while preserving every retained video row."""
+
+        if self.clean_commit_active:
+            raise RuntimeError("cannot drop audio history during an active clean commit")
+        removed_tokens = self.history_audio_tokens
+        if not self._commit_token_counts:
+            return 0
+        self._retain_commit_rows([(index, True) for index in range(len(self._commit_token_counts))])
+        return removed_tokens
+
+    def rollback(self) -> None:
+        """Discard the currently staged clean chunk (its tail rows are simply not adopted)."""
+
+        self._clear_staging()
+
+    def clear(self) -> None:
+        """Clear persistent and staged KV and reset the logical chunk count."""
+
+        for paged in self._layers.values():
+            paged.release()
+        self._commit_token_counts.clear()
+        self._commit_token_tags.clear()
+        self._block_index = 0
+        self._clear_staging()
+
+    def retained_rows(self, selection: list[tuple[int, bool]]) -> tuple[list[int], list[int], list[tuple[int, ...]]]:
+        """Logical rows kept by a ``(commit, video_only)`` selection, with counts and tags."""
+
+        offsets = [0]
+        for count in self._commit_token_counts:
+            offsets.append(offsets[-1] + count)
+        selected_rows: list[int] = []
+        selected_counts: list[int] = []
+        selected_tags: list[tuple[int, ...]] = []
+        for block_index, video_only in selection:
+            tags = self._commit_token_tags[block_index]
+            start = offsets[block_index]
+            local_rows = [i for i, tag in enumerate(tags) if not video_only or tag == VIDEO_TOKEN_TAG]
+            if not local_rows:
+                continue
+            selected_rows.extend(start + row for row in local_rows)
+            kept_tags = tuple(tags[row] for row in local_rows)
+            selected_counts.append(len(kept_tags))
+            selected_tags.append(kept_tags)
+        return selected_rows, selected_counts, selected_tags
+
+    def _retain_commit_rows(self, selection: list[tuple[int, bool]]) -> None:
+        selected_rows, selected_counts, selected_tags = self.retained_rows(selection)
+        if not selected_rows:
+            for paged in self._layers.values():
+                paged.release()
+            self._commit_token_counts.clear()
+            self._commit_token_tags.clear()
+            return
+        rows = torch.tensor(selected_rows, dtype=torch.int32)
+        for paged in self._layers.values():
+            if paged.history_rows:
+                paged.gather(rows)
+        self._commit_token_counts = selected_counts
+        self._commit_token_tags = selected_tags
+
+    def _clear_staging(self) -> None:
+        self._staged.clear()
+        self._staged_block = None
+        self._staged_tags = None
+        self._staged_indices = None
+
+
+__all__ = [
+    "AUDIO_TOKEN_TAG",
+    "AVKV",
+    "CleanAVKVCache",
+    "KVContract",
+    "MAIN_LAYER_NAMES",
+    "PagedLayerKV",
+    "VIDEO_TOKEN_TAG",
+    "kv_contract_from_model",
+]

@@ -1,0 +1,322 @@
+"""Streaming attention hook with the reference's call protocol, on the sm_100a kernels.
+
+Mirrors ``H3StreamingAttentionHook`` (T/streaming/attention_hook.py:39-252): the same
+keyword call, validation order and messages, live-document rule, modes and receipt
+counters. Per packed document the visibility is unchanged:
+
+* the live document's condition (text) rows attend to condition K/V only;
+* its media rows attend to [condition, persistent clean AV history, current media];
+* every other (pad) document attends to itself.
+
+What changes is the data path. Instead of ``index_select`` + ``torch.cat`` of the whole
+history and one FlashAttention-3 launch per part, the hook writes the current media,
+condition and other-document K/V rows into the layer's page sequence right after the
+persistent history::
+
+    logical KV rows: [history | media | condition | other documents]
+
+and runs every document's attention in one kernel launch over that sequence. In
+CLEAN_COMMIT mode the media rows written there are exactly the rows the cache stages, so
+the commit needs no further copy.
+
+Backends (``attention_backend``): ``"flash_attn_3"``/``"flash_attn3"``/``"sdpa"`` (dense
+bf16), ``"flash_attn3_fp8_dynamic"`` (per-call per-head e4m3 Q/K/V,
+F/streaming/attention_hook.py:1081-1098) and ``"flex_dynamic_blocksparse"`` (history
+block top-k, F/inference/dynamic_block_sparse.py:50-172).
+"""
+
+from __future__ import annotations
+
+from enum import Enum
+from typing import Sequence
+
+import torch
+
+from . import _lib
+from .cache import CleanAVKVCache
+from .kernels import AttentionProblem, attention_fwd, kv_copy_rows, quantize_fp8_e4m3_per_head, quantize_fp8_pool
+
+DENSE_BACKENDS = ("flash_attn_3", "flash_attn3", "sdpa", "h3sa_dense")
+FP8_BACKENDS = ("flash_attn3_fp8_dynamic",)
+SPARSE_BACKENDS = ("flex_dynamic_blocksparse",)
+
+
+class HookMode(str, Enum):
+    IDLE = "idle"
+    NOISY = "noisy"
+    CLEAN_COMMIT = "clean_commit"
+
+
+def _live_documents_from_mask(commit_mask: torch.Tensor,
+                              boundaries: Sequence[tuple[int, int]]) -> tuple[int, ...]:
+    """Documents holding any committed row (T/streaming/attention_hook.py:28-36)."""
+
+    live: list[int] = []
+    for document_index, (start, stop) in enumerate(boundaries):
+        if bool(commit_mask[start:stop].any().item()):
+            live.append(document_index)
+    return tuple(live)
+
+
+def _as_range(indices: torch.Tensor) -> tuple[int, int] | None:
+    """(first, stop) when the sorted host index list is one contiguous run."""
+
+    n = int(indices.numel())
+    if n == 0:
+        return None
+    first = int(indices[0])
+    last = int(indices[-1])
+    return (first, last + 1) if last - first + 1 == n else None
+
+
+class _DocumentPlan:
+    """Row bookkeeping of one activation, resolved on the first layer call."""
+
+    def __init__(self, boundaries: tuple[tuple[int, int], ...], live: int,
+                 commit_mask_host: torch.Tensor, device: torch.device) -> None:
+        start, stop = boundaries[live]
+        media_mask = commit_mask_host[start:stop]
+        cond = torch.nonzero(~media_mask, as_tuple=False).flatten() + start
+        media = torch.nonzero(media_mask, as_tuple=False).flatten() + start
+        if cond.numel() == 0 or media.numel() == 0:
+            raise RuntimeError("live streaming document must contain condition and media rows")
+        self.boundaries = boundaries
+        self.live = live
+        self.n_cond = int(cond.numel())
+        self.n_media = int(media.numel())
+        self.cond_range = _as_range(cond)
+        self.media_range = _as_range(media)
+        self.cond_index = cond.to(device=device, dtype=torch.int32)
+        self.media_index = media.to(device=device, dtype=torch.int32)
+        self.others = [(a, b) for i, (a, b) in enumerate(boundaries) if i != live and b > a]
+
+
+class H3StreamingAttentionHook:
+    """Condition current media on text, persistent clean AV KV, and current KV."""
+
+    def __init__(self, cache: CleanAVKVCache, *, backend: str = "flash_attn_3",
+                 history_density: float = 0.5) -> None:
+        if backend not in DENSE_BACKENDS + FP8_BACKENDS + SPARSE_BACKENDS:
+            raise ValueError(f"unsupported H3 streaming attention backend: {backend}")
+        if not 0.0 < history_density <= 1.0:
+            raise ValueError("dynamic history KV density must be in (0, 1]")
+        self.cache = cache
+        self.backend = backend
+        self.history_density = float(history_density)
+        self.kernel_calls = 0
+        self.query_tokens = 0
+        self.key_tokens = 0
+        self.launches = 0
+        self.mode = HookMode.IDLE
+        self._plan: _DocumentPlan | None = None
+        self._plan_key: tuple[int, ...] | None = None
+        self._device_error: torch.Tensor | None = None
+        self._fp8_pools: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def receipt(self) -> dict[str, object]:
+        return {
+            "backend": f"h3sa_sm100a_{self.backend}",
+            "tensor_layout": "NHD",
+            "is_causal": False,
+            "kernel_calls": self.kernel_calls,
+            "query_tokens": self.query_tokens,
+            "key_tokens": self.key_tokens,
+            "launches": self.launches,
+        }
+
+    @property
+    def active(self) -> bool:
+        return self.mode is not HookMode.IDLE
+
+    def activate(self, mode: HookMode) -> None:
+        if self.active:
+            raise RuntimeError("streaming attention hook is already active")
+        if mode not in (HookMode.NOISY, HookMode.CLEAN_COMMIT):
+            raise ValueError(f"unsupported streaming hook mode: {mode}")
+        self.mode = mode
+        self._plan = None
+        self._plan_key = None
+
+    def deactivate(self) -> None:
+        self.mode = HookMode.IDLE
+        self._plan = None
+        self._plan_key = None
+
+    def device_error(self, device: torch.device) -> torch.Tensor:
+        if self._device_error is None or self._device_error.device != device:
+            self._device_error = torch.zeros(1, dtype=torch.int32, device=device)
+        return self._device_error
+
+    def check_device_error(self) -> None:
+        """Raise if any kernel of this hook reported a device-side failure (synchronises)."""
+
+        if self._device_error is not None:
+            code = int(self._device_error.item())
+            if code:
+                raise RuntimeError(f"h3sa device error flags {code:#x}")
+
+    def _validate_qkv(self, layer_name: str, query: torch.Tensor, key: torch.Tensor,
+                      value: torch.Tensor) -> None:
+        contract = self.cache.contract
+        expected_tail = (contract.local_heads, contract.head_dim)
+        if query.shape != key.shape or value.shape != key.shape or key.ndim != 3:
+            raise RuntimeError(f"{layer_name}: query/key/value must have matching rank-3 shapes")
+        if tuple(key.shape[1:]) != expected_tail:
+            raise RuntimeError(
+                f"{layer_name}: expected local attention tail {expected_tail}, "
+                f"got {tuple(key.shape[1:])}"
+            )
+        if query.dtype != contract.dtype or key.dtype != contract.dtype or value.dtype != contract.dtype:
+            raise RuntimeError(f"{layer_name}: streaming attention requires {contract.dtype} QKV")
+        if (query.device.type != contract.device_type or key.device.type != contract.device_type
+                or value.device.type != contract.device_type):
+            raise RuntimeError(f"{layer_name}: streaming attention requires {contract.device_type} QKV")
+
+    def _resolve_plan(self, boundaries: tuple[tuple[int, int], ...],
+                      commit_mask: torch.Tensor, device: torch.device) -> _DocumentPlan:
+        points = tuple(b for _, b in boundaries)
+        if self._plan is not None and self._plan_key == points:
+            return self._plan
+        live = _live_documents_from_mask(commit_mask, boundaries)
+        if len(live) != 1:
+            raise RuntimeError(f"direct streaming expects exactly one live document, got {live}")
+        plan = _DocumentPlan(boundaries, live[0], commit_mask.detach().to("cpu", torch.bool), device)
+        self._plan, self._plan_key = plan, points
+        return plan
+
+    def __call__(self, *, attention: object, layer_name: str, query: torch.Tensor,
+                 key: torch.Tensor, value: torch.Tensor, token_tags: torch.Tensor,
+                 commit_mask: torch.Tensor, cu_seqlens_host: Sequence[int]) -> torch.Tensor:
+        if not self.active:
+            raise RuntimeError("streaming attention hook was called while inactive")
+        self._validate_qkv(layer_name, query, key, value)
+        if commit_mask.ndim != 1 or commit_mask.shape[0] != query.shape[0]:
+            raise RuntimeError(f"{layer_name}: commit_mask does not match packed QKV rows")
+        if token_tags.ndim != 1 or token_tags.shape[0] != query.shape[0]:
+            raise RuntimeError(f"{layer_name}: token_tags does not match packed QKV rows")
+        points = tuple(int(point) for point in cu_seqlens_host)
+        if (len(points) < 2 or points[0] != 0 or points[-1] != query.shape[0]
+                or any(left > right for left, right in zip(points, points[1:]))):
+            raise RuntimeError(f"{layer_name}: invalid packed sequence boundaries")
+        boundaries = tuple(zip(points[:-1], points[1:]))
+        plan = self._resolve_plan(boundaries, commit_mask, query.device)
+        scale = float(getattr(attention, "softmax_scale"))
+
+        query = query.contiguous()
+        key = key.contiguous()
+        value = value.contiguous()
+        paged = self.cache.layer(layer_name, query.device)
+        err = self.device_error(query.device)
+        n_hist = paged.history_rows
+        m0 = n_hist
+        c0 = m0 + plan.n_media
+        o0 = c0 + plan.n_cond
+
+        # 1. current K/V rows into the tail of the layer's page sequence
+        if plan.media_range is not None:
+            paged.write(key, value, start=m0, count=plan.n_media, src_start=plan.media_range[0])
+        else:
+            paged.write(key, value, start=m0, count=plan.n_media, src_index=plan.media_index)
+        if plan.cond_range is not None:
+            paged.write(key, value, start=c0, count=plan.n_cond, src_start=plan.cond_range[0])
+        else:
+            paged.write(key, value, start=c0, count=plan.n_cond, src_index=plan.cond_index)
+        other_kv: list[tuple[int, int, int]] = []
+        cursor = o0
+        for a, b in plan.others:
+            paged.write(key, value, start=cursor, count=b - a, src_start=a)
+            other_kv.append((a, b, cursor))
+            cursor += b - a
+
+        # 2. attention problems over packed query rows (gathered when not contiguous)
+        out = torch.empty_like(query)
+        q_src = query
+        media_q = plan.media_range
+        cond_q = plan.cond_range
+        gathered = None
+        if media_q is None or cond_q is None:
+            gathered = torch.empty(plan.n_media + plan.n_cond, *query.shape[1:], dtype=query.dtype,
+                                   device=query.device)
+            kv_copy_rows([query], [gathered], count=plan.n_media, src_index=plan.media_index)
+            kv_copy_rows([query], [gathered], count=plan.n_cond, src_index=plan.cond_index,
+                         dst_start=plan.n_media)
+            q_src = gathered
+            media_q = (0, plan.n_media)
+            cond_q = (plan.n_media, plan.n_media + plan.n_cond)
+        n_kv_media = o0  # history + media + condition
+        media_problem = AttentionProblem(media_q[0], media_q[1], 0, n_kv_media,
+                                         sparse=self.backend in SPARSE_BACKENDS)
+        cond_problem = AttentionProblem(cond_q[0], cond_q[1], c0, o0)
+        out_main = out if gathered is None else torch.empty_like(gathered)
+        self._launch(layer_name, paged, q_src, out_main, [media_problem, cond_problem], scale,
+                     n_kv_media, n_hist, plan, err)
+        if other_kv:
+            probs = [AttentionProblem(a, b, c, c + (b - a)) for a, b, c in other_kv]
+            for i in range(0, len(probs), _lib.MAX_PROBLEMS):
+                attention_fwd(query, out, paged.key, paged.value, paged.table,
+                              probs[i:i + _lib.MAX_PROBLEMS], scale, device_error=err)
+                self.launches += 1
+        if gathered is not None:
+            kv_copy_rows([out_main], [out], count=plan.n_media, src_start=0,
+                         dst_index=plan.media_index)
+            kv_copy_rows([out_main], [out], count=plan.n_cond, src_start=plan.n_media,
+                         dst_index=plan.cond_index)
+
+        self.kernel_calls += 2 + len(other_kv)
+        self.query_tokens += int(query.shape[0])
+        self.key_tokens += n_kv_media + plan.n_cond + sum(b - a for a, b, _ in other_kv)
+
+        if self.mode is HookMode.CLEAN_COMMIT:
+            self.cache.stage_in_place(layer_name, key, value, token_tags, commit_mask)
+        return out
+
+    # ------------------------------------------------------------------ launches
+    def _launch(self, layer_name: str, paged, q_src: torch.Tensor, out: torch.Tensor,
+                problems: list[AttentionProblem], scale: float, n_kv: int, n_hist: int,
+                plan: _DocumentPlan, err: torch.Tensor) -> None:
+        if self.backend in FP8_BACKENDS:
+            self._launch_fp8(layer_name, paged, q_src, out, problems, scale, n_kv, err)
+            return
+        lists = {}
+        if self.backend in SPARSE_BACKENDS:
+            from .block_sparse import history_block_lists
+
+            lists = history_block_lists(q_src, problems[0], paged, n_hist=n_hist, n_kv=n_kv,
+                                        density=self.history_density, scale=scale)
+            if not lists:
+                problems = [AttentionProblem(p.q_lo, p.q_hi, p.kv_lo, p.kv_hi) for p in problems]
+        attention_fwd(q_src, out, paged.key, paged.value, paged.table, problems, scale,
+                      device_error=err, **lists)
+        self.launches += 1
+
+    def _launch_fp8(self, layer_name: str, paged, q_src: torch.Tensor, out: torch.Tensor,
+                    problems: list[AttentionProblem], scale: float, n_kv: int,
+                    err: torch.Tensor) -> None:
+        media, cond = problems
+        pools = self._fp8_pools.get(layer_name)
+        if pools is None or pools[0].shape != paged.key.shape:
+            pools = (torch.zeros_like(paged.key, dtype=torch.float8_e4m3fn),
+                     torch.zeros_like(paged.value, dtype=torch.float8_e4m3fn))
+            self._fp8_pools[layer_name] = pools
+        k8, v8 = pools
+        heads = paged.heads
+        k_scale = torch.empty(heads, dtype=torch.float32, device=q_src.device)
+        v_scale = torch.empty_like(k_scale)
+        quantize_fp8_pool(paged.key, k8, k_scale, paged.table, n_kv, device_error=err)
+        quantize_fp8_pool(paged.value, v8, v_scale, paged.table, n_kv, device_error=err)
+        q_media = q_src[media.q_lo:media.q_hi].unsqueeze(0)
+        q8, q_scale = quantize_fp8_e4m3_per_head(q_media)
+        out_media = torch.empty(media.q_hi - media.q_lo, *q_src.shape[1:], dtype=torch.bfloat16,
+                                device=q_src.device)
+        attention_fwd(q8.squeeze(0), out_media, k8, v8, paged.table,
+                      [AttentionProblem(0, media.q_hi - media.q_lo, media.kv_lo, media.kv_hi)],
+                      scale, q_scale=q_scale.reshape(-1).contiguous(), k_scale=k_scale,
+                      v_scale=v_scale, device_error=err)
+        out[media.q_lo:media.q_hi].copy_(out_media)
+        # condition rows attend to condition K/V only; that tiny call stays in bf16
+        attention_fwd(q_src, out, paged.key, paged.value, paged.table, [cond], scale,
+                      device_error=err)
+        self.launches += 2
+
+
+__all__ = ["H3StreamingAttentionHook", "HookMode"]

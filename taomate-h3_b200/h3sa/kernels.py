@@ -196,3 +196,17 @@ def quantize_fp8_pool(
     call("h3sa_quantize_fp8_pool", ptr(pool), ptr(pool_fp8), ptr(scale), heads, pages,
          ptr(page_table), int(page_table.numel()), int(rows), ptr(device_error),
          stream_handle(None))
+
+
+def permute_rows(src: torch.Tensor, dst: torch.Tensor, dims: Sequence[int],
+                 src_strides: Sequence[int], dst_strides: Sequence[int], row_bytes: int,
+                 *, stream: torch.cuda.Stream | None = None) -> None:
+    """Copy ``row_bytes`` records over a 4-D index space with byte strides on both sides."""
+
+    _require_cuda(src, dst)
+    if len(dims) != 4 or len(src_strides) != 4 or len(dst_strides) != 4:
+        raise ValueError("permute_rows takes a 4-D index space")
+    d = (ctypes.c_int64 * 4)(*[int(x) for x in dims])
+    ss = (ctypes.c_int64 * 4)(*[int(x) for x in src_strides])
+    ds = (ctypes.c_int64 * 4)(*[int(x) for x in dst_strides])
+    call("h3sa_permute_rows", ptr(src), ptr(dst), d, ss, ds, int(row_bytes), stream_handle(stream))
