@@ -14,6 +14,31 @@
 
 namespace h3sa {
 
+// Exponentials per 16 scores evaluated by the FMA-pipe polynomial instead of the MUFU
+// (0 measured fastest on B200 for d = 128: the MUFU keeps up, the polynomial costs issue).
+#ifndef H3SA_EXP_POLY_PER16
+#define H3SA_EXP_POLY_PER16 0
+#endif
+constexpr int kExpPolyPer16 = H3SA_EXP_POLY_PER16;
+static_assert(kExpPolyPer16 % 2 == 0 && kExpPolyPer16 <= 16, "poly exponentials come in pairs");
+
+
+// Optional per-block timeline of two CTAs (first and middle of the grid), compiled only with
+// -DH3SA_TRACE: clock64() at fixed points of the producer, MMA and softmax loops.
+#ifdef H3SA_TRACE
+constexpr int kTraceBlocks = 48;
+__device__ long long g_h3sa_trace[2][kTraceBlocks][24];
+#define H3SA_TRACE_AT(blk, ev)                                                              \
+  do {                                                                                     \
+    const int slot_ = blockIdx.x == 0 ? 0 : (blockIdx.x == gridDim.x / 2 ? 1 : -1);        \
+    if (slot_ >= 0 && (blk) < kTraceBlocks) g_h3sa_trace[slot_][(blk)][(ev)] = clock64();  \
+  } while (0)
+#else
+#define H3SA_TRACE_AT(blk, ev) \
+  do {                         \
+  } while (0)
+#endif
+
 template <bool kFp8>
 struct AttnCfg {
   static constexpr int kElem = kFp8 ? 1 : 2;
@@ -201,12 +226,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           break;
         }
         if (!mbar_wait(smem_u32(&sm.k_empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        H3SA_TRACE_AT(i, 14);
         const uint32_t kb = smem_u32(&sm.k_full[s]);
         mbar_expect_tx(kb, Cfg::kTileBytes);
         for (int a = 0; a < Cfg::kAtoms; ++a)
           tma_load_3d(smem_u32(sm.k[s]) + a * Cfg::kAtomBytes, &tmK, kb, a * (128 / Cfg::kElem),
                       page * kBlockN, head);
         if (!mbar_wait(smem_u32(&sm.v_empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        H3SA_TRACE_AT(i, 15);
         const uint32_t vb = smem_u32(&sm.v_full[s]);
         mbar_expect_tx(vb, Cfg::kTileBytes);
         for (int a = 0; a < Cfg::kAtoms; ++a)
@@ -266,11 +293,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         if (ok && pend) ok = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
         if (!ok) break;
+        H3SA_TRACE_AT(i, 10);
         tc_fence_after();
         // tile 0: PV for the previous block, then QK for this one (same TMEM columns)
         if (pend & 1) {
           ok = mbar_wait(smem_u32(&sm.p_full[0]), (cnt0 - 1) & 1, abort_flag, p.err);
           if (!ok) break;
+          H3SA_TRACE_AT(i, 11);
           tc_fence_after();
           issue_pv(tS0, tO0, pv0, ps);
           pv0 = 1;
@@ -284,6 +313,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (pend & 2) {
           ok = mbar_wait(smem_u32(&sm.p_full[1]), (cnt1 - 1) & 1, abort_flag, p.err);
           if (!ok) break;
+          H3SA_TRACE_AT(i, 12);
           tc_fence_after();
           issue_pv(tS1, tO1, pv1, ps);
           pv1 = 1;
@@ -296,6 +326,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (pend) tc_commit(smem_u32(&sm.v_empty[ps]));
         if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
         pend = m;
+        H3SA_TRACE_AT(i, 13);
       }
       if (ok) {
         tc_commit(smem_u32(&sm.o_done[0]));
@@ -343,6 +374,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         block_at(i, b, m);
         if (!((m >> t) & 1)) continue;
         if (!(ok = mbar_wait(smem_u32(&sm.s_full[t]), c & 1, abort_flag, p.err))) break;
+        const bool tr = (warp & 3) == 0 && lane == 0;
+        if (tr) H3SA_TRACE_AT(i, 5 * t + 0);
         tc_fence_after();
         uint32_t r0[32], r1[32], r2[32], r3[32];
         tmem_ld32(tS + 0, r0);
@@ -354,6 +387,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         reg_fence32(r1);
         reg_fence32(r2);
         reg_fence32(r3);
+        if (tr) H3SA_TRACE_AT(i, 5 * t + 1);
         float s[kBlockN];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -380,10 +414,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mx3 = fmax3(mx3, s[j + 3], s[j + 7]);
         }
         const float mx = fmaxf(fmax3(mx0, mx1, mx2), mx3);
+        if (tr) H3SA_TRACE_AT(i, 16 + 2 * t);
         const float m_blk = mx * scale_log2;
         const bool need = m_blk > m_used + kRescaleThreshold;
         const float m_new = need ? m_blk : m_used;
-        if (c > 0 && __any_sync(0xffffffffu, need)) {
+        const bool any_need = c > 0 && __any_sync(0xffffffffu, need);
+        if (tr) H3SA_TRACE_AT(i, 17 + 2 * t);
+        if (any_need) {
           const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
           l_sum *= alpha;
 #pragma unroll
@@ -399,52 +436,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_wait_st();
         }
         m_used = m_new;
-        // x = s * scale_log2 - (m_used - boost), in packed pairs
+        if (tr) H3SA_TRACE_AT(i, 5 * t + 2);
+        // x = s * scale_log2 - (m_used - boost) in packed fp32 pairs, then 2^x on the MUFU
+        // (kExpPolyPer16 of every 16 on the FMA pipe); P packed for the PV MMA, row sum in fp32.
         const float bias = kBoost - m_used;
         const uint64_t bias2 = f2_pack(bias, bias);
-        uint64_t sum2 = f2_pack(0.f, 0.f);
 #pragma unroll
-        for (int j = 0; j < kBlockN; j += 4) {
-          float x0, x1, x2, x3;
+        for (int j = 0; j < kBlockN; j += 2) {
+          float x0, x1;
           f2_unpack(f2_fma(f2_pack(s[j], s[j + 1]), scale2, bias2), x0, x1);
-          f2_unpack(f2_fma(f2_pack(s[j + 2], s[j + 3]), scale2, bias2), x2, x3);
-          // half of the exponentials on the MUFU, half on the FMA pipe
-          s[j] = fast_exp2(x0);
-          s[j + 1] = fast_exp2(x1);
-          exp2_poly_pair(x2, x3, s[j + 2], s[j + 3]);
-          if (partial) {
-            const int jj = j;
-            if (jj + 2 < lo || jj + 2 >= hi) s[j + 2] = 0.f;
-            if (jj + 3 < lo || jj + 3 >= hi) s[j + 3] = 0.f;
+          s[j] = x0;
+          s[j + 1] = x1;
+        }
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+        uint32_t pk[kBlockN / 2];  // bf16: one pair per word; e4m3: two pairs per word
+#pragma unroll
+        for (int j = 0; j < kBlockN; j += 2) {
+          float p0, p1;
+          if ((j % 16) < kExpPolyPer16) {
+            exp2_poly_pair(s[j], s[j + 1], p0, p1);
+            if (partial) {
+              if (j < lo || j >= hi) p0 = 0.f;
+              if (j + 1 < lo || j + 1 >= hi) p1 = 0.f;
+            }
+          } else {
+            p0 = fast_exp2(s[j]);
+            p1 = fast_exp2(s[j + 1]);
           }
-          sum2 = f2_add(sum2, f2_add(f2_pack(s[j], s[j + 1]), f2_pack(s[j + 2], s[j + 3])));
+          sum2 = f2_add(sum2, f2_pack(p0, p1));
+          if constexpr (kFp8) {
+            uint16_t q;
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(q) : "f"(p1), "f"(p0));
+            if ((j & 2) == 0) pk[j / 4] = q;
+            else pk[j / 4] |= static_cast<uint32_t>(q) << 16;
+          } else {
+            pk[j / 2] = pack_bf16x2(p0, p1);
+          }
         }
         float sa, sb;
         f2_unpack(sum2, sa, sb);
         l_sum += sa + sb;
-        if constexpr (kFp8) {
-          uint32_t pk[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            uint16_t lo16, hi16;
-            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo16) : "f"(s[4 * j + 1]), "f"(s[4 * j]));
-            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi16) : "f"(s[4 * j + 3]), "f"(s[4 * j + 2]));
-            pk[j] = static_cast<uint32_t>(lo16) | (static_cast<uint32_t>(hi16) << 16);
-          }
-          tmem_st32(tP, pk);
-        } else {
-#pragma unroll
-          for (int half = 0; half < 2; ++half) {
-            uint32_t pk[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              pk[j] = pack_bf16x2(s[64 * half + 2 * j], s[64 * half + 2 * j + 1]);
-            tmem_st32(tP + half * 32, pk);
-          }
-        }
+        if (tr) H3SA_TRACE_AT(i, 5 * t + 3);
+        tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(pk));
+        if constexpr (!kFp8) tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(smem_u32(&sm.p_full[t]));
+        if (tr) H3SA_TRACE_AT(i, 5 * t + 4);
         ++c;
       }
       if (ok) ok = mbar_wait(smem_u32(&sm.o_done[t]), 0, abort_flag, p.err);
@@ -592,6 +630,13 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
 int attention_launch(const AttnLaunch& L, bool fp8, cudaStream_t stream) {
   return fp8 ? launch_attention<true>(L, stream) : launch_attention<false>(L, stream);
 }
+
+#ifdef H3SA_TRACE
+extern "C" H3SA_API int h3sa_trace_copy(void* host, size_t bytes) {
+  if (bytes > sizeof(g_h3sa_trace)) bytes = sizeof(g_h3sa_trace);
+  return cudaMemcpyFromSymbol(host, g_h3sa_trace, bytes) == cudaSuccess ? 0 : 3;
+}
+#endif
 
 size_t attention_smem_bytes(bool fp8) {
   return fp8 ? attn_smem_bytes<true>() : attn_smem_bytes<false>();

@@ -31,8 +31,14 @@ constexpr int kAttnThreads = 384;
 // setmaxnreg split: warps 0-3 (producer, MMA, two idle) keep kRegsControl registers, the two
 // softmax warpgroups get kRegsSoftmax. The sum must fit the launch allocation
 // (threads x registers per thread at launch, 168 under these launch bounds).
-constexpr int kRegsControl = 56;
-constexpr int kRegsSoftmax = 216;
+#ifndef H3SA_REGS_CONTROL
+#define H3SA_REGS_CONTROL 56
+#endif
+#ifndef H3SA_REGS_SOFTMAX
+#define H3SA_REGS_SOFTMAX 216
+#endif
+constexpr int kRegsControl = H3SA_REGS_CONTROL;
+constexpr int kRegsSoftmax = H3SA_REGS_SOFTMAX;
 constexpr int kRegSplitTotal = 128 * kRegsControl + 256 * kRegsSoftmax;
 constexpr int kMaxProblems = 4;
 constexpr int kMaxUnionBlocks = 2048;

@@ -1,0 +1,65 @@
+"""Seeded inputs shared by the golden generator and the tests (numpy PCG64 + bf16 RNE)."""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def bf16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even to bf16 values, returned as float32."""
+
+    b = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    b = (b + 0x7FFF + ((b >> 16) & 1)) & 0xFFFF0000
+    return b.astype(np.uint32).view(np.float32)
+
+
+def rms(x: np.ndarray) -> np.ndarray:
+    return (x / np.sqrt((x.astype(np.float64) ** 2).mean(axis=-1, keepdims=True) + 1e-5)).astype(np.float32)
+
+
+def hook_cpu_inputs(seed: int = 0, heads: int = 8, head_dim: int = 64, seq: int = 320,
+                    hist: int = 1024) -> dict:
+    """CPU benchmark configuration: q/k RMS-normalised N(0,1), v N(0,1), bf16 values.
+
+    Packed rows [16 text | 16 + 16 audio | 256 video | 16 pad] (seq 320), 1024 cached rows.
+    """
+
+    rng = np.random.default_rng(seed)
+    q = bf16(rms(rng.standard_normal((seq, heads, head_dim)).astype(np.float32)))
+    k = bf16(rms(rng.standard_normal((seq, heads, head_dim)).astype(np.float32)))
+    v = bf16(rng.standard_normal((seq, heads, head_dim)).astype(np.float32))
+    hist_k = bf16(rms(rng.standard_normal((hist, heads, head_dim)).astype(np.float32)))
+    hist_v = bf16(rng.standard_normal((hist, heads, head_dim)).astype(np.float32))
+    tags = np.full(seq, -1, dtype=np.int64)
+    tags[:16] = 1
+    tags[16:48] = 2
+    tags[48:304] = 0
+    return {"q": q, "k": k, "v": v, "hist_k": hist_k, "hist_v": hist_v, "token_tags": tags,
+            "commit_mask": (tags == 0) | (tags == 2), "cu_seqlens": [0, 304, 320],
+            "scale": head_dim ** -0.5}
+
+
+def fp8_input(seed: int = 5) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((1, 300, 3, 128)).astype(np.float32)
+    x = np.where(rng.random(x.shape) < 0.01, x * 8.0, x)
+    return bf16(x)
+
+
+def mask_inputs(seed: int = 3, heads: int = 2, nq: int = 384, nh: int = 1000) -> tuple[np.ndarray, np.ndarray]:
+    rng = np.random.default_rng(seed)
+    q = bf16(rng.standard_normal((1, heads, nq, 128)).astype(np.float32))
+    hk = bf16(rng.standard_normal((1, heads, nh, 128)).astype(np.float32))
+    return q, hk
+
+
+def prologue_inputs(seed: int = 11, seq: int = 128, heads: int = 4, head_dim: int = 128) -> dict:
+    rng = np.random.default_rng(seed)
+    qkv = bf16(rng.standard_normal((seq, 3 * heads * head_dim)).astype(np.float32) * 1.7)
+    q_w = bf16(1.0 + 0.1 * rng.standard_normal(head_dim).astype(np.float32))
+    k_w = bf16(1.0 + 0.1 * rng.standard_normal(head_dim).astype(np.float32))
+    return {"qkv": qkv, "q_weight": q_w, "k_weight": k_w}
+
+
+def ulysses_merged(rank: int, tokens: int = 6, heads: int = 4, d: int = 16) -> np.ndarray:
+    return np.random.default_rng(100 + rank).standard_normal((tokens, 3 * heads * d)).astype(np.float32)

@@ -1,0 +1,249 @@
+"""Generate the golden fixtures by running the REFERENCE's own Python code on CPU.
+
+Run in a checkout that has the reference sources (default /root/reference, override with
+H3SA_REFERENCE); the GPU box and the test suite only read the committed .npz outputs.
+
+    python tests/golden/make_golden.py
+
+Inputs come from numpy's PCG64 generator (platform independent) so the tests can rebuild
+them from the seeds recorded in each fixture. Fixtures:
+
+* prologue.npz   QK-RMSNorm + RoPE of a merged QKV shard through the reference's unfused
+                 CPU path (nn.RMSNorm, rope_cos_sin_cache, apply_rope_qk;
+                 T/model/layers.py:138-196) with positions from minimax_h3_packed_sequence.
+* hook_cpu.npz   the CPU benchmark configuration (H=8, d=64, 256 video + 32 audio queries,
+                 1024 cached + 288 current keys, 16 text rows) through the reference
+                 H3StreamingAttentionHook (T/streaming/attention_hook.py) with
+                 FlashAttention-3 replaced by torch SDPA (the math FA3 implements).
+* fp8.npz        quantize_fp8_e4m3_per_head (F/inference/fused_kernels.py:823-834).
+* mask.npz       _dynamic_history_mask (F/inference/dynamic_block_sparse.py:50-124).
+* cache.npz      CleanAVKVCache row tables through a commit / retain / audio-drop schedule
+                 (T/streaming/cache.py), rows tagged by (commit, local row) in the K values.
+* ulysses.npz    merged_qkv_sequence_to_heads / heads_to_sequence on two gloo ranks
+                 (T/distributed/ulysses.py).
+"""
+
+from __future__ import annotations
+
+import os
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+REF = Path(os.environ.get("H3SA_REFERENCE", "/root/reference"))
+sys.path.insert(0, str(HERE))
+
+from inputs import bf16, fp8_input, hook_cpu_inputs, mask_inputs, prologue_inputs, ulysses_merged  # noqa: E402
+
+
+def _import_reference():
+    sys.path.insert(0, str(REF / "src"))
+    sys.path.insert(0, str(REF / "src" / "taomate-fl2av" / "src"))
+    import torch
+
+    stub = types.ModuleType("flash_attn_interface")
+
+    def flash_attn_func(q, k, v, softmax_scale=None, causal=False, num_splits=1):
+        o = torch.nn.functional.scaled_dot_product_attention(
+            q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=softmax_scale,
+            is_causal=causal)
+        return o.transpose(1, 2)
+
+    stub.flash_attn_func = flash_attn_func
+    sys.modules["flash_attn_interface"] = stub
+
+
+# ----------------------------------------------------------------------------- prologue
+def make_prologue(path: Path) -> None:
+    import torch
+    from taomate_h3.model.layers import MiniMaxH3Rope, apply_rope_qk, rope_cos_sin_cache
+    from taomate_h3.model.packed_sequence import minimax_h3_packed_sequence
+
+    seed, heads, head_dim, per_axis = 11, 4, 128, 16
+    layout = minimax_h3_packed_sequence(text_len=16, latent_t=2, latent_h=8, latent_w=12,
+                                        audio_t=8)
+    seq = int(layout["seq_len"])
+    inp = prologue_inputs(seed, seq, heads, head_dim)
+    qkv, q_w, k_w = inp["qkv"], inp["q_weight"], inp["k_weight"]
+    inv_freq = (10000.0 ** (-2.0 * np.arange(per_axis) / (2.0 * per_axis))).astype(np.float32)
+    rope = MiniMaxH3Rope(per_axis)
+    rope.inv_freq.copy_(torch.from_numpy(inv_freq))
+    freqs = rope(layout["img_position_ids"].unsqueeze(0))
+    cache = rope_cos_sin_cache(freqs, dtype=torch.bfloat16)
+    positions = torch.arange(seq)
+    t = torch.from_numpy(qkv).bfloat16().view(seq, 3, heads, head_dim)
+    q_norm = torch.nn.RMSNorm(head_dim, eps=1e-5, dtype=torch.bfloat16)
+    k_norm = torch.nn.RMSNorm(head_dim, eps=1e-5, dtype=torch.bfloat16)
+    with torch.no_grad():
+        q_norm.weight.copy_(torch.from_numpy(q_w))
+        k_norm.weight.copy_(torch.from_numpy(k_w))
+        q, k = apply_rope_qk(q_norm(t[:, 0]), k_norm(t[:, 1]), cache, positions)
+    bits = lambda t: t.contiguous().view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+    np.savez(path, seed=seed, heads=heads, head_dim=head_dim, per_axis=per_axis, seq=seq,
+             inv_freq=inv_freq, grid=layout["img_position_ids"].numpy(),
+             cos_sin_bf16=bits(cache), q_bf16=bits(q), k_bf16=bits(k))
+
+
+# ----------------------------------------------------------------------------- hook
+def make_hook(path: Path) -> None:
+    import torch
+    from taomate_h3.streaming.attention_hook import H3StreamingAttentionHook, HookMode
+    from taomate_h3.streaming.cache import AVKV, CleanAVKVCache, KVContract
+
+    seed = 0
+    inp = hook_cpu_inputs(seed)
+    heads, head_dim = inp["q"].shape[1:]
+    contract = KVContract(local_heads=heads, head_dim=head_dim, dtype=torch.float32,
+                          device_type="cpu")
+    cache = CleanAVKVCache(contract)
+    cache._history["blocks.0.attn"] = AVKV(torch.from_numpy(inp["hist_k"]),
+                                           torch.from_numpy(inp["hist_v"]))
+    hook = H3StreamingAttentionHook(cache)
+    hook.activate(HookMode.NOISY)
+
+    class Attn:
+        softmax_scale = inp["scale"]
+
+    out = hook(attention=Attn(), layer_name="blocks.0.attn", query=torch.from_numpy(inp["q"]),
+               key=torch.from_numpy(inp["k"]), value=torch.from_numpy(inp["v"]),
+               token_tags=torch.from_numpy(inp["token_tags"]),
+               commit_mask=torch.from_numpy(inp["commit_mask"]),
+               cu_seqlens_host=tuple(inp["cu_seqlens"])).numpy()
+    np.savez(path, seed=seed, rows=np.arange(0, out.shape[0], 4), out=out[::4],
+             out_sum=np.float64(out.astype(np.float64).sum()),
+             out_l2=np.float64(np.sqrt((out.astype(np.float64) ** 2).sum())),
+             receipt=np.array([hook.kernel_calls, hook.query_tokens, hook.key_tokens]))
+
+
+# ----------------------------------------------------------------------------- fp8
+def make_fp8(path: Path) -> None:
+    import torch
+    from digitalhuman_h3.inference.fused_kernels import quantize_fp8_e4m3_per_head
+
+    seed = 5
+    x = fp8_input(seed)
+    q, s = quantize_fp8_e4m3_per_head(torch.from_numpy(x).bfloat16())
+    np.savez(path, seed=seed, q=q.view(torch.uint8).numpy(), scale=s.numpy())
+
+
+# ----------------------------------------------------------------------------- mask
+def make_mask(path: Path) -> None:
+    import torch
+    from digitalhuman_h3.inference.dynamic_block_sparse import _dynamic_history_mask
+
+    seed, heads, nq, nh, extra, density = 3, 2, 384, 1000, 400, 0.3
+    q, hk = mask_inputs(seed, heads, nq, nh)
+    mask, receipt = _dynamic_history_mask(torch, query=torch.from_numpy(q),
+                                          history_key=torch.from_numpy(hk),
+                                          total_key_tokens=nh + extra, density=density,
+                                          block_size=128)
+    np.savez(path, seed=seed, heads=heads, nq=nq, nh=nh, total=nh + extra, density=density,
+             kv_num_blocks=mask.kv_num_blocks.numpy(), kv_indices=mask.kv_indices.numpy(),
+             selected=receipt["selected_history_blocks"])
+
+
+# ----------------------------------------------------------------------------- cache
+def make_cache(path: Path) -> None:
+    import torch
+    from taomate_h3.streaming.cache import MAIN_LAYER_NAMES, CleanAVKVCache, KVContract
+
+    rng = np.random.default_rng(9)
+    contract = KVContract(local_heads=1, head_dim=2, dtype=torch.float32, device_type="cpu")
+    cache = CleanAVKVCache(contract)
+    steps = []
+    schedule = ["commit", "retain", "commit", "retain", "commit", "retain", "commit", "retain",
+                "drop", "commit", "retain", "commit", "retain"]
+    serial = 0
+    for op in schedule:
+        if op == "commit":
+            text = 3 + int(rng.integers(0, 3))
+            audio = 2 * int(rng.integers(2, 5))
+            video = int(rng.integers(5, 12))
+            pad = int(rng.integers(0, 3))
+            tags = np.array([1] * text + [2] * audio + [0] * video + [-1] * pad)
+            commit = (tags == 0) | (tags == 2)
+            n = len(tags)
+            ids = np.zeros((n, 1, 2), dtype=np.float32)
+            staged = np.nonzero(commit)[0]
+            ids[staged, 0, 0] = serial
+            ids[staged, 0, 1] = np.arange(staged.size)
+            cache.begin_clean_commit(cache.committed_blocks)
+            for name in MAIN_LAYER_NAMES:
+                t = torch.from_numpy(ids)
+                cache.stage(name, t, t.clone(), torch.from_numpy(tags), torch.from_numpy(commit))
+            cache.commit()
+            steps.append(("commit", tags, serial))
+            serial += 1
+        elif op == "retain":
+            cache.retain_sink_and_recent_commits()
+            steps.append(("retain", None, None))
+        else:
+            removed = cache.drop_audio_history()
+            steps.append(("drop", None, removed))
+        hist = cache.history("blocks.0.attn")
+        rows = np.zeros((0, 2), dtype=np.int64) if hist is None else hist.key[:, 0, :].numpy().astype(np.int64)
+        steps[-1] = steps[-1] + (rows,)
+    arrays = {"ops": np.array([s[0] for s in steps])}
+    for i, (op, tags, extra, rows) in enumerate(steps):
+        if tags is not None:
+            arrays[f"tags_{i}"] = tags
+        if op == "drop":
+            arrays[f"removed_{i}"] = np.array(extra)
+        arrays[f"rows_{i}"] = rows
+    np.savez(path, **arrays)
+
+
+# ----------------------------------------------------------------------------- ulysses
+def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+    from taomate_h3.distributed.parallel import ParallelContext
+    from taomate_h3.distributed.ulysses import heads_to_sequence, merged_qkv_sequence_to_heads
+
+    sys.path.insert(0, str(HERE))
+    _import_reference()
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    ctx = ParallelContext(1, 0, world, rank, dist.group.WORLD, dist.group.WORLD)
+    tokens, heads, d = 6, 4, 16
+    merged = ulysses_merged(rank, tokens, heads, d)
+    q, k, v = merged_qkv_sequence_to_heads(torch.from_numpy(merged), num_heads=heads,
+                                           head_dim=d, context=ctx)
+    o = heads_to_sequence(q.contiguous(), context=ctx)
+    np.savez(os.path.join(out_dir, f"ulysses_rank{rank}.npz"), q=q.numpy(),
+             k=k.numpy(), v=v.numpy(), o=o.numpy())
+    dist.destroy_process_group()
+
+
+def make_ulysses(path: Path) -> None:
+    import socket
+    import tempfile
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_ulysses_worker, args=(2, port, tmp), nprocs=2, start_method="spawn")
+        parts = [np.load(os.path.join(tmp, f"ulysses_rank{r}.npz")) for r in range(2)]
+        np.savez(path, **{f"{key}{r}": parts[r][key] for r in range(2)
+                          for key in ("q", "k", "v", "o")})
+
+
+def main() -> None:
+    _import_reference()
+    makers = {"prologue.npz": make_prologue, "hook_cpu.npz": make_hook, "fp8.npz": make_fp8,
+              "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses}
+    for name, fn in makers.items():
+        fn(HERE / name)
+        print(f"wrote {name} ({(HERE / name).stat().st_size} bytes)")
+
+
+if __name__ == "__main__":
+    main()

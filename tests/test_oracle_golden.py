@@ -1,0 +1,154 @@
+"""Pin the CPU oracle against golden vectors produced by the reference's own code.
+
+The fixtures under tests/golden/ were written by tests/golden/make_golden.py, which runs the
+reference Python (CleanAVKVCache, H3StreamingAttentionHook, quantize_fp8_e4m3_per_head,
+_dynamic_history_mask, the RMSNorm/RoPE CPU path, Ulysses on two gloo ranks) on CPU.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+sys.path.insert(0, str(GOLDEN))
+
+from inputs import fp8_input, hook_cpu_inputs, mask_inputs, prologue_inputs, ulysses_merged  # noqa: E402
+
+from oracle import attention as oatt  # noqa: E402
+from oracle import block_mask as omask  # noqa: E402
+from oracle import cache_index as ocache  # noqa: E402
+from oracle import fp8 as ofp8  # noqa: E402
+from oracle import prologue as opro  # noqa: E402
+from oracle import ulysses as ouly  # noqa: E402
+
+
+def load(name: str) -> dict:
+    with np.load(GOLDEN / name) as f:
+        return {k: f[k] for k in f.files}
+
+
+def bf16_from_bits(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def ulp_distance_bf16(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    ia = (a.astype(np.float32).view(np.uint32) >> 16).astype(np.int64)
+    ib = (b.astype(np.float32).view(np.uint32) >> 16).astype(np.int64)
+    sa = np.where(ia & 0x8000, -(ia & 0x7FFF), ia)
+    sb = np.where(ib & 0x8000, -(ib & 0x7FFF), ib)
+    return np.abs(sa - sb)
+
+
+def test_fp8_quantiser_bit_exact() -> None:
+    g = load("fp8.npz")
+    q, scale = ofp8.quantize_fp8_e4m3_per_head(fp8_input(int(g["seed"])))
+    assert np.array_equal(scale, g["scale"])
+    assert np.array_equal(q, g["q"])
+
+
+def test_e4m3_encoder_matches_torch_cast() -> None:
+    rng = np.random.default_rng(1)
+    x = np.clip(rng.standard_normal(50000).astype(np.float32) * 40, -448, 448)
+    ref = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    assert np.array_equal(ofp8.e4m3_encode(x), ref)
+
+
+def test_dynamic_history_mask_matches_reference() -> None:
+    g = load("mask.npz")
+    q, hk = mask_inputs(int(g["seed"]), int(g["heads"]), int(g["nq"]), int(g["nh"]))
+    m = omask.dynamic_history_mask(q[0], hk[0], int(g["total"]), float(g["density"]))
+    assert np.array_equal(m["kv_num_blocks"], g["kv_num_blocks"][0])
+    assert np.array_equal(m["kv_indices"], g["kv_indices"][0])
+    # the cut is well away from fp32 rounding, so the reference's fp32 scores agree
+    full = int(g["nh"]) // 128
+    for h in range(m["scores"].shape[0]):
+        for j in range(m["scores"].shape[1]):
+            margin = omask.selection_margin(m["scores"][h, j], np.ones(full, bool), m["selected_count"])
+            assert margin > 1e-5
+
+
+def test_cache_rows_match_reference() -> None:
+    g = load("cache.npz")
+    cache = ocache.CacheIndexOracle()
+    for i, op in enumerate(g["ops"]):
+        if op == "commit":
+            tags = g[f"tags_{i}"].tolist()
+            cache.commit(tags, [t in (0, 2) for t in tags])
+        elif op == "retain":
+            cache.retain_sink_and_recent_commits()
+        else:
+            assert cache.drop_audio_history() == int(g[f"removed_{i}"])
+        assert np.array_equal(np.array(cache.rows, dtype=np.int64).reshape(-1, 2), g[f"rows_{i}"])
+
+
+def test_ulysses_layouts_match_reference() -> None:
+    g = load("ulysses.npz")
+    merged = [ulysses_merged(r) for r in range(2)]
+    out = ouly.merged_qkv_sequence_to_heads(merged, num_heads=4, head_dim=16)
+    for r in range(2):
+        for i, key in enumerate("qkv"):
+            assert np.array_equal(out[r][i], g[f"{key}{r}"])
+    o = ouly.heads_to_sequence([out[r][0] for r in range(2)])
+    for r in range(2):
+        assert np.array_equal(o[r], g[f"o{r}"])
+
+
+def test_rope_cache_matches_reference() -> None:
+    g = load("prologue.npz")
+    cs = opro.rope_cos_sin(g["grid"], g["inv_freq"])
+    ref = bf16_from_bits(g["cos_sin_bf16"])
+    d = ulp_distance_bf16(cs, ref)
+    assert d.max() <= 1 and (d == 0).mean() > 0.999
+
+
+def test_prologue_matches_reference_cpu_path() -> None:
+    g = load("prologue.npz")
+    seq, heads, hd = int(g["seq"]), int(g["heads"]), int(g["head_dim"])
+    inp = prologue_inputs(int(g["seed"]), seq, heads, hd)
+    cs = bf16_from_bits(g["cos_sin_bf16"])
+    out = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, np.arange(seq),
+                             heads, hd, 1e-5).reshape(seq, 3, heads, hd)
+    for i, key in ((0, "q_bf16"), (1, "k_bf16")):
+        ref = bf16_from_bits(g[key])
+        d = ulp_distance_bf16(out[:, i], ref)
+        # the reference CPU path rounds RMSNorm before the weight product; the fused
+        # kernel semantics the oracle follows round once: at most one bf16 ulp apart
+        assert d.max() <= 2 and (d == 0).mean() > 0.97
+    assert np.array_equal(out[:, 2], inp["qkv"].reshape(seq, 3, heads, hd)[:, 2])
+
+
+def test_streaming_hook_matches_reference() -> None:
+    g = load("hook_cpu.npz")
+    inp = hook_cpu_inputs(int(g["seed"]))
+    out = oatt.streaming_hook_attention(
+        torch.from_numpy(inp["q"]), torch.from_numpy(inp["k"]), torch.from_numpy(inp["v"]),
+        torch.from_numpy(inp["commit_mask"]), inp["cu_seqlens"],
+        (torch.from_numpy(inp["hist_k"]), torch.from_numpy(inp["hist_v"])), inp["scale"]).numpy()
+    np.testing.assert_allclose(out[g["rows"]], g["out"], rtol=1e-5, atol=1e-6)
+    assert abs(out.astype(np.float64).sum() - float(g["out_sum"])) < 1e-3
+
+
+@pytest.mark.parametrize("density", [0.25, 0.5])
+def test_composite_mask_properties(density: float) -> None:
+    rng = np.random.default_rng(2)
+    h, nq, nh = 2, 700, 1024
+    q = rng.standard_normal((h, nq, 128)).astype(np.float32)
+    k = rng.standard_normal((h, nh + nq, 128)).astype(np.float32)
+    q_audio = np.zeros(nq, bool)
+    q_audio[:30] = True
+    k_audio = np.zeros(nh + nq, bool)
+    k_audio[nh:nh + 30] = True
+    m = omask.composite_mask(q, k, n_hist=nh, q_audio=q_audio, k_audio=k_audio, density=density)
+    kb = (nh + nq + 127) // 128
+    for hh in range(h):
+        for j in range(m["kv_num_blocks"].shape[1]):
+            keep = m["kv_indices"][hh, j, : m["kv_num_blocks"][hh, j]]
+            assert np.all(np.diff(keep) > 0) and keep.max() < kb
+            assert set(np.nonzero(m["forced"][j])[0]) <= set(keep.tolist())
+            assert keep.size == max(m["budget"], int(m["forced"][j].sum()))
+    assert m["kv_num_blocks"][:, 0].min() == kb  # the audio query block attends everywhere
