@@ -138,6 +138,53 @@ H3SA_API int h3sa_permute_rows(const void* src, void* dst, const int64_t* dims,
                                const int64_t* src_strides, const int64_t* dst_strides,
                                int32_t row_bytes, void* stream);
 
+/* QK-RMSNorm + rotate-half RoPE in place on merged QKV [tokens, 3, heads, head_dim] bf16
+ * (V untouched): inv = 1/sqrt(mean(v^2) + eps), n = bf16(v * inv * w), rope = bf16(bf16(n *
+ * cos) + bf16(rot(n) * sin)) on dims [0, rotary). cos_sin: bf16 [cache_rows, rotary] (cos in
+ * the first rotary/2 columns, sin in the rest); positions: int64 [tokens] rows of it.
+ * Replaces fused_qkv_qk_norm_rope_ (T/inference/fused_kernels.py:805-855). */
+H3SA_API int h3sa_qkv_norm_rope(void* qkv, const void* q_weight, const void* k_weight,
+                                const void* cos_sin, int32_t cache_rows, int32_t rotary,
+                                const int64_t* positions, int32_t tokens, int32_t heads,
+                                int32_t head_dim, float eps, int32_t* device_error, void* stream);
+
+/* The same prologue reading merged QKV and writing Q, K (normalised, rotated) and V into the
+ * Ulysses send layout [world, 3, tokens, heads/world, head_dim] in one pass: the prologue
+ * and the send-side permute of merged_qkv_sequence_to_heads (T/distributed/ulysses.py:
+ * 103-132) fused. */
+H3SA_API int h3sa_qkv_norm_rope_pack(const void* qkv, void* send, const void* q_weight,
+                                     const void* k_weight, const void* cos_sin,
+                                     int32_t cache_rows, int32_t rotary,
+                                     const int64_t* positions, int32_t tokens, int32_t heads,
+                                     int32_t head_dim, int32_t world, float eps,
+                                     int32_t* device_error, void* stream);
+
+/* Block-sparse selection policy for h3sa_block_mask. */
+typedef struct h3sa_mask_policy {
+  int32_t mode;                   /* 0: history top-k, 1: composite */
+  int32_t n_hist;                 /* history rows: logical KV rows [0, n_hist) */
+  int32_t n_kv;                   /* logical KV rows of the attention */
+  int32_t sinks;                  /* mode 1: leading KV blocks always kept */
+  int32_t window;                 /* mode 1: +- band of KV blocks around a query block */
+  int32_t reserved;
+  double density;                 /* (0, 1] */
+  const uint8_t* q_block_audio;   /* mode 1: [q blocks] 1 if the block holds an audio query */
+  const uint8_t* kv_block_audio;  /* mode 1: [KV blocks] 1 if the block holds an audio key */
+} h3sa_mask_policy;
+
+/* Per (head, 128-row query block of rows [q_lo, q_hi)) KV block selection written as the
+ * flex BlockMask inputs kv_num_blocks int32 [heads, q blocks] and kv_indices int32
+ * [heads, q blocks, kv_index_stride] (ascending, zero padded). Scores are block-mean dot
+ * products in fixed-order fp64; mode 0 restates _dynamic_history_mask
+ * (F/inference/dynamic_block_sparse.py:50-124). Uses fp64 block-mean scratch from the
+ * stream-ordered allocator. */
+H3SA_API int h3sa_block_mask(const void* query, int32_t rows, int32_t heads, int32_t head_dim,
+                             int32_t q_lo, int32_t q_hi, const void* key_pool,
+                             int32_t pool_pages, const int32_t* page_table,
+                             int32_t table_blocks, const h3sa_mask_policy* policy,
+                             int32_t* kv_num_blocks, int32_t* kv_indices,
+                             int32_t kv_index_stride, int32_t* device_error, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

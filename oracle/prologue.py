@@ -11,8 +11,9 @@ Restates, in numpy:
   normalized = bf16(v * rsqrt(mean(v^2) + eps) * w); rope = bf16(bf16(normalized * cos) +
   bf16(rotated * sin)) on dims [0, rotary), normalized elsewhere; V untouched.
 
-The variance is accumulated in fp64 and rounded once to fp32 here; a GPU kernel's fp32
-reduction order and reciprocal square root may move a result by one bf16 ulp.
+The sum of squares is exact (fp64), the mean is rounded to fp32, eps is added in fp32 as
+the reference adds it, and the reciprocal square root is evaluated in fp64 and rounded
+once, so a GPU kernel following the same steps reproduces these values bit for bit.
 """
 
 from __future__ import annotations
@@ -117,7 +118,8 @@ def qkv_norm_rope(qkv: np.ndarray, q_weight: np.ndarray, k_weight: np.ndarray,
     for qk, w in ((0, q_weight), (1, k_weight)):
         v = view[:, qk].astype(np.float32)                                  # [T, H, d]
         var = (v.astype(np.float64) ** 2).sum(axis=-1) / head_dim
-        inv = (1.0 / np.sqrt(var.astype(np.float32).astype(np.float64) + eps)).astype(np.float32)
+        ve = (var.astype(np.float32) + np.float32(eps)).astype(np.float32)
+        inv = (1.0 / np.sqrt(ve.astype(np.float64))).astype(np.float32)
         w = np.asarray(w, dtype=np.float32)
         normalized = round_bf16((v * inv[..., None]).astype(np.float32) * w)
         vp = v[..., np.where(rotating, partner, idx)]

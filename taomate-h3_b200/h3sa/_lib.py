@@ -37,6 +37,20 @@ class Problem(ctypes.Structure):
     ]
 
 
+class MaskPolicy(ctypes.Structure):
+    _fields_ = [
+        ("mode", ctypes.c_int32),
+        ("n_hist", ctypes.c_int32),
+        ("n_kv", ctypes.c_int32),
+        ("sinks", ctypes.c_int32),
+        ("window", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("density", ctypes.c_double),
+        ("q_block_audio", ctypes.c_void_p),
+        ("kv_block_audio", ctypes.c_void_p),
+    ]
+
+
 class Rows(ctypes.Structure):
     _fields_ = [
         ("base", ctypes.c_void_p),
@@ -73,6 +87,13 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     ),
     "h3sa_quantize_fp8_per_head": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "h3sa_quantize_fp8_pool": (ctypes.c_int, [_P, _P, _P, _I, _I, _P, _I, _I, _P, _P]),
+    "h3sa_qkv_norm_rope": (ctypes.c_int, [_P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _F, _P, _P]),
+    "h3sa_qkv_norm_rope_pack": (
+        ctypes.c_int, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _F, _P, _P]),
+    "h3sa_block_mask": (
+        ctypes.c_int,
+        [_P, _I, _I, _I, _I, _I, _P, _I, _P, _I, ctypes.POINTER(MaskPolicy), _P, _P, _I, _P, _P],
+    ),
     "h3sa_permute_rows": (
         ctypes.c_int,
         [_P, _P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),

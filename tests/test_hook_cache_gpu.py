@@ -1,0 +1,240 @@
+"""The drop-in hook and paged cache on the GPU, against the oracle and reference goldens.
+
+* Cache: the reference's own commit / retain / audio-drop schedule (tests/golden/cache.npz)
+  replayed through the paged cache; history row tables must match exactly.
+* Hook: the CPU benchmark configuration's structure (16 text, 32 audio, 256 video, 16 pad
+  rows, 1024 cached rows) at head_dim 128, dense / FP8 / block-sparse backends, contiguous
+  and scattered condition rows, NOISY and CLEAN_COMMIT modes.
+"""
+
+from __future__ import annotations
+
+import math
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+sys.path.insert(0, str(GOLDEN))
+
+from oracle import attention as oatt  # noqa: E402
+from oracle import block_mask as omask  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = 1e-2
+FP8_TOL = 3e-2
+
+
+def rel_l2(a: torch.Tensor, b: torch.Tensor) -> float:
+    return float((a.float().cpu() - b.float().cpu()).norm() / b.float().cpu().norm())
+
+
+class Attn:
+    softmax_scale = 128 ** -0.5
+
+
+def test_cache_schedule_matches_reference_golden() -> None:
+    from h3sa.cache import MAIN_LAYER_NAMES, CleanAVKVCache, KVContract
+
+    with np.load(GOLDEN / "cache.npz") as f:
+        g = {k: f[k] for k in f.files}
+    cache = CleanAVKVCache(KVContract(local_heads=1, head_dim=8), initial_pages=1)
+    serial = 0
+    for i, op in enumerate(g["ops"]):
+        if op == "commit":
+            tags = torch.from_numpy(g[f"tags_{i}"])
+            commit = (tags == 0) | (tags == 2)
+            ids = torch.zeros(len(tags), 1, 8)
+            staged = torch.nonzero(commit).flatten()
+            ids[staged, 0, 0] = serial
+            ids[staged, 0, 1] = torch.arange(staged.numel(), dtype=torch.float32)
+            kv = ids.to(torch.bfloat16).cuda()
+            cache.begin_clean_commit(cache.committed_blocks)
+            for name in MAIN_LAYER_NAMES:
+                cache.stage(name, kv, kv.clone(), tags.cuda(), commit.cuda())
+            cache.commit()
+            serial += 1
+        elif op == "retain":
+            cache.retain_sink_and_recent_commits()
+        else:
+            assert cache.drop_audio_history() == int(g[f"removed_{i}"])
+        for name in ("blocks.0.attn", "blocks.49.attn"):
+            hist = cache.history(name)
+            rows = np.zeros((0, 2), np.int64) if hist is None else \
+                hist.key[:, 0, :2].float().cpu().numpy().astype(np.int64)
+            assert np.array_equal(rows, g[f"rows_{i}"]), (i, op, name)
+        assert cache.history_tokens == g[f"rows_{i}"].shape[0]
+
+
+def _layout(heads: int, hist: int, scattered: bool, seed: int = 0) -> dict:
+    rng = np.random.default_rng(seed)
+    seq = 320
+    tags = np.full(seq, -1, np.int64)
+    tags[:16] = 1
+    tags[16:48] = 2
+    tags[48:304] = 0
+    if scattered:  # condition rows interleaved with media inside the live document
+        tags[:304] = np.concatenate([tags[16:48], tags[:8], tags[48:304], tags[8:16]])
+    def rms(x):
+        return x / np.sqrt((x ** 2).mean(-1, keepdims=True) + 1e-5)
+    t = lambda x: torch.from_numpy(x.astype(np.float32)).bfloat16().cuda()  # noqa: E731
+    return {
+        "q": t(rms(rng.standard_normal((seq, heads, 128)))),
+        "k": t(rms(rng.standard_normal((seq, heads, 128)))),
+        "v": t(rng.standard_normal((seq, heads, 128))),
+        "hist_k": t(rms(rng.standard_normal((hist, heads, 128)))),
+        "hist_v": t(rng.standard_normal((hist, heads, 128))),
+        "tags": torch.from_numpy(tags).cuda(),
+        "commit": torch.from_numpy((tags == 0) | (tags == 2)).cuda(),
+        "cu": (0, 304, 320),
+    }
+
+
+def _cache_with_history(heads: int, x: dict, layer: str = "blocks.0.attn"):
+    from h3sa.cache import CleanAVKVCache, KVContract
+
+    cache = CleanAVKVCache(KVContract(local_heads=heads, head_dim=128),
+                           layer_names=(layer,))
+    n = x["hist_k"].shape[0]
+    if n:
+        paged = cache.layer(layer)
+        paged.write(x["hist_k"], x["hist_v"], start=0, count=n)
+        paged.history_rows = n
+        cache._commit_token_counts.append(n)
+        cache._commit_token_tags.append(tuple([0] * n))
+    return cache
+
+
+def _oracle(x: dict, hist: bool = True) -> torch.Tensor:
+    return oatt.streaming_hook_attention(
+        x["q"].float().cpu(), x["k"].float().cpu(), x["v"].float().cpu(), x["commit"].cpu(),
+        x["cu"], (x["hist_k"].float().cpu(), x["hist_v"].float().cpu()) if hist else None,
+        Attn.softmax_scale)
+
+
+@pytest.mark.parametrize("scattered", [False, True])
+def test_hook_dense_matches_oracle(scattered: bool) -> None:
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads = 4
+    x = _layout(heads, 1024, scattered)
+    cache = _cache_with_history(heads, x)
+    hook = H3StreamingAttentionHook(cache)
+    hook.activate(HookMode.NOISY)
+    out = hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+               value=x["v"], token_tags=x["tags"], commit_mask=x["commit"],
+               cu_seqlens_host=x["cu"])
+    hook.check_device_error()
+    assert rel_l2(out, _oracle(x)) <= BF16_TOL
+    assert cache.history_rows("blocks.0.attn") == 1024  # NOISY never mutates history
+
+
+def test_hook_clean_commit_then_reads_new_history() -> None:
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads = 4
+    x = _layout(heads, 0, False, seed=5)
+    cache = _cache_with_history(heads, x)
+    hook = H3StreamingAttentionHook(cache)
+    cache.begin_clean_commit(cache.committed_blocks)
+    hook.activate(HookMode.CLEAN_COMMIT)
+    out = hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+               value=x["v"], token_tags=x["tags"], commit_mask=x["commit"],
+               cu_seqlens_host=x["cu"])
+    hook.deactivate()
+    cache.commit()
+    assert rel_l2(out, _oracle(x, hist=False)) <= BF16_TOL
+    hist = cache.history("blocks.0.attn")
+    media = torch.nonzero(x["commit"]).flatten()
+    assert torch.equal(hist.key, x["k"][media]) and torch.equal(hist.value, x["v"][media])
+    # next chunk attends to the committed media rows as history
+    y = _layout(heads, 0, False, seed=6)
+    hook.activate(HookMode.NOISY)
+    out2 = hook(attention=Attn(), layer_name="blocks.0.attn", query=y["q"], key=y["k"],
+                value=y["v"], token_tags=y["tags"], commit_mask=y["commit"],
+                cu_seqlens_host=y["cu"])
+    y["hist_k"], y["hist_v"] = hist.key, hist.value
+    assert rel_l2(out2, _oracle(y)) <= BF16_TOL
+
+
+def test_hook_fp8_dynamic_matches_dequantised_oracle() -> None:
+    import h3sa
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads = 4
+    x = _layout(heads, 1024, False, seed=2)
+    cache = _cache_with_history(heads, x)
+    hook = H3StreamingAttentionHook(cache, backend="flash_attn3_fp8_dynamic")
+    hook.activate(HookMode.NOISY)
+    out = hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+               value=x["v"], token_tags=x["tags"], commit_mask=x["commit"],
+               cu_seqlens_host=x["cu"])
+    hook.check_device_error()
+    # media rows: per-head e4m3 over [cond | history | media] K and V and over media Q
+    media = torch.arange(16, 304, device="cuda")  # audio + video rows of the live document
+    cond = torch.arange(0, 16, device="cuda")
+    k_all = torch.cat([x["k"][cond], x["hist_k"], x["k"][media]])
+    v_all = torch.cat([x["v"][cond], x["hist_v"], x["v"][media]])
+    deq = lambda t: (lambda q, s: q.float() * s.reshape(1, 1, -1, 1))(*h3sa.quantize_fp8_e4m3_per_head(t.unsqueeze(0)))  # noqa: E731
+    ref_media = oatt.attention(deq(x["q"][media])[0].cpu(), deq(k_all)[0].cpu(), deq(v_all)[0].cpu(),
+                               Attn.softmax_scale)
+    assert rel_l2(out[16:304], ref_media) <= FP8_TOL
+    full = _oracle(x)
+    assert rel_l2(out[:16], full[:16]) <= BF16_TOL
+
+
+def test_hook_block_sparse_matches_masked_oracle() -> None:
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads, hist = 2, 2048
+    x = _layout(heads, hist, False, seed=3)
+    cache = _cache_with_history(heads, x)
+    density = 0.3
+    hook = H3StreamingAttentionHook(cache, backend="flex_dynamic_blocksparse",
+                                    history_density=density)
+    hook.activate(HookMode.NOISY)
+    out = hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+               value=x["v"], token_tags=x["tags"], commit_mask=x["commit"],
+               cu_seqlens_host=x["cu"])
+    hook.check_device_error()
+    media = slice(16, 304)  # audio + video rows of the live document
+    q = x["q"][media].float().cpu()
+    # logical KV [history | media | cond], mask per the reference rule on that sequence
+    k_all = torch.cat([x["hist_k"], x["k"][media], x["k"][:16]]).float().cpu()
+    v_all = torch.cat([x["hist_v"], x["v"][media], x["v"][:16]]).float().cpu()
+    m = omask.dynamic_history_mask(q.numpy().transpose(1, 0, 2),
+                                   k_all[:hist].numpy().transpose(1, 0, 2), k_all.shape[0], density)
+    nq, nk = q.shape[0], k_all.shape[0]
+    allowed = torch.zeros(heads, nq, nk, dtype=torch.bool)
+    for h in range(heads):
+        for j in range(m["kv_num_blocks"].shape[1]):
+            for b in m["kv_indices"][h, j, : m["kv_num_blocks"][h, j]]:
+                allowed[h, j * 128:(j + 1) * 128, b * 128:(b + 1) * 128] = True
+    ref = oatt.attention(q, k_all, v_all, Attn.softmax_scale, allowed)
+    assert rel_l2(out[media], ref) <= BF16_TOL
+    assert math.isclose(float(m["selected_count"]), math.ceil(hist // 128 * density))
+
+
+def test_hook_rejects_like_reference() -> None:
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads = 4
+    x = _layout(heads, 0, False)
+    cache = _cache_with_history(heads, x)
+    hook = H3StreamingAttentionHook(cache)
+    with pytest.raises(RuntimeError, match="called while inactive"):
+        hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+             value=x["v"], token_tags=x["tags"], commit_mask=x["commit"], cu_seqlens_host=x["cu"])
+    hook.activate(HookMode.NOISY)
+    with pytest.raises(RuntimeError, match="invalid packed sequence boundaries"):
+        hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+             value=x["v"], token_tags=x["tags"], commit_mask=x["commit"], cu_seqlens_host=(0, 5))
+    two_live = x["commit"].clone()
+    two_live[310] = True
+    with pytest.raises(RuntimeError, match="exactly one live document"):
+        hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+             value=x["v"], token_tags=x["tags"], commit_mask=two_live, cu_seqlens_host=x["cu"])

@@ -1,0 +1,205 @@
+"""Host-side logic on CPU: C-ABI exports and validation, hook / cache / prologue errors.
+
+Nothing here launches a kernel: every call either returns a validation status from the C
+library before touching the device or raises in the Python layer before reaching it.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _lib():
+    import h3sa._lib as lib
+
+    return lib
+
+
+def test_every_declared_symbol_is_exported() -> None:
+    header = (ROOT / "include" / "h3sa.h").read_text()
+    declared = re.findall(r"H3SA_API\s+[\w\s\*]+?\b(h3sa_\w+)\s*\(", header)
+    assert len(declared) >= 12
+    lib = ctypes.CDLL(str(_lib().library_path()))
+    for name in declared:
+        assert hasattr(lib, name), name
+    assert set(declared) <= set(_lib().SIGNATURES)
+
+
+def test_abi_version_and_smem() -> None:
+    lib = _lib()
+    assert lib.LIB.h3sa_abi_version() == 1
+    assert 200_000 < lib.LIB.h3sa_attention_smem_bytes(0) <= 232_448
+    assert lib.LIB.h3sa_attention_smem_bytes(1) < lib.LIB.h3sa_attention_smem_bytes(0)
+
+
+def _attn(**over):
+    lib = _lib()
+    probs = (lib.Problem * 1)()
+    probs[0].q_lo, probs[0].q_hi, probs[0].kv_lo, probs[0].kv_hi = 0, 128, 0, 128
+    args = dict(query=16, out=32, rows=128, heads=2, head_dim=128, key=48, value=64, pages=1,
+                table=80, blocks=1, probs=probs, n=1)
+    args.update(over)
+    return lib.LIB.h3sa_attention_fwd(args["query"], args["out"], args["rows"], args["heads"],
+                                      args["head_dim"], args["key"], args["value"], args["pages"],
+                                      args["table"], args["blocks"], args["probs"], args["n"],
+                                      0.08, None, None, 0, 0, None, None)
+
+
+def test_attention_argument_validation() -> None:
+    lib = _lib()
+    assert _attn(head_dim=64) == lib.H3SA_ERR_UNSUPPORTED
+    assert "head_dim 128" in lib.last_error()
+    assert _attn(query=None) == lib.H3SA_ERR_INVALID
+    assert _attn(query=17) == lib.H3SA_ERR_INVALID and "16-byte aligned" in lib.last_error()
+    assert _attn(n=5) == lib.H3SA_ERR_INVALID
+    bad = (lib.Problem * 1)()
+    bad[0].q_lo, bad[0].q_hi, bad[0].kv_lo, bad[0].kv_hi = 0, 129, 0, 128
+    assert _attn(probs=bad) == lib.H3SA_ERR_INVALID and "query rows" in lib.last_error()
+    bad[0].q_hi, bad[0].kv_hi = 128, 200
+    assert _attn(probs=bad) == lib.H3SA_ERR_INVALID and "KV rows" in lib.last_error()
+    bad[0].kv_hi, bad[0].sparse = 128, 1
+    assert _attn(probs=bad) == lib.H3SA_ERR_INVALID and "block lists" in lib.last_error()
+
+
+def test_other_entry_validation() -> None:
+    lib = _lib()
+    L = lib.LIB
+    assert L.h3sa_quantize_fp8_per_head(16, 32, 48, 1, 10, 2, 64, None) == lib.H3SA_ERR_UNSUPPORTED
+    assert L.h3sa_quantize_fp8_per_head(16, 32, 48, 0, 10, 2, 128, None) == lib.H3SA_ERR_INVALID
+    rows = (lib.Rows * 3)()
+    assert L.h3sa_kv_copy_rows(rows, rows, 3, None, 0, None, 0, 1, 1, 256, None, None) == lib.H3SA_ERR_INVALID
+    assert L.h3sa_qkv_norm_rope(16, 32, 48, 64, 10, 7, 80, 4, 2, 128, 1e-5, None, None) == lib.H3SA_ERR_UNSUPPORTED
+    assert "rotary" in lib.last_error()
+    assert L.h3sa_qkv_norm_rope_pack(16, 32, 48, 64, 80, 10, 96, 96, 4, 6, 128, 4, 1e-5, None, None) == lib.H3SA_ERR_INVALID
+    assert "divisible by Ulysses" in lib.last_error()
+    pol = lib.MaskPolicy(mode=0, n_hist=1024, n_kv=2048, density=0.0)
+    assert L.h3sa_block_mask(16, 128, 2, 128, 0, 128, 32, 16, 48, 16, pol, 64, 80, 16, None, None) == lib.H3SA_ERR_INVALID
+    assert "density must be in (0, 1]" in lib.last_error()
+    pol = lib.MaskPolicy(mode=0, n_hist=100, n_kv=2048, density=0.5)
+    assert L.h3sa_block_mask(16, 128, 2, 128, 0, 128, 32, 16, 48, 16, pol, 64, 80, 16, None, None) == lib.H3SA_ERR_INVALID
+    assert "no complete K/V block" in lib.last_error()
+    dims = (ctypes.c_int64 * 4)(1, 1, 1, 1)
+    assert L.h3sa_permute_rows(16, 33, dims, dims, dims, 16, None) == lib.H3SA_ERR_INVALID
+
+
+class _Attn:
+    softmax_scale = 128 ** -0.5
+
+
+def _hook_args(q, **over):
+    args = dict(attention=_Attn(), layer_name="blocks.0.attn", query=q, key=q, value=q,
+                token_tags=torch.zeros(q.shape[0], dtype=torch.long),
+                commit_mask=torch.ones(q.shape[0], dtype=torch.bool), cu_seqlens_host=(0, q.shape[0]))
+    args.update(over)
+    return args
+
+
+def test_hook_validation_messages_match_reference() -> None:
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    hook = H3StreamingAttentionHook(CleanAVKVCache(KVContract(local_heads=2, head_dim=128)))
+    q = torch.zeros(8, 2, 128, dtype=torch.bfloat16)
+    with pytest.raises(RuntimeError, match="called while inactive"):
+        hook(**_hook_args(q))
+    hook.activate(HookMode.NOISY)
+    with pytest.raises(RuntimeError, match="already active"):
+        hook.activate(HookMode.NOISY)
+    with pytest.raises(RuntimeError, match="requires cuda QKV"):
+        hook(**_hook_args(q))
+    with pytest.raises(RuntimeError, match="expected local attention tail"):
+        hook(**_hook_args(torch.zeros(8, 3, 128, dtype=torch.bfloat16)))
+    with pytest.raises(RuntimeError, match="requires torch.bfloat16 QKV"):
+        hook(**_hook_args(torch.zeros(8, 2, 128)))
+    hook.deactivate()
+    with pytest.raises(ValueError, match="unsupported streaming hook mode"):
+        hook.activate(HookMode.IDLE)
+    with pytest.raises(ValueError, match="unsupported H3 streaming attention backend"):
+        H3StreamingAttentionHook(hook.cache, backend="sage_attn")
+
+
+def test_cache_transactions_match_reference() -> None:
+    from h3sa.cache import CleanAVKVCache, KVContract
+
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128))
+    q = torch.zeros(4, 2, 128, dtype=torch.bfloat16)
+    tags = torch.tensor([1, 2, 0, 0])
+    mask = tags >= 0
+    with pytest.raises(RuntimeError, match="begin_clean_commit"):
+        cache.stage("blocks.0.attn", q, q, tags, mask)
+    with pytest.raises(RuntimeError, match="no clean KV commit is active"):
+        cache.commit()
+    with pytest.raises(RuntimeError, match="expected clean chunk 0, got 3"):
+        cache.begin_clean_commit(3)
+    cache.begin_clean_commit(0)
+    with pytest.raises(RuntimeError, match="already active"):
+        cache.begin_clean_commit(0)
+    with pytest.raises(KeyError, match="unexpected transformer layer"):
+        cache.stage("blocks.50.attn", q, q, tags, mask)
+    with pytest.raises(RuntimeError, match="matching rank-3 shapes"):
+        cache.stage("blocks.0.attn", q[0], q[0], tags, mask)
+    with pytest.raises(RuntimeError, match="packed metadata length"):
+        cache.stage("blocks.0.attn", q, q, tags[:3], mask[:3])
+    with pytest.raises(RuntimeError, match="cannot trim persistent KV"):
+        cache.retain_sink_and_recent_commits()
+    with pytest.raises(RuntimeError, match="cannot drop audio history"):
+        cache.drop_audio_history()
+    with pytest.raises(RuntimeError, match="missing 50 transformer layers"):
+        cache.commit()
+    cache.rollback()
+    assert not cache.clean_commit_active and cache.committed_blocks == 0
+
+
+def test_cache_retained_rows_match_oracle() -> None:
+    from h3sa.cache import CleanAVKVCache, KVContract
+
+    from oracle.cache_index import CacheIndexOracle
+
+    cache = CleanAVKVCache(KVContract(local_heads=1, head_dim=8))
+    oracle = CacheIndexOracle()
+    for n_audio, n_video in ((4, 6), (2, 9), (6, 3), (4, 4)):
+        tags = [2] * n_audio + [0] * n_video
+        oracle.commit(tags, [True] * len(tags))
+        cache._commit_token_counts.append(len(tags))
+        cache._commit_token_tags.append(tuple(tags))
+    sel = [(0, True), (2, False), (3, False)]
+    rows, counts, kept = cache.retained_rows(sel)
+    oracle._retain(sel)
+    assert [divmod(r, 1) for r in rows] and len(rows) == oracle.history_tokens
+    assert counts == oracle.counts and kept == oracle.tags
+
+
+def test_prologue_validation_messages() -> None:
+    from h3sa.prologue import fused_qkv_qk_norm_rope_
+
+    w = torch.ones(128, dtype=torch.bfloat16)
+    cs = torch.zeros(4, 96, dtype=torch.bfloat16)
+    qkv = torch.zeros(4, 3 * 2 * 128, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="contiguous"):
+        fused_qkv_qk_norm_rope_(qkv.t(), w, w, cs, torch.arange(4), 1e-5)
+    with pytest.raises(ValueError, match="BF16"):
+        fused_qkv_qk_norm_rope_(qkv.float(), w, w, cs, torch.arange(4), 1e-5)
+    with pytest.raises(ValueError, match="three complete projections"):
+        fused_qkv_qk_norm_rope_(torch.zeros(4, 700, dtype=torch.bfloat16), w, w, cs, torch.arange(4), 1e-5)
+    with pytest.raises(ValueError, match="positions do not cover"):
+        fused_qkv_qk_norm_rope_(qkv, w, w, cs, torch.arange(3), 1e-5)
+    with pytest.raises(ValueError, match="cache span is invalid"):
+        fused_qkv_qk_norm_rope_(qkv, w, w, torch.zeros(4, 97, dtype=torch.bfloat16), torch.arange(4), 1e-5)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        fused_qkv_qk_norm_rope_(qkv, w, w, cs, torch.arange(4), 1e-5)
+
+
+def test_parallel_context_validation() -> None:
+    from h3sa.ulysses import ParallelContext
+
+    with pytest.raises(ValueError, match="invalid ulysses topology"):
+        ParallelContext(1, 0, 2, 2, object(), object())
+    with pytest.raises(ValueError, match="process groups are required"):
+        ParallelContext(1, 0, 2, 1, None, object())

@@ -1,0 +1,264 @@
+"""GPU parity of the feeding kernels against the oracle and the reference golden vectors.
+
+Bit-exact: e4m3 quantiser, block masks, Ulysses layouts, KV row copies, prologue (against
+the oracle, which follows the same exact arithmetic); the prologue against the reference's
+own CPU path is held to the same agreement as the oracle (<= 1 bf16 ulp, >= 99.9% exact).
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+sys.path.insert(0, str(GOLDEN))
+
+from inputs import fp8_input, mask_inputs, prologue_inputs  # noqa: E402
+
+from oracle import block_mask as omask  # noqa: E402
+from oracle import fp8 as ofp8  # noqa: E402
+from oracle import prologue as opro  # noqa: E402
+from oracle import ulysses as ouly  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _g(name: str) -> dict:
+    with np.load(GOLDEN / name) as f:
+        return {k: f[k] for k in f.files}
+
+
+def _bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def _cuda_bf16(x: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(torch.bfloat16).cuda()
+
+
+def test_fp8_quantiser_bit_exact_vs_reference() -> None:
+    import h3sa
+
+    g = _g("fp8.npz")
+    x = _cuda_bf16(fp8_input(int(g["seed"])))
+    q, s = h3sa.quantize_fp8_e4m3_per_head(x)
+    torch.cuda.synchronize()
+    assert np.array_equal(s.cpu().numpy(), g["scale"])
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), g["q"])
+
+
+@pytest.mark.parametrize("shape", [(2, 1, 5, 128), (1, 1000, 7, 128), (1, 257, 3, 128)])
+def test_fp8_quantiser_vs_oracle(shape: tuple[int, ...]) -> None:
+    import h3sa
+
+    rng = np.random.default_rng(sum(shape))
+    x = rng.standard_normal(shape).astype(np.float32) * 3
+    xb = _cuda_bf16(x)
+    q, s = h3sa.quantize_fp8_e4m3_per_head(xb)
+    oq, os_ = ofp8.quantize_fp8_e4m3_per_head(xb.float().cpu().numpy())
+    assert np.array_equal(s.cpu().numpy(), os_)
+    assert np.array_equal(q.view(torch.uint8).cpu().numpy(), oq)
+
+
+def test_fp8_pool_quantiser_matches_packed() -> None:
+    """Quantising logical rows through a shuffled page table == quantising the packed rows."""
+
+    import h3sa
+
+    rng = np.random.default_rng(4)
+    rows, heads = 1000, 3
+    x = _cuda_bf16(rng.standard_normal((rows, heads, 128)).astype(np.float32))
+    pages = 12
+    table = torch.randperm(pages)[:8].to(torch.int32).cuda()
+    pool = torch.zeros(heads, pages * 128, 128, dtype=torch.bfloat16, device="cuda")
+    h3sa.kv_copy_rows([x], [pool], count=rows, dst_table=table)
+    pool8 = torch.zeros_like(pool, dtype=torch.float8_e4m3fn)
+    scale = torch.empty(heads, dtype=torch.float32, device="cuda")
+    h3sa.quantize_fp8_pool(pool, pool8, scale, table, rows)
+    back = torch.empty(rows, heads, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    h3sa.kv_copy_rows([pool8], [back], count=rows, src_table=table)
+    q, s = h3sa.quantize_fp8_e4m3_per_head(x.unsqueeze(0))
+    assert torch.equal(scale, s.reshape(-1))
+    assert torch.equal(back.view(torch.uint8), q.squeeze(0).view(torch.uint8))
+
+
+def _paged(keys: np.ndarray, shuffle: bool = True):
+    """Logical rows [N, H, d] into a paged pool object with key/table attributes."""
+
+    import h3sa
+
+    n, heads, _ = keys.shape
+    blocks = (n + 127) // 128
+    pages = blocks + 3
+    table = (torch.randperm(pages)[:blocks] if shuffle else torch.arange(blocks)).to(torch.int32).cuda()
+    pool = torch.zeros(heads, pages * 128, 128, dtype=torch.bfloat16, device="cuda")
+    h3sa.kv_copy_rows([_cuda_bf16(keys)], [pool], count=n, dst_table=table)
+
+    class P:
+        key = pool
+        value = pool
+
+    P.table = table
+    return P
+
+
+def test_history_mask_matches_reference_golden() -> None:
+    from h3sa.block_sparse import history_block_mask
+
+    g = _g("mask.npz")
+    q, hk = mask_inputs(int(g["seed"]), int(g["heads"]), int(g["nq"]), int(g["nh"]))
+    nq, nh, total = int(g["nq"]), int(g["nh"]), int(g["total"])
+    extra = np.random.default_rng(0).standard_normal((int(g["heads"]), total - nh, 128)).astype(np.float32)
+    keys = np.concatenate([hk[0], extra], axis=1).transpose(1, 0, 2)       # [N, H, d]
+    paged = _paged(keys)
+    query = _cuda_bf16(q[0].transpose(1, 0, 2))                            # [nq, H, d]
+    num, idx = history_block_mask(query, paged, q_lo=0, q_hi=nq, n_hist=nh, n_kv=total,
+                                  density=float(g["density"]))
+    torch.cuda.synchronize()
+    assert np.array_equal(num.cpu().numpy(), g["kv_num_blocks"][0])
+    assert np.array_equal(idx.cpu().numpy(), g["kv_indices"][0])
+
+
+@pytest.mark.parametrize("nq,nh,density", [(700, 1024, 0.25), (300, 1500, 0.5), (129, 2048, 0.1)])
+def test_composite_mask_bit_exact_vs_oracle(nq: int, nh: int, density: float) -> None:
+    from h3sa.block_sparse import block_flags, composite_block_mask
+
+    rng = np.random.default_rng(nq + nh)
+    heads = 3
+    q = (rng.standard_normal((nq, heads, 128)) * 0.7).astype(np.float32)
+    k = rng.standard_normal((nh + nq, heads, 128)).astype(np.float32)
+    qb = torch.from_numpy(q).bfloat16().float().numpy()
+    kb = torch.from_numpy(k).bfloat16().float().numpy()
+    q_audio = np.zeros(nq, bool)
+    q_audio[: min(40, nq)] = True
+    k_audio = np.zeros(nh + nq, bool)
+    k_audio[:20] = True
+    k_audio[nh:nh + min(40, nq)] = True
+    ref = omask.composite_mask(qb.transpose(1, 0, 2), kb.transpose(1, 0, 2), n_hist=nh,
+                               q_audio=q_audio, k_audio=k_audio, density=density)
+    paged = _paged(k)
+    num, idx = composite_block_mask(
+        _cuda_bf16(q), paged, q_lo=0, q_hi=nq, n_hist=nh, n_kv=nh + nq,
+        q_block_audio=block_flags(torch.from_numpy(q_audio), nq),
+        kv_block_audio=block_flags(torch.from_numpy(k_audio), nh + nq), density=density)
+    torch.cuda.synchronize()
+    assert np.array_equal(num.cpu().numpy(), ref["kv_num_blocks"])
+    assert np.array_equal(idx.cpu().numpy(), ref["kv_indices"])
+
+
+@pytest.mark.parametrize("nq,nh,density", [(512, 1280, 0.3), (1000, 3000, 0.5), (200, 4096, 0.05)])
+def test_history_mask_bit_exact_vs_oracle(nq: int, nh: int, density: float) -> None:
+    from h3sa.block_sparse import history_block_mask
+
+    rng = np.random.default_rng(nq * 3 + nh)
+    heads = 2
+    q = torch.from_numpy(rng.standard_normal((nq, heads, 128)).astype(np.float32)).bfloat16().float().numpy()
+    k = torch.from_numpy(rng.standard_normal((nh + nq + 64, heads, 128)).astype(np.float32)).bfloat16().float().numpy()
+    ref = omask.dynamic_history_mask(q.transpose(1, 0, 2), k[:nh].transpose(1, 0, 2),
+                                     k.shape[0], density)
+    num, idx = history_block_mask(_cuda_bf16(q), _paged(k), q_lo=0, q_hi=nq, n_hist=nh,
+                                  n_kv=k.shape[0], density=density)
+    torch.cuda.synchronize()
+    assert np.array_equal(num.cpu().numpy(), ref["kv_num_blocks"])
+    assert np.array_equal(idx.cpu().numpy(), ref["kv_indices"])
+
+
+def _prologue_case(seq: int, heads: int, seed: int = 11):
+    inp = prologue_inputs(seed, seq, heads, 128)
+    layout = opro.packed_layout(text_len=16, latent_t=2, latent_h=8, latent_w=12, audio_t=8)
+    grid = layout["grid"][:seq] if seq <= layout["seq_len"] else np.resize(layout["grid"], (seq, 3))
+    cs = opro.rope_cos_sin(grid, opro.default_inv_freq(16))
+    return inp, cs
+
+
+def test_prologue_bit_exact_vs_oracle_and_golden() -> None:
+    from h3sa.prologue import fused_qkv_qk_norm_rope_
+
+    g = _g("prologue.npz")
+    seq, heads = int(g["seq"]), int(g["heads"])
+    inp = prologue_inputs(int(g["seed"]), seq, heads, 128)
+    cs = _bf16_bits_to_f32(g["cos_sin_bf16"])
+    qkv = _cuda_bf16(inp["qkv"])
+    fused_qkv_qk_norm_rope_(qkv, _cuda_bf16(inp["q_weight"]), _cuda_bf16(inp["k_weight"]),
+                            _cuda_bf16(cs), torch.arange(seq, device="cuda"), 1e-5)
+    out = qkv.float().cpu().numpy()
+    ref = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, np.arange(seq),
+                             heads, 128, 1e-5)
+    assert np.array_equal(out, ref)
+    view = out.reshape(seq, 3, heads, 128)
+    for i, key in ((0, "q_bf16"), (1, "k_bf16")):
+        gold = _bf16_bits_to_f32(g[key])
+        diff = np.abs(view[:, i] - gold)
+        assert (diff == 0).mean() > 0.999
+        assert np.all(diff <= np.abs(gold) * 2.0 ** -7 + 1e-30)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_prologue_pack_matches_oracle_send_layout(world: int) -> None:
+    from h3sa.prologue import qkv_norm_rope_pack
+
+    seq, heads = 96, 8
+    inp, cs = _prologue_case(seq, heads, seed=3)
+    pos = np.random.default_rng(1).integers(0, cs.shape[0], seq)
+    send = qkv_norm_rope_pack(_cuda_bf16(inp["qkv"]), _cuda_bf16(inp["q_weight"]),
+                              _cuda_bf16(inp["k_weight"]), _cuda_bf16(cs),
+                              torch.from_numpy(pos).cuda(), 1e-5, world=world)
+    ref = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, pos, heads, 128, 1e-5)
+    expect = ref.reshape(seq, 3, world, heads // world, 128).transpose(2, 1, 0, 3, 4)
+    assert np.array_equal(send.float().cpu().numpy(), expect)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_ulysses_layouts_vs_oracle(world: int) -> None:
+    """Pack -> emulated all-to-all -> unpack on one GPU equals the oracle's every-rank view."""
+
+    from h3sa.ulysses import pack_qkv_send, unpack_o_recv, unpack_qkv_recv
+
+    tokens, heads, d = 10, 16, 128
+    hl = heads // world
+    rng = np.random.default_rng(world)
+    merged = [rng.standard_normal((tokens, 3 * heads * d)).astype(np.float32) for _ in range(world)]
+    mb = [torch.from_numpy(m).bfloat16().float().numpy() for m in merged]
+    sends = []
+    for r in range(world):
+        s = torch.empty(world, 3, tokens, hl, d, dtype=torch.bfloat16, device="cuda")
+        pack_qkv_send(_cuda_bf16(mb[r]), s, world=world, num_heads=heads, head_dim=d)
+        sends.append(s)
+    expect = ouly.merged_qkv_sequence_to_heads(mb, heads, d)
+    outs = []
+    for r in range(world):
+        recv = torch.stack([sends[s][r] for s in range(world)])
+        out = torch.empty(3, world * tokens, hl, d, dtype=torch.bfloat16, device="cuda")
+        unpack_qkv_recv(recv, out, world=world, tokens=tokens, local_heads=hl, head_dim=d)
+        for i in range(3):
+            assert np.array_equal(out[i].float().cpu().numpy(), expect[r][i])
+        outs.append(out[0])
+    expect_o = ouly.heads_to_sequence([e[0] for e in expect])
+    for r in range(world):
+        recv = torch.stack([outs[s].view(world, tokens, hl, d)[r] for s in range(world)])
+        o = torch.empty(tokens, heads, d, dtype=torch.bfloat16, device="cuda")
+        unpack_o_recv(recv, o, world=world, tokens=tokens, local_heads=hl, head_dim=d)
+        assert np.array_equal(o.float().cpu().numpy(), expect_o[r])
+
+
+def test_kv_copy_rows_index_and_bounds() -> None:
+    import h3sa
+
+    rows, heads = 300, 3
+    x = torch.randn(rows, heads, 128, device="cuda").bfloat16()
+    table = torch.tensor([5, 1, 4], dtype=torch.int32, device="cuda")
+    pool = torch.zeros(heads, 6 * 128, 128, dtype=torch.bfloat16, device="cuda")
+    idx = torch.randperm(rows)[:200].to(torch.int32).cuda()
+    h3sa.kv_copy_rows([x], [pool], count=200, src_index=idx, dst_table=table, dst_start=50)
+    back = torch.empty(200, heads, 128, dtype=torch.bfloat16, device="cuda")
+    h3sa.kv_copy_rows([pool], [back], count=200, src_table=table, src_start=50)
+    assert torch.equal(back, x[idx.long()])
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    bad = torch.tensor([0, rows + 5], dtype=torch.int32, device="cuda")
+    h3sa.kv_copy_rows([x], [pool], count=2, src_index=bad, dst_table=table, device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 4

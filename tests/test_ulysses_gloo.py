@@ -1,0 +1,70 @@
+"""The N > 1 exchange on two CPU ranks (gloo): the oracle's every-rank emulation of the
+Ulysses all-to-all equals a real all_to_all_single of its send layouts, and the Ulysses
+entry points validate their arguments under a live process group like the reference."""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    sys.path.insert(0, str(ROOT))
+    sys.path.insert(0, str(ROOT / "taomate-h3_b200"))
+    from h3sa.ulysses import ParallelContext, merged_qkv_sequence_to_heads
+
+    from oracle import ulysses as ouly
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    tokens, heads, d = 5, 4, 8
+    merged = [np.random.default_rng(50 + r).standard_normal((tokens, 3 * heads * d)).astype(np.float32)
+              for r in range(world)]
+    hl = heads // world
+    send = torch.from_numpy(merged[rank].reshape(tokens, 3, world, hl, d)
+                            .transpose(2, 1, 0, 3, 4).copy())
+    recv = torch.empty_like(send)
+    dist.all_to_all_single(recv, send)
+    got = recv.permute(1, 0, 2, 3, 4).reshape(3, world * tokens, hl, d).numpy()
+    expect = ouly.merged_qkv_sequence_to_heads(merged, heads, d)[rank]
+    ok = all(np.array_equal(got[i], expect[i]) for i in range(3))
+    # argument validation happens before any device work, under the live group
+    ctx = ParallelContext(1, 0, world, rank, dist.group.WORLD, dist.group.WORLD)
+    msg = ""
+    try:
+        merged_qkv_sequence_to_heads(torch.zeros(tokens, 3 * 3 * d), num_heads=3, head_dim=d, context=ctx)
+    except ValueError as exc:
+        msg = str(exc)
+    try:
+        merged_qkv_sequence_to_heads(torch.zeros(tokens, 7), num_heads=3, head_dim=d, context=ctx)
+    except ValueError as exc:
+        msg += "|" + str(exc)
+    t = torch.tensor([float(rank + 1)])
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    np.save(os.path.join(out_dir, f"r{rank}.npy"), np.array([ok, t.item() == world], dtype=bool))
+    with open(os.path.join(out_dir, f"m{rank}.txt"), "w") as f:
+        f.write(msg)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_rank_exchange_and_validation(tmp_path: Path) -> None:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    mp.start_processes(_worker, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
+    for r in range(2):
+        assert np.load(tmp_path / f"r{r}.npy").all()
+        msg = (tmp_path / f"m{r}.txt").read_text()
+        assert "merged QKV heads are not divisible by Ulysses" in msg
+        assert "merged QKV width differs" in msg
