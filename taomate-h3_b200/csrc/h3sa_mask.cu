@@ -44,7 +44,7 @@ struct MaskParams {
   int full_hist, keep_count, budget;
   double scale;
   double* q_mean;                 // [H, QB, d]
-  double* k_mean;                 // [H, kb_means, d]
+  double* k_mean;                 // [H, d, kb_means] (d-major: the score loop reads it coalesced)
   int* kv_num_blocks;
   int* kv_indices;
   int stride;
@@ -61,9 +61,19 @@ __global__ void __launch_bounds__(128) mask_means_kernel(const MaskParams p) {
   if (blk < p.qb) {
     const int r0 = p.q_lo + blk * kBlockM;
     const int r1 = min(r0 + kBlockM, p.q_hi);
-    for (int r = r0; r < r1; ++r)
-      sum += static_cast<double>(
-          __bfloat162float(p.query[(static_cast<size_t>(r) * p.heads + h) * kHeadDim + d]));
+    // four independent partial sums: exact in fp64, so their order does not matter
+    const __nv_bfloat16* qb = p.query + static_cast<size_t>(h) * kHeadDim + d;
+    const size_t rs = static_cast<size_t>(p.heads) * kHeadDim;
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    int r = r0;
+    for (; r + 4 <= r1; r += 4) {
+      a0 += static_cast<double>(__bfloat162float(qb[(r + 0) * rs]));
+      a1 += static_cast<double>(__bfloat162float(qb[(r + 1) * rs]));
+      a2 += static_cast<double>(__bfloat162float(qb[(r + 2) * rs]));
+      a3 += static_cast<double>(__bfloat162float(qb[(r + 3) * rs]));
+    }
+    for (; r < r1; ++r) a0 += static_cast<double>(__bfloat162float(qb[r * rs]));
+    sum = (a0 + a1) + (a2 + a3);
     count = r1 - r0;
     p.q_mean[(static_cast<size_t>(h) * p.qb + blk) * kHeadDim + d] = sum / count;
   } else {
@@ -77,10 +87,19 @@ __global__ void __launch_bounds__(128) mask_means_kernel(const MaskParams p) {
     }
     const __nv_bfloat16* base =
         p.key_pool + ((static_cast<size_t>(h) * p.pool_pages + page) * kBlockN) * kHeadDim + d;
-    for (int r = r0; r < r1; ++r)
-      sum += static_cast<double>(__bfloat162float(base[static_cast<size_t>(r - r0) * kHeadDim]));
+    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+    const int n = r1 - r0;
+    int i = 0;
+    for (; i + 4 <= n; i += 4) {
+      a0 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 0) * kHeadDim]));
+      a1 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 1) * kHeadDim]));
+      a2 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 2) * kHeadDim]));
+      a3 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 3) * kHeadDim]));
+    }
+    for (; i < n; ++i) a0 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i) * kHeadDim]));
+    sum = (a0 + a1) + (a2 + a3);
     count = r1 - r0;
-    p.k_mean[(static_cast<size_t>(h) * p.kb_means + b) * kHeadDim + d] = sum / count;
+    p.k_mean[(static_cast<size_t>(h) * kHeadDim + d) * p.kb_means + b] = sum / count;
   }
 }
 
@@ -124,9 +143,11 @@ __global__ void __launch_bounds__(256) mask_select_kernel(const MaskParams p) {
   // scores of the candidates: sequential fp64 dot over d
   for (int b = tid; b < p.kb; b += blockDim.x) {
     if (!cand[b]) continue;
-    const double* km = p.k_mean + (static_cast<size_t>(h) * p.kb_means + b) * kHeadDim;
+    const double* km = p.k_mean + static_cast<size_t>(h) * kHeadDim * p.kb_means + b;
     double acc = 0.0;
-    for (int d = 0; d < kHeadDim; ++d) acc = __dadd_rn(acc, __dmul_rn(qm[d], km[d]));
+#pragma unroll 8
+    for (int d = 0; d < kHeadDim; ++d)
+      acc = __dadd_rn(acc, __dmul_rn(qm[d], km[static_cast<size_t>(d) * p.kb_means]));
     score[b] = __dmul_rn(acc, p.scale);
   }
   __syncthreads();

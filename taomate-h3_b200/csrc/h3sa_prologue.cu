@@ -5,8 +5,8 @@
 //   inv  = 1 / sqrt(mean(v^2) + eps)
 //   n    = bf16(v * inv * w)                          for every dim
 //   rope = bf16(bf16(n * cos) + bf16(rot(n) * sin))   for dims [0, rotary)
-// with rot(n)[i] = -n[i + rotary/2] (i < rotary/2), n[i - rotary/2] otherwise. One warp per
-// (token, head, q|k) row of 128 values, 4 per lane. The sum of squares is exact (each
+// with rot(n)[i] = -n[i + rotary/2] (i < rotary/2), n[i - rotary/2] otherwise. Half a warp per
+// (token, head, q|k) row of 128 values, 8 per lane. The sum of squares is exact (each
 // square of a bf16 value is exact in fp32 and the 128 of them sum exactly in fp64), so the
 // result does not depend on the reduction order; mean in fp64 rounded to fp32, eps added in
 // fp32 (as the reference adds it), reciprocal square root in IEEE fp64 rounded once to fp32.
@@ -46,77 +46,107 @@ __device__ __forceinline__ __nv_bfloat16* dst_row(const PrologueParams& p, int t
          (((static_cast<size_t>(w) * 3 + j) * p.tokens + t) * hl + (h - w * hl)) * kHeadDim;
 }
 
+// Half a warp per (token, head, plane) row: 16 lanes x 8 values. In place only the Q and K
+// planes are visited; the pack variant also copies V.
 __global__ void __launch_bounds__(256) qkv_norm_rope_kernel(const PrologueParams p) {
   const int lane = threadIdx.x & 31;
-  const long long warps = static_cast<long long>(gridDim.x) * (blockDim.x >> 5);
-  const long long total = static_cast<long long>(p.tokens) * p.heads * 3;
+  const int sub = lane & 15;                 // lane within the row
+  const int base_lane = lane & 16;           // first lane of this half-warp
+  const unsigned half_mask = 0xFFFFu << base_lane;
+  const int planes = (p.world > 1) ? 3 : 2;
+  const long long total = static_cast<long long>(p.tokens) * p.heads * planes;
+  const long long step = static_cast<long long>(gridDim.x) * (blockDim.x >> 4);
   const int half = p.rotary >> 1;
-  for (long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-       row < total; row += warps) {
-    const int j = static_cast<int>(row % 3);          // 0 q, 1 k, 2 v
-    const long long th = row / 3;
+  // this lane's 8 norm weights of each projection, read once
+  float wq[8], wk[8];
+  {
+    const uint4 a = reinterpret_cast<const uint4*>(p.q_weight)[sub];
+    const uint4 b = reinterpret_cast<const uint4*>(p.k_weight)[sub];
+    const uint32_t ua[4] = {a.x, a.y, a.z, a.w}, ub[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      wq[2 * i] = __uint_as_float(ua[i] << 16);
+      wq[2 * i + 1] = __uint_as_float(ua[i] & 0xFFFF0000u);
+      wk[2 * i] = __uint_as_float(ub[i] << 16);
+      wk[2 * i + 1] = __uint_as_float(ub[i] & 0xFFFF0000u);
+    }
+  }
+  const int d0 = 8 * sub;
+  const bool rotating = d0 < p.rotary;
+  const bool low = d0 < half;
+  const int partner = base_lane + (low ? sub + (half >> 3) : sub - (half >> 3));
+  const int phase = rotating ? (low ? d0 : d0 - half) : 0;
+  for (long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 4) + (threadIdx.x >> 4);
+       row < total; row += step) {
+    const int j = static_cast<int>(row % planes);   // 0 q, 1 k, 2 v (pack only)
+    const long long th = row / planes;
     const int h = static_cast<int>(th % p.heads);
     const int t = static_cast<int>(th / p.heads);
     const __nv_bfloat16* src = p.src + ((static_cast<size_t>(t) * 3 + j) * p.heads + h) * kHeadDim;
     __nv_bfloat16* dst = dst_row(p, t, j, h);
-    const uint2 raw = reinterpret_cast<const uint2*>(src)[lane];
-    if (j == 2) {  // V: copied (send layout) or untouched (in place)
-      if (dst != src) reinterpret_cast<uint2*>(dst)[lane] = raw;
+    const uint4 raw = reinterpret_cast<const uint4*>(src)[sub];
+    if (j == 2) {  // V into the send layout, unchanged
+      reinterpret_cast<uint4*>(dst)[sub] = raw;
       continue;
     }
-    float v[4];
-    v[0] = __uint_as_float(raw.x << 16);
-    v[1] = __uint_as_float(raw.x & 0xFFFF0000u);
-    v[2] = __uint_as_float(raw.y << 16);
-    v[3] = __uint_as_float(raw.y & 0xFFFF0000u);
+    const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = __uint_as_float(u[i] << 16);
+      v[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+    }
     double ss = 0.0;
 #pragma unroll
-    for (int e = 0; e < 4; ++e) ss += static_cast<double>(v[e] * v[e]);
+    for (int e = 0; e < 8; ++e) ss += static_cast<double>(v[e] * v[e]);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float var = static_cast<float>(ss / static_cast<double>(kHeadDim));
+    for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o, 16);
+    // mean of the exact sum (scaling by 1/128 is exact), eps added in fp32
+    const float var = static_cast<float>(ss * (1.0 / kHeadDim));
     const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(__fadd_rn(var, p.eps))));
-    const __nv_bfloat16* wp = (j == 0) ? p.q_weight : p.k_weight;
-    float n[4];
+    float n[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) n[e] = bf16r(__fmul_rn(__fmul_rn(v[e], inv), __bfloat162float(wp[4 * lane + e])));
-    // partner values for the rotate-half: lane +- rotary/8 (4 dims per lane)
-    const int shift = half >> 2;
-    const bool low = 4 * lane < half;
-    const int src_lane = low ? lane + shift : lane - shift;
-    float pn[4];
+    for (int e = 0; e < 8; ++e)
+      n[e] = bf16r(__fmul_rn(__fmul_rn(v[e], inv), j == 0 ? wq[e] : wk[e]));
+    float pn[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) pn[e] = __shfl_sync(0xffffffffu, n[e], src_lane & 31);
-    float out[4];
+    for (int e = 0; e < 8; ++e) pn[e] = __shfl_sync(half_mask, n[e], partner);
     const long long pos = p.positions[t];
     if (pos < 0 || pos >= p.cache_rows) {
-      if (p.err) atomicOr(p.err, kErrBadIndex);
+      if (p.err && sub == 0) atomicOr(p.err, kErrBadIndex);
       continue;
     }
-    const __nv_bfloat16* cs = p.cos_sin + static_cast<size_t>(pos) * p.rotary;
+    float out[8];
+    if (rotating) {
+      const __nv_bfloat16* cs = p.cos_sin + static_cast<size_t>(pos) * p.rotary;
+      const uint4 cr = *reinterpret_cast<const uint4*>(cs + phase);
+      const uint4 sr = *reinterpret_cast<const uint4*>(cs + half + phase);
+      const uint32_t cu[4] = {cr.x, cr.y, cr.z, cr.w}, su[4] = {sr.x, sr.y, sr.z, sr.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int d = 4 * lane + e;
-      if (d < p.rotary) {
-        const int ph = d % half;
-        const float c = __bfloat162float(cs[ph]);
-        const float s = __bfloat162float(cs[half + ph]);
-        const float rot = low ? -pn[e] : pn[e];
-        out[e] = bf16r(bf16r(__fmul_rn(n[e], c)) + bf16r(__fmul_rn(rot, s)));
-      } else {
-        out[e] = n[e];
+      for (int i = 0; i < 4; ++i) {
+        const float c0 = __uint_as_float(cu[i] << 16), c1 = __uint_as_float(cu[i] & 0xFFFF0000u);
+        const float s0 = __uint_as_float(su[i] << 16), s1 = __uint_as_float(su[i] & 0xFFFF0000u);
+        const float r0 = low ? -pn[2 * i] : pn[2 * i];
+        const float r1 = low ? -pn[2 * i + 1] : pn[2 * i + 1];
+        out[2 * i] = bf16r(bf16r(__fmul_rn(n[2 * i], c0)) + bf16r(__fmul_rn(r0, s0)));
+        out[2 * i + 1] = bf16r(bf16r(__fmul_rn(n[2 * i + 1], c1)) + bf16r(__fmul_rn(r1, s1)));
       }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) out[e] = n[e];
     }
-    uint2 o;
+    uint4 o;
     o.x = (__float_as_uint(out[0]) >> 16) | (__float_as_uint(out[1]) & 0xFFFF0000u);
     o.y = (__float_as_uint(out[2]) >> 16) | (__float_as_uint(out[3]) & 0xFFFF0000u);
-    reinterpret_cast<uint2*>(dst)[lane] = o;
+    o.z = (__float_as_uint(out[4]) >> 16) | (__float_as_uint(out[5]) & 0xFFFF0000u);
+    o.w = (__float_as_uint(out[6]) >> 16) | (__float_as_uint(out[7]) & 0xFFFF0000u);
+    reinterpret_cast<uint4*>(dst)[sub] = o;
   }
 }
 
 static int prologue_launch(const PrologueParams& p, cudaStream_t stream) {
-  const long long rows = static_cast<long long>(p.tokens) * p.heads * 3;
-  long long blocks = (rows + 7) / 8;
+  const long long rows = static_cast<long long>(p.tokens) * p.heads * (p.world > 1 ? 3 : 2);
+  long long blocks = (rows + 15) / 16;
   if (blocks > 148 * 32) blocks = 148 * 32;
   if (blocks < 1) blocks = 1;
   qkv_norm_rope_kernel<<<static_cast<int>(blocks), 256, 0, stream>>>(p);
@@ -135,9 +165,12 @@ static int check_prologue(const void* qkv, const void* q_weight, const void* k_w
     return set_error(H3SA_ERR_INVALID, "qkv prologue: null pointer argument");
   if (tokens < 0 || heads <= 0 || cache_rows <= 0)
     return set_error(H3SA_ERR_INVALID, "qkv prologue: invalid sizes");
-  if (rotary <= 0 || rotary > head_dim || (rotary % 8) != 0)
-    return set_error(H3SA_ERR_UNSUPPORTED, "qkv prologue: rotary span must be a multiple of 8 "
+  if (rotary <= 0 || rotary > head_dim || (rotary % 16) != 0)
+    return set_error(H3SA_ERR_UNSUPPORTED, "qkv prologue: rotary span must be a multiple of 16 "
                      "within the head, got %d", rotary);
+  if ((reinterpret_cast<uintptr_t>(cos_sin) | reinterpret_cast<uintptr_t>(q_weight) |
+       reinterpret_cast<uintptr_t>(k_weight)) & 15)
+    return set_error(H3SA_ERR_INVALID, "qkv prologue: weights and RoPE cache must be 16-byte aligned");
   if (reinterpret_cast<uintptr_t>(qkv) & 15)
     return set_error(H3SA_ERR_INVALID, "qkv prologue: tensors must be 16-byte aligned");
   return H3SA_OK;
