@@ -160,11 +160,22 @@ __global__ void __launch_bounds__(256) quant_finalize_kernel(const float* partia
   }
 }
 
-__device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s) {
-  a = fminf(fmaxf(__fdiv_rn(a, s), -kFp8Max), kFp8Max);
-  b = fminf(fmaxf(__fdiv_rn(b, s), -kFp8Max), kFp8Max);
-  c = fminf(fmaxf(__fdiv_rn(c, s), -kFp8Max), kFp8Max);
-  d = fminf(fmaxf(__fdiv_rn(d, s), -kFp8Max), kFp8Max);
+// Correctly rounded x / s from y = RN(1 / s) with two residual corrections: q0 = RN(x * y) is
+// within two ulps of the quotient, one correction q1 = RN(q0 + RN(x - s * q0) * y) makes it
+// faithful, after which the residual x - s * q1 is exact in an FMA and RN(q1 + r1 * y) is the
+// correctly rounded quotient (Markstein's division theorem). Same results as an IEEE division
+// for the normal-range quotients a per-head scale produces.
+__device__ __forceinline__ float div_by_scale(float x, float s, float y) {
+  const float q0 = __fmul_rn(x, y);
+  const float q1 = __fmaf_rn(__fmaf_rn(-s, q0, x), y, q0);
+  return __fmaf_rn(__fmaf_rn(-s, q1, x), y, q1);
+}
+
+__device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s, float y) {
+  a = fminf(fmaxf(div_by_scale(a, s, y), -kFp8Max), kFp8Max);
+  b = fminf(fmaxf(div_by_scale(b, s, y), -kFp8Max), kFp8Max);
+  c = fminf(fmaxf(div_by_scale(c, s, y), -kFp8Max), kFp8Max);
+  d = fminf(fmaxf(div_by_scale(d, s, y), -kFp8Max), kFp8Max);
   uint16_t lo, hi;
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
   asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
@@ -197,6 +208,7 @@ __global__ void __launch_bounds__(256) quant_apply_kernel(const QuantSpace q, co
       continue;
     }
     const float sc = __ldg(scale + b * q.heads + h);
+    const float inv = __frcp_rn(sc);
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(q.src + off) + c);
     const uint32_t w[4] = {v.x, v.y, v.z, v.w};
     float f[8];
@@ -206,8 +218,8 @@ __global__ void __launch_bounds__(256) quant_apply_kernel(const QuantSpace q, co
       f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
     }
     uint2 o;
-    o.x = quant4(f[0], f[1], f[2], f[3], sc);
-    o.y = quant4(f[4], f[5], f[6], f[7], sc);
+    o.x = quant4(f[0], f[1], f[2], f[3], sc, inv);
+    o.y = quant4(f[4], f[5], f[6], f[7], sc, inv);
     reinterpret_cast<uint2*>(q.dst + off)[c] = o;
   }
 }
