@@ -120,6 +120,20 @@ H3SA_API int h3sa_kv_copy_rows(const h3sa_rows* src, const h3sa_rows* dst, int32
 H3SA_API int h3sa_quantize_fp8_per_head(const void* x, void* y, float* scale, int32_t batch,
                                int32_t seq, int32_t heads, int32_t dim, void* stream);
 
+/* The same quantiser, same arguments and results, but it allocates no device memory: its
+ * scratch is a fixed 256 KiB device array inside the library, so
+ * batch * heads * ceil(seq / 256) must be at most 65536 (H3SA_ERR_INVALID otherwise). It is
+ * for callers that may not allocate while they run (a caller that owns all device memory
+ * through its own pool, or one running where the stream-ordered allocator must not be
+ * touched). The first call on each device looks up the array's device address with that
+ * device current; make that first call before any stream capture. The array is shared by
+ * every call on a device: calls whose device work can overlap (unordered streams, several
+ * host threads) race on it and must be serialised by the caller. No counterpart in the
+ * reference. */
+H3SA_API int h3sa_quantize_fp8_per_head_noalloc(const void* x, void* y, float* scale,
+                                                int32_t batch, int32_t seq, int32_t heads,
+                                                int32_t dim, void* stream);
+
 /* The same quantiser over logical KV rows [0, rows) of a paged bf16 pool, written to an e4m3
  * pool through the same page table: one scale per head over the whole logical sequence, as
  * the FP8 dynamic backend quantises the concatenated K (or V) parts

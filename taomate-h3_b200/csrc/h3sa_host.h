@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -44,5 +45,25 @@ struct AttnLaunch {
 
 int attention_launch(const AttnLaunch& L, bool fp8, cudaStream_t stream);
 size_t attention_smem_bytes(bool fp8);
+
+// Per-head e4m3 quantiser over packed [batch, seq, heads, 128] rows or a paged pool.
+constexpr int kQuantChunkRows = 256;  // rows per partial-amax slot
+
+struct QuantSpace {
+  const __nv_bfloat16* src;
+  uint8_t* dst;
+  int paged;
+  int batch;
+  int seq;  // rows per (batch, head)
+  int heads;
+  int pool_pages;
+  const int* page_table;
+  int table_blocks;
+};
+
+// Launch amax-partial, finalize and apply; `partial` holds batch * heads * chunks floats,
+// every one of which the first kernel writes before the second reads it.
+int quantize_launch(const QuantSpace& q, float* scale, float* partial, int chunks, int* err,
+                    cudaStream_t stream);
 
 }  // namespace h3sa

@@ -74,20 +74,7 @@ __global__ void __launch_bounds__(256) kv_copy_kernel(const CopyParams p) {
 }
 
 // ------------------------------------------------------------------ e4m3 quantiser
-constexpr int kQuantChunkRows = 256;
 constexpr float kFp8Max = 448.0f;
-
-struct QuantSpace {
-  const __nv_bfloat16* src;
-  uint8_t* dst;
-  int paged;
-  int batch;
-  int seq;  // rows per (batch, head)
-  int heads;
-  int pool_pages;
-  const int* page_table;
-  int table_blocks;
-};
 
 // Element offset of (b, s, h, 0); -1 when a page lookup fails.
 __device__ __forceinline__ long long quant_offset(const QuantSpace& q, int b, int s, int h) {
