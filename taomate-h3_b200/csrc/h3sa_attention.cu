@@ -243,103 +243,110 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
   } else if (warp == 1) {
     // ================================================================ MMA issuer
+    // The whole warp runs this loop (all values warp-uniform); one elected lane issues each
+    // tcgen05 instruction. Shared-memory descriptors are formed once per buffer and advanced
+    // by constant offsets.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-    if (lane == 0) {
-      const uint32_t tS0 = tbase + 0u, tS1 = tbase + 128u;
-      const uint32_t tO0 = tbase + 256u, tO1 = tbase + 384u;
-      int cnt0 = 0, cnt1 = 0;       // QK MMAs issued per tile (softmax rounds requested)
-      int pv0 = 0, pv1 = 0;         // PV issued at least once per tile
-      int pend = 0;                 // tiles whose PV for block i-1 is still to be issued
-      bool ok = mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err);
+    const uint32_t tS0 = tbase + 0u, tS1 = tbase + 128u;
+    const uint32_t tO0 = tbase + 256u, tO1 = tbase + 384u;
+    const uint32_t qlo0 = sdesc_lo(smem_u32(sm.q[0]), 16);
+    const uint32_t klo0 = sdesc_lo(smem_u32(sm.k[0]), 16);
+    const uint32_t vlo0 = sdesc_lo(smem_u32(sm.v[0]), Cfg::kAtomBytes);
+    constexpr uint32_t kTileDesc = Cfg::kTileBytes >> 4;  // descriptor step between buffers
+    int cnt0 = 0, cnt1 = 0;       // QK MMAs issued per tile (softmax rounds requested)
+    int pv0 = 0, pv1 = 0;         // PV issued at least once per tile
+    int pend = 0;                 // tiles whose PV for block i-1 is still to be issued
+    bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err));
+    tc_fence_after();
+    auto issue_pv = [&](uint32_t tS, uint32_t tO, int started, int vs) {
+      const uint32_t vlo = vlo0 + static_cast<uint32_t>(vs) * kTileDesc;
+#pragma unroll
+      for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
+        const uint64_t bdesc = sdesc_join(vlo + ((kk * Cfg::kPvRowsPerStep * 128) >> 4));
+        const uint32_t a_tmem = tS + 64u + kk * 8u;
+        if constexpr (kFp8)
+          mma_ts_f8(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
+        else
+          mma_ts(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
+      }
+    };
+    auto issue_qk = [&](uint32_t tS, int t, int ks) {
+      const uint32_t qlo = qlo0 + static_cast<uint32_t>(t) * kTileDesc;
+      const uint32_t klo = klo0 + static_cast<uint32_t>(ks) * kTileDesc;
+#pragma unroll
+      for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
+        const uint32_t off = ((kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
+                              (kk * Cfg::kKStepBytes) % 128) >> 4;
+        if constexpr (kFp8)
+          mma_ss_f8(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
+                    kk > 0 ? 1u : 0u);
+        else
+          mma_ss(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
+                 kk > 0 ? 1u : 0u);
+      }
+    };
+    for (int i = 0; ok && i <= nblk; ++i) {
+      const bool last = (i == nblk);
+      const int s = i % kKVStages;
+      const uint32_t ph = (i / kKVStages) & 1;
+      const int ps = (i + kKVStages - 1) % kKVStages;
+      const uint32_t pph = ((i - 1) / kKVStages) & 1;
+      int b = 0, m = 0;
+      bool w = true;
+      if (!last) {
+        block_at(i, b, m);
+        w = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err);
+      }
+      if (w && pend) w = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
+      if (!(ok = __all_sync(0xffffffffu, w))) break;
+      H3SA_TRACE_AT(i, 10);
       tc_fence_after();
-      auto issue_pv = [&](uint32_t tS, uint32_t tO, int started, int vs) {
-        const uint32_t vaddr = smem_u32(sm.v[vs]);
-#pragma unroll
-        for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
-          const uint64_t bdesc =
-              sdesc_sw128(vaddr + kk * Cfg::kPvRowsPerStep * 128, Cfg::kAtomBytes, 1024);
-          const uint32_t a_tmem = tS + 64u + kk * 8u;
-          if constexpr (kFp8)
-            mma_ts_f8(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
-          else
-            mma_ts(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
-        }
-      };
-      auto issue_qk = [&](uint32_t tS, int t, int ks) {
-        const uint32_t qaddr = smem_u32(sm.q[t]);
-        const uint32_t kaddr = smem_u32(sm.k[ks]);
-#pragma unroll
-        for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
-          const uint32_t off = (kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
-                               (kk * Cfg::kKStepBytes) % 128;
-          const uint64_t adesc = sdesc_sw128(qaddr + off, 16, 1024);
-          const uint64_t bdesc = sdesc_sw128(kaddr + off, 16, 1024);
-          if constexpr (kFp8)
-            mma_ss_f8(tS, adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
-          else
-            mma_ss(tS, adesc, bdesc, Cfg::kIdescQK, kk > 0 ? 1u : 0u);
-        }
-      };
-      for (int i = 0; ok && i <= nblk; ++i) {
-        const bool last = (i == nblk);
-        const int s = i % kKVStages;
-        const uint32_t ph = (i / kKVStages) & 1;
-        const int ps = (i + kKVStages - 1) % kKVStages;
-        const uint32_t pph = ((i - 1) / kKVStages) & 1;
-        int b = 0, m = 0;
-        if (!last) {
-          block_at(i, b, m);
-          ok = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err);
-        }
-        if (ok && pend) ok = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
+      // tile 0: PV for the previous block, then QK for this one (same TMEM columns)
+      if (pend & 1) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(smem_u32(&sm.p_full[0]), (cnt0 - 1) & 1, abort_flag, p.err));
         if (!ok) break;
-        H3SA_TRACE_AT(i, 10);
+        H3SA_TRACE_AT(i, 11);
         tc_fence_after();
-        // tile 0: PV for the previous block, then QK for this one (same TMEM columns)
-        if (pend & 1) {
-          ok = mbar_wait(smem_u32(&sm.p_full[0]), (cnt0 - 1) & 1, abort_flag, p.err);
-          if (!ok) break;
-          H3SA_TRACE_AT(i, 11);
-          tc_fence_after();
-          issue_pv(tS0, tO0, pv0, ps);
-          pv0 = 1;
-        }
-        if (m & 1) {
-          issue_qk(tS0, 0, s);
-          tc_commit(smem_u32(&sm.s_full[0]));
-          ++cnt0;
-        }
-        // tile 1
-        if (pend & 2) {
-          ok = mbar_wait(smem_u32(&sm.p_full[1]), (cnt1 - 1) & 1, abort_flag, p.err);
-          if (!ok) break;
-          H3SA_TRACE_AT(i, 12);
-          tc_fence_after();
-          issue_pv(tS1, tO1, pv1, ps);
-          pv1 = 1;
-        }
-        if (m & 2) {
-          issue_qk(tS1, 1, s);
-          tc_commit(smem_u32(&sm.s_full[1]));
-          ++cnt1;
-        }
-        if (pend) tc_commit(smem_u32(&sm.v_empty[ps]));
-        if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
-        pend = m;
-        H3SA_TRACE_AT(i, 13);
+        issue_pv(tS0, tO0, pv0, ps);
+        pv0 = 1;
       }
-      if (ok) {
-        tc_commit(smem_u32(&sm.o_done[0]));
-        if (n_tiles > 1) tc_commit(smem_u32(&sm.o_done[1]));
+      if (m & 1) {
+        issue_qk(tS0, 0, s);
+        tc_commit(smem_u32(&sm.s_full[0]));
+        ++cnt0;
       }
-      // Whatever happened, do not leave tensor-core work in flight past the teardown.
-      tc_commit(smem_u32(&sm.drain));
-      const unsigned long long t0 = global_ns();
-      while (!mbar_try_wait(smem_u32(&sm.drain), 0)) {
-        if (global_ns() - t0 > kWaitTimeoutNs) {
-          if (p.err) atomicOr(p.err, kErrWaitTimeout);
-          break;
-        }
+      // tile 1
+      if (pend & 2) {
+        ok = __all_sync(0xffffffffu,
+                        mbar_wait(smem_u32(&sm.p_full[1]), (cnt1 - 1) & 1, abort_flag, p.err));
+        if (!ok) break;
+        H3SA_TRACE_AT(i, 12);
+        tc_fence_after();
+        issue_pv(tS1, tO1, pv1, ps);
+        pv1 = 1;
+      }
+      if (m & 2) {
+        issue_qk(tS1, 1, s);
+        tc_commit(smem_u32(&sm.s_full[1]));
+        ++cnt1;
+      }
+      if (pend) tc_commit(smem_u32(&sm.v_empty[ps]));
+      if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
+      pend = m;
+      H3SA_TRACE_AT(i, 13);
+    }
+    if (ok) {
+      tc_commit(smem_u32(&sm.o_done[0]));
+      if (n_tiles > 1) tc_commit(smem_u32(&sm.o_done[1]));
+    }
+    // Whatever happened, do not leave tensor-core work in flight past the teardown.
+    tc_commit(smem_u32(&sm.drain));
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(smem_u32(&sm.drain), 0)) {
+      if (global_ns() - t0 > kWaitTimeoutNs) {
+        if (p.err && lane == 0) atomicOr(p.err, kErrWaitTimeout);
+        break;
       }
     }
   } else if (warp < 4) {

@@ -32,7 +32,7 @@ constexpr int kAttnThreads = 384;
 // softmax warpgroups get kRegsSoftmax. The sum must fit the launch allocation
 // (threads x registers per thread at launch, 168 under these launch bounds).
 #ifndef H3SA_REGS_CONTROL
-#define H3SA_REGS_CONTROL 56
+#define H3SA_REGS_CONTROL 64
 #endif
 #ifndef H3SA_REGS_SOFTMAX
 #define H3SA_REGS_SOFTMAX 216
