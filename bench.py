@@ -67,31 +67,43 @@ def _ncu_traffic() -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason sampling during the timed region."""
+    """nvidia-smi clock / power / throttle-reason sampling, kept only inside the timed window.
 
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Samples every 20 ms with their timestamps; `mark_start()` / `mark_stop()` bracket the timed
+    region (host wall clock, after a device synchronize) and `summary()` reports the samples that
+    fall between them (all samples, flagged, if the window caught none).
+    """
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int) -> None:
         self.index = index
         self.proc: subprocess.Popen | None = None
+        self.t0 = self.t1 = None
 
     def __enter__(self) -> "ClockSampler":
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (OSError, FileNotFoundError):
             self.proc = None
         time.sleep(0.3)
         return self
 
+    def mark_start(self) -> None:
+        self.t0 = time.time()
+
+    def mark_stop(self) -> None:
+        self.t1 = time.time()
+
     def __exit__(self, *exc: object) -> None:
         self.lines: list[str] = []
         if self.proc is not None:
-            time.sleep(0.25)
+            time.sleep(0.1)
             self.proc.terminate()
             try:
                 out, _ = self.proc.communicate(timeout=5)
@@ -100,25 +112,39 @@ class ClockSampler:
                 out, _ = self.proc.communicate()
             self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
-    def summary(self) -> dict:
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
+    @staticmethod
+    def _epoch(stamp: str) -> float | None:
+        import datetime
+
+        for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                return datetime.datetime.strptime(stamp.strip(), fmt).timestamp()
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        if not sm:
+        return None
+
+    def summary(self) -> dict:
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
+        for ln in getattr(self, "lines", []):
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 10:
+                continue
+            try:
+                rows.append((self._epoch(parts[0]), float(parts[2]), float(parts[3]),
+                             float(parts[4]), parts[6:10]))
+            except ValueError:
+                continue
+        if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = [r for r in rows if r[0] is not None and self.t0 is not None and
+                  self.t1 is not None and self.t0 <= r[0] <= self.t1]
+        use = inside or rows
+        reasons = sorted({n for r in use for n, f in zip(names, r[4]) if f.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[1] for r in use),
+                "sm_max_mhz": max(r[2] for r in use), "reasons": reasons,
+                "power_w": statistics.median(r[3] for r in use), "samples": len(use),
+                "window": "timed region" if inside else "whole run (no sample inside the timed region)"}
 
 
 def _dist() -> tuple[int, int, int]:
@@ -294,6 +320,115 @@ class Step:
         return self.out
 
 
+def _time_launch(fn, iters: int) -> float:
+    """Mean device time (ms) of `fn` over `iters` launches after two warm-up calls."""
+
+    for _ in range(2):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def _variants(peaks: dict, iters: int = 10) -> dict:
+    """Kernel-only timings of the path's FP8 and block-sparse variants on this GPU.
+
+    * FP8: the 1080p per-GPU problem of the TP2 x SP4 configuration (24 heads / TP 2 / SP 4 =
+      3 heads; 24480 video + 125 audio queries over a 32768-row cache plus the chunk), e4m3
+      Q/K/V with per-head scales, inputs N(0,1) with 1% outliers x8 (seeded).
+    * Block-sparse: the 768p per-GPU problem at SP=8 (3 heads; 12509 queries over 16384 + 12509
+      keys) with the composite 128x128 block mask (audio blocks, 2 sinks, +-4-block band, top-k
+      fill to 25% of blocks).
+    FLOPs count only the work the kernel must do (kept blocks for the sparse case).
+    """
+
+    import types
+
+    import h3sa
+    from h3sa.block_sparse import composite_block_mask
+    from h3sa.kernels import PAGE_ROWS
+
+    dev = torch.device("cuda")
+    d = CFG["head_dim"]
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+
+    def pools(rows: int, heads: int, k: torch.Tensor, v: torch.Tensor):
+        pages = (rows + PAGE_ROWS - 1) // PAGE_ROWS
+        table = torch.arange(pages, dtype=torch.int32, device=dev)
+        kp = torch.zeros(heads, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=dev)
+        vp = torch.zeros_like(kp)
+        h3sa.kv_copy_rows([k, v], [kp, vp], count=rows, dst_table=table)
+        return kp, vp, table
+
+    # ---- FP8 e4m3, 1080p per GPU
+    heads, nq, nh = 3, 24480 + 125, 32768
+    nk = nh + nq
+
+    def outliers(x: torch.Tensor) -> torch.Tensor:
+        mask = torch.rand(x.shape, device=dev, generator=g) < 0.01
+        return torch.where(mask, x * 8, x)
+
+    q = outliers(torch.randn(nq, heads, d, device=dev, generator=g)).to(torch.bfloat16)
+    k = outliers(torch.randn(nk, heads, d, device=dev, generator=g)).to(torch.bfloat16)
+    v = outliers(torch.randn(nk, heads, d, device=dev, generator=g)).to(torch.bfloat16)
+    kp, vp, table = pools(nk, heads, k, v)
+    k8 = torch.empty_like(kp, dtype=torch.float8_e4m3fn)
+    v8 = torch.empty_like(vp, dtype=torch.float8_e4m3fn)
+    ks = torch.empty(heads, dtype=torch.float32, device=dev)
+    vs = torch.empty_like(ks)
+    h3sa.quantize_fp8_pool(kp, k8, ks, table, nk)
+    h3sa.quantize_fp8_pool(vp, v8, vs, table, nk)
+    q8, qs = h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0))
+    o = torch.empty(nq, heads, d, dtype=torch.bfloat16, device=dev)
+    probs = [h3sa.AttentionProblem(0, nq, 0, nk)]
+    ms = _time_launch(lambda: h3sa.attention_fwd(q8[0], o, k8, v8, table, probs, d ** -0.5,
+                                                 q_scale=qs[0], k_scale=ks, v_scale=vs), iters)
+    tf = 4.0 * nq * nk * d * heads / (ms * 1e-3) / 1e12
+    fp8_peak = 2.0 * peaks["bf16"]
+    out["fp8_1080p_tp2sp4_per_gpu"] = {
+        "ms": ms, "tflops": tf, "heads": heads, "queries": nq, "keys": nk,
+        "roofline": {"bound": "tensor", "peak": fp8_peak, "frac": tf / fp8_peak,
+                     "peak_source": "2 x measured bf16 burst (no measured e4m3 GEMM peak; "
+                                    "nominal dense e4m3 is 4500)"}}
+    del q, k, v, kp, vp, k8, v8, q8, o
+
+    # ---- block-sparse bf16, 768p SP=8 per GPU
+    heads, nq, nh = 3, CFG["video"] + CFG["audio"], CFG["history"]
+    nk = nh + nq
+    q = torch.randn(nq, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(nk, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(nk, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    kp, vp, table = pools(nk, heads, k, v)
+    qb, kb = (nq + PAGE_ROWS - 1) // PAGE_ROWS, (nk + PAGE_ROWS - 1) // PAGE_ROWS
+    q_audio = torch.zeros(qb, dtype=torch.uint8, device=dev)
+    q_audio[CFG["video"] // PAGE_ROWS:] = 1           # the chunk's audio rows follow its video
+    kv_audio = torch.zeros(kb, dtype=torch.uint8, device=dev)
+    kv_audio[(nh + CFG["video"]) // PAGE_ROWS:] = 1
+    kv_audio[torch.arange(31, nh // PAGE_ROWS, 32, device=dev)] = 1  # one audio block per 4096 history rows
+    paged = types.SimpleNamespace(key=kp, table=table)
+    num, idx = composite_block_mask(q, paged, q_lo=0, q_hi=nq, n_hist=nh, n_kv=nk,
+                                    q_block_audio=q_audio, kv_block_audio=kv_audio, density=0.25)
+    o = torch.empty(nq, heads, d, dtype=torch.bfloat16, device=dev)
+    probs = [h3sa.AttentionProblem(0, nq, 0, nk, sparse=True)]
+    ms = _time_launch(lambda: h3sa.attention_fwd(q, o, kp, vp, table, probs, d ** -0.5,
+                                                 kv_num_blocks=num, kv_indices=idx), iters)
+    kept = int(num.sum().item())
+    density = kept / (heads * qb * kb)
+    flops = 4.0 * kept * PAGE_ROWS * PAGE_ROWS * d  # kept 128x128 blocks (tail blocks counted whole)
+    tf = flops / (ms * 1e-3) / 1e12
+    out["sparse_768p_sp8_per_gpu"] = {
+        "ms": ms, "tflops_on_kept_blocks": tf, "kept_block_fraction": density, "heads": heads,
+        "queries": nq, "keys": nk,
+        "roofline": {"bound": "tensor", "peak": peaks["bf16"], "frac": tf / peaks["bf16"]}}
+    return out
+
+
 def _max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -362,12 +497,16 @@ def run_h3sa(args: argparse.Namespace) -> None:
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         _barrier(world)
+        torch.cuda.synchronize()
+        clocks.mark_start()
         start.record()
         for i in range(args.steps):
             step_ev[i][0].record()
             step.run(attn_ev[i])
             step_ev[i][1].record()
         stop.record()
+        torch.cuda.synchronize()
+        clocks.mark_stop()
         _barrier(world)
     total_ms = _max_over_ranks(start.elapsed_time(stop), world)
     attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
@@ -406,6 +545,8 @@ def run_h3sa(args: argparse.Namespace) -> None:
     if rank == 0 and world == 1 and not args.no_comparator:
         extra["comparator"] = _comparator_sdpa(step)
         extra["comparator"]["speedup_p50"] = extra["comparator"]["ms_p50"] / attn_avg
+    if rank == 0 and world == 1 and not args.no_variants:
+        extra["variants"] = _variants(peaks)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = _cpu_baseline()
@@ -464,6 +605,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-comparator", action="store_true")
+    ap.add_argument("--no-variants", action="store_true",
+                    help="skip the kernel-only FP8 1080p and block-sparse 768p timings")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "h3sa":
         args.warmup = 3

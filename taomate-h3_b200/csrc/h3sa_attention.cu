@@ -23,6 +23,13 @@ constexpr int kExpPolyPer16 = H3SA_EXP_POLY_PER16;
 static_assert(kExpPolyPer16 % 2 == 0 && kExpPolyPer16 <= 16, "poly exponentials come in pairs");
 
 
+// Ping-pong between the two softmax warpgroups of a dense two-tile CTA: the exponential
+// phase of tile 1 for block i runs after that of tile 0 for block i, and tile 0's for block
+// i + 1 after tile 1's for block i, so the two never share the MUFU and issue slots.
+#ifndef H3SA_PINGPONG
+#define H3SA_PINGPONG 0
+#endif
+
 // Optional per-block timeline of two CTAs (first and middle of the grid), compiled only with
 // -DH3SA_TRACE: clock64() at fixed points of the producer, MMA and softmax loops.
 #ifdef H3SA_TRACE
@@ -64,6 +71,7 @@ struct alignas(1024) AttnSmem {
   uint64_t k_full[kKVStages], k_empty[kKVStages];
   uint64_t v_full[kKVStages], v_empty[kKVStages];
   uint64_t s_full[2], p_full[2], o_done[2];
+  uint64_t exp_done[2];  // ping-pong tokens: one phase per exponential round of each tile
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -159,16 +167,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     mbar_init(smem_u32(&sm.q_full), 1);
     for (int s = 0; s < kKVStages; ++s) {
       mbar_init(smem_u32(&sm.k_full[s]), 1);
-      mbar_init(smem_u32(&sm.k_empty[s]), 1);
+      mbar_init(smem_u32(&sm.k_empty[s]), n_tiles);  // one release per MMA warp
       mbar_init(smem_u32(&sm.v_full[s]), 1);
-      mbar_init(smem_u32(&sm.v_empty[s]), 1);
+      mbar_init(smem_u32(&sm.v_empty[s]), n_tiles);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(smem_u32(&sm.s_full[t]), 1);
       mbar_init(smem_u32(&sm.p_full[t]), 128);
       mbar_init(smem_u32(&sm.o_done[t]), 1);
+      mbar_init(smem_u32(&sm.exp_done[t]), 128);
     }
-    mbar_init(smem_u32(&sm.drain), 1);
+    mbar_init(smem_u32(&sm.drain), n_tiles);
     sm.abort_flag = 0;
     sm.n_blocks = b_hi - b_lo;
     fence_mbar_init();
@@ -201,19 +210,28 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   // Register split (every warp of a warpgroup executes the same setmaxnreg at the top of its
   // role): the producer/MMA warpgroup gives registers to the two softmax warpgroups.
-  if (warp == 0) {
-    // ================================================================ TMA producer
+  if (warp == 0 || warp == 3) {
+    // ================================================================ TMA producers
+    // Warp 0 loads Q and streams K blocks, warp 3 streams V blocks: K for block i + 2 is
+    // released by the QK MMAs of block i, V by the later PV MMAs, so each stream runs ahead
+    // on its own stage barriers.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+    const bool is_k = (warp == 0);
     if (lane == 0 && !*abort_flag) {
-      tma_prefetch_desc(&tmQ);
-      tma_prefetch_desc(&tmK);
-      tma_prefetch_desc(&tmV);
-      const uint32_t qbar = smem_u32(&sm.q_full);
-      mbar_expect_tx(qbar, n_tiles * Cfg::kTileBytes);
-      for (int t = 0; t < n_tiles; ++t)
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_3d(smem_u32(sm.q[t]) + a * Cfg::kAtomBytes, &tmQ, qbar, a * (128 / Cfg::kElem),
-                      head, q_row0 + t * kBlockM);
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      tma_prefetch_desc(map);
+      if (is_k) {
+        tma_prefetch_desc(&tmQ);
+        const uint32_t qbar = smem_u32(&sm.q_full);
+        mbar_expect_tx(qbar, n_tiles * Cfg::kTileBytes);
+        for (int t = 0; t < n_tiles; ++t)
+          for (int a = 0; a < Cfg::kAtoms; ++a)
+            tma_load_3d(smem_u32(sm.q[t]) + a * Cfg::kAtomBytes, &tmQ, qbar,
+                        a * (128 / Cfg::kElem), head, q_row0 + t * kBlockM);
+      }
+      uint64_t* full = is_k ? sm.k_full : sm.v_full;
+      uint64_t* empty = is_k ? sm.k_empty : sm.v_empty;
+      uint8_t* buf = is_k ? &sm.k[0][0] : &sm.v[0][0];
       for (int i = 0; i < nblk; ++i) {
         const int s = i % kKVStages;
         const uint32_t ph = (i / kKVStages) & 1;
@@ -225,133 +243,103 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           *abort_flag = 1;
           break;
         }
-        if (!mbar_wait(smem_u32(&sm.k_empty[s]), ph ^ 1, abort_flag, p.err)) break;
-        H3SA_TRACE_AT(i, 14);
-        const uint32_t kb = smem_u32(&sm.k_full[s]);
-        mbar_expect_tx(kb, Cfg::kTileBytes);
+        if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        H3SA_TRACE_AT(i, is_k ? 14 : 15);
+        const uint32_t fb = smem_u32(&full[s]);
+        mbar_expect_tx(fb, Cfg::kTileBytes);
+        const uint32_t dst = smem_u32(buf) + s * Cfg::kTileBytes;
         for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_3d(smem_u32(sm.k[s]) + a * Cfg::kAtomBytes, &tmK, kb, a * (128 / Cfg::kElem),
-                      page * kBlockN, head);
-        if (!mbar_wait(smem_u32(&sm.v_empty[s]), ph ^ 1, abort_flag, p.err)) break;
-        H3SA_TRACE_AT(i, 15);
-        const uint32_t vb = smem_u32(&sm.v_full[s]);
-        mbar_expect_tx(vb, Cfg::kTileBytes);
-        for (int a = 0; a < Cfg::kAtoms; ++a)
-          tma_load_3d(smem_u32(sm.v[s]) + a * Cfg::kAtomBytes, &tmV, vb, a * (128 / Cfg::kElem),
-                      page * kBlockN, head);
+          tma_load_3d(dst + a * Cfg::kAtomBytes, map, fb, a * (128 / Cfg::kElem), page * kBlockN,
+                      head);
       }
     }
-  } else if (warp == 1) {
-    // ================================================================ MMA issuer
-    // The whole warp runs this loop (all values warp-uniform); one elected lane issues each
-    // tcgen05 instruction. Shared-memory descriptors are formed once per buffer and advanced
-    // by constant offsets.
+  } else if (warp == 1 || warp == 2) {
+    // ================================================================ MMA issuers
+    // Warp 1 issues the MMAs of query tile 0, warp 2 those of tile 1. A warp stays blocked in
+    // tcgen05.mma until the tensor pipe takes the instruction, so one issuer per tile keeps
+    // the pipe fed while the other waits on its softmax or on a barrier. Each warp runs its
+    // loop converged (all values warp-uniform); one elected lane issues every tcgen05
+    // instruction. Shared-memory descriptors advance by constant 32-bit steps.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-    const uint32_t tS0 = tbase + 0u, tS1 = tbase + 128u;
-    const uint32_t tO0 = tbase + 256u, tO1 = tbase + 384u;
-    const uint32_t qlo0 = sdesc_lo(smem_u32(sm.q[0]), 16);
-    const uint32_t klo0 = sdesc_lo(smem_u32(sm.k[0]), 16);
-    const uint32_t vlo0 = sdesc_lo(smem_u32(sm.v[0]), Cfg::kAtomBytes);
-    constexpr uint32_t kTileDesc = Cfg::kTileBytes >> 4;  // descriptor step between buffers
-    int cnt0 = 0, cnt1 = 0;       // QK MMAs issued per tile (softmax rounds requested)
-    int pv0 = 0, pv1 = 0;         // PV issued at least once per tile
-    int pend = 0;                 // tiles whose PV for block i-1 is still to be issued
-    bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err));
-    tc_fence_after();
-    auto issue_pv = [&](uint32_t tS, uint32_t tO, int started, int vs) {
-      const uint32_t vlo = vlo0 + static_cast<uint32_t>(vs) * kTileDesc;
-#pragma unroll
-      for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
-        const uint64_t bdesc = sdesc_join(vlo + ((kk * Cfg::kPvRowsPerStep * 128) >> 4));
-        const uint32_t a_tmem = tS + 64u + kk * 8u;
-        if constexpr (kFp8)
-          mma_ts_f8(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
-        else
-          mma_ts(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
-      }
-    };
-    auto issue_qk = [&](uint32_t tS, int t, int ks) {
-      const uint32_t qlo = qlo0 + static_cast<uint32_t>(t) * kTileDesc;
-      const uint32_t klo = klo0 + static_cast<uint32_t>(ks) * kTileDesc;
-#pragma unroll
-      for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
-        const uint32_t off = ((kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
-                              (kk * Cfg::kKStepBytes) % 128) >> 4;
-        if constexpr (kFp8)
-          mma_ss_f8(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
-                    kk > 0 ? 1u : 0u);
-        else
-          mma_ss(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
-                 kk > 0 ? 1u : 0u);
-      }
-    };
-    for (int i = 0; ok && i <= nblk; ++i) {
-      const bool last = (i == nblk);
-      const int s = i % kKVStages;
-      const uint32_t ph = (i / kKVStages) & 1;
-      const int ps = (i + kKVStages - 1) % kKVStages;
-      const uint32_t pph = ((i - 1) / kKVStages) & 1;
-      int b = 0, m = 0;
-      bool w = true;
-      if (!last) {
-        block_at(i, b, m);
-        w = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err);
-      }
-      if (w && pend) w = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
-      if (!(ok = __all_sync(0xffffffffu, w))) break;
-      H3SA_TRACE_AT(i, 10);
+    const int mt = warp - 1;  // the query tile this warp serves
+    if (mt < n_tiles) {
+      const uint32_t tS = tbase + static_cast<uint32_t>(mt) * 128u;
+      const uint32_t tO = tbase + 256u + static_cast<uint32_t>(mt) * 128u;
+      const uint32_t qlo = sdesc_lo(smem_u32(sm.q[mt]), 16);
+      const uint32_t klo0 = sdesc_lo(smem_u32(sm.k[0]), 16);
+      const uint32_t vlo0 = sdesc_lo(smem_u32(sm.v[0]), Cfg::kAtomBytes);
+      constexpr uint32_t kTileDesc = Cfg::kTileBytes >> 4;  // descriptor step between stages
+      int cnt = 0;       // QK MMAs issued (softmax rounds requested)
+      int started = 0;   // PV issued at least once
+      bool pend = false; // PV for the previous block still to be issued
+      bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err));
       tc_fence_after();
-      // tile 0: PV for the previous block, then QK for this one (same TMEM columns)
-      if (pend & 1) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(smem_u32(&sm.p_full[0]), (cnt0 - 1) & 1, abort_flag, p.err));
-        if (!ok) break;
-        H3SA_TRACE_AT(i, 11);
+      for (int i = 0; ok && i <= nblk; ++i) {
+        const bool last = (i == nblk);
+        const int s = i % kKVStages;
+        const uint32_t ph = (i / kKVStages) & 1;
+        const int ps = (i + kKVStages - 1) % kKVStages;
+        const uint32_t pph = ((i - 1) / kKVStages) & 1;
+        int b = 0, m = 0;
+        bool w = true;
+        if (!last) {
+          block_at(i, b, m);
+          w = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err);
+        }
+        if (w && pend) w = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
+        if (w && pend) w = mbar_wait(smem_u32(&sm.p_full[mt]), (cnt - 1) & 1, abort_flag, p.err);
+        if (!(ok = __all_sync(0xffffffffu, w))) break;
+        if (mt == 0) H3SA_TRACE_AT(i, 10);
         tc_fence_after();
-        issue_pv(tS0, tO0, pv0, ps);
-        pv0 = 1;
+        // PV for the previous block, then QK for this one: same TMEM columns, and the tensor
+        // pipe runs one warp's MMAs in issue order.
+        if (pend) {
+          const uint32_t vlo = vlo0 + static_cast<uint32_t>(ps) * kTileDesc;
+#pragma unroll
+          for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
+            const uint64_t bdesc = sdesc_join(vlo + ((kk * Cfg::kPvRowsPerStep * 128) >> 4));
+            const uint32_t a_tmem = tS + 64u + kk * 8u;
+            if constexpr (kFp8)
+              mma_ts_f8(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
+            else
+              mma_ts(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
+          }
+          started = 1;
+        }
+        const bool mine = !last && ((m >> mt) & 1);
+        if (mine) {
+          const uint32_t klo = klo0 + static_cast<uint32_t>(s) * kTileDesc;
+#pragma unroll
+          for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
+            const uint32_t off = ((kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
+                                  (kk * Cfg::kKStepBytes) % 128) >> 4;
+            if constexpr (kFp8)
+              mma_ss_f8(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
+                        kk > 0 ? 1u : 0u);
+            else
+              mma_ss(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
+                     kk > 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&sm.s_full[mt]));
+          ++cnt;
+        }
+        // this warp's share of the stage releases (the barriers count one per MMA warp)
+        if (i > 0) tc_commit(smem_u32(&sm.v_empty[ps]));
+        if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
+        pend = mine;
+        if (mt == 0) H3SA_TRACE_AT(i, 13);
       }
-      if (m & 1) {
-        issue_qk(tS0, 0, s);
-        tc_commit(smem_u32(&sm.s_full[0]));
-        ++cnt0;
+      if (ok) tc_commit(smem_u32(&sm.o_done[mt]));
+      // Whatever happened, leave no tensor-core work in flight past the teardown.
+      tc_commit(smem_u32(&sm.drain));
+      const unsigned long long t0 = global_ns();
+      while (!mbar_try_wait(smem_u32(&sm.drain), 0)) {
+        if (global_ns() - t0 > kWaitTimeoutNs) {
+          if (p.err && lane == 0) atomicOr(p.err, kErrWaitTimeout);
+          break;
+        }
       }
-      // tile 1
-      if (pend & 2) {
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait(smem_u32(&sm.p_full[1]), (cnt1 - 1) & 1, abort_flag, p.err));
-        if (!ok) break;
-        H3SA_TRACE_AT(i, 12);
-        tc_fence_after();
-        issue_pv(tS1, tO1, pv1, ps);
-        pv1 = 1;
-      }
-      if (m & 2) {
-        issue_qk(tS1, 1, s);
-        tc_commit(smem_u32(&sm.s_full[1]));
-        ++cnt1;
-      }
-      if (pend) tc_commit(smem_u32(&sm.v_empty[ps]));
-      if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
-      pend = m;
-      H3SA_TRACE_AT(i, 13);
     }
-    if (ok) {
-      tc_commit(smem_u32(&sm.o_done[0]));
-      if (n_tiles > 1) tc_commit(smem_u32(&sm.o_done[1]));
-    }
-    // Whatever happened, do not leave tensor-core work in flight past the teardown.
-    tc_commit(smem_u32(&sm.drain));
-    const unsigned long long t0 = global_ns();
-    while (!mbar_try_wait(smem_u32(&sm.drain), 0)) {
-      if (global_ns() - t0 > kWaitTimeoutNs) {
-        if (p.err && lane == 0) atomicOr(p.err, kErrWaitTimeout);
-        break;
-      }
-    }
-  } else if (warp < 4) {
-    // ================================================================ idle warps 2-3
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
   } else {
     // ================================================================ softmax / epilogue
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
@@ -371,6 +359,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // kRescaleThreshold (log2 units); P is then bounded by 2^(threshold + boost).
       constexpr float kRescaleThreshold = kFp8 ? 2.0f : 8.0f;
       constexpr float kBoost = kFp8 ? 6.0f : 0.0f;  // e4m3 P: keep the bulk above 2^-6
+      const bool pingpong = H3SA_PINGPONG && !pr.sparse && n_tiles == 2;
       float m_used = -INFINITY;
       float l_sum = 0.f;
       int c = 0;
@@ -443,6 +432,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_wait_st();
         }
         m_used = m_new;
+        // ping-pong: round c of tile 1 follows round c of tile 0; round c of tile 0 follows
+        // round c - 1 of tile 1
+        if (pingpong && (t == 1 || c > 0)) {
+          const uint32_t ph = static_cast<uint32_t>(t == 1 ? c : c - 1) & 1u;
+          if (!(ok = mbar_wait(smem_u32(&sm.exp_done[t ^ 1]), ph, abort_flag, p.err))) break;
+        }
         if (tr) H3SA_TRACE_AT(i, 5 * t + 2);
         // x = s * scale_log2 - (m_used - boost) in packed fp32 pairs, then 2^x on the MUFU
         // (kExpPolyPer16 of every 16 on the FMA pipe); P packed for the PV MMA, row sum in fp32.
@@ -480,6 +475,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             pk[j / 2] = pack_bf16x2(p0, p1);
           }
         }
+        if (pingpong) mbar_arrive(smem_u32(&sm.exp_done[t]));
         float sa, sb;
         f2_unpack(sum2, sa, sb);
         l_sum += sa + sb;

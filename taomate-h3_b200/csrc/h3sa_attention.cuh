@@ -32,10 +32,10 @@ constexpr int kAttnThreads = 384;
 // softmax warpgroups get kRegsSoftmax. The sum must fit the launch allocation
 // (threads x registers per thread at launch, 168 under these launch bounds).
 #ifndef H3SA_REGS_CONTROL
-#define H3SA_REGS_CONTROL 64
+#define H3SA_REGS_CONTROL 48
 #endif
 #ifndef H3SA_REGS_SOFTMAX
-#define H3SA_REGS_SOFTMAX 216
+#define H3SA_REGS_SOFTMAX 224
 #endif
 constexpr int kRegsControl = H3SA_REGS_CONTROL;
 constexpr int kRegsSoftmax = H3SA_REGS_SOFTMAX;
