@@ -491,7 +491,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (ok) ok = mbar_wait(smem_u32(&sm.o_done[t]), 0, abort_flag, p.err);
       if (ok) {
         tc_fence_after();
-        float out_scale = 1.0f / l_sum;
+        // c == 0: this tile's block list was empty, its rows see no key and are written as
+        // zeros (TMEM O was never written)
+        const bool any = c > 0;
+        float out_scale = any ? 1.0f / l_sum : 0.f;
         if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
         const int qrow = q_row0 + t * kBlockM + row;
         const bool valid = qrow < pr.q_hi;
@@ -500,9 +503,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t r[32];
-          tmem_ld32(tO + ch * 32, r);
-          tmem_wait_ld();
-          reg_fence32(r);
+          if (any) {
+            tmem_ld32(tO + ch * 32, r);
+            tmem_wait_ld();
+            reg_fence32(r);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) r[j] = 0u;
+          }
           uint32_t o[16];
 #pragma unroll
           for (int j = 0; j < 16; ++j)

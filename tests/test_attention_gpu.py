@@ -233,3 +233,128 @@ def test_large_480p_shape() -> None:
     ms = start.elapsed_time(stop) / 10
     flops = 4.0 * nq * nk * 128 * heads
     print(f"\n480p chunk attention: {ms:.3f} ms, {flops / ms / 1e9:.1f} TFLOP/s")
+
+
+# ---- large grids (more units than SMs), odd tile counts, short and partial KV ranges
+
+def _dense_case(heads: int, nq: int, kv_lo: int, nk: int, seed: int):
+    h3sa = _h3sa()
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    kv_rows = kv_lo + nk
+    q = torch.randn(nq, heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    k = torch.randn(kv_rows, heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    v = torch.randn(kv_rows, heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    pages = (kv_rows + 127) // 128
+    table = torch.randperm(pages, device="cuda", generator=gen).to(torch.int32)
+    kp = torch.zeros(heads, pages * 128, 128, dtype=torch.bfloat16, device="cuda")
+    vp = torch.zeros_like(kp)
+    h3sa.kv_copy_rows([k, v], [kp, vp], count=kv_rows, dst_table=table)
+    return q, k, v, kp, vp, table
+
+
+@pytest.mark.parametrize("nq,kv_lo,nk", [(15000, 50, 1100), (14900, 0, 1000), (14900, 130, 300)])
+def test_dense_split_across_ctas(nq: int, kv_lo: int, nk: int) -> None:
+    """More query-tile pairs than SMs, odd tile counts (a single-tile pair per head), partial
+    first/last KV blocks and a KV range of only 3 blocks."""
+
+    h3sa = _h3sa()
+    heads = 3
+    q, k, v, kp, vp, table = _dense_case(heads, nq, kv_lo, nk, seed=nq + nk)
+    out = torch.full_like(q, float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    h3sa.attention_fwd(q, out, kp, vp, table, [h3sa.AttentionProblem(0, nq, kv_lo, kv_lo + nk)],
+                       scale, device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = ref_attention(q, k[kv_lo:], v[kv_lo:], scale)
+    assert not torch.isnan(out).any()
+    assert rel_l2(out, ref) <= BF16_TOL
+    # every row individually (a wrongly merged piece shows up as a bad row)
+    row_err = ((out.float() - ref).norm(dim=-1) / ref.norm(dim=-1)).max()
+    assert float(row_err) <= 5e-2
+
+
+def test_fp8_split_across_ctas() -> None:
+    h3sa = _h3sa()
+    heads, nq, nk = 3, 14900, 1100
+    q, k, v, kp, vp, table = _dense_case(heads, nq, 0, nk, seed=99)
+    q8, qs = h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0))
+    k8 = torch.zeros_like(kp, dtype=torch.float8_e4m3fn)
+    v8 = torch.zeros_like(vp, dtype=torch.float8_e4m3fn)
+    ks = torch.empty(heads, dtype=torch.float32, device="cuda")
+    vs = torch.empty(heads, dtype=torch.float32, device="cuda")
+    h3sa.quantize_fp8_pool(kp, k8, ks, table, nk)
+    h3sa.quantize_fp8_pool(vp, v8, vs, table, nk)
+    out = torch.empty_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    h3sa.attention_fwd(q8.squeeze(0), out, k8, v8, table, [h3sa.AttentionProblem(0, nq, 0, nk)],
+                       scale, q_scale=qs.reshape(-1).contiguous(), k_scale=ks, v_scale=vs,
+                       device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    k8p, kss = h3sa.quantize_fp8_e4m3_per_head(k.unsqueeze(0))
+    v8p, vss = h3sa.quantize_fp8_e4m3_per_head(v.unsqueeze(0))
+    deq = lambda x8, sc: x8.squeeze(0).float() * sc.reshape(1, -1, 1)  # noqa: E731
+    ref_deq = ref_attention(deq(q8, qs), deq(k8p, kss), deq(v8p, vss), scale)
+    assert rel_l2(out, ref_deq) <= FP8_TOL
+
+
+def test_block_sparse_imbalanced_and_empty_units() -> None:
+    """One query block keeps every KV block, most keep a few, one pair keeps none (its rows
+    see no key and are written as zeros)."""
+
+    h3sa = _h3sa()
+    heads, nq, nk = 2, 1280, 20000
+    gen = torch.Generator().manual_seed(23)
+    q, k, v, kp, vp, table = _dense_case(heads, nq, 0, nk, seed=23)
+    qb, kb = nq // 128, (nk + 127) // 128
+    num = torch.zeros(heads, qb, dtype=torch.int32)
+    idx = torch.zeros(heads, qb, kb, dtype=torch.int32)
+    allowed = torch.zeros(heads, nq, nk, dtype=torch.bool)
+    for h in range(heads):
+        for j in range(qb):
+            if j in (2, 3):          # pair 1: no block at all
+                continue
+            if j == qb - 1:
+                keep = list(range(kb))
+            else:
+                keep = sorted(set(torch.randperm(kb, generator=gen)[: 3 + (j * 5 + h) % 17].tolist()))
+            num[h, j] = len(keep)
+            idx[h, j, : len(keep)] = torch.tensor(keep, dtype=torch.int32)
+            for b in keep:
+                allowed[h, j * 128:(j + 1) * 128, b * 128:(b + 1) * 128] = True
+    out = torch.full_like(q, float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    h3sa.attention_fwd(q, out, kp, vp, table, [h3sa.AttentionProblem(0, nq, 0, nk, sparse=True)],
+                       scale, kv_num_blocks=num.cuda(), kv_indices=idx.cuda(), device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    empty = slice(256, 512)
+    assert torch.count_nonzero(out[empty]) == 0
+    keep_rows = torch.ones(nq, dtype=torch.bool)
+    keep_rows[empty] = False
+    ref = ref_attention(q, k, v, scale, allowed.cuda())
+    assert rel_l2(out[keep_rows], ref[keep_rows.cuda()]) <= BF16_TOL
+
+
+def test_block_sparse_bad_list_reports_error() -> None:
+    """A list entry outside the problem's KV blocks sets the bad-index bit and the launch
+    ends (no wait is left hanging)."""
+
+    h3sa = _h3sa()
+    heads, nq, nk = 1, 256, 1024
+    q, k, v, kp, vp, table = _dense_case(heads, nq, 0, nk, seed=5)
+    num = torch.tensor([[3, 2]], dtype=torch.int32)
+    idx = torch.zeros(1, 2, 8, dtype=torch.int32)
+    idx[0, 0, :3] = torch.tensor([1, 4, 9], dtype=torch.int32)   # block 9 > the 8 KV blocks
+    idx[0, 1, :2] = torch.tensor([0, 7], dtype=torch.int32)
+    out = torch.empty_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    h3sa.attention_fwd(q, out, kp, vp, table, [h3sa.AttentionProblem(0, nq, 0, nk, sparse=True)],
+                       128 ** -0.5, kv_num_blocks=num.cuda(), kv_indices=idx.cuda(),
+                       device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) & 4
