@@ -395,7 +395,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int col0 = b * kBlockN;
         const int lo = pr.kv_lo - col0;  // valid columns [lo, hi)
         const int hi = pr.kv_hi - col0;
-        const bool partial = (lo > 0 || hi < kBlockN);
+        // Only the first and last block of a problem can be partial. The flag goes through an
+        // opaque move: otherwise the compiler can see that every per-column condition below
+        // implies it, drop the branch and run 2 x 128 compare/selects on every block.
+        int partial_i = (lo > 0 || hi < kBlockN) ? 1 : 0;
+        asm volatile("" : "+r"(partial_i));
+        const bool partial = partial_i != 0;
         if (partial) {
 #pragma unroll
           for (int j = 0; j < kBlockN; ++j)
