@@ -245,12 +245,16 @@ def run_reference(args: argparse.Namespace) -> None:
 class Step:
     """Device buffers and launches of one benchmark step on this rank."""
 
-    def __init__(self, world: int, rank: int, device: torch.device) -> None:
+    def __init__(self, world: int, rank: int, device: torch.device, fused: bool = True) -> None:
         import h3sa
         from h3sa.kernels import PAGE_ROWS
 
         self.h3sa = h3sa
         self.world, self.rank, self.device = world, rank, device
+        # SP > 1: the two Ulysses exchanges as peer stores (scatter kernel, attention epilogue)
+        # over NVLink, or NCCL all-to-all with layout copies (the reference's structure)
+        self.fused = fused and world > 1
+        self.phases = self.PHASES_FUSED if self.fused else self.PHASES
         geo = _geometry(world)
         self.geo = geo
         heads, d = CFG["heads"], CFG["head_dim"]
@@ -269,7 +273,15 @@ class Step:
         hist = torch.randn(nh, hl, d, device=device, generator=g).to(torch.bfloat16)
         h3sa.kv_copy_rows([hist, hist], [self.kpool, self.vpool], count=nh, dst_table=self.table)
         rows, tokens = geo["rows"], geo["tokens"]
-        if world > 1:
+        if self.fused:
+            from h3sa.peer import PeerBuffer
+
+            self.qkv_peer = PeerBuffer((3, rows, hl, d))
+            self.out_peer = PeerBuffer((tokens, heads, d))
+            self.qkv = self.qkv_peer.tensor
+            self.final = self.out_peer.tensor
+            self.flag = torch.zeros(1, dtype=torch.float32, device=device)
+        elif world > 1:
             self.send = torch.empty(world, 3, tokens, hl, d, dtype=torch.bfloat16, device=device)
             self.recv = torch.empty_like(self.send)
             self.qkv = torch.empty(3, rows, hl, d, dtype=torch.bfloat16, device=device)
@@ -288,35 +300,88 @@ class Step:
         self.flops = 4.0 * nq * (nh + nq) * d * hl  # this rank's algorithmic FLOPs
         self.launches_per_step = 2 + (4 if world > 1 else 0)
 
+    PHASES = ("pack", "qkv_all_to_all", "unpack", "cache_append", "attention", "o_all_to_all",
+              "o_unpack")
+    PHASES_FUSED = ("qkv_scatter", "barrier_before_attention", "unused", "cache_append",
+                    "attention_with_o_scatter", "barrier_after_attention", "unused2")
+    EXCHANGE_PHASES = ("qkv_all_to_all", "o_all_to_all", "qkv_scatter",
+                       "barrier_before_attention", "barrier_after_attention")
+
     def run(self, attn_events: tuple[torch.cuda.Event, torch.cuda.Event] | None = None,
-            merged: torch.Tensor | None = None) -> torch.Tensor:
+            merged: torch.Tensor | None = None,
+            marks: list[torch.cuda.Event] | None = None) -> torch.Tensor:
+        """One step; `marks` (len(PHASES) + 1 events) are recorded at the phase boundaries."""
+
         from h3sa.ulysses import pack_qkv_send, unpack_o_recv, unpack_qkv_recv
 
         h3sa, geo, hl = self.h3sa, self.geo, self.hl
         d, heads = CFG["head_dim"], CFG["heads"]
         src = self.merged if merged is None else merged
+
+        def mark(i: int) -> None:
+            if marks is not None:
+                marks[i].record()
+
+        mark(0)
+        if self.fused:
+            from h3sa.peer import attention_fwd_scatter, barrier, scatter_qkv
+
+            scatter_qkv(src, self.qkv_peer, num_heads=heads, head_dim=d)
+            mark(1)
+            barrier(flag=self.flag)
+            mark(2)
+            mark(3)
+            q, k, v = self.qkv[0], self.qkv[1], self.qkv[2]
+            h3sa.kv_copy_rows([k, v], [self.kpool, self.vpool], count=geo["rows"],
+                              dst_table=self.table, dst_start=self.n_hist, device_error=self.err)
+            mark(4)
+            if attn_events is not None:
+                attn_events[0].record()
+            attention_fwd_scatter(q, self.kpool, self.vpool, self.table, self.problems, self.scale,
+                                  self.out_peer, device_error=self.err)
+            if attn_events is not None:
+                attn_events[1].record()
+            mark(5)
+            barrier(flag=self.flag)
+            mark(6)
+            mark(7)
+            return self.final
         if self.world > 1:
             pack_qkv_send(src, self.send, world=self.world, num_heads=heads, head_dim=d)
+            mark(1)
             torch.distributed.all_to_all_single(self.recv, self.send)
+            mark(2)
             unpack_qkv_recv(self.recv, self.qkv, world=self.world, tokens=geo["tokens"],
                             local_heads=hl, head_dim=d)
         elif merged is not None:
             self.qkv.copy_(merged.view(geo["rows"], 3, heads, d).permute(1, 0, 2, 3))
+            mark(1)
+            mark(2)
+        else:
+            mark(1)
+            mark(2)
+        mark(3)
         q, k, v = self.qkv[0], self.qkv[1], self.qkv[2]
         # current chunk's K/V rows (media + pad document) after the history
         h3sa.kv_copy_rows([k, v], [self.kpool, self.vpool], count=geo["rows"], dst_table=self.table,
                           dst_start=self.n_hist, device_error=self.err)
+        mark(4)
         if attn_events is not None:
             attn_events[0].record()
         h3sa.attention_fwd(q, self.out, self.kpool, self.vpool, self.table, self.problems,
                            self.scale, device_error=self.err)
         if attn_events is not None:
             attn_events[1].record()
+        mark(5)
         if self.world > 1:
             torch.distributed.all_to_all_single(self.orecv, self.out)
+            mark(6)
             unpack_o_recv(self.orecv, self.final, world=self.world, tokens=geo["tokens"],
                           local_heads=hl, head_dim=d)
+            mark(7)
             return self.final
+        mark(6)
+        mark(7)
         return self.out
 
 
@@ -484,7 +549,7 @@ def run_h3sa(args: argparse.Namespace) -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    step = Step(world, rank, device)
+    step = Step(world, rank, device, fused=not args.unfused)
     peaks = _peaks()
 
     for _ in range(args.warmup):
@@ -494,6 +559,8 @@ def run_h3sa(args: argparse.Namespace) -> None:
                for _ in range(args.steps)]
     step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
+    phase_ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(step.phases) + 1)]
+                for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         _barrier(world)
@@ -502,7 +569,7 @@ def run_h3sa(args: argparse.Namespace) -> None:
         start.record()
         for i in range(args.steps):
             step_ev[i][0].record()
-            step.run(attn_ev[i])
+            step.run(attn_ev[i], marks=phase_ev[i])
             step_ev[i][1].record()
         stop.record()
         torch.cuda.synchronize()
@@ -510,6 +577,9 @@ def run_h3sa(args: argparse.Namespace) -> None:
         _barrier(world)
     total_ms = _max_over_ranks(start.elapsed_time(stop), world)
     attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
+    phases = {name: _max_over_ranks(statistics.median(ev[j].elapsed_time(ev[j + 1]) for ev in phase_ev),
+                                    world)
+              for j, name in enumerate(step.phases) if not name.startswith("unused")}
     step_ms = [a.elapsed_time(b) for a, b in step_ev]
     attn_avg = _max_over_ranks(sum(attn_ms) / len(attn_ms), world)
     p50 = _max_over_ranks(statistics.median(step_ms), world)
@@ -576,11 +646,16 @@ def run_h3sa(args: argparse.Namespace) -> None:
                         "current] keys, H=24, d=128, dense non-causal",
             "ulysses_sp": world, "heads_per_gpu": step.hl, "packed_rows": geo["rows"],
             "pad_rows": geo["pad"], "parallelism": f"sp{world}",
+            "exchange": ("peer stores over NVLink (scatter kernel + attention epilogue)" if step.fused
+                         else ("NCCL all_to_all_single + layout copies" if world > 1 else "none")),
             "l2": "inputs larger than L2 (Q 77 MB + K/V pool 355 MB at SP=1)",
         },
         "per_gpu_tflops": value / world,
         "tokens_per_s": geo["nq"] * args.steps / (total_ms * 1e-3),
-        "latency_ms": {"p50": p50, "p90": p90, "attention_kernel_avg": attn_avg},
+        "latency_ms": {"p50": p50, "p90": p90, "attention_kernel_avg": attn_avg,
+                       "phases_p50_max_over_ranks": phases,
+                       "p50_without_exchanges": p50 - sum(v for k_, v in phases.items()
+                                                          if k_ in Step.EXCHANGE_PHASES)},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peaks["bf16"],
                      "unit": "TFLOP/s", "frac": achieved / peaks["bf16"],
                      "frac_of_sustained": achieved / peaks["bf16_sustained"],
@@ -605,6 +680,8 @@ def main() -> None:
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-comparator", action="store_true")
+    ap.add_argument("--unfused", action="store_true",
+                    help="SP > 1: NCCL all-to-all + layout copies instead of peer stores")
     ap.add_argument("--no-variants", action="store_true",
                     help="skip the kernel-only FP8 1080p and block-sparse 768p timings")
     args = ap.parse_args()

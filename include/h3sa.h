@@ -90,6 +90,25 @@ H3SA_API int h3sa_attention_fwd(const void* query, void* out, int32_t rows, int3
                        int32_t q_blocks, int32_t kv_index_stride, int32_t* device_error,
                        void* stream);
 
+/* h3sa_attention_fwd with the Ulysses heads -> sequence exchange fused into the output store:
+ * query row r (of `rows`, the all-rank sequence) is written, for local head h, to
+ * out_peers[r / out_rows_per_rank] (a device array of out_ranks device addresses, this rank's
+ * IPC mappings of every rank's [out_rows_per_rank, out_heads, 128] bf16 output) at row
+ * r % out_rows_per_rank, head out_head0 + h. The stores go over NVLink to the other ranks;
+ * the caller orders them with the readers (a barrier after the launch on every rank).
+ * Replaces heads_to_sequence after the hook (T/distributed/ulysses.py:77-84): the O
+ * all-to-all and its layout copies. */
+H3SA_API int h3sa_attention_fwd_scatter(const void* query, int32_t rows, int32_t heads,
+                               int32_t head_dim, const void* key_pool, const void* value_pool,
+                               int32_t pool_pages, const int32_t* page_table,
+                               int32_t table_blocks, const h3sa_problem* problems,
+                               int32_t num_problems, float softmax_scale,
+                               const int32_t* kv_num_blocks, const int32_t* kv_indices,
+                               int32_t q_blocks, int32_t kv_index_stride,
+                               const uint64_t* out_peers, int32_t out_ranks,
+                               int32_t out_rows_per_rank, int32_t out_heads, int32_t out_head0,
+                               int32_t* device_error, void* stream);
+
 /* The same attention on e4m3 query and KV pools with per-head dequantisation scales
  * (q_scale, k_scale, v_scale: fp32 [heads], device), bf16 output: the FP8 FlashAttention-3
  * call with q/k/v_descale (F/streaming/attention_hook.py:1081-1107). */
@@ -198,6 +217,27 @@ H3SA_API int h3sa_block_mask(const void* query, int32_t rows, int32_t heads, int
                              int32_t table_blocks, const h3sa_mask_policy* policy,
                              int32_t* kv_num_blocks, int32_t* kv_indices,
                              int32_t kv_index_stride, int32_t* device_error, void* stream);
+
+/* Peer memory for the fused Ulysses exchanges (no counterpart in the reference, whose
+ * exchange is torch.distributed.all_to_all_single over NCCL). h3sa_peer_alloc returns
+ * cudaMalloc memory that h3sa_ipc_handle exports (a 64-byte cudaIpcMemHandle_t) and that
+ * another process on the node maps with h3sa_ipc_open (close with h3sa_ipc_close). */
+H3SA_API int h3sa_peer_alloc(size_t bytes, void** ptr);
+H3SA_API int h3sa_peer_free(void* ptr);
+H3SA_API int h3sa_ipc_handle(const void* ptr, void* handle);
+H3SA_API int h3sa_ipc_open(const void* handle, void** ptr);
+H3SA_API int h3sa_ipc_close(void* ptr);
+
+/* Sequence -> heads exchange as one kernel: this rank's merged QKV shard
+ * [tokens, 3, heads, 128] bf16 (post prologue) is stored straight into the attention-ready
+ * q/k/v planes [3, world * tokens, heads / world, 128] of the rank owning each head, at rows
+ * [rank * tokens, (rank + 1) * tokens). peer_qkv: device array of world device addresses (this
+ * rank's IPC mappings of every rank's planes). Replaces merged_qkv_sequence_to_heads
+ * (T/distributed/ulysses.py:103-132): the send permute, the all-to-all and the receive
+ * permute. The caller orders the stores with the readers (a barrier before attention). */
+H3SA_API int h3sa_scatter_qkv(const void* merged, int32_t tokens, int32_t heads,
+                              int32_t head_dim, int32_t world, int32_t rank,
+                              const uint64_t* peer_qkv, void* stream);
 
 #ifdef __cplusplus
 }

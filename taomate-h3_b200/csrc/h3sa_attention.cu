@@ -503,8 +503,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
         const int qrow = q_row0 + t * kBlockM + row;
         const bool valid = qrow < pr.q_hi;
-        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
-                             (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim;
+        __nv_bfloat16* dst;
+        if (p.out_peers) {
+          // heads -> sequence exchange fused into the store: row qrow belongs to the sequence
+          // shard of rank qrow / rows_per_rank, which holds all heads of its rows
+          const int owner = min(qrow / p.out_rows_per_rank, p.out_ranks - 1);
+          const int orow = qrow - owner * p.out_rows_per_rank;
+          dst = reinterpret_cast<__nv_bfloat16*>(static_cast<uintptr_t>(p.out_peers[owner])) +
+                (static_cast<size_t>(orow) * p.out_heads + p.out_head0 + head) * kHeadDim;
+        } else {
+          dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
+                (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim;
+        }
 #pragma unroll
         for (int ch = 0; ch < 4; ++ch) {
           uint32_t r[32];
@@ -528,6 +538,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
               d4[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
           }
         }
+        // peer stores: make them visible system-wide before the kernel is seen as done
+        if (p.out_peers) __threadfence_system();
       }
     }
   }
@@ -589,6 +601,11 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   prm.q_blocks = L.q_blocks;
   prm.kv_stride = L.kv_stride;
   prm.err = L.device_error;
+  prm.out_peers = L.out_peers;
+  prm.out_ranks = L.out_ranks;
+  prm.out_rows_per_rank = L.out_rows_per_rank;
+  prm.out_heads = L.out_heads;
+  prm.out_head0 = L.out_head0;
   int ctas = 0;
   int n = 0;
   for (int i = 0; i < L.num_problems; ++i) {

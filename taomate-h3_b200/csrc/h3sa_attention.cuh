@@ -73,6 +73,12 @@ struct AttnParams {
   int q_blocks;
   int kv_stride;
   int* err;                  // device error word (nullable)
+  // output rows scattered to peers (see AttnLaunch in h3sa_host.h); null: write `out`
+  const uint64_t* out_peers;
+  int out_ranks;
+  int out_rows_per_rank;
+  int out_heads;
+  int out_head0;
 };
 
 }  // namespace h3sa

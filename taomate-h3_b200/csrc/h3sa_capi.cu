@@ -152,6 +152,55 @@ int h3sa_attention_fwd(const void* query, void* out, int32_t rows, int32_t heads
   return attention_launch(L, false, static_cast<cudaStream_t>(stream));
 }
 
+int h3sa_attention_fwd_scatter(const void* query, int32_t rows, int32_t heads, int32_t head_dim,
+                               const void* key_pool, const void* value_pool, int32_t pool_pages,
+                               const int32_t* page_table, int32_t table_blocks,
+                               const h3sa_problem* problems, int32_t num_problems,
+                               float softmax_scale, const int32_t* kv_num_blocks,
+                               const int32_t* kv_indices, int32_t q_blocks,
+                               int32_t kv_index_stride, const uint64_t* out_peers,
+                               int32_t out_ranks, int32_t out_rows_per_rank, int32_t out_heads,
+                               int32_t out_head0, int32_t* device_error, void* stream) {
+  // `out` is not used on this path; the argument check wants a non-null, aligned pointer
+  int rc = check_attention_args(query, const_cast<void*>(query), rows, heads, head_dim, key_pool,
+                                value_pool,
+                                pool_pages, page_table, table_blocks, problems, num_problems,
+                                kv_num_blocks, kv_indices, q_blocks, kv_index_stride);
+  if (rc) return rc;
+  if (!out_peers || out_ranks <= 0 || out_rows_per_rank <= 0 || out_head0 < 0 ||
+      out_head0 + heads > out_heads)
+    return set_error(H3SA_ERR_INVALID, "attention scatter: invalid output layout (ranks %d, "
+                     "rows per rank %d, heads %d + %d of %d)", out_ranks, out_rows_per_rank,
+                     out_head0, heads, out_heads);
+  if (static_cast<int64_t>(out_ranks) * out_rows_per_rank < rows)
+    return set_error(H3SA_ERR_INVALID, "attention scatter: %d ranks x %d rows do not cover %d "
+                     "query rows", out_ranks, out_rows_per_rank, rows);
+  AttnLaunch L{};
+  L.query = query;
+  L.out = nullptr;
+  L.rows = rows;
+  L.heads = heads;
+  L.key_pool = key_pool;
+  L.value_pool = value_pool;
+  L.pool_pages = pool_pages;
+  L.page_table = page_table;
+  L.table_blocks = table_blocks;
+  L.problems = problems;
+  L.num_problems = num_problems;
+  L.softmax_scale = softmax_scale;
+  L.kv_num_blocks = kv_num_blocks;
+  L.kv_indices = kv_indices;
+  L.q_blocks = q_blocks;
+  L.kv_stride = kv_index_stride;
+  L.device_error = device_error;
+  L.out_peers = out_peers;
+  L.out_ranks = out_ranks;
+  L.out_rows_per_rank = out_rows_per_rank;
+  L.out_heads = out_heads;
+  L.out_head0 = out_head0;
+  return attention_launch(L, false, static_cast<cudaStream_t>(stream));
+}
+
 int h3sa_attention_fwd_fp8(const void* query, void* out, int32_t rows, int32_t heads,
                            int32_t head_dim, const void* key_pool, const void* value_pool,
                            int32_t pool_pages, const int32_t* page_table, int32_t table_blocks,

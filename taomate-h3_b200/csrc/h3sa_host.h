@@ -41,6 +41,14 @@ struct AttnLaunch {
   int q_blocks;
   int kv_stride;
   int32_t* device_error;
+  // Output to peers (Ulysses heads -> sequence fused into the epilogue): when set, query row r
+  // is written to out_peers[r / out_rows_per_rank] at row r % out_rows_per_rank of a
+  // [rows_per_rank, out_heads, 128] tensor, head out_head0 + h. Otherwise to `out`.
+  const uint64_t* out_peers;
+  int out_ranks;
+  int out_rows_per_rank;
+  int out_heads;
+  int out_head0;
 };
 
 int attention_launch(const AttnLaunch& L, bool fp8, cudaStream_t stream);

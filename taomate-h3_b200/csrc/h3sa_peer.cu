@@ -1,0 +1,131 @@
+// Peer memory for the fused Ulysses exchanges over NVLink.
+//
+// The sequence -> heads exchange before attention and the heads -> sequence exchange after it
+// are all-to-alls between the ranks of one node. Instead of NCCL all-to-all plus layout copies
+// on both sides, each rank writes straight into the other ranks' buffers through CUDA IPC
+// mappings: h3sa_scatter_qkv stores this rank's rows of every head into the attention-ready
+// q/k/v planes of the rank that owns the head, and the attention epilogue stores each output
+// row into the sequence shard of the rank that owns the row (h3sa_attention_fwd_scatter).
+// Plain 16-byte stores to peer memory over NVLink; no bulk or tensor copy touches a peer.
+#include <cuda_runtime.h>
+
+#include <cstring>
+
+#include "h3sa_host.h"
+
+namespace h3sa {
+
+constexpr int kPeerHeadDim = 128;
+
+struct ScatterParams {
+  const uint4* src;         // [tokens, 3, heads, 128] bf16, this rank's sequence shard
+  const uint64_t* peers;    // [world] base of each rank's [3, world * tokens, heads_local, 128]
+  int tokens;
+  int heads;
+  int heads_local;
+  int world;
+  int rank;
+};
+
+// One thread per 16-byte chunk: chunk c of (token t, plane w, head h) goes to the rank owning h,
+// at plane w, row rank * tokens + t, local head h % heads_local. Reads are contiguous; each
+// destination row of 256 bytes is written by 16 consecutive threads.
+__global__ void scatter_qkv_kernel(const ScatterParams p) {
+  constexpr int kChunks = kPeerHeadDim * 2 / 16;  // 16-byte chunks per row
+  const long long total = static_cast<long long>(p.tokens) * 3 * p.heads * kChunks;
+  const long long rows_all = static_cast<long long>(p.world) * p.tokens;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % kChunks);
+    long long r = i / kChunks;
+    const int h = static_cast<int>(r % p.heads);
+    r /= p.heads;
+    const int w = static_cast<int>(r % 3);
+    const long long t = r / 3;
+    const int dest = h / p.heads_local;
+    const int hl = h - dest * p.heads_local;
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<uintptr_t>(__ldg(p.peers + dest)));
+    const long long drow = (w * rows_all + static_cast<long long>(p.rank) * p.tokens + t) *
+                               p.heads_local + hl;
+    dst[drow * kChunks + c] = __ldg(p.src + i);
+  }
+  __threadfence_system();
+}
+
+}  // namespace h3sa
+
+using namespace h3sa;
+
+extern "C" {
+
+int h3sa_peer_alloc(size_t bytes, void** ptr) {
+  if (!ptr || bytes == 0) return set_error(H3SA_ERR_INVALID, "peer_alloc: invalid arguments");
+  *ptr = nullptr;
+  cudaError_t e = cudaMalloc(ptr, bytes);
+  if (e != cudaSuccess) return set_cuda_error("cudaMalloc(peer buffer)", e);
+  return H3SA_OK;
+}
+
+int h3sa_peer_free(void* ptr) {
+  if (!ptr) return H3SA_OK;
+  cudaError_t e = cudaFree(ptr);
+  if (e != cudaSuccess) return set_cuda_error("cudaFree(peer buffer)", e);
+  return H3SA_OK;
+}
+
+int h3sa_ipc_handle(const void* ptr, void* handle) {
+  if (!ptr || !handle) return set_error(H3SA_ERR_INVALID, "ipc_handle: null argument");
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return set_cuda_error("cudaIpcGetMemHandle", e);
+  std::memcpy(handle, &h, sizeof(h));
+  return H3SA_OK;
+}
+
+int h3sa_ipc_open(const void* handle, void** ptr) {
+  if (!handle || !ptr) return set_error(H3SA_ERR_INVALID, "ipc_open: null argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_cuda_error("cudaIpcOpenMemHandle", e);
+  return H3SA_OK;
+}
+
+int h3sa_ipc_close(void* ptr) {
+  if (!ptr) return H3SA_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  if (e != cudaSuccess) return set_cuda_error("cudaIpcCloseMemHandle", e);
+  return H3SA_OK;
+}
+
+int h3sa_scatter_qkv(const void* merged, int32_t tokens, int32_t heads, int32_t head_dim,
+                     int32_t world, int32_t rank, const uint64_t* peer_qkv, void* stream) {
+  if (head_dim != kPeerHeadDim)
+    return set_error(H3SA_ERR_UNSUPPORTED, "scatter_qkv: head_dim must be 128, got %d", head_dim);
+  if (!merged || !peer_qkv || tokens <= 0 || heads <= 0 || world <= 0 || rank < 0 ||
+      rank >= world)
+    return set_error(H3SA_ERR_INVALID, "scatter_qkv: invalid arguments");
+  if (heads % world)
+    return set_error(H3SA_ERR_INVALID, "scatter_qkv: num_heads=%d not divisible by Ulysses "
+                     "world size %d", heads, world);
+  if (reinterpret_cast<uintptr_t>(merged) & 15)
+    return set_error(H3SA_ERR_INVALID, "scatter_qkv: input must be 16-byte aligned");
+  ScatterParams p;
+  p.src = static_cast<const uint4*>(merged);
+  p.peers = peer_qkv;
+  p.tokens = tokens;
+  p.heads = heads;
+  p.heads_local = heads / world;
+  p.world = world;
+  p.rank = rank;
+  const long long work = static_cast<long long>(tokens) * 3 * heads * (kPeerHeadDim * 2 / 16);
+  long long blocks = (work + 255) / 256;
+  if (blocks > 148LL * 8) blocks = 148LL * 8;
+  scatter_qkv_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("scatter_qkv_kernel launch", e);
+  return H3SA_OK;
+}
+
+}  // extern "C"

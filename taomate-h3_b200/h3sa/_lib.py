@@ -95,6 +95,17 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         ctypes.c_int,
         [_P, _I, _I, _I, _I, _I, _P, _I, _P, _I, ctypes.POINTER(MaskPolicy), _P, _P, _I, _P, _P],
     ),
+    "h3sa_attention_fwd_scatter": (
+        ctypes.c_int,
+        [_P, _I, _I, _I, _P, _P, _I, _P, _I, ctypes.POINTER(Problem), _I, _F, _P, _P, _I, _I,
+         _P, _I, _I, _I, _I, _P, _P],
+    ),
+    "h3sa_peer_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "h3sa_peer_free": (ctypes.c_int, [_P]),
+    "h3sa_ipc_handle": (ctypes.c_int, [_P, _P]),
+    "h3sa_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
+    "h3sa_ipc_close": (ctypes.c_int, [_P]),
+    "h3sa_scatter_qkv": (ctypes.c_int, [_P, _I, _I, _I, _I, _I, _P, _P]),
     "h3sa_permute_rows": (
         ctypes.c_int,
         [_P, _P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),

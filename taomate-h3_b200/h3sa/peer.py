@@ -1,0 +1,154 @@
+"""Peer buffers and the fused Ulysses exchanges over NVLink (one process per GPU, one node).
+
+The reference exchanges Ulysses shards with ``torch.distributed.all_to_all_single`` plus a
+layout copy on each side (``T/distributed/ulysses.py:10-132``). Here every rank maps every
+other rank's exchange buffers through CUDA IPC once, and the kernels store across NVLink
+directly: ``scatter_qkv`` writes this rank's rows of every head into the attention-ready q/k/v
+planes of the rank owning the head; ``attention_fwd_scatter`` writes each output row into the
+sequence shard of the rank owning the row. A ``barrier`` (a one-element all-reduce, ordered on
+the stream) separates the writers from the readers.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Sequence
+
+import torch
+
+from . import _lib
+from ._lib import call, ptr, stream_handle
+from .kernels import PAGE_ROWS, AttentionProblem, _problems, _require_cuda
+
+_IPC_HANDLE_BYTES = 64
+
+
+class _CudaArray:
+    """Minimal ``__cuda_array_interface__`` owner so torch can wrap a raw allocation."""
+
+    def __init__(self, address: int, shape: tuple[int, ...], typestr: str) -> None:
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": typestr,
+                                         "data": (address, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerBuffer:
+    """A bf16 device buffer of the same shape on every rank of ``group``, mapped by all.
+
+    ``tensor`` is this rank's buffer; ``peer_table`` is an int64 device tensor holding the
+    address of every rank's buffer as mapped in this process (its own at index ``rank``).
+    Collective: every rank of the group constructs it with the same shape.
+    """
+
+    def __init__(self, shape: Sequence[int], group=None) -> None:
+        import torch.distributed as dist
+
+        self.shape = tuple(int(s) for s in shape)
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        nbytes = math.prod(self.shape) * 2
+        addr = ctypes.c_void_p()
+        call("h3sa_peer_alloc", ctypes.c_size_t(nbytes), ctypes.byref(addr))
+        self._local = int(addr.value)
+        self._opened: list[int] = []
+        self._owner = _CudaArray(self._local, self.shape, "<i2")
+        self.tensor = torch.as_tensor(self._owner, device="cuda").view(torch.bfloat16)
+        handle = (ctypes.c_char * _IPC_HANDLE_BYTES)()
+        call("h3sa_ipc_handle", self._local, handle)
+        handles: list[bytes | None] = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        addresses = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                addresses.append(self._local)
+                continue
+            opened = ctypes.c_void_p()
+            buf = (ctypes.c_char * _IPC_HANDLE_BYTES).from_buffer_copy(h)
+            call("h3sa_ipc_open", buf, ctypes.byref(opened))
+            self._opened.append(int(opened.value))
+            addresses.append(int(opened.value))
+        self.peer_table = torch.tensor(addresses, dtype=torch.int64, device="cuda")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective in practice: peers
+        must be done with this rank's buffer)."""
+
+        for a in self._opened:
+            _lib.LIB.h3sa_ipc_close(a)
+        self._opened = []
+        if self._local:
+            del self.tensor
+            _lib.LIB.h3sa_peer_free(self._local)
+            self._local = 0
+
+
+def barrier(group=None, flag: torch.Tensor | None = None) -> None:
+    """Stream-ordered barrier: a one-element all-reduce. Kernels enqueued after it on any rank
+    start after every rank's kernels enqueued before it have finished."""
+
+    import torch.distributed as dist
+
+    t = flag if flag is not None else torch.zeros(1, dtype=torch.float32, device="cuda")
+    dist.all_reduce(t, group=group)
+
+
+def scatter_qkv(merged: torch.Tensor, qkv: PeerBuffer, *, num_heads: int, head_dim: int = 128,
+                stream: torch.cuda.Stream | None = None) -> None:
+    """Sequence -> heads: this rank's post-prologue shard ``[T, 3 * H * d]`` (or
+    ``[T, 3, H, d]``) stored into every owner rank's ``[3, W * T, H / W, d]`` planes."""
+
+    _require_cuda(merged)
+    if merged.dtype != torch.bfloat16 or not merged.is_contiguous():
+        raise ValueError("scatter_qkv expects a contiguous bf16 merged QKV shard")
+    tokens = int(merged.shape[0])
+    world = qkv.world
+    if num_heads % world:
+        raise ValueError(f"num_heads={num_heads} must be divisible by Ulysses world size {world}")
+    if merged.numel() != tokens * 3 * num_heads * head_dim:
+        raise ValueError("merged QKV shard must hold 3 * num_heads * head_dim values per token")
+    if qkv.shape != (3, world * tokens, num_heads // world, head_dim):
+        raise ValueError(f"peer q/k/v planes must be [3, {world * tokens}, "
+                         f"{num_heads // world}, {head_dim}], got {list(qkv.shape)}")
+    call("h3sa_scatter_qkv", ptr(merged), tokens, num_heads, head_dim, world, qkv.rank,
+         ptr(qkv.peer_table), stream_handle(stream))
+
+
+def attention_fwd_scatter(
+    query: torch.Tensor,
+    key_pool: torch.Tensor,
+    value_pool: torch.Tensor,
+    page_table: torch.Tensor,
+    problems: Sequence[AttentionProblem],
+    softmax_scale: float,
+    out: PeerBuffer,
+    *,
+    kv_num_blocks: torch.Tensor | None = None,
+    kv_indices: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """Attention whose output rows go straight to the owning rank's sequence shard
+    ``out`` (``[T, H, d]`` on every rank): heads -> sequence fused into the store."""
+
+    _require_cuda(query, key_pool, value_pool, page_table, kv_num_blocks, kv_indices)
+    rows, heads, head_dim = (int(s) for s in query.shape)
+    if query.dtype != torch.bfloat16 or key_pool.dtype != torch.bfloat16:
+        raise RuntimeError("attention takes bf16 query and KV pools")
+    tokens, heads_total = out.shape[0], out.shape[1]
+    if out.shape[2] != head_dim or tokens * out.world < rows:
+        raise ValueError("output shard must be [T, H, d] with W * T covering the query rows")
+    pool_pages = int(key_pool.shape[1]) // PAGE_ROWS
+    q_blocks = stride = 0
+    if kv_num_blocks is not None:
+        q_blocks = int(kv_num_blocks.shape[-1])
+        stride = int(kv_indices.shape[-1])
+    call("h3sa_attention_fwd_scatter", ptr(query), rows, heads, head_dim, ptr(key_pool),
+         ptr(value_pool), pool_pages, ptr(page_table), int(page_table.numel()),
+         _problems(problems), len(problems), float(softmax_scale), ptr(kv_num_blocks),
+         ptr(kv_indices), q_blocks, stride, ptr(out.peer_table), out.world, tokens, heads_total,
+         out.rank * heads, ptr(device_error), stream_handle(stream))
+
+
+__all__ = ["PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv"]

@@ -1,0 +1,116 @@
+"""Fused Ulysses exchanges over peer memory against the NCCL all-to-all path (2+ GPUs).
+
+Two ranks, one process per GPU (NCCL). Each rank holds a seeded post-prologue QKV shard;
+the NCCL path (pack, all_to_all_single, unpack / attention / all_to_all_single, unpack) and
+the fused path (scatter_qkv into peer q/k/v planes / attention storing into peer output
+shards) must give bit-identical q/k/v planes and final outputs: both run the same kernels and
+differ only in where the bytes go. Skipped with fewer than two GPUs.
+"""
+
+from __future__ import annotations
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int) -> None:
+    import datetime
+
+    sys.path.insert(0, str(ROOT / "taomate-h3_b200"))
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        import h3sa
+        from h3sa.kernels import PAGE_ROWS
+        from h3sa.peer import PeerBuffer, attention_fwd_scatter, barrier, scatter_qkv
+        from h3sa.ulysses import pack_qkv_send, unpack_o_recv, unpack_qkv_recv
+
+        heads, d, tokens, hist = 4, 128, 300, 256
+        hl, rows = heads // world, tokens * world
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        merged = torch.randn(tokens, 3 * heads * d, device=dev, generator=g).to(torch.bfloat16)
+        hist_kv = torch.randn(hist, hl, d, device=dev,
+                              generator=torch.Generator(device=dev).manual_seed(7 + rank)).to(torch.bfloat16)
+        pages = (hist + rows + PAGE_ROWS - 1) // PAGE_ROWS
+        table = torch.arange(pages, dtype=torch.int32, device=dev)
+        scale = d ** -0.5
+        probs = [h3sa.AttentionProblem(0, rows - 20, 0, hist + rows - 20),
+                 h3sa.AttentionProblem(rows - 20, rows, hist + rows - 20, hist + rows)]
+
+        def pools():
+            kp = torch.zeros(hl, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=dev)
+            vp = torch.zeros_like(kp)
+            h3sa.kv_copy_rows([hist_kv, hist_kv], [kp, vp], count=hist, dst_table=table)
+            return kp, vp
+
+        # NCCL path
+        send = torch.empty(world, 3, tokens, hl, d, dtype=torch.bfloat16, device=dev)
+        recv = torch.empty_like(send)
+        qkv_ref = torch.empty(3, rows, hl, d, dtype=torch.bfloat16, device=dev)
+        pack_qkv_send(merged, send, world=world, num_heads=heads, head_dim=d)
+        torch.distributed.all_to_all_single(recv, send)
+        unpack_qkv_recv(recv, qkv_ref, world=world, tokens=tokens, local_heads=hl, head_dim=d)
+        kp, vp = pools()
+        h3sa.kv_copy_rows([qkv_ref[1], qkv_ref[2]], [kp, vp], count=rows, dst_table=table,
+                          dst_start=hist)
+        out = torch.empty(rows, hl, d, dtype=torch.bfloat16, device=dev)
+        h3sa.attention_fwd(qkv_ref[0], out, kp, vp, table, probs, scale)
+        orecv = torch.empty(world, tokens, hl, d, dtype=torch.bfloat16, device=dev)
+        final_ref = torch.empty(tokens, heads, d, dtype=torch.bfloat16, device=dev)
+        torch.distributed.all_to_all_single(orecv, out)
+        unpack_o_recv(orecv, final_ref, world=world, tokens=tokens, local_heads=hl, head_dim=d)
+
+        # fused path, twice (the second run overwrites buffers the first one filled)
+        qkv_peer = PeerBuffer((3, rows, hl, d))
+        out_peer = PeerBuffer((tokens, heads, d))
+        err = torch.zeros(1, dtype=torch.int32, device=dev)
+        for _ in range(2):
+            qkv_peer.tensor.zero_()
+            out_peer.tensor.zero_()
+            barrier()
+            scatter_qkv(merged, qkv_peer, num_heads=heads, head_dim=d)
+            barrier()
+            assert torch.equal(qkv_peer.tensor, qkv_ref), "q/k/v planes differ"
+            kp2, vp2 = pools()
+            h3sa.kv_copy_rows([qkv_peer.tensor[1], qkv_peer.tensor[2]], [kp2, vp2], count=rows,
+                              dst_table=table, dst_start=hist)
+            attention_fwd_scatter(qkv_peer.tensor[0], kp2, vp2, table, probs, scale, out_peer,
+                                  device_error=err)
+            barrier()
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            assert torch.equal(out_peer.tensor, final_ref), "final sequence shards differ"
+        barrier()
+        torch.cuda.synchronize()
+        qkv_peer.close()
+        out_peer.close()
+    finally:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+def test_fused_exchanges_match_nccl_path() -> None:
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
