@@ -276,8 +276,11 @@ class Step:
         if self.fused:
             from h3sa.peer import PeerBuffer
 
+            from h3sa.peer import PeerBarrier
+
             self.qkv_peer = PeerBuffer((3, rows, hl, d))
             self.out_peer = PeerBuffer((tokens, heads, d))
+            self.peer_barrier = PeerBarrier(device_error=None)
             self.qkv = self.qkv_peer.tensor
             self.final = self.out_peer.tensor
             self.flag = torch.zeros(1, dtype=torch.float32, device=device)
@@ -291,6 +294,8 @@ class Step:
             self.qkv = self.merged.view(rows, 3, heads, d).permute(1, 0, 2, 3).contiguous()
         self.out = torch.empty(rows, hl, d, dtype=torch.bfloat16, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
+        if self.fused:
+            self.peer_barrier.err = self.err  # a barrier wait that gives up shows in device_error
         P = h3sa.AttentionProblem
         nq, pad = geo["nq"], geo["pad"]
         self.problems = [P(0, nq, 0, nh + nq)]
@@ -324,11 +329,11 @@ class Step:
 
         mark(0)
         if self.fused:
-            from h3sa.peer import attention_fwd_scatter, barrier, scatter_qkv
+            from h3sa.peer import attention_fwd_scatter, scatter_qkv
 
             scatter_qkv(src, self.qkv_peer, num_heads=heads, head_dim=d)
             mark(1)
-            barrier(flag=self.flag)
+            self.peer_barrier()
             mark(2)
             mark(3)
             q, k, v = self.qkv[0], self.qkv[1], self.qkv[2]
@@ -342,7 +347,7 @@ class Step:
             if attn_events is not None:
                 attn_events[1].record()
             mark(5)
-            barrier(flag=self.flag)
+            self.peer_barrier()
             mark(6)
             mark(7)
             return self.final

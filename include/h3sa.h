@@ -235,6 +235,15 @@ H3SA_API int h3sa_ipc_close(void* ptr);
  * rank's IPC mappings of every rank's planes). Replaces merged_qkv_sequence_to_heads
  * (T/distributed/ulysses.py:103-132): the send permute, the all-to-all and the receive
  * permute. The caller orders the stores with the readers (a barrier before attention). */
+/* Barrier of the ranks of one node over peer memory, ordered on `stream`: stores `epoch`
+ * into slot `rank` of every rank's uint32 flag array (peer_flags: device array of world device
+ * addresses, this rank's mappings of every rank's array, zero-initialised) and waits until its
+ * own array holds at least `epoch` in every slot. Work enqueued after it on any rank starts
+ * after every rank's work enqueued before it. `epoch` must grow by one per call (wrapping
+ * compare); a wait that gives up after 2 s sets H3SA_DEVERR_WAIT_TIMEOUT in device_error. */
+H3SA_API int h3sa_peer_barrier(const uint64_t* peer_flags, int32_t world, int32_t rank,
+                               uint32_t epoch, int32_t* device_error, void* stream);
+
 H3SA_API int h3sa_scatter_qkv(const void* merged, int32_t tokens, int32_t heads,
                               int32_t head_dim, int32_t world, int32_t rank,
                               const uint64_t* peer_qkv, void* stream);

@@ -27,29 +27,83 @@ struct ScatterParams {
   int rank;
 };
 
-// One thread per 16-byte chunk: chunk c of (token t, plane w, head h) goes to the rank owning h,
-// at plane w, row rank * tokens + t, local head h % heads_local. Reads are contiguous; each
-// destination row of 256 bytes is written by 16 consecutive threads.
+// 16-byte chunk c of (token t, plane w, head h) goes to the rank owning h, at plane w, row
+// rank * tokens + t, local head h % heads_local. Reads are contiguous; each destination row of
+// 256 bytes is written by 16 consecutive threads. Every thread moves kUnroll chunks a grid
+// stride apart, loads first, so that that many stores per thread are in flight over NVLink.
+constexpr int kScatterUnroll = 4;
+
+__device__ __forceinline__ uint4* scatter_dst(const ScatterParams& p, long long i) {
+  constexpr int kChunks = kPeerHeadDim * 2 / 16;
+  const int c = static_cast<int>(i % kChunks);
+  long long r = i / kChunks;
+  const int h = static_cast<int>(r % p.heads);
+  r /= p.heads;
+  const int w = static_cast<int>(r % 3);
+  const long long t = r / 3;
+  const int dest = h / p.heads_local;
+  const int hl = h - dest * p.heads_local;
+  const long long rows_all = static_cast<long long>(p.world) * p.tokens;
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<uintptr_t>(__ldg(p.peers + dest)));
+  const long long drow =
+      (w * rows_all + static_cast<long long>(p.rank) * p.tokens + t) * p.heads_local + hl;
+  return dst + drow * kChunks + c;
+}
+
 __global__ void scatter_qkv_kernel(const ScatterParams p) {
   constexpr int kChunks = kPeerHeadDim * 2 / 16;  // 16-byte chunks per row
   const long long total = static_cast<long long>(p.tokens) * 3 * p.heads * kChunks;
-  const long long rows_all = static_cast<long long>(p.world) * p.tokens;
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int c = static_cast<int>(i % kChunks);
-    long long r = i / kChunks;
-    const int h = static_cast<int>(r % p.heads);
-    r /= p.heads;
-    const int w = static_cast<int>(r % 3);
-    const long long t = r / 3;
-    const int dest = h / p.heads_local;
-    const int hl = h - dest * p.heads_local;
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<uintptr_t>(__ldg(p.peers + dest)));
-    const long long drow = (w * rows_all + static_cast<long long>(p.rank) * p.tokens + t) *
-                               p.heads_local + hl;
-    dst[drow * kChunks + c] = __ldg(p.src + i);
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long base = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x;
+       base < total; base += stride * kScatterUnroll) {
+    uint4 v[kScatterUnroll];
+#pragma unroll
+    for (int u = 0; u < kScatterUnroll; ++u) {
+      const long long i = base + u * stride;
+      if (i < total) v[u] = __ldg(p.src + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kScatterUnroll; ++u) {
+      const long long i = base + u * stride;
+      if (i < total) *scatter_dst(p, i) = v[u];
+    }
   }
   __threadfence_system();
+}
+
+// Barrier over peer memory for the ranks of one node: every rank stores `epoch` into slot
+// `rank` of every rank's flag array (release, system scope), then waits until all slots of
+// its own array hold at least `epoch` (acquire). One thread per peer. The wait is bounded:
+// after 2 s it sets H3SA_DEVERR_WAIT_TIMEOUT in `err` and returns.
+constexpr long long kBarrierSpinNs = 2000000000LL;  // 2 s
+
+__global__ void peer_barrier_kernel(const uint64_t* flags, int world, int rank,
+                                    unsigned int epoch, int* err) {
+  const int q = threadIdx.x;
+  if (q < world) {
+    unsigned int* remote =
+        reinterpret_cast<unsigned int*>(static_cast<uintptr_t>(flags[q])) + rank;
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(remote), "r"(epoch) : "memory");
+  }
+  __syncthreads();
+  if (q < world) {
+    const unsigned int* mine =
+        reinterpret_cast<const unsigned int*>(static_cast<uintptr_t>(flags[rank])) + q;
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(mine) : "memory");
+      if (static_cast<int>(v - epoch) >= 0) break;
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+      if (static_cast<long long>(t - t0) > kBarrierSpinNs) {
+        if (err) atomicOr(err, H3SA_DEVERR_WAIT_TIMEOUT);
+        break;
+      }
+    }
+  }
+  __syncthreads();
 }
 
 }  // namespace h3sa
@@ -121,10 +175,21 @@ int h3sa_scatter_qkv(const void* merged, int32_t tokens, int32_t heads, int32_t 
   p.rank = rank;
   const long long work = static_cast<long long>(tokens) * 3 * heads * (kPeerHeadDim * 2 / 16);
   long long blocks = (work + 255) / 256;
-  if (blocks > 148LL * 8) blocks = 148LL * 8;
+  if (blocks > 148LL * 16) blocks = 148LL * 16;
   scatter_qkv_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("scatter_qkv_kernel launch", e);
+  return H3SA_OK;
+}
+
+int h3sa_peer_barrier(const uint64_t* peer_flags, int32_t world, int32_t rank, uint32_t epoch,
+                      int32_t* device_error, void* stream) {
+  if (!peer_flags || world <= 0 || world > 1024 || rank < 0 || rank >= world || epoch == 0)
+    return set_error(H3SA_ERR_INVALID, "peer_barrier: invalid arguments");
+  peer_barrier_kernel<<<1, ((world + 31) / 32) * 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      peer_flags, world, rank, epoch, device_error);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("peer_barrier_kernel launch", e);
   return H3SA_OK;
 }
 

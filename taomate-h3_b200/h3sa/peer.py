@@ -84,6 +84,30 @@ class PeerBuffer:
             self._local = 0
 
 
+class PeerBarrier:
+    """Barrier of the group's ranks over peer memory (``h3sa_peer_barrier``), ordered on the
+    stream like a kernel: a few microseconds over NVLink instead of a NCCL all-reduce.
+    Collective to construct; every rank then calls it the same number of times."""
+
+    def __init__(self, group=None, device_error: torch.Tensor | None = None) -> None:
+        import torch.distributed as dist
+
+        self.flags = PeerBuffer((2 * dist.get_world_size(group),), group)  # uint32 per rank
+        self.flags.tensor.zero_()
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
+        self.epoch = 0
+        self.err = device_error
+
+    def __call__(self, stream: torch.cuda.Stream | None = None) -> None:
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
+        call("h3sa_peer_barrier", ptr(self.flags.peer_table), self.flags.world, self.flags.rank,
+             ctypes.c_uint32(self.epoch), ptr(self.err), stream_handle(stream))
+
+    def close(self) -> None:
+        self.flags.close()
+
+
 def barrier(group=None, flag: torch.Tensor | None = None) -> None:
     """Stream-ordered barrier: a one-element all-reduce. Kernels enqueued after it on any rank
     start after every rank's kernels enqueued before it have finished."""
@@ -151,4 +175,4 @@ def attention_fwd_scatter(
          out.rank * heads, ptr(device_error), stream_handle(stream))
 
 
-__all__ = ["PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv"]
+__all__ = ["PeerBarrier", "PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv"]

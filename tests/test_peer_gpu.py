@@ -41,7 +41,7 @@ def _worker(rank: int, world: int, port: int) -> None:
     try:
         import h3sa
         from h3sa.kernels import PAGE_ROWS
-        from h3sa.peer import PeerBuffer, attention_fwd_scatter, barrier, scatter_qkv
+        from h3sa.peer import PeerBarrier, PeerBuffer, attention_fwd_scatter, barrier, scatter_qkv
         from h3sa.ulysses import pack_qkv_send, unpack_o_recv, unpack_qkv_recv
 
         heads, d, tokens, hist = 4, 128, 300, 256
@@ -83,19 +83,22 @@ def _worker(rank: int, world: int, port: int) -> None:
         qkv_peer = PeerBuffer((3, rows, hl, d))
         out_peer = PeerBuffer((tokens, heads, d))
         err = torch.zeros(1, dtype=torch.int32, device=dev)
-        for _ in range(2):
+        peer_barrier = PeerBarrier(device_error=err)
+        for it in range(3):
+            # the NCCL barrier and the peer-memory barrier order the same way
+            sync = barrier if it == 0 else peer_barrier
             qkv_peer.tensor.zero_()
             out_peer.tensor.zero_()
-            barrier()
+            sync()
             scatter_qkv(merged, qkv_peer, num_heads=heads, head_dim=d)
-            barrier()
+            sync()
             assert torch.equal(qkv_peer.tensor, qkv_ref), "q/k/v planes differ"
             kp2, vp2 = pools()
             h3sa.kv_copy_rows([qkv_peer.tensor[1], qkv_peer.tensor[2]], [kp2, vp2], count=rows,
                               dst_table=table, dst_start=hist)
             attention_fwd_scatter(qkv_peer.tensor[0], kp2, vp2, table, probs, scale, out_peer,
                                   device_error=err)
-            barrier()
+            sync()
             torch.cuda.synchronize()
             assert int(err.item()) == 0
             assert torch.equal(out_peer.tensor, final_ref), "final sequence shards differ"
@@ -103,6 +106,7 @@ def _worker(rank: int, world: int, port: int) -> None:
         torch.cuda.synchronize()
         qkv_peer.close()
         out_peer.close()
+        peer_barrier.close()
     finally:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
