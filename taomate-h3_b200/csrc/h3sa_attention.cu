@@ -23,6 +23,18 @@ constexpr int kExpPolyPer16 = H3SA_EXP_POLY_PER16;
 static_assert(kExpPolyPer16 % 2 == 0 && kExpPolyPer16 <= 16, "poly exponentials come in pairs");
 
 
+// e4m3 P = 2^(x - m_used + boost) stays at most 2^(threshold + boost), which must not pass the
+// e4m3 maximum 448 (< 2^9); the boost lifts small P values out of the subnormal range. At the
+// 1080p shape with x8 outliers, threshold/boost 2/6, 4/4 and 8/0 measured 1.68 / 1.64 / 1.60 ms
+// and 0.96 / 1.29 / 1.74 % relative L2 against attention on the dequantised inputs.
+#ifndef H3SA_FP8_RESCALE_THRESHOLD
+#define H3SA_FP8_RESCALE_THRESHOLD 4.0f
+#endif
+#ifndef H3SA_FP8_BOOST
+#define H3SA_FP8_BOOST 4.0f
+#endif
+static_assert(H3SA_FP8_RESCALE_THRESHOLD + H3SA_FP8_BOOST <= 8.5f, "e4m3 P would saturate");
+
 // Ping-pong between the two softmax warpgroups of a dense two-tile CTA: the exponential
 // phase of tile 1 for block i runs after that of tile 0 for block i, and tile 0's for block
 // i + 1 after tile 1's for block i, so the two never share the MUFU and issue slots.
@@ -272,6 +284,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       int cnt = 0;       // QK MMAs issued (softmax rounds requested)
       int started = 0;   // PV issued at least once
       bool pend = false; // PV for the previous block still to be issued
+      int pb = 0;        // block index of the previous block
       bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err));
       tc_fence_after();
       for (int i = 0; ok && i <= nblk; ++i) {
@@ -286,7 +299,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           block_at(i, b, m);
           w = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err);
         }
-        if (w && pend) w = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
+        // Every warp waits for the previous block's V before releasing its stage, used or not:
+        // the release barriers count one arrival per warp and phase, and a warp running ahead
+        // (its tile skips blocks) must not arrive twice on one phase, which would free a stage
+        // the other warp still reads.
+        if (w && i > 0) w = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
         if (w && pend) w = mbar_wait(smem_u32(&sm.p_full[mt]), (cnt - 1) & 1, abort_flag, p.err);
         if (!(ok = __all_sync(0xffffffffu, w))) break;
         if (mt == 0) H3SA_TRACE_AT(i, 10);
@@ -294,6 +311,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // PV for the previous block, then QK for this one: same TMEM columns, and the tensor
         // pipe runs one warp's MMAs in issue order.
         if (pend) {
+          // A partial block's P is zero outside its valid rows, but the tensor core still
+          // multiplies those zeros with whatever the V rows hold there (rows of the page the
+          // problem does not own, possibly never written: a NaN code would poison O). Zero
+          // those V rows in shared memory first; both MMA warps may do it, writing the same
+          // zeros, and the TMA for this stage has completed (v_full).
+          {
+            const int col0 = pb * kBlockN;
+            const int vlo_row = max(pr.kv_lo - col0, 0);
+            const int vhi_row = min(pr.kv_hi - col0, kBlockN);
+            if (vlo_row > 0 || vhi_row < kBlockN) {
+              uint8_t* vbase = &sm.v[ps][0];
+              const int nbad = vlo_row + (kBlockN - vhi_row);
+              for (int idx = lane; idx < nbad * Cfg::kAtoms * 8; idx += 32) {
+                const int chunk = idx & 7;
+                const int rest = idx >> 3;
+                const int a = rest % Cfg::kAtoms;
+                const int k = rest / Cfg::kAtoms;
+                const int r = k < vlo_row ? k : vhi_row + (k - vlo_row);
+                reinterpret_cast<uint4*>(vbase + a * Cfg::kAtomBytes + r * 128)[chunk] =
+                    make_uint4(0u, 0u, 0u, 0u);
+              }
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              __syncwarp();
+            }
+          }
           const uint32_t vlo = vlo0 + static_cast<uint32_t>(ps) * kTileDesc;
 #pragma unroll
           for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
@@ -327,6 +369,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (i > 0) tc_commit(smem_u32(&sm.v_empty[ps]));
         if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
         pend = mine;
+        pb = b;
         if (mt == 0) H3SA_TRACE_AT(i, 13);
       }
       if (ok) tc_commit(smem_u32(&sm.o_done[mt]));
@@ -357,8 +400,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         scale_log2 = p.scale_log2;
       // Lazy rescaling: O and l are rescaled only when a row maximum grows by more than
       // kRescaleThreshold (log2 units); P is then bounded by 2^(threshold + boost).
-      constexpr float kRescaleThreshold = kFp8 ? 2.0f : 8.0f;
-      constexpr float kBoost = kFp8 ? 6.0f : 0.0f;  // e4m3 P: keep the bulk above 2^-6
+      constexpr float kRescaleThreshold = kFp8 ? H3SA_FP8_RESCALE_THRESHOLD : 8.0f;
+      constexpr float kBoost = kFp8 ? H3SA_FP8_BOOST : 0.0f;  // e4m3 P: bulk above 2^-6
       const bool pingpong = H3SA_PINGPONG && !pr.sparse && n_tiles == 2;
       float m_used = -INFINITY;
       float l_sum = 0.f;

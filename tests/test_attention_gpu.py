@@ -358,3 +358,55 @@ def test_block_sparse_bad_list_reports_error() -> None:
                        device_error=err)
     torch.cuda.synchronize()
     assert int(err.item()) & 4
+
+
+def test_pool_rows_outside_the_kv_range_do_not_leak() -> None:
+    """Rows of the first/last page outside [kv_lo, kv_hi) may hold anything (here NaN, as an
+    unwritten pool can): the output must not see them, bf16 and e4m3."""
+
+    h3sa = _h3sa()
+    heads, nq, kv_lo, nk = 2, 300, 50, 1000
+    gen = torch.Generator(device="cuda").manual_seed(41)
+    kv_rows = kv_lo + nk
+    q = torch.randn(nq, heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    k = torch.randn(kv_rows, heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    v = torch.randn(kv_rows, heads, 128, device="cuda", generator=gen).to(torch.bfloat16)
+    pages = (kv_rows + 127) // 128
+    table = torch.arange(pages, dtype=torch.int32, device="cuda")
+    kp = torch.full((heads, pages * 128, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
+    vp = torch.full_like(kp, float("nan"))
+    # only the rows of the range are written; the pages' rows before kv_lo and after kv_hi stay NaN
+    h3sa.kv_copy_rows([k[kv_lo:], v[kv_lo:]], [kp, vp], count=nk, dst_table=table, dst_start=kv_lo)
+    out = torch.empty_like(q)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    h3sa.attention_fwd(q, out, kp, vp, table, [h3sa.AttentionProblem(0, nq, kv_lo, kv_rows)],
+                       scale, device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.isfinite(out.float()).all()
+    assert rel_l2(out, ref_attention(q, k[kv_lo:], v[kv_lo:], scale)) <= BF16_TOL
+
+    # e4m3 pools: 0x7F is a NaN code; quantise only the logical rows [0, nk)
+    q8, qs = h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0))
+    kp2 = torch.zeros(heads, pages * 128, 128, dtype=torch.bfloat16, device="cuda")
+    vp2 = torch.zeros_like(kp2)
+    h3sa.kv_copy_rows([k[:nk], v[:nk]], [kp2, vp2], count=nk, dst_table=table)
+    k8 = torch.full((heads, pages * 128, 128), 0x7F, dtype=torch.uint8, device="cuda").view(torch.float8_e4m3fn)
+    v8 = torch.full_like(k8.view(torch.uint8), 0x7F).view(torch.float8_e4m3fn)
+    ks = torch.empty(heads, dtype=torch.float32, device="cuda")
+    vs = torch.empty(heads, dtype=torch.float32, device="cuda")
+    h3sa.quantize_fp8_pool(kp2, k8, ks, table, nk)
+    h3sa.quantize_fp8_pool(vp2, v8, vs, table, nk)
+    out8 = torch.empty_like(q)
+    h3sa.attention_fwd(q8.squeeze(0), out8, k8, v8, table, [h3sa.AttentionProblem(0, nq, 0, nk)],
+                       scale, q_scale=qs.reshape(-1).contiguous(), k_scale=ks, v_scale=vs,
+                       device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.isfinite(out8.float()).all()
+    k8p, kss = h3sa.quantize_fp8_e4m3_per_head(k[:nk].unsqueeze(0))
+    v8p, vss = h3sa.quantize_fp8_e4m3_per_head(v[:nk].unsqueeze(0))
+    deq = lambda x8, sc: x8.squeeze(0).float() * sc.reshape(1, -1, 1)  # noqa: E731
+    ref8 = ref_attention(deq(q8, qs), deq(k8p, kss), deq(v8p, vss), scale)
+    assert rel_l2(out8, ref8) <= FP8_TOL
