@@ -414,6 +414,7 @@ def _variants(peaks: dict, iters: int = 10) -> dict:
     * Block-sparse: the 768p per-GPU problem at SP=8 (3 heads; 12509 queries over 16384 + 12509
       keys) with the composite 128x128 block mask (audio blocks, 2 sinks, +-4-block band, top-k
       fill to 25% of blocks).
+    * Dense bf16 at 480p on one GPU (24 heads; 4985 queries over 19940 + 4985 keys).
     FLOPs count only the work the kernel must do (kept blocks for the sparse case).
     """
 
@@ -495,6 +496,23 @@ def _variants(peaks: dict, iters: int = 10) -> dict:
     out["sparse_768p_sp8_per_gpu"] = {
         "ms": ms, "tflops_on_kept_blocks": tf, "kept_block_fraction": density, "heads": heads,
         "queries": nq, "keys": nk,
+        "roofline": {"bound": "tensor", "peak": peaks["bf16"], "frac": tf / peaks["bf16"]}}
+    del q, k, v, kp, vp, o
+
+    # ---- dense bf16, 480p chunk on one GPU (24 heads; 4860 video + 125 audio queries over
+    # 4 prior chunks = 19940 cached rows plus the chunk)
+    heads, nq, nh = 24, 4860 + 125, 19940
+    nk = nh + nq
+    q = torch.randn(nq, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(nk, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(nk, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    kp, vp, table = pools(nk, heads, k, v)
+    o = torch.empty(nq, heads, d, dtype=torch.bfloat16, device=dev)
+    probs = [h3sa.AttentionProblem(0, nq, 0, nk)]
+    ms = _time_launch(lambda: h3sa.attention_fwd(q, o, kp, vp, table, probs, d ** -0.5), iters)
+    tf = 4.0 * nq * nk * d * heads / (ms * 1e-3) / 1e12
+    out["dense_480p_1gpu"] = {
+        "ms": ms, "tflops": tf, "heads": heads, "queries": nq, "keys": nk,
         "roofline": {"bound": "tensor", "peak": peaks["bf16"], "frac": tf / peaks["bf16"]}}
     return out
 

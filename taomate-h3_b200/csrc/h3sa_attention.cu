@@ -544,42 +544,64 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const bool any = c > 0;
         float out_scale = any ? 1.0f / l_sum : 0.f;
         if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        // destination of this thread's row; 0 for rows past the problem's query range
         const int qrow = q_row0 + t * kBlockM + row;
-        const bool valid = qrow < pr.q_hi;
-        __nv_bfloat16* dst;
-        if (p.out_peers) {
-          // heads -> sequence exchange fused into the store: row qrow belongs to the sequence
-          // shard of rank qrow / rows_per_rank, which holds all heads of its rows
-          const int owner = min(qrow / p.out_rows_per_rank, p.out_ranks - 1);
-          const int orow = qrow - owner * p.out_rows_per_rank;
-          dst = reinterpret_cast<__nv_bfloat16*>(static_cast<uintptr_t>(p.out_peers[owner])) +
-                (static_cast<size_t>(orow) * p.out_heads + p.out_head0 + head) * kHeadDim;
-        } else {
-          dst = reinterpret_cast<__nv_bfloat16*>(p.out) +
-                (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim;
-        }
-#pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
-          uint32_t r[32];
-          if (any) {
-            tmem_ld32(tO + ch * 32, r);
-            tmem_wait_ld();
-            reg_fence32(r);
+        unsigned long long dst = 0;
+        if (qrow < pr.q_hi) {
+          if (p.out_peers) {
+            // heads -> sequence exchange fused into the store: row qrow belongs to the
+            // sequence shard of rank qrow / rows_per_rank, which holds all heads of its rows
+            const int owner = min(qrow / p.out_rows_per_rank, p.out_ranks - 1);
+            const int orow = qrow - owner * p.out_rows_per_rank;
+            dst = p.out_peers[owner] +
+                  (static_cast<size_t>(orow) * p.out_heads + p.out_head0 + head) * kHeadDim * 2;
           } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) r[j] = 0u;
+            dst = reinterpret_cast<uintptr_t>(p.out) +
+                  (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim * 2;
           }
-          uint32_t o[16];
+        }
+        // The rows leave through shared memory. Every MMA that read this tile's Q buffer has
+        // completed (o_done), so each warp stages its 32 rows there, half a row (64 columns,
+        // 128 bytes) at a time, chunks XOR-swizzled by row, and stores them back with 8 lanes
+        // per row: one warp store instruction writes four whole 128-byte lines instead of 32
+        // scattered 16-byte pieces, which matters most for rows bound for a peer over NVLink.
+        uint8_t* stage = sm.q[t] + (warp & 3) * (32 * 128);
 #pragma unroll
-          for (int j = 0; j < 16; ++j)
-            o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * out_scale,
-                               __uint_as_float(r[2 * j + 1]) * out_scale);
-          if (valid) {
-            uint4* d4 = reinterpret_cast<uint4*>(dst + ch * 32);
+        for (int half = 0; half < 2; ++half) {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              d4[j] = make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+          for (int hc = 0; hc < 2; ++hc) {
+            uint32_t r[32];
+            if (any) {
+              tmem_ld32(tO + (half * 2 + hc) * 32, r);
+              tmem_wait_ld();
+              reg_fence32(r);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) r[j] = 0u;
+            }
+            uint32_t o[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+              o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * out_scale,
+                                 __uint_as_float(r[2 * j + 1]) * out_scale);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int chunk = hc * 4 + j;
+              *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+                  make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+            }
           }
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int r = it * 4 + (lane >> 3);
+            const int chunk = lane & 7;
+            const uint4 v =
+                *reinterpret_cast<const uint4*>(stage + r * 128 + ((chunk ^ (r & 7)) << 4));
+            const unsigned long long d = __shfl_sync(0xffffffffu, dst, r);
+            if (d) reinterpret_cast<uint4*>(static_cast<uintptr_t>(d) + half * 128)[chunk] = v;
+          }
+          __syncwarp();
         }
         // peer stores: make them visible system-wide before the kernel is seen as done
         if (p.out_peers) __threadfence_system();
