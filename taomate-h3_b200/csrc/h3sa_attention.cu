@@ -14,15 +14,6 @@
 
 namespace h3sa {
 
-// Exponentials per 16 scores evaluated by the FMA-pipe polynomial instead of the MUFU
-// (0 measured fastest on B200 for d = 128: the MUFU keeps up, the polynomial costs issue).
-#ifndef H3SA_EXP_POLY_PER16
-#define H3SA_EXP_POLY_PER16 0
-#endif
-constexpr int kExpPolyPer16 = H3SA_EXP_POLY_PER16;
-static_assert(kExpPolyPer16 % 2 == 0 && kExpPolyPer16 <= 16, "poly exponentials come in pairs");
-
-
 // e4m3 P = 2^(x - m_used + boost) stays at most 2^(threshold + boost), which must not pass the
 // e4m3 maximum 448 (< 2^9); the boost lifts small P values out of the subnormal range. At the
 // 1080p shape with x8 outliers, threshold/boost 2/6, 4/4 and 8/0 measured 1.68 / 1.64 / 1.60 ms
@@ -35,11 +26,21 @@ static_assert(kExpPolyPer16 % 2 == 0 && kExpPolyPer16 <= 16, "poly exponentials 
 #endif
 static_assert(H3SA_FP8_RESCALE_THRESHOLD + H3SA_FP8_BOOST <= 8.5f, "e4m3 P would saturate");
 
-// Ping-pong between the two softmax warpgroups of a dense two-tile CTA: the exponential
-// phase of tile 1 for block i runs after that of tile 0 for block i, and tile 0's for block
-// i + 1 after tile 1's for block i, so the two never share the MUFU and issue slots.
+// K and V ring depths. P of each query tile sits in shared memory, which leaves room for two
+// K stages and one V stage of bf16 tiles within the 227 KB a CTA can have; e4m3 tiles are half
+// the size and keep two V stages.
+#ifndef H3SA_K_STAGES
+#define H3SA_K_STAGES 2
+#endif
+#ifndef H3SA_V_STAGES_BF16
+#define H3SA_V_STAGES_BF16 1
+#endif
+
+// Ping-pong of the exponential phases of the two query tiles of a CTA: the softmax warps of
+// tile 0 and tile 1 that share an SM sub-partition take turns on its MUFU, so one computes
+// exponentials while the other reads scores, takes row maxima and stores P.
 #ifndef H3SA_PINGPONG
-#define H3SA_PINGPONG 0
+#define H3SA_PINGPONG 1
 #endif
 
 // Optional per-block timeline of two CTAs (first and middle of the grid), compiled only with
@@ -64,46 +65,53 @@ struct AttnCfg {
   static constexpr int kTileBytes = kBlockM * kHeadDim * kElem;  // 32 KB bf16, 16 KB e4m3
   static constexpr int kAtoms = kHeadDim * kElem / 128;          // 128-byte swizzle atoms per row
   static constexpr int kAtomBytes = kBlockM * 128;               // 16 KB
-  static constexpr int kKSteps = kFp8 ? 4 : 8;                   // MMA K steps over d (QK^T)
-  static constexpr int kKStepBytes = 32;                         // bytes of K per MMA step
-  static constexpr int kPvRowsPerStep = kFp8 ? 32 : 16;          // kv rows per PV MMA step
-  static constexpr int kPCols = kBlockN * kElem / 4;             // TMEM columns of packed P
+  static constexpr int kKSteps = kFp8 ? 4 : 8;  // MMA K steps over d (QK^T) and over kv (PV)
+  static constexpr int kKStepBytes = 32;        // bytes of an operand row per MMA K step
+  static constexpr int kPvRowsPerStep = kFp8 ? 32 : 16;  // kv rows per PV MMA step
+  static constexpr int kKStages = H3SA_K_STAGES;
+  static constexpr int kVStages = kFp8 ? 2 : H3SA_V_STAGES_BF16;
   static constexpr uint32_t kIdescQK = kFp8 ? idesc_e4m3(kBlockM, kBlockN, false)
                                             : idesc_bf16(kBlockM, kBlockN, false);
+  // PV: A = P (K-major, shared memory), B = V (rows of kv, so N = d is the contiguous dim)
   static constexpr uint32_t kIdescPV = kFp8 ? idesc_e4m3(kBlockM, kHeadDim, true)
                                             : idesc_bf16(kBlockM, kHeadDim, true);
+  static_assert(kBlockN / kPvRowsPerStep == kKSteps, "P is laid out like Q");
 };
+
+constexpr int kMaskWords = kMaxUnionBlocks / 32;
 
 template <bool kFp8>
 struct alignas(1024) AttnSmem {
-  uint8_t q[2][AttnCfg<kFp8>::kTileBytes];
-  uint8_t k[kKVStages][AttnCfg<kFp8>::kTileBytes];
-  uint8_t v[kKVStages][AttnCfg<kFp8>::kTileBytes];
+  using Cfg = AttnCfg<kFp8>;
+  uint8_t q[2][Cfg::kTileBytes];
+  uint8_t p[2][Cfg::kTileBytes];  // P of each query tile: the layout of a Q tile (K-major, SW128)
+  uint8_t k[Cfg::kKStages][Cfg::kTileBytes];
+  uint8_t v[Cfg::kVStages][Cfg::kTileBytes];
   uint64_t q_full;
-  uint64_t k_full[kKVStages], k_empty[kKVStages];
-  uint64_t v_full[kKVStages], v_empty[kKVStages];
-  uint64_t s_full[2], p_full[2], o_done[2];
-  uint64_t exp_done[2];  // ping-pong tokens: one phase per exponential round of each tile
+  uint64_t k_full[Cfg::kKStages], k_empty[Cfg::kKStages];
+  uint64_t v_full[Cfg::kVStages], v_empty[Cfg::kVStages];
+  uint64_t s_full[2], s_free[2], p_full[2], pv_done[2], o_done[2];
+  uint64_t exp_tok[2][4];  // [tile][sub-partition]: that warp finished a round's exponentials
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
   int n_blocks;
-  int16_t blk[kMaxUnionBlocks];
-  uint8_t blk_mask[kMaxUnionBlocks];
-  uint8_t present[kMaxUnionBlocks];
+  uint32_t kv_mask[2][kMaskWords];  // block-sparse: bit i = tile t attends to block b_lo + i
 };
 
 template <bool kFp8>
 constexpr size_t attn_smem_bytes() {
   return sizeof(AttnSmem<kFp8>) + 1024;  // + slack for 1024-byte alignment of the base
 }
+static_assert(attn_smem_bytes<false>() <= 232448, "bf16 attention needs more than 227 KB");
+static_assert(attn_smem_bytes<true>() <= 232448, "e4m3 attention needs more than 227 KB");
 
-// Union of the two per-q-block KV block lists of a CTA, with a per-block tile mask
-// (bit 0: tile 0 attends to the block, bit 1: tile 1). Blocks are marked in a presence
-// map over [b_lo, b_hi) and compacted in ascending order by one warp.
-__device__ void build_union(const int* A, int na, const int* B, int nb, int b_lo, int b_hi,
-                            uint8_t* present, int16_t* blk, uint8_t* blk_mask, int* n_out,
-                            int* err, volatile int* abort_flag) {
+// The block-sparse lists of a CTA's two query tiles as bitmaps over [b_lo, b_hi), built by one
+// warp; n_out = number of blocks in their union. Indices outside the range set kErrBadIndex
+// and abort the CTA.
+__device__ void build_masks(const int* A, int na, const int* B, int nb, int b_lo, int b_hi,
+                            uint32_t (*mask)[kMaskWords], int* n_out, int* err,
+                            volatile int* abort_flag) {
   const int lane = threadIdx.x & 31;
   const int range = b_hi - b_lo;
   if (range > kMaxUnionBlocks) {
@@ -114,41 +122,55 @@ __device__ void build_union(const int* A, int na, const int* B, int nb, int b_lo
     }
     return;
   }
-  for (int i = lane; i < range; i += 32) present[i] = 0;
+  for (int i = lane; i < 2 * kMaskWords; i += 32) mask[i / kMaskWords][i % kMaskWords] = 0u;
   __syncwarp();
   for (int i = lane; i < na; i += 32) {
     const int v = __ldg(A + i) - b_lo;
-    if (v >= 0 && v < range) present[v] = 1;
+    if (v >= 0 && v < range) atomicOr(&mask[0][v >> 5], 1u << (v & 31));
     else { if (err) atomicOr(err, kErrBadIndex); *abort_flag = 1; }
   }
-  __syncwarp();
   for (int i = lane; i < nb; i += 32) {
     const int v = __ldg(B + i) - b_lo;
-    if (v >= 0 && v < range) present[v] |= 2;
+    if (v >= 0 && v < range) atomicOr(&mask[1][v >> 5], 1u << (v & 31));
     else { if (err) atomicOr(err, kErrBadIndex); *abort_flag = 1; }
   }
   __syncwarp();
-  const int chunk = (range + 31) / 32;
-  const int beg = min(lane * chunk, range);
-  const int end = min(beg + chunk, range);
   int cnt = 0;
-  for (int i = beg; i < end; ++i) cnt += present[i] ? 1 : 0;
-  int incl = cnt;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int y = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += y;
-  }
-  int pos = incl - cnt;
-  for (int i = beg; i < end; ++i) {
-    if (present[i]) {
-      blk[pos] = static_cast<int16_t>(i + b_lo);
-      blk_mask[pos] = present[i];
-      ++pos;
-    }
-  }
-  if (lane == 31) *n_out = incl;
+  for (int w = lane; w < kMaskWords; w += 32) cnt += __popc(mask[0][w] | mask[1][w]);
+  cnt = __reduce_add_sync(0xffffffffu, cnt);
+  if (lane == 0) *n_out = cnt;
   __syncwarp();
+}
+
+// A CTA's KV blocks in ascending order; every role walks the same sequence with its own
+// cursor. Dense problems take every block of [b_lo, b_hi); block-sparse ones the union of the
+// two bitmaps. Bit t of m is set when query tile t attends to the block.
+struct BlockWalk {
+  int next = 0;      // dense: next block offset; block-sparse: next bitmap word
+  uint32_t rem = 0;  // block-sparse: blocks of word next - 1 not yet visited
+};
+
+__device__ __forceinline__ void walk_next(BlockWalk& s, bool sparse, int b_lo, int dense_mask,
+                                          const uint32_t (*mask)[kMaskWords], int& b, int& m) {
+  if (!sparse) {
+    b = b_lo + s.next++;
+    m = dense_mask;
+    return;
+  }
+  while (s.rem == 0u && s.next < kMaskWords) {
+    s.rem = mask[0][s.next] | mask[1][s.next];
+    ++s.next;
+  }
+  if (s.rem == 0u) {  // walked past the union (callers stop at n_blocks): attend nothing
+    b = b_lo;
+    m = 0;
+    return;
+  }
+  const int w = s.next - 1;
+  const int bit = __ffs(s.rem) - 1;
+  s.rem &= s.rem - 1u;
+  b = b_lo + w * 32 + bit;
+  m = static_cast<int>(((mask[0][w] >> bit) & 1u) | (((mask[1][w] >> bit) & 1u) << 1));
 }
 
 template <bool kFp8>
@@ -156,6 +178,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
   using Cfg = AttnCfg<kFp8>;
+  constexpr int kKS = Cfg::kKStages;
+  constexpr int kVS = Cfg::kVStages;
   extern __shared__ uint8_t smem_raw[];
   AttnSmem<kFp8>& sm = *reinterpret_cast<AttnSmem<kFp8>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -177,17 +201,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(smem_u32(&sm.q_full), 1);
-    for (int s = 0; s < kKVStages; ++s) {
+    for (int s = 0; s < kKS; ++s) {
       mbar_init(smem_u32(&sm.k_full[s]), 1);
       mbar_init(smem_u32(&sm.k_empty[s]), n_tiles);  // one release per MMA warp
+    }
+    for (int s = 0; s < kVS; ++s) {
       mbar_init(smem_u32(&sm.v_full[s]), 1);
       mbar_init(smem_u32(&sm.v_empty[s]), n_tiles);
     }
     for (int t = 0; t < 2; ++t) {
       mbar_init(smem_u32(&sm.s_full[t]), 1);
-      mbar_init(smem_u32(&sm.p_full[t]), 128);
+      mbar_init(smem_u32(&sm.s_free[t]), 4);    // one per softmax warp of the tile
+      mbar_init(smem_u32(&sm.p_full[t]), 128);  // every softmax thread
+      mbar_init(smem_u32(&sm.pv_done[t]), 1);
       mbar_init(smem_u32(&sm.o_done[t]), 1);
-      mbar_init(smem_u32(&sm.exp_done[t]), 128);
+      for (int q = 0; q < 4; ++q) mbar_init(smem_u32(&sm.exp_tok[t][q]), 1);
     }
     mbar_init(smem_u32(&sm.drain), n_tiles);
     sm.abort_flag = 0;
@@ -205,8 +233,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int* A = p.kv_indices + (static_cast<size_t>(head) * p.q_blocks + qb) * p.kv_stride;
     const int na = min(__ldg(nums + qb), p.kv_stride);
     const int nb = (n_tiles > 1) ? min(__ldg(nums + qb + 1), p.kv_stride) : 0;
-    build_union(A, na, A + p.kv_stride, nb, b_lo, b_hi, sm.present, sm.blk, sm.blk_mask,
-                &sm.n_blocks, p.err, abort_flag);
+    build_masks(A, na, A + p.kv_stride, nb, b_lo, b_hi, sm.kv_mask, &sm.n_blocks, p.err,
+                abort_flag);
   }
   tc_fence_before();
   __syncthreads();
@@ -215,18 +243,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tbase = sm.tmem_base;
   const int nblk = sm.n_blocks;
   const int dense_mask = (n_tiles > 1) ? 3 : 1;
-  auto block_at = [&](int i, int& b, int& m) {
-    if (pr.sparse) { b = sm.blk[i]; m = sm.blk_mask[i]; }
-    else { b = b_lo + i; m = dense_mask; }
+  BlockWalk walk;
+  auto next_block = [&](int& b, int& m) {
+    walk_next(walk, pr.sparse != 0, b_lo, dense_mask, sm.kv_mask, b, m);
   };
 
   // Register split (every warp of a warpgroup executes the same setmaxnreg at the top of its
   // role): the producer/MMA warpgroup gives registers to the two softmax warpgroups.
   if (warp == 0 || warp == 3) {
     // ================================================================ TMA producers
-    // Warp 0 loads Q and streams K blocks, warp 3 streams V blocks: K for block i + 2 is
-    // released by the QK MMAs of block i, V by the later PV MMAs, so each stream runs ahead
-    // on its own stage barriers.
+    // Warp 0 loads Q and streams K blocks, warp 3 streams V blocks: K for block i is released
+    // by the QK MMAs of block i, V by the PV MMAs, so each stream runs ahead on its own ring.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     const bool is_k = (warp == 0);
     if (lane == 0 && !*abort_flag) {
@@ -241,25 +268,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             tma_load_3d(smem_u32(sm.q[t]) + a * Cfg::kAtomBytes, &tmQ, qbar,
                         a * (128 / Cfg::kElem), head, q_row0 + t * kBlockM);
       }
-      uint64_t* full = is_k ? sm.k_full : sm.v_full;
-      uint64_t* empty = is_k ? sm.k_empty : sm.v_empty;
-      uint8_t* buf = is_k ? &sm.k[0][0] : &sm.v[0][0];
       for (int i = 0; i < nblk; ++i) {
-        const int s = i % kKVStages;
-        const uint32_t ph = (i / kKVStages) & 1;
+        const int s = is_k ? i % kKS : i % kVS;
+        const uint32_t ph = (is_k ? i / kKS : i / kVS) & 1;
         int b, m;
-        block_at(i, b, m);
+        next_block(b, m);
         int page = (b >= 0 && b < p.table_blocks) ? __ldg(p.page_table + b) : -1;
         if (page < 0 || page >= p.pool_pages) {
           if (p.err) atomicOr(p.err, kErrBadPage);
           *abort_flag = 1;
           break;
         }
-        if (!mbar_wait(smem_u32(&empty[s]), ph ^ 1, abort_flag, p.err)) break;
+        uint64_t* empty = is_k ? &sm.k_empty[s] : &sm.v_empty[s];
+        if (!mbar_wait(smem_u32(empty), ph ^ 1, abort_flag, p.err)) break;
         H3SA_TRACE_AT(i, is_k ? 14 : 15);
-        const uint32_t fb = smem_u32(&full[s]);
+        const uint32_t fb = smem_u32(is_k ? &sm.k_full[s] : &sm.v_full[s]);
         mbar_expect_tx(fb, Cfg::kTileBytes);
-        const uint32_t dst = smem_u32(buf) + s * Cfg::kTileBytes;
+        const uint32_t dst = smem_u32(is_k ? sm.k[s] : sm.v[s]);
         for (int a = 0; a < Cfg::kAtoms; ++a)
           tma_load_3d(dst + a * Cfg::kAtomBytes, map, fb, a * (128 / Cfg::kElem), page * kBlockN,
                       head);
@@ -272,85 +297,44 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // the pipe fed while the other waits on its softmax or on a barrier. Each warp runs its
     // loop converged (all values warp-uniform); one elected lane issues every tcgen05
     // instruction. Shared-memory descriptors advance by constant 32-bit steps.
+    //
+    // Per block i: QK(i) into S_t as soon as the softmax has read the previous scores out of
+    // TMEM (s_free), then PV(i - 1) once that softmax has written P to shared memory (p_full).
+    // S and P no longer share TMEM, so the next QK overlaps the current softmax.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     const int mt = warp - 1;  // the query tile this warp serves
     if (mt < n_tiles) {
       const uint32_t tS = tbase + static_cast<uint32_t>(mt) * 128u;
       const uint32_t tO = tbase + 256u + static_cast<uint32_t>(mt) * 128u;
       const uint32_t qlo = sdesc_lo(smem_u32(sm.q[mt]), 16);
+      const uint32_t plo = sdesc_lo(smem_u32(sm.p[mt]), 16);
       const uint32_t klo0 = sdesc_lo(smem_u32(sm.k[0]), 16);
       const uint32_t vlo0 = sdesc_lo(smem_u32(sm.v[0]), Cfg::kAtomBytes);
       constexpr uint32_t kTileDesc = Cfg::kTileBytes >> 4;  // descriptor step between stages
-      int cnt = 0;       // QK MMAs issued (softmax rounds requested)
-      int started = 0;   // PV issued at least once
-      bool pend = false; // PV for the previous block still to be issued
-      int pb = 0;        // block index of the previous block
+      int cnt = 0;        // QK MMAs issued (softmax rounds requested)
+      int npv = 0;        // PV rounds issued
+      bool pend = false;  // PV for the previous block still to be issued
+      int pb = 0;         // block index of the previous block
       bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err));
       tc_fence_after();
       for (int i = 0; ok && i <= nblk; ++i) {
         const bool last = (i == nblk);
-        const int s = i % kKVStages;
-        const uint32_t ph = (i / kKVStages) & 1;
-        const int ps = (i + kKVStages - 1) % kKVStages;
-        const uint32_t pph = ((i - 1) / kKVStages) & 1;
+        const int sk = i % kKS;
         int b = 0, m = 0;
         bool w = true;
         if (!last) {
-          block_at(i, b, m);
-          w = mbar_wait(smem_u32(&sm.k_full[s]), ph, abort_flag, p.err);
-        }
-        // Every warp waits for the previous block's V before releasing its stage, used or not:
-        // the release barriers count one arrival per warp and phase, and a warp running ahead
-        // (its tile skips blocks) must not arrive twice on one phase, which would free a stage
-        // the other warp still reads.
-        if (w && i > 0) w = mbar_wait(smem_u32(&sm.v_full[ps]), pph, abort_flag, p.err);
-        if (w && pend) w = mbar_wait(smem_u32(&sm.p_full[mt]), (cnt - 1) & 1, abort_flag, p.err);
-        if (!(ok = __all_sync(0xffffffffu, w))) break;
-        if (mt == 0) H3SA_TRACE_AT(i, 10);
-        tc_fence_after();
-        // PV for the previous block, then QK for this one: same TMEM columns, and the tensor
-        // pipe runs one warp's MMAs in issue order.
-        if (pend) {
-          // A partial block's P is zero outside its valid rows, but the tensor core still
-          // multiplies those zeros with whatever the V rows hold there (rows of the page the
-          // problem does not own, possibly never written: a NaN code would poison O). Zero
-          // those V rows in shared memory first; both MMA warps may do it, writing the same
-          // zeros, and the TMA for this stage has completed (v_full).
-          {
-            const int col0 = pb * kBlockN;
-            const int vlo_row = max(pr.kv_lo - col0, 0);
-            const int vhi_row = min(pr.kv_hi - col0, kBlockN);
-            if (vlo_row > 0 || vhi_row < kBlockN) {
-              uint8_t* vbase = &sm.v[ps][0];
-              const int nbad = vlo_row + (kBlockN - vhi_row);
-              for (int idx = lane; idx < nbad * Cfg::kAtoms * 8; idx += 32) {
-                const int chunk = idx & 7;
-                const int rest = idx >> 3;
-                const int a = rest % Cfg::kAtoms;
-                const int k = rest / Cfg::kAtoms;
-                const int r = k < vlo_row ? k : vhi_row + (k - vlo_row);
-                reinterpret_cast<uint4*>(vbase + a * Cfg::kAtomBytes + r * 128)[chunk] =
-                    make_uint4(0u, 0u, 0u, 0u);
-              }
-              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-              __syncwarp();
-            }
-          }
-          const uint32_t vlo = vlo0 + static_cast<uint32_t>(ps) * kTileDesc;
-#pragma unroll
-          for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
-            const uint64_t bdesc = sdesc_join(vlo + ((kk * Cfg::kPvRowsPerStep * 128) >> 4));
-            const uint32_t a_tmem = tS + 64u + kk * 8u;
-            if constexpr (kFp8)
-              mma_ts_f8(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
-            else
-              mma_ts(tO, a_tmem, bdesc, Cfg::kIdescPV, (started | kk) ? 1u : 0u);
-          }
-          started = 1;
+          next_block(b, m);
+          w = mbar_wait(smem_u32(&sm.k_full[sk]), (i / kKS) & 1, abort_flag, p.err);
         }
         const bool mine = !last && ((m >> mt) & 1);
+        // S_t is overwritten only once the softmax has loaded the previous round's scores
+        if (w && mine && cnt > 0)
+          w = mbar_wait(smem_u32(&sm.s_free[mt]), (cnt - 1) & 1, abort_flag, p.err);
+        if (!(ok = __all_sync(0xffffffffu, w))) break;
+        H3SA_TRACE_AT(i, mt == 0 ? 10 : 16);
+        tc_fence_after();
         if (mine) {
-          const uint32_t klo = klo0 + static_cast<uint32_t>(s) * kTileDesc;
+          const uint32_t klo = klo0 + static_cast<uint32_t>(sk) * kTileDesc;
 #pragma unroll
           for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
             const uint32_t off = ((kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
@@ -365,9 +349,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tc_commit(smem_u32(&sm.s_full[mt]));
           ++cnt;
         }
-        // this warp's share of the stage releases (the barriers count one per MMA warp)
-        if (i > 0) tc_commit(smem_u32(&sm.v_empty[ps]));
-        if (!last) tc_commit(smem_u32(&sm.k_empty[s]));
+        // this warp's share of the K stage release (the barriers count one per MMA warp)
+        if (!last) tc_commit(smem_u32(&sm.k_empty[sk]));
+        if (i > 0) {
+          const int sv = (i - 1) % kVS;
+          // Every warp waits for the previous block's V before releasing its stage, used or
+          // not: the release barriers count one arrival per warp and phase, and a warp running
+          // ahead (its tile skips blocks) must not arrive twice on one phase.
+          w = mbar_wait(smem_u32(&sm.v_full[sv]), ((i - 1) / kVS) & 1, abort_flag, p.err);
+          if (w && pend) w = mbar_wait(smem_u32(&sm.p_full[mt]), npv & 1, abort_flag, p.err);
+          if (!(ok = __all_sync(0xffffffffu, w))) break;
+          H3SA_TRACE_AT(i, 11 + mt);
+          tc_fence_after();
+          if (pend) {
+            // A partial block's P is zero outside its valid rows, but the tensor core still
+            // multiplies those zeros with whatever the V rows hold there (rows of the page the
+            // problem does not own, possibly never written: a NaN code would poison O). Zero
+            // those V rows in shared memory first; both MMA warps may do it, writing the same
+            // zeros, and the TMA for this stage has completed (v_full).
+            const int col0 = pb * kBlockN;
+            const int vlo_row = max(pr.kv_lo - col0, 0);
+            const int vhi_row = min(pr.kv_hi - col0, kBlockN);
+            if (vlo_row > 0 || vhi_row < kBlockN) {
+              uint8_t* vbase = sm.v[sv];
+              const int nbad = vlo_row + (kBlockN - vhi_row);
+              for (int idx = lane; idx < nbad * Cfg::kAtoms * 8; idx += 32) {
+                const int chunk = idx & 7;
+                const int rest = idx >> 3;
+                const int a = rest % Cfg::kAtoms;
+                const int k = rest / Cfg::kAtoms;
+                const int r = k < vlo_row ? k : vhi_row + (k - vlo_row);
+                reinterpret_cast<uint4*>(vbase + a * Cfg::kAtomBytes + r * 128)[chunk] =
+                    make_uint4(0u, 0u, 0u, 0u);
+              }
+              asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+              __syncwarp();
+            }
+            const uint32_t vlo = vlo0 + static_cast<uint32_t>(sv) * kTileDesc;
+#pragma unroll
+            for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
+              const uint32_t off = ((kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
+                                    (kk * Cfg::kKStepBytes) % 128) >> 4;
+              const uint64_t bdesc =
+                  sdesc_join(vlo + ((kk * Cfg::kPvRowsPerStep * 128) >> 4));
+              const uint32_t acc = (npv > 0 || kk > 0) ? 1u : 0u;
+              if constexpr (kFp8)
+                mma_ss_f8(tO, sdesc_join(plo + off), bdesc, Cfg::kIdescPV, acc);
+              else
+                mma_ss(tO, sdesc_join(plo + off), bdesc, Cfg::kIdescPV, acc);
+            }
+            tc_commit(smem_u32(&sm.pv_done[mt]));
+            ++npv;
+          }
+          tc_commit(smem_u32(&sm.v_empty[sv]));
+        }
         pend = mine;
         pb = b;
         if (mt == 0) H3SA_TRACE_AT(i, 13);
@@ -391,8 +426,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const int row = (warp & 3) * 32 + lane;
       const uint32_t lane_off = static_cast<uint32_t>((warp & 3) * 32) << 16;
       const uint32_t tS = tbase + static_cast<uint32_t>(t) * 128u + lane_off;
-      const uint32_t tP = tS + 64u;
       const uint32_t tO = tbase + 256u + static_cast<uint32_t>(t) * 128u + lane_off;
+      uint8_t* const prow = sm.p[t] + row * 128;  // this row in each 16 KB atom of P
       float scale_log2;
       if constexpr (kFp8)
         scale_log2 = __ldg(p.q_scale + head) * __ldg(p.k_scale + head) * p.softmax_scale_log2;
@@ -402,16 +437,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // kRescaleThreshold (log2 units); P is then bounded by 2^(threshold + boost).
       constexpr float kRescaleThreshold = kFp8 ? H3SA_FP8_RESCALE_THRESHOLD : 8.0f;
       constexpr float kBoost = kFp8 ? H3SA_FP8_BOOST : 0.0f;  // e4m3 P: bulk above 2^-6
-      const bool pingpong = H3SA_PINGPONG && !pr.sparse && n_tiles == 2;
       float m_used = -INFINITY;
       float l_sum = 0.f;
       int c = 0;
       bool ok = true;
       const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+      // The exponentials of block i of tile 1 follow those of block i of tile 0, and those of
+      // block i + 1 of tile 0 follow those of block i of tile 1; a tile that skips a block
+      // (block-sparse lists) still takes and passes the turn.
+      const bool pingpong = H3SA_PINGPONG && n_tiles == 2;
+      const uint32_t tok_wait = smem_u32(&sm.exp_tok[t ^ 1][warp & 3]);
+      const uint32_t tok_give = smem_u32(&sm.exp_tok[t][warp & 3]);
       for (int i = 0; i < nblk; ++i) {
         int b, m;
-        block_at(i, b, m);
-        if (!((m >> t) & 1)) continue;
+        next_block(b, m);
+        const bool turn_wait = pingpong && (t == 1 || i > 0);
+        const uint32_t turn_ph = static_cast<uint32_t>(t == 1 ? i : i - 1) & 1u;
+        if (!((m >> t) & 1)) {
+          if (pingpong) {
+            if (turn_wait && !(ok = mbar_wait(tok_wait, turn_ph, abort_flag, p.err))) break;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(tok_give);
+          }
+          continue;
+        }
         if (!(ok = mbar_wait(smem_u32(&sm.s_full[t]), c & 1, abort_flag, p.err))) break;
         const bool tr = (warp & 3) == 0 && lane == 0;
         if (tr) H3SA_TRACE_AT(i, 5 * t + 0);
@@ -426,6 +475,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         reg_fence32(r1);
         reg_fence32(r2);
         reg_fence32(r3);
+        // the scores are in registers: the next QK may overwrite S_t
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.s_free[t]));
         if (tr) H3SA_TRACE_AT(i, 5 * t + 1);
         float s[kBlockN];
 #pragma unroll
@@ -458,15 +511,56 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mx3 = fmax3(mx3, s[j + 3], s[j + 7]);
         }
         const float mx = fmaxf(fmax3(mx0, mx1, mx2), mx3);
-        if (tr) H3SA_TRACE_AT(i, 16 + 2 * t);
         const float m_blk = mx * scale_log2;
         const bool need = m_blk > m_used + kRescaleThreshold;
         const float m_new = need ? m_blk : m_used;
+        // O is rescaled further down, once the previous PV has completed; l now
+        const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
         const bool any_need = c > 0 && __any_sync(0xffffffffu, need);
-        if (tr) H3SA_TRACE_AT(i, 17 + 2 * t);
+        l_sum *= alpha;
+        m_used = m_new;
+        // x = s * scale_log2 - (m_used - boost) in packed fp32 pairs, then 2^x on the MUFU; P
+        // packed for the PV MMA, row sum in fp32.
+        const float bias = kBoost - m_used;
+        const uint64_t bias2 = f2_pack(bias, bias);
+#pragma unroll
+        for (int j = 0; j < kBlockN; j += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(s[j], s[j + 1]), scale2, bias2), x0, x1);
+          s[j] = x0;
+          s[j + 1] = x1;
+        }
+        if (turn_wait && !(ok = mbar_wait(tok_wait, turn_ph, abort_flag, p.err))) break;
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+        uint32_t pk[kBlockN / 2];  // bf16: one pair per word; e4m3: two pairs per word
+#pragma unroll
+        for (int j = 0; j < kBlockN; j += 2) {
+          const float p0 = fast_exp2(s[j]);
+          const float p1 = fast_exp2(s[j + 1]);
+          sum2 = f2_add(sum2, f2_pack(p0, p1));
+          if constexpr (kFp8) {
+            uint16_t q;
+            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(q) : "f"(p1), "f"(p0));
+            if ((j & 2) == 0) pk[j / 4] = q;
+            else pk[j / 4] |= static_cast<uint32_t>(q) << 16;
+          } else {
+            pk[j / 2] = pack_bf16x2(p0, p1);
+          }
+        }
+        if (pingpong) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tok_give);
+        }
+        float sa, sb;
+        f2_unpack(sum2, sa, sb);
+        l_sum += sa + sb;
+        if (tr) H3SA_TRACE_AT(i, 5 * t + 3);
+        // The previous PV has read P out of shared memory and finished accumulating into O.
+        if (c > 0 && !(ok = mbar_wait(smem_u32(&sm.pv_done[t]), (c - 1) & 1, abort_flag, p.err)))
+          break;
+        if (tr) H3SA_TRACE_AT(i, 5 * t + 2);
         if (any_need) {
-          const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
-          l_sum *= alpha;
+          tc_fence_after();
 #pragma unroll
           for (int ch = 0; ch < 4; ++ch) {
             uint32_t o[32];
@@ -479,58 +573,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           tmem_wait_st();
         }
-        m_used = m_new;
-        // ping-pong: round c of tile 1 follows round c of tile 0; round c of tile 0 follows
-        // round c - 1 of tile 1
-        if (pingpong && (t == 1 || c > 0)) {
-          const uint32_t ph = static_cast<uint32_t>(t == 1 ? c : c - 1) & 1u;
-          if (!(ok = mbar_wait(smem_u32(&sm.exp_done[t ^ 1]), ph, abort_flag, p.err))) break;
-        }
-        if (tr) H3SA_TRACE_AT(i, 5 * t + 2);
-        // x = s * scale_log2 - (m_used - boost) in packed fp32 pairs, then 2^x on the MUFU
-        // (kExpPolyPer16 of every 16 on the FMA pipe); P packed for the PV MMA, row sum in fp32.
-        const float bias = kBoost - m_used;
-        const uint64_t bias2 = f2_pack(bias, bias);
+        // P row into shared memory in the 128-byte-swizzled K-major layout the PV MMA reads
+        // (16-byte chunk c of a row at position c ^ (row % 8) of its 128-byte line)
+        constexpr int kChunks = kBlockN * Cfg::kElem / 16;
 #pragma unroll
-        for (int j = 0; j < kBlockN; j += 2) {
-          float x0, x1;
-          f2_unpack(f2_fma(f2_pack(s[j], s[j + 1]), scale2, bias2), x0, x1);
-          s[j] = x0;
-          s[j + 1] = x1;
+        for (int ch = 0; ch < kChunks; ++ch) {
+          uint8_t* dst = prow + (ch >> 3) * Cfg::kAtomBytes + (((ch & 7) ^ (row & 7)) << 4);
+          *reinterpret_cast<uint4*>(dst) =
+              make_uint4(pk[4 * ch], pk[4 * ch + 1], pk[4 * ch + 2], pk[4 * ch + 3]);
         }
-        uint64_t sum2 = f2_pack(0.f, 0.f);
-        uint32_t pk[kBlockN / 2];  // bf16: one pair per word; e4m3: two pairs per word
-#pragma unroll
-        for (int j = 0; j < kBlockN; j += 2) {
-          float p0, p1;
-          if ((j % 16) < kExpPolyPer16) {
-            exp2_poly_pair(s[j], s[j + 1], p0, p1);
-            if (partial) {
-              if (j < lo || j >= hi) p0 = 0.f;
-              if (j + 1 < lo || j + 1 >= hi) p1 = 0.f;
-            }
-          } else {
-            p0 = fast_exp2(s[j]);
-            p1 = fast_exp2(s[j + 1]);
-          }
-          sum2 = f2_add(sum2, f2_pack(p0, p1));
-          if constexpr (kFp8) {
-            uint16_t q;
-            asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(q) : "f"(p1), "f"(p0));
-            if ((j & 2) == 0) pk[j / 4] = q;
-            else pk[j / 4] |= static_cast<uint32_t>(q) << 16;
-          } else {
-            pk[j / 2] = pack_bf16x2(p0, p1);
-          }
-        }
-        if (pingpong) mbar_arrive(smem_u32(&sm.exp_done[t]));
-        float sa, sb;
-        f2_unpack(sum2, sa, sb);
-        l_sum += sa + sb;
-        if (tr) H3SA_TRACE_AT(i, 5 * t + 3);
-        tmem_st32(tP, *reinterpret_cast<uint32_t(*)[32]>(pk));
-        if constexpr (!kFp8) tmem_st32(tP + 32, *reinterpret_cast<uint32_t(*)[32]>(pk + 32));
-        tmem_wait_st();
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();
         mbar_arrive(smem_u32(&sm.p_full[t]));
         if (tr) H3SA_TRACE_AT(i, 5 * t + 4);

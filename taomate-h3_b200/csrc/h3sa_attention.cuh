@@ -3,20 +3,23 @@
 // One CTA owns two 128-row query tiles of one head and walks a list of 128-row KV blocks
 // taken from a paged, head-major KV pool (page p of head h = rows [128p, 128p+128) of
 // that head's plane). Warp roles:
-//   warp 0      TMA producer: Q tiles once, then K and V blocks through 2-stage rings.
-//   warp 1      TMEM owner and MMA issuer (one thread): S_t = Q_t K^T (smem x smem),
-//               O_t += P_t V (P from TMEM x V from smem), fp32 accumulators in TMEM.
-//   warps 2-3   idle (warp 2 builds the block-sparse union list before the roles start)
+//   warp 0      TMA producer of the Q tiles (once) and of K blocks (2-stage ring).
+//   warp 3      TMA producer of V blocks (1 stage for bf16, 2 for e4m3).
+//   warp 1, 2   MMA issuers of query tile 0 and tile 1 (warp 1 also owns TMEM), converged
+//               warps with one elected lane per tcgen05 instruction:
+//               S_t = Q_t K^T (smem x smem) and O_t += P_t V (smem x smem), fp32 in TMEM.
+//               Warp 2 builds the block-sparse bitmaps before the roles start.
 //   warps 4-7   softmax of tile 0, warps 8-11 softmax of tile 1 (one thread per query row;
-//               warp w reads TMEM lanes 32*(w%4) .. +31):
-//               online max / sum, lazy O rescale, P written back to TMEM as bf16, and the
-//               final normalise + bf16 store.
-// TMEM columns: S0 [0,128) with P0 aliased at [64,128), S1 [128,256) with P1 at
-// [192,256), O0 [256,384), O1 [384,512).
+//               warp w reads TMEM lanes 32*(w%4) .. +31): online max / sum, lazy O rescale,
+//               P written to shared memory in the MMA operand layout, and the final
+//               normalise + bf16 store.
+// TMEM columns: S0 [0,128), S1 [128,256), O0 [256,384), O1 [384,512). Shared memory: Q0, Q1,
+// P0, P1, the K ring and the V ring.
 //
-// The MMA issue order per KV block i is PV_t(i-1) then QK_t(i) for each tile t. The QK
-// that overwrites S_t (and so P_t) is issued after the PV that reads P_t; tcgen05.mma
-// operations issued by one thread execute in issue order, which orders the two.
+// The MMA warp of tile t issues QK_t(i) once the softmax has loaded S_t(i-1) into registers
+// (s_free) and PV_t(i-1) once it has written P_t(i-1) (p_full), so QK_t(i) runs while the
+// softmax of block i-1 computes its exponentials. The softmax writes P_t(i) only after
+// PV_t(i-1) has completed (pv_done), and rescales O_t at that point when its row maximum grew.
 #pragma once
 
 #include "h3sa_ptx.cuh"
@@ -26,9 +29,8 @@ namespace h3sa {
 constexpr int kHeadDim = 128;
 constexpr int kBlockM = 128;
 constexpr int kBlockN = 128;
-constexpr int kKVStages = 2;
 constexpr int kAttnThreads = 384;
-// setmaxnreg split: warps 0-3 (producer, MMA, two idle) keep kRegsControl registers, the two
+// setmaxnreg split: warps 0-3 (producers and MMA issuers) keep kRegsControl registers, the two
 // softmax warpgroups get kRegsSoftmax. The sum must fit the launch allocation
 // (threads x registers per thread at launch, 168 under these launch bounds).
 #ifndef H3SA_REGS_CONTROL

@@ -284,29 +284,4 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   return d;
 }
 
-// 2^x for a pair on the FMA pipe: x = n + f with n = rint(x) from the 1.5 * 2^23 shift
-// trick, 2^f on [-0.5, 0.5] by a cubic fitted for minimax relative error (7.5e-5, fitted
-// for this kernel), and 2^n added to the exponent field. Inputs are clamped to >= -127.
-__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, float& y1) {
-  constexpr float kShift = 12582912.0f;  // 1.5 * 2^23
-  const uint64_t shift = f2_pack(kShift, kShift);
-  const uint64_t nshift = f2_pack(-kShift, -kShift);
-  const uint64_t x = f2_pack(fmaxf(x0, -127.0f), fmaxf(x1, -127.0f));
-  const uint64_t t = f2_add(x, shift);
-  const uint64_t r = f2_add(t, nshift);
-  float r0, r1, xa, xb;
-  f2_unpack(r, r0, r1);
-  f2_unpack(x, xa, xb);
-  const uint64_t f = f2_pack(xa - r0, xb - r1);
-  uint64_t p = f2_fma(f2_pack(0.05517132143404307f, 0.05517132143404307f), f,
-                      f2_pack(0.24261054228171952f, 0.24261054228171952f));
-  p = f2_fma(p, f, f2_pack(0.6932609856052563f, 0.6932609856052563f));
-  p = f2_fma(p, f, f2_pack(0.999928109364153f, 0.999928109364153f));
-  float p0, p1, t0, t1;
-  f2_unpack(p, p0, p1);
-  f2_unpack(t, t0, t1);
-  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
-  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
-}
-
 }  // namespace h3sa
