@@ -77,6 +77,12 @@ H3SA_API size_t h3sa_attention_smem_bytes(int fp8);
  * [heads, q_blocks] and kv_indices [heads, q_blocks, kv_index_stride] (int32, device; each
  * list sorted ascending, absolute logical block indices); q-block j of a problem covers query
  * rows [q_lo + 128j, q_lo + 128j + 128). Dense-only launches pass NULL lists.
+ * Block-sparse problems spanning more than 64 KV blocks run split-KV: a pair of query blocks
+ * with a long union list is processed as up to 4 KV segments whose partial results are merged
+ * on the device. Their workspace belongs to the (device, stream) pair and is grown on demand;
+ * growing it allocates device memory and waits for the device, so it must not happen during
+ * stream capture (make one uncaptured call of the same size first). Launches on one stream
+ * share it; launches on different streams get their own.
  *
  * Replaces: the FlashAttention-3 calls of the streaming hook and the K/V concatenation in
  * front of them (T/streaming/attention_hook.py:77-92; F/streaming/attention_hook.py:288-316,

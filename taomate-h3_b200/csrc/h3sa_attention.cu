@@ -96,6 +96,7 @@ struct alignas(1024) AttnSmem {
   uint32_t tmem_base;
   int abort_flag;
   int n_blocks;
+  int split_last;  // split-KV: this CTA finished its pair last and merges the segments
   uint32_t kv_mask[2][kMaskWords];  // block-sparse: bit i = tile t attends to block b_lo + i
 };
 
@@ -173,6 +174,69 @@ __device__ __forceinline__ void walk_next(BlockWalk& s, bool sparse, int b_lo, i
   m = static_cast<int>(((mask[0][w] >> bit) & 1u) | (((mask[1][w] >> bit) & 1u) << 1));
 }
 
+// Skip the first k blocks of the walk (the start of this CTA's split-KV segment).
+__device__ __forceinline__ void walk_skip(BlockWalk& s, bool sparse, int k,
+                                          const uint32_t (*mask)[kMaskWords]) {
+  if (!sparse) {
+    s.next += k;
+    return;
+  }
+  while (k > 0) {
+    if (s.rem == 0u) {
+      if (s.next >= kMaskWords) return;
+      s.rem = mask[0][s.next] | mask[1][s.next];
+      ++s.next;
+      continue;
+    }
+    const int c = __popc(s.rem);
+    if (c <= k) {
+      k -= c;
+      s.rem = 0u;
+    } else {
+      for (; k > 0; --k) s.rem &= s.rem - 1u;
+    }
+  }
+}
+
+// Store the 128 output rows of a query tile as bf16. Each warp stages its 32 rows in `stage`
+// (32 rows x 128 bytes: half a row at a time, 16-byte chunks XOR-swizzled by row) and stores
+// them with 8 lanes per row, so one warp store instruction writes four whole 128-byte lines
+// instead of 32 scattered 16-byte pieces (this matters most for rows bound for a peer GPU over
+// NVLink). `dst` is this thread's row address (0: no row); `row_values(ch, v)` yields the 32
+// scaled fp32 values of column chunk ch (0..3) of this thread's row.
+template <typename RowValues>
+__device__ __forceinline__ void store_tile_rows(uint8_t* stage, int lane, unsigned long long dst,
+                                                RowValues&& row_values) {
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+#pragma unroll
+    for (int hc = 0; hc < 2; ++hc) {
+      float v[32];
+      row_values(half * 2 + hc, v);
+      uint32_t o[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int chunk = hc * 4 + j;
+        *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+            make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int r = it * 4 + (lane >> 3);
+      const int chunk = lane & 7;
+      const uint4 val =
+          *reinterpret_cast<const uint4*>(stage + r * 128 + ((chunk ^ (r & 7)) << 4));
+      const unsigned long long d = __shfl_sync(0xffffffffu, dst, r);
+      if (d) reinterpret_cast<uint4*>(static_cast<uintptr_t>(d) + half * 128)[chunk] = val;
+    }
+    __syncwarp();
+  }
+}
+
 template <bool kFp8>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -192,8 +256,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   while (pi + 1 < p.n_prob && static_cast<int>(blockIdx.x) >= p.prob[pi + 1].cta_begin) ++pi;
   const AttnProblemDev pr = p.prob[pi];
   const int local = static_cast<int>(blockIdx.x) - pr.cta_begin;
-  const int head = local / pr.pairs;
-  const int pair = local - head * pr.pairs;
+  const int seg = local % pr.split;  // split-KV segment of this CTA (block-sparse problems)
+  const int head = local / pr.split / pr.pairs;
+  const int pair = local / pr.split - head * pr.pairs;
   const int n_tiles = min(2, pr.tiles - pair * 2);
   const int q_row0 = pr.q_lo + pair * 2 * kBlockM;
   const int b_lo = pr.kv_lo / kBlockN;
@@ -222,10 +287,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     sm.n_blocks = b_hi - b_lo;
     fence_mbar_init();
   }
-  if (warp == 1) {
-    tmem_alloc(smem_u32(&sm.tmem_base), 512);
-    tmem_relinquish();
-  }
   __syncthreads();
   if (pr.sparse && warp == 2) {
     const int qb = (q_row0 - pr.q_lo) / kBlockM;
@@ -236,14 +297,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     build_masks(A, na, A + p.kv_stride, nb, b_lo, b_hi, sm.kv_mask, &sm.n_blocks, p.err,
                 abort_flag);
   }
+  __syncthreads();
+
+  // Split-KV: a union of more than kSplitSegBlocks blocks is cut into up to pr.split equal
+  // segments, one per CTA of the pair; each writes unnormalised partial results and the last
+  // to finish merges them. CTAs beyond the segments needed leave before taking TMEM.
+  const int n_all = sm.n_blocks;
+  const int nseg = pr.split > 1 ? max(1, min(pr.split, (n_all + kSplitSegBlocks - 1) / kSplitSegBlocks))
+                                : 1;
+  if (seg >= nseg) return;
+  const int seg_len = (n_all + nseg - 1) / nseg;
+  const int seg_lo = min(n_all, seg * seg_len);
+  const int nblk = min(n_all, seg_lo + seg_len) - seg_lo;
+  const bool split_out = nseg > 1;
+  const int gseg = (pr.pair_begin + head * pr.pairs + pair) * pr.split;  // first segment slot
+
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), 512);
+    tmem_relinquish();
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
 
   const uint32_t tbase = sm.tmem_base;
-  const int nblk = sm.n_blocks;
   const int dense_mask = (n_tiles > 1) ? 3 : 1;
   BlockWalk walk;
+  walk_skip(walk, pr.sparse != 0, seg_lo, sm.kv_mask);
+  // destination of output row `row` of query tile t; 0 for rows past the problem's range
+  auto row_dst = [&](int t, int row) -> unsigned long long {
+    const int qrow = q_row0 + t * kBlockM + row;
+    if (qrow >= pr.q_hi) return 0ull;
+    if (p.out_peers) {
+      // heads -> sequence exchange fused into the store: row qrow belongs to the sequence
+      // shard of rank qrow / rows_per_rank, which holds all heads of its rows
+      const int owner = min(qrow / p.out_rows_per_rank, p.out_ranks - 1);
+      const int orow = qrow - owner * p.out_rows_per_rank;
+      return p.out_peers[owner] +
+             (static_cast<size_t>(orow) * p.out_heads + p.out_head0 + head) * kHeadDim * 2;
+    }
+    return reinterpret_cast<uintptr_t>(p.out) +
+           (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim * 2;
+  };
   auto next_block = [&](int& b, int& m) {
     walk_next(walk, pr.sparse != 0, b_lo, dense_mask, sm.kv_mask, b, m);
   };
@@ -591,71 +686,103 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (ok) ok = mbar_wait(smem_u32(&sm.o_done[t]), 0, abort_flag, p.err);
       if (ok) {
         tc_fence_after();
-        // c == 0: this tile's block list was empty, its rows see no key and are written as
-        // zeros (TMEM O was never written)
+        // c == 0: this tile attended no block (of this segment), its rows see no key and are
+        // written as zeros (TMEM O was never written)
         const bool any = c > 0;
-        float out_scale = any ? 1.0f / l_sum : 0.f;
-        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
-        // destination of this thread's row; 0 for rows past the problem's query range
-        const int qrow = q_row0 + t * kBlockM + row;
-        unsigned long long dst = 0;
-        if (qrow < pr.q_hi) {
-          if (p.out_peers) {
-            // heads -> sequence exchange fused into the store: row qrow belongs to the
-            // sequence shard of rank qrow / rows_per_rank, which holds all heads of its rows
-            const int owner = min(qrow / p.out_rows_per_rank, p.out_ranks - 1);
-            const int orow = qrow - owner * p.out_rows_per_rank;
-            dst = p.out_peers[owner] +
-                  (static_cast<size_t>(orow) * p.out_heads + p.out_head0 + head) * kHeadDim * 2;
-          } else {
-            dst = reinterpret_cast<uintptr_t>(p.out) +
-                  (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim * 2;
-          }
-        }
-        // The rows leave through shared memory. Every MMA that read this tile's Q buffer has
-        // completed (o_done), so each warp stages its 32 rows there, half a row (64 columns,
-        // 128 bytes) at a time, chunks XOR-swizzled by row, and stores them back with 8 lanes
-        // per row: one warp store instruction writes four whole 128-byte lines instead of 32
-        // scattered 16-byte pieces, which matters most for rows bound for a peer over NVLink.
-        uint8_t* stage = sm.q[t] + (warp & 3) * (32 * 128);
+        if (split_out) {
+          // unnormalised partial of this segment: O (fp32), the row's running maximum (log2
+          // units of the scaled scores) and its sum of P
+          const size_t slot = (static_cast<size_t>(gseg + seg) * 2 + t) * kBlockM + row;
+          float4* po = reinterpret_cast<float4*>(p.split_o + slot * kHeadDim);
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-#pragma unroll
-          for (int hc = 0; hc < 2; ++hc) {
+          for (int ch = 0; ch < 4; ++ch) {
             uint32_t r[32];
             if (any) {
-              tmem_ld32(tO + (half * 2 + hc) * 32, r);
+              tmem_ld32(tO + ch * 32, r);
               tmem_wait_ld();
               reg_fence32(r);
             } else {
 #pragma unroll
               for (int j = 0; j < 32; ++j) r[j] = 0u;
             }
-            uint32_t o[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j)
-              o[j] = pack_bf16x2(__uint_as_float(r[2 * j]) * out_scale,
-                                 __uint_as_float(r[2 * j + 1]) * out_scale);
+            for (int j = 0; j < 8; ++j)
+              po[ch * 8 + j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                           __uint_as_float(r[4 * j + 2]),
+                                           __uint_as_float(r[4 * j + 3]));
+          }
+          p.split_ml[slot * 2] = any ? m_used : -INFINITY;
+          p.split_ml[slot * 2 + 1] = any ? l_sum : 0.f;
+          __threadfence();
+        } else {
+          float out_scale = any ? 1.0f / l_sum : 0.f;
+          if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+          store_tile_rows(sm.q[t] + (warp & 3) * (32 * 128), lane, row_dst(t, row),
+                          [&](int ch, float (&v)[32]) {
+                            uint32_t r[32];
+                            if (any) {
+                              tmem_ld32(tO + ch * 32, r);
+                              tmem_wait_ld();
+                              reg_fence32(r);
+                            } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const int chunk = hc * 4 + j;
-              *reinterpret_cast<uint4*>(stage + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
-                  make_uint4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+                              for (int j = 0; j < 32; ++j) r[j] = 0u;
+                            }
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * out_scale;
+                          });
+          // peer stores: make them visible system-wide before the kernel is seen as done
+          if (p.out_peers) __threadfence_system();
+        }
+      }
+    }
+    if (split_out) {
+      // Last-arriver merge over the pair's segments (no waiting: the CTA whose increment
+      // completes the count merges). Named barrier 1 spans the 256 softmax threads, every one
+      // of which reaches it.
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (threadIdx.x == 128) {
+        __threadfence();
+        const int done = atomicAdd(p.split_count + gseg / pr.split, 1);
+        sm.split_last = (done == nseg - 1) ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (sm.split_last && t < n_tiles && !*abort_flag) {
+        __threadfence();
+        const int row = (warp & 3) * 32 + lane;
+        float mx = -INFINITY;
+        for (int sg = 0; sg < nseg; ++sg) {
+          const size_t slot = (static_cast<size_t>(gseg + sg) * 2 + t) * kBlockM + row;
+          mx = fmaxf(mx, __ldcg(p.split_ml + slot * 2));
+        }
+        float acc[kHeadDim];
+#pragma unroll
+        for (int j = 0; j < kHeadDim; ++j) acc[j] = 0.f;
+        float lsum = 0.f;
+        if (mx > -INFINITY) {
+          for (int sg = 0; sg < nseg; ++sg) {
+            const size_t slot = (static_cast<size_t>(gseg + sg) * 2 + t) * kBlockM + row;
+            const float ms = __ldcg(p.split_ml + slot * 2);
+            const float w = ms > -INFINITY ? fast_exp2(ms - mx) : 0.f;
+            lsum += w * __ldcg(p.split_ml + slot * 2 + 1);
+            const float4* po = reinterpret_cast<const float4*>(p.split_o + slot * kHeadDim);
+#pragma unroll
+            for (int j = 0; j < kHeadDim / 4; ++j) {
+              const float4 v = __ldcg(po + j);
+              acc[4 * j] += w * v.x;
+              acc[4 * j + 1] += w * v.y;
+              acc[4 * j + 2] += w * v.z;
+              acc[4 * j + 3] += w * v.w;
             }
           }
-          __syncwarp();
-#pragma unroll
-          for (int it = 0; it < 8; ++it) {
-            const int r = it * 4 + (lane >> 3);
-            const int chunk = lane & 7;
-            const uint4 v =
-                *reinterpret_cast<const uint4*>(stage + r * 128 + ((chunk ^ (r & 7)) << 4));
-            const unsigned long long d = __shfl_sync(0xffffffffu, dst, r);
-            if (d) reinterpret_cast<uint4*>(static_cast<uintptr_t>(d) + half * 128)[chunk] = v;
-          }
-          __syncwarp();
         }
-        // peer stores: make them visible system-wide before the kernel is seen as done
+        float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
+        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        store_tile_rows(sm.q[t] + (warp & 3) * (32 * 128), lane, row_dst(t, row),
+                        [&](int ch, float (&v)[32]) {
+#pragma unroll
+                          for (int j = 0; j < 32; ++j) v[j] = acc[ch * 32 + j] * out_scale;
+                        });
         if (p.out_peers) __threadfence_system();
       }
     }
@@ -670,6 +797,61 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // ------------------------------------------------------------------------ host side
+
+// Split-KV workspace of one (device, stream): grown on demand, never shrunk. Growing it waits
+// for the device (the old buffer may be in use by launches already queued) and so cannot run
+// inside stream capture; a capture needs an earlier call on that stream with at least as many
+// split pairs. Launches on one stream are ordered, so they can share the buffer.
+struct SplitSpace {
+  float* o;
+  float* ml;
+  int* count;
+};
+
+static int split_workspace(int pairs, cudaStream_t stream, SplitSpace& out) {
+  struct Entry {
+    int dev;
+    cudaStream_t stream;
+    int pairs;
+    void* base;
+  };
+  static std::mutex mu;
+  static Entry entries[64];
+  static int n_entries = 0;
+  const size_t o_floats = static_cast<size_t>(pairs) * kSplitMax * 2 * kBlockM * kHeadDim;
+  const size_t ml_floats = static_cast<size_t>(pairs) * kSplitMax * 2 * kBlockM * 2;
+  const size_t bytes = (o_floats + ml_floats) * sizeof(float) + static_cast<size_t>(pairs) * 4;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  Entry* e = nullptr;
+  for (int i = 0; i < n_entries; ++i)
+    if (entries[i].dev == dev && entries[i].stream == stream) e = &entries[i];
+  if (!e) {
+    if (n_entries == 64)
+      return set_error(H3SA_ERR_UNSUPPORTED, "attention: split-KV workspaces for more than 64 "
+                       "(device, stream) pairs");
+    e = &entries[n_entries++];
+    *e = Entry{dev, stream, 0, nullptr};
+  }
+  if (e->pairs < pairs) {
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return set_cuda_error("split-KV workspace (synchronize)", err);
+    if (e->base) cudaFree(e->base);
+    e->base = nullptr;
+    e->pairs = 0;
+    err = cudaMalloc(&e->base, bytes);
+    if (err != cudaSuccess) return set_cuda_error("cudaMalloc(split-KV workspace)", err);
+    e->pairs = pairs;
+  }
+  float* base = static_cast<float*>(e->base);
+  out.o = base;
+  out.ml = base + o_floats;
+  out.count = reinterpret_cast<int*>(base + o_floats + ml_floats);
+  cudaError_t err = cudaMemsetAsync(out.count, 0, static_cast<size_t>(pairs) * 4, stream);
+  if (err != cudaSuccess) return set_cuda_error("cudaMemsetAsync(split-KV counters)", err);
+  return H3SA_OK;
+}
 
 template <bool kFp8>
 static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
@@ -725,6 +907,7 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   prm.out_head0 = L.out_head0;
   int ctas = 0;
   int n = 0;
+  int split_pairs = 0;
   for (int i = 0; i < L.num_problems; ++i) {
     const auto& src = L.problems[i];
     if (src.q_hi <= src.q_lo) continue;
@@ -736,11 +919,25 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
     d.sparse = src.sparse ? 1 : 0;
     d.tiles = (src.q_hi - src.q_lo + kBlockM - 1) / kBlockM;
     d.pairs = (d.tiles + 1) / 2;
+    // block-sparse lists are uneven (rows that keep every block next to rows that keep a
+    // quarter): those pairs get kSplitMax CTAs and decide on the device how many to use
+    const int nblocks = (src.kv_hi + kBlockN - 1) / kBlockN - src.kv_lo / kBlockN;
+    d.split = (d.sparse && nblocks > kSplitSegBlocks) ? kSplitMax : 1;
+    d.pair_begin = split_pairs;
+    if (d.split > 1) split_pairs += d.pairs * L.heads;
     d.cta_begin = ctas;
-    ctas += d.pairs * L.heads;
+    ctas += d.pairs * L.heads * d.split;
   }
   prm.n_prob = n;
   if (ctas == 0) return H3SA_OK;
+  if (split_pairs > 0) {
+    SplitSpace ws;
+    int rc = split_workspace(split_pairs, stream, ws);
+    if (rc) return rc;
+    prm.split_o = ws.o;
+    prm.split_ml = ws.ml;
+    prm.split_count = ws.count;
+  }
   const size_t smem = attn_smem_bytes<kFp8>();
   static std::mutex mu;
   static bool configured[64] = {false};

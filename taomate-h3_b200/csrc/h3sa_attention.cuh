@@ -44,6 +44,13 @@ constexpr int kRegsSoftmax = H3SA_REGS_SOFTMAX;
 constexpr int kRegSplitTotal = 128 * kRegsControl + 256 * kRegsSoftmax;
 constexpr int kMaxProblems = 4;
 constexpr int kMaxUnionBlocks = 2048;
+// Split-KV for block-sparse problems: up to kSplitMax CTAs per query-tile pair, one segment of
+// at least kSplitSegBlocks blocks of the pair's union list each.
+#ifndef H3SA_SPLIT_SEG_BLOCKS
+#define H3SA_SPLIT_SEG_BLOCKS 64
+#endif
+constexpr int kSplitMax = 4;
+constexpr int kSplitSegBlocks = H3SA_SPLIT_SEG_BLOCKS;
 
 struct AttnProblemDev {
   int q_lo, q_hi;    // query / output rows [q_lo, q_hi) of the packed [rows, heads, d] tensors
@@ -52,6 +59,8 @@ struct AttnProblemDev {
   int cta_begin;     // first CTA of this problem in the flattened grid
   int tiles;         // ceil((q_hi - q_lo) / 128)
   int pairs;         // ceil(tiles / 2)
+  int split;         // CTAs per pair (split-KV segments; 1 = no split)
+  int pair_begin;    // index of this problem's first pair among the split problems' pairs
 };
 
 struct AttnParams {
@@ -75,6 +84,11 @@ struct AttnParams {
   int q_blocks;
   int kv_stride;
   int* err;                  // device error word (nullable)
+  // split-KV workspace (problems with split > 1): per segment slot and tile, 128 rows of
+  // unnormalised O [128] and (max, sum); one arrival counter per pair, zero at launch
+  float* split_o;
+  float* split_ml;
+  int* split_count;
   // output rows scattered to peers (see AttnLaunch in h3sa_host.h); null: write `out`
   const uint64_t* out_peers;
   int out_ranks;

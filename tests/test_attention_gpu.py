@@ -410,3 +410,59 @@ def test_pool_rows_outside_the_kv_range_do_not_leak() -> None:
     deq = lambda x8, sc: x8.squeeze(0).float() * sc.reshape(1, -1, 1)  # noqa: E731
     ref8 = ref_attention(deq(q8, qs), deq(k8p, kss), deq(v8p, vss), scale)
     assert rel_l2(out8, ref8) <= FP8_TOL
+
+
+@pytest.mark.parametrize("fp8", [False, True])
+def test_block_sparse_split_kv_segments(fp8: bool) -> None:
+    """Block-sparse pairs with long lists run as several CTAs, one KV segment each, merged by
+    the last to finish: a pair whose first tile keeps only early blocks (its later segments
+    hold no block of that tile), a pair whose second tile keeps no block (zeros), a
+    single-tile pair keeping every block, a partial first KV block, e4m3 and bf16."""
+
+    h3sa = _h3sa()
+    heads, nq, kv_lo, nk = 2, 4 * 128 + 37, 100, 24000
+    q, k, v, kp, vp, table = _dense_case(heads, nq, kv_lo, nk, seed=31)
+    kv_hi = kv_lo + nk
+    qb, kb = (nq + 127) // 128, (kv_hi + 127) // 128
+    num = torch.zeros(heads, qb, dtype=torch.int32)
+    idx = torch.zeros(heads, qb, kb, dtype=torch.int32)
+    allowed = torch.zeros(heads, nq, kv_hi, dtype=torch.bool)
+    for h in range(heads):
+        lists = {0: list(range(0, 20)), 1: list(range(kb)), 2: list(range(h, kb, 2)), 3: [],
+                 4: list(range(kb))}
+        for j, keep in lists.items():
+            num[h, j] = len(keep)
+            if keep:
+                idx[h, j, : len(keep)] = torch.tensor(keep, dtype=torch.int32)
+            for b in keep:
+                allowed[h, j * 128:(j + 1) * 128, max(b * 128, kv_lo):(b + 1) * 128] = True
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    prob = [h3sa.AttentionProblem(0, nq, kv_lo, kv_hi, sparse=True)]
+    lists_kw = dict(kv_num_blocks=num.cuda(), kv_indices=idx.cuda(), device_error=err)
+    out = torch.full_like(q, float("nan"))
+    if fp8:
+        q8, qs = h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0))
+        k8 = torch.zeros_like(kp, dtype=torch.float8_e4m3fn)
+        v8 = torch.zeros_like(vp, dtype=torch.float8_e4m3fn)
+        ks = torch.empty(heads, dtype=torch.float32, device="cuda")
+        vs = torch.empty(heads, dtype=torch.float32, device="cuda")
+        h3sa.quantize_fp8_pool(kp, k8, ks, table, kv_hi)
+        h3sa.quantize_fp8_pool(vp, v8, vs, table, kv_hi)
+        h3sa.attention_fwd(q8.squeeze(0), out, k8, v8, table, prob, scale,
+                           q_scale=qs.reshape(-1).contiguous(), k_scale=ks, v_scale=vs, **lists_kw)
+        k8r, kss = h3sa.quantize_fp8_e4m3_per_head(k.unsqueeze(0))
+        v8r, vss = h3sa.quantize_fp8_e4m3_per_head(v.unsqueeze(0))
+        deq = lambda x8, sc: x8.squeeze(0).float() * sc.reshape(1, -1, 1)
+        qr, kr, vr, tol = deq(q8, qs), deq(k8r, kss), deq(v8r, vss), FP8_TOL
+    else:
+        h3sa.attention_fwd(q, out, kp, vp, table, prob, scale, **lists_kw)
+        qr, kr, vr, tol = q, k, v, BF16_TOL
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    empty = slice(3 * 128, 4 * 128)
+    assert torch.count_nonzero(out[empty]) == 0
+    keep_rows = torch.ones(nq, dtype=torch.bool)
+    keep_rows[empty] = False
+    ref = ref_attention(qr, kr, vr, scale, allowed.cuda())
+    assert rel_l2(out[keep_rows], ref[keep_rows.cuda()]) <= tol
