@@ -9,8 +9,6 @@ differ only in where the bytes go. Skipped with fewer than two GPUs.
 
 from __future__ import annotations
 
-import os
-import socket
 import sys
 from pathlib import Path
 
@@ -22,22 +20,16 @@ pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parent.parent
 
 
-def _free_port() -> int:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _worker(rank: int, world: int, port: int) -> None:
+def _worker(rank: int, world: int, rendezvous: str) -> None:
     import datetime
 
     sys.path.insert(0, str(ROOT / "taomate-h3_b200"))
-    os.environ["MASTER_ADDR"] = "127.0.0.1"
-    os.environ["MASTER_PORT"] = str(port)
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
-                                         timeout=datetime.timedelta(seconds=60), device_id=dev)
+    # file rendezvous: no port to race for
+    torch.distributed.init_process_group("nccl", init_method=f"file://{rendezvous}", rank=rank,
+                                         world_size=world, timeout=datetime.timedelta(seconds=60),
+                                         device_id=dev)
     try:
         import h3sa
         from h3sa.kernels import PAGE_ROWS
@@ -112,9 +104,9 @@ def _worker(rank: int, world: int, port: int) -> None:
         torch.distributed.destroy_process_group()
 
 
-def test_fused_exchanges_match_nccl_path() -> None:
+def test_fused_exchanges_match_nccl_path(tmp_path: Path) -> None:
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(2, _free_port()), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, str(tmp_path / "rendezvous")), nprocs=2, join=True)

@@ -6,7 +6,6 @@ from __future__ import annotations
 
 import datetime
 import os
-import socket
 import sys
 from pathlib import Path
 
@@ -18,14 +17,14 @@ import torch.multiprocessing as mp
 ROOT = Path(__file__).resolve().parents[1]
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+def _worker(rank: int, world: int, rendezvous: str, out_dir: str) -> None:
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "taomate-h3_b200"))
     from h3sa.ulysses import ParallelContext, merged_qkv_sequence_to_heads
 
     from oracle import ulysses as ouly
 
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+    dist.init_process_group("gloo", init_method=f"file://{rendezvous}", rank=rank,
                             world_size=world, timeout=datetime.timedelta(seconds=60))
     tokens, heads, d = 5, 4, 8
     merged = [np.random.default_rng(50 + r).standard_normal((tokens, 3 * heads * d)).astype(np.float32)
@@ -59,10 +58,9 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
 
 
 def test_two_rank_exchange_and_validation(tmp_path: Path) -> None:
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
-    mp.start_processes(_worker, args=(2, port, str(tmp_path)), nprocs=2, start_method="spawn")
+    # file rendezvous: no port to race for
+    mp.start_processes(_worker, args=(2, str(tmp_path / "rendezvous"), str(tmp_path)), nprocs=2,
+                       start_method="spawn")
     for r in range(2):
         assert np.load(tmp_path / f"r{r}.npy").all()
         msg = (tmp_path / f"m{r}.txt").read_text()
