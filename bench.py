@@ -1,11 +1,15 @@
 #!/usr/bin/env python
 """Benchmark: 768p streaming chunk attention (TaoMate-H3 hot path) on B200.
 
-One step = one streaming-hook layer call of the 768p chunk on this rank: (SP > 1) pack the
-local merged QKV shard, NCCL all-to-all seq->heads, unpack; write the current chunk's K/V
-rows into the paged cache after the 16384-row history; attention of the 12509 media queries
-over [history | current] (plus the pad document over itself); (SP > 1) all-to-all of O back
-and unpack. Ulysses SP = number of GPUs, heads 24 / SP per GPU.
+One step = one streaming-hook layer call of the 768p chunk on this rank: the seq->heads
+exchange of the local merged QKV shard (SP > 1), the current chunk's K/V rows written into the
+paged cache after the 16384-row history, attention of the 12509 media queries over
+[history | current] (plus the pad document over itself), and the heads->seq exchange of O
+(SP > 1). Ulysses SP = number of GPUs, heads 24 / SP per GPU. For SP > 1 the exchanges are
+peer stores over NVLink by default: one kernel scatters Q to the owners' planes and K/V
+straight into the owners' caches, and the attention epilogue stores O into the owners'
+sequence shards. `--unfused` uses NCCL all-to-all with pack/unpack kernels and a separate
+cache append instead (the reference's structure).
 
 Prints one JSON line (rank 0). ``value`` = total attention TFLOP/s of the whole job
 (4 * Nq * Nk * d * H per step / max-over-ranks device time). ``e2e`` repeats the step
@@ -270,29 +274,33 @@ class Step:
         total_rows = nh + geo["rows"]
         pages = (total_rows + PAGE_ROWS - 1) // PAGE_ROWS
         self.table = torch.arange(pages, dtype=torch.int32, device=device)
-        self.kpool = torch.zeros(hl, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=device)
-        self.vpool = torch.zeros_like(self.kpool)
-        hist = torch.randn(nh, hl, d, device=device, generator=g).to(torch.bfloat16)
-        h3sa.kv_copy_rows([hist, hist], [self.kpool, self.vpool], count=nh, dst_table=self.table)
         rows, tokens = geo["rows"], geo["tokens"]
         if self.fused:
-            from h3sa.peer import PeerBuffer
+            # every rank maps every rank's Q plane, KV pools and output shard: the QKV scatter
+            # writes the current chunk's K/V straight into the owners' pools
+            from h3sa.peer import PeerBarrier, PeerBuffer
 
-            from h3sa.peer import PeerBarrier
-
-            self.qkv_peer = PeerBuffer((3, rows, hl, d))
+            self.kpool_peer = PeerBuffer((hl, pages * PAGE_ROWS, d))
+            self.vpool_peer = PeerBuffer((hl, pages * PAGE_ROWS, d))
+            self.kpool, self.vpool = self.kpool_peer.tensor, self.vpool_peer.tensor
+            self.kpool.zero_()
+            self.vpool.zero_()
+            self.q_peer = PeerBuffer((rows, hl, d))
             self.out_peer = PeerBuffer((tokens, heads, d))
             self.peer_barrier = PeerBarrier(device_error=None)
-            self.qkv = self.qkv_peer.tensor
             self.final = self.out_peer.tensor
-            self.flag = torch.zeros(1, dtype=torch.float32, device=device)
-        elif world > 1:
+        else:
+            self.kpool = torch.zeros(hl, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=device)
+            self.vpool = torch.zeros_like(self.kpool)
+        hist = torch.randn(nh, hl, d, device=device, generator=g).to(torch.bfloat16)
+        h3sa.kv_copy_rows([hist, hist], [self.kpool, self.vpool], count=nh, dst_table=self.table)
+        if world > 1 and not self.fused:
             self.send = torch.empty(world, 3, tokens, hl, d, dtype=torch.bfloat16, device=device)
             self.recv = torch.empty_like(self.send)
             self.qkv = torch.empty(3, rows, hl, d, dtype=torch.bfloat16, device=device)
             self.orecv = torch.empty(world, tokens, hl, d, dtype=torch.bfloat16, device=device)
             self.final = torch.empty(tokens, heads, d, dtype=torch.bfloat16, device=device)
-        else:
+        elif world == 1:
             self.qkv = self.merged.view(rows, 3, heads, d).permute(1, 0, 2, 3).contiguous()
         self.out = torch.empty(rows, hl, d, dtype=torch.bfloat16, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
@@ -305,13 +313,15 @@ class Step:
             self.problems.append(P(nq, rows, nh + nq, nh + rows))
         self.scale = d ** -0.5
         self.flops = 4.0 * nq * (nh + nq) * d * hl  # this rank's algorithmic FLOPs
-        self.launches_per_step = 2 + (4 if world > 1 else 0)
+        # h3sa kernels per step: SP=1 cache append + attention; NCCL path + pack, two unpacks;
+        # peer path: scatter into the caches, barrier, attention, barrier
+        self.launches_per_step = 4 if self.fused else 2 + (3 if world > 1 else 0)
 
     PHASES = ("pack", "qkv_all_to_all", "unpack", "cache_append", "attention", "o_all_to_all",
               "o_unpack")
-    PHASES_FUSED = ("qkv_scatter", "barrier_before_attention", "unused", "cache_append",
+    PHASES_FUSED = ("qkv_scatter_into_cache", "barrier_before_attention", "unused", "unused_append",
                     "attention_with_o_scatter", "barrier_after_attention", "unused2")
-    EXCHANGE_PHASES = ("qkv_all_to_all", "o_all_to_all", "qkv_scatter",
+    EXCHANGE_PHASES = ("qkv_all_to_all", "o_all_to_all", "qkv_scatter_into_cache",
                        "barrier_before_attention", "barrier_after_attention")
 
     def run(self, attn_events: tuple[torch.cuda.Event, torch.cuda.Event] | None = None,
@@ -331,20 +341,21 @@ class Step:
 
         mark(0)
         if self.fused:
-            from h3sa.peer import attention_fwd_scatter, scatter_qkv
+            from h3sa.peer import attention_fwd_scatter, scatter_qkv_paged
 
-            scatter_qkv(src, self.qkv_peer, num_heads=heads, head_dim=d)
+            # Q to the owners' planes, K/V into the owners' caches after the history
+            scatter_qkv_paged(src, self.q_peer, self.kpool_peer, self.vpool_peer, self.table,
+                              dst_start=self.n_hist, num_heads=heads, head_dim=d,
+                              device_error=self.err)
             mark(1)
             self.peer_barrier()
             mark(2)
             mark(3)
-            q, k, v = self.qkv[0], self.qkv[1], self.qkv[2]
-            h3sa.kv_copy_rows([k, v], [self.kpool, self.vpool], count=geo["rows"],
-                              dst_table=self.table, dst_start=self.n_hist, device_error=self.err)
             mark(4)
             if attn_events is not None:
                 attn_events[0].record()
-            attention_fwd_scatter(q, self.kpool, self.vpool, self.table, self.problems, self.scale,
+            attention_fwd_scatter(self.q_peer.tensor, self.kpool, self.vpool, self.table,
+                                  self.problems, self.scale,
                                   self.out_peer, device_error=self.err)
             if attn_events is not None:
                 attn_events[1].record()

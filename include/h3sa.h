@@ -254,6 +254,21 @@ H3SA_API int h3sa_scatter_qkv(const void* merged, int32_t tokens, int32_t heads,
                               int32_t head_dim, int32_t world, int32_t rank,
                               const uint64_t* peer_qkv, void* stream);
 
+/* h3sa_scatter_qkv with the cache append folded in: Q rows go to peer_q[owner] (a
+ * [world * tokens, heads / world, 128] plane, row rank * tokens + t), K and V rows straight into
+ * the owner's paged pools peer_key_pool[owner] / peer_value_pool[owner] ([heads / world,
+ * pool_pages * 128, 128] bf16) at logical row dst_start + rank * tokens + t through page_table,
+ * which must be the same on every rank (the ranks of a Ulysses group commit the same rows).
+ * A page-table entry outside the pool sets H3SA_DEVERR_BAD_PAGE and the row is skipped.
+ * Replaces: merged_qkv_sequence_to_heads (T/distributed/ulysses.py:103-132) followed by the
+ * cache's stage/commit copy of the current chunk's K/V (T/streaming/cache.py:133-171). */
+H3SA_API int h3sa_scatter_qkv_paged(const void* merged, int32_t tokens, int32_t heads,
+                                    int32_t head_dim, int32_t world, int32_t rank,
+                                    const uint64_t* peer_q, const uint64_t* peer_key_pool,
+                                    const uint64_t* peer_value_pool, int32_t pool_pages,
+                                    const int32_t* page_table, int32_t table_blocks,
+                                    int32_t dst_start, int32_t* device_error, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

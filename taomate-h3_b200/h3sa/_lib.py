@@ -106,6 +106,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "h3sa_ipc_open": (ctypes.c_int, [_P, ctypes.POINTER(ctypes.c_void_p)]),
     "h3sa_ipc_close": (ctypes.c_int, [_P]),
     "h3sa_scatter_qkv": (ctypes.c_int, [_P, _I, _I, _I, _I, _I, _P, _P]),
+    "h3sa_scatter_qkv_paged": (ctypes.c_int,
+                               [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _I, _I, _P, _P]),
     "h3sa_peer_barrier": (ctypes.c_int, [_P, _I, _I, ctypes.c_uint32, _P, _P]),
     "h3sa_permute_rows": (
         ctypes.c_int,

@@ -139,6 +139,41 @@ def scatter_qkv(merged: torch.Tensor, qkv: PeerBuffer, *, num_heads: int, head_d
          ptr(qkv.peer_table), stream_handle(stream))
 
 
+def scatter_qkv_paged(merged: torch.Tensor, q: PeerBuffer, key_pool: PeerBuffer,
+                      value_pool: PeerBuffer, page_table: torch.Tensor, *, dst_start: int,
+                      num_heads: int, head_dim: int = 128,
+                      device_error: torch.Tensor | None = None,
+                      stream: torch.cuda.Stream | None = None) -> None:
+    """Sequence -> heads with the cache append folded in: this rank's post-prologue shard
+    ``[T, 3 * H * d]`` goes to every owner rank's ``[W * T, H / W, d]`` Q plane and, for K and
+    V, straight into the owner's paged pools ``[H / W, pages * 128, d]`` at logical rows
+    ``dst_start + rank * T + t`` through ``page_table``, which must be the same on every rank
+    (the ranks of a Ulysses group commit the same rows)."""
+
+    _require_cuda(merged, page_table, device_error)
+    if merged.dtype != torch.bfloat16 or not merged.is_contiguous():
+        raise ValueError("scatter_qkv_paged expects a contiguous bf16 merged QKV shard")
+    tokens = int(merged.shape[0])
+    world = q.world
+    if num_heads % world:
+        raise ValueError(f"num_heads={num_heads} must be divisible by Ulysses world size {world}")
+    if merged.numel() != tokens * 3 * num_heads * head_dim:
+        raise ValueError("merged QKV shard must hold 3 * num_heads * head_dim values per token")
+    hl = num_heads // world
+    if q.shape != (world * tokens, hl, head_dim):
+        raise ValueError(f"peer Q plane must be [{world * tokens}, {hl}, {head_dim}], "
+                         f"got {list(q.shape)}")
+    if key_pool.shape != value_pool.shape or key_pool.shape[0] != hl or key_pool.shape[2] != head_dim \
+            or key_pool.shape[1] % PAGE_ROWS:
+        raise ValueError(f"peer KV pools must both be [{hl}, pages * {PAGE_ROWS}, {head_dim}]")
+    if page_table.dtype != torch.int32:
+        raise ValueError("page_table must be int32")
+    call("h3sa_scatter_qkv_paged", ptr(merged), tokens, num_heads, head_dim, world, q.rank,
+         ptr(q.peer_table), ptr(key_pool.peer_table), ptr(value_pool.peer_table),
+         key_pool.shape[1] // PAGE_ROWS, ptr(page_table), int(page_table.numel()), int(dst_start),
+         ptr(device_error), stream_handle(stream))
+
+
 def attention_fwd_scatter(
     query: torch.Tensor,
     key_pool: torch.Tensor,
@@ -175,4 +210,5 @@ def attention_fwd_scatter(
          out.rank * heads, ptr(device_error), stream_handle(stream))
 
 
-__all__ = ["PeerBarrier", "PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv"]
+__all__ = ["PeerBarrier", "PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv",
+           "scatter_qkv_paged"]

@@ -4,7 +4,9 @@ Two ranks, one process per GPU (NCCL). Each rank holds a seeded post-prologue QK
 the NCCL path (pack, all_to_all_single, unpack / attention / all_to_all_single, unpack) and
 the fused path (scatter_qkv into peer q/k/v planes / attention storing into peer output
 shards) must give bit-identical q/k/v planes and final outputs: both run the same kernels and
-differ only in where the bytes go. Skipped with fewer than two GPUs.
+differ only in where the bytes go. scatter_qkv_paged, which writes K/V straight into the
+owners' paged caches, must leave the same caches as the all-to-all plus kv_copy_rows. Skipped
+with fewer than two GPUs.
 """
 
 from __future__ import annotations
@@ -94,10 +96,33 @@ def _worker(rank: int, world: int, rendezvous: str) -> None:
             torch.cuda.synchronize()
             assert int(err.item()) == 0
             assert torch.equal(out_peer.tensor, final_ref), "final sequence shards differ"
+        # Q to the owners' planes and K/V straight into the owners' paged caches
+        from h3sa.peer import scatter_qkv_paged
+
+        kp_ref, vp_ref = pools()
+        h3sa.kv_copy_rows([qkv_ref[1], qkv_ref[2]], [kp_ref, vp_ref], count=rows, dst_table=table,
+                          dst_start=hist)
+        q_peer = PeerBuffer((rows, hl, d))
+        k_peer = PeerBuffer((hl, pages * PAGE_ROWS, d))
+        v_peer = PeerBuffer((hl, pages * PAGE_ROWS, d))
+        for it in range(2):
+            q_peer.tensor.zero_()
+            kp3, vp3 = pools()
+            k_peer.tensor.copy_(kp3)
+            v_peer.tensor.copy_(vp3)
+            peer_barrier()
+            scatter_qkv_paged(merged, q_peer, k_peer, v_peer, table, dst_start=hist,
+                              num_heads=heads, head_dim=d, device_error=err)
+            peer_barrier()
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            assert torch.equal(q_peer.tensor, qkv_ref[0]), "q plane differs"
+            assert torch.equal(k_peer.tensor, kp_ref), "key cache differs"
+            assert torch.equal(v_peer.tensor, vp_ref), "value cache differs"
         barrier()
         torch.cuda.synchronize()
-        qkv_peer.close()
-        out_peer.close()
+        for buf in (qkv_peer, out_peer, q_peer, k_peer, v_peer):
+            buf.close()
         peer_barrier.close()
     finally:
         torch.distributed.barrier()
