@@ -418,39 +418,51 @@ def _time_launch(fn, iters: int) -> float:
     return a.elapsed_time(b) / iters
 
 
-def _variants(peaks: dict, iters: int = 10) -> dict:
-    """Kernel-only timings of the path's FP8 and block-sparse variants on this GPU.
+VARIANTS = ("fp8", "sparse", "480p")
 
-    * FP8: the 1080p per-GPU problem of the TP2 x SP4 configuration (24 heads / TP 2 / SP 4 =
+
+def _variants(peaks: dict, iters: int = 10, only: str | None = None) -> dict:
+    """Kernel-only timings of the path's other variants on this GPU (all, or `only` one).
+
+    * fp8: the 1080p per-GPU problem of the TP2 x SP4 configuration (24 heads / TP 2 / SP 4 =
       3 heads; 24480 video + 125 audio queries over a 32768-row cache plus the chunk), e4m3
       Q/K/V with per-head scales, inputs N(0,1) with 1% outliers x8 (seeded).
-    * Block-sparse: the 768p per-GPU problem at SP=8 (3 heads; 12509 queries over 16384 + 12509
+    * sparse: the 768p per-GPU problem at SP=8 (3 heads; 12509 queries over 16384 + 12509
       keys) with the composite 128x128 block mask (audio blocks, 2 sinks, +-4-block band, top-k
       fill to 25% of blocks).
-    * Dense bf16 at 480p on one GPU (24 heads; 4985 queries over 19940 + 4985 keys).
-    FLOPs count only the work the kernel must do (kept blocks for the sparse case).
+    * 480p: dense bf16 on one GPU (24 heads; 4985 queries over 19940 + 4985 keys).
+    FLOPs count only the work the kernel must do (kept blocks for the sparse case). Each
+    variant times `iters` launches after two warm-up launches.
     """
 
-    import types
-
     import h3sa
-    from h3sa.block_sparse import composite_block_mask
     from h3sa.kernels import PAGE_ROWS
 
     dev = torch.device("cuda")
-    d = CFG["head_dim"]
-    out = {}
     g = torch.Generator(device=dev).manual_seed(7)
 
     def pools(rows: int, heads: int, k: torch.Tensor, v: torch.Tensor):
         pages = (rows + PAGE_ROWS - 1) // PAGE_ROWS
         table = torch.arange(pages, dtype=torch.int32, device=dev)
-        kp = torch.zeros(heads, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=dev)
+        kp = torch.zeros(heads, pages * PAGE_ROWS, CFG["head_dim"], dtype=torch.bfloat16,
+                         device=dev)
         vp = torch.zeros_like(kp)
         h3sa.kv_copy_rows([k, v], [kp, vp], count=rows, dst_table=table)
         return kp, vp, table
 
-    # ---- FP8 e4m3, 1080p per GPU
+    out = {}
+    for name, fn in (("fp8", _variant_fp8), ("sparse", _variant_sparse), ("480p", _variant_480p)):
+        if only in (None, name):
+            out.update(fn(peaks, iters, dev, g, pools))
+            torch.cuda.empty_cache()
+    return out
+
+
+def _variant_fp8(peaks: dict, iters: int, dev: torch.device, g: torch.Generator, pools) -> dict:
+    import h3sa
+
+    d = CFG["head_dim"]
+    out = {}
     heads, nq, nh = 3, 24480 + 125, 32768
     nk = nh + nq
 
@@ -480,9 +492,19 @@ def _variants(peaks: dict, iters: int = 10) -> dict:
         "roofline": {"bound": "tensor", "peak": fp8_peak, "frac": tf / fp8_peak,
                      "peak_source": "2 x measured bf16 burst (no measured e4m3 GEMM peak; "
                                     "nominal dense e4m3 is 4500)"}}
-    del q, k, v, kp, vp, k8, v8, q8, o
+    return out
 
-    # ---- block-sparse bf16, 768p SP=8 per GPU
+
+def _variant_sparse(peaks: dict, iters: int, dev: torch.device, g: torch.Generator,
+                    pools) -> dict:
+    import types
+
+    import h3sa
+    from h3sa.block_sparse import composite_block_mask
+    from h3sa.kernels import PAGE_ROWS
+
+    d = CFG["head_dim"]
+    out = {}
     heads, nq, nh = 3, CFG["video"] + CFG["audio"], CFG["history"]
     nk = nh + nq
     q = torch.randn(nq, heads, d, device=dev, generator=g).to(torch.bfloat16)
@@ -510,10 +532,14 @@ def _variants(peaks: dict, iters: int = 10) -> dict:
         "ms": ms, "tflops_on_kept_blocks": tf, "kept_block_fraction": density, "heads": heads,
         "queries": nq, "keys": nk,
         "roofline": {"bound": "tensor", "peak": peaks["bf16"], "frac": tf / peaks["bf16"]}}
-    del q, k, v, kp, vp, o
+    return out
 
-    # ---- dense bf16, 480p chunk on one GPU (24 heads; 4860 video + 125 audio queries over
-    # 4 prior chunks = 19940 cached rows plus the chunk)
+
+def _variant_480p(peaks: dict, iters: int, dev: torch.device, g: torch.Generator, pools) -> dict:
+    import h3sa
+
+    d = CFG["head_dim"]
+    out = {}
     heads, nq, nh = 24, 4860 + 125, 19940
     nk = nh + nq
     q = torch.randn(nq, heads, d, device=dev, generator=g).to(torch.bfloat16)
@@ -747,8 +773,15 @@ def main() -> None:
     ap.add_argument("--unfused", action="store_true",
                     help="SP > 1: NCCL all-to-all + layout copies instead of peer stores")
     ap.add_argument("--no-variants", action="store_true",
-                    help="skip the kernel-only FP8 1080p and block-sparse 768p timings")
+                    help="skip the kernel-only FP8 1080p, block-sparse 768p and 480p timings")
+    ap.add_argument("--variant", choices=VARIANTS,
+                    help="time only this kernel-only variant on one GPU and print its JSON "
+                         "(2 warm-up launches, then --steps launches)")
     args = ap.parse_args()
+    if args.variant:
+        torch.cuda.set_device(0)
+        print(json.dumps(_variants(_peaks(), iters=args.steps, only=args.variant)), flush=True)
+        return
     if args.warmup < 3 and args.impl == "h3sa":
         args.warmup = 3
     if args.impl == "reference":
