@@ -41,9 +41,6 @@ __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
 __device__ __forceinline__ void fence_mbar_init() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
-__device__ __forceinline__ void fence_async_smem() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
 __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
@@ -136,15 +133,6 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
       "@e tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
-// D(tmem) (+)= A(tmem) * B(smem desc)
-__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                       uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred e, p;\n\t" H3SA_ELECT_PRED
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
 __device__ __forceinline__ void mma_ss_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -152,14 +140,6 @@ __device__ __forceinline__ void mma_ss_f8(uint32_t d_tmem, uint64_t a_desc, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void mma_ts_f8(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
-                                          uint32_t idesc, uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred e, p;\n\t" H3SA_ELECT_PRED
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
 __device__ __forceinline__ void tmem_wait_ld() {
@@ -191,34 +171,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       H3SA_W8(0), H3SA_W8(8), H3SA_W8(16), H3SA_W8(24)
       : "memory");
 }
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
-      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
-      H3SA_W8(0), H3SA_W8(8)
-      : "memory");
-}
 #undef H3SA_R8
 #undef H3SA_W8
 
-// ---------------------------------------------------------------- descriptors
-// Shared-memory matrix descriptor for a tile written by TMA with 128-byte swizzling:
-// rows of 128 bytes, groups of 8 rows 1024 bytes apart (stride byte offset), the
-// leading byte offset used only by MN-major operands that span two 128-byte atoms.
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes,
-                                                uint32_t sbo_bytes) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
-  d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
-  d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
-  d |= static_cast<uint64_t>(1) << 46;  // descriptor version for sm_100
-  d |= static_cast<uint64_t>(2) << 61;  // 128-byte swizzle
-  return d;
-}
 
-// The same descriptor split in halves: the upper word is fixed for 128-byte swizzling with a
-// 1024-byte stride byte offset, the lower word holds start address and leading byte offset, so
-// descriptors of neighbouring tiles differ by a 32-bit add (addresses stay below 2^18).
+// ---------------------------------------------------------------- descriptors
+// Shared-memory matrix descriptor of a tile written by TMA with 128-byte swizzling: rows of
+// 128 bytes, groups of 8 rows 1024 bytes apart (stride byte offset), and a leading byte offset
+// used only by MN-major operands that span two 128-byte atoms. Bits 0-13: start address >> 4;
+// 16-29: leading byte offset >> 4; 32-45: stride byte offset >> 4; 46: descriptor version for
+// sm_100; 61-63: swizzle mode (2 = 128 bytes). It is kept in two 32-bit halves: the upper one
+// is fixed, the lower one holds start address and leading byte offset, so descriptors of
+// neighbouring tiles differ by a 32-bit add (addresses stay below 2^18).
 constexpr uint32_t kSdescHiSw128 = (1024u >> 4) | (1u << 14) | (2u << 29);
 __device__ __forceinline__ uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo_bytes) {
   return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
