@@ -466,3 +466,130 @@ def test_block_sparse_split_kv_segments(fp8: bool) -> None:
     keep_rows[empty] = False
     ref = ref_attention(qr, kr, vr, scale, allowed.cuda())
     assert rel_l2(out[keep_rows], ref[keep_rows.cuda()]) <= tol
+
+
+# ---- full BASELINE sizes, checked on sampled query rows against an fp32 reference
+
+def _sample_rows(nq: int, count: int, seed: int) -> torch.Tensor:
+    """Sorted random query rows, always including the first and last (partial tile) rows."""
+
+    g = torch.Generator().manual_seed(seed)
+    rows = torch.randperm(nq, generator=g)[:count]
+    rows = torch.cat((rows, torch.tensor([0, nq - 1])))
+    return torch.unique(rows).cuda()
+
+
+def _full_case(heads: int, nq: int, nh: int, seed: int, outliers: bool = False):
+    h3sa = _h3sa()
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    nk = nh + nq
+
+    def draw(rows: int) -> torch.Tensor:
+        x = torch.randn(rows, heads, 128, device="cuda", generator=gen)
+        if outliers:
+            x = torch.where(torch.rand(x.shape, device="cuda", generator=gen) < 0.01, x * 8, x)
+        return x.to(torch.bfloat16)
+
+    q, k, v = draw(nq), draw(nk), draw(nk)
+    pages = (nk + 127) // 128
+    table = torch.randperm(pages, device="cuda", generator=gen).to(torch.int32)
+    kp = torch.zeros(heads, pages * 128, 128, dtype=torch.bfloat16, device="cuda")
+    vp = torch.zeros_like(kp)
+    h3sa.kv_copy_rows([k, v], [kp, vp], count=nk, dst_table=table)
+    return q, k, v, kp, vp, table
+
+
+def test_full_768p_dense_sampled_rows() -> None:
+    """The 768p chunk at SP=1 (H=24, 12509 queries x [16384 history + 12509 current] keys,
+    shuffled pages): 512 sampled query rows of every head against fp32 attention."""
+
+    h3sa = _h3sa()
+    heads, nq, nh = 24, 12384 + 125, 16384
+    q, k, v, kp, vp, table = _full_case(heads, nq, nh, seed=768)
+    out = torch.full_like(q, float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    h3sa.attention_fwd(q, out, kp, vp, table, [h3sa.AttentionProblem(0, nq, 0, nh + nq)], scale,
+                       device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    rows = _sample_rows(nq, 512, seed=1)
+    ref = ref_attention(q[rows], k, v, scale)
+    assert rel_l2(out[rows], ref) <= BF16_TOL
+    assert not torch.isnan(out).any()
+
+
+def test_full_1080p_fp8_sampled_rows() -> None:
+    """The 1080p per-GPU problem of TP2 x SP4 (3 heads, 24605 queries x [32768 + 24605] keys,
+    1 % of the inputs x8), e4m3 with per-head scales: 512 sampled query rows against fp32
+    attention on the dequantised inputs."""
+
+    h3sa = _h3sa()
+    heads, nq, nh = 3, 24480 + 125, 32768
+    nk = nh + nq
+    q, k, v, kp, vp, table = _full_case(heads, nq, nh, seed=1080, outliers=True)
+    q8, qs = h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0))
+    k8 = torch.zeros_like(kp, dtype=torch.float8_e4m3fn)
+    v8 = torch.zeros_like(vp, dtype=torch.float8_e4m3fn)
+    ks = torch.empty(heads, dtype=torch.float32, device="cuda")
+    vs = torch.empty(heads, dtype=torch.float32, device="cuda")
+    h3sa.quantize_fp8_pool(kp, k8, ks, table, nk)
+    h3sa.quantize_fp8_pool(vp, v8, vs, table, nk)
+    out = torch.full_like(q, float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    h3sa.attention_fwd(q8.squeeze(0), out, k8, v8, table, [h3sa.AttentionProblem(0, nq, 0, nk)],
+                       scale, q_scale=qs.reshape(-1).contiguous(), k_scale=ks, v_scale=vs,
+                       device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert not torch.isnan(out).any()
+    k8r, kss = h3sa.quantize_fp8_e4m3_per_head(k.unsqueeze(0))
+    v8r, vss = h3sa.quantize_fp8_e4m3_per_head(v.unsqueeze(0))
+    assert torch.equal(kss.reshape(-1), ks) and torch.equal(vss.reshape(-1), vs)
+    deq = lambda x8, sc: x8.squeeze(0).float() * sc.reshape(1, -1, 1)  # noqa: E731
+    rows = _sample_rows(nq, 512, seed=2)
+    ref = ref_attention(deq(q8, qs)[rows], deq(k8r, kss), deq(v8r, vss), scale)
+    assert rel_l2(out[rows], ref) <= FP8_TOL
+
+
+def test_full_768p_sparse_sampled_rows() -> None:
+    """The 768p per-GPU problem at SP=8 (3 heads) with the composite block mask built on the
+    GPU (audio blocks, 2 sinks, +-4-block band, top-k fill to 25 %), run through split-KV:
+    512 sampled query rows against fp32 attention restricted to each row's kept blocks."""
+
+    import types
+
+    from h3sa.block_sparse import composite_block_mask
+
+    h3sa = _h3sa()
+    heads, video, audio, nh = 3, 12384, 125, 16384
+    nq = video + audio
+    nk = nh + nq
+    q, k, v, kp, vp, table = _full_case(heads, nq, nh, seed=88)
+    qb, kb = (nq + 127) // 128, (nk + 127) // 128
+    q_audio = torch.zeros(qb, dtype=torch.uint8, device="cuda")
+    q_audio[video // 128:] = 1
+    kv_audio = torch.zeros(kb, dtype=torch.uint8, device="cuda")
+    kv_audio[(nh + video) // 128:] = 1
+    kv_audio[torch.arange(31, nh // 128, 32, device="cuda")] = 1
+    num, idx = composite_block_mask(q, types.SimpleNamespace(key=kp, table=table), q_lo=0,
+                                    q_hi=nq, n_hist=nh, n_kv=nk, q_block_audio=q_audio,
+                                    kv_block_audio=kv_audio, density=0.25)
+    out = torch.full_like(q, float("nan"))
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    scale = 128 ** -0.5
+    h3sa.attention_fwd(q, out, kp, vp, table, [h3sa.AttentionProblem(0, nq, 0, nk, sparse=True)],
+                       scale, kv_num_blocks=num, kv_indices=idx, device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert not torch.isnan(out).any()
+    rows = _sample_rows(nq, 512, seed=3)
+    allowed = torch.zeros(heads, rows.numel(), kb, dtype=torch.bool, device="cuda")
+    qblk = rows // 128
+    for h in range(heads):
+        for i, j in enumerate(qblk.tolist()):
+            allowed[h, i, idx[h, j, : int(num[h, j])].long()] = True
+    allowed = allowed.repeat_interleave(128, dim=2)[:, :, :nk]
+    ref = ref_attention(q[rows], k, v, scale, allowed)
+    assert rel_l2(out[rows], ref) <= BF16_TOL
