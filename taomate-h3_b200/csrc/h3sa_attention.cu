@@ -203,12 +203,13 @@ __device__ __forceinline__ void walk_skip(BlockWalk& s, bool sparse, int k,
 // them with 8 lanes per row, so one warp store instruction writes four whole 128-byte lines
 // instead of 32 scattered 16-byte pieces (this matters most for rows bound for a peer GPU over
 // NVLink). `dst` is this thread's row address (0: no row); `row_values(ch, v)` yields the 32
-// scaled fp32 values of column chunk ch (0..3) of this thread's row.
-template <typename RowValues>
+// scaled fp32 values of column chunk ch (0..3) of this thread's row. Halves [kHalfBegin,
+// kHalfEnd) of the row are stored (a warp that owns half of each row stores one half).
+template <int kHalfBegin = 0, int kHalfEnd = 2, typename RowValues>
 __device__ __forceinline__ void store_tile_rows(uint8_t* stage, int lane, unsigned long long dst,
                                                 RowValues&& row_values) {
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
+  for (int half = kHalfBegin; half < kHalfEnd; ++half) {
 #pragma unroll
     for (int hc = 0; hc < 2; ++hc) {
       float v[32];
@@ -796,6 +797,610 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   }
 }
 
+// ============================================================================ one-tile kernel
+// One 128-row query tile per CTA with S double-buffered in TMEM (S0 [0,128), S1 [128,256),
+// O [256,384)). P goes back into TMEM over the upper half of the S buffer it came from and is
+// read by a TMEM x smem MMA. The MMA warp issues PV(i) and then QK(i + 2) into the buffer PV(i)
+// has just read (one thread's tcgen05.mma execute in issue order), so the scores of block
+// i + 1 are ready while the softmax works on block i: no QK waits for a softmax. Eight softmax
+// warps: warps 4-7 and 8-11 cover the same 32-row quarters (TMEM lanes 32 * (warp % 4)), the
+// first four the left 64 columns of each row and the last four the right 64; the two halves of
+// a row exchange their maxima through shared memory once per block.
+// One-tile kernel: the two column halves of a row run independent online softmaxes with an
+// O accumulator each (O0 [256,384), O1 [384,512)), merged at the end (1), or share each
+// block's row maximum through shared memory (0). Measured on the 768p SP=8 block-sparse mask:
+// 0.236 ms independent, 0.253 ms shared.
+#ifndef H3SA_ONE_TILE_INDEP
+#define H3SA_ONE_TILE_INDEP 1
+#endif
+
+template <bool kFp8>
+struct Attn1Cfg {
+  static constexpr int kKStages = kFp8 ? 3 : 2;
+  static constexpr int kVStages = kFp8 ? 3 : 2;
+};
+
+template <bool kFp8>
+struct alignas(1024) Attn1Smem {
+  using Cfg = AttnCfg<kFp8>;
+  using Cfg1 = Attn1Cfg<kFp8>;
+  uint8_t q[Cfg::kTileBytes];
+  uint8_t k[Cfg1::kKStages][Cfg::kTileBytes];  // also the epilogue's staging (4 KB per warp)
+  uint8_t v[Cfg1::kVStages][Cfg::kTileBytes];
+  uint64_t q_full;
+  uint64_t k_full[Cfg1::kKStages], k_empty[Cfg1::kKStages];
+  uint64_t v_full[Cfg1::kVStages], v_empty[Cfg1::kVStages];
+  uint64_t s_full[2], pv_done[2], o_done;  // pv_done: per half (kIndep)
+  // P written, per column half (kIndep; otherwise [0] counts both) and block parity: with
+  // independent halves one half can run a block ahead, and one barrier per half would then
+  // complete twice before the MMA warp waits on it
+  uint64_t p_full[2][2];
+  uint64_t half_x[4];  // per row quarter: both column halves posted their value
+  uint64_t drain;
+  float mx_x[2][2][kBlockM];  // [block parity][column half][row]: half-row maxima
+  float l_x[2][kBlockM];      // [column half][row]: half-row sums at the end
+  uint32_t tmem_base;
+  int abort_flag;
+  int n_blocks;
+  int split_last;
+  uint32_t kv_mask[2][kMaskWords];  // block-sparse: the tile's list (second row unused)
+};
+
+template <bool kFp8>
+constexpr size_t attn1_smem_bytes() {
+  return sizeof(Attn1Smem<kFp8>) + 1024;
+}
+static_assert(attn1_smem_bytes<false>() <= 232448, "bf16 one-tile attention exceeds 227 KB");
+static_assert(attn1_smem_bytes<true>() <= 232448, "e4m3 one-tile attention exceeds 227 KB");
+static_assert(AttnCfg<false>::kTileBytes * Attn1Cfg<false>::kKStages >= 8 * 32 * 128 &&
+                  AttnCfg<true>::kTileBytes * Attn1Cfg<true>::kKStages >= 8 * 32 * 128,
+              "the K ring must hold the epilogue staging of eight warps");
+
+template <bool kFp8, bool kIndep>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn1_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
+  using Cfg = AttnCfg<kFp8>;
+  using Cfg1 = Attn1Cfg<kFp8>;
+  constexpr int kKS = Cfg1::kKStages;
+  constexpr int kVS = Cfg1::kVStages;
+  extern __shared__ uint8_t smem_raw[];
+  Attn1Smem<kFp8>& sm = *reinterpret_cast<Attn1Smem<kFp8>*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort_flag = &sm.abort_flag;
+
+  // ---- locate this CTA's work: problem, head, query tile, split-KV segment
+  int pi = 0;
+  while (pi + 1 < p.n_prob && static_cast<int>(blockIdx.x) >= p.prob[pi + 1].cta_begin) ++pi;
+  const AttnProblemDev pr = p.prob[pi];
+  const int local = static_cast<int>(blockIdx.x) - pr.cta_begin;
+  const int seg = local % pr.split;
+  const int unit = local / pr.split;  // `pairs` counts query tiles for this kernel
+  const int head = unit / pr.pairs;
+  const int tile = unit - head * pr.pairs;
+  const int q_row0 = pr.q_lo + tile * kBlockM;
+  const int b_lo = pr.kv_lo / kBlockN;
+  const int b_hi = (pr.kv_hi + kBlockN - 1) / kBlockN;
+
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&sm.q_full), 1);
+    for (int s = 0; s < kKS; ++s) {
+      mbar_init(smem_u32(&sm.k_full[s]), 1);
+      mbar_init(smem_u32(&sm.k_empty[s]), 1);
+    }
+    for (int s = 0; s < kVS; ++s) {
+      mbar_init(smem_u32(&sm.v_full[s]), 1);
+      mbar_init(smem_u32(&sm.v_empty[s]), 1);
+    }
+    mbar_init(smem_u32(&sm.s_full[0]), 1);
+    mbar_init(smem_u32(&sm.s_full[1]), 1);
+    for (int hh = 0; hh < 2; ++hh)
+      for (int par = 0; par < 2; ++par)  // every softmax thread (of the half with kIndep)
+        mbar_init(smem_u32(&sm.p_full[hh][par]), (kIndep || hh == 1) ? 128 : 256);
+    mbar_init(smem_u32(&sm.pv_done[0]), 1);
+    mbar_init(smem_u32(&sm.pv_done[1]), 1);
+    mbar_init(smem_u32(&sm.o_done), 1);
+    for (int q = 0; q < 4; ++q) mbar_init(smem_u32(&sm.half_x[q]), 2);  // one per half warp
+    mbar_init(smem_u32(&sm.drain), 1);
+    sm.abort_flag = 0;
+    sm.n_blocks = b_hi - b_lo;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (pr.sparse && warp == 2) {
+    const int* nums = p.kv_num_blocks + static_cast<size_t>(head) * p.q_blocks;
+    const int* A = p.kv_indices + (static_cast<size_t>(head) * p.q_blocks + tile) * p.kv_stride;
+    const int na = min(__ldg(nums + tile), p.kv_stride);
+    build_masks(A, na, A, 0, b_lo, b_hi, sm.kv_mask, &sm.n_blocks, p.err, abort_flag);
+  }
+  __syncthreads();
+
+  // split-KV segments, as in attn_fwd_kernel
+  const int n_all = sm.n_blocks;
+  const int nseg = pr.split > 1 ? max(1, min(pr.split, (n_all + kSplitSegBlocks - 1) / kSplitSegBlocks))
+                                : 1;
+  if (seg >= nseg) return;
+  const int seg_len = (n_all + nseg - 1) / nseg;
+  const int seg_lo = min(n_all, seg * seg_len);
+  const int nblk = min(n_all, seg_lo + seg_len) - seg_lo;
+  const bool split_out = nseg > 1;
+  const int gseg = (pr.pair_begin + head * pr.pairs + tile) * pr.split;
+
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+
+  const uint32_t tbase = sm.tmem_base;
+  BlockWalk walk;
+  walk_skip(walk, pr.sparse != 0, seg_lo, sm.kv_mask);
+  auto next_block = [&](int& b) {
+    int m;
+    walk_next(walk, pr.sparse != 0, b_lo, 1, sm.kv_mask, b, m);
+  };
+  auto row_dst = [&](int row) -> unsigned long long {
+    const int qrow = q_row0 + row;
+    if (qrow >= pr.q_hi) return 0ull;
+    if (p.out_peers) {
+      const int owner = min(qrow / p.out_rows_per_rank, p.out_ranks - 1);
+      const int orow = qrow - owner * p.out_rows_per_rank;
+      return p.out_peers[owner] +
+             (static_cast<size_t>(orow) * p.out_heads + p.out_head0 + head) * kHeadDim * 2;
+    }
+    return reinterpret_cast<uintptr_t>(p.out) +
+           (static_cast<size_t>(qrow) * p.heads + head) * kHeadDim * 2;
+  };
+
+  if (warp == 0 || warp == 3) {
+    // ================================================================ TMA producers
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+    const bool is_k = (warp == 0);
+    if (lane == 0 && !*abort_flag) {
+      const CUtensorMap* map = is_k ? &tmK : &tmV;
+      tma_prefetch_desc(map);
+      if (is_k) {
+        tma_prefetch_desc(&tmQ);
+        const uint32_t qbar = smem_u32(&sm.q_full);
+        mbar_expect_tx(qbar, Cfg::kTileBytes);
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_3d(smem_u32(sm.q) + a * Cfg::kAtomBytes, &tmQ, qbar, a * (128 / Cfg::kElem),
+                      head, q_row0);
+      }
+      for (int i = 0; i < nblk; ++i) {
+        const int s = is_k ? i % kKS : i % kVS;
+        const uint32_t ph = (is_k ? i / kKS : i / kVS) & 1;
+        int b;
+        next_block(b);
+        int page = (b >= 0 && b < p.table_blocks) ? __ldg(p.page_table + b) : -1;
+        if (page < 0 || page >= p.pool_pages) {
+          if (p.err) atomicOr(p.err, kErrBadPage);
+          *abort_flag = 1;
+          break;
+        }
+        uint64_t* empty = is_k ? &sm.k_empty[s] : &sm.v_empty[s];
+        if (!mbar_wait(smem_u32(empty), ph ^ 1, abort_flag, p.err)) break;
+        const uint32_t fb = smem_u32(is_k ? &sm.k_full[s] : &sm.v_full[s]);
+        mbar_expect_tx(fb, Cfg::kTileBytes);
+        const uint32_t dst = smem_u32(is_k ? sm.k[s] : sm.v[s]);
+        for (int a = 0; a < Cfg::kAtoms; ++a)
+          tma_load_3d(dst + a * Cfg::kAtomBytes, map, fb, a * (128 / Cfg::kElem), page * kBlockN,
+                      head);
+      }
+    }
+  } else if (warp == 1) {
+    // ================================================================ MMA issuer
+    // QK(0), QK(1), then per block i: PV(i) once P(i) is in TMEM, and QK(i + 2) into the S
+    // buffer PV(i) has just read.
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+    const uint32_t tO = tbase + 256u;
+    const uint32_t qlo = sdesc_lo(smem_u32(sm.q), 16);
+    const uint32_t klo0 = sdesc_lo(smem_u32(sm.k[0]), 16);
+    const uint32_t vlo0 = sdesc_lo(smem_u32(sm.v[0]), Cfg::kAtomBytes);
+    constexpr uint32_t kTileDesc = Cfg::kTileBytes >> 4;
+    bool ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sm.q_full), 0, abort_flag, p.err));
+    tc_fence_after();
+    auto issue_qk = [&](int i) -> bool {
+      const int sk = i % kKS;
+      const bool w = mbar_wait(smem_u32(&sm.k_full[sk]), (i / kKS) & 1, abort_flag, p.err);
+      if (!__all_sync(0xffffffffu, w)) return false;
+      tc_fence_after();
+      const uint32_t tS = tbase + static_cast<uint32_t>(i & 1) * 128u;
+      const uint32_t klo = klo0 + static_cast<uint32_t>(sk) * kTileDesc;
+#pragma unroll
+      for (int kk = 0; kk < Cfg::kKSteps; ++kk) {
+        const uint32_t off = ((kk * Cfg::kKStepBytes / 128) * Cfg::kAtomBytes +
+                              (kk * Cfg::kKStepBytes) % 128) >> 4;
+        if constexpr (kFp8)
+          mma_ss_f8(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
+                    kk > 0 ? 1u : 0u);
+        else
+          mma_ss(tS, sdesc_join(qlo + off), sdesc_join(klo + off), Cfg::kIdescQK,
+                 kk > 0 ? 1u : 0u);
+      }
+      tc_commit(smem_u32(&sm.s_full[i & 1]));
+      tc_commit(smem_u32(&sm.k_empty[sk]));
+      return true;
+    };
+    if (ok && nblk > 0) ok = issue_qk(0);
+    if (ok && nblk > 1) ok = issue_qk(1);
+    for (int i = 0; ok && i < nblk; ++i) {
+      int b;
+      next_block(b);
+      const int sv = i % kVS;
+      bool w = mbar_wait(smem_u32(&sm.v_full[sv]), (i / kVS) & 1, abort_flag, p.err);
+      if (w) w = mbar_wait(smem_u32(&sm.p_full[0][i & 1]), (i >> 1) & 1, abort_flag, p.err);
+      if (!(ok = __all_sync(0xffffffffu, w))) break;
+      tc_fence_after();
+      {
+        // V rows of a partial block outside the problem's KV range are zeroed first (they
+        // may hold never-written bytes; P is zero there but 0 x NaN is not)
+        const int col0 = b * kBlockN;
+        const int vlo_row = max(pr.kv_lo - col0, 0);
+        const int vhi_row = min(pr.kv_hi - col0, kBlockN);
+        if (vlo_row > 0 || vhi_row < kBlockN) {
+          uint8_t* vbase = sm.v[sv];
+          const int nbad = vlo_row + (kBlockN - vhi_row);
+          for (int idx = lane; idx < nbad * Cfg::kAtoms * 8; idx += 32) {
+            const int chunk = idx & 7;
+            const int rest = idx >> 3;
+            const int a = rest % Cfg::kAtoms;
+            const int k = rest / Cfg::kAtoms;
+            const int r = k < vlo_row ? k : vhi_row + (k - vlo_row);
+            reinterpret_cast<uint4*>(vbase + a * Cfg::kAtomBytes + r * 128)[chunk] =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+        }
+      }
+      const uint32_t vlo = vlo0 + static_cast<uint32_t>(sv) * kTileDesc;
+      const uint32_t tSb = tbase + static_cast<uint32_t>(i & 1) * 128u;
+      if constexpr (kIndep) {
+        // each half's P (its 64 KV rows) into its own O: P_h over S columns [64h, 64h + 64)
+        constexpr int kSteps = 64 / Cfg::kPvRowsPerStep;
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          if (hh == 1) {
+            const bool w1 =
+                mbar_wait(smem_u32(&sm.p_full[1][i & 1]), (i >> 1) & 1, abort_flag, p.err);
+            if (!(ok = __all_sync(0xffffffffu, w1))) break;
+            tc_fence_after();
+          }
+#pragma unroll
+          for (int kk = 0; kk < kSteps; ++kk) {
+            const uint64_t bdesc =
+                sdesc_join(vlo + (((64 * hh + kk * Cfg::kPvRowsPerStep) * 128) >> 4));
+            const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t a_tmem = tSb + 64u * hh + kk * 8u;
+            if constexpr (kFp8)
+              mma_ts_f8(tO + 128u * hh, a_tmem, bdesc, Cfg::kIdescPV, acc);
+            else
+              mma_ts(tO + 128u * hh, a_tmem, bdesc, Cfg::kIdescPV, acc);
+          }
+          tc_commit(smem_u32(&sm.pv_done[hh]));
+        }
+        if (!ok) break;
+      } else {
+        const uint32_t tP = tSb + 64u;
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / Cfg::kPvRowsPerStep; ++kk) {
+          const uint64_t bdesc = sdesc_join(vlo + ((kk * Cfg::kPvRowsPerStep * 128) >> 4));
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          if constexpr (kFp8)
+            mma_ts_f8(tO, tP + kk * 8u, bdesc, Cfg::kIdescPV, acc);
+          else
+            mma_ts(tO, tP + kk * 8u, bdesc, Cfg::kIdescPV, acc);
+        }
+        tc_commit(smem_u32(&sm.pv_done[0]));
+      }
+      tc_commit(smem_u32(&sm.v_empty[sv]));
+      if (i + 2 < nblk) ok = issue_qk(i + 2);
+    }
+    if (ok) tc_commit(smem_u32(&sm.o_done));
+    tc_commit(smem_u32(&sm.drain));
+    const unsigned long long t0 = global_ns();
+    while (!mbar_try_wait(smem_u32(&sm.drain), 0)) {
+      if (global_ns() - t0 > kWaitTimeoutNs) {
+        if (p.err && lane == 0) atomicOr(p.err, kErrWaitTimeout);
+        break;
+      }
+    }
+  } else if (warp == 2) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+  } else {
+    // ================================================================ softmax / epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+    const int q = warp & 3;          // row quarter = TMEM lane quarter
+    const int h = (warp - 4) >> 2;   // column half of each row
+    const int row = q * 32 + lane;
+    const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+    // this half's O accumulator (kIndep), or the shared one
+    const uint32_t tO = tbase + 256u + (kIndep ? 128u * h : 0u) + lane_off;
+    const uint32_t xbar = smem_u32(&sm.half_x[q]);
+    float scale_log2;
+    if constexpr (kFp8)
+      scale_log2 = __ldg(p.q_scale + head) * __ldg(p.k_scale + head) * p.softmax_scale_log2;
+    else
+      scale_log2 = p.scale_log2;
+    constexpr float kRescaleThreshold = kFp8 ? H3SA_FP8_RESCALE_THRESHOLD : 8.0f;
+    constexpr float kBoost = kFp8 ? H3SA_FP8_BOOST : 0.0f;
+    float m_used = -INFINITY;
+    float l_sum = 0.f;
+    bool ok = true;
+    const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+    int i = 0;
+    for (; i < nblk; ++i) {
+      int b;
+      next_block(b);
+      if (!(ok = mbar_wait(smem_u32(&sm.s_full[i & 1]), (i >> 1) & 1, abort_flag, p.err))) break;
+      tc_fence_after();
+      const uint32_t tS = tbase + static_cast<uint32_t>(i & 1) * 128u + lane_off;
+      uint32_t r0[32], r1[32];
+      tmem_ld32(tS + 64u * h, r0);
+      tmem_ld32(tS + 64u * h + 32u, r1);
+      tmem_wait_ld();
+      reg_fence32(r0);
+      reg_fence32(r1);
+      float s[64];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        s[j] = __uint_as_float(r0[j]);
+        s[32 + j] = __uint_as_float(r1[j]);
+      }
+      const int col0 = b * kBlockN + 64 * h;
+      const int lo = pr.kv_lo - col0;  // valid columns [lo, hi) of this half
+      const int hi = pr.kv_hi - col0;
+      int partial_i = (lo > 0 || hi < 64) ? 1 : 0;
+      asm volatile("" : "+r"(partial_i));
+      if (partial_i) {
+#pragma unroll
+        for (int j = 0; j < 64; ++j)
+          if (j < lo || j >= hi) s[j] = -INFINITY;
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int j = 4; j < 64; j += 8) {
+        mx0 = fmax3(mx0, s[j], s[j + 4]);
+        mx1 = fmax3(mx1, s[j + 1], s[j + 5]);
+        mx2 = fmax3(mx2, s[j + 2], s[j + 6]);
+        mx3 = fmax3(mx3, s[j + 3], s[j + 7]);
+      }
+      const float mh = fmaxf(fmax3(mx0, mx1, mx2), mx3);
+      // both halves of the row: post this half's maximum, read the other's (the barrier also
+      // orders the other half's TMEM load of S before this half's P store over it)
+      float mx = mh;
+      if constexpr (!kIndep) {
+        sm.mx_x[i & 1][h][row] = mh;
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(xbar);
+        if (!(ok = mbar_wait(xbar, i & 1, abort_flag, p.err))) break;
+        tc_fence_after();
+        mx = fmaxf(mh, sm.mx_x[i & 1][h ^ 1][row]);
+      }
+      const float m_blk = mx * scale_log2;
+      const bool need = m_blk > m_used + kRescaleThreshold;
+      const float m_new = need ? m_blk : m_used;
+      const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
+      const bool any_need = i > 0 && __any_sync(0xffffffffu, need);
+      l_sum *= alpha;
+      m_used = m_new;
+      // a half that has seen no valid score yet (all its columns outside the KV range so far;
+      // possible with independent halves) keeps its P at zero instead of -inf + inf
+      const float bias = kBoost - (m_used == -INFINITY ? 0.f : m_used);
+      const uint64_t bias2 = f2_pack(bias, bias);
+#pragma unroll
+      for (int j = 0; j < 64; j += 2) {
+        float x0, x1;
+        f2_unpack(f2_fma(f2_pack(s[j], s[j + 1]), scale2, bias2), x0, x1);
+        s[j] = x0;
+        s[j + 1] = x1;
+      }
+      uint64_t sum2 = f2_pack(0.f, 0.f);
+      uint32_t pk[32];  // bf16: 32 words of pairs; e4m3: 16 words of quads
+#pragma unroll
+      for (int j = 0; j < 64; j += 2) {
+        const float p0 = fast_exp2(s[j]);
+        const float p1 = fast_exp2(s[j + 1]);
+        sum2 = f2_add(sum2, f2_pack(p0, p1));
+        if constexpr (kFp8) {
+          uint16_t qq;
+          asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(qq) : "f"(p1), "f"(p0));
+          if ((j & 2) == 0) pk[j / 4] = qq;
+          else pk[j / 4] |= static_cast<uint32_t>(qq) << 16;
+        } else {
+          pk[j / 2] = pack_bf16x2(p0, p1);
+        }
+      }
+      float sa, sb;
+      f2_unpack(sum2, sa, sb);
+      l_sum += sa + sb;
+      if (any_need) {
+        // PV(i - 1) has finished accumulating; rescale this half's O columns
+        if (!(ok = mbar_wait(smem_u32(&sm.pv_done[kIndep ? h : 0]), (i - 1) & 1, abort_flag,
+                             p.err)))
+          break;
+        tc_fence_after();
+        // this half's O (kIndep: all 128 columns of its own accumulator; otherwise its 64
+        // columns of the shared one)
+#pragma unroll
+        for (int ch = 0; ch < (kIndep ? 4 : 2); ++ch) {
+          const uint32_t addr = kIndep ? tO + ch * 32 : tO + 64u * h + ch * 32;
+          uint32_t o[32];
+          tmem_ld32(addr, o);
+          tmem_wait_ld();
+          reg_fence32(o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+          tmem_st32(addr, o);
+        }
+      }
+      // P over S: kIndep puts each half's P over its own S columns [64h, ...); otherwise both
+      // halves fill the upper half, bf16 columns [64 + 32h, +32), e4m3 [64 + 16h, +16)
+      const uint32_t tPst = kIndep ? tS + 64u * h : tS + 64u + (kFp8 ? 16u : 32u) * h;
+      if constexpr (kFp8)
+        tmem_st16(tPst, pk);
+      else
+        tmem_st32(tPst, *reinterpret_cast<uint32_t(*)[32]>(pk));
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(smem_u32(&sm.p_full[kIndep ? h : 0][i & 1]));
+    }
+    // combine the two halves' statistics (one more exchange on the same barrier): the row sum
+    // (shared maximum), or with kIndep each half's maximum, sum and O weight
+    float m_fin = m_used, l_fin = 0.f, w0 = 1.f, w1 = 0.f;
+    if (ok) {
+      sm.l_x[h][row] = l_sum;
+      if constexpr (kIndep) sm.mx_x[0][h][row] = m_used;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(xbar);
+      ok = mbar_wait(xbar, (kIndep ? 0 : nblk) & 1, abort_flag, p.err);
+      if (ok) {
+        const float l_other = sm.l_x[h ^ 1][row];
+        if constexpr (kIndep) {
+          const float m_other = sm.mx_x[0][h ^ 1][row];
+          const float m0 = h == 0 ? m_used : m_other;
+          const float m1 = h == 0 ? m_other : m_used;
+          const float l0 = h == 0 ? l_sum : l_other;
+          const float l1 = h == 0 ? l_other : l_sum;
+          m_fin = fmaxf(m0, m1);
+          w0 = m0 > -INFINITY ? fast_exp2(m0 - m_fin) : 0.f;
+          w1 = m1 > -INFINITY ? fast_exp2(m1 - m_fin) : 0.f;
+          l_fin = w0 * l0 + w1 * l1;
+        } else {
+          l_fin = l_sum + l_other;
+        }
+      }
+    }
+    if (ok) ok = mbar_wait(smem_u32(&sm.o_done), 0, abort_flag, p.err);
+    if (ok) {
+      tc_fence_after();
+      const bool any = nblk > 0;
+      const uint32_t tO0 = tbase + 256u + lane_off;
+      // unnormalised output columns [32 ch, 32 ch + 32) of this row
+      auto raw = [&](int ch, float (&v)[32]) {
+        if (!any) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          return;
+        }
+        uint32_t a[32];
+        tmem_ld32(tO0 + ch * 32, a);
+        if constexpr (kIndep) {
+          uint32_t c2[32];
+          tmem_ld32(tO0 + 128u + ch * 32, c2);
+          tmem_wait_ld();
+          reg_fence32(a);
+          reg_fence32(c2);
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            v[j] = w0 * __uint_as_float(a[j]) + w1 * __uint_as_float(c2[j]);
+        } else {
+          tmem_wait_ld();
+          reg_fence32(a);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(a[j]);
+        }
+      };
+      if (split_out) {
+        const size_t slot = static_cast<size_t>(gseg + seg) * 2 * kBlockM + row;
+        float4* po = reinterpret_cast<float4*>(p.split_o + slot * kHeadDim + 64 * h);
+#pragma unroll
+        for (int ch = 0; ch < 2; ++ch) {
+          float v[32];
+          raw(2 * h + ch, v);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            po[ch * 8 + j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        }
+        if (h == 0) {
+          p.split_ml[slot * 2] = any ? m_fin : -INFINITY;
+          p.split_ml[slot * 2 + 1] = any ? l_fin : 0.f;
+        }
+        __threadfence();
+      } else {
+        float out_scale = (any && l_fin > 0.f) ? 1.0f / l_fin : 0.f;
+        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        uint8_t* stage = sm.k[0] + (warp - 4) * (32 * 128);
+        auto values = [&](int ch, float (&v)[32]) {
+          raw(ch, v);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] *= out_scale;
+        };
+        if (h == 0) store_tile_rows<0, 1>(stage, lane, row_dst(row), values);
+        else store_tile_rows<1, 2>(stage, lane, row_dst(row), values);
+        if (p.out_peers) __threadfence_system();
+      }
+    }
+    if (split_out) {
+      // last-arriver merge over the tile's segments (named barrier 1 spans the 256 softmax
+      // threads, every one of which reaches it)
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (threadIdx.x == 128) {
+        __threadfence();
+        const int done = atomicAdd(p.split_count + gseg / pr.split, 1);
+        sm.split_last = (done == nseg - 1) ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (sm.split_last && !*abort_flag) {
+        __threadfence();
+        float mx = -INFINITY;
+        for (int sg = 0; sg < nseg; ++sg) {
+          const size_t slot = static_cast<size_t>(gseg + sg) * 2 * kBlockM + row;
+          mx = fmaxf(mx, __ldcg(p.split_ml + slot * 2));
+        }
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; ++j) acc[j] = 0.f;
+        float lsum = 0.f;
+        if (mx > -INFINITY) {
+          for (int sg = 0; sg < nseg; ++sg) {
+            const size_t slot = static_cast<size_t>(gseg + sg) * 2 * kBlockM + row;
+            const float ms = __ldcg(p.split_ml + slot * 2);
+            const float w = ms > -INFINITY ? fast_exp2(ms - mx) : 0.f;
+            lsum += w * __ldcg(p.split_ml + slot * 2 + 1);
+            const float4* po = reinterpret_cast<const float4*>(p.split_o + slot * kHeadDim + 64 * h);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float4 v = __ldcg(po + j);
+              acc[4 * j] += w * v.x;
+              acc[4 * j + 1] += w * v.y;
+              acc[4 * j + 2] += w * v.z;
+              acc[4 * j + 3] += w * v.w;
+            }
+          }
+        }
+        float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
+        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        uint8_t* stage = sm.k[0] + (warp - 4) * (32 * 128);
+        if (h == 0)
+          store_tile_rows<0, 1>(stage, lane, row_dst(row), [&](int ch, float (&v)[32]) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = acc[ch * 32 + j] * out_scale;
+          });
+        else
+          store_tile_rows<1, 2>(stage, lane, row_dst(row), [&](int ch, float (&v)[32]) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = acc[(ch - 2) * 32 + j] * out_scale;
+          });
+        if (p.out_peers) __threadfence_system();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
 // ------------------------------------------------------------------------ host side
 
 // Split-KV workspace of one (device, stream): grown on demand, never shrunk. Growing it waits
@@ -905,6 +1510,12 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   prm.out_rows_per_rank = L.out_rows_per_rank;
   prm.out_heads = L.out_heads;
   prm.out_head0 = L.out_head0;
+  // Launches with a block-sparse problem run the one-tile kernel: each CTA walks its own
+  // tile's list (no union of two lists) and the small CTAs balance uneven lists. Dense launches
+  // run the two-tile kernel, whose two tiles' softmax phases interleave on each SM.
+  bool one_tile = false;
+  for (int i = 0; i < L.num_problems; ++i)
+    one_tile = one_tile || (L.problems[i].sparse && L.problems[i].q_hi > L.problems[i].q_lo);
   int ctas = 0;
   int n = 0;
   int split_pairs = 0;
@@ -918,7 +1529,8 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
     d.kv_hi = src.kv_hi;
     d.sparse = src.sparse ? 1 : 0;
     d.tiles = (src.q_hi - src.q_lo + kBlockM - 1) / kBlockM;
-    d.pairs = (d.tiles + 1) / 2;
+    // work units of one CTA: pairs of query tiles, or single tiles for the one-tile kernel
+    d.pairs = one_tile ? d.tiles : (d.tiles + 1) / 2;
     // block-sparse lists are uneven (rows that keep every block next to rows that keep a
     // quarter): those pairs get kSplitMax CTAs and decide on the device how many to use
     const int nblocks = (src.kv_hi + kBlockN - 1) / kBlockN - src.kv_lo / kBlockN;
@@ -938,37 +1550,38 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
     prm.split_ml = ws.ml;
     prm.split_count = ws.count;
   }
-  const size_t smem = attn_smem_bytes<kFp8>();
+  const size_t smem = one_tile ? attn1_smem_bytes<kFp8>() : attn_smem_bytes<kFp8>();
+  const auto kernel = one_tile ? attn1_fwd_kernel<kFp8, H3SA_ONE_TILE_INDEP != 0>
+                               : attn_fwd_kernel<kFp8>;
+  // per kernel (two-tile / one-tile) and device: the shared-memory attribute is set once, and
+  // setmaxnreg.inc waits until the registers it asks for are free in the block's launch
+  // allocation, so a build whose register count cannot fund the split is refused
   static std::mutex mu;
-  static bool configured[64] = {false};
+  static bool configured[2][64] = {};
+  static bool checked[2] = {};
+  const int which = one_tile ? 1 : 0;
   int dev = 0;
   cudaGetDevice(&dev);
   {
     std::lock_guard<std::mutex> lk(mu);
-    if (dev < 64 && !configured[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(attn_fwd_kernel<kFp8>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (dev < 64 && !configured[which][dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(smem));
       if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute", e);
-      configured[dev] = true;
+      configured[which][dev] = true;
     }
-  }
-  {
-    // setmaxnreg.inc waits until the registers it asks for are free in the block's launch
-    // allocation; refuse to launch a build whose register count cannot fund the split.
-    static int checked[2] = {0, 0};
-    if (!checked[kFp8 ? 1 : 0]) {
+    if (!checked[which]) {
       cudaFuncAttributes attr;
-      cudaError_t e = cudaFuncGetAttributes(&attr, attn_fwd_kernel<kFp8>);
+      cudaError_t e = cudaFuncGetAttributes(&attr, kernel);
       if (e != cudaSuccess) return set_cuda_error("cudaFuncGetAttributes", e);
       if (attr.numRegs * kAttnThreads < kRegSplitTotal)
         return set_error(H3SA_ERR_UNSUPPORTED, "attention build has %d registers per thread; the "
                          "warp-role register split needs %d", attr.numRegs,
                          (kRegSplitTotal + kAttnThreads - 1) / kAttnThreads);
-      checked[kFp8 ? 1 : 0] = 1;
+      checked[which] = true;
     }
   }
-  attn_fwd_kernel<kFp8><<<ctas, kAttnThreads, smem, stream>>>(tmQ, tmK, tmV, prm);
+  kernel<<<ctas, kAttnThreads, smem, stream>>>(tmQ, tmK, tmV, prm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("attn_fwd_kernel launch", e);
   return H3SA_OK;
