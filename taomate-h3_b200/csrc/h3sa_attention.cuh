@@ -20,6 +20,10 @@
 // (s_free) and PV_t(i-1) once it has written P_t(i-1) (p_full), so QK_t(i) runs while the
 // softmax of block i-1 computes its exponentials. The softmax writes P_t(i) only after
 // PV_t(i-1) has completed (pv_done), and rescales O_t at that point when its row maximum grew.
+//
+// Launches with a block-sparse problem use attn1_fwd_kernel instead: one query tile per CTA,
+// S double-buffered in TMEM, and the two column halves of each row as independent online
+// softmaxes with one O accumulator each (see h3sa_attention.cu).
 #pragma once
 
 #include "h3sa_ptx.cuh"
