@@ -798,14 +798,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // ============================================================================ one-tile kernel
-// One 128-row query tile per CTA with S double-buffered in TMEM (S0 [0,128), S1 [128,256),
-// O [256,384)). P goes back into TMEM over the upper half of the S buffer it came from and is
-// read by a TMEM x smem MMA. The MMA warp issues PV(i) and then QK(i + 2) into the buffer PV(i)
-// has just read (one thread's tcgen05.mma execute in issue order), so the scores of block
-// i + 1 are ready while the softmax works on block i: no QK waits for a softmax. Eight softmax
-// warps: warps 4-7 and 8-11 cover the same 32-row quarters (TMEM lanes 32 * (warp % 4)), the
-// first four the left 64 columns of each row and the last four the right 64; the two halves of
-// a row exchange their maxima through shared memory once per block.
+// Used for launches with a block-sparse problem. One 128-row query tile per CTA, walking the
+// tile's own block list, with S double-buffered in TMEM (S0 [0,128), S1 [128,256)). P goes
+// back into TMEM over the S buffer it came from and is read by a TMEM x smem MMA. The MMA warp
+// issues PV(i) and then QK(i + 2) into the buffer PV(i) has just read (one thread's
+// tcgen05.mma execute in issue order), so the scores of block i + 1 are ready while the
+// softmax works on block i: no QK waits for a softmax.
+//
+// Eight softmax warps: warps 4-7 and 8-11 cover the same 32-row quarters (TMEM lanes
+// 32 * (warp % 4)), the first four the left 64 columns of each row and the last four the right
+// 64. With kIndep (the default) the two halves are independent online softmaxes, each with its
+// own running maximum and sum, its P over its own S columns and its own O accumulator (O0
+// [256,384), O1 [384,512)), merged at the end; otherwise they exchange each block's row
+// maximum through shared memory and share one O [256,384) with P over S's upper half.
 // One-tile kernel: the two column halves of a row run independent online softmaxes with an
 // O accumulator each (O0 [256,384), O1 [384,512)), merged at the end (1), or share each
 // block's row maximum through shared memory (0). Measured on the 768p SP=8 block-sparse mask:
