@@ -45,6 +45,9 @@ static_assert(H3SA_FP8_RESCALE_THRESHOLD + H3SA_FP8_BOOST <= 8.5f, "e4m3 P would
 
 // Optional per-block timeline of two CTAs (first and middle of the grid), compiled only with
 // -DH3SA_TRACE: clock64() at fixed points of the producer, MMA and softmax loops.
+#ifndef H3SA_TRACE_QUARTER
+#define H3SA_TRACE_QUARTER 0  // one-tile kernel: the row quarter whose softmax warps are traced
+#endif
 #ifdef H3SA_TRACE
 constexpr int kTraceBlocks = 48;
 __device__ long long g_h3sa_trace[2][kTraceBlocks][24];
@@ -819,6 +822,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #define H3SA_ONE_TILE_INDEP 1
 #endif
 
+// Dense launches run the two-tile kernel (0) or the one-tile kernel as well (1).
+#ifndef H3SA_ONE_TILE_DENSE
+#define H3SA_ONE_TILE_DENSE 0
+#endif
+
 template <bool kFp8>
 struct Attn1Cfg {
   static constexpr int kKStages = kFp8 ? 3 : 2;
@@ -1040,6 +1048,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool w = mbar_wait(smem_u32(&sm.v_full[sv]), (i / kVS) & 1, abort_flag, p.err);
       if (w) w = mbar_wait(smem_u32(&sm.p_full[0][i & 1]), (i >> 1) & 1, abort_flag, p.err);
       if (!(ok = __all_sync(0xffffffffu, w))) break;
+      if (lane == 0) H3SA_TRACE_AT(i, 12);
       tc_fence_after();
       {
         // V rows of a partial block outside the problem's KV range are zeroed first (they
@@ -1074,6 +1083,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             const bool w1 =
                 mbar_wait(smem_u32(&sm.p_full[1][i & 1]), (i >> 1) & 1, abort_flag, p.err);
             if (!(ok = __all_sync(0xffffffffu, w1))) break;
+            if (lane == 0) H3SA_TRACE_AT(i, 13);
             tc_fence_after();
           }
 #pragma unroll
@@ -1105,6 +1115,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       tc_commit(smem_u32(&sm.v_empty[sv]));
       if (i + 2 < nblk) ok = issue_qk(i + 2);
+      if (lane == 0) H3SA_TRACE_AT(i, 14);
     }
     if (ok) tc_commit(smem_u32(&sm.o_done));
     tc_commit(smem_u32(&sm.drain));
@@ -1142,7 +1153,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     for (; i < nblk; ++i) {
       int b;
       next_block(b);
+      const bool tr = q == H3SA_TRACE_QUARTER && lane == 0;
       if (!(ok = mbar_wait(smem_u32(&sm.s_full[i & 1]), (i >> 1) & 1, abort_flag, p.err))) break;
+      if (tr) H3SA_TRACE_AT(i, 6 * h + 0);
       tc_fence_after();
       const uint32_t tS = tbase + static_cast<uint32_t>(i & 1) * 128u + lane_off;
       uint32_t r0[32], r1[32];
@@ -1151,6 +1164,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_wait_ld();
       reg_fence32(r0);
       reg_fence32(r1);
+      if (tr) H3SA_TRACE_AT(i, 6 * h + 1);
       float s[64];
 #pragma unroll
       for (int j = 0; j < 32; ++j) {
@@ -1199,6 +1213,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // possible with independent halves) keeps its P at zero instead of -inf + inf
       const float bias = kBoost - (m_used == -INFINITY ? 0.f : m_used);
       const uint64_t bias2 = f2_pack(bias, bias);
+      if (tr) H3SA_TRACE_AT(i, 6 * h + 2);
 #pragma unroll
       for (int j = 0; j < 64; j += 2) {
         float x0, x1;
@@ -1225,6 +1240,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       float sa, sb;
       f2_unpack(sum2, sa, sb);
       l_sum += sa + sb;
+      if (tr) H3SA_TRACE_AT(i, 6 * h + 3);
       if (any_need) {
         // PV(i - 1) has finished accumulating; rescale this half's O columns
         if (!(ok = mbar_wait(smem_u32(&sm.pv_done[kIndep ? h : 0]), (i - 1) & 1, abort_flag,
@@ -1255,6 +1271,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(smem_u32(&sm.p_full[kIndep ? h : 0][i & 1]));
+      if (tr) H3SA_TRACE_AT(i, 6 * h + 4);
     }
     // combine the two halves' statistics (one more exchange on the same barrier): the row sum
     // (shared maximum), or with kIndep each half's maximum, sum and O weight
@@ -1518,7 +1535,7 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   // Launches with a block-sparse problem run the one-tile kernel: each CTA walks its own
   // tile's list (no union of two lists) and the small CTAs balance uneven lists. Dense launches
   // run the two-tile kernel, whose two tiles' softmax phases interleave on each SM.
-  bool one_tile = false;
+  bool one_tile = H3SA_ONE_TILE_DENSE != 0;
   for (int i = 0; i < L.num_problems; ++i)
     one_tile = one_tile || (L.problems[i].sparse && L.problems[i].q_hi > L.problems[i].q_lo);
   int ctas = 0;
