@@ -53,7 +53,10 @@ constexpr int kMaxUnionBlocks = 2048;
 #ifndef H3SA_SPLIT_SEG_BLOCKS
 #define H3SA_SPLIT_SEG_BLOCKS 64
 #endif
-constexpr int kSplitMax = 4;
+#ifndef H3SA_SPLIT_MAX
+#define H3SA_SPLIT_MAX 4
+#endif
+constexpr int kSplitMax = H3SA_SPLIT_MAX;
 constexpr int kSplitSegBlocks = H3SA_SPLIT_SEG_BLOCKS;
 
 struct AttnProblemDev {
