@@ -805,8 +805,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 // tile's own block list, with S double-buffered in TMEM (S0 [0,128), S1 [128,256)). P goes
 // back into TMEM over the S buffer it came from and is read by a TMEM x smem MMA. The MMA warp
 // issues PV(i) and then QK(i + 2) into the buffer PV(i) has just read (one thread's
-// tcgen05.mma execute in issue order), so the scores of block i + 1 are ready while the
-// softmax works on block i: no QK waits for a softmax.
+// tcgen05.mma execute in issue order), so the scores of block i + 1 are computed while the
+// softmax works on block i. QK(i + 2) still waits for the softmax of block i, through PV(i).
 //
 // Eight softmax warps: warps 4-7 and 8-11 cover the same 32-row quarters (TMEM lanes
 // 32 * (warp % 4)), the first four the left 64 columns of each row and the last four the right
