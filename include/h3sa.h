@@ -77,9 +77,9 @@ H3SA_API size_t h3sa_attention_smem_bytes(int fp8);
  * [heads, q_blocks] and kv_indices [heads, q_blocks, kv_index_stride] (int32, device; each
  * list sorted ascending, absolute logical block indices); q-block j of a problem covers query
  * rows [q_lo + 128j, q_lo + 128j + 128). Dense-only launches pass NULL lists.
- * Block-sparse problems spanning more than 64 KV blocks run split-KV: a pair of query blocks
- * with a long union list is processed as up to 4 KV segments whose partial results are merged
- * on the device. Their workspace belongs to the (device, stream) pair and is grown on demand;
+ * Block-sparse problems spanning more than 64 KV blocks run split-KV: a query block with a
+ * long list (launches with a block-sparse problem give every query block its own list) is
+ * processed as up to 4 KV segments whose partial results are merged on the device. Their workspace belongs to the (device, stream) pair and is grown on demand;
  * growing it allocates device memory and waits for the device, so it must not happen during
  * stream capture (make one uncaptured call of the same size first). Launches on one stream
  * share it; launches on different streams get their own.
