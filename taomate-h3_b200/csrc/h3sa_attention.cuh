@@ -48,8 +48,9 @@ constexpr int kRegsSoftmax = H3SA_REGS_SOFTMAX;
 constexpr int kRegSplitTotal = 128 * kRegsControl + 256 * kRegsSoftmax;
 constexpr int kMaxProblems = 4;
 constexpr int kMaxUnionBlocks = 2048;
-// Split-KV for block-sparse problems: up to kSplitMax CTAs per query-tile pair, one segment of
-// at least kSplitSegBlocks blocks of the pair's union list each.
+// Split-KV for block-sparse problems: up to kSplitMax CTAs per work unit (a query tile in the
+// one-tile kernel, a query-tile pair with its union list in the two-tile kernel), one segment
+// of at least kSplitSegBlocks blocks of the unit's list each.
 #ifndef H3SA_SPLIT_SEG_BLOCKS
 #define H3SA_SPLIT_SEG_BLOCKS 64
 #endif
