@@ -1435,6 +1435,11 @@ struct SplitSpace {
   int* count;
 };
 
+// Guards the split-KV workspaces. The caller holds it from split_workspace() until its kernel
+// is enqueued, so a workspace that another host thread grows (after a device synchronisation)
+// is never freed between handing out its pointers and the launch that uses them.
+static std::mutex g_split_mu;
+
 static int split_workspace(int pairs, cudaStream_t stream, SplitSpace& out) {
   struct Entry {
     int dev;
@@ -1442,7 +1447,6 @@ static int split_workspace(int pairs, cudaStream_t stream, SplitSpace& out) {
     int pairs;
     void* base;
   };
-  static std::mutex mu;
   static Entry entries[64];
   static int n_entries = 0;
   const size_t o_floats = static_cast<size_t>(pairs) * kSplitMax * 2 * kBlockM * kHeadDim;
@@ -1450,7 +1454,6 @@ static int split_workspace(int pairs, cudaStream_t stream, SplitSpace& out) {
   const size_t bytes = (o_floats + ml_floats) * sizeof(float) + static_cast<size_t>(pairs) * 4;
   int dev = 0;
   cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lk(mu);
   Entry* e = nullptr;
   for (int i = 0; i < n_entries; ++i)
     if (entries[i].dev == dev && entries[i].stream == stream) e = &entries[i];
@@ -1564,7 +1567,9 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   }
   prm.n_prob = n;
   if (ctas == 0) return H3SA_OK;
+  std::unique_lock<std::mutex> ws_lock(g_split_mu, std::defer_lock);
   if (split_pairs > 0) {
+    ws_lock.lock();  // held until the launch below is enqueued
     SplitSpace ws;
     int rc = split_workspace(split_pairs, stream, ws);
     if (rc) return rc;
