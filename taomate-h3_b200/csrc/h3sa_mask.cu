@@ -266,8 +266,9 @@ int h3sa_block_mask(const void* query, int32_t rows, int32_t heads, int32_t head
   mask_means_kernel<<<dim3(heads, p.qb + p.kb_means), 128, 0, s>>>(p);
   mask_select_kernel<<<dim3(heads, p.qb), 256, 0, s>>>(p);
   e = cudaGetLastError();
-  cudaFreeAsync(scratch, s);
+  const cudaError_t ef = cudaFreeAsync(scratch, s);
   if (e != cudaSuccess) return set_cuda_error("block mask launch", e);
+  if (ef != cudaSuccess) return set_cuda_error("cudaFreeAsync(block mask scratch)", ef);
   return H3SA_OK;
 }
 
