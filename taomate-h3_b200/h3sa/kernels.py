@@ -50,6 +50,56 @@ def _require_cuda(*tensors: torch.Tensor | None) -> None:
             raise RuntimeError("h3sa kernels require contiguous tensors")
 
 
+def _check_attention_args(
+    query: torch.Tensor,
+    out: torch.Tensor,
+    key_pool: torch.Tensor,
+    value_pool: torch.Tensor,
+    page_table: torch.Tensor,
+    kv_num_blocks: torch.Tensor | None,
+    kv_indices: torch.Tensor | None,
+    q_scale: torch.Tensor | None,
+    k_scale: torch.Tensor | None,
+    v_scale: torch.Tensor | None,
+) -> None:
+    """Shape, dtype and device checks of ``attention_fwd`` that the C ABI cannot make: it
+    sees raw pointers, so a short scale or block-list tensor would be read past its end."""
+
+    if query.ndim != 3:
+        raise RuntimeError("attention query must be [rows, heads, head_dim]")
+    heads = int(query.shape[1])
+    others = [out, key_pool, value_pool, page_table, kv_num_blocks, kv_indices, q_scale, k_scale,
+              v_scale]
+    if any(t is not None and t.device != query.device for t in others):
+        raise RuntimeError("attention tensors must all be on the query's device")
+    if out.shape != query.shape or out.dtype != torch.bfloat16:
+        raise RuntimeError("attention output must be bf16 with the query's shape")
+    if key_pool.shape != value_pool.shape or key_pool.ndim != 3 or key_pool.shape[0] != heads:
+        raise RuntimeError("KV pools must be [heads, pages*128, head_dim] with matching shapes")
+    if value_pool.dtype != key_pool.dtype:
+        raise RuntimeError("key and value pools must have the same dtype")
+    if page_table.dtype != torch.int32:
+        raise RuntimeError("page table must be int32")
+    if (kv_num_blocks is None) != (kv_indices is None):
+        raise RuntimeError("block lists need both kv_num_blocks and kv_indices")
+    if kv_num_blocks is not None and kv_indices is not None:
+        if kv_num_blocks.dtype != torch.int32 or kv_indices.dtype != torch.int32:
+            raise RuntimeError("block lists must be int32 kv_num_blocks and kv_indices")
+        q_blocks = int(kv_num_blocks.shape[-1])
+        stride = int(kv_indices.shape[-1])
+        if (kv_indices.ndim < 2 or int(kv_indices.shape[-2]) != q_blocks
+                or kv_num_blocks.numel() < heads * q_blocks
+                or kv_indices.numel() < heads * q_blocks * stride):
+            raise RuntimeError("block lists must be kv_num_blocks [heads, q_blocks] and "
+                               "kv_indices [heads, q_blocks, stride] for every query head")
+    scales = (q_scale, k_scale, v_scale)
+    if any(t is not None for t in scales):
+        if any(t is None for t in scales):
+            raise RuntimeError("fp8 attention needs q_scale, k_scale and v_scale")
+        if any(t.dtype != torch.float32 or t.numel() < heads for t in scales):  # type: ignore[union-attr]
+            raise RuntimeError("fp8 attention scales must be float32 with one value per head")
+
+
 def attention_fwd(
     query: torch.Tensor,
     out: torch.Tensor,
@@ -69,19 +119,14 @@ def attention_fwd(
 ) -> torch.Tensor:
     """Launch the sm_100a attention kernel (bf16, or e4m3 when scales are given)."""
 
-    _require_cuda(query, out, key_pool, value_pool, page_table, kv_num_blocks, kv_indices)
+    _require_cuda(query, out, key_pool, value_pool, page_table, kv_num_blocks, kv_indices,
+                  q_scale, k_scale, v_scale)
+    _check_attention_args(query, out, key_pool, value_pool, page_table, kv_num_blocks, kv_indices,
+                          q_scale, k_scale, v_scale)
     rows, heads, head_dim = (int(s) for s in query.shape)
-    if out.shape != query.shape or out.dtype != torch.bfloat16:
-        raise RuntimeError("attention output must be bf16 with the query's shape")
-    if key_pool.shape != value_pool.shape or key_pool.ndim != 3 or key_pool.shape[0] != heads:
-        raise RuntimeError("KV pools must be [heads, pages*128, head_dim] with matching shapes")
-    if page_table.dtype != torch.int32:
-        raise RuntimeError("page table must be int32")
     pool_pages = int(key_pool.shape[1]) // PAGE_ROWS
     q_blocks = stride = 0
-    if kv_num_blocks is not None:
-        if kv_indices is None or kv_num_blocks.dtype != torch.int32 or kv_indices.dtype != torch.int32:
-            raise RuntimeError("block lists must be int32 kv_num_blocks and kv_indices")
+    if kv_num_blocks is not None and kv_indices is not None:
         q_blocks = int(kv_num_blocks.shape[-1])
         stride = int(kv_indices.shape[-1])
     probs = _problems(problems)
@@ -95,7 +140,6 @@ def attention_fwd(
     if fp8:
         if query.dtype != torch.float8_e4m3fn or key_pool.dtype != torch.float8_e4m3fn:
             raise RuntimeError("fp8 attention takes e4m3 query and KV pools")
-        _require_cuda(q_scale, k_scale, v_scale)
         call("h3sa_attention_fwd_fp8", *common, ptr(q_scale), ptr(k_scale), ptr(v_scale), *tail)
     else:
         if query.dtype != torch.bfloat16 or key_pool.dtype != torch.bfloat16:

@@ -69,6 +69,49 @@ def test_attention_argument_validation() -> None:
     assert _attn(probs=bad) == lib.H3SA_ERR_INVALID and "block lists" in lib.last_error()
 
 
+def test_attention_wrapper_argument_checks() -> None:
+    """The wrapper rejects block lists and fp8 scales the kernel would read past their end,
+    and mismatched pools, before anything reaches the C ABI (CPU tensors: shape checks only)."""
+
+    from h3sa.kernels import _check_attention_args
+
+    heads, rows, d = 3, 256, 128
+    q = torch.zeros(rows, heads, d, dtype=torch.bfloat16)
+    out = torch.zeros_like(q)
+    kp = torch.zeros(heads, 1024, d, dtype=torch.bfloat16)
+    vp = torch.zeros_like(kp)
+    table = torch.zeros(8, dtype=torch.int32)
+    num = torch.zeros(heads, 2, dtype=torch.int32)
+    idx = torch.zeros(heads, 2, 8, dtype=torch.int32)
+    s = torch.ones(heads, dtype=torch.float32)
+
+    def check(**kw):
+        args = dict(query=q, out=out, key_pool=kp, value_pool=vp, page_table=table,
+                    kv_num_blocks=None, kv_indices=None, q_scale=None, k_scale=None, v_scale=None)
+        args.update(kw)
+        _check_attention_args(**args)
+
+    check()
+    check(kv_num_blocks=num, kv_indices=idx)
+    check(kv_num_blocks=num.unsqueeze(0), kv_indices=idx.unsqueeze(0))  # flex [1, H, ...] layout
+    check(q_scale=s, k_scale=s, v_scale=s)
+    for bad, msg in [
+        (dict(kv_num_blocks=num[:1], kv_indices=idx[:1]), "for every query head"),
+        (dict(kv_num_blocks=num, kv_indices=idx[:, :1]), "for every query head"),
+        (dict(kv_num_blocks=num), "both kv_num_blocks and kv_indices"),
+        (dict(kv_num_blocks=num.long(), kv_indices=idx), "int32"),
+        (dict(q_scale=s, k_scale=s), "q_scale, k_scale and v_scale"),
+        (dict(q_scale=s[:2], k_scale=s, v_scale=s), "one value per head"),
+        (dict(q_scale=s.half(), k_scale=s, v_scale=s), "one value per head"),
+        (dict(value_pool=vp.float()), "same dtype"),
+        (dict(value_pool=vp[:2]), "matching shapes"),
+        (dict(out=out.float()), "bf16 with the query's shape"),
+        (dict(page_table=table.long()), "int32"),
+    ]:
+        with pytest.raises(RuntimeError, match=msg):
+            check(**bad)
+
+
 def test_other_entry_validation() -> None:
     lib = _lib()
     L = lib.LIB
