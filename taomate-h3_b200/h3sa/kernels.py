@@ -164,6 +164,26 @@ def _rows(t: torch.Tensor, page_table: torch.Tensor | None) -> Rows:
     return r
 
 
+def _check_copy_args(src: Sequence[torch.Tensor], dst: Sequence[torch.Tensor],
+                     src_table: torch.Tensor | None, dst_table: torch.Tensor | None) -> tuple[int, int]:
+    """Every src/dst tensor of one ``kv_copy_rows`` call must have the same heads and row size:
+    the kernel addresses all of them with the first source's (its row bounds are checked on
+    the device, its head and row extents are not). Returns (heads, row_bytes)."""
+
+    if len(src) != len(dst) or not 1 <= len(src) <= 2:
+        raise ValueError("one or two src/dst tensor pairs")
+    shapes = []
+    for tensors, table in ((src, src_table), (dst, dst_table)):
+        for t in tensors:
+            if t.ndim != 3:
+                raise RuntimeError("kv_copy_rows takes [heads, pages*128, d] pages or [rows, heads, d] rows")
+            heads = int(t.shape[0] if table is not None else t.shape[1])
+            shapes.append((heads, int(t.shape[-1]) * t.element_size()))
+    if any(sh != shapes[0] for sh in shapes):
+        raise RuntimeError("kv_copy_rows tensors must all have the same heads and row size")
+    return shapes[0]
+
+
 def kv_copy_rows(
     src: Sequence[torch.Tensor],
     dst: Sequence[torch.Tensor],
@@ -188,10 +208,9 @@ def kv_copy_rows(
     if len(src) != len(dst) or not 1 <= len(src) <= 2:
         raise ValueError("one or two src/dst tensor pairs")
     _require_cuda(*src, *dst, src_table, dst_table, src_index, dst_index)
+    heads, row_bytes = _check_copy_args(src, dst, src_table, dst_table)
     if count == 0:
         return
-    heads = int(src[0].shape[0] if src_table is not None else src[0].shape[1])
-    row_bytes = int(src[0].shape[-1]) * src[0].element_size()
     s_arr = (Rows * len(src))(*[_rows(t, src_table) for t in src])
     d_arr = (Rows * len(dst))(*[_rows(t, dst_table) for t in dst])
     for idx in (src_index, dst_index):

@@ -112,6 +112,35 @@ def test_attention_wrapper_argument_checks() -> None:
             check(**bad)
 
 
+def test_kv_copy_shape_checks() -> None:
+    """kv_copy_rows addresses every tensor with the first source's heads and row size, so
+    the wrapper refuses mixed shapes before launching (CPU tensors: shape checks only)."""
+
+    from h3sa.kernels import _check_copy_args
+
+    packed = torch.zeros(300, 3, 128, dtype=torch.bfloat16)
+    pool = torch.zeros(3, 4 * 128, 128, dtype=torch.bfloat16)
+    table = torch.zeros(4, dtype=torch.int32)
+    assert _check_copy_args([packed], [pool], None, table) == (3, 256)
+    assert _check_copy_args([pool, pool], [packed, packed], table, None) == (3, 256)
+    pool8 = torch.zeros(3, 4 * 128, 128, dtype=torch.float8_e4m3fn)
+    back8 = torch.zeros(128, 3, 128, dtype=torch.float8_e4m3fn)
+    assert _check_copy_args([pool8], [back8], table, None) == (3, 128)
+    for src, dst, st, dt in [
+        ([packed], [pool[:2]], None, table),                       # fewer heads in dst
+        ([packed], [pool.float()], None, table),                   # wider rows in dst
+        ([packed], [torch.zeros(3, 4 * 128, 64, dtype=torch.bfloat16)], None, table),
+        ([packed, packed[:, :2]], [pool, pool], None, table),      # second pair differs
+        ([packed], [pool8], None, table),                          # bf16 rows into e4m3 pages
+    ]:
+        with pytest.raises(RuntimeError, match="same heads and row size"):
+            _check_copy_args(src, dst, st, dt)
+    with pytest.raises(RuntimeError, match="pages"):
+        _check_copy_args([packed[0]], [pool], None, table)
+    with pytest.raises(ValueError):
+        _check_copy_args([packed, packed, packed], [pool, pool, pool], None, table)
+
+
 def test_other_entry_validation() -> None:
     lib = _lib()
     L = lib.LIB
