@@ -242,6 +242,22 @@ def quantize_fp8_e4m3_per_head(value: torch.Tensor) -> tuple[torch.Tensor, torch
     return out, scale
 
 
+def _check_quant_pool_args(pool: torch.Tensor, pool_fp8: torch.Tensor, scale: torch.Tensor,
+                           page_table: torch.Tensor) -> None:
+    """The e4m3 pool and the scales are written through raw pointers sized from ``pool``."""
+
+    if pool.ndim != 3 or pool.dtype != torch.bfloat16:
+        raise RuntimeError("quantize_fp8_pool takes a bf16 pool [heads, pages*128, head_dim]")
+    if pool_fp8.shape != pool.shape or pool_fp8.dtype != torch.float8_e4m3fn:
+        raise RuntimeError("the e4m3 pool must be float8_e4m3fn with the bf16 pool's shape")
+    if scale.dtype != torch.float32 or scale.numel() < int(pool.shape[0]):
+        raise RuntimeError("quantize_fp8_pool scales must be float32 with one value per head")
+    if page_table.dtype != torch.int32:
+        raise RuntimeError("page table must be int32")
+    if any(t.device != pool.device for t in (pool_fp8, scale, page_table)):
+        raise RuntimeError("quantize_fp8_pool tensors must all be on the pool's device")
+
+
 def quantize_fp8_pool(
     pool: torch.Tensor,
     pool_fp8: torch.Tensor,
@@ -254,6 +270,7 @@ def quantize_fp8_pool(
     """Per-head e4m3 quantisation of logical rows ``[0, rows)`` of a paged bf16 pool."""
 
     _require_cuda(pool, pool_fp8, scale, page_table)
+    _check_quant_pool_args(pool, pool_fp8, scale, page_table)
     heads = int(pool.shape[0])
     pages = int(pool.shape[1]) // PAGE_ROWS
     call("h3sa_quantize_fp8_pool", ptr(pool), ptr(pool_fp8), ptr(scale), heads, pages,

@@ -141,6 +141,28 @@ def test_kv_copy_shape_checks() -> None:
         _check_copy_args([packed, packed, packed], [pool, pool, pool], None, table)
 
 
+def test_quantize_pool_checks() -> None:
+    """The pool quantiser refuses an e4m3 pool or scale vector smaller than the bf16 pool."""
+
+    from h3sa.kernels import _check_quant_pool_args
+
+    pool = torch.zeros(3, 256, 128, dtype=torch.bfloat16)
+    pool8 = torch.zeros_like(pool, dtype=torch.float8_e4m3fn)
+    scale = torch.zeros(3, dtype=torch.float32)
+    table = torch.zeros(2, dtype=torch.int32)
+    _check_quant_pool_args(pool, pool8, scale, table)
+    for args, msg in [
+        ((pool, pool8[:, :128], scale, table), "bf16 pool's shape"),
+        ((pool, pool.clone(), scale, table), "float8_e4m3fn"),
+        ((pool, pool8, scale[:2], table), "one value per head"),
+        ((pool, pool8, scale.double(), table), "one value per head"),
+        ((pool.float(), pool8, scale, table), "bf16 pool"),
+        ((pool, pool8, scale, table.long()), "int32"),
+    ]:
+        with pytest.raises(RuntimeError, match=msg):
+            _check_quant_pool_args(*args)
+
+
 def test_other_entry_validation() -> None:
     lib = _lib()
     L = lib.LIB
