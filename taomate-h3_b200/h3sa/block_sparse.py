@@ -50,6 +50,11 @@ def composite_block_mask(query: torch.Tensor, paged, *, q_lo: int, q_hi: int, n_
                          device_error: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
     qa = q_block_audio.to(device=query.device, dtype=torch.uint8).contiguous()
     ka = kv_block_audio.to(device=query.device, dtype=torch.uint8).contiguous()
+    # the kernel reads one flag per query block and per KV block through raw pointers
+    if qa.numel() < (q_hi - q_lo + PAGE_ROWS - 1) // PAGE_ROWS:
+        raise ValueError("q_block_audio needs one flag per 128-row query block")
+    if ka.numel() < (n_kv + PAGE_ROWS - 1) // PAGE_ROWS:
+        raise ValueError("kv_block_audio needs one flag per 128-row KV block")
     pol = MaskPolicy(mode=1, n_hist=int(n_hist), n_kv=int(n_kv), sinks=int(sinks),
                      window=int(window), density=float(density), q_block_audio=ptr(qa),
                      kv_block_audio=ptr(ka))

@@ -163,6 +163,25 @@ def test_quantize_pool_checks() -> None:
             _check_quant_pool_args(*args)
 
 
+def test_composite_mask_flag_lengths() -> None:
+    """The composite mask refuses audio flag vectors shorter than its block counts."""
+
+    import types
+
+    from h3sa.block_sparse import composite_block_mask
+
+    q = torch.zeros(300, 2, 128, dtype=torch.bfloat16)  # 3 query blocks
+    paged = types.SimpleNamespace(key=torch.zeros(2, 1024, 128, dtype=torch.bfloat16),
+                                  table=torch.zeros(8, dtype=torch.int32))
+    kw = dict(q_lo=0, q_hi=300, n_hist=512, n_kv=812)  # 7 KV blocks
+    with pytest.raises(ValueError, match="query block"):
+        composite_block_mask(q, paged, q_block_audio=torch.zeros(2), kv_block_audio=torch.zeros(7),
+                             **kw)
+    with pytest.raises(ValueError, match="KV block"):
+        composite_block_mask(q, paged, q_block_audio=torch.zeros(3), kv_block_audio=torch.zeros(6),
+                             **kw)
+
+
 def test_other_entry_validation() -> None:
     lib = _lib()
     L = lib.LIB
