@@ -195,6 +195,9 @@ def attention_fwd_scatter(
     rows, heads, head_dim = (int(s) for s in query.shape)
     if query.dtype != torch.bfloat16 or key_pool.dtype != torch.bfloat16:
         raise RuntimeError("attention takes bf16 query and KV pools")
+    if key_pool.shape != value_pool.shape or key_pool.ndim != 3 or key_pool.shape[0] != heads \
+            or value_pool.dtype != key_pool.dtype:
+        raise RuntimeError("KV pools must be [heads, pages*128, head_dim] with matching shapes")
     tokens, heads_total = out.shape[0], out.shape[1]
     if out.shape[2] != head_dim or tokens * out.world < rows:
         raise ValueError("output shard must be [T, H, d] with W * T covering the query rows")
