@@ -278,14 +278,32 @@ def quantize_fp8_pool(
          stream_handle(None))
 
 
+def _check_permute_extent(src: torch.Tensor, dst: torch.Tensor, dims: Sequence[int],
+                          src_strides: Sequence[int], dst_strides: Sequence[int],
+                          row_bytes: int) -> None:
+    """Every record the index space addresses must lie inside its tensor: the kernel gets
+    only base pointers and byte strides."""
+
+    if len(dims) != 4 or len(src_strides) != 4 or len(dst_strides) != 4:
+        raise ValueError("permute_rows takes a 4-D index space")
+    if any(int(x) < 0 for x in (*dims, *src_strides, *dst_strides)) or int(row_bytes) <= 0:
+        raise ValueError("permute_rows takes non-negative extents and strides")
+    if any(int(x) == 0 for x in dims):
+        return
+    for t, strides, side in ((src, src_strides, "source"), (dst, dst_strides, "destination")):
+        last = sum((int(n) - 1) * int(st) for n, st in zip(dims, strides)) + int(row_bytes)
+        if last > t.numel() * t.element_size():
+            raise ValueError(f"permute_rows {side} holds {t.numel() * t.element_size()} bytes, "
+                             f"the index space reaches byte {last}")
+
+
 def permute_rows(src: torch.Tensor, dst: torch.Tensor, dims: Sequence[int],
                  src_strides: Sequence[int], dst_strides: Sequence[int], row_bytes: int,
                  *, stream: torch.cuda.Stream | None = None) -> None:
     """Copy ``row_bytes`` records over a 4-D index space with byte strides on both sides."""
 
     _require_cuda(src, dst)
-    if len(dims) != 4 or len(src_strides) != 4 or len(dst_strides) != 4:
-        raise ValueError("permute_rows takes a 4-D index space")
+    _check_permute_extent(src, dst, dims, src_strides, dst_strides, row_bytes)
     d = (ctypes.c_int64 * 4)(*[int(x) for x in dims])
     ss = (ctypes.c_int64 * 4)(*[int(x) for x in src_strides])
     ds = (ctypes.c_int64 * 4)(*[int(x) for x in dst_strides])

@@ -182,6 +182,38 @@ def test_composite_mask_flag_lengths() -> None:
                              **kw)
 
 
+def test_ulysses_layouts_stay_inside_their_buffers(monkeypatch) -> None:
+    """The Ulysses pack/unpack layouts address exactly their buffers; a buffer one record too
+    small is refused before launching (library call stubbed, CPU tensors)."""
+
+    from h3sa import kernels, ulysses
+
+    launched = []
+    monkeypatch.setattr(kernels, "_require_cuda", lambda *t: None)
+    monkeypatch.setattr(kernels, "call", lambda name, *a: launched.append(name))
+    monkeypatch.setattr(kernels, "stream_handle", lambda s=None: 0)
+    world, tokens, heads, d = 4, 37, 8, 128
+    hl = heads // world
+    merged = torch.zeros(tokens, 3 * heads * d, dtype=torch.bfloat16)
+    send = torch.zeros(world, 3, tokens, hl, d, dtype=torch.bfloat16)
+    ulysses.pack_qkv_send(merged, send, world=world, num_heads=heads, head_dim=d)
+    out = torch.zeros(3, world * tokens, hl, d, dtype=torch.bfloat16)
+    ulysses.unpack_qkv_recv(send, out, world=world, tokens=tokens, local_heads=hl, head_dim=d)
+    orecv = torch.zeros(world, tokens, hl, d, dtype=torch.bfloat16)
+    oseq = torch.zeros(tokens, world * hl, d, dtype=torch.bfloat16)
+    ulysses.unpack_o_recv(orecv, oseq, world=world, tokens=tokens, local_heads=hl, head_dim=d)
+    assert launched == ["h3sa_permute_rows"] * 3
+    with pytest.raises(ValueError, match="destination"):
+        short = torch.zeros(send.numel() - d, dtype=torch.bfloat16)  # one record short
+        ulysses.pack_qkv_send(merged, short, world=world, num_heads=heads, head_dim=d)
+    with pytest.raises(ValueError, match="source"):
+        ulysses.unpack_qkv_recv(send[:, :, :-1], out, world=world, tokens=tokens, local_heads=hl,
+                                head_dim=d)
+    with pytest.raises(ValueError, match="destination"):
+        ulysses.unpack_o_recv(orecv, oseq[:-1], world=world, tokens=tokens, local_heads=hl,
+                              head_dim=d)
+
+
 def test_other_entry_validation() -> None:
     lib = _lib()
     L = lib.LIB
