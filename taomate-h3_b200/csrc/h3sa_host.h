@@ -56,6 +56,7 @@ size_t attention_smem_bytes(bool fp8);
 
 // Per-head e4m3 quantiser over packed [batch, seq, heads, 128] rows or a paged pool.
 constexpr int kQuantChunkRows = 256;  // rows per partial-amax slot
+constexpr int kQuantMaxBatchHeads = 65535;  // (batch, head) pairs run along gridDim.y
 
 struct QuantSpace {
   const __nv_bfloat16* src;

@@ -97,13 +97,16 @@ __device__ __forceinline__ float bf16_bits_abs_max8(uint4 v) {
   return m;
 }
 
-// grid (batch*heads, chunks): max |x| over kQuantChunkRows rows of one (batch, head).
+// grid (chunks, batch*heads): max |x| over kQuantChunkRows rows of one (batch, head). Chunks
+// run along x, whose extent has no practical limit; batch*heads along y (at most 65535).
+// fmaxf drops a NaN operand, as the reference's GPU quantiser does (Triton's max reduction);
+// its CPU fallback (torch amax) would propagate it instead.
 __global__ void __launch_bounds__(256) quant_amax_partial_kernel(const QuantSpace q, float* partial,
                                                                  int chunks, int* err) {
-  const int bh = blockIdx.x;
+  const int bh = blockIdx.y;
   const int b = bh / q.heads;
   const int h = bh - b * q.heads;
-  const int chunk = blockIdx.y;
+  const int chunk = blockIdx.x;
   const int lane16 = threadIdx.x & 15;   // 16-byte column chunk of the 256-byte row
   const int rsub = threadIdx.x >> 4;     // 16 rows per pass
   float m = 0.f;
@@ -250,7 +253,10 @@ static int grid_for(long long work, int threads) {
 
 int quantize_launch(const QuantSpace& q, float* scale, float* partial, int chunks, int* err,
                     cudaStream_t stream) {
-  quant_amax_partial_kernel<<<dim3(q.batch * q.heads, chunks), 256, 0, stream>>>(q, partial,
+  if (q.batch * q.heads > kQuantMaxBatchHeads)
+    return set_error(H3SA_ERR_INVALID, "fp8 quantiser: batch * heads = %d exceeds %d",
+                     q.batch * q.heads, kQuantMaxBatchHeads);
+  quant_amax_partial_kernel<<<dim3(chunks, q.batch * q.heads), 256, 0, stream>>>(q, partial,
                                                                                  chunks, err);
   quant_finalize_kernel<<<q.batch * q.heads, 256, 0, stream>>>(partial, chunks, scale);
   const long long work = static_cast<long long>(q.batch) * q.seq * q.heads * (kHeadDim / 8);
@@ -330,6 +336,9 @@ int h3sa_quantize_fp8_per_head(const void* x, void* y, float* scale, int32_t bat
     return set_error(H3SA_ERR_INVALID, "quantize_fp8_per_head: invalid arguments");
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
     return set_error(H3SA_ERR_INVALID, "quantize_fp8_per_head: tensors must be 16-byte aligned");
+  if (static_cast<long long>(batch) * heads > kQuantMaxBatchHeads)
+    return set_error(H3SA_ERR_INVALID, "quantize_fp8_per_head: batch * heads = %lld exceeds %d",
+                     static_cast<long long>(batch) * heads, kQuantMaxBatchHeads);
   QuantSpace q{};
   q.src = static_cast<const __nv_bfloat16*>(x);
   q.dst = static_cast<uint8_t*>(y);

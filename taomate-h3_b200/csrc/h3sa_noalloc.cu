@@ -22,7 +22,7 @@
 namespace h3sa {
 
 // 64 Ki floats = 256 KiB: batch * heads * ceil(seq / 256) partial maxima at most, e.g.
-// 24 heads of up to 699,050 rows each.
+// 24 heads of up to 2730 * 256 = 698,880 rows each (one more chunk would need 65,544 slots).
 constexpr int kNoAllocScratchFloats = 65536;
 constexpr int kMaxDevices = 64;
 
@@ -66,6 +66,10 @@ int h3sa_quantize_fp8_per_head_noalloc(const void* x, void* y, float* scale, int
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(y) & 15))
     return set_error(H3SA_ERR_INVALID,
                      "quantize_fp8_per_head_noalloc: tensors must be 16-byte aligned");
+  if (static_cast<long long>(batch) * heads > kQuantMaxBatchHeads)
+    return set_error(H3SA_ERR_INVALID,
+                     "quantize_fp8_per_head_noalloc: batch * heads = %lld exceeds %d",
+                     static_cast<long long>(batch) * heads, kQuantMaxBatchHeads);
   const long long chunks = (static_cast<long long>(seq) + kQuantChunkRows - 1) / kQuantChunkRows;
   const long long slots = static_cast<long long>(batch) * heads * chunks;
   if (slots > kNoAllocScratchFloats)

@@ -68,6 +68,19 @@ class AVKV:
     value: torch.Tensor
 
 
+def _upload_pages(table: torch.Tensor, pages: list[int]) -> None:
+    """Copy a page list into the head of a device page table, ordered on the current stream
+    without blocking the host: the list goes through a pinned staging tensor, which the
+    host allocator keeps alive until the copy has run."""
+
+    if not pages:
+        return
+    host = torch.tensor(pages, dtype=torch.int32)
+    if table.is_cuda:
+        host = host.pin_memory()
+    table[: len(pages)].copy_(host, non_blocking=table.is_cuda)
+
+
 class PagedLayerKV:
     """Page pool and page sequence of one layer.
 
@@ -104,8 +117,7 @@ class PagedLayerKV:
         self.key, self.value = key, value
         self.capacity = capacity
         table = torch.zeros(capacity, dtype=torch.int32, device=self.device)
-        if self.pages:
-            table[: len(self.pages)] = torch.tensor(self.pages, dtype=torch.int32)
+        _upload_pages(table, self.pages)
         self.table = table
 
     def _take(self, count: int) -> list[int]:
@@ -115,9 +127,7 @@ class PagedLayerKV:
         return taken
 
     def _sync_table(self) -> None:
-        n = len(self.pages)
-        if n:
-            self.table[:n].copy_(torch.tensor(self.pages, dtype=torch.int32), non_blocking=False)
+        _upload_pages(self.table, self.pages)
 
     def reserve(self, rows: int) -> None:
         """Make the page sequence cover logical rows [0, rows)."""
@@ -141,8 +151,7 @@ class PagedLayerKV:
         count = int(rows.numel())
         new_pages = self._take((count + PAGE_ROWS - 1) // PAGE_ROWS)
         table = torch.zeros(self.capacity, dtype=torch.int32, device=self.device)
-        if new_pages:
-            table[: len(new_pages)] = torch.tensor(new_pages, dtype=torch.int32)
+        _upload_pages(table, new_pages)
         if count:
             kv_copy_rows([self.key, self.value], [self.key, self.value], count=count,
                          src_table=self.table, dst_table=table,

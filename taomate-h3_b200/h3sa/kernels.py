@@ -288,6 +288,11 @@ def _check_permute_extent(src: torch.Tensor, dst: torch.Tensor, dims: Sequence[i
         raise ValueError("permute_rows takes a 4-D index space")
     if any(int(x) < 0 for x in (*dims, *src_strides, *dst_strides)) or int(row_bytes) <= 0:
         raise ValueError("permute_rows takes non-negative extents and strides")
+    # the kernel moves 16-byte vectors: every record must start on a 16-byte boundary
+    if int(row_bytes) % 16 or any(int(x) % 16 for x in (*src_strides, *dst_strides)):
+        raise ValueError("permute_rows row_bytes and strides must be multiples of 16 bytes")
+    if src.data_ptr() % 16 or dst.data_ptr() % 16:
+        raise ValueError("permute_rows tensors must start on a 16-byte boundary")
     if any(int(x) == 0 for x in dims):
         return
     for t, strides, side in ((src, src_strides, "source"), (dst, dst_strides, "destination")):

@@ -1,7 +1,8 @@
 """Generate the golden fixtures by running the REFERENCE's own Python code on CPU.
 
-Run in a checkout that has the reference sources (default /root/reference, override with
-H3SA_REFERENCE); the GPU box and the test suite only read the committed .npz outputs.
+Run where the reference sources are checked out: by default a ``reference`` checkout beside
+this repository's directory, or the path in H3SA_REFERENCE. The GPU box and the test suite
+only read the committed .npz outputs.
 
     python tests/golden/make_golden.py
 
@@ -33,7 +34,8 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("H3SA_REFERENCE", "/root/reference"))
+# the reference checkout: a sibling of this repository unless H3SA_REFERENCE names it
+REF = Path(os.environ.get("H3SA_REFERENCE", HERE.parents[2] / "reference"))
 sys.path.insert(0, str(HERE))
 
 from inputs import bf16, fp8_input, hook_cpu_inputs, mask_inputs, prologue_inputs, ulysses_merged  # noqa: E402

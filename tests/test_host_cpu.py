@@ -349,3 +349,23 @@ def test_parallel_context_validation() -> None:
         ParallelContext(1, 0, 2, 2, object(), object())
     with pytest.raises(ValueError, match="process groups are required"):
         ParallelContext(1, 0, 2, 1, None, object())
+
+
+def test_permute_rows_refuses_unaligned_records(monkeypatch) -> None:
+    """The permute kernel moves 16-byte vectors: record sizes, strides and base pointers that
+    are not 16-byte multiples are refused in the wrapper (library call stubbed, CPU tensors)."""
+
+    from h3sa import kernels
+
+    monkeypatch.setattr(kernels, "_require_cuda", lambda *t: None)
+    monkeypatch.setattr(kernels, "call", lambda name, *a: None)
+    monkeypatch.setattr(kernels, "stream_handle", lambda s=None: 0)
+    src = torch.zeros(4096, dtype=torch.uint8)
+    dst = torch.zeros(4096, dtype=torch.uint8)
+    kernels.permute_rows(src, dst, (2, 2, 1, 1), (256, 128, 0, 0), (128, 256, 0, 0), 128)
+    with pytest.raises(ValueError, match="multiples of 16"):
+        kernels.permute_rows(src, dst, (2, 2, 1, 1), (256, 128, 0, 0), (128, 256, 0, 0), 120)
+    with pytest.raises(ValueError, match="multiples of 16"):
+        kernels.permute_rows(src, dst, (2, 2, 1, 1), (264, 128, 0, 0), (128, 256, 0, 0), 128)
+    with pytest.raises(ValueError, match="16-byte boundary"):
+        kernels.permute_rows(src[8:], dst, (2, 2, 1, 1), (256, 128, 0, 0), (128, 256, 0, 0), 128)

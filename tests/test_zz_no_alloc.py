@@ -45,9 +45,46 @@ def test_noalloc_matches_allocating_entry_on_consecutive_calls() -> None:
         assert torch.equal(y_new.view(torch.uint8), y_ref.view(torch.uint8)), i
 
 
+@pytest.mark.gpu
+def test_noalloc_leaves_the_stream_ordered_pool_untouched() -> None:
+    """The allocating entry takes its scratch from the device's default stream-ordered pool;
+    the no-allocation entry must not: the pool's used-memory high-water mark, reset before
+    the call, stays at what was in use before it."""
+
+    runtime = pytest.importorskip("cuda.bindings.runtime")
+    driver = pytest.importorskip("cuda.bindings.driver")
+    dev = torch.cuda.current_device()
+    err, pool = runtime.cudaDeviceGetDefaultMemPool(dev)
+    assert err == runtime.cudaError_t.cudaSuccess
+    high = runtime.cudaMemPoolAttr.cudaMemPoolAttrUsedMemHigh
+    cur = runtime.cudaMemPoolAttr.cudaMemPoolAttrUsedMemCurrent
+
+    def watermark(entry: str, x: torch.Tensor) -> tuple[int, int]:
+        torch.cuda.synchronize()
+        assert runtime.cudaMemPoolSetAttribute(pool, high, driver.cuuint64_t(0))[0] == \
+            runtime.cudaError_t.cudaSuccess
+        before = int(runtime.cudaMemPoolGetAttribute(pool, cur)[1])
+        _quantise(entry, x)
+        torch.cuda.synchronize()
+        return before, int(runtime.cudaMemPoolGetAttribute(pool, high)[1])
+
+    x = torch.randn(1, 4096, 8, 128, device="cuda").bfloat16()
+    _quantise("h3sa_quantize_fp8_per_head_noalloc", x)  # first call: per-device set-up
+    before, peak = watermark("h3sa_quantize_fp8_per_head_noalloc", x)
+    assert peak == before, (before, peak)
+    before, peak = watermark("h3sa_quantize_fp8_per_head", x)
+    assert peak > before, "the allocating entry should show its scratch in the pool"
+
+
 def test_noalloc_rejects_sizes_beyond_scratch() -> None:
     lib = _lib()
     seq = 256 * (NOALLOC_SLOTS // 4) + 1  # 4 heads of ceil(seq / 256) chunks: one slot too many
     rc = lib.LIB.h3sa_quantize_fp8_per_head_noalloc(16, 32, 48, 1, seq, 4, 128, None)
     assert rc == lib.H3SA_ERR_INVALID
     assert "exceeds the fixed scratch" in lib.last_error()
+    # (batch, head) pairs run along the grid's y extent, at most 65535 of them; a single head
+    # may have any number of 256-row chunks (they run along x)
+    rc = lib.LIB.h3sa_quantize_fp8_per_head_noalloc(16, 32, 48, 1, 1, 65536, 128, None)
+    assert rc == lib.H3SA_ERR_INVALID and "batch * heads" in lib.last_error()
+    rc = lib.LIB.h3sa_quantize_fp8_per_head(16, 32, 48, 2, 1, 40000, 128, None)
+    assert rc == lib.H3SA_ERR_INVALID and "batch * heads" in lib.last_error()
