@@ -250,6 +250,15 @@ H3SA_API int h3sa_ipc_close(void* ptr);
 H3SA_API int h3sa_peer_barrier(const uint64_t* peer_flags, int32_t world, int32_t rank,
                                uint32_t epoch, int32_t* device_error, void* stream);
 
+/* h3sa_peer_barrier with the caller's wait limit limit_ns in (0, 60 s] instead of 2 s: a rank
+ * that has not arrived by then leaves this rank's wait with H3SA_DEVERR_WAIT_TIMEOUT set, so a
+ * dead or late peer shows up as a device error word the host reads, never as a hung stream.
+ * Counterpart of the reference's collective error path, which gathers every rank's failure
+ * into one error for the caller (T/runtime/direct.py:227-237). */
+H3SA_API int h3sa_peer_barrier_limit(const uint64_t* peer_flags, int32_t world, int32_t rank,
+                                     uint32_t epoch, int64_t limit_ns, int32_t* device_error,
+                                     void* stream);
+
 H3SA_API int h3sa_scatter_qkv(const void* merged, int32_t tokens, int32_t heads,
                               int32_t head_dim, int32_t world, int32_t rank,
                               const uint64_t* peer_qkv, void* stream);

@@ -146,11 +146,12 @@ __global__ void scatter_qkv_paged_kernel(const ScatterPagedParams p) {
 // Barrier over peer memory for the ranks of one node: every rank stores `epoch` into slot
 // `rank` of every rank's flag array (release, system scope), then waits until all slots of
 // its own array hold at least `epoch` (acquire). One thread per peer. The wait is bounded:
-// after 2 s it sets H3SA_DEVERR_WAIT_TIMEOUT in `err` and returns.
+// after `limit_ns` (2 s by default) it sets H3SA_DEVERR_WAIT_TIMEOUT in `err` and returns.
 constexpr long long kBarrierSpinNs = 2000000000LL;  // 2 s
+constexpr long long kBarrierMaxSpinNs = 60000000000LL;  // longest limit a caller may set
 
 __global__ void peer_barrier_kernel(const uint64_t* flags, int world, int rank,
-                                    unsigned int epoch, int* err) {
+                                    unsigned int epoch, long long limit_ns, int* err) {
   const int q = threadIdx.x;
   if (q < world) {
     unsigned int* remote =
@@ -169,7 +170,7 @@ __global__ void peer_barrier_kernel(const uint64_t* flags, int world, int rank,
       if (static_cast<int>(v - epoch) >= 0) break;
       unsigned long long t;
       asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-      if (static_cast<long long>(t - t0) > kBarrierSpinNs) {
+      if (static_cast<long long>(t - t0) > limit_ns) {
         if (err) atomicOr(err, H3SA_DEVERR_WAIT_TIMEOUT);
         break;
       }
@@ -302,15 +303,25 @@ int h3sa_scatter_qkv_paged(const void* merged, int32_t tokens, int32_t heads, in
   return H3SA_OK;
 }
 
-int h3sa_peer_barrier(const uint64_t* peer_flags, int32_t world, int32_t rank, uint32_t epoch,
-                      int32_t* device_error, void* stream) {
+int h3sa_peer_barrier_limit(const uint64_t* peer_flags, int32_t world, int32_t rank,
+                            uint32_t epoch, int64_t limit_ns, int32_t* device_error,
+                            void* stream) {
   if (!peer_flags || world <= 0 || world > 1024 || rank < 0 || rank >= world || epoch == 0)
     return set_error(H3SA_ERR_INVALID, "peer_barrier: invalid arguments");
+  if (limit_ns <= 0 || limit_ns > kBarrierMaxSpinNs)
+    return set_error(H3SA_ERR_INVALID, "peer_barrier: wait limit %lld ns outside (0, %lld]",
+                     static_cast<long long>(limit_ns), kBarrierMaxSpinNs);
   peer_barrier_kernel<<<1, ((world + 31) / 32) * 32, 0, static_cast<cudaStream_t>(stream)>>>(
-      peer_flags, world, rank, epoch, device_error);
+      peer_flags, world, rank, epoch, static_cast<long long>(limit_ns), device_error);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("peer_barrier_kernel launch", e);
   return H3SA_OK;
+}
+
+int h3sa_peer_barrier(const uint64_t* peer_flags, int32_t world, int32_t rank, uint32_t epoch,
+                      int32_t* device_error, void* stream) {
+  return h3sa_peer_barrier_limit(peer_flags, world, rank, epoch, kBarrierSpinNs, device_error,
+                                 stream);
 }
 
 }  // extern "C"

@@ -109,6 +109,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "h3sa_scatter_qkv_paged": (ctypes.c_int,
                                [_P, _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _I, _I, _P, _P]),
     "h3sa_peer_barrier": (ctypes.c_int, [_P, _I, _I, ctypes.c_uint32, _P, _P]),
+    "h3sa_peer_barrier_limit": (ctypes.c_int, [_P, _I, _I, ctypes.c_uint32, ctypes.c_int64, _P,
+                                               _P]),
     "h3sa_permute_rows": (
         ctypes.c_int,
         [_P, _P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_int64),

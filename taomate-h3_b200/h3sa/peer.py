@@ -89,20 +89,25 @@ class PeerBarrier:
     stream like a kernel: a few microseconds over NVLink instead of a NCCL all-reduce.
     Collective to construct; every rank then calls it the same number of times."""
 
-    def __init__(self, group=None, device_error: torch.Tensor | None = None) -> None:
+    def __init__(self, group=None, device_error: torch.Tensor | None = None,
+                 timeout_s: float = 2.0) -> None:
         import torch.distributed as dist
 
+        if not 0.0 < timeout_s <= 60.0:
+            raise ValueError("peer barrier wait limit must be in (0, 60] seconds")
         self.flags = PeerBuffer((2 * dist.get_world_size(group),), group)  # uint32 per rank
         self.flags.tensor.zero_()
         torch.cuda.synchronize()
         dist.barrier(group=group)
         self.epoch = 0
         self.err = device_error
+        self.limit_ns = int(timeout_s * 1e9)
 
     def __call__(self, stream: torch.cuda.Stream | None = None) -> None:
         self.epoch = (self.epoch + 1) & 0xFFFFFFFF or 1
-        call("h3sa_peer_barrier", ptr(self.flags.peer_table), self.flags.world, self.flags.rank,
-             ctypes.c_uint32(self.epoch), ptr(self.err), stream_handle(stream))
+        call("h3sa_peer_barrier_limit", ptr(self.flags.peer_table), self.flags.world,
+             self.flags.rank, ctypes.c_uint32(self.epoch), ctypes.c_int64(self.limit_ns),
+             ptr(self.err), stream_handle(stream))
 
     def close(self) -> None:
         self.flags.close()

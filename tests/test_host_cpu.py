@@ -369,3 +369,12 @@ def test_permute_rows_refuses_unaligned_records(monkeypatch) -> None:
         kernels.permute_rows(src, dst, (2, 2, 1, 1), (264, 128, 0, 0), (128, 256, 0, 0), 128)
     with pytest.raises(ValueError, match="16-byte boundary"):
         kernels.permute_rows(src[8:], dst, (2, 2, 1, 1), (256, 128, 0, 0), (128, 256, 0, 0), 128)
+
+
+def test_peer_barrier_limit_validation() -> None:
+    lib = _lib()
+    L = lib.LIB
+    for limit in (0, -5, 61_000_000_000):
+        rc = L.h3sa_peer_barrier_limit(16, 2, 0, 1, limit, None, None)
+        assert rc == lib.H3SA_ERR_INVALID and "wait limit" in lib.last_error()
+    assert L.h3sa_peer_barrier_limit(16, 2, 2, 1, 1000, None, None) == lib.H3SA_ERR_INVALID
