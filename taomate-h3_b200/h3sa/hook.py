@@ -35,6 +35,7 @@ import torch
 from . import _lib
 from .cache import CleanAVKVCache
 from .kernels import AttentionProblem, attention_fwd, kv_copy_rows, quantize_fp8_e4m3_per_head, quantize_fp8_pool
+from .peer import attention_fwd_scatter
 
 DENSE_BACKENDS = ("flash_attn_3", "flash_attn3", "sdpa", "h3sa_dense")
 FP8_BACKENDS = ("flash_attn3_fp8_dynamic",)
@@ -112,6 +113,11 @@ class H3StreamingAttentionHook:
         self._plan_key: tuple[int, ...] | None = None
         self._device_error: torch.Tensor | None = None
         self._fp8_pools: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+        # Set by h3sa.layer for a call whose heads -> sequence exchange is peer stores: the
+        # attention epilogue then writes every output row into its owner's sequence shard
+        # (last_output_exchanged tells the caller whether that happened).
+        self.output_exchange = None
+        self.last_output_exchanged = False
 
     def receipt(self) -> dict[str, object]:
         return {
@@ -248,13 +254,24 @@ class H3StreamingAttentionHook:
                                          sparse=self.backend in SPARSE_BACKENDS)
         cond_problem = AttentionProblem(cond_q[0], cond_q[1], c0, o0)
         out_main = out if gathered is None else torch.empty_like(gathered)
+        # rows stored straight into the owners' sequence shards when the output rows are the
+        # query rows (no gather) and the launch is bf16
+        exchange = self.output_exchange
+        if exchange is not None and (gathered is not None or self.backend in FP8_BACKENDS):
+            exchange = None
+        self.last_output_exchanged = exchange is not None
         self._launch(layer_name, paged, q_src, out_main, [media_problem, cond_problem], scale,
-                     n_kv_media, n_hist, plan, err)
+                     n_kv_media, n_hist, plan, err, exchange)
         if other_kv:
             probs = [AttentionProblem(a, b, c, c + (b - a)) for a, b, c in other_kv]
             for i in range(0, len(probs), _lib.MAX_PROBLEMS):
-                attention_fwd(query, out, paged.key, paged.value, paged.table,
-                              probs[i:i + _lib.MAX_PROBLEMS], scale, device_error=err)
+                chunk = probs[i:i + _lib.MAX_PROBLEMS]
+                if exchange is not None:
+                    attention_fwd_scatter(query, paged.key, paged.value, paged.table, chunk, scale,
+                                          exchange.out, device_error=err)
+                else:
+                    attention_fwd(query, out, paged.key, paged.value, paged.table, chunk, scale,
+                                  device_error=err)
                 self.launches += 1
         if gathered is not None:
             kv_copy_rows([out_main], [out], count=plan.n_media, src_start=0,
@@ -273,7 +290,7 @@ class H3StreamingAttentionHook:
     # ------------------------------------------------------------------ launches
     def _launch(self, layer_name: str, paged, q_src: torch.Tensor, out: torch.Tensor,
                 problems: list[AttentionProblem], scale: float, n_kv: int, n_hist: int,
-                plan: _DocumentPlan, err: torch.Tensor) -> None:
+                plan: _DocumentPlan, err: torch.Tensor, exchange=None) -> None:
         if self.backend in FP8_BACKENDS:
             self._launch_fp8(layer_name, paged, q_src, out, problems, scale, n_kv, err)
             return
@@ -285,8 +302,12 @@ class H3StreamingAttentionHook:
                                         density=self.history_density, scale=scale)
             if not lists:
                 problems = [AttentionProblem(p.q_lo, p.q_hi, p.kv_lo, p.kv_hi) for p in problems]
-        attention_fwd(q_src, out, paged.key, paged.value, paged.table, problems, scale,
-                      device_error=err, **lists)
+        if exchange is not None:
+            attention_fwd_scatter(q_src, paged.key, paged.value, paged.table, problems, scale,
+                                  exchange.out, device_error=err, **lists)
+        else:
+            attention_fwd(q_src, out, paged.key, paged.value, paged.table, problems, scale,
+                          device_error=err, **lists)
         self.launches += 1
 
     def _launch_fp8(self, layer_name: str, paged, q_src: torch.Tensor, out: torch.Tensor,

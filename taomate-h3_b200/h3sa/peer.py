@@ -69,6 +69,7 @@ class PeerBuffer:
             call("h3sa_ipc_open", buf, ctypes.byref(opened))
             self._opened.append(int(opened.value))
             addresses.append(int(opened.value))
+        self.addresses = addresses  # host copy of peer_table
         self.peer_table = torch.tensor(addresses, dtype=torch.int64, device="cuda")
 
     def close(self) -> None:
