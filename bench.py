@@ -1,21 +1,22 @@
 #!/usr/bin/env python
 """Benchmark: 768p streaming chunk attention (TaoMate-H3 hot path) on B200.
 
-One step = one streaming-hook layer call of the 768p chunk on this rank: the seq->heads
-exchange of the local merged QKV shard (SP > 1), the current chunk's K/V rows written into the
-paged cache after the 16384-row history, attention of the 12509 media queries over
-[history | current] (plus the pad document over itself), and the heads->seq exchange of O
-(SP > 1). Ulysses SP = number of GPUs, heads 24 / SP per GPU. For SP > 1 the exchanges are
-peer stores over NVLink by default: one kernel scatters Q to the owners' planes and K/V
-straight into the owners' caches, and the attention epilogue stores O into the owners'
-sequence shards. `--unfused` uses NCCL all-to-all with pack/unpack kernels and a separate
-cache append instead (the reference's structure).
+One step = one streaming layer call of the 768p chunk on this rank, from the raw merged QKV
+projection shard to the attention output: the QK-RMSNorm + RoPE prologue, the seq->heads
+exchange (SP > 1), the current chunk's K/V rows written into the paged cache after the
+16384-row history, attention of the 12509 media queries over [history | current] (plus the
+pad document over itself), and the heads->seq exchange of O (SP > 1). Ulysses SP = number of
+GPUs, heads 24 / SP per GPU. By default the prologue, the exchange and the cache append are
+one kernel storing Q into the owners' planes and K/V straight into the owners' caches (over
+NVLink at SP > 1), and the attention epilogue stores O into the owners' sequence shards.
+`--unfused` runs the reference's structure instead: prologue into a send buffer, NCCL
+all-to-all, unpack, cache append, attention, NCCL all-to-all, unpack.
 
 Prints one JSON line (rank 0). ``value`` = total attention TFLOP/s of the whole job
-(4 * Nq * Nk * d * H per step / max-over-ranks device time). ``e2e`` repeats the step
-through the public API with every step's input copied from pinned host memory and its output
-copied back inside the timed region; the copies are double-buffered on their own streams, so
-the upload and download of neighbouring steps overlap the compute of the current one.
+(4 * Nq * Nk * d * H per step / max-over-ranks device time). ``e2e`` runs the drop-in path a
+maintainer installs (h3sa.layer.attention_from_projection through the streaming hook) with
+every step's raw projection copied from pinned host memory and its output copied back inside
+the timed region; ``e2e_kernel_path`` does the same around the timed step's own calls.
 ``--impl reference`` times the reference's CPU attention (its PyTorch path restated in
 oracle/) on this host's cores on a bounded query sample.
 """
@@ -248,63 +249,87 @@ def run_reference(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
+def _rope_cache(rows: int, rotary: int, device: torch.device) -> torch.Tensor:
+    """Synthetic bf16 cos|sin cache [rows, rotary]: one position per packed row, the standard
+    base-10000 frequencies (the model builds its 3-axis table the same size)."""
+
+    half = rotary // 2
+    inv = 10000.0 ** (-torch.arange(half, dtype=torch.float64, device=device) / half)
+    ang = torch.arange(rows, dtype=torch.float64, device=device)[:, None] * inv[None, :]
+    return torch.cat((ang.cos(), ang.sin()), dim=1).to(torch.bfloat16)
+
+
 class Step:
-    """Device buffers and launches of one benchmark step on this rank."""
+    """Device buffers and launches of one benchmark step on this rank.
+
+    Input: this rank's raw merged QKV projection shard [T, 3*H*d] (before the QK-RMSNorm /
+    RoPE prologue). Fused path (default, any SP): one kernel normalises and rotates Q/K and
+    stores Q into the owning rank's attention plane and K/V straight into the owner's paged
+    cache after the history (local at SP=1); a peer barrier (SP>1); attention, whose
+    epilogue stores each output row into the owner's sequence shard (SP>1); a peer barrier.
+    Unfused path (--unfused, the reference's structure): prologue into the send layout, NCCL
+    all-to-all, unpack, cache append, attention, NCCL all-to-all, unpack.
+    """
+
+    PHASES_FUSED = ("prologue_scatter_into_cache", "barrier_before_attention",
+                    "attention_with_o_store", "barrier_after_attention")
+    PHASES_NCCL = ("prologue_pack", "qkv_all_to_all", "unpack", "cache_append", "attention",
+                   "o_all_to_all", "o_unpack")
+    EXCHANGE_PHASES = ("qkv_all_to_all", "o_all_to_all", "barrier_before_attention",
+                       "barrier_after_attention")
 
     def __init__(self, world: int, rank: int, device: torch.device, fused: bool = True) -> None:
         import h3sa
         from h3sa.kernels import PAGE_ROWS
+        from h3sa.peer import LocalBuffer, PeerBarrier, PeerBuffer
 
         self.h3sa = h3sa
         self.world, self.rank, self.device = world, rank, device
-        # SP > 1: the two Ulysses exchanges as peer stores (scatter kernel, attention epilogue)
-        # over NVLink, or NCCL all-to-all with layout copies (the reference's structure)
-        self.fused = fused and world > 1
-        self.phases = self.PHASES_FUSED if self.fused else self.PHASES
+        self.fused = fused or world == 1
+        self.phases = self.PHASES_FUSED if self.fused else self.PHASES_NCCL
         geo = _geometry(world)
         self.geo = geo
         heads, d = CFG["heads"], CFG["head_dim"]
         hl = geo["heads_local"]
         self.hl = hl
+        rows, tokens = geo["rows"], geo["tokens"]
         g = torch.Generator(device=device).manual_seed(1000 + rank)
-        # this rank's post-prologue merged QKV shard [T, 3*H*d] (q, k RMS-normalised ~ N(0,1))
-        self.merged = torch.randn(geo["tokens"], 3 * heads * d, device=device, generator=g).to(torch.bfloat16)
+        # this rank's raw merged QKV projection shard [T, 3*H*d] ~ N(0,1)
+        self.merged = torch.randn(tokens, 3 * heads * d, device=device, generator=g).to(torch.bfloat16)
+        gw = torch.Generator(device=device).manual_seed(99)  # weights: the same on every rank
+        self.q_weight = (1 + 0.05 * torch.randn(d, device=device, generator=gw)).to(torch.bfloat16)
+        self.k_weight = (1 + 0.05 * torch.randn(d, device=device, generator=gw)).to(torch.bfloat16)
+        self.cos_sin = _rope_cache(CFG["history"] + rows, 96, device)
+        self.positions = CFG["history"] + rank * tokens + torch.arange(tokens, device=device)
         nh = CFG["history"]
         self.n_hist = nh
-        total_rows = nh + geo["rows"]
-        pages = (total_rows + PAGE_ROWS - 1) // PAGE_ROWS
+        pages = (nh + rows + PAGE_ROWS - 1) // PAGE_ROWS
         self.table = torch.arange(pages, dtype=torch.int32, device=device)
-        rows, tokens = geo["rows"], geo["tokens"]
-        if self.fused:
-            # every rank maps every rank's Q plane, KV pools and output shard: the QKV scatter
-            # writes the current chunk's K/V straight into the owners' pools
-            from h3sa.peer import PeerBarrier, PeerBuffer
-
-            self.kpool_peer = PeerBuffer((hl, pages * PAGE_ROWS, d))
-            self.vpool_peer = PeerBuffer((hl, pages * PAGE_ROWS, d))
-            self.kpool, self.vpool = self.kpool_peer.tensor, self.vpool_peer.tensor
-            self.kpool.zero_()
-            self.vpool.zero_()
-            self.q_peer = PeerBuffer((rows, hl, d))
-            self.out_peer = PeerBuffer((tokens, heads, d))
+        shape_pool = (hl, pages * PAGE_ROWS, d)
+        if world > 1:
+            # every rank maps every rank's Q plane, KV pools and output shard
+            self.k_buf, self.v_buf = PeerBuffer(shape_pool), PeerBuffer(shape_pool)
+            self.q_buf = PeerBuffer((rows, hl, d))
+            self.out_buf = PeerBuffer((tokens, heads, d))
             self.peer_barrier = PeerBarrier(device_error=None)
-            self.final = self.out_peer.tensor
         else:
-            self.kpool = torch.zeros(hl, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=device)
-            self.vpool = torch.zeros_like(self.kpool)
+            self.k_buf = LocalBuffer(torch.zeros(shape_pool, dtype=torch.bfloat16, device=device))
+            self.v_buf = LocalBuffer(torch.zeros(shape_pool, dtype=torch.bfloat16, device=device))
+            self.q_buf = LocalBuffer(torch.zeros(rows, hl, d, dtype=torch.bfloat16, device=device))
+        self.kpool, self.vpool = self.k_buf.tensor, self.v_buf.tensor
+        self.kpool.zero_()
+        self.vpool.zero_()
         hist = torch.randn(nh, hl, d, device=device, generator=g).to(torch.bfloat16)
         h3sa.kv_copy_rows([hist, hist], [self.kpool, self.vpool], count=nh, dst_table=self.table)
-        if world > 1 and not self.fused:
+        if not self.fused:
             self.send = torch.empty(world, 3, tokens, hl, d, dtype=torch.bfloat16, device=device)
             self.recv = torch.empty_like(self.send)
             self.qkv = torch.empty(3, rows, hl, d, dtype=torch.bfloat16, device=device)
             self.orecv = torch.empty(world, tokens, hl, d, dtype=torch.bfloat16, device=device)
             self.final = torch.empty(tokens, heads, d, dtype=torch.bfloat16, device=device)
-        elif world == 1:
-            self.qkv = self.merged.view(rows, 3, heads, d).permute(1, 0, 2, 3).contiguous()
         self.out = torch.empty(rows, hl, d, dtype=torch.bfloat16, device=device)
         self.err = torch.zeros(1, dtype=torch.int32, device=device)
-        if self.fused:
+        if world > 1:
             self.peer_barrier.err = self.err  # a barrier wait that gives up shows in device_error
         P = h3sa.AttentionProblem
         nq, pad = geo["nq"], geo["pad"]
@@ -313,23 +338,19 @@ class Step:
             self.problems.append(P(nq, rows, nh + nq, nh + rows))
         self.scale = d ** -0.5
         self.flops = 4.0 * nq * (nh + nq) * d * hl  # this rank's algorithmic FLOPs
-        # h3sa kernels per step: SP=1 cache append + attention; NCCL path + pack, two unpacks;
-        # peer path: scatter into the caches, barrier, attention, barrier
-        self.launches_per_step = 4 if self.fused else 2 + (3 if world > 1 else 0)
-
-    PHASES = ("pack", "qkv_all_to_all", "unpack", "cache_append", "attention", "o_all_to_all",
-              "o_unpack")
-    PHASES_FUSED = ("qkv_scatter_into_cache", "barrier_before_attention", "unused", "unused_append",
-                    "attention_with_o_scatter", "barrier_after_attention", "unused2")
-    EXCHANGE_PHASES = ("qkv_all_to_all", "o_all_to_all", "qkv_scatter_into_cache",
-                       "barrier_before_attention", "barrier_after_attention")
+        # h3sa kernels per step: fused: prologue/scatter + attention (+ 2 barriers at SP>1);
+        # NCCL: prologue pack + unpack + cache append + attention + unpack
+        self.launches_per_step = (2 + (2 if world > 1 else 0)) if self.fused else 5
 
     def run(self, attn_events: tuple[torch.cuda.Event, torch.cuda.Event] | None = None,
             merged: torch.Tensor | None = None,
             marks: list[torch.cuda.Event] | None = None) -> torch.Tensor:
-        """One step; `marks` (len(PHASES) + 1 events) are recorded at the phase boundaries."""
+        """One step from the raw projection `merged` (default: the step's own); `marks`
+        (len(phases) + 1 events) are recorded at the phase boundaries."""
 
-        from h3sa.ulysses import pack_qkv_send, unpack_o_recv, unpack_qkv_recv
+        from h3sa.peer import attention_fwd_scatter
+        from h3sa.prologue import qkv_norm_rope_pack, qkv_norm_rope_scatter_paged
+        from h3sa.ulysses import unpack_o_recv, unpack_qkv_recv
 
         h3sa, geo, hl = self.h3sa, self.geo, self.hl
         d, heads = CFG["head_dim"], CFG["heads"]
@@ -339,68 +360,65 @@ class Step:
             if marks is not None:
                 marks[i].record()
 
-        mark(0)
-        if self.fused:
-            from h3sa.peer import attention_fwd_scatter, scatter_qkv_paged
-
-            # Q to the owners' planes, K/V into the owners' caches after the history
-            scatter_qkv_paged(src, self.q_peer, self.kpool_peer, self.vpool_peer, self.table,
-                              dst_start=self.n_hist, num_heads=heads, head_dim=d,
-                              device_error=self.err)
-            mark(1)
-            self.peer_barrier()
-            mark(2)
-            mark(3)
-            mark(4)
+        def attention(fn) -> None:
             if attn_events is not None:
                 attn_events[0].record()
-            attention_fwd_scatter(self.q_peer.tensor, self.kpool, self.vpool, self.table,
-                                  self.problems, self.scale,
-                                  self.out_peer, device_error=self.err)
+            fn()
             if attn_events is not None:
                 attn_events[1].record()
-            mark(5)
-            self.peer_barrier()
-            mark(6)
-            mark(7)
-            return self.final
-        if self.world > 1:
-            pack_qkv_send(src, self.send, world=self.world, num_heads=heads, head_dim=d)
+
+        mark(0)
+        if self.fused:
+            # prologue + Q to the owners' planes + K/V into the owners' caches after the history
+            qkv_norm_rope_scatter_paged(src, self.q_weight, self.k_weight, self.cos_sin,
+                                        self.positions, 1e-5, q=self.q_buf, key_pool=self.k_buf,
+                                        value_pool=self.v_buf, page_table=self.table,
+                                        dst_start=self.n_hist, device_error=self.err)
             mark(1)
-            torch.distributed.all_to_all_single(self.recv, self.send)
+            if self.world > 1:
+                self.peer_barrier()
             mark(2)
-            unpack_qkv_recv(self.recv, self.qkv, world=self.world, tokens=geo["tokens"],
-                            local_heads=hl, head_dim=d)
-        elif merged is not None:
-            self.qkv.copy_(merged.view(geo["rows"], 3, heads, d).permute(1, 0, 2, 3))
-            mark(1)
-            mark(2)
-        else:
-            mark(1)
-            mark(2)
+            if self.world > 1:
+                attention(lambda: attention_fwd_scatter(
+                    self.q_buf.tensor, self.kpool, self.vpool, self.table, self.problems,
+                    self.scale, self.out_buf, device_error=self.err))
+            else:
+                attention(lambda: h3sa.attention_fwd(
+                    self.q_buf.tensor, self.out, self.kpool, self.vpool, self.table,
+                    self.problems, self.scale, device_error=self.err))
+            mark(3)
+            if self.world > 1:
+                self.peer_barrier()
+            mark(4)
+            return self.out_buf.tensor if self.world > 1 else self.out
+        qkv_norm_rope_pack(src, self.q_weight, self.k_weight, self.cos_sin, self.positions, 1e-5,
+                           world=self.world, send=self.send)
+        mark(1)
+        torch.distributed.all_to_all_single(self.recv, self.send)
+        mark(2)
+        unpack_qkv_recv(self.recv, self.qkv, world=self.world, tokens=geo["tokens"],
+                        local_heads=hl, head_dim=d)
         mark(3)
         q, k, v = self.qkv[0], self.qkv[1], self.qkv[2]
         # current chunk's K/V rows (media + pad document) after the history
-        h3sa.kv_copy_rows([k, v], [self.kpool, self.vpool], count=geo["rows"], dst_table=self.table,
-                          dst_start=self.n_hist, device_error=self.err)
+        h3sa.kv_copy_rows([k, v], [self.kpool, self.vpool], count=geo["rows"],
+                          dst_table=self.table, dst_start=self.n_hist, device_error=self.err)
         mark(4)
-        if attn_events is not None:
-            attn_events[0].record()
-        h3sa.attention_fwd(q, self.out, self.kpool, self.vpool, self.table, self.problems,
-                           self.scale, device_error=self.err)
-        if attn_events is not None:
-            attn_events[1].record()
+        attention(lambda: h3sa.attention_fwd(q, self.out, self.kpool, self.vpool, self.table,
+                                             self.problems, self.scale, device_error=self.err))
         mark(5)
-        if self.world > 1:
-            torch.distributed.all_to_all_single(self.orecv, self.out)
-            mark(6)
-            unpack_o_recv(self.orecv, self.final, world=self.world, tokens=geo["tokens"],
-                          local_heads=hl, head_dim=d)
-            mark(7)
-            return self.final
+        torch.distributed.all_to_all_single(self.orecv, self.out)
         mark(6)
+        unpack_o_recv(self.orecv, self.final, world=self.world, tokens=geo["tokens"],
+                      local_heads=hl, head_dim=d)
         mark(7)
-        return self.out
+        return self.final
+
+    def close(self) -> None:
+        if self.world > 1:
+            for b in (self.k_buf, self.v_buf, self.q_buf, self.out_buf):
+                b.close()
+            self.peer_barrier.close()
 
 
 def _time_launch(fn, iters: int) -> float:
@@ -576,10 +594,11 @@ def _comparator_sdpa(step: Step, iters: int = 5) -> dict:
 
     geo, hl, d = step.geo, step.hl, CFG["head_dim"]
     nh, nq = step.n_hist, geo["nq"]
-    q = step.qkv[0][:nq]
+    q = step.q_buf.tensor[:nq]  # the step has run: Q and the chunk's K/V rows are in place
     hist_k = step.kpool[:, :nh].transpose(0, 1).contiguous()
     hist_v = step.vpool[:, :nh].transpose(0, 1).contiguous()
-    cur_k, cur_v = step.qkv[1][:nq], step.qkv[2][:nq]
+    cur_k = step.kpool[:, nh:nh + nq].transpose(0, 1).contiguous()
+    cur_v = step.vpool[:, nh:nh + nq].transpose(0, 1).contiguous()
 
     def call() -> torch.Tensor:
         key = torch.cat((hist_k, cur_k), dim=0)
@@ -603,6 +622,130 @@ def _comparator_sdpa(step: Step, iters: int = 5) -> dict:
     return {"impl": "torch SDPA on this GPU via the reference's sdpa-backend call pattern "
                     "(cat K/V parts + F.scaled_dot_product_attention)",
             "ms_p50": statistics.median(times)}
+
+
+def _copy_loop_ms(run, host_in: torch.Tensor, out_shape, steps: int, world: int,
+                  device: torch.device) -> float:
+    """ms per step of `run(dev_in) -> result` with the step's input uploaded from pinned host
+    memory and its result downloaded into pinned host memory every step, all inside the
+    timed region. Copies run on their own streams, double-buffered: the upload of step i + 1
+    and the download of step i - 1 overlap the compute of step i."""
+
+    host_out = [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    dev_in = [torch.empty(host_in.shape, dtype=host_in.dtype, device=device) for _ in range(2)]
+    dev_out = [torch.empty(out_shape, dtype=torch.bfloat16, device=device) for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
+    ev = {name: [torch.cuda.Event() for _ in range(2)]
+          for name in ("in_ready", "in_free", "out_ready", "out_free")}
+
+    def one(i: int) -> None:
+        k = i % 2
+        h2d.wait_event(ev["in_free"][k])      # compute of step i - 2 is done with dev_in[k]
+        with torch.cuda.stream(h2d):
+            dev_in[k].copy_(host_in, non_blocking=True)
+            ev["in_ready"][k].record(h2d)
+        comp.wait_event(ev["in_ready"][k])
+        res = run(dev_in[k])
+        ev["in_free"][k].record(comp)
+        comp.wait_event(ev["out_free"][k])    # download of step i - 2 is done with dev_out[k]
+        dev_out[k].copy_(res.reshape(out_shape), non_blocking=True)
+        ev["out_ready"][k].record(comp)
+        d2h.wait_event(ev["out_ready"][k])
+        with torch.cuda.stream(d2h):
+            host_out[k].copy_(dev_out[k], non_blocking=True)
+            ev["out_free"][k].record(d2h)
+
+    for i in range(3):
+        one(i)
+    torch.cuda.synchronize()
+    _barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(comp)
+    h2d.wait_stream(comp)
+    for i in range(steps):
+        one(i)
+    b.record(d2h)
+    torch.cuda.synchronize()
+    _barrier(world)
+    return _max_over_ranks(a.elapsed_time(b), world) / steps
+
+
+TEXT_ROWS = 64  # the live document's text condition rows (the hook protocol requires some)
+
+
+def _e2e_hook(step: Step, steps: int, world: int, rank: int, device: torch.device) -> dict:
+    """The drop-in path a maintainer installs, end to end: this rank's raw QKV projection shard
+    from pinned host memory -> h3sa.layer.attention_from_projection (fused_qkv_qk_norm_rope_,
+    Ulysses sequence -> heads, H3StreamingAttentionHook.__call__ writing the chunk into its
+    paged cache and attending, heads -> sequence) -> the out_proj input back to pinned host
+    memory. Packed sequence [64 text | 12384 video + 125 audio | pad]: the hook's live
+    document needs condition rows."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+    from h3sa.layer import PeerUlysses, attention_from_projection
+    from h3sa.ulysses import ParallelContext
+
+    heads, d, nh = CFG["heads"], CFG["head_dim"], CFG["history"]
+    hl = heads // world
+    nq = CFG["video"] + CFG["audio"]
+    used = TEXT_ROWS + nq
+    align = CFG["align"] * world // _gcd(CFG["align"], world)
+    rows = (used + align - 1) // align * align
+    tokens = rows // world
+    g = torch.Generator(device=device).manual_seed(2000 + rank)
+    merged = torch.randn(tokens, 3 * heads * d, device=device, generator=g).to(torch.bfloat16)
+    host_in = merged.cpu().pin_memory()
+    cos_sin = _rope_cache(nh + rows, 96, device)
+    positions = nh + rank * tokens + torch.arange(tokens, device=device)
+    tags = torch.zeros(rows, dtype=torch.long, device=device)
+    tags[:TEXT_ROWS] = 1
+    tags[TEXT_ROWS + CFG["video"]:used] = 2
+    tags[used:] = -1
+    commit = torch.zeros(rows, dtype=torch.bool, device=device)
+    commit[TEXT_ROWS:used] = True
+    cu = (0, used, rows)
+    cache = CleanAVKVCache(KVContract(local_heads=hl, head_dim=d), layer_names=("blocks.0.attn",),
+                           device=device)
+    paged = cache.layer("blocks.0.attn", device)
+    hist = torch.randn(nh, hl, d, device=device, generator=g).to(torch.bfloat16)
+    paged.write(hist, hist, start=0, count=nh)
+    paged.history_rows = nh
+    hook = H3StreamingAttentionHook(cache)
+    hook.activate(HookMode.NOISY)
+
+    class Attn:
+        softmax_scale = d ** -0.5
+
+    ulysses: dict = {}
+    exchange = None
+    if world > 1:
+        exchange = PeerUlysses(tokens, heads, d, device_error=hook.device_error(device))
+        ulysses["exchange"] = exchange
+
+    def run(x: torch.Tensor) -> torch.Tensor:
+        return attention_from_projection(
+            x, q_weight=step.q_weight, k_weight=step.k_weight, rope_cache=(cos_sin, positions),
+            eps=1e-5, num_heads=heads, head_dim=d, hook=hook, attention=Attn(),
+            layer_name="blocks.0.attn", token_tags=tags, commit_mask=commit, cu_seqlens_host=cu,
+            **ulysses)
+
+    ms = _copy_loop_ms(run, host_in, (tokens, heads * d), steps, world, device)
+    hook.check_device_error()
+    if exchange is not None:
+        exchange.close()
+    flops = 4.0 * d * heads * (nq * (nh + nq + TEXT_ROWS) + TEXT_ROWS ** 2 + (rows - used) ** 2)
+    return {"value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms_per_step": ms,
+            "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+            "d2h_bytes_per_step": tokens * heads * d * 2,
+            "api": "h3sa.layer.attention_from_projection: fused_qkv_qk_norm_rope_ -> Ulysses "
+                   + ("peer exchange" if world > 1 else "(SP=1: none)")
+                   + " -> H3StreamingAttentionHook.__call__ -> heads_to_sequence",
+            "workload": f"{TEXT_ROWS} text + {nq} media queries per layer call (media over "
+                        f"[{nh} history | media | text] keys), raw QKV projection in, out_proj "
+                        "input out",
+            "copies": "pinned host buffers, double-buffered on separate H2D / D2H streams"}
 
 
 def run_h3sa(args: argparse.Namespace) -> None:
@@ -641,65 +784,29 @@ def run_h3sa(args: argparse.Namespace) -> None:
     attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
     phases = {name: _max_over_ranks(statistics.median(ev[j].elapsed_time(ev[j + 1]) for ev in phase_ev),
                                     world)
-              for j, name in enumerate(step.phases) if not name.startswith("unused")}
+              for j, name in enumerate(step.phases)}
     step_ms = [a.elapsed_time(b) for a, b in step_ev]
     attn_avg = _max_over_ranks(sum(attn_ms) / len(attn_ms), world)
     p50 = _max_over_ranks(statistics.median(step_ms), world)
     p90 = _max_over_ranks(sorted(step_ms)[int(0.9 * (len(step_ms) - 1))], world)
     err = int(step.err.item())
 
-    # e2e: public API with pinned host input / output each step. Copies run on their own
-    # streams, double-buffered: the upload of step i + 1 and the download of step i - 1
-    # overlap the compute of step i (two copy engines, one per direction).
-    e2e = None
+    # e2e: the drop-in hook path with host buffers (headline), and the kernel-level step of
+    # the timed region with the same copies
+    e2e = e2e_kernels = None
     if not args.no_e2e:
+        e2e = _e2e_hook(step, args.steps, world, rank, device)
         host_in = step.merged.cpu().pin_memory()
-        out_shape = step.final.shape if world > 1 else step.out.shape
-        host_out = [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-        dev_in = [torch.empty_like(step.merged) for _ in range(2)]
-        dev_out = [torch.empty(out_shape, dtype=torch.bfloat16, device=device) for _ in range(2)]
-        comp = torch.cuda.current_stream()
-        h2d, d2h = torch.cuda.Stream(), torch.cuda.Stream()
-        ev = {name: [torch.cuda.Event() for _ in range(2)]
-              for name in ("in_ready", "in_free", "out_ready", "out_free")}
-
-        def e2e_step(i: int) -> None:
-            k = i % 2
-            h2d.wait_event(ev["in_free"][k])      # compute of step i - 2 is done with dev_in[k]
-            with torch.cuda.stream(h2d):
-                dev_in[k].copy_(host_in, non_blocking=True)
-                ev["in_ready"][k].record(h2d)
-            comp.wait_event(ev["in_ready"][k])
-            res = step.run(merged=dev_in[k])
-            ev["in_free"][k].record(comp)
-            comp.wait_event(ev["out_free"][k])    # download of step i - 2 is done with dev_out[k]
-            dev_out[k].copy_(res, non_blocking=True)
-            ev["out_ready"][k].record(comp)
-            d2h.wait_event(ev["out_ready"][k])
-            with torch.cuda.stream(d2h):
-                host_out[k].copy_(dev_out[k], non_blocking=True)
-                ev["out_free"][k].record(d2h)
-
-        for i in range(2):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        _barrier(world)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(comp)
-        h2d.wait_stream(comp)
-        for i in range(args.steps):
-            e2e_step(i)
-        b.record(d2h)
-        torch.cuda.synchronize()
-        _barrier(world)
-        e2e_ms = _max_over_ranks(a.elapsed_time(b), world) / args.steps
+        res = step.run()
+        ms = _copy_loop_ms(lambda x: step.run(merged=x), host_in, tuple(res.shape), args.steps,
+                           world, device)
         total_flops = 4.0 * step.geo["nq"] * step.geo["nk"] * CFG["head_dim"] * CFG["heads"]
-        e2e = {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
-               "ms_per_step": e2e_ms, "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
-               "d2h_bytes_per_step": host_out[0].numel() * host_out[0].element_size(),
-               "api": "h3sa.ulysses + h3sa.kv_copy_rows + h3sa.attention_fwd (C ABI via ctypes)",
-               "copies": "pinned host buffers, double-buffered on separate H2D / D2H streams, "
-                         "overlapping the compute of the neighbouring steps"}
+        e2e_kernels = {"value": total_flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                       "ms_per_step": ms,
+                       "h2d_bytes_per_step": host_in.numel() * host_in.element_size(),
+                       "d2h_bytes_per_step": res.numel() * res.element_size(),
+                       "api": "the timed step's C-ABI calls (fused prologue/exchange/cache "
+                              "append, attention) with host buffers"}
 
     extra = {}
     if rank == 0 and world == 1 and not args.no_comparator:
@@ -718,6 +825,10 @@ def run_h3sa(args: argparse.Namespace) -> None:
     value = total_flops * args.steps / (total_ms * 1e-3) / 1e12
     achieved = step.flops / (attn_avg * 1e-3) / 1e12
     traffic = _ncu_traffic()
+    clk = clocks.summary()
+    if clk.get("sm_mhz"):
+        # time x clock: a kernel bound by the SM clock keeps this product as the clock moves
+        clk["attention_ms_x_sm_mhz"] = attn_avg * clk["sm_mhz"]
     line = {
         "metric": METRIC,
         "value": value,
@@ -733,10 +844,13 @@ def run_h3sa(args: argparse.Namespace) -> None:
         "data": "synthetic",
         "config": {
             "workload": "768p chunk: 12384 video + 125 audio queries x [16384 history + 12509 "
-                        "current] keys, H=24, d=128, dense non-causal",
+                        "current] keys, H=24, d=128, dense non-causal; each step starts from "
+                        "the raw merged QKV projection (QK-RMSNorm + RoPE prologue included)",
             "ulysses_sp": world, "heads_per_gpu": step.hl, "packed_rows": geo["rows"],
             "pad_rows": geo["pad"], "parallelism": f"sp{world}",
-            "exchange": ("peer stores over NVLink (scatter kernel + attention epilogue)" if step.fused
+            "exchange": ("peer stores over NVLink (prologue kernel storing Q and K/V into "
+                         "the owners' planes and caches, attention epilogue storing O)"
+                         if step.fused and world > 1
                          else ("NCCL all_to_all_single + layout copies" if world > 1 else "none")),
             "l2": "inputs larger than L2 (Q 77 MB + K/V pool 355 MB at SP=1)",
         },
@@ -753,8 +867,9 @@ def run_h3sa(args: argparse.Namespace) -> None:
                      "traffic": traffic},
         "cpu_baseline": cpu,
         "e2e": e2e,
+        "e2e_kernel_path": e2e_kernels,
         "gpu_launches": step.launches_per_step * args.steps,
-        "clocks": clocks.summary(),
+        "clocks": clk,
         "device_error": err,
         **extra,
     }
@@ -764,7 +879,7 @@ def run_h3sa(args: argparse.Namespace) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["h3sa", "reference"], default="h3sa")
     ap.add_argument("--no-e2e", action="store_true")

@@ -198,6 +198,27 @@ H3SA_API int h3sa_qkv_norm_rope_pack(const void* qkv, void* send, const void* q_
                                      int32_t head_dim, int32_t world, float eps,
                                      int32_t* device_error, void* stream);
 
+/* The prologue fused with the sequence -> heads exchange and the cache append: this rank's
+ * merged QKV shard [tokens, 3, heads, 128] bf16 (straight from the QKV projection, not
+ * modified) is normalised and rotated, and every row is stored at the rank owning its head:
+ * Q rows into peer_q[owner] (a [world * tokens, heads / world, 128] plane, row
+ * rank * tokens + t), K and V rows into the owner's paged pools peer_key_pool[owner] /
+ * peer_value_pool[owner] ([heads / world, pool_pages * 128, 128] bf16) at logical row
+ * dst_start + rank * tokens + t through page_table (the same on every rank of the group).
+ * world = 1 with this rank's own addresses writes the local plane and cache. A page-table
+ * entry outside the pool sets H3SA_DEVERR_BAD_PAGE and the row is skipped. The caller orders
+ * the stores with the readers (a barrier before attention).
+ * Replaces, in one kernel: fused_qkv_qk_norm_rope_ (T/inference/fused_kernels.py:805-855),
+ * merged_qkv_sequence_to_heads (T/distributed/ulysses.py:103-132) and the cache's copy of the
+ * chunk's K/V (T/streaming/cache.py:133-171). */
+H3SA_API int h3sa_qkv_norm_rope_scatter_paged(
+    const void* qkv, const void* q_weight, const void* k_weight, const void* cos_sin,
+    int32_t cache_rows, int32_t rotary, const int64_t* positions, int32_t tokens, int32_t heads,
+    int32_t head_dim, int32_t world, int32_t rank, const uint64_t* peer_q,
+    const uint64_t* peer_key_pool, const uint64_t* peer_value_pool, int32_t pool_pages,
+    const int32_t* page_table, int32_t table_blocks, int32_t dst_start, float eps,
+    int32_t* device_error, void* stream);
+
 /* Block-sparse selection policy for h3sa_block_mask. */
 typedef struct h3sa_mask_policy {
   int32_t mode;                   /* 0: history top-k, 1: composite */

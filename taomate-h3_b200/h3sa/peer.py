@@ -85,6 +85,23 @@ class PeerBuffer:
             self._local = 0
 
 
+class LocalBuffer:
+    """One rank's tensor in the form the peer kernels take (``peer_table`` of one address,
+    world 1): runs the fused exchange kernels on a single GPU, where every row is local."""
+
+    def __init__(self, tensor: torch.Tensor) -> None:
+        if not tensor.is_cuda or not tensor.is_contiguous():
+            raise ValueError("LocalBuffer needs a contiguous CUDA tensor")
+        self.tensor = tensor
+        self.shape = tuple(int(s) for s in tensor.shape)
+        self.world, self.rank = 1, 0
+        self.addresses = [tensor.data_ptr()]
+        self.peer_table = torch.tensor(self.addresses, dtype=torch.int64, device=tensor.device)
+
+    def close(self) -> None:
+        self.peer_table = None
+
+
 class PeerBarrier:
     """Barrier of the group's ranks over peer memory (``h3sa_peer_barrier``), ordered on the
     stream like a kernel: a few microseconds over NVLink instead of a NCCL all-reduce.
@@ -219,5 +236,5 @@ def attention_fwd_scatter(
          out.rank * heads, ptr(device_error), stream_handle(stream))
 
 
-__all__ = ["PeerBarrier", "PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv",
+__all__ = ["LocalBuffer", "PeerBarrier", "PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv",
            "scatter_qkv_paged"]

@@ -70,4 +70,46 @@ def qkv_norm_rope_pack(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torc
     return send
 
 
-__all__ = ["fused_qkv_qk_norm_rope_", "qkv_norm_rope_pack"]
+
+
+def qkv_norm_rope_scatter_paged(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                                cos_sin_cache: torch.Tensor, positions: torch.Tensor, eps: float,
+                                *, q, key_pool, value_pool, page_table: torch.Tensor,
+                                dst_start: int, device_error: torch.Tensor | None = None,
+                                stream: torch.cuda.Stream | None = None) -> None:
+    """The layer prologue fused with the sequence -> heads exchange and the cache append.
+
+    ``qkv`` is this rank's raw merged projection ``[T, 3*H*d]`` (read only). ``q``,
+    ``key_pool`` and ``value_pool`` are ``h3sa.peer.PeerBuffer`` objects (or
+    ``h3sa.peer.LocalBuffer`` for one GPU): the all-rank Q plane ``[W*T, H/W, d]`` and the
+    paged pools ``[H/W, pages*128, d]`` of every rank. Q rows land in their owners' planes and
+    K/V rows in their owners' caches at logical rows ``dst_start + rank*T + t``.
+    """
+
+    from .kernels import PAGE_ROWS
+
+    tokens, heads, head_dim, cache, positions = _check(qkv, q_weight, k_weight, cos_sin_cache,
+                                                       positions)
+    world, rank = q.world, q.rank
+    if heads % world:
+        raise ValueError("merged QKV heads are not divisible by Ulysses")
+    hl = heads // world
+    if tuple(q.shape) != (world * tokens, hl, head_dim):
+        raise ValueError(f"Q plane must be [{world * tokens}, {hl}, {head_dim}], got {list(q.shape)}")
+    if (tuple(key_pool.shape) != tuple(value_pool.shape) or len(key_pool.shape) != 3
+            or key_pool.shape[0] != hl or key_pool.shape[2] != head_dim
+            or key_pool.shape[1] % PAGE_ROWS):
+        raise ValueError(f"KV pools must both be [{hl}, pages * {PAGE_ROWS}, {head_dim}]")
+    if key_pool.world != world or value_pool.world != world:
+        raise ValueError("Q plane and KV pools must span the same ranks")
+    if page_table.dtype != torch.int32 or not page_table.is_cuda:
+        raise ValueError("page_table must be an int32 CUDA tensor")
+    call("h3sa_qkv_norm_rope_scatter_paged", ptr(qkv), ptr(q_weight.contiguous()),
+         ptr(k_weight.contiguous()), ptr(cache), int(cache.shape[0]), int(cache.shape[1]),
+         ptr(positions), tokens, heads, head_dim, world, rank, ptr(q.peer_table),
+         ptr(key_pool.peer_table), ptr(value_pool.peer_table), int(key_pool.shape[1]) // PAGE_ROWS,
+         ptr(page_table), int(page_table.numel()), int(dst_start), float(eps), ptr(device_error),
+         stream_handle(stream))
+
+
+__all__ = ["fused_qkv_qk_norm_rope_", "qkv_norm_rope_pack", "qkv_norm_rope_scatter_paged"]

@@ -262,3 +262,48 @@ def test_kv_copy_rows_index_and_bounds() -> None:
     h3sa.kv_copy_rows([x], [pool], count=2, src_index=bad, dst_table=table, device_error=err)
     torch.cuda.synchronize()
     assert int(err.item()) & 4
+
+
+@pytest.mark.parametrize("seq,heads,dst_start", [(300, 8, 0), (1000, 24, 130), (37, 3, 1000)])
+def test_prologue_scatter_into_cache_matches_oracle(seq: int, heads: int, dst_start: int) -> None:
+    """The fused prologue + exchange + cache append on one GPU (world 1): Q rows in the plane,
+    K/V rows in the paged pools through a shuffled page table, all bit-exact vs the oracle;
+    pool rows outside the chunk untouched."""
+
+    from h3sa.kernels import PAGE_ROWS
+    from h3sa.peer import LocalBuffer
+    from h3sa.prologue import qkv_norm_rope_scatter_paged
+
+    inp, cs = _prologue_case(seq, heads, seed=5)
+    rng = np.random.default_rng(2)
+    pos = rng.integers(0, cs.shape[0], seq)
+    blocks = (dst_start + seq + PAGE_ROWS - 1) // PAGE_ROWS
+    pages = blocks + 3
+    table = torch.from_numpy(rng.permutation(pages)[:blocks].astype(np.int32)).cuda()
+    fill = 7.0
+    kpool = torch.full((heads, pages * PAGE_ROWS, 128), fill, dtype=torch.bfloat16, device="cuda")
+    vpool = torch.full_like(kpool, fill)
+    q = torch.zeros(seq, heads, 128, dtype=torch.bfloat16, device="cuda")
+    raw = _cuda_bf16(inp["qkv"])
+    before = raw.clone()
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    qkv_norm_rope_scatter_paged(raw, _cuda_bf16(inp["q_weight"]), _cuda_bf16(inp["k_weight"]),
+                                _cuda_bf16(cs), torch.from_numpy(pos).cuda(), 1e-5,
+                                q=LocalBuffer(q), key_pool=LocalBuffer(kpool),
+                                value_pool=LocalBuffer(vpool), page_table=table,
+                                dst_start=dst_start, device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    assert torch.equal(raw, before), "the merged input must be left as it was"
+    ref = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, pos, heads, 128,
+                             1e-5).reshape(seq, 3, heads, 128)
+    assert np.array_equal(q.float().cpu().numpy(), ref[:, 0])
+    tab = table.cpu().numpy()
+    logical = dst_start + np.arange(seq)
+    phys = tab[logical // PAGE_ROWS] * PAGE_ROWS + logical % PAGE_ROWS
+    for pool, plane in ((kpool, 1), (vpool, 2)):
+        host = pool.float().cpu().numpy()
+        assert np.array_equal(host[:, phys].transpose(1, 0, 2), ref[:, plane])
+        untouched = np.ones(pool.shape[1], dtype=bool)
+        untouched[phys] = False
+        assert np.all(host[:, untouched] == fill)

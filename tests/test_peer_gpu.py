@@ -119,6 +119,39 @@ def _worker(rank: int, world: int, rendezvous: str) -> None:
             assert torch.equal(q_peer.tensor, qkv_ref[0]), "q plane differs"
             assert torch.equal(k_peer.tensor, kp_ref), "key cache differs"
             assert torch.equal(v_peer.tensor, vp_ref), "value cache differs"
+        # the prologue fused into the same exchange, from the raw projection: the same planes
+        # and caches as the in-place prologue followed by scatter_qkv_paged
+        from h3sa.prologue import fused_qkv_qk_norm_rope_, qkv_norm_rope_scatter_paged
+
+        gp = torch.Generator(device=dev).manual_seed(55)  # same on every rank
+        wq = (1 + 0.1 * torch.randn(d, device=dev, generator=gp)).to(torch.bfloat16)
+        wk = (1 + 0.1 * torch.randn(d, device=dev, generator=gp)).to(torch.bfloat16)
+        cos_sin = torch.randn(4096, 96, device=dev, generator=gp).to(torch.bfloat16)
+        positions = torch.randint(0, 4096, (tokens,), device=dev, generator=g)
+        post = merged.clone()
+        fused_qkv_qk_norm_rope_(post, wq, wk, cos_sin, positions, 1e-5)
+        kp_ref, vp_ref = pools()
+        k_peer.tensor.copy_(kp_ref)
+        v_peer.tensor.copy_(vp_ref)
+        peer_barrier()
+        scatter_qkv_paged(post, q_peer, k_peer, v_peer, table, dst_start=hist, num_heads=heads,
+                          head_dim=d, device_error=err)
+        peer_barrier()
+        q_ref2, k_ref2, v_ref2 = (b.tensor.clone() for b in (q_peer, k_peer, v_peer))
+        for it in range(2):
+            q_peer.tensor.zero_()
+            k_peer.tensor.copy_(kp_ref)
+            v_peer.tensor.copy_(vp_ref)
+            peer_barrier()
+            qkv_norm_rope_scatter_paged(merged, wq, wk, cos_sin, positions, 1e-5, q=q_peer,
+                                        key_pool=k_peer, value_pool=v_peer, page_table=table,
+                                        dst_start=hist, device_error=err)
+            peer_barrier()
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            assert torch.equal(q_peer.tensor, q_ref2), "fused prologue: q plane differs"
+            assert torch.equal(k_peer.tensor, k_ref2), "fused prologue: key cache differs"
+            assert torch.equal(v_peer.tensor, v_ref2), "fused prologue: value cache differs"
         barrier()
         torch.cuda.synchronize()
         for buf in (qkv_peer, out_peer, q_peer, k_peer, v_peer):
