@@ -127,6 +127,25 @@ H3SA_API int h3sa_attention_fwd_fp8(const void* query, void* out, int32_t rows, 
                            const int32_t* kv_indices, int32_t q_blocks, int32_t kv_index_stride,
                            int32_t* device_error, void* stream);
 
+/* The e4m3 attention over a segmented KV sequence whose parts carry their own per-head
+ * scales: the FP8 history the reference quantises once per committed block plus the current
+ * parts quantised per call, all attended in one pass. block_part (int32 [table_blocks],
+ * device) gives, for every logical KV block, its part index in the low 16 bits and its valid
+ * rows (1..128) in the high 16 bits: every part starts on a 128-row block boundary and the
+ * rows after it in its last block are masked (and should hold finite values, e.g. zeros).
+ * part_k_scale / part_v_scale: fp32 [num_parts, heads]; q_scale fp32 [heads]. Scores use
+ * q_scale * k_scale(part); P carries v_scale(part) / max_part v_scale in its exponent and O is
+ * scaled by that maximum, so the result is exact attention over the dequantised parts.
+ * Replaces the segmented FP8 FlashAttention-3 calls, one per part, and their LSE merge
+ * (F/streaming/attention_hook.py:1015-1066, merge 319-334). */
+H3SA_API int h3sa_attention_fwd_fp8_parts(
+    const void* query, void* out, int32_t rows, int32_t heads, int32_t head_dim,
+    const void* key_pool, const void* value_pool, int32_t pool_pages, const int32_t* page_table,
+    int32_t table_blocks, const h3sa_problem* problems, int32_t num_problems, float softmax_scale,
+    const float* q_scale, const int32_t* block_part, int32_t num_parts, const float* part_k_scale,
+    const float* part_v_scale, const int32_t* kv_num_blocks, const int32_t* kv_indices,
+    int32_t q_blocks, int32_t kv_index_stride, int32_t* device_error, void* stream);
+
 /* Row copies between packed tensors and paged pools (num_tensors pairs, same indexing):
  * for i < count and every head, src row (src_index ? src_index[i] : src_start + i) goes to
  * dst row (dst_index ? dst_index[i] : dst_start + i). row_bytes = head_dim * element size
@@ -166,6 +185,24 @@ H3SA_API int h3sa_quantize_fp8_per_head_noalloc(const void* x, void* y, float* s
 H3SA_API int h3sa_quantize_fp8_pool(const void* pool, void* pool_fp8, float* scale, int32_t heads,
                            int32_t pool_pages, const int32_t* page_table, int32_t table_blocks,
                            int32_t rows, int32_t* device_error, void* stream);
+
+/* The per-head e4m3 quantiser over one part of a row space, the form a segmented FP8 history
+ * needs: rows [src_start, src_start + count) of num_tensors (1 or 2, e.g. K and V) bf16 row
+ * spaces (packed or paged, 256-byte rows) are quantised, each tensor with its own per-head
+ * scale max(amax / 448, 1e-12) over those rows (fp32 [heads] in scale0 / scale1), into e4m3
+ * row spaces (128-byte rows) at [dst_start, dst_start + count). zero_tail != 0 writes zeros
+ * into the destination rows after the part up to the end of its 128-row block (paged
+ * destinations), so the block's unused rows hold finite values. amax_workspace: uint32
+ * [num_tensors * heads] of device memory owned by the caller, cleared on `stream` first; calls
+ * that share it must be ordered. Same arithmetic and results as h3sa_quantize_fp8_per_head on
+ * those rows. Replaces the commit-time quantisation of a history block and the per-call
+ * quantisation of the current parts (F/streaming/cache.py:835-855;
+ * F/streaming/attention_hook.py:1029-1049). */
+H3SA_API int h3sa_quantize_fp8_rows(const h3sa_rows* src, const h3sa_rows* dst,
+                                    int32_t num_tensors, int32_t src_start, int32_t dst_start,
+                                    int32_t count, int32_t heads, float* scale0, float* scale1,
+                                    uint32_t* amax_workspace, int32_t zero_tail,
+                                    int32_t* device_error, void* stream);
 
 /* Generic layout permute of 16-byte-aligned records: for every index (i0, i1, i2, i3) of
  * the row-major space dims[4], copy row_bytes from src + sum(i_k * src_strides[k]) to

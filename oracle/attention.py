@@ -110,3 +110,30 @@ __all__ = [
     "streaming_hook_attention",
     "time_cpu_attention",
 ]
+
+
+def segmented_fp8_attention(query: torch.Tensor, parts: Sequence[tuple], scale: float) -> torch.Tensor:
+    """The segmented FP8 backend (F/streaming/attention_hook.py:1015-1066): Q quantised per
+    head, one FP8 attention per K/V part with that part's own dequantisation scales, the
+    partial outputs merged by their log-sum-exp (``_merge_segmented_flash_attention``,
+    :319-334). ``parts``: (k_bytes, v_bytes, k_scale [H], v_scale [H]) with e4m3 bytes
+    [n, H, d] (numpy uint8). Returns float32 [nq, H, d]."""
+
+    from . import fp8 as ofp8
+    import numpy as np
+
+    q8, q_scale = ofp8.quantize_fp8_e4m3_per_head(query.float().numpy()[None])
+    q = torch.from_numpy(ofp8.dequantize(q8, q_scale)[0])
+    outs, lses = [], []
+    for k8, v8, ks, vs in parts:
+        k = torch.from_numpy(ofp8.e4m3_decode(k8) * np.asarray(ks, np.float32)[None, :, None])
+        v = torch.from_numpy(ofp8.e4m3_decode(v8) * np.asarray(vs, np.float32)[None, :, None])
+        s = torch.einsum("qhd,khd->hqk", q.double(), k.double()) * scale
+        lse = torch.logsumexp(s, dim=-1)                       # [H, nq]
+        p = torch.exp(s - lse[..., None])
+        outs.append(torch.einsum("hqk,khd->qhd", p, v.double()))
+        lses.append(lse)
+    lse = torch.stack(lses, dim=0)                             # [parts, H, nq]
+    weights = torch.exp(lse - torch.logsumexp(lse, dim=0, keepdim=True))
+    merged = sum(o * w.permute(1, 0)[..., None] for o, w in zip(outs, weights))
+    return merged.float()

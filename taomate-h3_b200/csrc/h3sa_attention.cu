@@ -540,7 +540,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       float l_sum = 0.f;
       int c = 0;
       bool ok = true;
-      const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+      uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+      // segmented e4m3 KV: per-block K and V scales (see block_scales)
+      const bool parts = kFp8 && p.block_part != nullptr;
+      float q_sl2 = 0.f, lv_ref = 0.f, v_out = 1.f;
+      if constexpr (kFp8) {
+        v_out = __ldg(p.v_scale + head);
+        if (parts) {
+          q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
+          v_out = part_v_ref(p, head);
+          lv_ref = __log2f(v_out);
+        }
+      }
       // The exponentials of block i of tile 1 follow those of block i of tile 0, and those of
       // block i + 1 of tile 0 follow those of block i of tile 1; a tile that skips a block
       // (block-sparse lists) still takes and passes the turn.
@@ -559,6 +570,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (lane == 0) mbar_arrive(tok_give);
           }
           continue;
+        }
+        BlockScales bs{scale_log2, 0.f, 1.f, kBlockN};
+        if (parts) {
+          bs = block_scales(p, head, b, q_sl2, lv_ref);
+          scale2 = f2_pack(bs.sl2, bs.sl2);
         }
         if (!(ok = mbar_wait(smem_u32(&sm.s_full[t]), c & 1, abort_flag, p.err))) break;
         const bool tr = (warp & 3) == 0 && lane == 0;
@@ -589,9 +605,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const int col0 = b * kBlockN;
         const int lo = pr.kv_lo - col0;  // valid columns [lo, hi)
-        const int hi = pr.kv_hi - col0;
-        // Only the first and last block of a problem can be partial. The flag goes through an
-        // opaque move: otherwise the compiler can see that every per-column condition below
+        const int hi = min(pr.kv_hi - col0, bs.rows);
+        // Only the first and last block of a problem (or of a segmented e4m3 part) can be
+        // partial. The flag goes through an opaque move: otherwise the compiler can see that every per-column condition below
         // implies it, drop the branch and run 2 x 128 compare/selects on every block.
         int partial_i = (lo > 0 || hi < kBlockN) ? 1 : 0;
         asm volatile("" : "+r"(partial_i));
@@ -610,7 +626,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mx3 = fmax3(mx3, s[j + 3], s[j + 7]);
         }
         const float mx = fmaxf(fmax3(mx0, mx1, mx2), mx3);
-        const float m_blk = mx * scale_log2;
+        const float m_blk = mx * bs.sl2;
         const bool need = m_blk > m_used + kRescaleThreshold;
         const float m_new = need ? m_blk : m_used;
         // O is rescaled further down, once the previous PV has completed; l now
@@ -620,7 +636,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         m_used = m_new;
         // x = s * scale_log2 - (m_used - boost) in packed fp32 pairs, then 2^x on the MUFU; P
         // packed for the PV MMA, row sum in fp32.
-        const float bias = kBoost - m_used;
+        const float bias = kBoost - m_used + bs.lr;
         const uint64_t bias2 = f2_pack(bias, bias);
 #pragma unroll
         for (int j = 0; j < kBlockN; j += 2) {
@@ -652,7 +668,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         float sa, sb;
         f2_unpack(sum2, sa, sb);
-        l_sum += sa + sb;
+        l_sum += (sa + sb) * bs.inv;
         if (tr) H3SA_TRACE_AT(i, 5 * t + 3);
         // The previous PV has read P out of shared memory and finished accumulating into O.
         if (c > 0 && !(ok = mbar_wait(smem_u32(&sm.pv_done[t]), (c - 1) & 1, abort_flag, p.err)))
@@ -720,7 +736,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           __threadfence();
         } else {
           float out_scale = any ? 1.0f / l_sum : 0.f;
-          if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+          if constexpr (kFp8) out_scale *= v_out;
           store_tile_rows(sm.q[t] + (warp & 3) * (32 * 128), lane, row_dst(t, row),
                           [&](int ch, float (&v)[32]) {
                             uint32_t r[32];
@@ -781,7 +797,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
-        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        if constexpr (kFp8)
+          out_scale *= p.block_part ? part_v_ref(p, head) : __ldg(p.v_scale + head);
         store_tile_rows(sm.q[t] + (warp & 3) * (32 * 128), lane, row_dst(t, row),
                         [&](int ch, float (&v)[32]) {
 #pragma unroll
@@ -1148,12 +1165,24 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float m_used = -INFINITY;
     float l_sum = 0.f;
     bool ok = true;
-    const uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+    uint64_t scale2 = f2_pack(scale_log2, scale_log2);
+    // segmented e4m3 KV: per-block K and V scales (see block_scales)
+    const bool parts = kFp8 && p.block_part != nullptr;
+    float q_sl2 = 0.f, lv_ref = 0.f;
+    if (parts) {
+      q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
+      lv_ref = __log2f(part_v_ref(p, head));
+    }
     int i = 0;
     for (; i < nblk; ++i) {
       int b;
       next_block(b);
       const bool tr = q == H3SA_TRACE_QUARTER && lane == 0;
+      BlockScales bs{scale_log2, 0.f, 1.f, kBlockN};
+      if (parts) {
+        bs = block_scales(p, head, b, q_sl2, lv_ref);
+        scale2 = f2_pack(bs.sl2, bs.sl2);
+      }
       if (!(ok = mbar_wait(smem_u32(&sm.s_full[i & 1]), (i >> 1) & 1, abort_flag, p.err))) break;
       if (tr) H3SA_TRACE_AT(i, 6 * h + 0);
       tc_fence_after();
@@ -1173,7 +1202,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const int col0 = b * kBlockN + 64 * h;
       const int lo = pr.kv_lo - col0;  // valid columns [lo, hi) of this half
-      const int hi = pr.kv_hi - col0;
+      const int hi = min(pr.kv_hi - col0, bs.rows - 64 * h);
       int partial_i = (lo > 0 || hi < 64) ? 1 : 0;
       asm volatile("" : "+r"(partial_i));
       if (partial_i) {
@@ -1202,7 +1231,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         mx = fmaxf(mh, sm.mx_x[i & 1][h ^ 1][row]);
       }
-      const float m_blk = mx * scale_log2;
+      const float m_blk = mx * bs.sl2;
       const bool need = m_blk > m_used + kRescaleThreshold;
       const float m_new = need ? m_blk : m_used;
       const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
@@ -1211,7 +1240,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       m_used = m_new;
       // a half that has seen no valid score yet (all its columns outside the KV range so far;
       // possible with independent halves) keeps its P at zero instead of -inf + inf
-      const float bias = kBoost - (m_used == -INFINITY ? 0.f : m_used);
+      const float bias = kBoost - (m_used == -INFINITY ? 0.f : m_used) + bs.lr;
       const uint64_t bias2 = f2_pack(bias, bias);
       if (tr) H3SA_TRACE_AT(i, 6 * h + 2);
 #pragma unroll
@@ -1239,7 +1268,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       float sa, sb;
       f2_unpack(sum2, sa, sb);
-      l_sum += sa + sb;
+      l_sum += (sa + sb) * bs.inv;
       if (tr) H3SA_TRACE_AT(i, 6 * h + 3);
       if (any_need) {
         // PV(i - 1) has finished accumulating; rescale this half's O columns
@@ -1347,7 +1376,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __threadfence();
       } else {
         float out_scale = (any && l_fin > 0.f) ? 1.0f / l_fin : 0.f;
-        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        if constexpr (kFp8)
+          out_scale *= p.block_part ? part_v_ref(p, head) : __ldg(p.v_scale + head);
         uint8_t* stage = sm.k[0] + (warp - 4) * (32 * 128);
         auto values = [&](int ch, float (&v)[32]) {
           raw(ch, v);
@@ -1398,7 +1428,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
-        if constexpr (kFp8) out_scale *= __ldg(p.v_scale + head);
+        if constexpr (kFp8)
+          out_scale *= p.block_part ? part_v_ref(p, head) : __ldg(p.v_scale + head);
         uint8_t* stage = sm.k[0] + (warp - 4) * (32 * 128);
         if (h == 0)
           store_tile_rows<0, 1>(stage, lane, row_dst(row), [&](int ch, float (&v)[32]) {
@@ -1525,6 +1556,10 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   prm.q_scale = L.q_scale;
   prm.k_scale = L.k_scale;
   prm.v_scale = L.v_scale;
+  prm.block_part = L.block_part;
+  prm.part_k_scale = L.part_k_scale;
+  prm.part_v_scale = L.part_v_scale;
+  prm.n_parts = L.n_parts;
   prm.kv_num_blocks = L.kv_num_blocks;
   prm.kv_indices = L.kv_indices;
   prm.q_blocks = L.q_blocks;

@@ -86,6 +86,13 @@ struct AttnParams {
   const float* k_scale;
   const float* v_scale;
   float softmax_scale_log2;
+  // Segmented e4m3 KV (null: one K and one V scale per head): block_part[b] of logical KV
+  // block b holds its part index (low 16 bits) and its valid rows (high 16 bits, 1..128; parts
+  // start on block boundaries); part_k_scale / part_v_scale are [n_parts, heads].
+  const int* block_part;
+  const float* part_k_scale;
+  const float* part_v_scale;
+  int n_parts;
   // block-sparse lists in the flex BlockMask layout, used by problems with sparse = 1
   const int* kv_num_blocks;  // [heads, q_blocks]
   const int* kv_indices;     // [heads, q_blocks, kv_stride]
@@ -104,5 +111,33 @@ struct AttnParams {
   int out_heads;
   int out_head0;
 };
+
+// Dequantisation factors of KV block b of a segmented e4m3 sequence for head `head`:
+// S scale (log2 units), log2 of the part's V scale over the head's reference V scale (added
+// to the exponent of P, so P carries the V scale ratio), its inverse factor for the row sum,
+// and the block's valid rows.
+struct BlockScales {
+  float sl2, lr, inv;
+  int rows;
+};
+
+__device__ __forceinline__ BlockScales block_scales(const AttnParams& p, int head, int b,
+                                                    float q_sl2, float lv_ref) {
+  const int e = __ldg(p.block_part + b);
+  const int part = e & 0xFFFF;
+  BlockScales r;
+  r.rows = e >> 16;
+  r.sl2 = q_sl2 * __ldg(p.part_k_scale + part * p.heads + head);
+  r.lr = __log2f(__ldg(p.part_v_scale + part * p.heads + head)) - lv_ref;
+  r.inv = exp2f(-r.lr);
+  return r;
+}
+
+// The head's reference V scale: the largest over the parts (so every part's ratio is <= 1).
+__device__ __forceinline__ float part_v_ref(const AttnParams& p, int head) {
+  float v = 0.f;
+  for (int i = 0; i < p.n_parts; ++i) v = fmaxf(v, __ldg(p.part_v_scale + i * p.heads + head));
+  return v;
+}
 
 }  // namespace h3sa

@@ -239,4 +239,51 @@ int h3sa_attention_fwd_fp8(const void* query, void* out, int32_t rows, int32_t h
   return attention_launch(L, true, static_cast<cudaStream_t>(stream));
 }
 
+int h3sa_attention_fwd_fp8_parts(const void* query, void* out, int32_t rows, int32_t heads,
+                                 int32_t head_dim, const void* key_pool, const void* value_pool,
+                                 int32_t pool_pages, const int32_t* page_table,
+                                 int32_t table_blocks, const h3sa_problem* problems,
+                                 int32_t num_problems, float softmax_scale, const float* q_scale,
+                                 const int32_t* block_part, int32_t num_parts,
+                                 const float* part_k_scale, const float* part_v_scale,
+                                 const int32_t* kv_num_blocks, const int32_t* kv_indices,
+                                 int32_t q_blocks, int32_t kv_index_stride, int32_t* device_error,
+                                 void* stream) {
+  int rc = check_attention_args(query, out, rows, heads, head_dim, key_pool, value_pool,
+                                pool_pages, page_table, table_blocks, problems, num_problems,
+                                kv_num_blocks, kv_indices, q_blocks, kv_index_stride);
+  if (rc) return rc;
+  if (!q_scale || !block_part || !part_k_scale || !part_v_scale)
+    return set_error(H3SA_ERR_INVALID, "fp8 part attention: null scale or part pointer");
+  if (num_parts < 1 || num_parts > 0xFFFF)
+    return set_error(H3SA_ERR_INVALID, "fp8 part attention: %d parts outside [1, 65535]",
+                     num_parts);
+  AttnLaunch L{};
+  L.query = query;
+  L.out = out;
+  L.rows = rows;
+  L.heads = heads;
+  L.key_pool = key_pool;
+  L.value_pool = value_pool;
+  L.pool_pages = pool_pages;
+  L.page_table = page_table;
+  L.table_blocks = table_blocks;
+  L.problems = problems;
+  L.num_problems = num_problems;
+  L.softmax_scale = softmax_scale;
+  L.q_scale = q_scale;
+  L.k_scale = part_k_scale;  // part 0's row; the kernel reads per-block scales instead
+  L.v_scale = part_v_scale;
+  L.block_part = block_part;
+  L.part_k_scale = part_k_scale;
+  L.part_v_scale = part_v_scale;
+  L.n_parts = num_parts;
+  L.kv_num_blocks = kv_num_blocks;
+  L.kv_indices = kv_indices;
+  L.q_blocks = q_blocks;
+  L.kv_stride = kv_index_stride;
+  L.device_error = device_error;
+  return attention_launch(L, true, static_cast<cudaStream_t>(stream));
+}
+
 }  // extern "C"

@@ -36,6 +36,11 @@ struct AttnLaunch {
   const float* q_scale;  // e4m3 path only, [heads]
   const float* k_scale;
   const float* v_scale;
+  // segmented e4m3 KV (see AttnParams): per block part | rows << 16, per (part, head) scales
+  const int32_t* block_part;
+  const float* part_k_scale;
+  const float* part_v_scale;
+  int n_parts;
   const int32_t* kv_num_blocks;
   const int32_t* kv_indices;
   int q_blocks;

@@ -215,6 +215,98 @@ __global__ void __launch_bounds__(256) quant_apply_kernel(const QuantSpace q, co
 }
 
 
+// ------------------------------------------------------------------ per-part e4m3 quantiser
+// Rows [src_start, src_start + count) of up to two bf16 row spaces (packed or paged) are
+// quantised per head, each tensor with its own scale max(amax / 448, 1e-12), into e4m3 row
+// spaces at [dst_start, dst_start + count). With zero_tail, the destination rows after the
+// part up to the end of its last 128-row block are set to zero, so a part that starts on a
+// block boundary leaves finite keys and values in the block's unused rows.
+struct QuantRowsParams {
+  RowsDev src[2];
+  RowsDev dst[2];
+  float* scale[2];      // [heads] per tensor
+  unsigned* amax[2];    // [heads] per tensor: max |x| as float bits, zero before the amax pass
+  int ntensors;
+  int src_start;
+  int dst_start;
+  int count;
+  int tail;             // zero rows after the part (0 without zero_tail)
+  int heads;
+  int* err;
+};
+
+// grid (ceil(count / 256), heads, ntensors): max |x| over 256 rows of one head, merged into
+// the head's amax word with an integer atomic (non-negative floats order like their bits).
+__global__ void __launch_bounds__(256) quant_rows_amax_kernel(const QuantRowsParams p) {
+  const int h = blockIdx.y;
+  const int t = blockIdx.z;
+  const int c = threadIdx.x & 15;
+  float m = 0.f;
+  const int end = min(p.count, static_cast<int>(blockIdx.x + 1) * kQuantChunkRows);
+  for (int i = blockIdx.x * kQuantChunkRows + (threadIdx.x >> 4); i < end; i += 16) {
+    const uint8_t* s = row_address(p.src[t], p.src_start + i, h, p.heads, kHeadDim * 2);
+    if (!s) {
+      if (p.err) atomicOr(p.err, kErrBadIndex);
+      continue;
+    }
+    m = fmaxf(m, bf16_bits_abs_max8(__ldg(reinterpret_cast<const uint4*>(s) + c)));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float red[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float r = red[0];
+    for (int i = 1; i < 8; ++i) r = fmaxf(r, red[i]);
+    atomicMax(p.amax[t] + h, __float_as_uint(r));
+  }
+}
+
+// One thread per 8 values of a (tensor, row, head): quantise with the head's scale, or write
+// zeros in the tail rows; thread (row 0, head h, chunk 0) also stores the scale.
+__global__ void __launch_bounds__(256) quant_rows_apply_kernel(const QuantRowsParams p) {
+  const int rows = p.count + p.tail;
+  const long long per_tensor = static_cast<long long>(rows) * p.heads * 16;
+  const long long total = per_tensor * p.ntensors;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int t = static_cast<int>(idx / per_tensor);
+    const int rem = static_cast<int>(idx - t * per_tensor);
+    const int c = rem & 15;
+    const int rh = rem >> 4;
+    const int h = rh % p.heads;
+    const int i = rh / p.heads;
+    uint8_t* d = row_address(p.dst[t], p.dst_start + i, h, p.heads, kHeadDim);
+    if (!d) {
+      if (p.err) atomicOr(p.err, kErrBadIndex);
+      continue;
+    }
+    if (i >= p.count) {
+      reinterpret_cast<uint2*>(d)[c] = make_uint2(0u, 0u);
+      continue;
+    }
+    const float sc = fmaxf(__fdiv_rn(__uint_as_float(__ldcg(p.amax[t] + h)), kFp8Max), 1.0e-12f);
+    if (i == 0 && c == 0) p.scale[t][h] = sc;
+    const uint8_t* s = row_address(p.src[t], p.src_start + i, h, p.heads, kHeadDim * 2);
+    if (!s) continue;  // reported by the amax pass
+    const float inv = __frcp_rn(sc);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(s) + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      f[2 * k] = __uint_as_float(w[k] << 16);
+      f[2 * k + 1] = __uint_as_float(w[k] & 0xFFFF0000u);
+    }
+    uint2 o;
+    o.x = quant4(f[0], f[1], f[2], f[3], sc, inv);
+    o.y = quant4(f[4], f[5], f[6], f[7], sc, inv);
+    reinterpret_cast<uint2*>(d)[c] = o;
+  }
+}
+
+
 // ------------------------------------------------------------------ layout permutes
 struct PermuteParams {
   const uint8_t* src;
@@ -366,6 +458,57 @@ int h3sa_quantize_fp8_pool(const void* pool, void* pool_fp8, float* scale, int32
   q.page_table = page_table;
   q.table_blocks = table_blocks;
   return quantize_with_scratch(q, scale, device_error, static_cast<cudaStream_t>(stream));
+}
+
+int h3sa_quantize_fp8_rows(const h3sa_rows* src, const h3sa_rows* dst, int32_t num_tensors,
+                           int32_t src_start, int32_t dst_start, int32_t count, int32_t heads,
+                           float* scale0, float* scale1, uint32_t* amax_workspace,
+                           int32_t zero_tail, int32_t* device_error, void* stream) {
+  if (num_tensors < 1 || num_tensors > 2 || !src || !dst || !scale0 || !amax_workspace ||
+      (num_tensors == 2 && !scale1))
+    return set_error(H3SA_ERR_INVALID, "quantize_fp8_rows: invalid tensors or outputs");
+  if (count < 0 || heads <= 0 || heads > kQuantMaxBatchHeads || src_start < 0 || dst_start < 0)
+    return set_error(H3SA_ERR_INVALID, "quantize_fp8_rows: count=%d heads=%d start=%d/%d", count,
+                     heads, src_start, dst_start);
+  QuantRowsParams p;
+  memset(&p, 0, sizeof(p));
+  for (int t = 0; t < num_tensors; ++t) {
+    const h3sa_rows* rs[2] = {&src[t], &dst[t]};
+    RowsDev* rd[2] = {&p.src[t], &p.dst[t]};
+    for (int k = 0; k < 2; ++k) {
+      if (!rs[k]->base || (reinterpret_cast<uintptr_t>(rs[k]->base) & 15))
+        return set_error(H3SA_ERR_INVALID, "quantize_fp8_rows: null or unaligned base");
+      if (rs[k]->extent <= 0 || (rs[k]->paged && (!rs[k]->page_table || rs[k]->table_blocks <= 0)))
+        return set_error(H3SA_ERR_INVALID, "quantize_fp8_rows: bad row space");
+      rd[k]->base = static_cast<uint8_t*>(rs[k]->base);
+      rd[k]->paged = rs[k]->paged ? 1 : 0;
+      rd[k]->extent = rs[k]->extent;
+      rd[k]->page_table = rs[k]->page_table;
+      rd[k]->table_blocks = rs[k]->table_blocks;
+    }
+    p.amax[t] = reinterpret_cast<unsigned*>(amax_workspace) + t * heads;
+  }
+  p.scale[0] = scale0;
+  p.scale[1] = scale1;
+  p.ntensors = num_tensors;
+  p.src_start = src_start;
+  p.dst_start = dst_start;
+  p.count = count;
+  p.heads = heads;
+  p.err = device_error;
+  const int end = dst_start + count;
+  p.tail = (zero_tail && dst[0].paged) ? (kBlockN - end % kBlockN) % kBlockN : 0;
+  if (count == 0) return H3SA_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(amax_workspace, 0, sizeof(uint32_t) * num_tensors * heads, st);
+  if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(amax workspace)", e);
+  const int chunks = (count + kQuantChunkRows - 1) / kQuantChunkRows;
+  quant_rows_amax_kernel<<<dim3(chunks, heads, num_tensors), 256, 0, st>>>(p);
+  const long long work = static_cast<long long>(count + p.tail) * heads * 16 * num_tensors;
+  quant_rows_apply_kernel<<<grid_for(work, 256), 256, 0, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("quantize_fp8_rows launch", e);
+  return H3SA_OK;
 }
 
 int h3sa_permute_rows(const void* src, void* dst, const int64_t* dims, const int64_t* src_strides,

@@ -81,12 +81,20 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
         [_P, _P, _I, _I, _I, _P, _P, _I, _P, _I, ctypes.POINTER(Problem), _I, _F,
          _P, _P, _P, _P, _P, _I, _I, _P, _P],
     ),
+    "h3sa_attention_fwd_fp8_parts": (
+        ctypes.c_int,
+        [_P, _P, _I, _I, _I, _P, _P, _I, _P, _I, ctypes.POINTER(Problem), _I, _F,
+         _P, _P, _I, _P, _P, _P, _P, _I, _I, _P, _P],
+    ),
     "h3sa_kv_copy_rows": (
         ctypes.c_int,
         [ctypes.POINTER(Rows), ctypes.POINTER(Rows), _I, _P, _I, _P, _I, _I, _I, _I, _P, _P],
     ),
     "h3sa_quantize_fp8_per_head": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _I, _P]),
     "h3sa_quantize_fp8_per_head_noalloc": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _I, _P]),
+    "h3sa_quantize_fp8_rows": (
+        ctypes.c_int,
+        [ctypes.POINTER(Rows), ctypes.POINTER(Rows), _I, _I, _I, _I, _I, _P, _P, _P, _I, _P, _P]),
     "h3sa_quantize_fp8_pool": (ctypes.c_int, [_P, _P, _P, _I, _I, _P, _I, _I, _P, _P]),
     "h3sa_qkv_norm_rope": (ctypes.c_int, [_P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _F, _P, _P]),
     "h3sa_qkv_norm_rope_pack": (

@@ -103,6 +103,7 @@ class PagedLayerKV:
         self.pages: list[int] = []
         self.table = torch.zeros(0, dtype=torch.int32, device=device)
         self.history_rows = 0
+        self.fp8: SegmentedFp8History | None = None  # e4m3 history (segmented FP8 caches)
         self._grow(max(1, initial_pages))
 
     def _grow(self, capacity: int) -> None:
@@ -177,6 +178,118 @@ class PagedLayerKV:
         self.history_rows = 0
 
 
+class SegmentedFp8History:
+    """The e4m3 copy of one layer's committed history, one part per commit.
+
+    Each committed block is quantised once, at commit, with its own per-head K and V scales
+    (F/streaming/cache.py:835-855), and keeps them when retention later drops rows from it.
+    Parts are stored in an e4m3 page sequence of their own, each starting on a 128-row block
+    boundary, so every KV block belongs to one part: ``block_part`` holds, per logical block,
+    the part index and the block's valid rows (``part | rows << 16``), the layout
+    ``h3sa_attention_fwd_fp8_parts`` reads. The rows after a part in its last block hold
+    zeros or earlier quantiser outputs, always finite, and are masked by the kernel.
+    """
+
+    def __init__(self, heads: int, head_dim: int, device: torch.device) -> None:
+        self.heads = heads
+        self.store = PagedLayerKV(heads, head_dim, torch.float8_e4m3fn, device)
+        self.starts: list[int] = []   # first logical e4m3 row of each part (block aligned)
+        self.rows: list[int] = []     # rows of each part
+        self.k_scale = torch.zeros(0, heads, dtype=torch.float32, device=device)
+        self.v_scale = torch.zeros(0, heads, dtype=torch.float32, device=device)
+        self.workspace = torch.zeros(2 * heads, dtype=torch.int32, device=device)
+
+    @property
+    def end(self) -> int:
+        """First block-aligned logical row after the last part."""
+
+        if not self.starts:
+            return 0
+        last = self.starts[-1] + self.rows[-1]
+        return (last + PAGE_ROWS - 1) // PAGE_ROWS * PAGE_ROWS
+
+    def block_part(self, extra: list[tuple[int, int]] = ()) -> torch.Tensor:
+        """int32 device table over the store's capacity: the parts plus ``extra`` (start,
+        rows) parts that follow them (their indices continue the numbering)."""
+
+        entries = [0] * self.store.capacity
+        for i, (s0, n) in enumerate(list(zip(self.starts, self.rows)) + list(extra)):
+            for b in range(s0 // PAGE_ROWS, (s0 + n + PAGE_ROWS - 1) // PAGE_ROWS):
+                entries[b] = i | (min(PAGE_ROWS, s0 + n - b * PAGE_ROWS) << 16)
+        table = torch.zeros(self.store.capacity, dtype=torch.int32, device=self.store.device)
+        _upload_pages(table, entries)
+        return table
+
+    def append_part(self, key: torch.Tensor, value: torch.Tensor, *, src_start: int, count: int,
+                    src_table: torch.Tensor | None, k_scale: torch.Tensor,
+                    v_scale: torch.Tensor, start: int | None = None) -> int:
+        """Quantise ``count`` bf16 rows of key/value (paged when ``src_table`` is given) into
+        a part at ``start`` (default: after the last part); scales into ``k_scale`` /
+        ``v_scale`` (fp32 [heads]). Returns the part's start. Does not record the part."""
+
+        from .kernels import quantize_fp8_rows
+
+        s0 = self.end if start is None else start
+        self.store.reserve(s0 + count)
+        quantize_fp8_rows([key, value], [self.store.key, self.store.value], [k_scale, v_scale],
+                          self.workspace, count=count, src_start=src_start, dst_start=s0,
+                          src_table=src_table, dst_table=self.store.table, zero_tail=True)
+        return s0
+
+    def commit_part(self, key: torch.Tensor, value: torch.Tensor, *, src_start: int, count: int,
+                    src_table: torch.Tensor | None) -> None:
+        """Quantise a committed block into a new part with its own scales."""
+
+        ks = torch.empty(1, self.heads, dtype=torch.float32, device=self.store.device)
+        vs = torch.empty_like(ks)
+        s0 = self.append_part(key, value, src_start=src_start, count=count, src_table=src_table,
+                              k_scale=ks[0], v_scale=vs[0])
+        self.starts.append(s0)
+        self.rows.append(count)
+        self.k_scale = torch.cat((self.k_scale, ks))
+        self.v_scale = torch.cat((self.v_scale, vs))
+
+    def retain(self, selection: list[tuple[int, list[int]]]) -> None:
+        """Keep, in order, the given (part, local rows) selections: each becomes a part of its
+        own in fresh block-aligned pages, with its original scales."""
+
+        old_table = self.store.table
+        old_pages = self.store.pages
+        starts, rows, src_rows, dst_rows = [], [], [], []
+        cursor = 0
+        for part, local in selection:
+            if not local:
+                continue
+            starts.append(cursor)
+            rows.append(len(local))
+            src_rows.extend(self.starts[part] + r for r in local)
+            dst_rows.extend(cursor + i for i in range(len(local)))
+            cursor = (cursor + len(local) + PAGE_ROWS - 1) // PAGE_ROWS * PAGE_ROWS
+        keep = [part for part, local in selection if local]
+        new_pages = self.store._take(cursor // PAGE_ROWS)
+        table = torch.zeros(self.store.capacity, dtype=torch.int32, device=self.store.device)
+        _upload_pages(table, new_pages)
+        if src_rows:
+            dev = self.store.device
+            kv_copy_rows([self.store.key, self.store.value], [self.store.key, self.store.value],
+                         count=len(src_rows), src_table=old_table, dst_table=table,
+                         src_index=torch.tensor(src_rows, dtype=torch.int32).pin_memory().to(dev, non_blocking=True),
+                         dst_index=torch.tensor(dst_rows, dtype=torch.int32).pin_memory().to(dev, non_blocking=True))
+        self.store.free.extend(reversed(old_pages))
+        self.store.pages = new_pages
+        self.store.table = table
+        idx = torch.tensor(keep, dtype=torch.long, device=self.store.device)
+        self.k_scale = self.k_scale.index_select(0, idx)
+        self.v_scale = self.v_scale.index_select(0, idx)
+        self.starts, self.rows = starts, rows
+
+    def release(self) -> None:
+        self.store.release()
+        self.starts, self.rows = [], []
+        self.k_scale = self.k_scale[:0]
+        self.v_scale = self.v_scale[:0]
+
+
 def _validate_layer_name(layer_name: str, names: tuple[str, ...]) -> None:
     if layer_name not in names:
         raise KeyError(f"unexpected transformer layer: {layer_name}")
@@ -190,8 +303,12 @@ class CleanAVKVCache:
     """
 
     def __init__(self, contract: KVContract, *, layer_names: tuple[str, ...] = MAIN_LAYER_NAMES,
-                 device: torch.device | str | None = None, initial_pages: int = 8) -> None:
+                 device: torch.device | str | None = None, initial_pages: int = 8,
+                 segmented_fp8_history: bool = False) -> None:
         self.contract = contract
+        # also keep every committed block as an e4m3 part quantised once, at commit
+        # (F/streaming/cache.py:205-211, 835-855)
+        self.segmented_fp8_history = bool(segmented_fp8_history)
         self.layer_names = tuple(layer_names)
         self._device = torch.device(device) if device is not None else None
         self._initial_pages = initial_pages
@@ -240,6 +357,9 @@ class CleanAVKVCache:
             dev = device or self._device or torch.device("cuda", torch.cuda.current_device())
             paged = PagedLayerKV(self.contract.local_heads, self.contract.head_dim,
                                  self.contract.dtype, dev, self._initial_pages)
+            if self.segmented_fp8_history:
+                paged.fp8 = SegmentedFp8History(self.contract.local_heads, self.contract.head_dim,
+                                                dev)
             self._layers[layer_name] = paged
         return paged
 
@@ -343,7 +463,12 @@ class CleanAVKVCache:
             staged = self._staged.pop(layer_name)
             if staged != token_count:
                 raise RuntimeError(f"{layer_name}: staged {staged} rows, expected {token_count}")
-            self._layers[layer_name].history_rows += token_count
+            paged = self._layers[layer_name]
+            if paged.fp8 is not None:
+                # the staged rows sit right after the history: quantise them as one part
+                paged.fp8.commit_part(paged.key, paged.value, src_start=paged.history_rows,
+                                      count=token_count, src_table=paged.table)
+            paged.history_rows += token_count
         self._commit_token_counts.append(token_count)
         self._commit_token_tags.append(self._staged_tags)
         self._block_index += 1
@@ -382,6 +507,8 @@ class CleanAVKVCache:
 
         for paged in self._layers.values():
             paged.release()
+            if paged.fp8 is not None:
+                paged.fp8.release()
         self._commit_token_counts.clear()
         self._commit_token_tags.clear()
         self._block_index = 0
@@ -413,13 +540,20 @@ class CleanAVKVCache:
         if not selected_rows:
             for paged in self._layers.values():
                 paged.release()
+                if paged.fp8 is not None:
+                    paged.fp8.release()
             self._commit_token_counts.clear()
             self._commit_token_tags.clear()
             return
         rows = torch.tensor(selected_rows, dtype=torch.int32)
+        parts = [(block, [i for i, tag in enumerate(self._commit_token_tags[block])
+                          if not video_only or tag == VIDEO_TOKEN_TAG])
+                 for block, video_only in selection]
         for paged in self._layers.values():
             if paged.history_rows:
                 paged.gather(rows)
+            if paged.fp8 is not None and paged.fp8.starts:
+                paged.fp8.retain(parts)
         self._commit_token_counts = selected_counts
         self._commit_token_tags = selected_tags
 

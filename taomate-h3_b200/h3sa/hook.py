@@ -34,11 +34,13 @@ import torch
 
 from . import _lib
 from .cache import CleanAVKVCache
-from .kernels import AttentionProblem, attention_fwd, kv_copy_rows, quantize_fp8_e4m3_per_head, quantize_fp8_pool
+from .kernels import PAGE_ROWS
+from .kernels import (AttentionProblem, attention_fwd, attention_fwd_fp8_parts, kv_copy_rows,
+                      quantize_fp8_e4m3_per_head, quantize_fp8_pool)
 from .peer import attention_fwd_scatter
 
 DENSE_BACKENDS = ("flash_attn_3", "flash_attn3", "sdpa", "h3sa_dense")
-FP8_BACKENDS = ("flash_attn3_fp8_dynamic",)
+FP8_BACKENDS = ("flash_attn3_fp8_dynamic", "flash_attn3_fp8_segmented")
 SPARSE_BACKENDS = ("flex_dynamic_blocksparse",)
 
 
@@ -291,6 +293,9 @@ class H3StreamingAttentionHook:
     def _launch(self, layer_name: str, paged, q_src: torch.Tensor, out: torch.Tensor,
                 problems: list[AttentionProblem], scale: float, n_kv: int, n_hist: int,
                 plan: _DocumentPlan, err: torch.Tensor, exchange=None) -> None:
+        if self.backend == "flash_attn3_fp8_segmented":
+            self._launch_fp8_segmented(paged, q_src, out, problems, scale, n_hist, err)
+            return
         if self.backend in FP8_BACKENDS:
             self._launch_fp8(layer_name, paged, q_src, out, problems, scale, n_kv, err)
             return
@@ -335,6 +340,52 @@ class H3StreamingAttentionHook:
                       v_scale=v_scale, device_error=err)
         out[media.q_lo:media.q_hi].copy_(out_media)
         # condition rows attend to condition K/V only; that tiny call stays in bf16
+        attention_fwd(q_src, out, paged.key, paged.value, paged.table, [cond], scale,
+                      device_error=err)
+        self.launches += 2
+
+
+    def _launch_fp8_segmented(self, paged, q_src: torch.Tensor, out: torch.Tensor,
+                              problems: list[AttentionProblem], scale: float, n_hist: int,
+                              err: torch.Tensor) -> None:
+        """The segmented FP8 backend (F/streaming/attention_hook.py:1015-1066): every committed
+        history block is a part with the scales it was given at commit; the current media rows
+        and the condition rows are quantised now, each as a part of its own; one launch
+        attends over all parts with their own dequantisation (no LSE merge needed)."""
+
+        seg = paged.fp8
+        if seg is None:
+            raise RuntimeError("segmented FP8 attention needs a cache built with "
+                               "segmented_fp8_history=True")
+        media, cond = problems
+        heads = paged.heads
+        n_media = media.q_hi - media.q_lo
+        n_cond = cond.kv_hi - cond.kv_lo
+        n_parts = len(seg.starts)
+        ks = torch.empty(n_parts + 2, heads, dtype=torch.float32, device=q_src.device)
+        vs = torch.empty_like(ks)
+        if n_parts:
+            ks[:n_parts].copy_(seg.k_scale)
+            vs[:n_parts].copy_(seg.v_scale)
+        # current media rows [n_hist, n_hist + n_media) and condition rows [cond.kv_lo, ...) of
+        # the bf16 page sequence -> e4m3 parts after the history parts
+        m0 = seg.append_part(paged.key, paged.value, src_start=n_hist, count=n_media,
+                             src_table=paged.table, k_scale=ks[n_parts], v_scale=vs[n_parts])
+        c0 = (m0 + n_media + PAGE_ROWS - 1) // PAGE_ROWS * PAGE_ROWS
+        seg.append_part(paged.key, paged.value, src_start=cond.kv_lo, count=n_cond,
+                        src_table=paged.table, k_scale=ks[n_parts + 1],
+                        v_scale=vs[n_parts + 1], start=c0)
+        block_part = seg.block_part([(m0, n_media), (c0, n_cond)])
+        q8, q_scale = quantize_fp8_e4m3_per_head(q_src[media.q_lo:media.q_hi].unsqueeze(0))
+        out_media = torch.empty(n_media, *q_src.shape[1:], dtype=torch.bfloat16,
+                                device=q_src.device)
+        attention_fwd_fp8_parts(q8.squeeze(0), out_media, seg.store.key, seg.store.value,
+                                seg.store.table, [AttentionProblem(0, n_media, 0, c0 + n_cond)],
+                                scale, q_scale=q_scale.reshape(-1).contiguous(),
+                                block_part=block_part, part_k_scale=ks, part_v_scale=vs,
+                                device_error=err)
+        out[media.q_lo:media.q_hi].copy_(out_media)
+        # condition rows attend to condition K/V only; that small call stays in bf16
         attention_fwd(q_src, out, paged.key, paged.value, paged.table, [cond], scale,
                       device_error=err)
         self.launches += 2

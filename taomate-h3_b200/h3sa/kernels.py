@@ -313,3 +313,96 @@ def permute_rows(src: torch.Tensor, dst: torch.Tensor, dims: Sequence[int],
     ss = (ctypes.c_int64 * 4)(*[int(x) for x in src_strides])
     ds = (ctypes.c_int64 * 4)(*[int(x) for x in dst_strides])
     call("h3sa_permute_rows", ptr(src), ptr(dst), d, ss, ds, int(row_bytes), stream_handle(stream))
+
+
+def quantize_fp8_rows(
+    src: Sequence[torch.Tensor],
+    dst: Sequence[torch.Tensor],
+    scales: Sequence[torch.Tensor],
+    workspace: torch.Tensor,
+    *,
+    count: int,
+    src_start: int = 0,
+    dst_start: int = 0,
+    src_table: torch.Tensor | None = None,
+    dst_table: torch.Tensor | None = None,
+    zero_tail: bool = False,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> None:
+    """Per-head e4m3 quantisation of rows ``[src_start, src_start + count)`` of each bf16
+    ``src`` (packed ``[rows, heads, 128]`` or paged when ``src_table`` is given) into the
+    matching e4m3 ``dst`` at ``dst_start``; tensor t's scales go to ``scales[t]`` (fp32
+    ``[heads]``). ``workspace``: int32 ``[len(src) * heads]`` scratch owned by the caller.
+    ``zero_tail`` zeroes the paged destination rows after the part up to its block's end."""
+
+    if len(src) != len(dst) or len(src) != len(scales) or not 1 <= len(src) <= 2:
+        raise ValueError("one or two src/dst/scale triples")
+    _require_cuda(*src, *dst, *scales, workspace, src_table, dst_table, device_error)
+    heads = int(src[0].shape[0] if src_table is not None else src[0].shape[1])
+    for t, table, dtype in ((src, src_table, torch.bfloat16), (dst, dst_table, torch.float8_e4m3fn)):
+        for x in t:
+            h = int(x.shape[0] if table is not None else x.shape[1])
+            if x.ndim != 3 or h != heads or int(x.shape[-1]) != HEAD_DIM or x.dtype != dtype:
+                raise RuntimeError("quantize_fp8_rows takes bf16 sources and e4m3 destinations "
+                                   f"with {heads} heads of {HEAD_DIM}")
+    if any(s.dtype != torch.float32 or s.numel() < heads for s in scales):
+        raise RuntimeError("quantize_fp8_rows scales must be float32 with one value per head")
+    if workspace.dtype != torch.int32 or workspace.numel() < len(src) * heads:
+        raise RuntimeError("quantize_fp8_rows workspace must be int32 with len(src) * heads entries")
+    if count == 0:
+        return
+    s_arr = (Rows * len(src))(*[_rows(t, src_table) for t in src])
+    d_arr = (Rows * len(dst))(*[_rows(t, dst_table) for t in dst])
+    call("h3sa_quantize_fp8_rows", s_arr, d_arr, len(src), int(src_start), int(dst_start),
+         int(count), heads, ptr(scales[0]), ptr(scales[1]) if len(scales) > 1 else None,
+         ptr(workspace), 1 if zero_tail else 0, ptr(device_error), stream_handle(stream))
+
+
+def attention_fwd_fp8_parts(
+    query: torch.Tensor,
+    out: torch.Tensor,
+    key_pool: torch.Tensor,
+    value_pool: torch.Tensor,
+    page_table: torch.Tensor,
+    problems: Sequence[AttentionProblem],
+    softmax_scale: float,
+    *,
+    q_scale: torch.Tensor,
+    block_part: torch.Tensor,
+    part_k_scale: torch.Tensor,
+    part_v_scale: torch.Tensor,
+    kv_num_blocks: torch.Tensor | None = None,
+    kv_indices: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> torch.Tensor:
+    """e4m3 attention over a segmented KV sequence: ``block_part[b]`` = part of logical block
+    b | valid rows << 16, ``part_k_scale`` / ``part_v_scale`` fp32 ``[parts, heads]``."""
+
+    _require_cuda(query, out, key_pool, value_pool, page_table, kv_num_blocks, kv_indices,
+                  q_scale, block_part, part_k_scale, part_v_scale)
+    _check_attention_args(query, out, key_pool, value_pool, page_table, kv_num_blocks, kv_indices,
+                          q_scale, q_scale, q_scale)
+    rows, heads, head_dim = (int(s) for s in query.shape)
+    if query.dtype != torch.float8_e4m3fn or key_pool.dtype != torch.float8_e4m3fn:
+        raise RuntimeError("fp8 attention takes e4m3 query and KV pools")
+    if block_part.dtype != torch.int32 or block_part.numel() < page_table.numel():
+        raise RuntimeError("block_part must be int32 with one entry per page-table block")
+    if (part_k_scale.shape != part_v_scale.shape or part_k_scale.ndim != 2
+            or int(part_k_scale.shape[1]) != heads or part_k_scale.dtype != torch.float32
+            or part_v_scale.dtype != torch.float32):
+        raise RuntimeError("part scales must be float32 [parts, heads] with matching shapes")
+    if any(t.device != query.device for t in (block_part, part_k_scale, part_v_scale)):
+        raise RuntimeError("attention tensors must all be on the query's device")
+    q_blocks = stride = 0
+    if kv_num_blocks is not None and kv_indices is not None:
+        q_blocks = int(kv_num_blocks.shape[-1])
+        stride = int(kv_indices.shape[-1])
+    call("h3sa_attention_fwd_fp8_parts", ptr(query), ptr(out), rows, heads, head_dim,
+         ptr(key_pool), ptr(value_pool), int(key_pool.shape[1]) // PAGE_ROWS, ptr(page_table),
+         int(page_table.numel()), _problems(problems), len(problems), float(softmax_scale),
+         ptr(q_scale), ptr(block_part), int(part_k_scale.shape[0]), ptr(part_k_scale),
+         ptr(part_v_scale), ptr(kv_num_blocks), ptr(kv_indices), q_blocks, stride,
+         ptr(device_error), stream_handle(stream))
+    return out

@@ -238,3 +238,64 @@ def test_hook_rejects_like_reference() -> None:
     with pytest.raises(RuntimeError, match="exactly one live document"):
         hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
              value=x["v"], token_tags=x["tags"], commit_mask=two_live, cu_seqlens_host=x["cu"])
+
+
+def test_hook_fp8_segmented_history_matches_merged_oracle() -> None:
+    """Three clean commits with different value ranges build a segmented e4m3 history (each
+    block quantised once at commit with its own scales); retention then keeps block 0's video
+    rows (with block 0's scales) and the recent blocks. A NOISY call attends over the parts plus
+    the current media and condition parts; the media rows must match the reference's
+    segmented backend (one FP8 attention per part, LSE merge) on the same quantised bytes."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+    from oracle import fp8 as ofp8
+
+    heads = 2
+    cache = CleanAVKVCache(KVContract(local_heads=heads, head_dim=128),
+                           layer_names=("blocks.0.attn",), segmented_fp8_history=True)
+    hook = H3StreamingAttentionHook(cache, backend="flash_attn3_fp8_segmented")
+    committed = []
+    for i in range(3):
+        x = _layout(heads, 0, False, seed=20 + i)
+        x["k"] = (x["k"].float() * (1 + i)).bfloat16()
+        x["v"] = (x["v"].float() / (1 + 2 * i)).bfloat16()
+        cache.begin_clean_commit(cache.committed_blocks)
+        hook.activate(HookMode.CLEAN_COMMIT)
+        hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+             value=x["v"], token_tags=x["tags"], commit_mask=x["commit"], cu_seqlens_host=x["cu"])
+        hook.deactivate()
+        cache.commit()
+        media = torch.nonzero(x["commit"]).flatten()
+        committed.append((x["k"][media], x["v"][media], x["tags"][media]))
+    hook.check_device_error()
+    cache.retain_sink_and_recent_commits()  # block 0 keeps its video rows only
+
+    def q8(t: torch.Tensor):
+        q, s = ofp8.quantize_fp8_e4m3_per_head(t.float().cpu().numpy()[None])
+        return q[0], s[0]
+
+    parts = []
+    for i, (k, v, tags) in enumerate(committed):
+        (k8, ks), (v8, vs) = q8(k), q8(v)
+        if i == 0:
+            video = (tags == 0).cpu().numpy()
+            k8, v8 = k8[video], v8[video]
+        parts.append((k8, v8, ks, vs))
+    y = _layout(heads, 0, False, seed=30)
+    hook.activate(HookMode.NOISY)
+    out = hook(attention=Attn(), layer_name="blocks.0.attn", query=y["q"], key=y["k"],
+               value=y["v"], token_tags=y["tags"], commit_mask=y["commit"], cu_seqlens_host=y["cu"])
+    hook.check_device_error()
+    media = torch.arange(16, 304, device="cuda")
+    cond = torch.arange(0, 16, device="cuda")
+    (ck8, cks), (cv8, cvs) = q8(y["k"][cond]), q8(y["v"][cond])
+    (mk8, mks), (mv8, mvs) = q8(y["k"][media]), q8(y["v"][media])
+    ref = oatt.segmented_fp8_attention(y["q"][media].float().cpu(),
+                                       [(ck8, cv8, cks, cvs), *parts, (mk8, mv8, mks, mvs)],
+                                       Attn.softmax_scale)
+    assert rel_l2(out[16:304], ref) <= FP8_TOL
+    # condition rows see condition K/V only (bf16)
+    ref_cond = oatt.attention(y["q"][cond].float().cpu(), y["k"][cond].float().cpu(),
+                              y["v"][cond].float().cpu(), Attn.softmax_scale)
+    assert rel_l2(out[:16], ref_cond) <= BF16_TOL
