@@ -543,14 +543,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint64_t scale2 = f2_pack(scale_log2, scale_log2);
       // segmented e4m3 KV: per-block K and V scales (see block_scales)
       const bool parts = kFp8 && p.block_part != nullptr;
-      float q_sl2 = 0.f, lv_ref = 0.f, v_out = 1.f;
+      float q_sl2 = 0.f;
+      float v_cur = 1.f;  // O is accumulated in units of this V scale
       if constexpr (kFp8) {
-        v_out = __ldg(p.v_scale + head);
-        if (parts) {
-          q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
-          v_out = part_v_ref(p, head);
-          lv_ref = __log2f(v_out);
-        }
+        v_cur = __ldg(p.v_scale + head);
+        if (parts) q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
       }
       // The exponentials of block i of tile 1 follow those of block i of tile 0, and those of
       // block i + 1 of tile 0 follow those of block i of tile 1; a tile that skips a block
@@ -571,9 +568,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           continue;
         }
-        BlockScales bs{scale_log2, 0.f, 1.f, kBlockN};
+        BlockScales bs{scale_log2, v_cur, kBlockN};
         if (parts) {
-          bs = block_scales(p, head, b, q_sl2, lv_ref);
+          bs = block_scales(p, head, b, q_sl2);
           scale2 = f2_pack(bs.sl2, bs.sl2);
         }
         if (!(ok = mbar_wait(smem_u32(&sm.s_full[t]), c & 1, abort_flag, p.err))) break;
@@ -631,12 +628,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const float m_new = need ? m_blk : m_used;
         // O is rescaled further down, once the previous PV has completed; l now
         const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
-        const bool any_need = c > 0 && __any_sync(0xffffffffu, need);
+        // entering a part with another V scale moves O into its units (warp-uniform)
+        float vr = 1.0f;
+        if (parts) {
+          vr = c > 0 ? __fdividef(v_cur, bs.vs) : 1.0f;
+          v_cur = bs.vs;
+        }
+        const bool any_need = c > 0 && (__any_sync(0xffffffffu, need) || vr != 1.0f);
+        const float o_scale = alpha * vr;
         l_sum *= alpha;
         m_used = m_new;
         // x = s * scale_log2 - (m_used - boost) in packed fp32 pairs, then 2^x on the MUFU; P
         // packed for the PV MMA, row sum in fp32.
-        const float bias = kBoost - m_used + bs.lr;
+        const float bias = kBoost - m_used;
         const uint64_t bias2 = f2_pack(bias, bias);
 #pragma unroll
         for (int j = 0; j < kBlockN; j += 2) {
@@ -668,7 +672,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         float sa, sb;
         f2_unpack(sum2, sa, sb);
-        l_sum += (sa + sb) * bs.inv;
+        l_sum += sa + sb;
         if (tr) H3SA_TRACE_AT(i, 5 * t + 3);
         // The previous PV has read P out of shared memory and finished accumulating into O.
         if (c > 0 && !(ok = mbar_wait(smem_u32(&sm.pv_done[t]), (c - 1) & 1, abort_flag, p.err)))
@@ -683,7 +687,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             tmem_wait_ld();
             reg_fence32(o);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * o_scale);
             tmem_st32(tO + ch * 32, o);
           }
           tmem_wait_st();
@@ -710,8 +714,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         // written as zeros (TMEM O was never written)
         const bool any = c > 0;
         if (split_out) {
-          // unnormalised partial of this segment: O (fp32), the row's running maximum (log2
-          // units of the scaled scores) and its sum of P
+          // unnormalised partial of this segment: O (fp32, dequantised: times the V scale of
+          // its units), the row's running maximum (log2 units of the scaled scores) and its
+          // sum of P
           const size_t slot = (static_cast<size_t>(gseg + seg) * 2 + t) * kBlockM + row;
           float4* po = reinterpret_cast<float4*>(p.split_o + slot * kHeadDim);
 #pragma unroll
@@ -727,16 +732,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
 #pragma unroll
             for (int j = 0; j < 8; ++j)
-              po[ch * 8 + j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                           __uint_as_float(r[4 * j + 2]),
-                                           __uint_as_float(r[4 * j + 3]));
+              po[ch * 8 + j] = make_float4(__uint_as_float(r[4 * j]) * v_cur,
+                                           __uint_as_float(r[4 * j + 1]) * v_cur,
+                                           __uint_as_float(r[4 * j + 2]) * v_cur,
+                                           __uint_as_float(r[4 * j + 3]) * v_cur);
           }
           p.split_ml[slot * 2] = any ? m_used : -INFINITY;
           p.split_ml[slot * 2 + 1] = any ? l_sum : 0.f;
           __threadfence();
         } else {
           float out_scale = any ? 1.0f / l_sum : 0.f;
-          if constexpr (kFp8) out_scale *= v_out;
+          if constexpr (kFp8) out_scale *= v_cur;
           store_tile_rows(sm.q[t] + (warp & 3) * (32 * 128), lane, row_dst(t, row),
                           [&](int ch, float (&v)[32]) {
                             uint32_t r[32];
@@ -796,9 +802,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
           }
         }
-        float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
-        if constexpr (kFp8)
-          out_scale *= p.block_part ? part_v_ref(p, head) : __ldg(p.v_scale + head);
+        // the segments' O are already dequantised (see the partial store)
+        const float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
         store_tile_rows(sm.q[t] + (warp & 3) * (32 * 128), lane, row_dst(t, row),
                         [&](int ch, float (&v)[32]) {
 #pragma unroll
@@ -1168,19 +1173,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     uint64_t scale2 = f2_pack(scale_log2, scale_log2);
     // segmented e4m3 KV: per-block K and V scales (see block_scales)
     const bool parts = kFp8 && p.block_part != nullptr;
-    float q_sl2 = 0.f, lv_ref = 0.f;
-    if (parts) {
-      q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
-      lv_ref = __log2f(part_v_ref(p, head));
+    float q_sl2 = 0.f;
+    float v_cur = 1.f;  // O is accumulated in units of this V scale
+    if constexpr (kFp8) {
+      v_cur = __ldg(p.v_scale + head);
+      if (parts) q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
     }
     int i = 0;
     for (; i < nblk; ++i) {
       int b;
       next_block(b);
       const bool tr = q == H3SA_TRACE_QUARTER && lane == 0;
-      BlockScales bs{scale_log2, 0.f, 1.f, kBlockN};
+      BlockScales bs{scale_log2, v_cur, kBlockN};
       if (parts) {
-        bs = block_scales(p, head, b, q_sl2, lv_ref);
+        bs = block_scales(p, head, b, q_sl2);
         scale2 = f2_pack(bs.sl2, bs.sl2);
       }
       if (!(ok = mbar_wait(smem_u32(&sm.s_full[i & 1]), (i >> 1) & 1, abort_flag, p.err))) break;
@@ -1235,12 +1241,19 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const bool need = m_blk > m_used + kRescaleThreshold;
       const float m_new = need ? m_blk : m_used;
       const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
-      const bool any_need = i > 0 && __any_sync(0xffffffffu, need);
+      // entering a part with another V scale moves O into its units (warp-uniform)
+      float vr = 1.0f;
+      if (parts) {
+        vr = i > 0 ? __fdividef(v_cur, bs.vs) : 1.0f;
+        v_cur = bs.vs;
+      }
+      const bool any_need = i > 0 && (__any_sync(0xffffffffu, need) || vr != 1.0f);
+      const float o_scale = alpha * vr;
       l_sum *= alpha;
       m_used = m_new;
       // a half that has seen no valid score yet (all its columns outside the KV range so far;
       // possible with independent halves) keeps its P at zero instead of -inf + inf
-      const float bias = kBoost - (m_used == -INFINITY ? 0.f : m_used) + bs.lr;
+      const float bias = kBoost - (m_used == -INFINITY ? 0.f : m_used);
       const uint64_t bias2 = f2_pack(bias, bias);
       if (tr) H3SA_TRACE_AT(i, 6 * h + 2);
 #pragma unroll
@@ -1268,7 +1281,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       float sa, sb;
       f2_unpack(sum2, sa, sb);
-      l_sum += (sa + sb) * bs.inv;
+      l_sum += sa + sb;
       if (tr) H3SA_TRACE_AT(i, 6 * h + 3);
       if (any_need) {
         // PV(i - 1) has finished accumulating; rescale this half's O columns
@@ -1286,7 +1299,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           tmem_wait_ld();
           reg_fence32(o);
 #pragma unroll
-          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * alpha);
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * o_scale);
           tmem_st32(addr, o);
         }
       }
@@ -1366,8 +1379,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           float v[32];
           raw(2 * h + ch, v);
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            po[ch * 8 + j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+          for (int j = 0; j < 8; ++j)  // dequantised: times the V scale of O's units
+            po[ch * 8 + j] = make_float4(v[4 * j] * v_cur, v[4 * j + 1] * v_cur,
+                                         v[4 * j + 2] * v_cur, v[4 * j + 3] * v_cur);
         }
         if (h == 0) {
           p.split_ml[slot * 2] = any ? m_fin : -INFINITY;
@@ -1376,8 +1390,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         __threadfence();
       } else {
         float out_scale = (any && l_fin > 0.f) ? 1.0f / l_fin : 0.f;
-        if constexpr (kFp8)
-          out_scale *= p.block_part ? part_v_ref(p, head) : __ldg(p.v_scale + head);
+        if constexpr (kFp8) out_scale *= v_cur;
         uint8_t* stage = sm.k[0] + (warp - 4) * (32 * 128);
         auto values = [&](int ch, float (&v)[32]) {
           raw(ch, v);
@@ -1427,9 +1440,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
           }
         }
-        float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
-        if constexpr (kFp8)
-          out_scale *= p.block_part ? part_v_ref(p, head) : __ldg(p.v_scale + head);
+        // the segments' O are already dequantised (see the partial store)
+        const float out_scale = lsum > 0.f ? 1.0f / lsum : 0.f;
         uint8_t* stage = sm.k[0] + (warp - 4) * (32 * 128);
         if (h == 0)
           store_tile_rows<0, 1>(stage, lane, row_dst(row), [&](int ch, float (&v)[32]) {

@@ -112,32 +112,24 @@ struct AttnParams {
   int out_head0;
 };
 
-// Dequantisation factors of KV block b of a segmented e4m3 sequence for head `head`:
-// S scale (log2 units), log2 of the part's V scale over the head's reference V scale (added
-// to the exponent of P, so P carries the V scale ratio), its inverse factor for the row sum,
-// and the block's valid rows.
+// Dequantisation factors of KV block b of a segmented e4m3 sequence for head `head`: the S
+// scale (log2 units), the part's V scale and the block's valid rows. P stays unscaled; the
+// softmax keeps O in units of the current part's V scale and rescales it by v_prev / v_new
+// when the walk enters a part with another scale (parts are contiguous runs of blocks).
 struct BlockScales {
-  float sl2, lr, inv;
+  float sl2, vs;
   int rows;
 };
 
 __device__ __forceinline__ BlockScales block_scales(const AttnParams& p, int head, int b,
-                                                    float q_sl2, float lv_ref) {
+                                                    float q_sl2) {
   const int e = __ldg(p.block_part + b);
   const int part = e & 0xFFFF;
   BlockScales r;
   r.rows = e >> 16;
   r.sl2 = q_sl2 * __ldg(p.part_k_scale + part * p.heads + head);
-  r.lr = __log2f(__ldg(p.part_v_scale + part * p.heads + head)) - lv_ref;
-  r.inv = exp2f(-r.lr);
+  r.vs = __ldg(p.part_v_scale + part * p.heads + head);
   return r;
-}
-
-// The head's reference V scale: the largest over the parts (so every part's ratio is <= 1).
-__device__ __forceinline__ float part_v_ref(const AttnParams& p, int head) {
-  float v = 0.f;
-  for (int i = 0; i < p.n_parts; ++i) v = fmaxf(v, __ldg(p.part_v_scale + i * p.heads + head));
-  return v;
 }
 
 }  // namespace h3sa
