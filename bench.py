@@ -436,7 +436,101 @@ def _time_launch(fn, iters: int) -> float:
     return a.elapsed_time(b) / iters
 
 
-VARIANTS = ("fp8", "sparse", "480p")
+VARIANTS = ("fp8", "sparse", "480p", "feeders")
+
+
+def feeders(peaks: dict, iters: int = 20) -> dict:
+    """Device time and HBM throughput of the kernels that feed the attention, at the shapes
+    of the benchmark's configurations (algorithmic bytes: every byte read and written once):
+
+    * prologue_scatter_768p_sp1: the fused QK-RMSNorm + RoPE prologue storing Q into the
+      attention plane and K/V into the paged cache, from the raw 12544-row x 24-head merged
+      projection (read 231 MB, write 231 MB);
+    * prologue_in_place_768p: the drop-in in-place prologue (Q/K read and written: 154 MB each);
+    * cache_append_768p: the current chunk's K/V rows into the paged cache (154 MB each way);
+    * fp8_parts_1080p: per-part e4m3 quantisation of the current chunk's K and V at the 1080p
+      per-GPU shape (24605 rows x 3 heads; amax pass + quantise pass: read 2 x 37.8 MB,
+      write 18.9 MB);
+    * composite_mask_768p_sp8: the block-sparse mask for 3 heads of the 768p chunk (block
+      means of Q and K, scores, selection)."""
+
+    import h3sa
+    from h3sa.block_sparse import composite_block_mask
+    from h3sa.kernels import PAGE_ROWS, quantize_fp8_rows
+    from h3sa.peer import LocalBuffer
+    from h3sa.prologue import fused_qkv_qk_norm_rope_, qkv_norm_rope_scatter_paged
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(11)
+    heads, d, nh = CFG["heads"], CFG["head_dim"], CFG["history"]
+    geo = _geometry(1)
+    rows = geo["rows"]
+    hbm = peaks["hbm"]
+    out = {}
+
+    def entry(name: str, ms: float, nbytes: float, **extra) -> None:
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": ms, "bytes": nbytes, "gb_s": gbs, "frac_of_hbm": gbs / hbm, **extra}
+
+    merged = torch.randn(rows, 3 * heads * d, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    cs = _rope_cache(nh + rows, 96, dev)
+    pos = nh + torch.arange(rows, device=dev)
+    pages = (nh + rows + PAGE_ROWS - 1) // PAGE_ROWS
+    table = torch.arange(pages, dtype=torch.int32, device=dev)
+    kp = LocalBuffer(torch.zeros(heads, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=dev))
+    vp = LocalBuffer(torch.zeros_like(kp.tensor))
+    qb = LocalBuffer(torch.zeros(rows, heads, d, dtype=torch.bfloat16, device=dev))
+    ms = _time_launch(lambda: qkv_norm_rope_scatter_paged(
+        merged, w, w, cs, pos, 1e-5, q=qb, key_pool=kp, value_pool=vp, page_table=table,
+        dst_start=nh), iters)
+    entry("prologue_scatter_768p_sp1", ms, 2.0 * merged.numel() * 2)
+    work = merged.clone()
+    ms = _time_launch(lambda: fused_qkv_qk_norm_rope_(work, w, w, cs, pos, 1e-5), iters)
+    entry("prologue_in_place_768p", ms, 2.0 * 2 * rows * heads * d * 2)
+    k = torch.randn(rows, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn_like(k)
+    ms = _time_launch(lambda: h3sa.kv_copy_rows([k, v], [kp.tensor, vp.tensor], count=rows,
+                                                dst_table=table, dst_start=nh), iters)
+    entry("cache_append_768p", ms, 2.0 * 2 * k.numel() * 2)
+    del merged, work, k, v, kp, vp, qb
+    torch.cuda.empty_cache()
+
+    n8, h8 = 24480 + 125, 3
+    k = torch.randn(n8, h8, d, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn_like(k)
+    p8 = (n8 + PAGE_ROWS - 1) // PAGE_ROWS
+    t8 = torch.arange(p8, dtype=torch.int32, device=dev)
+    k8 = torch.zeros(h8, p8 * PAGE_ROWS, d, dtype=torch.float8_e4m3fn, device=dev)
+    v8 = torch.zeros_like(k8)
+    sc = torch.empty(2, h8, dtype=torch.float32, device=dev)
+    ws = torch.empty(2 * h8, dtype=torch.int32, device=dev)
+    ms = _time_launch(lambda: quantize_fp8_rows([k, v], [k8, v8], [sc[0], sc[1]], ws, count=n8,
+                                                dst_table=t8, zero_tail=True), iters)
+    entry("fp8_parts_1080p", ms, 2.0 * k.numel() * 2 * 2 + 2.0 * k.numel())
+    del k, v, k8, v8
+    torch.cuda.empty_cache()
+
+    import types
+
+    h3, nq = 3, geo["nq"]
+    nk = nh + nq
+    q = torch.randn(nq, h3, d, device=dev, generator=g).to(torch.bfloat16)
+    kk = torch.randn(nk, h3, d, device=dev, generator=g).to(torch.bfloat16)
+    pk = (nk + PAGE_ROWS - 1) // PAGE_ROWS
+    tk = torch.arange(pk, dtype=torch.int32, device=dev)
+    kpool = torch.zeros(h3, pk * PAGE_ROWS, d, dtype=torch.bfloat16, device=dev)
+    h3sa.kv_copy_rows([kk], [kpool], count=nk, dst_table=tk)
+    qa = torch.zeros((nq + PAGE_ROWS - 1) // PAGE_ROWS, dtype=torch.uint8, device=dev)
+    qa[CFG["video"] // PAGE_ROWS:] = 1
+    ka = torch.zeros(pk, dtype=torch.uint8, device=dev)
+    ka[(nh + CFG["video"]) // PAGE_ROWS:] = 1
+    paged = types.SimpleNamespace(key=kpool, table=tk)
+    ms = _time_launch(lambda: composite_block_mask(q, paged, q_lo=0, q_hi=nq, n_hist=nh, n_kv=nk,
+                                                   q_block_audio=qa, kv_block_audio=ka,
+                                                   density=0.25), iters)
+    entry("composite_mask_768p_sp8", ms, float(q.numel() * 2 + nk * h3 * d * 2))
+    return out
 
 
 def _variants(peaks: dict, iters: int = 10, only: str | None = None) -> dict:
@@ -469,6 +563,8 @@ def _variants(peaks: dict, iters: int = 10, only: str | None = None) -> dict:
         return kp, vp, table
 
     out = {}
+    if only == "feeders":
+        return {"feeders": feeders(peaks, iters)}
     for name, fn in (("fp8", _variant_fp8), ("sparse", _variant_sparse), ("480p", _variant_480p)):
         if only in (None, name):
             out.update(fn(peaks, iters, dev, g, pools))

@@ -80,6 +80,29 @@ __device__ __forceinline__ __nv_bfloat16* dst_row(const PrologueParams& p, int t
                     kHeadDim;
 }
 
+// RN32(1 / sqrt(x)) as the arithmetic above defines it (square root and division in IEEE fp64,
+// one rounding to fp32), without the fp64 square root and division in the common case. Two
+// Newton steps y <- y (3/2 - x y^2 / 2) in fp64 from the fp32 hardware estimate leave y within
+// a few fp64 ulps of 1/sqrt(x), as is the fp64 expression itself; both then round to the same
+// fp32 value unless they lie within 2^-46 (relative) of a midpoint between two fp32 values,
+// and in that case the fp64 expression is evaluated (Ziv's rounding test).
+__device__ __forceinline__ float rsqrt_rn32(float xf) {
+  if (isinf(xf)) return 0.f;
+  const double x = xf;
+  double y = rsqrtf(xf);
+  const double hx = 0.5 * x;
+#pragma unroll
+  for (int it = 0; it < 2; ++it) y = fma(y, fma(-hx * y, y, 0.5), y);
+  const float f = static_cast<float>(y);
+  const int bits = __float_as_int(f);
+  const double lo = 0.5 * (static_cast<double>(__int_as_float(bits - 1)) + f);
+  const double hi = 0.5 * (static_cast<double>(__int_as_float(bits + 1)) + f);
+  const double margin = y * 0x1p-46;
+  if (fabs(y - lo) < margin || fabs(y - hi) < margin)
+    return static_cast<float>(1.0 / sqrt(x));
+  return f;
+}
+
 // RMSNorm + rotate-half RoPE of one Q or K row held by a half-warp (8 values per lane, lane
 // `sub` holds dims [8 sub, 8 sub + 8)). c/sn: this lane's cos/sin values of the token
 // (rotating lanes only). Returns the lane's 8 output values packed as bf16.
@@ -101,7 +124,7 @@ __device__ __forceinline__ uint4 norm_rope_row(uint4 raw, const float (&w)[8], f
   for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o, 16);
   // mean of the exact sum (scaling by 1/128 is exact), eps added in fp32
   const float var = static_cast<float>(ss * (1.0 / kHeadDim));
-  const float inv = static_cast<float>(1.0 / sqrt(static_cast<double>(__fadd_rn(var, eps))));
+  const float inv = rsqrt_rn32(__fadd_rn(var, eps));
   float n[8];
 #pragma unroll
   for (int e = 0; e < 8; ++e) n[e] = bf16r(__fmul_rn(__fmul_rn(v[e], inv), w[e]));
