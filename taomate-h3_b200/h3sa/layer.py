@@ -150,7 +150,7 @@ def attention_from_projection(
                       token_tags=token_tags, commit_mask=commit_mask,
                       cu_seqlens_host=cu_seqlens_host)
         if ulysses:
-            output = heads_to_sequence(output, context=context)
+            output = heads_to_sequence(output, context=context, num_heads=num_heads)
     return output.reshape(tokens, num_heads * head_dim)
 
 

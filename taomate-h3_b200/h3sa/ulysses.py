@@ -1,7 +1,9 @@
 """Ulysses sequence<->head exchange on NCCL with h3sa layout kernels.
 
 Mirrors T/distributed/ulysses.py:10-139 (same functions, arguments, errors and result
-layouts). The permute+contiguous copies the reference wraps around each
+layouts) with FL2AV's head padding (F/distributed/ulysses.py:94-251): when the heads do not
+divide by the Ulysses world, every rank receives ceil(H/W) heads and the missing ones are
+zero; ``heads_to_sequence(..., num_heads=H)`` drops them again. The permute+contiguous copies the reference wraps around each
 ``all_to_all_single`` are done by ``h3sa_permute_rows`` (one 16-byte-vectorised pass each);
 the exchange itself is NCCL over NVLink through ``torch.distributed``.
 
@@ -51,17 +53,41 @@ def _require_dist(context: ParallelContext) -> None:
         raise RuntimeError("Ulysses process group is absent")
 
 
+def _tail(t: torch.Tensor, byte_offset: int) -> torch.Tensor:
+    """Flat view of a contiguous tensor from ``byte_offset`` on (the permute kernel addresses
+    records by byte strides from the view's start)."""
+
+    return t.reshape(-1)[byte_offset // t.element_size():]
+
+
+def _shards(num_heads: int, world: int) -> tuple[int, int, int]:
+    """(heads per rank, ranks whose shard holds only real heads, real heads of the next rank):
+    with H % W != 0 every rank gets ceil(H/W) heads and the missing ones are zero padding
+    (F/distributed/ulysses.py:218-222)."""
+
+    hl = -(-num_heads // world)
+    full = num_heads // hl
+    return hl, full, num_heads - full * hl
+
+
 def pack_qkv_send(merged: torch.Tensor, send: torch.Tensor, *, world: int, num_heads: int,
                   head_dim: int) -> None:
-    """merged ``[T, 3, W, Hl, d]`` -> send ``[W, 3, T, Hl, d]``."""
+    """merged ``[T, 3, H, d]`` -> send ``[W, 3, T, Hl, d]`` (Hl = ceil(H/W); padded heads
+    zero)."""
 
     tokens = int(merged.shape[0])
-    hl = num_heads // world
+    hl, full, rest = _shards(num_heads, world)
     rb = head_dim * merged.element_size()
-    # index space (W, 3, T, Hl); strides in bytes
+    if full < world:
+        send.zero_()
+    # index space (W, 3, T, heads of the shard); strides in bytes
     src = (hl * rb, num_heads * rb, 3 * num_heads * rb, rb)
     dst = (3 * tokens * hl * rb, tokens * hl * rb, hl * rb, rb)
-    permute_rows(merged, send, (world, 3, tokens, hl), src, dst, rb)
+    if full:
+        permute_rows(merged, send, (full, 3, tokens, hl), src, dst, rb)
+    if rest:
+        permute_rows(_tail(merged, full * hl * rb), _tail(send, full * dst[0]),
+                     (1, 3, tokens, rest), src, dst, rb)
 
 
 def unpack_qkv_recv(recv: torch.Tensor, out: torch.Tensor, *, world: int, tokens: int,
@@ -76,23 +102,33 @@ def unpack_qkv_recv(recv: torch.Tensor, out: torch.Tensor, *, world: int, tokens
 
 
 def unpack_o_recv(recv: torch.Tensor, out: torch.Tensor, *, world: int, tokens: int,
-                  local_heads: int, head_dim: int) -> None:
-    """recv ``[W, T, Hl, d]`` (head shards) -> out ``[T, W*Hl, d]``."""
+                  local_heads: int, head_dim: int, num_heads: int | None = None) -> None:
+    """recv ``[W, T, Hl, d]`` (head shards) -> out ``[T, H, d]``, H = ``num_heads`` (default
+    W*Hl): the zero padding of the last shards is dropped."""
 
     rb = head_dim * recv.element_size()
     hl = local_heads
+    heads = world * hl if num_heads is None else int(num_heads)
+    full, rest = heads // hl, heads % hl
     src = (tokens * hl * rb, hl * rb, rb, 0)                            # (W, T, Hl, 1)
-    dst = (hl * rb, world * hl * rb, rb, 0)
-    permute_rows(recv, out, (world, tokens, hl, 1), src, dst, rb)
+    dst = (hl * rb, heads * rb, rb, 0)
+    if full:
+        permute_rows(recv, out, (full, tokens, hl, 1), src, dst, rb)
+    if rest:
+        permute_rows(_tail(recv, full * src[0]), _tail(out, full * dst[0]), (1, tokens, rest, 1),
+                     src, dst, rb)
 
 
 def _all_to_all_swap(value: torch.Tensor, *, world_size: int, group: object,
-                     sequence_to_heads: bool) -> torch.Tensor:
+                     sequence_to_heads: bool, num_heads: int | None = None) -> torch.Tensor:
     """Swap sequence and head shards with one all-to-all (T/distributed/ulysses.py:10-55)."""
 
     if sequence_to_heads:
-        if value.ndim < 3 or int(value.shape[-2]) % world_size:
+        if value.ndim < 3:
             raise ValueError("Ulysses input heads must be divisible by its world size")
+        padding = (-int(value.shape[-2])) % world_size
+        if padding:  # zero heads up to a multiple of the world (F/distributed/ulysses.py:107-110)
+            value = torch.nn.functional.pad(value, (0, 0, 0, padding))
         if value.ndim != 3:
             packed = value.contiguous()
             lead = packed.shape[:-3]
@@ -119,17 +155,33 @@ def _all_to_all_swap(value: torch.Tensor, *, world_size: int, group: object,
     send = value.contiguous()
     recv = torch.empty_like(send)
     torch.distributed.all_to_all_single(recv, send, group=group)
-    out = torch.empty(tokens, world_size * hl, d, dtype=value.dtype, device=value.device)
-    unpack_o_recv(recv, out, world=world_size, tokens=tokens, local_heads=hl, head_dim=d)
+    heads = world_size * hl if num_heads is None else int(num_heads)
+    out = torch.empty(tokens, heads, d, dtype=value.dtype, device=value.device)
+    unpack_o_recv(recv, out, world=world_size, tokens=tokens, local_heads=hl, head_dim=d,
+                  num_heads=heads)
     return out
 
 
-def heads_to_sequence(value: torch.Tensor, *, context: ParallelContext) -> torch.Tensor:
-    """Inverse of sequence_to_heads (T/distributed/ulysses.py:77-84)."""
+def sequence_to_heads(value: torch.Tensor, *, context: ParallelContext) -> torch.Tensor:
+    """Trade Ulysses-local sequence rows for attention heads (F/distributed/ulysses.py:119-127);
+    heads are zero-padded to a multiple of the world first."""
+
+    if context.ulysses_world_size == 1:
+        return value
+    _require_dist(context)
+    return _all_to_all_swap(value, world_size=context.ulysses_world_size,
+                            group=context.ulysses_group, sequence_to_heads=True)
+
+
+def heads_to_sequence(value: torch.Tensor, *, context: ParallelContext,
+                      num_heads: int | None = None) -> torch.Tensor:
+    """Inverse of sequence_to_heads (T/distributed/ulysses.py:77-84); ``num_heads`` drops the
+    zero-padded heads of the last shards (F/distributed/ulysses.py:130-156)."""
 
     _require_dist(context)
     return _all_to_all_swap(value, world_size=context.ulysses_world_size,
-                            group=context.ulysses_group, sequence_to_heads=False)
+                            group=context.ulysses_group, sequence_to_heads=False,
+                            num_heads=num_heads)
 
 
 def packed_qkv_sequence_to_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *,
@@ -141,15 +193,15 @@ def packed_qkv_sequence_to_heads(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
     _require_dist(context)
     world = context.ulysses_world_size
     tokens, heads, d = (int(s) for s in q.shape)
-    if heads % world:
-        raise ValueError("Ulysses input heads must be divisible by its world size")
     merged = torch.stack((q, k, v), dim=1).reshape(tokens, 3 * heads * d)
     return merged_qkv_sequence_to_heads(merged, num_heads=heads, head_dim=d, context=context)
 
 
 def merged_qkv_sequence_to_heads(value: torch.Tensor, *, num_heads: int, head_dim: int,
                                  context: ParallelContext) -> tuple[torch.Tensor, ...]:
-    """Send an already merged QKV allocation through Ulysses (T/distributed/ulysses.py:103-132)."""
+    """Send an already merged QKV allocation through Ulysses (T/distributed/ulysses.py:103-132);
+    with H % W != 0 every rank receives ceil(H/W) heads, the missing ones zero
+    (F/distributed/ulysses.py:193-251)."""
 
     world_size = context.ulysses_world_size
     tokens = int(value.shape[0])
@@ -158,10 +210,8 @@ def merged_qkv_sequence_to_heads(value: torch.Tensor, *, num_heads: int, head_di
     packed = value.view(tokens, 3, num_heads, head_dim)
     if world_size == 1:
         return tuple(packed.unbind(dim=1))
-    if num_heads % world_size:
-        raise ValueError("merged QKV heads are not divisible by Ulysses")
     _require_dist(context)
-    hl = num_heads // world_size
+    hl = -(-num_heads // world_size)  # zero-padded shards when H % W != 0
     send = torch.empty(world_size, 3, tokens, hl, head_dim, dtype=value.dtype, device=value.device)
     pack_qkv_send(value.contiguous(), send, world=world_size, num_heads=num_heads, head_dim=head_dim)
     recv = torch.empty_like(send)
@@ -176,6 +226,7 @@ __all__ = [
     "heads_to_sequence",
     "merged_qkv_sequence_to_heads",
     "packed_qkv_sequence_to_heads",
+    "sequence_to_heads",
     "pack_qkv_send",
     "unpack_o_recv",
     "unpack_qkv_recv",

@@ -4,7 +4,7 @@ Run where the reference sources are checked out: by default a ``reference`` chec
 this repository's directory, or the path in H3SA_REFERENCE. The GPU box and the test suite
 only read the committed .npz outputs.
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py [fixture.npz ...]
 
 Inputs come from numpy's PCG64 generator (platform independent) so the tests can rebuild
 them from the seeds recorded in each fixture. Fixtures:
@@ -22,6 +22,8 @@ them from the seeds recorded in each fixture. Fixtures:
                  (T/streaming/cache.py), rows tagged by (commit, local row) in the K values.
 * ulysses.npz    merged_qkv_sequence_to_heads / heads_to_sequence on two gloo ranks
                  (T/distributed/ulysses.py).
+* ulysses_pad.npz the FL2AV versions with 3 heads over 2 ranks (zero-padded head shards,
+                 F/distributed/ulysses.py).
 """
 
 from __future__ import annotations
@@ -238,11 +240,62 @@ def make_ulysses(path: Path) -> None:
                           for key in ("q", "k", "v", "o")})
 
 
+def _ulysses_pad_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    """The FL2AV exchange with heads not divisible by the world (3 heads over 2 ranks): the
+    send side zero-pads to ceil(H/W) heads per rank, heads_to_sequence(num_heads=H) drops the
+    padding again (F/distributed/ulysses.py:107-110, 150-156, 218-222)."""
+
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(HERE))
+    _import_reference()
+    from digitalhuman_h3.distributed.parallel import ParallelContext
+    from digitalhuman_h3.distributed.ulysses import heads_to_sequence, merged_qkv_sequence_to_heads
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world, timeout=datetime.timedelta(seconds=60))
+    ctx = ParallelContext(tp_world_size=1, tp_rank=0, ulysses_world_size=world,
+                          ulysses_rank=rank, tp_group=dist.group.WORLD,
+                          ulysses_group=dist.group.WORLD)
+    tokens, heads, d = 6, 3, 16
+    merged = ulysses_merged(rank, tokens, heads, d)
+    q, k, v = merged_qkv_sequence_to_heads(torch.from_numpy(merged), num_heads=heads,
+                                           head_dim=d, context=ctx)
+    o = heads_to_sequence(q.contiguous(), context=ctx, num_heads=heads)
+    np.savez(os.path.join(out_dir, f"ulysses_pad_rank{rank}.npz"), q=q.numpy(),
+             k=k.numpy(), v=v.numpy(), o=o.numpy())
+    dist.destroy_process_group()
+
+
+def make_ulysses_pad(path: Path) -> None:
+    import socket
+    import tempfile
+
+    import torch.multiprocessing as mp
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    with tempfile.TemporaryDirectory() as tmp:
+        mp.start_processes(_ulysses_pad_worker, args=(2, port, tmp), nprocs=2,
+                           start_method="spawn")
+        parts = [np.load(os.path.join(tmp, f"ulysses_pad_rank{r}.npz")) for r in range(2)]
+        np.savez(path, **{f"{key}{r}": parts[r][key] for r in range(2)
+                          for key in ("q", "k", "v", "o")})
+
+
 def main() -> None:
     _import_reference()
     makers = {"prologue.npz": make_prologue, "hook_cpu.npz": make_hook, "fp8.npz": make_fp8,
-              "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses}
+              "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
+              "ulysses_pad.npz": make_ulysses_pad}
+    wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
+        if name not in wanted:
+            continue
         fn(HERE / name)
         print(f"wrote {name} ({(HERE / name).stat().st_size} bytes)")
 

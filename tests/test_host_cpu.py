@@ -378,3 +378,27 @@ def test_peer_barrier_limit_validation() -> None:
         rc = L.h3sa_peer_barrier_limit(16, 2, 0, 1, limit, None, None)
         assert rc == lib.H3SA_ERR_INVALID and "wait limit" in lib.last_error()
     assert L.h3sa_peer_barrier_limit(16, 2, 2, 1, 1000, None, None) == lib.H3SA_ERR_INVALID
+
+
+@pytest.mark.parametrize("heads,world", [(3, 2), (28, 8), (6, 4)])
+def test_padded_ulysses_layouts_stay_inside_their_buffers(monkeypatch, heads: int, world: int) -> None:
+    """Heads not divisible by the world: the pack and O-unpack layouts split into the ranks
+    with full shards and the partial one, and every launch stays inside its buffers."""
+
+    from h3sa import kernels, ulysses
+
+    launched = []
+    monkeypatch.setattr(kernels, "_require_cuda", lambda *t: None)
+    monkeypatch.setattr(kernels, "call", lambda name, *a: launched.append(name))
+    monkeypatch.setattr(kernels, "stream_handle", lambda s=None: 0)
+    tokens, d = 5, 128
+    hl = -(-heads // world)
+    merged = torch.zeros(tokens, 3 * heads * d, dtype=torch.bfloat16)
+    send = torch.zeros(world, 3, tokens, hl, d, dtype=torch.bfloat16)
+    ulysses.pack_qkv_send(merged, send, world=world, num_heads=heads, head_dim=d)
+    recv = torch.zeros(world, tokens, hl, d, dtype=torch.bfloat16)
+    out = torch.zeros(tokens, heads, d, dtype=torch.bfloat16)
+    ulysses.unpack_o_recv(recv, out, world=world, tokens=tokens, local_heads=hl, head_dim=d,
+                          num_heads=heads)
+    expect = (1 + (heads % hl != 0)) * 2
+    assert len(launched) == expect

@@ -212,20 +212,21 @@ def test_prologue_pack_matches_oracle_send_layout(world: int) -> None:
     assert np.array_equal(send.float().cpu().numpy(), expect)
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_ulysses_layouts_vs_oracle(world: int) -> None:
-    """Pack -> emulated all-to-all -> unpack on one GPU equals the oracle's every-rank view."""
+@pytest.mark.parametrize("heads,world", [(16, 2), (16, 4), (16, 8), (3, 2), (28, 8), (6, 4)])
+def test_ulysses_layouts_vs_oracle(heads: int, world: int) -> None:
+    """Pack -> emulated all-to-all -> unpack on one GPU equals the oracle's every-rank view,
+    including zero-padded head shards when the heads do not divide by the world."""
 
     from h3sa.ulysses import pack_qkv_send, unpack_o_recv, unpack_qkv_recv
 
-    tokens, heads, d = 10, 16, 128
-    hl = heads // world
+    tokens, d = 10, 128
+    hl = -(-heads // world)
     rng = np.random.default_rng(world)
     merged = [rng.standard_normal((tokens, 3 * heads * d)).astype(np.float32) for _ in range(world)]
     mb = [torch.from_numpy(m).bfloat16().float().numpy() for m in merged]
     sends = []
     for r in range(world):
-        s = torch.empty(world, 3, tokens, hl, d, dtype=torch.bfloat16, device="cuda")
+        s = torch.full((world, 3, tokens, hl, d), 9.0, dtype=torch.bfloat16, device="cuda")
         pack_qkv_send(_cuda_bf16(mb[r]), s, world=world, num_heads=heads, head_dim=d)
         sends.append(s)
     expect = ouly.merged_qkv_sequence_to_heads(mb, heads, d)
@@ -237,11 +238,12 @@ def test_ulysses_layouts_vs_oracle(world: int) -> None:
         for i in range(3):
             assert np.array_equal(out[i].float().cpu().numpy(), expect[r][i])
         outs.append(out[0])
-    expect_o = ouly.heads_to_sequence([e[0] for e in expect])
+    expect_o = ouly.heads_to_sequence([e[0] for e in expect], num_heads=heads)
     for r in range(world):
         recv = torch.stack([outs[s].view(world, tokens, hl, d)[r] for s in range(world)])
         o = torch.empty(tokens, heads, d, dtype=torch.bfloat16, device="cuda")
-        unpack_o_recv(recv, o, world=world, tokens=tokens, local_heads=hl, head_dim=d)
+        unpack_o_recv(recv, o, world=world, tokens=tokens, local_heads=hl, head_dim=d,
+                      num_heads=heads)
         assert np.array_equal(o.float().cpu().numpy(), expect_o[r])
 
 

@@ -98,6 +98,21 @@ def test_ulysses_layouts_match_reference() -> None:
         assert np.array_equal(o[r], g[f"o{r}"])
 
 
+def test_ulysses_padded_heads_match_reference() -> None:
+    """3 heads over 2 ranks: zero-padded head shards and the padding dropped on the way back,
+    against the FL2AV reference run on two gloo ranks."""
+
+    g = load("ulysses_pad.npz")
+    merged = [ulysses_merged(r, heads=3) for r in range(2)]
+    out = ouly.merged_qkv_sequence_to_heads(merged, num_heads=3, head_dim=16)
+    for r in range(2):
+        for i, key in enumerate("qkv"):
+            assert np.array_equal(out[r][i], g[f"{key}{r}"])
+    o = ouly.heads_to_sequence([out[r][0] for r in range(2)], num_heads=3)
+    for r in range(2):
+        assert np.array_equal(o[r], g[f"o{r}"])
+
+
 def test_rope_cache_matches_reference() -> None:
     g = load("prologue.npz")
     cs = opro.rope_cos_sin(g["grid"], g["inv_freq"])

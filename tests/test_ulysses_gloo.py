@@ -37,13 +37,22 @@ def _worker(rank: int, world: int, rendezvous: str, out_dir: str) -> None:
     got = recv.permute(1, 0, 2, 3, 4).reshape(3, world * tokens, hl, d).numpy()
     expect = ouly.merged_qkv_sequence_to_heads(merged, heads, d)[rank]
     ok = all(np.array_equal(got[i], expect[i]) for i in range(3))
+    # 3 heads over the ranks: zero-padded shards of ceil(3 / W) heads
+    ph = 3
+    pm = [np.random.default_rng(70 + r).standard_normal((tokens, 3 * ph * d)).astype(np.float32)
+          for r in range(world)]
+    phl = -(-ph // world)
+    padded = np.zeros((tokens, 3, world * phl, d), np.float32)
+    padded[:, :, :ph] = pm[rank].reshape(tokens, 3, ph, d)
+    psend = torch.from_numpy(padded.reshape(tokens, 3, world, phl, d).transpose(2, 1, 0, 3, 4).copy())
+    precv = torch.empty_like(psend)
+    dist.all_to_all_single(precv, psend)
+    pgot = precv.permute(1, 0, 2, 3, 4).reshape(3, world * tokens, phl, d).numpy()
+    pexpect = ouly.merged_qkv_sequence_to_heads(pm, ph, d)[rank]
+    ok = ok and all(np.array_equal(pgot[i], pexpect[i]) for i in range(3))
     # argument validation happens before any device work, under the live group
     ctx = ParallelContext(1, 0, world, rank, dist.group.WORLD, dist.group.WORLD)
     msg = ""
-    try:
-        merged_qkv_sequence_to_heads(torch.zeros(tokens, 3 * 3 * d), num_heads=3, head_dim=d, context=ctx)
-    except ValueError as exc:
-        msg = str(exc)
     try:
         merged_qkv_sequence_to_heads(torch.zeros(tokens, 7), num_heads=3, head_dim=d, context=ctx)
     except ValueError as exc:
@@ -64,5 +73,4 @@ def test_two_rank_exchange_and_validation(tmp_path: Path) -> None:
     for r in range(2):
         assert np.load(tmp_path / f"r{r}.npy").all()
         msg = (tmp_path / f"m{r}.txt").read_text()
-        assert "merged QKV heads are not divisible by Ulysses" in msg
         assert "merged QKV width differs" in msg
