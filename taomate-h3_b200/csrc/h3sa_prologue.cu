@@ -103,51 +103,57 @@ __device__ __forceinline__ float rsqrt_rn32(float xf) {
   return f;
 }
 
-// RMSNorm + rotate-half RoPE of one Q or K row held by a half-warp (8 values per lane, lane
-// `sub` holds dims [8 sub, 8 sub + 8)). c/sn: this lane's cos/sin values of the token
-// (rotating lanes only). Returns the lane's 8 output values packed as bf16.
-__device__ __forceinline__ uint4 norm_rope_row(uint4 raw, const float (&w)[8], float eps,
+// RMSNorm + rotate-half RoPE of one Q or K row held by a half-warp (lane `sub` holds dims
+// [8 sub, 8 sub + 8) as four bf16 pairs). w2: this lane's norm weights as fp32 pairs; c / sn:
+// its cos / sin values of the token as bf16 pairs (rotating lanes only). Every rounding point
+// of the arithmetic is kept, in packed form: v * inv * w in fp32 pairs (two roundings), one
+// rounding to bf16 per value (cvt.rn.bf16x2), then n * cos and rot(n) * sin as bf16 products
+// and their sum as a bf16 sum, each exact before its single rounding to bf16 as the
+// reference's fp32 product or sum rounded to bf16 is (a sum of two bf16 values that fp32
+// cannot hold exactly is far from any bf16 rounding midpoint). Partners exchange packed pairs.
+__device__ __forceinline__ uint4 norm_rope_row(uint4 raw, const uint64_t (&w2)[4], float eps,
                                                bool rotating, bool low, int partner,
-                                               unsigned half_mask, const float (&c)[8],
-                                               const float (&sn)[8]) {
+                                               unsigned half_mask, const uint32_t (&c)[4],
+                                               const uint32_t (&sn)[4]) {
   const uint32_t u[4] = {raw.x, raw.y, raw.z, raw.w};
-  float v[8];
+  float lo[4], hi[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    v[2 * i] = __uint_as_float(u[i] << 16);
-    v[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+    lo[i] = __uint_as_float(u[i] << 16);
+    hi[i] = __uint_as_float(u[i] & 0xFFFF0000u);
   }
+  // sum of squares: each square of a bf16 value is exact in fp64, and so is the sum
   double ss = 0.0;
 #pragma unroll
-  for (int e = 0; e < 8; ++e) ss += static_cast<double>(v[e] * v[e]);
+  for (int i = 0; i < 4; ++i) {
+    const double a = lo[i], b = hi[i];
+    ss = fma(a, a, ss);
+    ss = fma(b, b, ss);
+  }
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) ss += __shfl_xor_sync(half_mask, ss, o, 16);
   // mean of the exact sum (scaling by 1/128 is exact), eps added in fp32
   const float var = static_cast<float>(ss * (1.0 / kHeadDim));
   const float inv = rsqrt_rn32(__fadd_rn(var, eps));
-  float n[8];
+  const uint64_t inv2 = f2_pack(inv, inv);
+  uint32_t n[4];
 #pragma unroll
-  for (int e = 0; e < 8; ++e) n[e] = bf16r(__fmul_rn(__fmul_rn(v[e], inv), w[e]));
-  float pn[8];
-#pragma unroll
-  for (int e = 0; e < 8; ++e) pn[e] = __shfl_sync(half_mask, n[e], partner);
-  float out[8];
-  if (rotating) {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const float r = low ? -pn[e] : pn[e];
-      out[e] = bf16r(bf16r(__fmul_rn(n[e], c[e])) + bf16r(__fmul_rn(r, sn[e])));
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 8; ++e) out[e] = n[e];
+  for (int i = 0; i < 4; ++i) {
+    float x0, x1;
+    f2_unpack(f2_mul(f2_mul(f2_pack(lo[i], hi[i]), inv2), w2[i]), x0, x1);
+    n[i] = pack_bf16x2(x0, x1);
   }
-  uint4 o;
-  o.x = (__float_as_uint(out[0]) >> 16) | (__float_as_uint(out[1]) & 0xFFFF0000u);
-  o.y = (__float_as_uint(out[2]) >> 16) | (__float_as_uint(out[3]) & 0xFFFF0000u);
-  o.z = (__float_as_uint(out[4]) >> 16) | (__float_as_uint(out[5]) & 0xFFFF0000u);
-  o.w = (__float_as_uint(out[6]) >> 16) | (__float_as_uint(out[7]) & 0xFFFF0000u);
-  return o;
+  uint32_t pn[4];  // every lane of the half-warp takes part in the exchange
+#pragma unroll
+  for (int i = 0; i < 4; ++i) pn[i] = __shfl_sync(half_mask, n[i], partner);
+  if (!rotating) return make_uint4(n[0], n[1], n[2], n[3]);
+  uint32_t out[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t r = low ? pn[i] ^ 0x80008000u : pn[i];  // rot(n) = -n[i + rotary/2] first
+    out[i] = bf2_add(bf2_mul(n[i], c[i]), bf2_mul(r, sn[i]));
+  }
+  return make_uint4(out[0], out[1], out[2], out[3]);
 }
 
 __device__ __forceinline__ void unpack8(uint4 a, float (&f)[8]) {
@@ -159,78 +165,182 @@ __device__ __forceinline__ void unpack8(uint4 a, float (&f)[8]) {
   }
 }
 
-// Rows of a token handled per half-warp before the next loads are issued.
-constexpr int kRouteBatch = 4;
+// Staged pipeline, one CTA per contiguous range of tokens. Warp 8 (the producer) streams each
+// token into a ring of kPipeStages shared-memory slots with plain bulk copies: the token's
+// merged rows (Q and K heads in place, all three planes otherwise; contiguous in the merged
+// layout) and its cos / sin row, all completing on the slot's full barrier. Warps 0-7 (16
+// half-warps) take the slot's rows k, k + 16, ..., normalise and rotate the Q/K rows from
+// shared memory and store every row to its destination, then release the slot. A slot holds
+// a whole token (18 KB at 24 heads), so the copies of the next slots are in flight while the
+// consumers work: the bytes in flight per SM no longer depend on registers. Every wait is
+// bounded.
+constexpr int kPipeStages = 4;
+constexpr int kPipeConsumerWarps = 8;
+constexpr int kPipeThreads = (kPipeConsumerWarps + 1) * 32;
 
-// One CTA per token at a time (grid-stride over tokens); half-warp k of the CTA takes rows
-// k, k + 16, ... of the token's [3, H] rows (Q heads, then K, then V; in place only Q and K),
-// loading kRouteBatch rows before computing, so each lane has that many 16-byte loads in
-// flight. All index arithmetic is 32-bit; the plane of a row comes from two compares.
-__global__ void __launch_bounds__(256, 3) qkv_norm_rope_kernel(const PrologueParams p) {
-  const int lane = threadIdx.x & 31;
-  const int sub = lane & 15;                 // lane within the row
-  const int base_lane = lane & 16;           // first lane of this half-warp
-  const unsigned half_mask = 0xFFFFu << base_lane;
-  const int hw = threadIdx.x >> 4;           // half-warp of the CTA, 0..15
+struct PipeSmemLayout {
+  int slot_bytes;   // rows of a token, rounded to 128 bytes
+  int cs_bytes;     // cos / sin row, rounded to 16 bytes
+  int total;        // bytes of dynamic shared memory
+};
+
+__host__ __device__ inline PipeSmemLayout pipe_layout(int rows_pt, int rotary) {
+  PipeSmemLayout l;
+  l.slot_bytes = (rows_pt * kHeadDim * 2 + 127) / 128 * 128;
+  l.cs_bytes = (rotary * 2 + 15) / 16 * 16;
+  // slots, cos/sin rows, full + empty barriers, per-slot position-valid flags, abort flag
+  l.total = kPipeStages * (l.slot_bytes + l.cs_bytes) + kPipeStages * 2 * 8 + kPipeStages * 4 + 16;
+  return l;
+}
+
+__global__ void __launch_bounds__(kPipeThreads, 1) qkv_norm_rope_pipe_kernel(const PrologueParams p,
+                                                                             int tokens_per_cta) {
+  extern __shared__ __align__(128) uint8_t smem[];
   const int heads = p.heads;
-  const int rows = (p.mode == kRouteInPlace ? 2 : 3) * heads;
+  const int rows_pt = (p.mode == kRouteInPlace ? 2 : 3) * heads;
+  const PipeSmemLayout L = pipe_layout(rows_pt, p.rotary);
+  uint8_t* slots = smem;
+  uint8_t* cs_rows = smem + kPipeStages * L.slot_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(cs_rows + kPipeStages * L.cs_bytes);
+  uint64_t* empty = full + kPipeStages;
+  int* pos_ok = reinterpret_cast<int*>(empty + kPipeStages);
+  volatile int* abort_flag = pos_ok + kPipeStages;
+  const int t0 = blockIdx.x * tokens_per_cta;
+  const int t1 = min(p.tokens, t0 + tokens_per_cta);
+  const int n = max(0, t1 - t0);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPipeStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), kPipeConsumerWarps);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const uint32_t row_bytes = static_cast<uint32_t>(rows_pt) * kHeadDim * 2;
+  if (warp == kPipeConsumerWarps) {
+    // ------------------------------------------------------------------ producer
+    // positions of 32 tokens at a time, one per lane, handed to lane 0 by shuffles
+    int issued = 0;
+    for (int c0 = 0; c0 < n && !*abort_flag; c0 += 32) {
+      const long long my_pos = c0 + lane < n ? __ldg(p.positions + t0 + c0 + lane) : 0;
+      const int m = min(32, n - c0);
+      for (int k = 0; k < m; ++k) {
+        const long long pos = __shfl_sync(0xffffffffu, my_pos, k);
+        if (lane == 0) {
+          const int i = c0 + k;
+          const int s = i % kPipeStages;
+          const bool ok = i < kPipeStages ||
+                          mbar_wait(smem_u32(&empty[s]), ((i / kPipeStages) - 1) & 1, abort_flag,
+                                    p.err);
+          if (ok) {
+            const bool pv = pos >= 0 && pos < p.cache_rows;
+            pos_ok[s] = pv ? 1 : 0;
+            const uint32_t bar = smem_u32(&full[s]);
+            mbar_expect_tx(bar, row_bytes + (pv ? 2u * p.rotary : 0u));
+            bulk_load(smem_u32(slots + s * L.slot_bytes),
+                      p.src + static_cast<size_t>(t0 + i) * 3 * heads * kHeadDim, row_bytes, bar);
+            if (pv)
+              bulk_load(smem_u32(cs_rows + s * L.cs_bytes),
+                        p.cos_sin + static_cast<size_t>(pos) * p.rotary, 2u * p.rotary, bar);
+            issued = i + 1;
+          }
+        }
+        __syncwarp();
+        if (*abort_flag) break;
+      }
+    }
+    // leave no bulk copy in flight past the end of the CTA: wait for the last slots' data
+    if (lane == 0) {
+      for (int i = max(0, issued - kPipeStages); i < issued; ++i) {
+        const unsigned long long w0 = global_ns();
+        while (!mbar_try_wait(smem_u32(&full[i % kPipeStages]), (i / kPipeStages) & 1)) {
+          if (global_ns() - w0 > kWaitTimeoutNs) {
+            if (p.err) atomicOr(p.err, kErrWaitTimeout);
+            break;
+          }
+        }
+      }
+    }
+    return;
+  }
+  // -------------------------------------------------------------------- consumers
+  const int sub = lane & 15;
+  const int base_lane = lane & 16;
+  const unsigned half_mask = 0xFFFFu << base_lane;
+  const int hw = threadIdx.x >> 4;  // half-warp, 0..15
   const int half = p.rotary >> 1;
-  float wq[8], wk[8];
-  unpack8(reinterpret_cast<const uint4*>(p.q_weight)[sub], wq);
-  unpack8(reinterpret_cast<const uint4*>(p.k_weight)[sub], wk);
+  uint64_t wq[4], wk[4];  // this lane's norm weights as fp32 pairs
+  {
+    float fq[8], fk[8];
+    unpack8(reinterpret_cast<const uint4*>(p.q_weight)[sub], fq);
+    unpack8(reinterpret_cast<const uint4*>(p.k_weight)[sub], fk);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      wq[i] = f2_pack(fq[2 * i], fq[2 * i + 1]);
+      wk[i] = f2_pack(fk[2 * i], fk[2 * i + 1]);
+    }
+  }
   const int d0 = 8 * sub;
   const bool rotating = d0 < p.rotary;
   const bool low = d0 < half;
   const int partner = base_lane + (low ? sub + (half >> 3) : sub - (half >> 3));
   const int phase = rotating ? (low ? d0 : d0 - half) : 0;
-  for (int t = blockIdx.x; t < p.tokens; t += gridDim.x) {
-    const long long pos = __ldg(p.positions + t);
-    const bool pos_ok = pos >= 0 && pos < p.cache_rows;
-    if (!pos_ok && threadIdx.x == 0 && p.err) atomicOr(p.err, kErrBadIndex);
-    float c[8], sn[8];
-    if (rotating && pos_ok) {
-      const __nv_bfloat16* cs = p.cos_sin + static_cast<size_t>(pos) * p.rotary;
-      unpack8(__ldg(reinterpret_cast<const uint4*>(cs + phase)), c);
-      unpack8(__ldg(reinterpret_cast<const uint4*>(cs + half + phase)), sn);
-    } else {
-#pragma unroll
-      for (int e = 0; e < 8; ++e) c[e] = sn[e] = 0.f;
+  for (int i = 0; i < n; ++i) {
+    const int s = i % kPipeStages;
+    if (!mbar_wait(smem_u32(&full[s]), (i / kPipeStages) & 1, abort_flag, p.err)) break;
+    const int t = t0 + i;
+    const bool pv = pos_ok[s] != 0;
+    if (!pv && threadIdx.x == 0 && p.err) atomicOr(p.err, kErrBadIndex);
+    uint32_t c[4] = {0u, 0u, 0u, 0u}, sn[4] = {0u, 0u, 0u, 0u};
+    if (pv && rotating) {
+      const uint8_t* cs = cs_rows + s * L.cs_bytes;
+      const uint4 cr = *reinterpret_cast<const uint4*>(cs + 2 * phase);
+      const uint4 sr = *reinterpret_cast<const uint4*>(cs + 2 * (half + phase));
+      c[0] = cr.x; c[1] = cr.y; c[2] = cr.z; c[3] = cr.w;
+      sn[0] = sr.x; sn[1] = sr.y; sn[2] = sr.z; sn[3] = sr.w;
     }
-    const uint4* src = reinterpret_cast<const uint4*>(p.src) + static_cast<size_t>(t) * 3 * heads * 16;
-    for (int r0 = hw; r0 < rows; r0 += 16 * kRouteBatch) {
-      uint4 raw[kRouteBatch];
-#pragma unroll
-      for (int b = 0; b < kRouteBatch; ++b) {
-        const int r = r0 + 16 * b;
-        if (r < rows) raw[b] = __ldg(src + r * 16 + sub);
+    const uint4* rows = reinterpret_cast<const uint4*>(slots + s * L.slot_bytes);
+    for (int r = hw; r < rows_pt; r += 16) {
+      const int j = (r >= heads) + (r >= 2 * heads);
+      const int h = r - j * heads;
+      uint4 o = rows[r * 16 + sub];
+      if (j < 2) {
+        if (!pv) continue;
+        o = norm_rope_row(o, j == 0 ? wq : wk, p.eps, rotating, low, partner, half_mask, c, sn);
       }
-#pragma unroll
-      for (int b = 0; b < kRouteBatch; ++b) {
-        const int r = r0 + 16 * b;
-        if (r >= rows) break;
-        const int j = (r >= heads) + (r >= 2 * heads);
-        const int h = r - j * heads;
-        uint4 o = raw[b];
-        if (j < 2) {
-          if (!pos_ok) continue;
-          o = norm_rope_row(raw[b], j == 0 ? wq : wk, p.eps, rotating, low, partner, half_mask,
-                            c, sn);
-        }
-        __nv_bfloat16* dst = dst_row(p, t, j, h);
-        if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
-        else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
-      }
+      __nv_bfloat16* dst = dst_row(p, t, j, h);
+      if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
+      else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
     }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
   }
   if (p.mode == kRoutePeers) __threadfence_system();
 }
 
 static int prologue_launch(const PrologueParams& p, cudaStream_t stream) {
-  int blocks = p.tokens < 148 * 8 ? p.tokens : 148 * 8;
-  if (blocks < 1) blocks = 1;
-  qkv_norm_rope_kernel<<<blocks, 256, 0, stream>>>(p);
+  const int rows_pt = (p.mode == kRouteInPlace ? 2 : 3) * p.heads;
+  const PipeSmemLayout L = pipe_layout(rows_pt, p.rotary);
+  if (L.total > 227 * 1024)
+    return set_error(H3SA_ERR_UNSUPPORTED, "qkv prologue: %d heads need %d bytes of staging",
+                     p.heads, L.total);
+  if (L.total > 48 * 1024) {  // the opt-in applies to the current device
+    cudaError_t e = cudaFuncSetAttribute(qkv_norm_rope_pipe_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+    if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(prologue smem)", e);
+  }
+  // two CTAs per SM, one contiguous token range each
+  int ctas = 148 * 2;
+  if (ctas > p.tokens) ctas = p.tokens;
+  if (ctas < 1) ctas = 1;
+  const int per = (p.tokens + ctas - 1) / ctas;
+  ctas = (p.tokens + per - 1) / per;
+  qkv_norm_rope_pipe_kernel<<<ctas, kPipeThreads, L.total, stream>>>(p, per);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error("qkv_norm_rope_kernel launch", e);
+  if (e != cudaSuccess) return set_cuda_error("qkv_norm_rope_pipe_kernel launch", e);
   return H3SA_OK;
 }
 
