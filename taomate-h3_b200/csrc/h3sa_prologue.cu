@@ -39,6 +39,8 @@ struct PrologueParams {
   float eps;
   int* err;
   int mode;
+  int heads_local;  // heads / world
+  int hl_recip;     // ceil(65536 / heads_local): h / heads_local = (h * hl_recip) >> 16
   // kRoutePeers: every rank's Q plane and paged pools (device arrays of `world` addresses),
   // the page table shared by the group, and the first logical cache row of this chunk
   int rank;
@@ -57,13 +59,14 @@ __device__ __forceinline__ float bf16r(float x) {
 
 // Destination row (256 bytes) of (token t, plane j in {q, k, v}, head h); nullptr when a page
 // lookup fails (reported by the caller).
+template <int kMode>
 __device__ __forceinline__ __nv_bfloat16* dst_row(const PrologueParams& p, int t, int j, int h) {
-  if (p.mode == kRouteInPlace)
+  if constexpr (kMode == kRouteInPlace)
     return p.dst + ((static_cast<size_t>(t) * 3 + j) * p.heads + h) * kHeadDim;
-  const int hl = p.heads / p.world;
-  const int w = h / hl;
+  const int hl = p.heads_local;
+  const int w = (h * p.hl_recip) >> 16;  // h / hl, exact for h < 256 (host-checked)
   const int lh = h - w * hl;
-  if (p.mode == kRoutePack)
+  if constexpr (kMode == kRoutePack)
     return p.dst + (((static_cast<size_t>(w) * 3 + j) * p.tokens + t) * hl + lh) * kHeadDim;
   const int row = p.rank * p.tokens + t;  // row of the owner's all-rank sequence
   if (j == 0) {
@@ -193,11 +196,12 @@ __host__ __device__ inline PipeSmemLayout pipe_layout(int rows_pt, int rotary) {
   return l;
 }
 
-__global__ void __launch_bounds__(kPipeThreads, 1) qkv_norm_rope_pipe_kernel(const PrologueParams p,
+template <int kMode>
+__global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(const PrologueParams p,
                                                                              int tokens_per_cta) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int heads = p.heads;
-  const int rows_pt = (p.mode == kRouteInPlace ? 2 : 3) * heads;
+  const int rows_pt = (kMode == kRouteInPlace ? 2 : 3) * heads;
   const PipeSmemLayout L = pipe_layout(rows_pt, p.rotary);
   uint8_t* slots = smem;
   uint8_t* cs_rows = smem + kPipeStages * L.slot_bytes;
@@ -311,14 +315,15 @@ __global__ void __launch_bounds__(kPipeThreads, 1) qkv_norm_rope_pipe_kernel(con
         if (!pv) continue;
         o = norm_rope_row(o, j == 0 ? wq : wk, p.eps, rotating, low, partner, half_mask, c, sn);
       }
-      __nv_bfloat16* dst = dst_row(p, t, j, h);
+      __nv_bfloat16* dst = dst_row<kMode>(p, t, j, h);
       if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
       else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
   }
-  if (p.mode == kRoutePeers) __threadfence_system();
+  // stores to other GPUs: visible to them before the kernel is seen as done
+  if (kMode == kRoutePeers && p.world > 1) __threadfence_system();
 }
 
 static int prologue_launch(const PrologueParams& p, cudaStream_t stream) {
@@ -327,18 +332,25 @@ static int prologue_launch(const PrologueParams& p, cudaStream_t stream) {
   if (L.total > 227 * 1024)
     return set_error(H3SA_ERR_UNSUPPORTED, "qkv prologue: %d heads need %d bytes of staging",
                      p.heads, L.total);
+  auto kernel = p.mode == kRouteInPlace ? qkv_norm_rope_pipe_kernel<kRouteInPlace>
+               : p.mode == kRoutePack   ? qkv_norm_rope_pipe_kernel<kRoutePack>
+                                        : qkv_norm_rope_pipe_kernel<kRoutePeers>;
   if (L.total > 48 * 1024) {  // the opt-in applies to the current device
-    cudaError_t e = cudaFuncSetAttribute(qkv_norm_rope_pipe_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, L.total);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         L.total);
     if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(prologue smem)", e);
   }
-  // two CTAs per SM, one contiguous token range each
-  int ctas = 148 * 2;
+  PrologueParams q = p;
+  q.heads_local = p.heads / (p.world > 0 ? p.world : 1);
+  q.hl_recip = (65536 + q.heads_local - 1) / q.heads_local;
+  // as many CTAs per SM as the staging fits (three at 24 heads), one token range each
+  const int per_sm = (3 * (L.total + 1024) <= 228 * 1024) ? 3 : (2 * (L.total + 1024) <= 228 * 1024) ? 2 : 1;
+  int ctas = 148 * per_sm;
   if (ctas > p.tokens) ctas = p.tokens;
   if (ctas < 1) ctas = 1;
   const int per = (p.tokens + ctas - 1) / ctas;
   ctas = (p.tokens + per - 1) / per;
-  qkv_norm_rope_pipe_kernel<<<ctas, kPipeThreads, L.total, stream>>>(p, per);
+  kernel<<<ctas, kPipeThreads, L.total, stream>>>(q, per);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("qkv_norm_rope_pipe_kernel launch", e);
   return H3SA_OK;
@@ -352,6 +364,8 @@ static int check_prologue(const void* qkv, const void* q_weight, const void* k_w
     return set_error(H3SA_ERR_UNSUPPORTED, "qkv prologue requires head_dim 128, got %d", head_dim);
   if (!qkv || !q_weight || !k_weight || !cos_sin || !positions)
     return set_error(H3SA_ERR_INVALID, "qkv prologue: null pointer argument");
+  if (heads > 255)  // the staging ring holds whole tokens; far above the model's 56 heads
+    return set_error(H3SA_ERR_UNSUPPORTED, "qkv prologue: at most 255 heads, got %d", heads);
   if (tokens < 0 || heads <= 0 || cache_rows <= 0)
     return set_error(H3SA_ERR_INVALID, "qkv prologue: invalid sizes");
   if (rotary <= 0 || rotary > head_dim || (rotary % 16) != 0)
