@@ -22,6 +22,9 @@ them from the seeds recorded in each fixture. Fixtures:
                  (T/streaming/cache.py), rows tagged by (commit, local row) in the K values.
 * ulysses.npz    merged_qkv_sequence_to_heads / heads_to_sequence on two gloo ranks
                  (T/distributed/ulysses.py).
+* cache_f.npz    the FL2AV CleanAVKVCache (F/streaming/cache.py) row tables through bounded
+                 commits, count-based and sink + recent retention, audio drop and strided
+                 attention-history queries.
 * ulysses_pad.npz the FL2AV versions with 3 heads over 2 ranks (zero-padded head shards,
                  F/distributed/ulysses.py).
 """
@@ -200,6 +203,68 @@ def make_cache(path: Path) -> None:
     np.savez(path, **arrays)
 
 
+def make_cache_f(path: Path) -> None:
+    """The FL2AV cache (F/streaming/cache.py) through bounded commits, count-based retention,
+    sink + recent retention and audio drop, with its strided attention history queried along
+    the way. Its stage() accepts only CUDA bf16 K/V; the check is stubbed so the row
+    bookkeeping runs on CPU (rows tagged by (commit serial, local row), exact in bf16)."""
+
+    import torch
+    import digitalhuman_h3.streaming.cache as fcache
+
+    fcache._validate_av_pair = lambda pair, contract, *, layer: None
+    layer = "blocks.0.attn"
+    contract = fcache.KVContract(layer_names=(layer,), local_heads=1, head_dim=2)
+    cache = fcache.CleanAVKVCache(contract)
+    rng = np.random.default_rng(13)
+    schedule = [("commit",), ("commit",), ("commit",), ("attn", 3, 1, 2, False),
+                ("sink_recent", 1, True), ("commit",), ("attn", 3, 1, 3, True),
+                ("bounded", 3), ("bounded", 3), ("retain_recent", 2), ("commit",),
+                ("commit",), ("attn", 4, 2, 2, True), ("sink_recent", 2, False), ("drop",),
+                ("commit",), ("attn", 3, 0, 4, False), ("bounded", 1), ("commit",)]
+    arrays: dict[str, np.ndarray] = {}
+    serial = 0
+    for i, step in enumerate(schedule):
+        op = step[0]
+        if op in ("commit", "bounded"):
+            audio = 2 * int(rng.integers(2, 5))
+            video = int(rng.integers(6, 14))
+            tags = np.array([1] * 3 + [2] * audio + [0] * video + [-1] * 2)
+            commit = (tags == 0) | (tags == 2)
+            ids = np.zeros((len(tags), 1, 2), dtype=np.float32)
+            staged = np.nonzero(commit)[0]
+            ids[staged, 0, 0] = serial
+            ids[staged, 0, 1] = np.arange(staged.size)
+            cache.begin_clean_commit(cache.committed_blocks)
+            t = torch.from_numpy(ids).to(torch.bfloat16)
+            cache.stage(layer, t, t.clone(), torch.from_numpy(tags), torch.from_numpy(commit))
+            if op == "commit":
+                cache.commit()
+            else:
+                cache.commit(retain_recent_commit_count=int(step[1]))
+            arrays[f"tags_{i}"] = tags
+            serial += 1
+        elif op == "sink_recent":
+            cache.retain_sink_and_recent_commits(int(step[1]), sink_video_only=bool(step[2]))
+        elif op == "retain_recent":
+            cache.retain_recent_commits(int(step[1]))
+        elif op == "drop":
+            arrays[f"removed_{i}"] = np.array(cache.drop_audio_history())
+        elif op == "attn":
+            sel = cache.attention_history(layer, count=int(step[1]), recent_full_blocks=int(step[2]),
+                                          older_video_stride=int(step[3]),
+                                          preserve_sink=bool(step[4]))
+            arrays[f"attn_{i}"] = (np.zeros((0, 2), np.int64) if sel is None
+                                   else sel.key[:, 0, :].float().numpy().astype(np.int64))
+        hist = cache.history(layer)
+        arrays[f"rows_{i}"] = (np.zeros((0, 2), np.int64) if hist is None
+                               else hist.key[:, 0, :].float().numpy().astype(np.int64))
+        arrays[f"counts_{i}"] = np.array(cache.commit_token_counts, dtype=np.int64)
+        arrays[f"blocks_{i}"] = np.array(cache.committed_blocks)
+    arrays["schedule"] = np.array(["|".join(str(x) for x in st) for st in schedule])
+    np.savez(path, **arrays)
+
+
 # ----------------------------------------------------------------------------- ulysses
 def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import datetime
@@ -291,7 +356,7 @@ def main() -> None:
     _import_reference()
     makers = {"prologue.npz": make_prologue, "hook_cpu.npz": make_hook, "fp8.npz": make_fp8,
               "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
-              "ulysses_pad.npz": make_ulysses_pad}
+              "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

@@ -167,3 +167,39 @@ def test_composite_mask_properties(density: float) -> None:
             assert set(np.nonzero(m["forced"][j])[0]) <= set(keep.tolist())
             assert keep.size == max(m["budget"], int(m["forced"][j].sum()))
     assert m["kv_num_blocks"][:, 0].min() == kb  # the audio query block attends everywhere
+
+
+def replay_cache_f(g, apply):
+    """Walk the FL2AV cache schedule of cache_f.npz, calling ``apply(i, op, args, tags)``."""
+
+    for i, step in enumerate(g["schedule"]):
+        op, *args = str(step).split("|")
+        apply(i, op, args, g[f"tags_{i}"].tolist() if f"tags_{i}" in g else None)
+
+
+def test_fl2av_cache_rows_match_reference() -> None:
+    g = load("cache_f.npz")
+    cache = ocache.CacheIndexOracle()
+
+    def apply(i, op, args, tags):
+        mask = None if tags is None else [t in (0, 2) for t in tags]
+        if op == "commit":
+            cache.commit(tags, mask)
+        elif op == "bounded":
+            cache.commit_bounded(tags, mask, int(args[0]))
+        elif op == "sink_recent":
+            cache.retain_sink_and_recent(int(args[0]), args[1] == "True")
+        elif op == "retain_recent":
+            cache.retain_recent_commits(int(args[0]))
+        elif op == "drop":
+            assert cache.drop_audio_history() == int(g[f"removed_{i}"])
+        elif op == "attn":
+            rows = cache.attention_history_rows(int(args[0]), int(args[1]), int(args[2]),
+                                                args[3] == "True")
+            got = np.zeros((0, 2), np.int64) if rows is None else np.array(rows, np.int64)
+            assert np.array_equal(got, g[f"attn_{i}"]), i
+        assert np.array_equal(np.array(cache.rows, dtype=np.int64).reshape(-1, 2), g[f"rows_{i}"]), i
+        assert cache.counts == g[f"counts_{i}"].tolist(), i
+        assert cache.committed_blocks == int(g[f"blocks_{i}"]), i
+
+    replay_cache_f(g, apply)
