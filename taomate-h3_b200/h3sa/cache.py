@@ -320,16 +320,19 @@ class CleanAVKVCache:
         self._block_index = 0
         self._commit_token_counts: list[int] = []
         self._commit_token_tags: list[tuple[int, ...]] = []
+        self._invalid_after_failed_commit = False
 
     # ------------------------------------------------------------------ properties
     @property
     def committed_blocks(self) -> int:
         """Logical number of clean chunks committed since the last clear."""
 
+        self._require_valid()
         return self._block_index
 
     @property
     def history_tokens(self) -> int:
+        self._require_valid()
         return sum(self._commit_token_counts)
 
     @property
@@ -346,6 +349,32 @@ class CleanAVKVCache:
 
     def commit_token_tags(self) -> list[tuple[int, ...]]:
         return list(self._commit_token_tags)
+
+    @property
+    def commit_token_counts(self) -> tuple[int, ...]:
+        """Rows of each retained clean block, oldest first (F/streaming/cache.py:259-262)."""
+
+        self._require_valid()
+        return tuple(self._commit_token_counts)
+
+    @property
+    def retained_blocks(self) -> int:
+        return len(self._commit_token_counts)
+
+    def _require_valid(self) -> None:
+        if self._invalid_after_failed_commit:
+            raise RuntimeError("H3 cache is invalid after a failed clean commit")
+
+    def _invalidate_failed_commit(self) -> None:
+        for paged in self._layers.values():
+            paged.release()
+            if paged.fp8 is not None:
+                paged.fp8.release()
+        self._clear_staging()
+        self._block_index = 0
+        self._commit_token_counts.clear()
+        self._commit_token_tags.clear()
+        self._invalid_after_failed_commit = True
 
     # ------------------------------------------------------------------ paged access
     def layer(self, layer_name: str, device: torch.device | None = None) -> PagedLayerKV:
@@ -371,6 +400,7 @@ class CleanAVKVCache:
     def history(self, layer_name: str) -> AVKV | None:
         """Dense copies of the layer's committed rows (None when empty)."""
 
+        self._require_valid()
         _validate_layer_name(layer_name, self.layer_names)
         paged = self._layers.get(layer_name)
         if paged is None or paged.history_rows == 0:
@@ -449,9 +479,15 @@ class CleanAVKVCache:
         indices = self._resolve_stage(token_tags, commit_mask)
         self._staged[layer_name] = int(indices.numel())
 
-    def commit(self) -> None:
-        """Atomically append all staged layers to persistent history."""
+    def commit(self, *, retain_recent_commit_count: int | None = None) -> None:
+        """Atomically append all staged layers to persistent history; with
+        ``retain_recent_commit_count`` keep only that many newest blocks (FL2AV,
+        F/streaming/cache.py:780-821)."""
 
+        if retain_recent_commit_count is not None:
+            self.commit_bounded(retain_recent_commit_count)
+            return
+        self._require_valid()
         if not self.clean_commit_active:
             raise RuntimeError("no clean KV commit is active")
         missing = [name for name in self.layer_names if name not in self._staged]
@@ -460,30 +496,87 @@ class CleanAVKVCache:
         assert self._staged_tags is not None
         token_count = len(self._staged_tags)
         for layer_name in self.layer_names:
-            staged = self._staged.pop(layer_name)
+            staged = self._staged[layer_name]
             if staged != token_count:
                 raise RuntimeError(f"{layer_name}: staged {staged} rows, expected {token_count}")
-            paged = self._layers[layer_name]
-            if paged.fp8 is not None:
-                # the staged rows sit right after the history: quantise them as one part
-                paged.fp8.commit_part(paged.key, paged.value, src_start=paged.history_rows,
-                                      count=token_count, src_table=paged.table)
-            paged.history_rows += token_count
+        try:
+            for layer_name in self.layer_names:
+                paged = self._layers[layer_name]
+                if paged.fp8 is not None:
+                    # the staged rows sit right after the history: quantise them as one part
+                    paged.fp8.commit_part(paged.key, paged.value, src_start=paged.history_rows,
+                                          count=token_count, src_table=paged.table)
+                paged.history_rows += token_count
+        except BaseException:
+            # a commit that stops half way leaves layers out of step: the cache refuses further
+            # use until clear() (F/streaming/cache.py:766-778)
+            self._invalidate_failed_commit()
+            raise
         self._commit_token_counts.append(token_count)
         self._commit_token_tags.append(self._staged_tags)
         self._block_index += 1
         self._clear_staging()
 
-    def retain_sink_and_recent_commits(self) -> None:
-        """Keep the first chunk's video sink and the most recent clean chunks."""
+    def commit_bounded(self, count: int, *, advance_serial: bool = True) -> None:
+        """Commit the staged block keeping only the newest ``count`` blocks, the staged one
+        included (F/streaming/cache.py:857-927); without ``advance_serial`` the logical
+        chunk count stays."""
 
+        self._require_valid()
+        if isinstance(count, bool) or not isinstance(count, int) or count < 1:
+            raise ValueError("bounded clean commit count must be positive")
+        serial = self._block_index
+        self.commit()
+        if not advance_serial:
+            self._block_index = serial
+        blocks = len(self._commit_token_counts)
+        if blocks > count:
+            self._retain_commit_rows([(index, False) for index in range(blocks - count, blocks)])
+
+    def retain_recent_commits(self, count: int) -> None:
+        """Keep the newest ``count`` clean blocks (F/streaming/cache.py:929-962)."""
+
+        self._require_valid()
+        if isinstance(count, bool) or not isinstance(count, int) or count < 1:
+            raise ValueError("retained clean commit count must be a positive integer")
+        if self.clean_commit_active:
+            raise RuntimeError("cannot evict H3 history during a clean commit")
+        blocks = len(self._commit_token_counts)
+        if blocks <= count:
+            return
+        self._retain_commit_rows([(index, False) for index in range(blocks - count, blocks)])
+
+    def retain_sink_and_recent_commits(self, recent_count: int | None = None, *,
+                                       sink_video_only: bool = True) -> None:
+        """Keep the first chunk's video sink and the most recent clean chunks.
+
+        Without arguments, the T recipe: block 0's video rows and the two newest blocks
+        (T/streaming/cache.py:206-218). With ``recent_count`` (FL2AV,
+        F/streaming/cache.py:964-995): block 0, whole while it is still among the newest
+        ``recent_count`` blocks and otherwise its video rows only (all of it without
+        ``sink_video_only``), plus the newest ``recent_count`` blocks.
+        """
+
+        self._require_valid()
         if self.clean_commit_active:
             raise RuntimeError("cannot trim persistent KV during an active clean commit")
         block_count = len(self._commit_token_counts)
-        if block_count <= 2:
+        if recent_count is None:
+            if block_count <= 2:
+                return
+            recent_start = max(1, block_count - 2)
+            selection = [(0, True)] + [(index, False) for index in range(recent_start, block_count)]
+            self._retain_commit_rows(selection)
             return
-        recent_start = max(1, block_count - 2)
-        selection = [(0, True)] + [(index, False) for index in range(recent_start, block_count)]
+        if isinstance(recent_count, bool) or not isinstance(recent_count, int) or recent_count < 0:
+            raise ValueError("recent clean commit count must be non-negative")
+        if block_count == 0:
+            return
+        recent_start = max(0, block_count - recent_count)
+        selection = [(0, bool(sink_video_only and recent_start > 0))]
+        selection += [(index, False) for index in range(max(1, recent_start), block_count)]
+        if selection == [(index, False) for index in range(block_count)]:
+            return
         self._retain_commit_rows(selection)
 
     def drop_audio_history(self) -> int:
@@ -502,6 +595,134 @@ class CleanAVKVCache:
 
         self._clear_staging()
 
+    # ------------------------------------------------------------------ FL2AV history views
+    def _block_offsets(self) -> list[int]:
+        offsets = [0]
+        for count in self._commit_token_counts:
+            offsets.append(offsets[-1] + count)
+        return offsets
+
+    def _rows_view(self, layer_name: str, rows: list[int]) -> AVKV | None:
+        """Dense copies of the given logical history rows, in order (one gather launch)."""
+
+        paged = self._layers.get(layer_name)
+        if paged is None or not rows:
+            return None
+        key = torch.empty(len(rows), paged.heads, paged.head_dim, dtype=paged.dtype,
+                          device=paged.device)
+        value = torch.empty_like(key)
+        index = torch.tensor(rows, dtype=torch.int32).pin_memory().to(paged.device, non_blocking=True)
+        kv_copy_rows([paged.key, paged.value], [key, value], count=len(rows), src_table=paged.table,
+                     src_index=index)
+        return AVKV(key=key, value=value)
+
+    def history_blocks(self, layer_name: str) -> tuple[AVKV, ...]:
+        """One dense copy per retained clean block (F/streaming/cache.py:344-366)."""
+
+        self._require_valid()
+        _validate_layer_name(layer_name, self.layer_names)
+        offsets = self._block_offsets()
+        views = (self._rows_view(layer_name, list(range(offsets[i], offsets[i + 1])))
+                 for i in range(len(self._commit_token_counts)))
+        return tuple(v for v in views if v is not None)
+
+    def recent_history(self, layer_name: str, count: int) -> AVKV | None:
+        """The newest ``count`` blocks (F/streaming/cache.py:287-300)."""
+
+        if isinstance(count, bool) or not isinstance(count, int) or count < 0:
+            raise ValueError("recent H3 history count must be non-negative")
+        self._require_valid()
+        _validate_layer_name(layer_name, self.layer_names)
+        if count == 0 or not self._commit_token_counts:
+            return None
+        offsets = self._block_offsets()
+        first = max(0, len(self._commit_token_counts) - count)
+        return self._rows_view(layer_name, list(range(offsets[first], offsets[-1])))
+
+    def sink_and_recent_history(self, layer_name: str, recent_count: int) -> AVKV | None:
+        """Block 0 plus the newest ``recent_count`` other blocks (F/streaming/cache.py:302-342)."""
+
+        if isinstance(recent_count, bool) or not isinstance(recent_count, int) or recent_count < 0:
+            raise ValueError("recent H3 history count must be non-negative")
+        self._require_valid()
+        _validate_layer_name(layer_name, self.layer_names)
+        blocks = len(self._commit_token_counts)
+        if blocks == 0:
+            return None
+        offsets = self._block_offsets()
+        start = max(1, blocks - recent_count)
+        rows = list(range(offsets[0], offsets[1])) + list(range(offsets[start], offsets[-1]))
+        return self._rows_view(layer_name, rows)
+
+    def attention_history_rows(self, *, count: int, recent_full_blocks: int,
+                               older_video_stride: int, preserve_sink: bool = False) -> list[int] | None:
+        """Logical history rows of ``attention_history``, in order (None: no history)."""
+
+        if recent_full_blocks < 0 or older_video_stride < 1:
+            raise ValueError("invalid H3 attention-history policy")
+        self._require_valid()
+        n = len(self._commit_token_counts)
+        if n == 0 or count <= 0:
+            return None
+        if preserve_sink:
+            blocks = [0, *range(max(1, n - max(0, count - 1)), n)]
+        else:
+            blocks = list(range(max(0, n - count), n))
+        offsets = self._block_offsets()
+        dense = older_video_stride == 1 or recent_full_blocks >= len(blocks)
+        dense_start = max(0, len(blocks) - recent_full_blocks)
+        rows: list[int] = []
+        for position, block in enumerate(blocks):
+            start, tags = offsets[block], self._commit_token_tags[block]
+            if dense or position >= dense_start:
+                rows.extend(range(start, start + len(tags)))
+                continue
+            ordinal = 0
+            for i, tag in enumerate(tags):
+                if tag == AUDIO_TOKEN_TAG:
+                    rows.append(start + i)
+                elif tag == VIDEO_TOKEN_TAG:
+                    if ordinal % older_video_stride == 0:
+                        rows.append(start + i)
+                    ordinal += 1
+        return rows
+
+    def attention_history(self, layer_name: str, *, count: int, recent_full_blocks: int,
+                          older_video_stride: int, preserve_sink: bool = False) -> AVKV | None:
+        """Dense recent blocks and structured-sparse older video rows (every audio row and
+        every ``older_video_stride``-th video row of the older blocks) of the newest ``count``
+        blocks, or of block 0 plus the newest ``count - 1`` (F/streaming/cache.py:501-575)."""
+
+        _validate_layer_name(layer_name, self.layer_names)
+        rows = self.attention_history_rows(count=count, recent_full_blocks=recent_full_blocks,
+                                           older_video_stride=older_video_stride,
+                                           preserve_sink=preserve_sink)
+        return None if rows is None else self._rows_view(layer_name, rows)
+
+    def advance_serial_without_history_commit(self, block_index: int) -> None:
+        """Close one generated block without committing it (F/streaming/cache.py:1111-1122)."""
+
+        if self.clean_commit_active:
+            raise RuntimeError("cannot advance H3 serial during a clean commit")
+        if block_index != self._block_index:
+            raise ValueError(f"clean block order mismatch: expected {self._block_index}, "
+                             f"got {block_index}")
+        self._block_index += 1
+
+    def discard_retained_history_preserve_serial(self) -> int:
+        """Drop the retained history, keep the logical chunk count (F/streaming/cache.py:1123-1138)."""
+
+        if self.clean_commit_active:
+            raise RuntimeError("cannot discard H3 history during a clean commit")
+        removed = self.history_tokens
+        for paged in self._layers.values():
+            paged.release()
+            if paged.fp8 is not None:
+                paged.fp8.release()
+        self._commit_token_counts.clear()
+        self._commit_token_tags.clear()
+        return removed
+
     def clear(self) -> None:
         """Clear persistent and staged KV and reset the logical chunk count."""
 
@@ -513,6 +734,7 @@ class CleanAVKVCache:
         self._commit_token_tags.clear()
         self._block_index = 0
         self._clear_staging()
+        self._invalid_after_failed_commit = False
 
     def retained_rows(self, selection: list[tuple[int, bool]]) -> tuple[list[int], list[int], list[tuple[int, ...]]]:
         """Logical rows kept by a ``(commit, video_only)`` selection, with counts and tags."""

@@ -299,3 +299,62 @@ def test_hook_fp8_segmented_history_matches_merged_oracle() -> None:
     ref_cond = oatt.attention(y["q"][cond].float().cpu(), y["k"][cond].float().cpu(),
                               y["v"][cond].float().cpu(), Attn.softmax_scale)
     assert rel_l2(out[:16], ref_cond) <= BF16_TOL
+
+
+def test_fl2av_cache_schedule_matches_reference_golden() -> None:
+    """The FL2AV cache operations on the paged cache (bounded commits, count-based and sink +
+    recent retention, audio drop, strided attention history) against the row tables of the
+    reference's own F CleanAVKVCache (tests/golden/cache_f.npz), with a segmented e4m3
+    history kept alongside."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+
+    with np.load(GOLDEN / "cache_f.npz") as f:
+        g = {k: f[k] for k in f.files}
+    layer = "blocks.0.attn"
+    cache = CleanAVKVCache(KVContract(local_heads=1, head_dim=128), layer_names=(layer,),
+                           segmented_fp8_history=True)
+    serial = 0
+
+    def table(view) -> np.ndarray:
+        if view is None:
+            return np.zeros((0, 2), np.int64)
+        return view.key[:, 0, :2].float().cpu().numpy().astype(np.int64)
+
+    for i, step in enumerate(g["schedule"]):
+        op, *args = str(step).split("|")
+        if op in ("commit", "bounded"):
+            tags = g[f"tags_{i}"]
+            commit = (tags == 0) | (tags == 2)
+            ids = torch.zeros(len(tags), 1, 128)
+            staged = torch.from_numpy(np.nonzero(commit)[0])
+            ids[staged, 0, 0] = serial
+            ids[staged, 0, 1] = torch.arange(staged.numel()).float()
+            kv = ids.bfloat16().cuda()
+            cache.begin_clean_commit(cache.committed_blocks)
+            cache.stage(layer, kv, kv.clone(), torch.from_numpy(tags).cuda(),
+                        torch.from_numpy(commit).cuda())
+            if op == "commit":
+                cache.commit()
+            else:
+                cache.commit(retain_recent_commit_count=int(args[0]))
+            serial += 1
+        elif op == "sink_recent":
+            cache.retain_sink_and_recent_commits(int(args[0]), sink_video_only=args[1] == "True")
+        elif op == "retain_recent":
+            cache.retain_recent_commits(int(args[0]))
+        elif op == "drop":
+            assert cache.drop_audio_history() == int(g[f"removed_{i}"])
+        elif op == "attn":
+            got = cache.attention_history(layer, count=int(args[0]), recent_full_blocks=int(args[1]),
+                                          older_video_stride=int(args[2]),
+                                          preserve_sink=args[3] == "True")
+            assert np.array_equal(table(got), g[f"attn_{i}"]), i
+        assert np.array_equal(table(cache.history(layer)), g[f"rows_{i}"]), i
+        assert list(cache.commit_token_counts) == g[f"counts_{i}"].tolist(), i
+        assert cache.committed_blocks == int(g[f"blocks_{i}"]), i
+        # the e4m3 history holds one part per retained block, with the same row counts
+        seg = cache.layer(layer).fp8
+        assert seg.rows == list(cache.commit_token_counts), i
+        blocks = cache.history_blocks(layer)
+        assert [int(b.key.shape[0]) for b in blocks] == list(cache.commit_token_counts), i

@@ -402,3 +402,35 @@ def test_padded_ulysses_layouts_stay_inside_their_buffers(monkeypatch, heads: in
                           num_heads=heads)
     expect = (1 + (heads % hl != 0)) * 2
     assert len(launched) == expect
+
+
+def test_cache_refuses_use_after_a_failed_commit() -> None:
+    """A commit that fails half way (here: the e4m3 history quantiser cannot run on CPU
+    tensors) leaves the cache invalid until clear(), as FL2AV's does
+    (F/streaming/cache.py:766-778, 221-223)."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+
+    cache = CleanAVKVCache(KVContract(local_heads=1, head_dim=128, device_type="cpu"),
+                           layer_names=("blocks.0.attn",), device="cpu",
+                           segmented_fp8_history=True)
+    tags = torch.tensor([1, 2, 2, 0, 0, 0])
+    commit = torch.tensor([False, True, True, True, True, True])
+    kv = torch.zeros(6, 1, 128, dtype=torch.bfloat16)
+    cache.layer("blocks.0.attn", torch.device("cpu"))  # the hook creates the layer first
+    cache.begin_clean_commit(0)
+    cache.stage_in_place("blocks.0.attn", kv, kv, tags, commit)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cache.commit()
+    for probe in (lambda: cache.committed_blocks, lambda: cache.history_tokens,
+                  lambda: cache.history("blocks.0.attn"), lambda: cache.retain_recent_commits(1)):
+        with pytest.raises(RuntimeError, match="invalid after a failed clean commit"):
+            probe()
+    cache.clear()
+    assert cache.committed_blocks == 0 and cache.history_tokens == 0
+    with pytest.raises(ValueError, match="bounded clean commit count must be positive"):
+        cache.commit_bounded(0)
+    with pytest.raises(ValueError, match="retained clean commit count"):
+        cache.retain_recent_commits(0)
+    with pytest.raises(ValueError, match="recent clean commit count must be non-negative"):
+        cache.retain_sink_and_recent_commits(-1)
