@@ -62,22 +62,6 @@ __device__ long long g_h3sa_trace[2][kTraceBlocks][24];
   } while (0)
 #endif
 
-// Exponentials of P: columns (j mod 16) < H3SA_EXP2_FMA_PER16 of each row use the FMA-pipe
-// exp2 (exp2_pair_fma), the rest the MUFU, so both pipes share the work (even values only).
-#ifndef H3SA_EXP2_FMA_PER16
-#define H3SA_EXP2_FMA_PER16 0
-#endif
-static_assert(H3SA_EXP2_FMA_PER16 % 2 == 0 && H3SA_EXP2_FMA_PER16 <= 16, "pairs of columns");
-
-__device__ __forceinline__ void exp2_split(int j, float x0, float x1, float& p0, float& p1) {
-  if ((j & 15) < H3SA_EXP2_FMA_PER16) {  // j is a compile-time constant in the unrolled loops
-    f2_unpack(exp2_pair_fma(f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f))), p0, p1);
-  } else {
-    p0 = fast_exp2(x0);
-    p1 = fast_exp2(x1);
-  }
-}
-
 template <bool kFp8>
 struct AttnCfg {
   static constexpr int kElem = kFp8 ? 1 : 2;
@@ -670,8 +654,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint32_t pk[kBlockN / 2];  // bf16: one pair per word; e4m3: two pairs per word
 #pragma unroll
         for (int j = 0; j < kBlockN; j += 2) {
-          float p0, p1;
-          exp2_split(j, s[j], s[j + 1], p0, p1);
+          const float p0 = fast_exp2(s[j]);
+          const float p1 = fast_exp2(s[j + 1]);
           sum2 = f2_add(sum2, f2_pack(p0, p1));
           if constexpr (kFp8) {
             uint16_t q;
@@ -1283,8 +1267,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t pk[32];  // bf16: 32 words of pairs; e4m3: 16 words of quads
 #pragma unroll
       for (int j = 0; j < 64; j += 2) {
-        float p0, p1;
-        exp2_split(j, s[j], s[j + 1], p0, p1);
+        const float p0 = fast_exp2(s[j]);
+        const float p1 = fast_exp2(s[j + 1]);
         sum2 = f2_add(sum2, f2_pack(p0, p1));
         if constexpr (kFp8) {
           uint16_t qq;

@@ -288,29 +288,6 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   return d;
 }
 
-// 2^x for a pair of fp32 values on the FMA and integer pipes only (no MUFU and no conversion
-// instruction, which would share the MUFU's pipe): j = round(x) sits in the low mantissa bits
-// of x + 1.5 * 2^23, 2^(x - j) comes from a degree-3 polynomial on [-1/2, 1/2] fitted for
-// relative error (max 7.5e-5, well below a bf16 or e4m3 rounding of P), and j is added to
-// the exponent field with an integer add. x must lie in [-125, 127].
-__device__ __forceinline__ uint64_t exp2_pair_fma(uint64_t x) {
-  const uint64_t t = f2_add(x, f2_pack(12582912.0f, 12582912.0f));
-  const uint64_t j = f2_add(t, f2_pack(-12582912.0f, -12582912.0f));
-  const uint64_t f = f2_fma(j, f2_pack(-1.0f, -1.0f), x);
-  uint64_t q = f2_fma(f, f2_pack(0.055172763764858246f, 0.055172763764858246f),
-                      f2_pack(0.24261127412319183f, 0.24261127412319183f));
-  q = f2_fma(q, f, f2_pack(0.6932607889175415f, 0.6932607889175415f));
-  q = f2_fma(q, f, f2_pack(0.9999280571937561f, 0.9999280571937561f));
-  uint32_t tl, th, ql, qh;
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(tl), "=r"(th) : "l"(t));
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(ql), "=r"(qh) : "l"(q));
-  ql += tl << 23;  // the low 9 bits of t hold j (two's complement)
-  qh += th << 23;
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(ql), "r"(qh));
-  return r;
-}
-
 // Packed bf16 pairs: each lane's product / sum rounded once to bf16 (round to nearest even).
 __device__ __forceinline__ uint32_t bf2_mul(uint32_t a, uint32_t b) {
   uint32_t d;
