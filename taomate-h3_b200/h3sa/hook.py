@@ -61,6 +61,27 @@ def _live_documents_from_mask(commit_mask: torch.Tensor,
     return tuple(live)
 
 
+def _live_documents_from_mask_or_hint(commit_mask: torch.Tensor,
+                                      boundaries: Sequence[tuple[int, int]],
+                                      live_documents_hint: tuple[int, ...] | None) -> tuple[int, ...]:
+    """The FL2AV form: a caller that knows the live documents passes them and the commit mask
+    is not read for it (F/streaming/attention_hook.py:337-371, same checks and messages)."""
+
+    if live_documents_hint is None:
+        return _live_documents_from_mask(commit_mask, boundaries)
+    if not isinstance(live_documents_hint, tuple):
+        raise TypeError("live document hint must be a tuple")
+    count = len(boundaries)
+    if any(isinstance(i, bool) or not isinstance(i, int) or i < 0 or i >= count
+           for i in live_documents_hint):
+        raise ValueError("live document hint contains an invalid document index")
+    if tuple(sorted(set(live_documents_hint))) != live_documents_hint:
+        raise ValueError("live document hint must be sorted and unique")
+    if any(boundaries[i][0] == boundaries[i][1] for i in live_documents_hint):
+        raise ValueError("live document hint references an empty document")
+    return live_documents_hint
+
+
 def _as_range(indices: torch.Tensor) -> tuple[int, int] | None:
     """(first, stop) when the sorted host index list is one contiguous run."""
 
@@ -181,11 +202,12 @@ class H3StreamingAttentionHook:
             raise RuntimeError(f"{layer_name}: streaming attention requires {contract.device_type} QKV")
 
     def _resolve_plan(self, boundaries: tuple[tuple[int, int], ...],
-                      commit_mask: torch.Tensor, device: torch.device) -> _DocumentPlan:
+                      commit_mask: torch.Tensor, device: torch.device,
+                      live_documents_hint: tuple[int, ...] | None = None) -> _DocumentPlan:
         points = tuple(b for _, b in boundaries)
         if self._plan is not None and self._plan_key == points:
             return self._plan
-        live = _live_documents_from_mask(commit_mask, boundaries)
+        live = _live_documents_from_mask_or_hint(commit_mask, boundaries, live_documents_hint)
         if len(live) != 1:
             raise RuntimeError(f"direct streaming expects exactly one live document, got {live}")
         plan = _DocumentPlan(boundaries, live[0], commit_mask.detach().to("cpu", torch.bool), device)
@@ -194,7 +216,15 @@ class H3StreamingAttentionHook:
 
     def __call__(self, *, attention: object, layer_name: str, query: torch.Tensor,
                  key: torch.Tensor, value: torch.Tensor, token_tags: torch.Tensor,
-                 commit_mask: torch.Tensor, cu_seqlens_host: Sequence[int]) -> torch.Tensor:
+                 commit_mask: torch.Tensor, cu_seqlens_host: Sequence[int] | None = None,
+                 cu_seqlens: torch.Tensor | None = None, max_seqlen: int | None = None,
+                 live_documents_hint: tuple[int, ...] | None = None) -> torch.Tensor:
+        """The T call (T/streaming/attention_hook.py:118-129) or the FL2AV one
+        (F/streaming/attention_hook.py:739-753): ``cu_seqlens`` (device) stands in for
+        ``cu_seqlens_host`` when that is None, ``max_seqlen`` is not needed, and
+        ``live_documents_hint`` names the live document without reading the commit mask."""
+
+        del max_seqlen
         if not self.active:
             raise RuntimeError("streaming attention hook was called while inactive")
         self._validate_qkv(layer_name, query, key, value)
@@ -202,12 +232,16 @@ class H3StreamingAttentionHook:
             raise RuntimeError(f"{layer_name}: commit_mask does not match packed QKV rows")
         if token_tags.ndim != 1 or token_tags.shape[0] != query.shape[0]:
             raise RuntimeError(f"{layer_name}: token_tags does not match packed QKV rows")
+        if cu_seqlens_host is None:
+            if cu_seqlens is None:
+                raise RuntimeError(f"{layer_name}: packed sequence boundaries are missing")
+            cu_seqlens_host = cu_seqlens.tolist()
         points = tuple(int(point) for point in cu_seqlens_host)
         if (len(points) < 2 or points[0] != 0 or points[-1] != query.shape[0]
                 or any(left > right for left, right in zip(points, points[1:]))):
             raise RuntimeError(f"{layer_name}: invalid packed sequence boundaries")
         boundaries = tuple(zip(points[:-1], points[1:]))
-        plan = self._resolve_plan(boundaries, commit_mask, query.device)
+        plan = self._resolve_plan(boundaries, commit_mask, query.device, live_documents_hint)
         scale = float(getattr(attention, "softmax_scale"))
 
         query = query.contiguous()

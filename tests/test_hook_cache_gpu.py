@@ -358,3 +358,29 @@ def test_fl2av_cache_schedule_matches_reference_golden() -> None:
         assert seg.rows == list(cache.commit_token_counts), i
         blocks = cache.history_blocks(layer)
         assert [int(b.key.shape[0]) for b in blocks] == list(cache.commit_token_counts), i
+
+
+def test_hook_fl2av_call_form_matches_t_form() -> None:
+    """The FL2AV call (device cu_seqlens, max_seqlen, live_documents_hint) gives the same
+    bits as the T call with host boundaries."""
+
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads = 2
+    x = _layout(heads, 512, False, seed=8)
+    outs = []
+    for form in ("t", "f"):
+        cache = _cache_with_history(heads, x)
+        hook = H3StreamingAttentionHook(cache)
+        hook.activate(HookMode.NOISY)
+        kw = dict(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+                  value=x["v"], token_tags=x["tags"], commit_mask=x["commit"])
+        if form == "t":
+            out = hook(**kw, cu_seqlens_host=x["cu"])
+        else:
+            out = hook(**kw, cu_seqlens_host=None,
+                       cu_seqlens=torch.tensor(x["cu"], dtype=torch.int32, device="cuda"),
+                       max_seqlen=304, live_documents_hint=(0,))
+        hook.check_device_error()
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])

@@ -434,3 +434,25 @@ def test_cache_refuses_use_after_a_failed_commit() -> None:
         cache.retain_recent_commits(0)
     with pytest.raises(ValueError, match="recent clean commit count must be non-negative"):
         cache.retain_sink_and_recent_commits(-1)
+
+
+def test_live_document_hint_checks_match_reference() -> None:
+    """FL2AV's live_documents_hint: same checks and messages as
+    F/streaming/attention_hook.py:337-371; without a hint the commit mask decides."""
+
+    from h3sa.hook import _live_documents_from_mask_or_hint as live
+
+    bounds = ((0, 4), (4, 4), (4, 9))
+    mask = torch.tensor([False, True, True, False, False, False, False, False, False])
+    assert live(mask, bounds, None) == (0,)
+    assert live(mask, bounds, (2,)) == (2,)
+    with pytest.raises(TypeError, match="must be a tuple"):
+        live(mask, bounds, [0])
+    with pytest.raises(ValueError, match="invalid document index"):
+        live(mask, bounds, (3,))
+    with pytest.raises(ValueError, match="invalid document index"):
+        live(mask, bounds, (True,))
+    with pytest.raises(ValueError, match="sorted and unique"):
+        live(mask, bounds, (2, 0))
+    with pytest.raises(ValueError, match="empty document"):
+        live(mask, bounds, (1,))
