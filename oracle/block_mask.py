@@ -17,8 +17,9 @@ Two selection rules over the logical KV sequence ``[history | current ...]``:
 
 Arithmetic is fixed so that CPU and GPU selections agree bit for bit: block sums of bf16
 values in fp64 (exact for these magnitudes, hence order independent), means by one fp64
-division, dot products accumulated sequentially over d in fp64 with separate multiply and
-add, one fp64 multiply by d^-0.5. Ties rank the lower block index first. The reference
+division, dot products in fp64 with separate multiply and add, as eight partial sums (the
+terms d = g, g + 8, g + 16, ... accumulated in order for g = 0..7) combined as
+((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7)), one fp64 multiply by d^-0.5. Ties rank the lower block index first. The reference
 computes the same quantities in fp32 with an unspecified summation order and tie rule; the
 two agree wherever the k-th and (k+1)-th scores are further apart than fp32 rounding,
 which ``selection_margin`` reports.
@@ -48,12 +49,19 @@ def block_means(x: np.ndarray, block: int = BLOCK) -> np.ndarray:
     return sums / counts[None, :, None]
 
 
-def block_scores(q_mean: np.ndarray, k_mean: np.ndarray, head_dim: int) -> np.ndarray:
-    """[H, QB, D] x [H, KB, D] -> [H, QB, KB]: sequential fp64 dot over d, times d^-0.5."""
+PARTIALS = 8
 
-    acc = np.zeros((q_mean.shape[0], q_mean.shape[1], k_mean.shape[1]), dtype=np.float64)
+
+def block_scores(q_mean: np.ndarray, k_mean: np.ndarray, head_dim: int) -> np.ndarray:
+    """[H, QB, D] x [H, KB, D] -> [H, QB, KB]: fp64 dot over d in the fixed order above, times
+    d^-0.5."""
+
+    shape = (q_mean.shape[0], q_mean.shape[1], k_mean.shape[1])
+    part = [np.zeros(shape, dtype=np.float64) for _ in range(PARTIALS)]
     for dd in range(q_mean.shape[2]):
-        acc = acc + q_mean[:, :, None, dd] * k_mean[:, None, :, dd]
+        g = dd % PARTIALS
+        part[g] = part[g] + q_mean[:, :, None, dd] * k_mean[:, None, :, dd]
+    acc = ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]))
     return acc * (float(head_dim) ** -0.5)
 
 

@@ -11,10 +11,12 @@
 //          the +-`window` band around the query block's timeline position
 //          floor((n_hist + 128 j) / 128), then fill a ceil(density * KB) budget by score.
 //
-// Exact, order-independent arithmetic: block sums of bf16 values in fp64 (exact), means by
-// one fp64 division, dot products accumulated over d = 0..127 in order with separately
-// rounded fp64 multiply and add, one fp64 multiply by d^-0.5; ties rank the lower block
-// first. A CPU restatement of these steps reproduces the selection bit for bit.
+// Exact, order-fixed arithmetic: block sums of bf16 values in fp64 (exact), means by one fp64
+// division, dot products with separately rounded fp64 multiply and add as eight partial sums
+// (terms d = g, g + 8, ... in order, g = 0..7) combined as ((s0 + s1) + (s2 + s3)) +
+// ((s4 + s5) + (s6 + s7)), one fp64 multiply by d^-0.5; ties rank the lower block first. A CPU
+// restatement of these steps reproduces the selection bit for bit. Eight independent chains
+// keep the score loop from waiting on one 128-step chain of dependent additions.
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
@@ -144,10 +146,15 @@ __global__ void __launch_bounds__(256) mask_select_kernel(const MaskParams p) {
   for (int b = tid; b < p.kb; b += blockDim.x) {
     if (!cand[b]) continue;
     const double* km = p.k_mean + static_cast<size_t>(h) * kHeadDim * p.kb_means + b;
-    double acc = 0.0;
-#pragma unroll 8
-    for (int d = 0; d < kHeadDim; ++d)
-      acc = __dadd_rn(acc, __dmul_rn(qm[d], km[static_cast<size_t>(d) * p.kb_means]));
+    double part[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+#pragma unroll 4
+    for (int d0 = 0; d0 < kHeadDim; d0 += 8) {
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        part[g] = __dadd_rn(part[g], __dmul_rn(qm[d0 + g], km[static_cast<size_t>(d0 + g) * p.kb_means]));
+    }
+    const double acc = __dadd_rn(__dadd_rn(__dadd_rn(part[0], part[1]), __dadd_rn(part[2], part[3])),
+                                 __dadd_rn(__dadd_rn(part[4], part[5]), __dadd_rn(part[6], part[7])));
     score[b] = __dmul_rn(acc, p.scale);
   }
   __syncthreads();
