@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
+#include <climits>
 #include <cmath>
 #include <cstring>
 
@@ -53,55 +54,68 @@ struct MaskParams {
   int* err;
 };
 
-// grid (H, QB + kb_means), 128 threads (one per d column)
-__global__ void __launch_bounds__(128) mask_means_kernel(const MaskParams p) {
+// grid (H, QB + kb_means), 256 threads: lane c = tid % 16 owns dims [8c, 8c + 8) of every
+// row, row group g = tid / 16 takes rows g, g + 16, ... of the block; all of a thread's rows
+// are loaded (16-byte vectors, coalesced) before they are summed. The 16 row groups' fp64
+// partial sums are exact, so adding them in shared memory in any order gives the exact
+// block sum.
+__global__ void __launch_bounds__(256) mask_means_kernel(const MaskParams p) {
+  __shared__ double part[16][kHeadDim];
   const int h = blockIdx.x;
   const int blk = blockIdx.y;
-  const int d = threadIdx.x;
-  double sum = 0.0;
-  int count = 0;
-  if (blk < p.qb) {
-    const int r0 = p.q_lo + blk * kBlockM;
-    const int r1 = min(r0 + kBlockM, p.q_hi);
-    // four independent partial sums: exact in fp64, so their order does not matter
-    const __nv_bfloat16* qb = p.query + static_cast<size_t>(h) * kHeadDim + d;
-    const size_t rs = static_cast<size_t>(p.heads) * kHeadDim;
-    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-    int r = r0;
-    for (; r + 4 <= r1; r += 4) {
-      a0 += static_cast<double>(__bfloat162float(qb[(r + 0) * rs]));
-      a1 += static_cast<double>(__bfloat162float(qb[(r + 1) * rs]));
-      a2 += static_cast<double>(__bfloat162float(qb[(r + 2) * rs]));
-      a3 += static_cast<double>(__bfloat162float(qb[(r + 3) * rs]));
-    }
-    for (; r < r1; ++r) a0 += static_cast<double>(__bfloat162float(qb[r * rs]));
-    sum = (a0 + a1) + (a2 + a3);
-    count = r1 - r0;
-    p.q_mean[(static_cast<size_t>(h) * p.qb + blk) * kHeadDim + d] = sum / count;
+  const int c = threadIdx.x & 15;
+  const int g = threadIdx.x >> 4;
+  const bool is_q = blk < p.qb;
+  int r0, r1;
+  const __nv_bfloat16* base;  // row 0 of the block for this head, column 0
+  size_t row_stride;          // elements between rows
+  if (is_q) {
+    r0 = p.q_lo + blk * kBlockM;
+    r1 = min(r0 + kBlockM, p.q_hi);
+    base = p.query + (static_cast<size_t>(r0) * p.heads + h) * kHeadDim;
+    row_stride = static_cast<size_t>(p.heads) * kHeadDim;
   } else {
     const int b = blk - p.qb;
-    const int r0 = b * kBlockN;
-    const int r1 = min(r0 + kBlockN, p.mode == 0 ? p.full_hist * kBlockN : p.n_kv);
+    r0 = b * kBlockN;
+    r1 = min(r0 + kBlockN, p.mode == 0 ? p.full_hist * kBlockN : p.n_kv);
     const int page = (b < p.table_blocks) ? p.page_table[b] : -1;
     if (page < 0 || page >= p.pool_pages) {
-      if (d == 0 && p.err) atomicOr(p.err, kErrBadPage);
-      return;
+      if (threadIdx.x == 0 && p.err) atomicOr(p.err, kErrBadPage);
+      return;  // the whole CTA leaves before the barrier below
     }
-    const __nv_bfloat16* base =
-        p.key_pool + ((static_cast<size_t>(h) * p.pool_pages + page) * kBlockN) * kHeadDim + d;
-    double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
-    const int n = r1 - r0;
-    int i = 0;
-    for (; i + 4 <= n; i += 4) {
-      a0 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 0) * kHeadDim]));
-      a1 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 1) * kHeadDim]));
-      a2 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 2) * kHeadDim]));
-      a3 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i + 3) * kHeadDim]));
+    base = p.key_pool + ((static_cast<size_t>(h) * p.pool_pages + page) * kBlockN) * kHeadDim;
+    row_stride = kHeadDim;
+  }
+  const int n = r1 - r0;
+  uint4 v[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = g + 16 * k;
+    v[k] = i < n ? __ldg(reinterpret_cast<const uint4*>(base + i * row_stride) + c)
+                 : make_uint4(0u, 0u, 0u, 0u);
+  }
+  double acc[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      acc[2 * e] += static_cast<double>(__uint_as_float(w[e] << 16));
+      acc[2 * e + 1] += static_cast<double>(__uint_as_float(w[e] & 0xFFFF0000u));
     }
-    for (; i < n; ++i) a0 += static_cast<double>(__bfloat162float(base[static_cast<size_t>(i) * kHeadDim]));
-    sum = (a0 + a1) + (a2 + a3);
-    count = r1 - r0;
-    p.k_mean[(static_cast<size_t>(h) * kHeadDim + d) * p.kb_means + b] = sum / count;
+  }
+#pragma unroll
+  for (int e = 0; e < 8; ++e) part[g][8 * c + e] = acc[e];
+  __syncthreads();
+  if (threadIdx.x < kHeadDim) {
+    const int d = threadIdx.x;
+    double sum = 0.0;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) sum += part[k][d];
+    if (is_q)
+      p.q_mean[(static_cast<size_t>(h) * p.qb + blk) * kHeadDim + d] = sum / n;
+    else
+      p.k_mean[(static_cast<size_t>(h) * kHeadDim + d) * p.kb_means + (blk - p.qb)] = sum / n;
   }
 }
 
@@ -109,6 +123,7 @@ __global__ void __launch_bounds__(128) mask_means_kernel(const MaskParams p) {
 __global__ void __launch_bounds__(256) mask_select_kernel(const MaskParams p) {
   __shared__ double qm[kHeadDim];
   __shared__ double score[kMaskMaxBlocks];
+  __shared__ long long rank_key[kMaskMaxBlocks];
   __shared__ uint8_t cand[kMaskMaxBlocks];
   __shared__ uint8_t keep[kMaskMaxBlocks];
   __shared__ int warp_count[8];
@@ -142,29 +157,56 @@ __global__ void __launch_bounds__(256) mask_select_kernel(const MaskParams p) {
   int forced_total = 0;
   for (int w = 0; w < (blockDim.x >> 5); ++w) forced_total += warp_count[w];
   const int take = (p.mode == 0) ? p.keep_count : max(0, p.budget - forced_total);
-  // scores of the candidates: sequential fp64 dot over d
-  for (int b = tid; b < p.kb; b += blockDim.x) {
-    if (!cand[b]) continue;
-    const double* km = p.k_mean + static_cast<size_t>(h) * kHeadDim * p.kb_means + b;
-    double part[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
-#pragma unroll 4
-    for (int d0 = 0; d0 < kHeadDim; d0 += 8) {
+  // scores of the candidates: a warp takes four candidates at a time; lane l computes partial
+  // sum l % 8 (terms d = g, g + 8, ... in order) of candidate l / 8, and the eight partials
+  // are combined by shuffles in the fixed tree ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7))
+  {
+    const int lane = tid & 31;
+    const int g = lane & 7;
+    const int sub = lane >> 3;
+    const double* kh = p.k_mean + static_cast<size_t>(h) * kHeadDim * p.kb_means;
+    for (int b0 = (tid >> 5) * 4; b0 < p.kb; b0 += (blockDim.x >> 5) * 4) {
+      const int b = b0 + sub;
+      const bool active = b < p.kb && cand[b];
+      double part = 0.0;
+      if (active) {
+        double kv[16];
 #pragma unroll
-      for (int g = 0; g < 8; ++g)
-        part[g] = __dadd_rn(part[g], __dmul_rn(qm[d0 + g], km[static_cast<size_t>(d0 + g) * p.kb_means]));
+        for (int i = 0; i < 16; ++i) kv[i] = kh[static_cast<size_t>(g + 8 * i) * p.kb_means + b];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) part = __dadd_rn(part, __dmul_rn(qm[g + 8 * i], kv[i]));
+      }
+      const double p1 = __shfl_xor_sync(0xffffffffu, part, 1);
+      const double pair = (g & 1) ? __dadd_rn(p1, part) : __dadd_rn(part, p1);     // s0+s1, ...
+      const double p2 = __shfl_xor_sync(0xffffffffu, pair, 2);
+      const double quad = (g & 2) ? __dadd_rn(p2, pair) : __dadd_rn(pair, p2);   // (..)+(..)
+      const double p4 = __shfl_xor_sync(0xffffffffu, quad, 4);
+      const double all = (g & 4) ? __dadd_rn(p4, quad) : __dadd_rn(quad, p4);
+      if (active && g == 0) score[b] = __dmul_rn(all, p.scale);
     }
-    const double acc = __dadd_rn(__dadd_rn(__dadd_rn(part[0], part[1]), __dadd_rn(part[2], part[3])),
-                                 __dadd_rn(__dadd_rn(part[4], part[5]), __dadd_rn(part[6], part[7])));
-    score[b] = __dmul_rn(acc, p.scale);
+  }
+  __syncthreads();
+  // order-preserving integer keys of the scores (non-candidates lowest), so the ranking below
+  // compares integers instead of doubles
+  for (int b = tid; b < p.kb; b += blockDim.x) {
+    long long k = LLONG_MIN;
+    if (cand[b]) {
+      // -0 and +0 are equal scores (the lower index ranks first), so both map to key 0
+      const long long bits = score[b] == 0.0 ? 0LL : __double_as_longlong(score[b]);
+      k = bits >= 0 ? bits : bits ^ 0x7FFFFFFFFFFFFFFFLL;
+    }
+    rank_key[b] = k;
   }
   __syncthreads();
   // rank each candidate: better score, or equal score and lower index
   for (int b = tid; b < p.kb; b += blockDim.x) {
     if (!cand[b]) continue;
-    const double s = score[b];
+    const long long kb_key = rank_key[b];
     int rank = 0;
-    for (int c = 0; c < p.kb && rank < take; ++c)
-      if (cand[c] && (score[c] > s || (score[c] == s && c < b))) ++rank;
+    for (int c = 0; c < p.kb; ++c) {
+      const long long kc = rank_key[c];
+      rank += (kc > kb_key) | ((kc == kb_key) & (c < b));
+    }
     if (rank < take) keep[b] = 1;
   }
   __syncthreads();
@@ -210,6 +252,8 @@ int h3sa_block_mask(const void* query, int32_t rows, int32_t heads, int32_t head
   if (heads <= 0 || q_lo < 0 || q_hi <= q_lo || q_hi > rows || pool_pages <= 0 ||
       table_blocks <= 0)
     return set_error(H3SA_ERR_INVALID, "block mask: invalid sizes");
+  if ((reinterpret_cast<uintptr_t>(query) | reinterpret_cast<uintptr_t>(key_pool)) & 15)
+    return set_error(H3SA_ERR_INVALID, "block mask: query and key pool must be 16-byte aligned");
   const h3sa_mask_policy& pol = *policy;
   if (pol.mode != 0 && pol.mode != 1)
     return set_error(H3SA_ERR_INVALID, "block mask: unknown policy mode %d", pol.mode);
@@ -270,7 +314,7 @@ int h3sa_block_mask(const void* query, int32_t rows, int32_t heads, int32_t head
   if (e != cudaSuccess) return set_cuda_error("cudaMallocAsync(block mask scratch)", e);
   p.q_mean = static_cast<double*>(scratch);
   p.k_mean = p.q_mean + static_cast<size_t>(heads) * p.qb * kHeadDim;
-  mask_means_kernel<<<dim3(heads, p.qb + p.kb_means), 128, 0, s>>>(p);
+  mask_means_kernel<<<dim3(heads, p.qb + p.kb_means), 256, 0, s>>>(p);
   mask_select_kernel<<<dim3(heads, p.qb), 256, 0, s>>>(p);
   e = cudaGetLastError();
   const cudaError_t ef = cudaFreeAsync(scratch, s);
