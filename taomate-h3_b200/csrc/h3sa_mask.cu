@@ -20,7 +20,6 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 
-#include <climits>
 #include <cmath>
 #include <cstring>
 
@@ -123,7 +122,6 @@ __global__ void __launch_bounds__(256) mask_means_kernel(const MaskParams p) {
 __global__ void __launch_bounds__(256) mask_select_kernel(const MaskParams p) {
   __shared__ double qm[kHeadDim];
   __shared__ double score[kMaskMaxBlocks];
-  __shared__ long long rank_key[kMaskMaxBlocks];
   __shared__ uint8_t cand[kMaskMaxBlocks];
   __shared__ uint8_t keep[kMaskMaxBlocks];
   __shared__ int warp_count[8];
@@ -157,56 +155,29 @@ __global__ void __launch_bounds__(256) mask_select_kernel(const MaskParams p) {
   int forced_total = 0;
   for (int w = 0; w < (blockDim.x >> 5); ++w) forced_total += warp_count[w];
   const int take = (p.mode == 0) ? p.keep_count : max(0, p.budget - forced_total);
-  // scores of the candidates: a warp takes four candidates at a time; lane l computes partial
-  // sum l % 8 (terms d = g, g + 8, ... in order) of candidate l / 8, and the eight partials
-  // are combined by shuffles in the fixed tree ((s0 + s1) + (s2 + s3)) + ((s4 + s5) + (s6 + s7))
-  {
-    const int lane = tid & 31;
-    const int g = lane & 7;
-    const int sub = lane >> 3;
-    const double* kh = p.k_mean + static_cast<size_t>(h) * kHeadDim * p.kb_means;
-    for (int b0 = (tid >> 5) * 4; b0 < p.kb; b0 += (blockDim.x >> 5) * 4) {
-      const int b = b0 + sub;
-      const bool active = b < p.kb && cand[b];
-      double part = 0.0;
-      if (active) {
-        double kv[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) kv[i] = kh[static_cast<size_t>(g + 8 * i) * p.kb_means + b];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) part = __dadd_rn(part, __dmul_rn(qm[g + 8 * i], kv[i]));
-      }
-      const double p1 = __shfl_xor_sync(0xffffffffu, part, 1);
-      const double pair = (g & 1) ? __dadd_rn(p1, part) : __dadd_rn(part, p1);     // s0+s1, ...
-      const double p2 = __shfl_xor_sync(0xffffffffu, pair, 2);
-      const double quad = (g & 2) ? __dadd_rn(p2, pair) : __dadd_rn(pair, p2);   // (..)+(..)
-      const double p4 = __shfl_xor_sync(0xffffffffu, quad, 4);
-      const double all = (g & 4) ? __dadd_rn(p4, quad) : __dadd_rn(quad, p4);
-      if (active && g == 0) score[b] = __dmul_rn(all, p.scale);
-    }
-  }
-  __syncthreads();
-  // order-preserving integer keys of the scores (non-candidates lowest), so the ranking below
-  // compares integers instead of doubles
+  // scores of the candidates: sequential fp64 dot over d
   for (int b = tid; b < p.kb; b += blockDim.x) {
-    long long k = LLONG_MIN;
-    if (cand[b]) {
-      // -0 and +0 are equal scores (the lower index ranks first), so both map to key 0
-      const long long bits = score[b] == 0.0 ? 0LL : __double_as_longlong(score[b]);
-      k = bits >= 0 ? bits : bits ^ 0x7FFFFFFFFFFFFFFFLL;
+    if (!cand[b]) continue;
+    const double* km = p.k_mean + static_cast<size_t>(h) * kHeadDim * p.kb_means + b;
+    double part[8] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0};
+#pragma unroll 4
+    for (int d0 = 0; d0 < kHeadDim; d0 += 8) {
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        part[g] = __dadd_rn(part[g], __dmul_rn(qm[d0 + g], km[static_cast<size_t>(d0 + g) * p.kb_means]));
     }
-    rank_key[b] = k;
+    const double acc = __dadd_rn(__dadd_rn(__dadd_rn(part[0], part[1]), __dadd_rn(part[2], part[3])),
+                                 __dadd_rn(__dadd_rn(part[4], part[5]), __dadd_rn(part[6], part[7])));
+    score[b] = __dmul_rn(acc, p.scale);
   }
   __syncthreads();
   // rank each candidate: better score, or equal score and lower index
   for (int b = tid; b < p.kb; b += blockDim.x) {
     if (!cand[b]) continue;
-    const long long kb_key = rank_key[b];
+    const double s = score[b];
     int rank = 0;
-    for (int c = 0; c < p.kb; ++c) {
-      const long long kc = rank_key[c];
-      rank += (kc > kb_key) | ((kc == kb_key) & (c < b));
-    }
+    for (int c = 0; c < p.kb && rank < take; ++c)
+      if (cand[c] && (score[c] > s || (score[c] == s && c < b))) ++rank;
     if (rank < take) keep[b] = 1;
   }
   __syncthreads();
