@@ -606,7 +606,84 @@ def _variant_fp8(peaks: dict, iters: int, dev: torch.device, g: torch.Generator,
         "roofline": {"bound": "tensor", "peak": fp8_peak, "frac": tf / fp8_peak,
                      "peak_source": "2 x measured bf16 burst (no measured e4m3 GEMM peak; "
                                     "nominal dense e4m3 is 4500)"}}
+    out["fp8_segmented_step_1080p_per_gpu"] = _fp8_step(q, k, v, kp, vp, table, nh, iters, dev)
     return out
+
+
+def _fp8_step(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kp: torch.Tensor,
+              vp: torch.Tensor, table: torch.Tensor, nh: int, iters: int,
+              dev: torch.device) -> dict:
+    """One layer call of the segmented FP8 backend against the bf16 one at the same shape.
+
+    The history is four committed chunks of nh / 4 rows, each an e4m3 part quantised once at
+    commit with its own scales (not timed: it happens once per commit, not per call). Timed
+    per call, FP8: the current chunk's K/V as a new part (amax + quantise into block-aligned
+    e4m3 pages), Q quantised per head, one attention launch over the parts. bf16: the current
+    K/V rows appended to the bf16 cache, one attention launch."""
+
+    import h3sa
+    from h3sa.kernels import PAGE_ROWS, attention_fwd_fp8_parts, quantize_fp8_rows
+
+    d = CFG["head_dim"]
+    nq, heads = int(q.shape[0]), int(q.shape[1])
+    parts = [nh // 4] * 4 + [nq]
+    starts, cursor = [], 0
+    for n in parts:
+        starts.append(cursor)
+        cursor = (cursor + n + PAGE_ROWS - 1) // PAGE_ROWS * PAGE_ROWS
+    pages8 = cursor // PAGE_ROWS
+    t8 = torch.arange(pages8, dtype=torch.int32, device=dev)
+    k8 = torch.zeros(heads, pages8 * PAGE_ROWS, d, dtype=torch.float8_e4m3fn, device=dev)
+    v8 = torch.zeros_like(k8)
+    ks = torch.empty(len(parts), heads, dtype=torch.float32, device=dev)
+    vs = torch.empty_like(ks)
+    work = torch.empty(2 * heads, dtype=torch.int32, device=dev)
+    block_part = torch.zeros(pages8, dtype=torch.int32)
+    for i, (s0, n) in enumerate(zip(starts, parts)):
+        for b in range(s0 // PAGE_ROWS, (s0 + n + PAGE_ROWS - 1) // PAGE_ROWS):
+            block_part[b] = i | (min(PAGE_ROWS, s0 + n - b * PAGE_ROWS) << 16)
+    block_part = block_part.to(dev)
+    for i in range(4):  # history parts, quantised at their commits
+        quantize_fp8_rows([k, v], [k8, v8], [ks[i], vs[i]], work, count=parts[i],
+                          src_start=i * (nh // 4), dst_start=starts[i],
+                          dst_table=t8, zero_tail=True)
+    cur_k, cur_v = k[nh:].contiguous(), v[nh:].contiguous()
+    o = torch.empty(nq, heads, d, dtype=torch.bfloat16, device=dev)
+    probs8 = [h3sa.AttentionProblem(0, nq, 0, starts[-1] + nq)]
+    scale = d ** -0.5
+
+    def fp8_call() -> None:
+        quantize_fp8_rows([cur_k, cur_v], [k8, v8], [ks[4], vs[4]], work, count=nq,
+                          dst_start=starts[4], dst_table=t8, zero_tail=True)
+        q8, qs = h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0))
+        attention_fwd_fp8_parts(q8[0], o, k8, v8, t8, probs8, scale, q_scale=qs[0],
+                                block_part=block_part, part_k_scale=ks, part_v_scale=vs)
+
+    probs = [h3sa.AttentionProblem(0, nq, 0, nh + nq)]
+
+    def bf16_call() -> None:
+        h3sa.kv_copy_rows([cur_k, cur_v], [kp, vp], count=nq, dst_table=table, dst_start=nh)
+        h3sa.attention_fwd(q, o, kp, vp, table, probs, scale)
+
+    ms8 = _time_launch(fp8_call, iters)
+    ms16 = _time_launch(bf16_call, iters)
+    q8, qs = h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0))
+    ms_attn = _time_launch(lambda: attention_fwd_fp8_parts(
+        q8[0], o, k8, v8, t8, probs8, scale, q_scale=qs[0], block_part=block_part,
+        part_k_scale=ks, part_v_scale=vs), iters)
+    ms_plain_same_data = _time_launch(lambda: h3sa.attention_fwd(
+        q8[0], o, k8, v8, t8, probs8, scale, q_scale=qs[0], k_scale=ks[0].contiguous(),
+        v_scale=vs[0].contiguous()), iters)
+    ms_kv = _time_launch(lambda: quantize_fp8_rows([cur_k, cur_v], [k8, v8], [ks[4], vs[4]], work,
+                                                   count=nq, dst_start=starts[4], dst_table=t8,
+                                                   zero_tail=True), iters)
+    ms_q = _time_launch(lambda: h3sa.quantize_fp8_e4m3_per_head(q.unsqueeze(0)), iters)
+    flops = 4.0 * nq * (nh + nq) * d * heads
+    return {"fp8_ms": ms8, "bf16_ms": ms16, "speedup": ms16 / ms8,
+            "fp8_parts": {"attention_ms": ms_attn, "kv_part_quant_ms": ms_kv, "q_quant_ms": ms_q,
+                          "one_scale_kernel_same_data_ms": ms_plain_same_data},
+            "fp8_tflops": flops / (ms8 * 1e-3) / 1e12, "bf16_tflops": flops / (ms16 * 1e-3) / 1e12,
+            "history_parts": 4, "queries": nq, "keys": nh + nq, "heads": heads}
 
 
 def _variant_sparse(peaks: dict, iters: int, dev: torch.device, g: torch.Generator,

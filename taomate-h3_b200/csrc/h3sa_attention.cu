@@ -241,7 +241,9 @@ __device__ __forceinline__ void store_tile_rows(uint8_t* stage, int lane, unsign
   }
 }
 
-template <bool kFp8>
+// kParts (e4m3 only): the KV sequence is segmented e4m3 parts with their own scales
+// (AttnParams::block_part); a separate instantiation, so the other launches carry none of it.
+template <bool kFp8, bool kParts = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -542,13 +544,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
       uint64_t scale2 = f2_pack(scale_log2, scale_log2);
       // segmented e4m3 KV: per-block K and V scales (see block_scales)
-      const bool parts = kFp8 && p.block_part != nullptr;
+      constexpr bool parts = kFp8 && kParts;
       float q_sl2 = 0.f;
       float v_cur = 1.f;  // O is accumulated in units of this V scale
       if constexpr (kFp8) {
         v_cur = __ldg(p.v_scale + head);
         if (parts) q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
       }
+      float sl2 = scale_log2;  // S scale of the current part (log2 units)
+      int cur_part = -1;
       // The exponentials of block i of tile 1 follow those of block i of tile 0, and those of
       // block i + 1 of tile 0 follow those of block i of tile 1; a tile that skips a block
       // (block-sparse lists) still takes and passes the turn.
@@ -568,11 +572,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
           continue;
         }
-        BlockScales bs{scale_log2, v_cur, kBlockN};
-        if (parts) {
-          bs = block_scales(p, head, b, q_sl2);
-          scale2 = f2_pack(bs.sl2, bs.sl2);
-        }
+        int rows = kBlockN;
+        bool v_moved = false;  // O moves into another part's V-scale units at this block
+        float vr = 1.0f;
+        if (parts) part_step(p, head, b, q_sl2, c > 0, cur_part, rows, sl2, scale2, v_cur, vr,
+                             v_moved);
         if (!(ok = mbar_wait(smem_u32(&sm.s_full[t]), c & 1, abort_flag, p.err))) break;
         const bool tr = (warp & 3) == 0 && lane == 0;
         if (tr) H3SA_TRACE_AT(i, 5 * t + 0);
@@ -602,7 +606,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         }
         const int col0 = b * kBlockN;
         const int lo = pr.kv_lo - col0;  // valid columns [lo, hi)
-        const int hi = min(pr.kv_hi - col0, bs.rows);
+        const int hi = min(pr.kv_hi - col0, rows);
         // Only the first and last block of a problem (or of a segmented e4m3 part) can be
         // partial. The flag goes through an opaque move: otherwise the compiler can see that every per-column condition below
         // implies it, drop the branch and run 2 x 128 compare/selects on every block.
@@ -623,18 +627,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mx3 = fmax3(mx3, s[j + 3], s[j + 7]);
         }
         const float mx = fmaxf(fmax3(mx0, mx1, mx2), mx3);
-        const float m_blk = mx * bs.sl2;
+        const float m_blk = mx * sl2;
         const bool need = m_blk > m_used + kRescaleThreshold;
         const float m_new = need ? m_blk : m_used;
         // O is rescaled further down, once the previous PV has completed; l now
         const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
-        // entering a part with another V scale moves O into its units (warp-uniform)
-        float vr = 1.0f;
-        if (parts) {
-          vr = c > 0 ? __fdividef(v_cur, bs.vs) : 1.0f;
-          v_cur = bs.vs;
-        }
-        const bool any_need = c > 0 && (__any_sync(0xffffffffu, need) || vr != 1.0f);
+        const bool any_need = c > 0 && (__any_sync(0xffffffffu, need) || v_moved);
         const float o_scale = alpha * vr;
         l_sum *= alpha;
         m_used = m_new;
@@ -891,7 +889,7 @@ static_assert(AttnCfg<false>::kTileBytes * Attn1Cfg<false>::kKStages >= 8 * 32 *
                   AttnCfg<true>::kTileBytes * Attn1Cfg<true>::kKStages >= 8 * 32 * 128,
               "the K ring must hold the epilogue staging of eight warps");
 
-template <bool kFp8, bool kIndep>
+template <bool kFp8, bool kIndep, bool kParts = false>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn1_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const AttnParams p) {
@@ -1172,23 +1170,25 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     bool ok = true;
     uint64_t scale2 = f2_pack(scale_log2, scale_log2);
     // segmented e4m3 KV: per-block K and V scales (see block_scales)
-    const bool parts = kFp8 && p.block_part != nullptr;
+    constexpr bool parts = kFp8 && kParts;
     float q_sl2 = 0.f;
     float v_cur = 1.f;  // O is accumulated in units of this V scale
     if constexpr (kFp8) {
       v_cur = __ldg(p.v_scale + head);
       if (parts) q_sl2 = __ldg(p.q_scale + head) * p.softmax_scale_log2;
     }
+    float sl2 = scale_log2;  // S scale of the current part (log2 units)
+    int cur_part = -1;
     int i = 0;
     for (; i < nblk; ++i) {
       int b;
       next_block(b);
       const bool tr = q == H3SA_TRACE_QUARTER && lane == 0;
-      BlockScales bs{scale_log2, v_cur, kBlockN};
-      if (parts) {
-        bs = block_scales(p, head, b, q_sl2);
-        scale2 = f2_pack(bs.sl2, bs.sl2);
-      }
+      int rows = kBlockN;
+      bool v_moved = false;  // O moves into another part's V-scale units at this block
+      float vr = 1.0f;
+      if (parts) part_step(p, head, b, q_sl2, i > 0, cur_part, rows, sl2, scale2, v_cur, vr,
+                           v_moved);
       if (!(ok = mbar_wait(smem_u32(&sm.s_full[i & 1]), (i >> 1) & 1, abort_flag, p.err))) break;
       if (tr) H3SA_TRACE_AT(i, 6 * h + 0);
       tc_fence_after();
@@ -1208,7 +1208,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       }
       const int col0 = b * kBlockN + 64 * h;
       const int lo = pr.kv_lo - col0;  // valid columns [lo, hi) of this half
-      const int hi = min(pr.kv_hi - col0, bs.rows - 64 * h);
+      const int hi = min(pr.kv_hi - col0, rows - 64 * h);
       int partial_i = (lo > 0 || hi < 64) ? 1 : 0;
       asm volatile("" : "+r"(partial_i));
       if (partial_i) {
@@ -1237,17 +1237,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         tc_fence_after();
         mx = fmaxf(mh, sm.mx_x[i & 1][h ^ 1][row]);
       }
-      const float m_blk = mx * bs.sl2;
+      const float m_blk = mx * sl2;
       const bool need = m_blk > m_used + kRescaleThreshold;
       const float m_new = need ? m_blk : m_used;
       const float alpha = need ? fast_exp2(m_used - m_new) : 1.0f;
-      // entering a part with another V scale moves O into its units (warp-uniform)
-      float vr = 1.0f;
-      if (parts) {
-        vr = i > 0 ? __fdividef(v_cur, bs.vs) : 1.0f;
-        v_cur = bs.vs;
-      }
-      const bool any_need = i > 0 && (__any_sync(0xffffffffu, need) || vr != 1.0f);
+      const bool any_need = i > 0 && (__any_sync(0xffffffffu, need) || v_moved);
       const float o_scale = alpha * vr;
       l_sum *= alpha;
       m_used = m_new;
@@ -1526,7 +1520,7 @@ static int split_workspace(int pairs, cudaStream_t stream, SplitSpace& out) {
   return H3SA_OK;
 }
 
-template <bool kFp8>
+template <bool kFp8, bool kParts>
 static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
   using Cfg = AttnCfg<kFp8>;
   const CUtensorMapDataType dt =
@@ -1625,8 +1619,8 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
     prm.split_count = ws.count;
   }
   const size_t smem = one_tile ? attn1_smem_bytes<kFp8>() : attn_smem_bytes<kFp8>();
-  const auto kernel = one_tile ? attn1_fwd_kernel<kFp8, H3SA_ONE_TILE_INDEP != 0>
-                               : attn_fwd_kernel<kFp8>;
+  const auto kernel = one_tile ? attn1_fwd_kernel<kFp8, H3SA_ONE_TILE_INDEP != 0, kParts>
+                               : attn_fwd_kernel<kFp8, kParts>;
   // per kernel (two-tile / one-tile) and device: the shared-memory attribute is set once, and
   // setmaxnreg.inc waits until the registers it asks for are free in the block's launch
   // allocation, so a build whose register count cannot fund the split is refused
@@ -1662,7 +1656,9 @@ static int launch_attention(const AttnLaunch& L, cudaStream_t stream) {
 }
 
 int attention_launch(const AttnLaunch& L, bool fp8, cudaStream_t stream) {
-  return fp8 ? launch_attention<true>(L, stream) : launch_attention<false>(L, stream);
+  if (!fp8) return launch_attention<false, false>(L, stream);
+  return L.block_part ? launch_attention<true, true>(L, stream)
+                      : launch_attention<true, false>(L, stream);
 }
 
 #ifdef H3SA_TRACE

@@ -112,24 +112,30 @@ struct AttnParams {
   int out_head0;
 };
 
-// Dequantisation factors of KV block b of a segmented e4m3 sequence for head `head`: the S
-// scale (log2 units), the part's V scale and the block's valid rows. P stays unscaled; the
-// softmax keeps O in units of the current part's V scale and rescales it by v_prev / v_new
-// when the walk enters a part with another scale (parts are contiguous runs of blocks).
-struct BlockScales {
-  float sl2, vs;
-  int rows;
-};
-
-__device__ __forceinline__ BlockScales block_scales(const AttnParams& p, int head, int b,
-                                                    float q_sl2) {
+// Segmented e4m3 KV, at block b of the walk (head `head`): the block's valid rows, and on
+// entering another part (a few times a row; parts are contiguous runs of blocks and the walk
+// ascends) the part's S scale in log2 units and its V scale. P stays unscaled; O is kept in
+// units of the current part's V scale, so entering a part with another V scale sets
+// vr = v_prev / v_new, by which the softmax rescales O (with a nonzero O: has_o), and
+// v_moved. Warp-uniform: every lane of a warp walks the same block of the same head.
+__device__ __forceinline__ void part_step(const AttnParams& p, int head, int b, float q_sl2,
+                                          bool has_o, int& cur_part, int& rows, float& sl2,
+                                          uint64_t& scale2, float& v_cur, float& vr,
+                                          bool& v_moved) {
   const int e = __ldg(p.block_part + b);
+  rows = e >> 16;
   const int part = e & 0xFFFF;
-  BlockScales r;
-  r.rows = e >> 16;
-  r.sl2 = q_sl2 * __ldg(p.part_k_scale + part * p.heads + head);
-  r.vs = __ldg(p.part_v_scale + part * p.heads + head);
-  return r;
+  if (part == cur_part) return;
+  cur_part = part;
+  sl2 = q_sl2 * __ldg(p.part_k_scale + part * p.heads + head);
+  scale2 = f2_pack(sl2, sl2);
+  const float vs = __ldg(p.part_v_scale + part * p.heads + head);
+  if (vs == v_cur) return;
+  if (has_o) {
+    vr = __fdividef(v_cur, vs);
+    v_moved = true;
+  }
+  v_cur = vs;
 }
 
 }  // namespace h3sa
