@@ -134,8 +134,9 @@ H3SA_API int h3sa_attention_fwd_fp8(const void* query, void* out, int32_t rows, 
  * rows (1..128) in the high 16 bits: every part starts on a 128-row block boundary and the
  * rows after it in its last block are masked (and should hold finite values, e.g. zeros).
  * part_k_scale / part_v_scale: fp32 [num_parts, heads]; q_scale fp32 [heads]. Scores use
- * q_scale * k_scale(part); P carries v_scale(part) / max_part v_scale in its exponent and O is
- * scaled by that maximum, so the result is exact attention over the dequantised parts.
+ * q_scale * k_scale(part); P stays unscaled, O is accumulated in units of the current part's
+ * V scale and rescaled by v_prev / v_new where the walk enters a part with another V scale,
+ * so the result is attention over the dequantised parts.
  * Replaces the segmented FP8 FlashAttention-3 calls, one per part, and their LSE merge
  * (F/streaming/attention_hook.py:1015-1066, merge 319-334). */
 H3SA_API int h3sa_attention_fwd_fp8_parts(
@@ -203,6 +204,27 @@ H3SA_API int h3sa_quantize_fp8_rows(const h3sa_rows* src, const h3sa_rows* dst,
                                     int32_t count, int32_t heads, float* scale0, float* scale1,
                                     uint32_t* amax_workspace, int32_t zero_tail,
                                     int32_t* device_error, void* stream);
+
+/* Column means of bf16 rows per segment, the summaries of commit-level top-k selection:
+ * for segment i = (first logical row, rows) of segments (int32 [num_segments][2], device) and
+ * every head, means[i][head][d] = fp32 mean over the segment's rows of src[row][head][d] (src
+ * packed or paged, 256-byte rows; max_rows >= every segment's rows). Sums are fp64 in
+ * `workspace` (double [num_segments * heads * 128], device, cleared on `stream` first); the
+ * mean is their fp64 quotient rounded to fp32. Replaces key.float().mean(dim=0) of a committed
+ * history block (F/streaming/cache.py:854, after retention :1031-1034) and
+ * media_query.float().mean(dim=0) (F/streaming/attention_hook.py:1279). */
+H3SA_API int h3sa_segment_row_means(const h3sa_rows* src, const int32_t* segments,
+                                    int32_t num_segments, int32_t max_rows, int32_t heads,
+                                    double* workspace, float* means, int32_t* device_error,
+                                    void* stream);
+
+/* Commit-level top-k scores: scores[i] (fp64, device) = mean over heads of the dot product of
+ * summaries[i] (fp32 [num_parts][heads][128]) with query_mean (fp32 [heads][128]), products
+ * and sums in fp64. Replaces history_summary.mul(query_summary).sum(-1).mean(-1)
+ * (F/streaming/attention_hook.py:1281-1286); the top-k itself runs on the host, where the
+ * reference reads the selection back (.tolist(), :1287-1290). */
+H3SA_API int h3sa_commit_scores(const float* summaries, const float* query_mean,
+                                int32_t num_parts, int32_t heads, double* scores, void* stream);
 
 /* Generic layout permute of 16-byte-aligned records: for every index (i0, i1, i2, i3) of
  * the row-major space dims[4], copy row_bytes from src + sum(i_k * src_strides[k]) to

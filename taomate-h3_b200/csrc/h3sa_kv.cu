@@ -336,6 +336,88 @@ __global__ void __launch_bounds__(256) permute_rows_kernel(const PermuteParams p
   }
 }
 
+// ---------------------------------------------------------------- commit-level top-k summaries
+// Column means of bf16 rows per (segment, head): the key summary of a committed block
+// (F/streaming/cache.py:854, recomputed after retention at :1031-1034) and the media query
+// summary (F/streaming/attention_hook.py:1279). Sums are fp64, which holds a sum of up to
+// millions of bf16 values exactly at the magnitudes attention sees, so the atomic merge order
+// does not change them; the mean is the fp64 quotient rounded to fp32.
+constexpr int kSumChunkRows = 256;
+
+struct SegMeansParams {
+  RowsDev src;
+  const int* segments;  // [n][2]: first logical row, rows
+  int heads;
+  double* sums;         // [n][heads][128], zero before the sum pass
+  float* means;         // [n][heads][128]
+  int n;
+  int* err;
+};
+
+// grid (row chunks, heads, segments), 128 threads: thread d sums column d of its chunk.
+__global__ void __launch_bounds__(128) seg_col_sums_kernel(const SegMeansParams p) {
+  const int s = blockIdx.z;
+  const int h = blockIdx.y;
+  const int start = __ldg(p.segments + 2 * s);
+  const int rows = __ldg(p.segments + 2 * s + 1);
+  const int r0 = blockIdx.x * kSumChunkRows;
+  if (r0 >= rows) return;
+  const int r1 = min(rows, r0 + kSumChunkRows);
+  double acc0 = 0.0, acc1 = 0.0;  // two chains: rows alternate between them
+  int i = r0;
+  for (; i + 1 < r1; i += 2) {
+    const uint8_t* a = row_address(p.src, start + i, h, p.heads, kHeadDim * 2);
+    const uint8_t* b = row_address(p.src, start + i + 1, h, p.heads, kHeadDim * 2);
+    if (!a || !b) {
+      if (p.err) atomicOr(p.err, kErrBadIndex);
+      return;
+    }
+    const unsigned short va = __ldg(reinterpret_cast<const unsigned short*>(a) + threadIdx.x);
+    const unsigned short vb = __ldg(reinterpret_cast<const unsigned short*>(b) + threadIdx.x);
+    acc0 += static_cast<double>(__uint_as_float(static_cast<unsigned>(va) << 16));
+    acc1 += static_cast<double>(__uint_as_float(static_cast<unsigned>(vb) << 16));
+  }
+  if (i < r1) {
+    const uint8_t* a = row_address(p.src, start + i, h, p.heads, kHeadDim * 2);
+    if (!a) {
+      if (p.err) atomicOr(p.err, kErrBadIndex);
+      return;
+    }
+    const unsigned short va = __ldg(reinterpret_cast<const unsigned short*>(a) + threadIdx.x);
+    acc0 += static_cast<double>(__uint_as_float(static_cast<unsigned>(va) << 16));
+  }
+  atomicAdd(p.sums + (static_cast<size_t>(s) * p.heads + h) * kHeadDim + threadIdx.x, acc0 + acc1);
+}
+
+__global__ void __launch_bounds__(256) seg_col_means_kernel(const SegMeansParams p) {
+  const long long total = static_cast<long long>(p.n) * p.heads * kHeadDim;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(idx / (static_cast<long long>(p.heads) * kHeadDim));
+    const int rows = __ldg(p.segments + 2 * s + 1);
+    p.means[idx] = rows > 0 ? __double2float_rn(__ddiv_rn(__ldcg(p.sums + idx), rows)) : 0.f;
+  }
+}
+
+// score[i] = mean over heads of sum over d of summary[i][h][d] * query_mean[h][d]
+// (F/streaming/attention_hook.py:1281-1286), from the fp32 means in fp64 (the products of two
+// fp32 values are exact in fp64). One warp per part; fixed summation order.
+__global__ void __launch_bounds__(256) commit_scores_kernel(const float* summaries,
+                                                            const float* query_mean, int n,
+                                                            int heads, double* scores) {
+  const int part = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (part >= n) return;
+  const float* a = summaries + static_cast<size_t>(part) * heads * kHeadDim;
+  const int len = heads * kHeadDim;
+  double acc = 0.0;
+  for (int j = lane; j < len; j += 32)
+    acc = fma(static_cast<double>(__ldg(a + j)), static_cast<double>(__ldg(query_mean + j)), acc);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (lane == 0) scores[part] = __ddiv_rn(acc, heads);
+}
+
 static int grid_for(long long work, int threads) {
   long long g = (work + threads - 1) / threads;
   const long long cap = 148LL * 16;
@@ -534,6 +616,54 @@ int h3sa_permute_rows(const void* src, void* dst, const int64_t* dims, const int
   permute_rows_kernel<<<grid_for(work, 256), 256, 0, static_cast<cudaStream_t>(stream)>>>(p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("permute_rows_kernel launch", e);
+  return H3SA_OK;
+}
+
+int h3sa_segment_row_means(const h3sa_rows* src, const int32_t* segments, int32_t num_segments,
+                           int32_t max_rows, int32_t heads, double* workspace, float* means,
+                           int32_t* device_error, void* stream) {
+  if (!src || !segments || !workspace || !means || num_segments < 0 || max_rows < 0 || heads <= 0 ||
+      heads > kQuantMaxBatchHeads || num_segments > 65535)
+    return set_error(H3SA_ERR_INVALID, "segment_row_means: invalid arguments (segments=%d, heads=%d)",
+                     num_segments, heads);
+  if (!src->base || (reinterpret_cast<uintptr_t>(src->base) & 15) || src->extent <= 0 ||
+      (src->paged && (!src->page_table || src->table_blocks <= 0)))
+    return set_error(H3SA_ERR_INVALID, "segment_row_means: bad row space");
+  if (num_segments == 0) return H3SA_OK;
+  SegMeansParams p;
+  memset(&p, 0, sizeof(p));
+  p.src.base = static_cast<uint8_t*>(src->base);
+  p.src.paged = src->paged ? 1 : 0;
+  p.src.extent = src->extent;
+  p.src.page_table = src->page_table;
+  p.src.table_blocks = src->table_blocks;
+  p.segments = segments;
+  p.heads = heads;
+  p.sums = workspace;
+  p.means = means;
+  p.n = num_segments;
+  p.err = device_error;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const size_t cells = static_cast<size_t>(num_segments) * heads * kHeadDim;
+  cudaError_t e = cudaMemsetAsync(workspace, 0, cells * sizeof(double), st);
+  if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(segment sums)", e);
+  const int chunks = max_rows > 0 ? (max_rows + kSumChunkRows - 1) / kSumChunkRows : 1;
+  seg_col_sums_kernel<<<dim3(chunks, heads, num_segments), 128, 0, st>>>(p);
+  seg_col_means_kernel<<<grid_for(static_cast<long long>(cells), 256), 256, 0, st>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("segment_row_means launch", e);
+  return H3SA_OK;
+}
+
+int h3sa_commit_scores(const float* summaries, const float* query_mean, int32_t num_parts,
+                       int32_t heads, double* scores, void* stream) {
+  if (!summaries || !query_mean || !scores || num_parts < 0 || heads <= 0)
+    return set_error(H3SA_ERR_INVALID, "commit_scores: invalid arguments");
+  if (num_parts == 0) return H3SA_OK;
+  commit_scores_kernel<<<(num_parts + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      summaries, query_mean, num_parts, heads, scores);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("commit_scores launch", e);
   return H3SA_OK;
 }
 

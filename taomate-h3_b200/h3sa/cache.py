@@ -197,6 +197,9 @@ class SegmentedFp8History:
         self.rows: list[int] = []     # rows of each part
         self.k_scale = torch.zeros(0, heads, dtype=torch.float32, device=device)
         self.v_scale = torch.zeros(0, heads, dtype=torch.float32, device=device)
+        # fp32 [parts, heads, head_dim]: each part's mean bf16 key row, the summary that
+        # commit-level top-k scores against the media queries (F/streaming/cache.py:854)
+        self.key_summary = torch.zeros(0, heads, head_dim, dtype=torch.float32, device=device)
         self.workspace = torch.zeros(2 * heads, dtype=torch.int32, device=device)
 
     @property
@@ -220,6 +223,26 @@ class SegmentedFp8History:
         _upload_pages(table, entries)
         return table
 
+    def subset_tables(self, selected: list[int], current: list[tuple[int, int, int]]
+                      ) -> tuple[torch.Tensor, torch.Tensor, int]:
+        """Page table and block_part of a sequence made of the selected history parts (in the
+        given order) followed by ``current`` (part index, start, rows) parts of the store, all
+        keeping their part indices; returns them with the sequence's row count."""
+
+        pages, entries = [], []
+        parts = [(i, self.starts[i], self.rows[i]) for i in selected] + list(current)
+        for index, s0, n in parts:
+            for b in range(s0 // PAGE_ROWS, (s0 + n + PAGE_ROWS - 1) // PAGE_ROWS):
+                pages.append(self.store.pages[b])
+                entries.append(index | (min(PAGE_ROWS, s0 + n - b * PAGE_ROWS) << 16))
+        dev = self.store.device
+        table = torch.zeros(max(1, len(pages)), dtype=torch.int32, device=dev)
+        block_part = torch.zeros_like(table)
+        _upload_pages(table, pages)
+        _upload_pages(block_part, entries)
+        kv_end = (len(pages) - 1) * PAGE_ROWS + (entries[-1] >> 16) if pages else 0
+        return table, block_part, kv_end
+
     def append_part(self, key: torch.Tensor, value: torch.Tensor, *, src_start: int, count: int,
                     src_table: torch.Tensor | None, k_scale: torch.Tensor,
                     v_scale: torch.Tensor, start: int | None = None) -> int:
@@ -238,16 +261,34 @@ class SegmentedFp8History:
 
     def commit_part(self, key: torch.Tensor, value: torch.Tensor, *, src_start: int, count: int,
                     src_table: torch.Tensor | None) -> None:
-        """Quantise a committed block into a new part with its own scales."""
+        """Quantise a committed block into a new part with its own scales, and record its
+        key summary (the mean of its bf16 key rows)."""
+
+        from .kernels import segment_row_means
 
         ks = torch.empty(1, self.heads, dtype=torch.float32, device=self.store.device)
         vs = torch.empty_like(ks)
         s0 = self.append_part(key, value, src_start=src_start, count=count, src_table=src_table,
                               k_scale=ks[0], v_scale=vs[0])
+        summary = segment_row_means(key, [(src_start, count)], src_table=src_table)
         self.starts.append(s0)
         self.rows.append(count)
         self.k_scale = torch.cat((self.k_scale, ks))
         self.v_scale = torch.cat((self.v_scale, vs))
+        self.key_summary = torch.cat((self.key_summary, summary))
+
+    def refresh_summaries(self, key: torch.Tensor, table: torch.Tensor) -> None:
+        """Recompute every part's key summary from the bf16 history rows, where the parts'
+        rows follow one another in order (after retention, which keeps a part's scales but
+        recomputes its summary over the rows it kept: F/streaming/cache.py:1031-1034)."""
+
+        from .kernels import segment_row_means
+
+        segments, cursor = [], 0
+        for n in self.rows:
+            segments.append((cursor, n))
+            cursor += n
+        self.key_summary = segment_row_means(key, segments, src_table=table)
 
     def retain(self, selection: list[tuple[int, list[int]]]) -> None:
         """Keep, in order, the given (part, local rows) selections: each becomes a part of its
@@ -281,6 +322,7 @@ class SegmentedFp8History:
         idx = torch.tensor(keep, dtype=torch.long, device=self.store.device)
         self.k_scale = self.k_scale.index_select(0, idx)
         self.v_scale = self.v_scale.index_select(0, idx)
+        self.key_summary = self.key_summary.index_select(0, idx)  # refreshed by the cache
         self.starts, self.rows = starts, rows
 
     def release(self) -> None:
@@ -288,6 +330,7 @@ class SegmentedFp8History:
         self.starts, self.rows = [], []
         self.k_scale = self.k_scale[:0]
         self.v_scale = self.v_scale[:0]
+        self.key_summary = self.key_summary[:0]
 
 
 def _validate_layer_name(layer_name: str, names: tuple[str, ...]) -> None:
@@ -776,6 +819,7 @@ class CleanAVKVCache:
                 paged.gather(rows)
             if paged.fp8 is not None and paged.fp8.starts:
                 paged.fp8.retain(parts)
+                paged.fp8.refresh_summaries(paged.key, paged.table)
         self._commit_token_counts = selected_counts
         self._commit_token_tags = selected_tags
 

@@ -21,8 +21,11 @@ the commit needs no further copy.
 
 Backends (``attention_backend``): ``"flash_attn_3"``/``"flash_attn3"``/``"sdpa"`` (dense
 bf16), ``"flash_attn3_fp8_dynamic"`` (per-call per-head e4m3 Q/K/V,
-F/streaming/attention_hook.py:1081-1098) and ``"flex_dynamic_blocksparse"`` (history
-block top-k, F/inference/dynamic_block_sparse.py:50-172).
+F/streaming/attention_hook.py:1081-1098), ``"flash_attn3_fp8_segmented"`` (e4m3 history
+parts quantised once at commit, :1015-1066), ``"flash_attn3_fp8_segmented_topk"`` (the same
+over the committed blocks whose key summaries score highest against the media queries,
+:1256-1302) and ``"flex_dynamic_blocksparse"`` (history block top-k,
+F/inference/dynamic_block_sparse.py:50-172).
 """
 
 from __future__ import annotations
@@ -40,7 +43,9 @@ from .kernels import (AttentionProblem, attention_fwd, attention_fwd_fp8_parts, 
 from .peer import attention_fwd_scatter
 
 DENSE_BACKENDS = ("flash_attn_3", "flash_attn3", "sdpa", "h3sa_dense")
-FP8_BACKENDS = ("flash_attn3_fp8_dynamic", "flash_attn3_fp8_segmented")
+FP8_BACKENDS = ("flash_attn3_fp8_dynamic", "flash_attn3_fp8_segmented",
+                "flash_attn3_fp8_segmented_topk")
+SEGMENTED_BACKENDS = ("flash_attn3_fp8_segmented", "flash_attn3_fp8_segmented_topk")
 SPARSE_BACKENDS = ("flex_dynamic_blocksparse",)
 
 
@@ -119,7 +124,13 @@ class H3StreamingAttentionHook:
     """Condition current media on text, persistent clean AV KV, and current KV."""
 
     def __init__(self, cache: CleanAVKVCache, *, backend: str = "flash_attn_3",
-                 history_density: float = 0.5) -> None:
+                 history_density: float = 0.5, attention_backend: str | None = None,
+                 history_kv_dynamic_density: float | None = None) -> None:
+        # the FL2AV constructor's names for the same two knobs (F/streaming/attention_hook.py:377-394)
+        if attention_backend is not None:
+            backend = attention_backend
+        if history_kv_dynamic_density is not None:
+            history_density = history_kv_dynamic_density
         if backend not in DENSE_BACKENDS + FP8_BACKENDS + SPARSE_BACKENDS:
             raise ValueError(f"unsupported H3 streaming attention backend: {backend}")
         if not 0.0 < history_density <= 1.0:
@@ -131,6 +142,10 @@ class H3StreamingAttentionHook:
         self.query_tokens = 0
         self.key_tokens = 0
         self.launches = 0
+        # commit-level top-k counters (F/streaming/attention_hook.py:1292-1298)
+        self.dynamic_block_sparse_call_count = 0
+        self.dynamic_block_sparse_selected_blocks = 0
+        self.dynamic_block_sparse_history_blocks = 0
         self.mode = HookMode.IDLE
         self._plan: _DocumentPlan | None = None
         self._plan_key: tuple[int, ...] | None = None
@@ -327,7 +342,7 @@ class H3StreamingAttentionHook:
     def _launch(self, layer_name: str, paged, q_src: torch.Tensor, out: torch.Tensor,
                 problems: list[AttentionProblem], scale: float, n_kv: int, n_hist: int,
                 plan: _DocumentPlan, err: torch.Tensor, exchange=None) -> None:
-        if self.backend == "flash_attn3_fp8_segmented":
+        if self.backend in SEGMENTED_BACKENDS:
             self._launch_fp8_segmented(paged, q_src, out, problems, scale, n_hist, err)
             return
         if self.backend in FP8_BACKENDS:
@@ -409,12 +424,19 @@ class H3StreamingAttentionHook:
         seg.append_part(paged.key, paged.value, src_start=cond.kv_lo, count=n_cond,
                         src_table=paged.table, k_scale=ks[n_parts + 1],
                         v_scale=vs[n_parts + 1], start=c0)
-        block_part = seg.block_part([(m0, n_media), (c0, n_cond)])
+        selected = self._select_commits(seg, q_src, media, err)
+        if selected is None:
+            table = seg.store.table
+            block_part = seg.block_part([(m0, n_media), (c0, n_cond)])
+            kv_end = c0 + n_cond
+        else:
+            table, block_part, kv_end = seg.subset_tables(
+                selected, [(n_parts, m0, n_media), (n_parts + 1, c0, n_cond)])
         q8, q_scale = quantize_fp8_e4m3_per_head(q_src[media.q_lo:media.q_hi].unsqueeze(0))
         out_media = torch.empty(n_media, *q_src.shape[1:], dtype=torch.bfloat16,
                                 device=q_src.device)
         attention_fwd_fp8_parts(q8.squeeze(0), out_media, seg.store.key, seg.store.value,
-                                seg.store.table, [AttentionProblem(0, n_media, 0, c0 + n_cond)],
+                                table, [AttentionProblem(0, n_media, 0, kv_end)],
                                 scale, q_scale=q_scale.reshape(-1).contiguous(),
                                 block_part=block_part, part_k_scale=ks, part_v_scale=vs,
                                 device_error=err)
@@ -423,6 +445,33 @@ class H3StreamingAttentionHook:
         attention_fwd(q_src, out, paged.key, paged.value, paged.table, [cond], scale,
                       device_error=err)
         self.launches += 2
+
+    def _select_commits(self, seg, q_src: torch.Tensor, media: AttentionProblem,
+                        err: torch.Tensor) -> list[int] | None:
+        """Commit-level top-k of the segmented backend (F/streaming/attention_hook.py:1256-1302):
+        keep max(1, min(n, ceil(n * density))) committed blocks, those whose key summaries
+        have the highest mean-over-heads dot product with the media queries' mean row, in
+        commit order. None: attend to every committed block."""
+
+        import math
+
+        from .kernels import commit_scores, segment_row_means
+
+        n = len(seg.starts)
+        if self.backend != "flash_attn3_fp8_segmented_topk" or n == 0:
+            return None
+        count = max(1, min(n, math.ceil(n * self.history_density)))
+        self.dynamic_block_sparse_call_count += 1
+        self.dynamic_block_sparse_history_blocks += n
+        self.dynamic_block_sparse_selected_blocks += count
+        if count >= n:
+            return None
+        q_mean = segment_row_means(q_src, [(media.q_lo, media.q_hi - media.q_lo)],
+                                   device_error=err)
+        # the reference reads its selection back to the host (.tolist()); so does this
+        scores = commit_scores(seg.key_summary, q_mean[0]).cpu().tolist()
+        order = sorted(range(n), key=lambda i: (-scores[i], i))  # equal scores: older first
+        return sorted(order[:count])
 
 
 __all__ = ["H3StreamingAttentionHook", "HookMode"]

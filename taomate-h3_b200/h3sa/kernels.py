@@ -359,6 +359,61 @@ def quantize_fp8_rows(
          ptr(workspace), 1 if zero_tail else 0, ptr(device_error), stream_handle(stream))
 
 
+def segment_row_means(
+    src: torch.Tensor,
+    segments: Sequence[tuple[int, int]],
+    *,
+    src_table: torch.Tensor | None = None,
+    device_error: torch.Tensor | None = None,
+    stream: torch.cuda.Stream | None = None,
+) -> torch.Tensor:
+    """fp32 ``[len(segments), heads, 128]`` column means of bf16 rows: entry i is the mean over
+    rows ``[start, start + rows)`` of segment i of ``src`` (packed ``[rows, heads, 128]``, or
+    paged ``[heads, pages * 128, 128]`` with ``src_table``), from exact fp64 sums. The key
+    summary of a committed block and the media query summary of commit-level top-k
+    (F/streaming/cache.py:854; F/streaming/attention_hook.py:1279)."""
+
+    _require_cuda(src, src_table, device_error)
+    heads = int(src.shape[0] if src_table is not None else src.shape[1])
+    if src.ndim != 3 or src.dtype != torch.bfloat16 or int(src.shape[-1]) != HEAD_DIM:
+        raise RuntimeError(f"segment_row_means takes bf16 rows of {HEAD_DIM}")
+    # paged rows beyond the table are refused on the device (bad-index flag)
+    limit = int(src.shape[0]) if src_table is None else int(src_table.numel()) * PAGE_ROWS
+    seg = [(int(a), int(n)) for a, n in segments]
+    if any(a < 0 or n < 0 or a + n > limit for a, n in seg):
+        raise RuntimeError("segment_row_means: a segment reaches outside the rows")
+    means = torch.empty(len(seg), heads, HEAD_DIM, dtype=torch.float32, device=src.device)
+    if not seg:
+        return means
+    table = torch.tensor([v for pair in seg for v in pair], dtype=torch.int32)
+    table = table.pin_memory().to(src.device, non_blocking=True)
+    work = torch.empty(len(seg) * heads * HEAD_DIM, dtype=torch.float64, device=src.device)
+    rows = _rows(src, src_table)
+    call("h3sa_segment_row_means", ctypes.byref(rows), ptr(table), len(seg),
+         max(n for _, n in seg), heads, ptr(work), ptr(means), ptr(device_error),
+         stream_handle(stream))
+    return means
+
+
+def commit_scores(summaries: torch.Tensor, query_mean: torch.Tensor, *,
+                  stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+    """fp64 ``[parts]`` scores of commit-level top-k: the mean over heads of each summary's
+    dot product with the query mean (F/streaming/attention_hook.py:1281-1286)."""
+
+    _require_cuda(summaries, query_mean)
+    if (summaries.dtype != torch.float32 or query_mean.dtype != torch.float32
+            or summaries.ndim != 3 or tuple(summaries.shape[1:]) != tuple(query_mean.shape)
+            or int(query_mean.shape[-1]) != HEAD_DIM):
+        raise RuntimeError("commit_scores takes fp32 summaries [parts, heads, 128] and a "
+                           "query mean [heads, 128]")
+    summaries = summaries.contiguous()
+    query_mean = query_mean.contiguous()
+    scores = torch.empty(int(summaries.shape[0]), dtype=torch.float64, device=summaries.device)
+    call("h3sa_commit_scores", ptr(summaries), ptr(query_mean), int(summaries.shape[0]),
+         int(query_mean.shape[0]), ptr(scores), stream_handle(stream))
+    return scores
+
+
 def attention_fwd_fp8_parts(
     query: torch.Tensor,
     out: torch.Tensor,

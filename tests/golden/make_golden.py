@@ -27,6 +27,10 @@ them from the seeds recorded in each fixture. Fixtures:
                  attention-history queries.
 * ulysses_pad.npz the FL2AV versions with 3 heads over 2 ranks (zero-padded head shards,
                  F/distributed/ulysses.py).
+* topk.npz       key summaries of the FL2AV segmented-FP8 CleanAVKVCache
+                 (F/streaming/cache.py:836-855) over six commits and after a sink + recent
+                 retention, with the commit-level top-k selection of the segmented top-k
+                 backend (F/streaming/attention_hook.py:1256-1302) evaluated on them.
 """
 
 from __future__ import annotations
@@ -265,6 +269,60 @@ def make_cache_f(path: Path) -> None:
     np.savez(path, **arrays)
 
 
+def make_topk(path: Path) -> None:
+    """Six segmented-FP8 commits (2 heads of 128) with per-commit offsets, the key summaries
+    the reference cache stores for them, then the same after retain_sink_and_recent_commits
+    (which recomputes each kept block's summary over its kept rows). The selection is the
+    expression of F/streaming/attention_hook.py:1271-1290 (inline in the hook, which needs
+    CUDA) evaluated here on the reference's summaries. Its stage() accepts only CUDA bf16 K/V;
+    that check is stubbed so the cache runs on CPU."""
+
+    import math
+
+    import torch
+    import digitalhuman_h3.streaming.cache as fcache
+
+    fcache._validate_av_pair = lambda pair, contract, *, layer: None
+    layer = "blocks.0.attn"
+    contract = fcache.KVContract(layer_names=(layer,), local_heads=2, head_dim=128)
+    cache = fcache.CleanAVKVCache(contract, segmented_fp8_history=True)
+    rng = np.random.default_rng(21)
+    arrays: dict[str, np.ndarray] = {}
+    for serial in range(6):
+        audio = 2 * int(rng.integers(2, 5))
+        video = int(rng.integers(12, 30))
+        tags = np.array([1] * 3 + [2] * audio + [0] * video + [-1] * 2)
+        commit = (tags == 0) | (tags == 2)
+        offset = rng.standard_normal((1, 2, 128)).astype(np.float32)
+        key = bf16(0.5 * rng.standard_normal((len(tags), 2, 128)).astype(np.float32) + offset)
+        value = bf16(rng.standard_normal((len(tags), 2, 128)).astype(np.float32))
+        cache.begin_clean_commit(cache.committed_blocks)
+        cache.stage(layer, torch.from_numpy(key).to(torch.bfloat16),
+                    torch.from_numpy(value).to(torch.bfloat16), torch.from_numpy(tags),
+                    torch.from_numpy(commit))
+        cache.commit()
+        arrays[f"key_{serial}"] = key
+        arrays[f"tags_{serial}"] = tags
+
+    def select(stage: str, query: np.ndarray, density: float) -> None:
+        blocks = cache.history_blocks(layer)
+        summaries = torch.stack([pair.key_summary for pair in blocks], dim=0)
+        arrays[f"summary_{stage}"] = summaries.numpy()
+        q = torch.from_numpy(query).to(torch.bfloat16)
+        count = max(1, min(len(blocks), math.ceil(len(blocks) * density)))
+        scores = summaries.mul(q.float().mean(dim=0).unsqueeze(0)).sum(dim=-1).mean(dim=-1)
+        arrays[f"scores_{stage}"] = scores.numpy()
+        arrays[f"selected_{stage}"] = np.array(
+            scores.topk(count, sorted=False).indices.sort().values.tolist(), dtype=np.int64)
+        arrays[f"query_{stage}"] = query
+        arrays[f"density_{stage}"] = np.array(density)
+
+    select("full", bf16(rng.standard_normal((40, 2, 128)).astype(np.float32) + 0.3), 0.5)
+    cache.retain_sink_and_recent_commits(3, sink_video_only=True)
+    select("retained", bf16(rng.standard_normal((40, 2, 128)).astype(np.float32) - 0.2), 0.5)
+    arrays["retained_counts"] = np.array(cache.commit_token_counts, dtype=np.int64)
+    np.savez(path, **arrays)
+
 # ----------------------------------------------------------------------------- ulysses
 def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import datetime
@@ -356,7 +414,8 @@ def main() -> None:
     _import_reference()
     makers = {"prologue.npz": make_prologue, "hook_cpu.npz": make_hook, "fp8.npz": make_fp8,
               "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
-              "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f}
+              "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f,
+              "topk.npz": make_topk}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

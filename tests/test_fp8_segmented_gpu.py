@@ -135,3 +135,70 @@ def test_attention_over_parts_matches_segmented_oracle(sparse: bool) -> None:
     ref = oatt.segmented_fp8_attention(c["q"], c["oracle_parts"], scale)
     rel = float((out.float().cpu() - ref).norm() / ref.norm())
     assert rel <= TOL, f"segmented FP8 attention rel L2 {rel:.3e}"
+
+
+@pytest.mark.parametrize("paged", [False, True])
+def test_segment_row_means_and_commit_scores_match_oracle(paged: bool) -> None:
+    """Column means of bf16 row segments (sizes around the 256-row chunk) are bit-exact
+    against the oracle's fp64 mean rounded to fp32; the commit scores agree to fp64
+    rounding."""
+
+    from h3sa.kernels import commit_scores, kv_copy_rows, segment_row_means
+    from oracle import commit_topk as otopk
+
+    gen = np.random.default_rng(5)
+    heads, rows = 3, 1700
+    x = (gen.standard_normal((rows, heads, 128)) * 2 + 0.5).astype(np.float32)
+    xt = torch.from_numpy(x).bfloat16().cuda()
+    xb = xt.float().cpu().numpy()
+    segments = [(0, 1), (1, 255), (256, 256), (512, 257), (769, 700), (1469, 231), (5, 0)]
+    if paged:
+        pool, table = _paged(rows, heads, torch.bfloat16, gen)
+        kv_copy_rows([xt], [pool], count=rows, dst_table=table)
+        means = segment_row_means(pool, segments, src_table=table)
+    else:
+        means = segment_row_means(xt, segments)
+    torch.cuda.synchronize()
+    for i, (a, n) in enumerate(segments):
+        if n == 0:
+            assert torch.count_nonzero(means[i]) == 0
+            continue
+        ref = otopk.key_summary(xb[a:a + n])
+        assert np.array_equal(means[i].cpu().numpy(), ref), i
+    summaries = means[:6].contiguous()
+    q_mean = segment_row_means(xt, [(100, 900)])[0]
+    scores = commit_scores(summaries, q_mean).cpu().numpy()
+    ref = otopk.commit_scores(summaries.cpu().numpy(), q_mean.cpu().numpy())
+    np.testing.assert_allclose(scores, ref, rtol=1e-12, atol=1e-12)
+
+
+def test_cache_key_summaries_match_reference_golden() -> None:
+    """The segmented cache's per-part key summaries through the reference's own schedule
+    (tests/golden/topk.npz: six commits, then sink + recent retention that keeps block 0's
+    video rows): within an fp32 ulp of the reference cache's key.float().mean(dim=0)."""
+
+    from pathlib import Path
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+
+    g = np.load(Path(__file__).resolve().parent / "golden" / "topk.npz")
+    layer = "blocks.0.attn"
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128), layer_names=(layer,),
+                           segmented_fp8_history=True)
+    for i in range(6):
+        tags = torch.from_numpy(g[f"tags_{i}"]).cuda()
+        key = torch.from_numpy(g[f"key_{i}"]).bfloat16().cuda()
+        cache.begin_clean_commit(cache.committed_blocks)
+        cache.stage(layer, key, key.clone(), tags, (tags == 0) | (tags == 2))
+        cache.commit()
+
+    def check(stage: str) -> None:
+        got = cache.layer(layer).fp8.key_summary.cpu().numpy()
+        ref = g[f"summary_{stage}"]
+        assert got.shape == ref.shape, stage
+        assert np.all(np.abs(got - ref) <= np.spacing(np.abs(ref))), stage
+
+    check("full")
+    cache.retain_sink_and_recent_commits(3, sink_video_only=True)
+    assert list(cache.commit_token_counts) == list(g["retained_counts"])
+    check("retained")

@@ -384,3 +384,77 @@ def test_hook_fl2av_call_form_matches_t_form() -> None:
         hook.check_device_error()
         outs.append(out)
     assert torch.equal(outs[0], outs[1])
+
+
+def test_hook_fp8_segmented_topk_attends_selected_commits() -> None:
+    """flash_attn3_fp8_segmented_topk: four commits whose keys carry different offsets, then a
+    NOISY call at density 0.5. The hook must keep the two commits the oracle's summaries and
+    scores select (F/streaming/attention_hook.py:1256-1302) and its media rows must match the
+    segmented oracle over [condition, selected commits, current media]; the counters follow
+    the reference's."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+    from oracle import commit_topk as otopk
+    from oracle import fp8 as ofp8
+
+    heads = 2
+    cache = CleanAVKVCache(KVContract(local_heads=heads, head_dim=128),
+                           layer_names=("blocks.0.attn",), segmented_fp8_history=True)
+    hook = H3StreamingAttentionHook(cache, attention_backend="flash_attn3_fp8_segmented_topk",
+                                    history_kv_dynamic_density=0.5)
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    committed = []
+    for i in range(4):
+        x = _layout(heads, 0, False, seed=40 + i)
+        offset = torch.randn(1, heads, 128, device="cuda", generator=gen)
+        x["k"] = (x["k"].float() + 0.5 * offset).bfloat16()
+        cache.begin_clean_commit(cache.committed_blocks)
+        hook.activate(HookMode.CLEAN_COMMIT)
+        hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"],
+             value=x["v"], token_tags=x["tags"], commit_mask=x["commit"], cu_seqlens_host=x["cu"])
+        hook.deactivate()
+        cache.commit()
+        media = torch.nonzero(x["commit"]).flatten()
+        committed.append((x["k"][media], x["v"][media]))
+    hook.check_device_error()
+    calls_before = hook.dynamic_block_sparse_call_count
+
+    y = _layout(heads, 0, False, seed=50)
+    y["q"] = (y["q"].float() + 0.5 * torch.randn(1, heads, 128, device="cuda",
+                                                 generator=gen)).bfloat16()
+    media = torch.arange(16, 304, device="cuda")
+    cond = torch.arange(0, 16, device="cuda")
+    summaries = np.stack([otopk.key_summary(k.float().cpu().numpy()) for k, _ in committed])
+    scores = otopk.commit_scores(summaries, otopk.key_summary(y["q"][media].float().cpu().numpy()))
+    selected = otopk.select_commits(scores, 0.5)
+    assert len(selected) == 2
+    hook.activate(HookMode.NOISY)
+    out = hook(attention=Attn(), layer_name="blocks.0.attn", query=y["q"], key=y["k"],
+               value=y["v"], token_tags=y["tags"], commit_mask=y["commit"], cu_seqlens_host=y["cu"])
+    hook.deactivate()
+    hook.check_device_error()
+    assert hook.dynamic_block_sparse_call_count == calls_before + 1
+    assert hook.dynamic_block_sparse_selected_blocks >= 2
+
+    def q8(t: torch.Tensor):
+        q, s = ofp8.quantize_fp8_e4m3_per_head(t.float().cpu().numpy()[None])
+        return q[0], s[0]
+
+    def part(k: torch.Tensor, v: torch.Tensor):
+        (k8, ks), (v8, vs) = q8(k), q8(v)
+        return k8, v8, ks, vs
+
+    parts = [part(*committed[i]) for i in selected]
+    (ck8, cks), (cv8, cvs) = q8(y["k"][cond]), q8(y["v"][cond])
+    (mk8, mks), (mv8, mvs) = q8(y["k"][media]), q8(y["v"][media])
+    ref = oatt.segmented_fp8_attention(y["q"][media].float().cpu(),
+                                       [(ck8, cv8, cks, cvs), *parts, (mk8, mv8, mks, mvs)],
+                                       Attn.softmax_scale)
+    assert rel_l2(out[16:304], ref) <= FP8_TOL
+    # attending to every commit instead gives a measurably different result
+    every = oatt.segmented_fp8_attention(
+        y["q"][media].float().cpu(),
+        [(ck8, cv8, cks, cvs), *[part(k, v) for k, v in committed], (mk8, mv8, mks, mvs)],
+        Attn.softmax_scale)
+    assert rel_l2(every, ref) > 2 * FP8_TOL

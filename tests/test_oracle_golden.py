@@ -203,3 +203,31 @@ def test_fl2av_cache_rows_match_reference() -> None:
         assert cache.committed_blocks == int(g[f"blocks_{i}"]), i
 
     replay_cache_f(g, apply)
+
+
+def test_commit_topk_matches_reference() -> None:
+    """Key summaries of the reference's segmented-FP8 cache (fresh commits, and after a sink +
+    recent retention that keeps block 0's video rows) and the commit-level top-k selection on
+    them (tests/golden/topk.npz)."""
+
+    from oracle import commit_topk as otopk
+
+    g = load("topk.npz")
+    blocks = []
+    for i in range(6):
+        tags = g[f"tags_{i}"]
+        blocks.append((g[f"key_{i}"][(tags == 0) | (tags == 2)], tags[(tags == 0) | (tags == 2)]))
+    kept = [blocks[0][0][blocks[0][1] == 0], blocks[3][0], blocks[4][0], blocks[5][0]]
+    assert [len(k) for k in kept] == list(g["retained_counts"])
+    for stage, rows in (("full", [b[0] for b in blocks]), ("retained", kept)):
+        summaries = np.stack([otopk.key_summary(r) for r in rows])
+        ref = g[f"summary_{stage}"]
+        # fp64-exact mean vs the reference's fp32 reduction: within an ulp
+        assert np.all(np.abs(summaries - ref) <= np.spacing(np.abs(ref))), stage
+        q_mean = otopk.key_summary(g[f"query_{stage}"])
+        scores = otopk.commit_scores(summaries, q_mean)
+        np.testing.assert_allclose(scores, g[f"scores_{stage}"], rtol=1e-5, atol=1e-5)
+        selected = otopk.select_commits(scores, float(g[f"density_{stage}"]))
+        assert selected == list(g[f"selected_{stage}"]), stage
+    assert otopk.selected_count(5, 0.5) == 3 and otopk.selected_count(1, 0.1) == 1
+    assert otopk.select_commits(np.array([1.0, 1.0, 0.5]), 0.5) == [0, 1]
