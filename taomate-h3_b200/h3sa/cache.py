@@ -419,6 +419,23 @@ class CleanAVKVCache:
         self._commit_token_tags.clear()
         self._invalid_after_failed_commit = True
 
+    # ------------------------------------------------------------------ snapshots
+    def save_snapshot(self, path) -> None:
+        """Write the committed history and its bookkeeping to ``path`` (h3sa.snapshot)."""
+
+        from .snapshot import save_cache
+
+        save_cache(self, path)
+
+    @classmethod
+    def load_snapshot(cls, path, *, device=None, contract: KVContract | None = None
+                      ) -> "CleanAVKVCache":
+        """A cache restored from a snapshot, ready to attend and commit where it stopped."""
+
+        from .snapshot import load_cache
+
+        return load_cache(path, device=device, contract=contract)
+
     # ------------------------------------------------------------------ paged access
     def layer(self, layer_name: str, device: torch.device | None = None) -> PagedLayerKV:
         """The layer's page sequence, created on first use."""

@@ -458,3 +458,76 @@ def test_hook_fp8_segmented_topk_attends_selected_commits() -> None:
         [(ck8, cv8, cks, cvs), *[part(k, v) for k, v in committed], (mk8, mv8, mks, mvs)],
         Attn.softmax_scale)
     assert rel_l2(every, ref) > 2 * FP8_TOL
+
+
+@pytest.mark.parametrize("segmented", [False, True])
+def test_cache_snapshot_round_trip_resumes_bit_exact(tmp_path, segmented: bool) -> None:
+    """A cache written to disk and loaded into a fresh process-side object (h3sa.snapshot)
+    holds the same history bytes, e4m3 parts, scales, summaries and bookkeeping; a NOISY call
+    and a further clean commit on the restored cache give bit-identical results to the
+    original's."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads = 2
+    layers = ("blocks.0.attn", "blocks.1.attn")
+    backend = "flash_attn3_fp8_segmented" if segmented else "flash_attn_3"
+    cache = CleanAVKVCache(KVContract(local_heads=heads, head_dim=128), layer_names=layers,
+                           segmented_fp8_history=segmented)
+
+    def step(c: CleanAVKVCache, x: dict, mode: HookMode) -> list[torch.Tensor]:
+        hook = H3StreamingAttentionHook(c, backend=backend)
+        if mode is HookMode.CLEAN_COMMIT:
+            c.begin_clean_commit(c.committed_blocks)
+        hook.activate(mode)
+        outs = [hook(attention=Attn(), layer_name=name, query=x["q"], key=x["k"], value=x["v"],
+                     token_tags=x["tags"], commit_mask=x["commit"], cu_seqlens_host=x["cu"])
+                for name in layers]
+        hook.deactivate()
+        if mode is HookMode.CLEAN_COMMIT:
+            c.commit()
+        hook.check_device_error()
+        return outs
+
+    for i in range(3):
+        step(cache, _layout(heads, 0, False, seed=60 + i), HookMode.CLEAN_COMMIT)
+    cache.retain_sink_and_recent_commits()  # block 0 keeps its video rows only
+    path = tmp_path / "cache.h3kv"
+    cache.save_snapshot(path)
+    restored = CleanAVKVCache.load_snapshot(path, contract=KVContract(local_heads=heads,
+                                                                     head_dim=128))
+    assert restored.committed_blocks == cache.committed_blocks
+    assert restored.commit_token_counts == cache.commit_token_counts
+    assert restored.commit_token_tags() == cache.commit_token_tags()
+    for name in layers:
+        a, b = cache.history(name), restored.history(name)
+        assert torch.equal(a.key, b.key) and torch.equal(a.value, b.value), name
+        if segmented:
+            sa, sb = cache.layer(name).fp8, restored.layer(name).fp8
+            assert sa.rows == sb.rows
+            assert torch.equal(sa.k_scale, sb.k_scale) and torch.equal(sa.v_scale, sb.v_scale)
+            assert torch.equal(sa.key_summary, sb.key_summary)
+            for (s0, n), (t0, m) in zip(zip(sa.starts, sa.rows), zip(sb.starts, sb.rows)):
+                ka, kb = sa.store.materialize(s0 + n), sb.store.materialize(t0 + m)
+                assert torch.equal(ka[0][s0:].view(torch.uint8), kb[0][t0:].view(torch.uint8))
+                assert torch.equal(ka[1][s0:].view(torch.uint8), kb[1][t0:].view(torch.uint8))
+    y = _layout(heads, 0, False, seed=70)
+    for got, want in zip(step(restored, y, HookMode.NOISY), step(cache, y, HookMode.NOISY)):
+        assert torch.equal(got, want)
+    z = _layout(heads, 0, False, seed=71)
+    step(cache, z, HookMode.CLEAN_COMMIT)
+    step(restored, z, HookMode.CLEAN_COMMIT)
+    for got, want in zip(step(restored, y, HookMode.NOISY), step(cache, y, HookMode.NOISY)):
+        assert torch.equal(got, want)
+    # a flipped byte is refused before anything reaches the device
+    from h3sa.snapshot import read_header
+
+    header, base = read_header(path)
+    last = header["sections"][-1]
+    raw = bytearray(path.read_bytes())
+    raw[base + last["offset"] + last["nbytes"] - 5] ^= 0x40
+    bad = tmp_path / "bad.h3kv"
+    bad.write_bytes(bytes(raw))
+    with pytest.raises(ValueError, match="CRC-32"):
+        CleanAVKVCache.load_snapshot(bad)

@@ -456,3 +456,49 @@ def test_live_document_hint_checks_match_reference() -> None:
         live(mask, bounds, (2, 0))
     with pytest.raises(ValueError, match="empty document"):
         live(mask, bounds, (1,))
+
+
+def test_snapshot_header_checks_run_before_device_work(tmp_path) -> None:
+    """A snapshot file is validated on the host: wrong magic, another format version, a
+    truncated or corrupted section and a contract mismatch are refused with ValueError."""
+
+    import json
+    import struct
+    import zlib
+
+    from h3sa import snapshot
+    from h3sa.cache import KVContract
+
+    data = bytes(range(256)) * 8
+    header = {"format": snapshot.FORMAT_VERSION,
+              "contract": {"local_heads": 2, "head_dim": 128, "dtype": "bfloat16",
+                           "device_type": "cuda"},
+              "layer_names": ["blocks.0.attn"], "segmented_fp8_history": False,
+              "block_index": 1, "commit_token_counts": [8], "commit_token_tags": [[0] * 8],
+              "layers": {}, "sections": [{"name": "blocks.0.attn/key", "offset": 0,
+                                          "nbytes": len(data), "crc32": zlib.crc32(data),
+                                          "dtype": "bfloat16", "shape": [4, 2, 128]}]}
+
+    def write(name: str, hdr: dict, payload: bytes, magic: bytes = snapshot.MAGIC):
+        head = json.dumps(hdr).encode()
+        base = (len(magic) + 8 + len(head) + 4095) // 4096 * 4096
+        p = tmp_path / name
+        p.write_bytes(magic + struct.pack("<Q", len(head)) + head
+                      + b"\0" * (base - len(magic) - 8 - len(head)) + payload)
+        return p
+
+    header_ok, base = snapshot.read_header(write("ok.h3kv", header, data))
+    assert header_ok["block_index"] == 1 and base == 4096
+    with pytest.raises(ValueError, match="not an H3 cache snapshot"):
+        snapshot.read_header(write("magic.h3kv", header, data, magic=b"NOTACACH"))
+    with pytest.raises(ValueError, match="format"):
+        snapshot.read_header(write("ver.h3kv", dict(header, format=99), data))
+    with pytest.raises(ValueError, match="truncated"):
+        snapshot.load_cache(write("short.h3kv", header, data[:100]))
+    corrupt = bytearray(data)
+    corrupt[17] ^= 1
+    with pytest.raises(ValueError, match="CRC-32"):
+        snapshot.load_cache(write("crc.h3kv", header, bytes(corrupt)))
+    with pytest.raises(ValueError, match="contract"):
+        snapshot.load_cache(write("c.h3kv", header, data),
+                            contract=KVContract(local_heads=4, head_dim=128))
