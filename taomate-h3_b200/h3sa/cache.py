@@ -68,6 +68,64 @@ class AVKV:
     value: torch.Tensor
 
 
+@dataclass(frozen=True)
+class VideoKV:
+    """Dense video-only keys and values for one attention layer (F/streaming/cache.py:44-54)."""
+
+    key: torch.Tensor
+    value: torch.Tensor
+
+
+def _check_prefix_pair(pair, contract: KVContract, layer: str) -> None:
+    tail = (contract.local_heads, contract.head_dim)
+    if (pair.key.ndim != 3 or pair.key.shape != pair.value.shape
+            or tuple(pair.key.shape[1:]) != tail or pair.key.dtype != contract.dtype
+            or pair.value.dtype != contract.dtype):
+        raise ValueError(f"{layer} temporary full-prefix K/V must be [tokens, {tail[0]}, "
+                         f"{tail[1]}] {contract.dtype}")
+
+
+class TemporaryVideoPrefix:
+    """Per-layer video K/V a full-prefix capture recorded, seen by later calls as an extra
+    part and never committed (F/streaming/cache.py:118-147)."""
+
+    def __init__(self, layers, *, contract: KVContract,
+                 layer_names: tuple[str, ...] | None = None) -> None:
+        names = tuple(layer_names or MAIN_LAYER_NAMES)
+        self.contract = contract
+        if set(layers) != set(names):
+            raise ValueError("temporary full-prefix must cover every main attention layer")
+        self._layers = {name: layers[name] for name in names}
+        for name, pair in self._layers.items():
+            _check_prefix_pair(pair, contract, name)
+        self.token_count = int(self._layers[names[0]].key.shape[0])
+        if any(int(p.key.shape[0]) != self.token_count for p in self._layers.values()):
+            raise ValueError("temporary full-prefix token counts differ by layer")
+
+    def get(self, layer: str):
+        return self._layers[layer]
+
+    def release(self) -> None:
+        self._layers.clear()
+
+
+class TemporaryAVPrefix(TemporaryVideoPrefix):
+    """Per-layer captured audio (two channels) and video K/V (F/streaming/cache.py:150-196)."""
+
+    def __init__(self, layers, *, video_token_count: int, audio_token_count_per_channel: int,
+                 contract: KVContract, layer_names: tuple[str, ...] | None = None) -> None:
+        for name, count in (("video count", video_token_count),
+                            ("per-channel audio count", audio_token_count_per_channel)):
+            if isinstance(count, bool) or not isinstance(count, int) or count <= 0:
+                raise ValueError(f"temporary AV full-prefix {name} must be positive")
+        super().__init__(layers, contract=contract, layer_names=layer_names)
+        self.video_token_count = video_token_count
+        self.audio_token_count_per_channel = audio_token_count_per_channel
+        self.audio_token_count = 2 * audio_token_count_per_channel
+        if self.token_count != video_token_count + self.audio_token_count:
+            raise ValueError("temporary AV full-prefix token count differs")
+
+
 def _upload_pages(table: torch.Tensor, pages: list[int]) -> None:
     """Copy a page list into the head of a device page table, ordered on the current stream
     without blocking the host: the list goes through a pinned staging tensor, which the
@@ -364,6 +422,8 @@ class CleanAVKVCache:
         self._commit_token_counts: list[int] = []
         self._commit_token_tags: list[tuple[int, ...]] = []
         self._invalid_after_failed_commit = False
+        # set by the FL2AV sink + recent retention; read by history_for_fused_current
+        self._sink_video_only = False
 
     # ------------------------------------------------------------------ properties
     @property
@@ -479,9 +539,18 @@ class CleanAVKVCache:
         self._staged_tags = None
         self._staged_indices = None
 
-    def _resolve_stage(self, token_tags: torch.Tensor, commit_mask: torch.Tensor) -> torch.Tensor:
+    def _resolve_stage(self, token_tags: torch.Tensor, commit_mask: torch.Tensor,
+                       commit_indices: torch.Tensor | None = None) -> torch.Tensor:
         if self._staged_indices is None:
-            indices = torch.nonzero(commit_mask.to(torch.bool), as_tuple=False).flatten()
+            if commit_indices is None:
+                indices = torch.nonzero(commit_mask.to(torch.bool), as_tuple=False).flatten()
+            else:
+                # FL2AV: the caller names the committed rows (a fused forward commits the
+                # previous document's media only, F/streaming/cache.py:589-640)
+                if (commit_indices.ndim != 1 or commit_indices.dtype != torch.long
+                        or commit_indices.device != token_tags.device):
+                    raise ValueError("clean H3 block contains no valid audio/video rows")
+                indices = commit_indices
             if indices.numel() == 0:
                 raise RuntimeError("clean commit did not contain audio/video rows")
             selected_tags = token_tags.index_select(0, indices)
@@ -517,26 +586,28 @@ class CleanAVKVCache:
             raise RuntimeError(f"{layer_name}: persistent KV must reside on {self.contract.device_type}")
 
     def stage(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,
-              token_tags: torch.Tensor, commit_mask: torch.Tensor) -> None:
+              token_tags: torch.Tensor, commit_mask: torch.Tensor, *,
+              commit_indices: torch.Tensor | None = None) -> None:
         """Stage clean audio/video rows produced by one transformer layer.
 
-        The committed rows (``nonzero(commit_mask)`` in packed order) are written into the
-        layer's tail, directly after its history.
+        The committed rows (``nonzero(commit_mask)`` in packed order, or ``commit_indices``)
+        are written into the layer's tail, directly after its history.
         """
 
         self._check_stage_args(layer_name, key, value, token_tags, commit_mask)
-        indices = self._resolve_stage(token_tags, commit_mask)
+        indices = self._resolve_stage(token_tags, commit_mask, commit_indices)
         paged = self.layer(layer_name, key.device)
         paged.write(key.contiguous(), value.contiguous(), start=paged.history_rows,
                     count=int(indices.numel()), src_index=indices.to(torch.int32))
         self._staged[layer_name] = int(indices.numel())
 
     def stage_in_place(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,
-                       token_tags: torch.Tensor, commit_mask: torch.Tensor) -> None:
+                       token_tags: torch.Tensor, commit_mask: torch.Tensor, *,
+                       commit_indices: torch.Tensor | None = None) -> None:
         """Stage rows the streaming hook already wrote to the tail, in commit order."""
 
         self._check_stage_args(layer_name, key, value, token_tags, commit_mask)
-        indices = self._resolve_stage(token_tags, commit_mask)
+        indices = self._resolve_stage(token_tags, commit_mask, commit_indices)
         self._staged[layer_name] = int(indices.numel())
 
     def commit(self, *, retain_recent_commit_count: int | None = None) -> None:
@@ -630,6 +701,7 @@ class CleanAVKVCache:
             return
         if isinstance(recent_count, bool) or not isinstance(recent_count, int) or recent_count < 0:
             raise ValueError("recent clean commit count must be non-negative")
+        self._sink_video_only = bool(sink_video_only)
         if block_count == 0:
             return
         recent_start = max(0, block_count - recent_count)
@@ -714,6 +786,43 @@ class CleanAVKVCache:
         rows = list(range(offsets[0], offsets[1])) + list(range(offsets[start], offsets[-1]))
         return self._rows_view(layer_name, rows)
 
+    def history_for_fused_current_rows(self, *, use_sink: bool = False,
+                                       recent_blocks: int | None = None) -> list[int] | None:
+        """Logical history rows of ``history_for_fused_current`` (None: no history)."""
+
+        self._require_valid()
+        offsets = self._block_offsets()
+        blocks = len(self._commit_token_counts)
+        if blocks == 0:
+            return None
+        if recent_blocks is None:
+            return list(range(offsets[-1]))
+        persistent_recent = max(0, recent_blocks - 1)
+        if not use_sink:
+            if persistent_recent == 0:
+                return None
+            first = max(0, blocks - persistent_recent)
+            return list(range(offsets[first], offsets[-1]))
+        start = max(1, blocks - persistent_recent)
+        sink_tags = self._commit_token_tags[0]
+        if (self._sink_video_only and self.retained_blocks + 1 > recent_blocks
+                and AUDIO_TOKEN_TAG in sink_tags):
+            # the pending document ages the sink out of the recent window: its audio rows go
+            sink = [row for row, tag in enumerate(sink_tags) if tag == VIDEO_TOKEN_TAG]
+        else:
+            sink = list(range(offsets[1]))
+        return sink + list(range(offsets[start], offsets[-1]))
+
+    def history_for_fused_current(self, layer_name: str, *, use_sink: bool = False,
+                                  recent_blocks: int | None = None) -> AVKV | None:
+        """The persistent part a fused forward's current document sees: all history, or
+        with ``recent_blocks`` one recent slot fewer (the packed previous document supplies
+        the newest block), optionally with the sink (F/streaming/cache.py:368-407)."""
+
+        _validate_layer_name(layer_name, self.layer_names)
+        rows = self.history_for_fused_current_rows(use_sink=use_sink, recent_blocks=recent_blocks)
+        return None if not rows else self._rows_view(layer_name, rows)
+
     def attention_history_rows(self, *, count: int, recent_full_blocks: int,
                                older_video_stride: int, preserve_sink: bool = False) -> list[int] | None:
         """Logical history rows of ``attention_history``, in order (None: no history)."""
@@ -795,6 +904,7 @@ class CleanAVKVCache:
         self._block_index = 0
         self._clear_staging()
         self._invalid_after_failed_commit = False
+        self._sink_video_only = False
 
     def retained_rows(self, selection: list[tuple[int, bool]]) -> tuple[list[int], list[int], list[tuple[int, ...]]]:
         """Logical rows kept by a ``(commit, video_only)`` selection, with counts and tags."""
@@ -850,6 +960,9 @@ class CleanAVKVCache:
 __all__ = [
     "AUDIO_TOKEN_TAG",
     "AVKV",
+    "TemporaryAVPrefix",
+    "TemporaryVideoPrefix",
+    "VideoKV",
     "CleanAVKVCache",
     "KVContract",
     "MAIN_LAYER_NAMES",

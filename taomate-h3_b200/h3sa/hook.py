@@ -1,23 +1,30 @@
 """Streaming attention hook with the reference's call protocol, on the sm_100a kernels.
 
-Mirrors ``H3StreamingAttentionHook`` (T/streaming/attention_hook.py:39-252): the same
-keyword call, validation order and messages, live-document rule, modes and receipt
-counters. Per packed document the visibility is unchanged:
+Mirrors ``H3StreamingAttentionHook`` in both of its forms: the T hook
+(T/streaming/attention_hook.py:39-252: ``activate(mode)``, NOISY / CLEAN_COMMIT) and the
+FL2AV one (F/streaming/attention_hook.py:373-1593: ``activate(*, mode, block_index,
+full_prefix, ...)``, the PROGRESS_COMMIT, FUSED_PROGRESS_DENOISE and FULL_PREFIX_CAPTURE
+modes, temporary full prefixes), with the same keyword call, validation order and messages,
+live-document rule and receipt counters. Per packed document the visibility is unchanged:
 
-* the live document's condition (text) rows attend to condition K/V only;
-* its media rows attend to [condition, persistent clean AV history, current media];
+* a live document's condition (text) rows attend to its condition K/V only;
+* its media rows attend to [condition, temporary prefix, persistent clean AV history,
+  current media] (F/streaming/attention_hook.py:193-216); in a fused progress-denoise
+  forward the current document sees the fused-current history view plus the previous
+  document's media rows instead of the full history, and the previous document is the block
+  being committed;
 * every other (pad) document attends to itself.
 
 What changes is the data path. Instead of ``index_select`` + ``torch.cat`` of the whole
-history and one FlashAttention-3 launch per part, the hook writes the current media,
-condition and other-document K/V rows into the layer's page sequence right after the
-persistent history::
+history and one FlashAttention-3 launch per part, the hook writes each live document's
+media, condition and extra K/V rows into the layer's page sequence after the persistent
+history::
 
-    logical KV rows: [history | media | condition | other documents]
+    logical KV rows: [history | doc A: media, condition, prefix | doc B: ... | others]
 
-and runs every document's attention in one kernel launch over that sequence. In
-CLEAN_COMMIT mode the media rows written there are exactly the rows the cache stages, so
-the commit needs no further copy.
+so that every query set attends to one contiguous range, and runs the live documents'
+attention in one kernel launch. The first live document's media rows sit right after the
+history: they are exactly the rows a clean commit stages, so the commit needs no copy.
 
 Backends (``attention_backend``): ``"flash_attn_3"``/``"flash_attn3"``/``"sdpa"`` (dense
 bf16), ``"flash_attn3_fp8_dynamic"`` (per-call per-head e4m3 Q/K/V,
@@ -25,7 +32,9 @@ F/streaming/attention_hook.py:1081-1098), ``"flash_attn3_fp8_segmented"`` (e4m3 
 parts quantised once at commit, :1015-1066), ``"flash_attn3_fp8_segmented_topk"`` (the same
 over the committed blocks whose key summaries score highest against the media queries,
 :1256-1302) and ``"flex_dynamic_blocksparse"`` (history block top-k,
-F/inference/dynamic_block_sparse.py:50-172).
+F/inference/dynamic_block_sparse.py:50-172). The e4m3 and block-sparse backends run the
+NOISY / CLEAN_COMMIT / PROGRESS_COMMIT modes without a temporary prefix; fused forwards,
+prefix captures and temporary prefixes run on the dense backends.
 """
 
 from __future__ import annotations
@@ -36,7 +45,8 @@ from typing import Sequence
 import torch
 
 from . import _lib
-from .cache import CleanAVKVCache
+from .cache import (AUDIO_TOKEN_TAG, VIDEO_TOKEN_TAG, AVKV, CleanAVKVCache, TemporaryAVPrefix,
+                    TemporaryVideoPrefix, VideoKV)
 from .kernels import PAGE_ROWS
 from .kernels import (AttentionProblem, attention_fwd, attention_fwd_fp8_parts, kv_copy_rows,
                       quantize_fp8_e4m3_per_head, quantize_fp8_pool)
@@ -53,6 +63,12 @@ class HookMode(str, Enum):
     IDLE = "idle"
     NOISY = "noisy"
     CLEAN_COMMIT = "clean_commit"
+    PROGRESS_COMMIT = "progress_commit"
+    FUSED_PROGRESS_DENOISE = "fused_progress_denoise"
+    FULL_PREFIX_CAPTURE = "full_prefix_capture"
+
+
+_COMMIT_MODES = (HookMode.CLEAN_COMMIT, HookMode.PROGRESS_COMMIT)
 
 
 def _live_documents_from_mask(commit_mask: torch.Tensor,
@@ -98,26 +114,73 @@ def _as_range(indices: torch.Tensor) -> tuple[int, int] | None:
     return (first, last + 1) if last - first + 1 == n else None
 
 
-class _DocumentPlan:
-    """Row bookkeeping of one activation, resolved on the first layer call."""
+def _full_prefix_capture_rows(tags: torch.Tensor, commit: torch.Tensor, video_rows: int,
+                              audio_rows_per_channel: int | None) -> torch.Tensor:
+    """Rows a full-prefix capture keeps: the newest ``video_rows`` committed video rows,
+    preceded by the newest ``audio_rows_per_channel`` audio rows of each of the two channels
+    (channel-major), F/streaming/attention_hook.py:254-285. Host tensors in and out."""
 
-    def __init__(self, boundaries: tuple[tuple[int, int], ...], live: int,
-                 commit_mask_host: torch.Tensor, device: torch.device) -> None:
-        start, stop = boundaries[live]
-        media_mask = commit_mask_host[start:stop]
+    video = torch.nonzero(commit & (tags == VIDEO_TOKEN_TAG), as_tuple=False).view(-1)
+    if int(video.numel()) < video_rows:
+        raise RuntimeError("full-prefix capture contains too few video rows")
+    video = video[-video_rows:]
+    if audio_rows_per_channel is None:
+        return video
+    audio = torch.nonzero(commit & (tags == AUDIO_TOKEN_TAG), as_tuple=False).view(-1)
+    if int(audio.numel()) % 2:
+        raise RuntimeError("full-prefix capture contains incomplete audio channels")
+    available = int(audio.numel()) // 2
+    if available < audio_rows_per_channel:
+        raise RuntimeError("full-prefix capture contains too few audio rows")
+    audio = audio.reshape(2, available)[:, -audio_rows_per_channel:].reshape(-1)
+    return torch.cat((audio, video))
+
+
+class _Rows:
+    """One set of packed rows: host indices, their device copy, and the run they form."""
+
+    def __init__(self, host: torch.Tensor, device: torch.device) -> None:
+        self.host = host
+        self.n = int(host.numel())
+        self.range = _as_range(host)
+        self.index = host.to(device=device, dtype=torch.int32)
+
+
+class _LiveDoc:
+    def __init__(self, index: int, start: int, stop: int, commit_host: torch.Tensor,
+                 device: torch.device) -> None:
+        media_mask = commit_host[start:stop]
         cond = torch.nonzero(~media_mask, as_tuple=False).flatten() + start
         media = torch.nonzero(media_mask, as_tuple=False).flatten() + start
         if cond.numel() == 0 or media.numel() == 0:
             raise RuntimeError("live streaming document must contain condition and media rows")
+        self.index = index
+        self.cond = _Rows(cond, device)
+        self.media = _Rows(media, device)
+
+
+class _DocumentPlan:
+    """Row bookkeeping of one activation, resolved on the first layer call.
+
+    ``docs``: the live documents in the order their rows follow the history (one; or, in a
+    fused forward, the previous document, whose media rows the commit stages, then the
+    current one). ``previous_media``: the previous document's media rows the current one
+    attends to (video only with ``fused_previous_video_only``)."""
+
+    def __init__(self, boundaries: tuple[tuple[int, int], ...], live: tuple[int, ...],
+                 commit_mask_host: torch.Tensor, tags_host: torch.Tensor | None,
+                 device: torch.device, previous_video_only: bool = False) -> None:
         self.boundaries = boundaries
         self.live = live
-        self.n_cond = int(cond.numel())
-        self.n_media = int(media.numel())
-        self.cond_range = _as_range(cond)
-        self.media_range = _as_range(media)
-        self.cond_index = cond.to(device=device, dtype=torch.int32)
-        self.media_index = media.to(device=device, dtype=torch.int32)
-        self.others = [(a, b) for i, (a, b) in enumerate(boundaries) if i != live and b > a]
+        self.docs = [_LiveDoc(i, *boundaries[i], commit_mask_host, device) for i in live]
+        self.others = [(a, b) for i, (a, b) in enumerate(boundaries) if i not in live and b > a]
+        self.previous_media: _Rows | None = None
+        if len(self.docs) == 2:
+            prev = self.docs[0].media.host
+            if previous_video_only:
+                assert tags_host is not None
+                prev = prev[tags_host[prev] == VIDEO_TOKEN_TAG]
+            self.previous_media = _Rows(prev, device)
 
 
 class H3StreamingAttentionHook:
@@ -147,8 +210,22 @@ class H3StreamingAttentionHook:
         self.dynamic_block_sparse_selected_blocks = 0
         self.dynamic_block_sparse_history_blocks = 0
         self.mode = HookMode.IDLE
+        self._fl2av = False  # activated through the FL2AV form
+        self.block_index: int | None = None
+        self.full_prefix: TemporaryAVPrefix | TemporaryVideoPrefix | None = None
+        self.fused_previous_full_prefix: TemporaryAVPrefix | TemporaryVideoPrefix | None = None
+        self.fused_previous_video_only = False
+        self.fused_current_use_sink: bool | None = None
+        self.fused_current_recent_blocks: int | None = None
+        self._denoise_step_index: int | None = None
+        self._phase_index: int | None = None
+        self._capture_video_rows = 0
+        self._capture_audio_rows_per_channel: int | None = None
+        self._captured_full_prefix_layers: dict[str, AVKV | VideoKV] = {}
+        self._capture_index: torch.Tensor | None = None
         self._plan: _DocumentPlan | None = None
         self._plan_key: tuple[int, ...] | None = None
+        self._plan_hint: tuple[int, ...] | None = None
         self._device_error: torch.Tensor | None = None
         self._fp8_pools: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
         # Set by h3sa.layer for a call whose heads -> sequence exchange is peer stores: the
@@ -172,20 +249,143 @@ class H3StreamingAttentionHook:
     def active(self) -> bool:
         return self.mode is not HookMode.IDLE
 
-    def activate(self, mode: HookMode) -> None:
+    # ------------------------------------------------------------------ modes
+    def activate(self, mode: HookMode | None = None, *, block_index: int | None = None,
+                 full_prefix: TemporaryAVPrefix | TemporaryVideoPrefix | None = None,
+                 fused_previous_full_prefix: TemporaryAVPrefix | TemporaryVideoPrefix | None = None,
+                 fused_previous_video_only: bool = False,
+                 fused_current_use_sink: bool | None = None,
+                 fused_current_recent_blocks: int | None = None,
+                 denoise_step_index: int | None = None,
+                 phase_index: int | None = None) -> None:
+        """``activate(mode)``: the T form (NOISY or CLEAN_COMMIT,
+        T/streaming/attention_hook.py:104-116). With ``block_index``: the FL2AV form and its
+        checks (F/streaming/attention_hook.py:577-643)."""
+
+        if block_index is None:
+            if self.active:
+                raise RuntimeError("streaming attention hook is already active")
+            if mode not in (HookMode.NOISY, HookMode.CLEAN_COMMIT):
+                raise ValueError(f"unsupported streaming hook mode: {mode}")
+            self._reset(mode)
+            return
+        mode = HookMode(mode)
         if self.active:
-            raise RuntimeError("streaming attention hook is already active")
-        if mode not in (HookMode.NOISY, HookMode.CLEAN_COMMIT):
-            raise ValueError(f"unsupported streaming hook mode: {mode}")
+            raise RuntimeError("H3 streaming attention hook is already active")
+        if block_index != self.cache.committed_blocks:
+            raise ValueError("streaming attention block differs from clean history")
+        if full_prefix is not None and full_prefix.contract != self.cache.contract:
+            raise ValueError("temporary prefix and persistent cache contracts differ")
+        if (fused_previous_full_prefix is not None
+                and fused_previous_full_prefix.contract != self.cache.contract):
+            raise ValueError("fused previous prefix and persistent cache contracts differ")
+        if fused_previous_full_prefix is not None and mode is not HookMode.FUSED_PROGRESS_DENOISE:
+            raise ValueError("fused previous prefix requires fused progress-denoise mode")
+        if fused_previous_video_only and mode is not HookMode.FUSED_PROGRESS_DENOISE:
+            raise ValueError(
+                "fused previous video-only visibility requires fused progress-denoise mode")
+        if ((fused_current_use_sink is not None or fused_current_recent_blocks is not None)
+                and mode is not HookMode.FUSED_PROGRESS_DENOISE):
+            raise ValueError("fused current history policy requires fused progress-denoise mode")
+        if denoise_step_index is not None and mode not in (HookMode.NOISY,
+                                                            HookMode.FUSED_PROGRESS_DENOISE):
+            raise ValueError("denoise step index requires noisy or fused progress-denoise mode")
+        if mode in (HookMode.IDLE, HookMode.FULL_PREFIX_CAPTURE):
+            raise ValueError(f"{mode.value} is not an activation mode")
+        self._require_dense_for(mode is HookMode.FUSED_PROGRESS_DENOISE
+                                or full_prefix is not None)
+        self._reset(mode)
+        self._fl2av = True
+        self.block_index = block_index
+        self.full_prefix = full_prefix
+        self.fused_previous_full_prefix = fused_previous_full_prefix
+        self.fused_previous_video_only = bool(fused_previous_video_only)
+        self.fused_current_use_sink = fused_current_use_sink
+        self.fused_current_recent_blocks = fused_current_recent_blocks
+        self._denoise_step_index = denoise_step_index
+        self._phase_index = phase_index
+
+    def _require_dense_for(self, extras: bool) -> None:
+        if extras and self.backend not in DENSE_BACKENDS:
+            raise ValueError(f"the {self.backend} backend runs NOISY, CLEAN_COMMIT and "
+                             "PROGRESS_COMMIT without a temporary prefix; fused forwards, "
+                             "prefix captures and temporary prefixes need a dense backend")
+
+    def _reset(self, mode: HookMode) -> None:
         self.mode = mode
+        self._fl2av = False
+        self.block_index = None
+        self.full_prefix = None
+        self.fused_previous_full_prefix = None
+        self.fused_previous_video_only = False
+        self.fused_current_use_sink = None
+        self.fused_current_recent_blocks = None
+        self._denoise_step_index = None
+        self._phase_index = None
+        self._capture_video_rows = 0
+        self._capture_audio_rows_per_channel = None
+        self._captured_full_prefix_layers = {}
+        self._capture_index = None
         self._plan = None
         self._plan_key = None
+        self._plan_hint = None
 
     def deactivate(self) -> None:
-        self.mode = HookMode.IDLE
-        self._plan = None
-        self._plan_key = None
+        self._reset(HookMode.IDLE)
 
+    def begin_full_prefix_capture(self, *, video_rows: int,
+                                  audio_rows_per_channel: int | None = None) -> None:
+        """Start a forward whose committed media rows become a temporary full prefix
+        (F/streaming/attention_hook.py:658-684): its media attend to the current document
+        only, and every layer's selected K/V rows are kept."""
+
+        if self.active:
+            raise RuntimeError("H3 streaming attention hook is already active")
+        if isinstance(video_rows, bool) or not isinstance(video_rows, int) or video_rows <= 0:
+            raise ValueError("full-prefix capture video_rows must be positive")
+        if audio_rows_per_channel is not None and (
+                isinstance(audio_rows_per_channel, bool)
+                or not isinstance(audio_rows_per_channel, int) or audio_rows_per_channel <= 0):
+            raise ValueError("full-prefix capture audio_rows_per_channel must be positive")
+        self._require_dense_for(True)
+        self._reset(HookMode.FULL_PREFIX_CAPTURE)
+        self._fl2av = True
+        self.block_index = self.cache.committed_blocks
+        self._capture_video_rows = video_rows
+        self._capture_audio_rows_per_channel = audio_rows_per_channel
+
+    def finish_full_prefix_capture(self) -> TemporaryAVPrefix | TemporaryVideoPrefix:
+        """The captured prefix, once every layer has run (F/streaming/attention_hook.py:709-735)."""
+
+        if self.mode is not HookMode.FULL_PREFIX_CAPTURE:
+            raise RuntimeError("no H3 full-prefix capture is active")
+        layers = self._captured_full_prefix_layers
+        names = self.cache.layer_names
+        if tuple(layers) != names:
+            missing = [name for name in names if name not in layers]
+            self.deactivate()
+            raise RuntimeError(f"full-prefix capture did not traverse all H3 layers: {missing}")
+        audio = self._capture_audio_rows_per_channel
+        if audio is None:
+            prefix = TemporaryVideoPrefix(layers, contract=self.cache.contract, layer_names=names)
+        else:
+            prefix = TemporaryAVPrefix(layers, video_token_count=self._capture_video_rows,
+                                       audio_token_count_per_channel=audio,
+                                       contract=self.cache.contract, layer_names=names)
+        self.deactivate()
+        return prefix
+
+    def _transient(self, layer_name: str, doc_position: int, fused: bool):
+        """The temporary prefix a live document sees: in a fused forward the previous
+        document keeps the prefix of its own time (F/streaming/attention_hook.py:686-707)."""
+
+        if self.mode is HookMode.FULL_PREFIX_CAPTURE:
+            return None
+        prefix = (self.fused_previous_full_prefix if fused and doc_position == 0
+                  else self.full_prefix)
+        return None if prefix is None else prefix.get(layer_name)
+
+    # ------------------------------------------------------------------ helpers
     def device_error(self, device: torch.device) -> torch.Tensor:
         if self._device_error is None or self._device_error.device != device:
             self._device_error = torch.zeros(1, dtype=torch.int32, device=device)
@@ -217,18 +417,33 @@ class H3StreamingAttentionHook:
             raise RuntimeError(f"{layer_name}: streaming attention requires {contract.device_type} QKV")
 
     def _resolve_plan(self, boundaries: tuple[tuple[int, int], ...],
-                      commit_mask: torch.Tensor, device: torch.device,
+                      commit_mask: torch.Tensor, token_tags: torch.Tensor, device: torch.device,
                       live_documents_hint: tuple[int, ...] | None = None) -> _DocumentPlan:
         points = tuple(b for _, b in boundaries)
-        if self._plan is not None and self._plan_key == points:
-            return self._plan
+        if self._plan is not None:
+            if self._plan_key == points:
+                if (self._fl2av and live_documents_hint is not None
+                        and live_documents_hint != self._plan.live):
+                    raise ValueError("live document hint changed within one streaming step")
+                return self._plan
+            if self._fl2av:
+                raise ValueError("packed H3 boundaries changed within one streaming step")
         live = _live_documents_from_mask_or_hint(commit_mask, boundaries, live_documents_hint)
-        if len(live) != 1:
+        fused = self.mode is HookMode.FUSED_PROGRESS_DENOISE
+        if self._fl2av:
+            expected = 2 if fused else 1
+            if len(live) != expected:
+                raise ValueError("streaming session target-document count differs from hook "
+                                 f"mode: expected={expected}, actual={len(live)}")
+        elif len(live) != 1:
             raise RuntimeError(f"direct streaming expects exactly one live document, got {live}")
-        plan = _DocumentPlan(boundaries, live[0], commit_mask.detach().to("cpu", torch.bool), device)
+        tags_host = token_tags.detach().to("cpu") if fused else None
+        plan = _DocumentPlan(boundaries, live, commit_mask.detach().to("cpu", torch.bool),
+                             tags_host, device, self.fused_previous_video_only)
         self._plan, self._plan_key = plan, points
         return plan
 
+    # ------------------------------------------------------------------ the call
     def __call__(self, *, attention: object, layer_name: str, query: torch.Tensor,
                  key: torch.Tensor, value: torch.Tensor, token_tags: torch.Tensor,
                  commit_mask: torch.Tensor, cu_seqlens_host: Sequence[int] | None = None,
@@ -237,7 +452,7 @@ class H3StreamingAttentionHook:
         """The T call (T/streaming/attention_hook.py:118-129) or the FL2AV one
         (F/streaming/attention_hook.py:739-753): ``cu_seqlens`` (device) stands in for
         ``cu_seqlens_host`` when that is None, ``max_seqlen`` is not needed, and
-        ``live_documents_hint`` names the live document without reading the commit mask."""
+        ``live_documents_hint`` names the live documents without reading the commit mask."""
 
         del max_seqlen
         if not self.active:
@@ -256,8 +471,11 @@ class H3StreamingAttentionHook:
                 or any(left > right for left, right in zip(points, points[1:]))):
             raise RuntimeError(f"{layer_name}: invalid packed sequence boundaries")
         boundaries = tuple(zip(points[:-1], points[1:]))
-        plan = self._resolve_plan(boundaries, commit_mask, query.device, live_documents_hint)
+        plan = self._resolve_plan(boundaries, commit_mask, token_tags, query.device,
+                                  live_documents_hint)
         scale = float(getattr(attention, "softmax_scale"))
+        fused = self.mode is HookMode.FUSED_PROGRESS_DENOISE
+        capture = self.mode is HookMode.FULL_PREFIX_CAPTURE
 
         query = query.contiguous()
         key = key.contiguous()
@@ -265,45 +483,82 @@ class H3StreamingAttentionHook:
         paged = self.cache.layer(layer_name, query.device)
         err = self.device_error(query.device)
         n_hist = paged.history_rows
-        m0 = n_hist
-        c0 = m0 + plan.n_media
-        o0 = c0 + plan.n_cond
 
-        # 1. current K/V rows into the tail of the layer's page sequence
-        if plan.media_range is not None:
-            paged.write(key, value, start=m0, count=plan.n_media, src_start=plan.media_range[0])
-        else:
-            paged.write(key, value, start=m0, count=plan.n_media, src_index=plan.media_index)
-        if plan.cond_range is not None:
-            paged.write(key, value, start=c0, count=plan.n_cond, src_start=plan.cond_range[0])
-        else:
-            paged.write(key, value, start=c0, count=plan.n_cond, src_index=plan.cond_index)
+        # 1. K/V rows of every live document into the page sequence after the history
+        cursor = n_hist
+        regions = []  # per live document: (media kv start, condition start, region end)
+
+        def put_rows(rows: _Rows) -> None:
+            nonlocal cursor
+            if rows.range is not None:
+                paged.write(key, value, start=cursor, count=rows.n, src_start=rows.range[0])
+            else:
+                paged.write(key, value, start=cursor, count=rows.n, src_index=rows.index)
+            cursor += rows.n
+
+        def put_dense(pair) -> None:
+            nonlocal cursor
+            n = int(pair.key.shape[0])
+            paged.write(pair.key.contiguous(), pair.value.contiguous(), start=cursor, count=n)
+            cursor += n
+
+        for position, doc in enumerate(plan.docs):
+            first = cursor
+            put_rows(doc.media)
+            c_start = cursor
+            put_rows(doc.cond)
+            transient = self._transient(layer_name, position, fused)
+            if transient is not None:
+                put_dense(transient)
+            if fused and position == 1:
+                assert plan.previous_media is not None
+                if plan.previous_media.n:
+                    put_rows(plan.previous_media)
+                view = self.cache.history_for_fused_current_rows(
+                    use_sink=bool(self.fused_current_use_sink),
+                    recent_blocks=self.fused_current_recent_blocks)
+                if view:
+                    index = torch.tensor(view, dtype=torch.int32).pin_memory().to(
+                        query.device, non_blocking=True)
+                    paged.reserve(cursor + len(view))
+                    kv_copy_rows([paged.key, paged.value], [paged.key, paged.value],
+                                 count=len(view), src_table=paged.table, dst_table=paged.table,
+                                 src_index=index, dst_start=cursor)
+                    cursor += len(view)
+                kv_start = first
+            else:
+                # the first document's media see the persistent history (none while capturing)
+                kv_start = n_hist if capture else 0
+            regions.append((kv_start, first, c_start, cursor))
         other_kv: list[tuple[int, int, int]] = []
-        cursor = o0
         for a, b in plan.others:
             paged.write(key, value, start=cursor, count=b - a, src_start=a)
             other_kv.append((a, b, cursor))
             cursor += b - a
 
-        # 2. attention problems over packed query rows (gathered when not contiguous)
+        # 2. one problem per query set (gathered into a compact buffer unless every set is a
+        # contiguous run of the packed rows)
+        sets = [rows for doc in plan.docs for rows in (doc.media, doc.cond)]
         out = torch.empty_like(query)
-        q_src = query
-        media_q = plan.media_range
-        cond_q = plan.cond_range
         gathered = None
-        if media_q is None or cond_q is None:
-            gathered = torch.empty(plan.n_media + plan.n_cond, *query.shape[1:], dtype=query.dtype,
-                                   device=query.device)
-            kv_copy_rows([query], [gathered], count=plan.n_media, src_index=plan.media_index)
-            kv_copy_rows([query], [gathered], count=plan.n_cond, src_index=plan.cond_index,
-                         dst_start=plan.n_media)
+        if all(r.range is not None for r in sets):
+            q_src = query
+            q_ranges = [r.range for r in sets]
+        else:
+            total = sum(r.n for r in sets)
+            gathered = torch.empty(total, *query.shape[1:], dtype=query.dtype, device=query.device)
+            q_ranges, at = [], 0
+            for r in sets:
+                kv_copy_rows([query], [gathered], count=r.n, src_index=r.index, dst_start=at)
+                q_ranges.append((at, at + r.n))
+                at += r.n
             q_src = gathered
-            media_q = (0, plan.n_media)
-            cond_q = (plan.n_media, plan.n_media + plan.n_cond)
-        n_kv_media = o0  # history + media + condition
-        media_problem = AttentionProblem(media_q[0], media_q[1], 0, n_kv_media,
-                                         sparse=self.backend in SPARSE_BACKENDS)
-        cond_problem = AttentionProblem(cond_q[0], cond_q[1], c0, o0)
+        problems = []
+        for d, (kv_start, m_start, c_start, end) in enumerate(regions):
+            mq, cq = q_ranges[2 * d], q_ranges[2 * d + 1]
+            problems.append(AttentionProblem(mq[0], mq[1], kv_start, end,
+                                             sparse=self.backend in SPARSE_BACKENDS))
+            problems.append(AttentionProblem(cq[0], cq[1], c_start, c_start + (cq[1] - cq[0])))
         out_main = out if gathered is None else torch.empty_like(gathered)
         # rows stored straight into the owners' sequence shards when the output rows are the
         # query rows (no gather) and the launch is bf16
@@ -311,8 +566,9 @@ class H3StreamingAttentionHook:
         if exchange is not None and (gathered is not None or self.backend in FP8_BACKENDS):
             exchange = None
         self.last_output_exchanged = exchange is not None
-        self._launch(layer_name, paged, q_src, out_main, [media_problem, cond_problem], scale,
-                     n_kv_media, n_hist, plan, err, exchange)
+        n_kv_media = regions[0][3]
+        self._launch(layer_name, paged, q_src, out_main, problems, scale, n_kv_media, n_hist,
+                     plan, err, exchange)
         if other_kv:
             probs = [AttentionProblem(a, b, c, c + (b - a)) for a, b, c in other_kv]
             for i in range(0, len(probs), _lib.MAX_PROBLEMS):
@@ -325,18 +581,43 @@ class H3StreamingAttentionHook:
                                   device_error=err)
                 self.launches += 1
         if gathered is not None:
-            kv_copy_rows([out_main], [out], count=plan.n_media, src_start=0,
-                         dst_index=plan.media_index)
-            kv_copy_rows([out_main], [out], count=plan.n_cond, src_start=plan.n_media,
-                         dst_index=plan.cond_index)
+            for r, (lo, hi) in zip(sets, q_ranges):
+                kv_copy_rows([out_main], [out], count=r.n, src_start=lo, dst_index=r.index)
 
-        self.kernel_calls += 2 + len(other_kv)
+        self.kernel_calls += len(problems) + len(other_kv)
         self.query_tokens += int(query.shape[0])
-        self.key_tokens += n_kv_media + plan.n_cond + sum(b - a for a, b, _ in other_kv)
+        self.key_tokens += sum(p.kv_hi - p.kv_lo for p in problems) + sum(
+            b - a for a, b, _ in other_kv)
 
-        if self.mode is HookMode.CLEAN_COMMIT:
+        # 3. what the mode keeps
+        if capture:
+            self._capture(layer_name, key, value, token_tags, commit_mask)
+        elif self.mode in _COMMIT_MODES:
+            # the live document's media rows were written right after the history
             self.cache.stage_in_place(layer_name, key, value, token_tags, commit_mask)
+        elif fused:
+            # the previous document is the committed block (F/streaming/attention_hook.py:1580-1590)
+            self.cache.stage_in_place(layer_name, key, value, token_tags, commit_mask,
+                                      commit_indices=plan.docs[0].media.host.to(
+                                          token_tags.device, torch.long))
         return out
+
+    def _capture(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,
+                 token_tags: torch.Tensor, commit_mask: torch.Tensor) -> None:
+        if layer_name in self._captured_full_prefix_layers:
+            raise ValueError(f"duplicate full-prefix K/V layer: {layer_name}")
+        if self._capture_index is None:
+            rows = _full_prefix_capture_rows(token_tags.detach().cpu(),
+                                             commit_mask.detach().cpu().to(torch.bool),
+                                             self._capture_video_rows,
+                                             self._capture_audio_rows_per_channel)
+            self._capture_index = rows.to(device=key.device, dtype=torch.int32)
+        n = int(self._capture_index.numel())
+        k = torch.empty(n, *key.shape[1:], dtype=key.dtype, device=key.device)
+        v = torch.empty_like(k)
+        kv_copy_rows([key, value], [k, v], count=n, src_index=self._capture_index)
+        pair = (VideoKV if self._capture_audio_rows_per_channel is None else AVKV)(key=k, value=v)
+        self._captured_full_prefix_layers[layer_name] = pair
 
     # ------------------------------------------------------------------ launches
     def _launch(self, layer_name: str, paged, q_src: torch.Tensor, out: torch.Tensor,

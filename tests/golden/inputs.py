@@ -63,3 +63,32 @@ def prologue_inputs(seed: int = 11, seq: int = 128, heads: int = 4, head_dim: in
 
 def ulysses_merged(rank: int, tokens: int = 6, heads: int = 4, d: int = 16) -> np.ndarray:
     return np.random.default_rng(100 + rank).standard_normal((tokens, 3 * heads * d)).astype(np.float32)
+
+
+# FL2AV hook schedule: (mode, live documents in the packed sequence, extra activate arguments)
+HOOK_F_SCHEDULE = (
+    ("clean_commit", 1, {}),
+    ("progress_commit", 1, {}),
+    ("capture", 1, {"video_rows": 24, "audio_rows_per_channel": 3}),
+    ("noisy_prefix", 1, {"denoise_step_index": 0}),
+    ("fused_recent", 2, {"fused_previous_video_only": True, "fused_current_use_sink": True,
+                         "fused_current_recent_blocks": 2}),
+    ("fused", 2, {}),
+    ("noisy", 1, {}),
+)
+
+
+def hook_f_inputs(step: int, live: int, heads: int = 2, head_dim: int = 128) -> dict:
+    """One packed call of the FL2AV hook schedule: ``live`` documents of [8 text | 4 + 4
+    audio | 48 video] rows each, then an 8-row pad document; q/k RMS-normalised, bf16."""
+
+    rng = np.random.default_rng(1000 + step)
+    doc = [1] * 8 + [2] * 8 + [0] * 48
+    tags = np.array(doc * live + [-1] * 8, dtype=np.int64)
+    n = len(tags)
+    q = bf16(rms(rng.standard_normal((n, heads, head_dim)).astype(np.float32)))
+    k = bf16(rms(rng.standard_normal((n, heads, head_dim)).astype(np.float32)))
+    v = bf16(rng.standard_normal((n, heads, head_dim)).astype(np.float32))
+    cu = [0] + [64 * (i + 1) for i in range(live)] + [n]
+    return {"q": q, "k": k, "v": v, "token_tags": tags, "commit_mask": (tags == 0) | (tags == 2),
+            "cu_seqlens": cu, "scale": head_dim ** -0.5}

@@ -27,6 +27,13 @@ them from the seeds recorded in each fixture. Fixtures:
                  attention-history queries.
 * ulysses_pad.npz the FL2AV versions with 3 heads over 2 ranks (zero-padded head shards,
                  F/distributed/ulysses.py).
+* hook_f.npz     the FL2AV H3StreamingAttentionHook (F/streaming/attention_hook.py) with its
+                 sdpa backend through every mode: clean and progress commits, a full-prefix
+                 capture, a noisy call over a temporary prefix, fused progress-denoise forwards
+                 (with the recent / sink / previous-video-only policy and without) and a final
+                 noisy call; layer 0's outputs, the captured prefix and the commit ledger. The
+                 hook insists on CUDA tensors: CPU tensors of a subclass that reports is_cuda
+                 stand in, and the K/V pair validators are stubbed.
 * topk.npz       key summaries of the FL2AV segmented-FP8 CleanAVKVCache
                  (F/streaming/cache.py:836-855) over six commits and after a sink + recent
                  retention, with the commit-level top-k selection of the segmented top-k
@@ -323,6 +330,77 @@ def make_topk(path: Path) -> None:
     arrays["retained_counts"] = np.array(cache.commit_token_counts, dtype=np.int64)
     np.savez(path, **arrays)
 
+def make_hook_f(path: Path) -> None:
+    import torch
+    import digitalhuman_h3.streaming.attention_hook as fhook
+    import digitalhuman_h3.streaming.cache as fcache
+    from inputs import HOOK_F_SCHEDULE, hook_f_inputs
+
+    fcache._validate_av_pair = lambda pair, contract, *, layer: None
+    fcache._validate_video_pair = lambda pair, contract, *, layer: None
+
+    class CudaFlagged(torch.Tensor):
+        """CPU tensor that answers is_cuda = True, so the hook's device checks pass."""
+
+        @property
+        def is_cuda(self):
+            return True
+
+    def t(x: np.ndarray, dtype=torch.bfloat16):
+        return torch.from_numpy(x).to(dtype).as_subclass(CudaFlagged)
+
+    class Attn:
+        softmax_scale = 128 ** -0.5
+
+    contract = fcache.KVContract(local_heads=2, head_dim=128)
+    cache = fcache.CleanAVKVCache(contract)
+    hook = fhook.H3StreamingAttentionHook(cache, attention_backend="sdpa")
+    arrays: dict[str, np.ndarray] = {}
+    prefix = None
+    for step, (name, live, extra) in enumerate(HOOK_F_SCHEDULE):
+        x = hook_f_inputs(step, live)
+        kwargs = dict(extra)
+        if name == "capture":
+            hook.begin_full_prefix_capture(**kwargs)
+        else:
+            mode = {"clean_commit": fhook.HookMode.CLEAN_COMMIT,
+                    "progress_commit": fhook.HookMode.PROGRESS_COMMIT,
+                    "noisy_prefix": fhook.HookMode.NOISY, "noisy": fhook.HookMode.NOISY,
+                    "fused_recent": fhook.HookMode.FUSED_PROGRESS_DENOISE,
+                    "fused": fhook.HookMode.FUSED_PROGRESS_DENOISE}[name]
+            kwargs["full_prefix"] = prefix if name in ("noisy_prefix", "fused_recent") else None
+            if name == "fused_recent":
+                kwargs["fused_previous_full_prefix"] = prefix
+                # keep every block but mark the sink video-only: the fused current view then
+                # drops the sink's audio once the pending block ages it out
+                cache.retain_sink_and_recent_commits(cache.retained_blocks, sink_video_only=True)
+            commit = mode in (fhook.HookMode.CLEAN_COMMIT, fhook.HookMode.PROGRESS_COMMIT,
+                              fhook.HookMode.FUSED_PROGRESS_DENOISE)
+            if commit:
+                cache.begin_clean_commit(cache.committed_blocks)
+            hook.activate(mode=mode, block_index=cache.committed_blocks, **kwargs)
+        q, k, v = t(x["q"]), t(x["k"]), t(x["v"])
+        tags = t(x["token_tags"], torch.int64)
+        mask = t(x["commit_mask"], torch.bool)
+        for layer in contract.layer_names:
+            out = hook(attention=Attn(), layer_name=layer, query=q, key=k, value=v,
+                       token_tags=tags, commit_mask=mask, cu_seqlens=None,
+                       cu_seqlens_host=tuple(x["cu_seqlens"]), max_seqlen=64)
+            if layer == contract.layer_names[0]:
+                arrays[f"out_{step}"] = torch.Tensor(out).float().numpy()
+        if name == "capture":
+            prefix = hook.finish_full_prefix_capture()
+            pair = prefix.get(contract.layer_names[0])
+            arrays["prefix_key"] = torch.Tensor(pair.key).float().numpy()
+            arrays["prefix_value"] = torch.Tensor(pair.value).float().numpy()
+        else:
+            hook.deactivate()
+            if commit:
+                cache.commit()
+        arrays[f"counts_{step}"] = np.array(cache.commit_token_counts, dtype=np.int64)
+        arrays[f"blocks_{step}"] = np.array(cache.committed_blocks)
+    np.savez_compressed(path, **arrays)
+
 # ----------------------------------------------------------------------------- ulysses
 def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import datetime
@@ -415,7 +493,7 @@ def main() -> None:
     makers = {"prologue.npz": make_prologue, "hook_cpu.npz": make_hook, "fp8.npz": make_fp8,
               "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
               "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f,
-              "topk.npz": make_topk}
+              "topk.npz": make_topk, "hook_f.npz": make_hook_f}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

@@ -531,3 +531,105 @@ def test_cache_snapshot_round_trip_resumes_bit_exact(tmp_path, segmented: bool) 
     bad.write_bytes(bytes(raw))
     with pytest.raises(ValueError, match="CRC-32"):
         CleanAVKVCache.load_snapshot(bad)
+
+
+def test_fl2av_hook_modes_match_reference_golden() -> None:
+    """The FL2AV activation form through every mode, replaying tests/golden/hook_f.npz (the
+    reference hook's own outputs): clean and progress commits, a full-prefix capture (its
+    rows bit-exact), a noisy call over the captured prefix, fused progress-denoise forwards
+    with and without the recent / sink / previous-video-only policy (each committing the
+    previous document) and a final noisy call. Layer 0's outputs within 1e-2 relative L2 of
+    the reference's bf16 SDPA, commit ledgers identical."""
+
+    sys.path.insert(0, str(GOLDEN))
+    from inputs import HOOK_F_SCHEDULE, hook_f_inputs
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    g = np.load(GOLDEN / "hook_f.npz")
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128))
+    hook = H3StreamingAttentionHook(cache, attention_backend="sdpa")
+    modes = {"clean_commit": HookMode.CLEAN_COMMIT, "progress_commit": HookMode.PROGRESS_COMMIT,
+             "noisy_prefix": HookMode.NOISY, "noisy": HookMode.NOISY,
+             "fused_recent": HookMode.FUSED_PROGRESS_DENOISE,
+             "fused": HookMode.FUSED_PROGRESS_DENOISE}
+    t = lambda a, dt=torch.bfloat16: torch.from_numpy(a).to(dt).cuda()  # noqa: E731
+    prefix = None
+    for step, (name, live, extra) in enumerate(HOOK_F_SCHEDULE):
+        x = hook_f_inputs(step, live)
+        commit = False
+        if name == "capture":
+            hook.begin_full_prefix_capture(**extra)
+        else:
+            kw = dict(extra)
+            kw["full_prefix"] = prefix if name in ("noisy_prefix", "fused_recent") else None
+            if name == "fused_recent":
+                kw["fused_previous_full_prefix"] = prefix
+                cache.retain_sink_and_recent_commits(cache.retained_blocks, sink_video_only=True)
+            mode = modes[name]
+            commit = mode in (HookMode.CLEAN_COMMIT, HookMode.PROGRESS_COMMIT,
+                              HookMode.FUSED_PROGRESS_DENOISE)
+            if commit:
+                cache.begin_clean_commit(cache.committed_blocks)
+            hook.activate(mode=mode, block_index=cache.committed_blocks, **kw)
+        q, k, v = t(x["q"]), t(x["k"]), t(x["v"])
+        tags, mask = t(x["token_tags"], torch.int64), t(x["commit_mask"], torch.bool)
+        for layer in cache.layer_names:
+            out = hook(attention=Attn(), layer_name=layer, query=q, key=k, value=v,
+                       token_tags=tags, commit_mask=mask, cu_seqlens=None,
+                       cu_seqlens_host=tuple(x["cu_seqlens"]), max_seqlen=64)
+            if layer == cache.layer_names[0]:
+                first = out
+        hook.check_device_error()
+        assert rel_l2(first, torch.from_numpy(g[f"out_{step}"])) <= BF16_TOL, (step, name)
+        if name == "capture":
+            prefix = hook.finish_full_prefix_capture()
+            pair = prefix.get(cache.layer_names[0])
+            assert torch.equal(pair.key.float().cpu(), torch.from_numpy(g["prefix_key"]))
+            assert torch.equal(pair.value.float().cpu(), torch.from_numpy(g["prefix_value"]))
+        else:
+            hook.deactivate()
+            if commit:
+                cache.commit()
+        assert list(cache.commit_token_counts) == list(g[f"counts_{step}"]), step
+        assert cache.committed_blocks == int(g[f"blocks_{step}"]), step
+
+
+def test_fl2av_activation_checks_match_reference() -> None:
+    """The FL2AV activate() checks and messages (F/streaming/attention_hook.py:577-620)."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128), layer_names=("blocks.0.attn",))
+    hook = H3StreamingAttentionHook(cache, attention_backend="sdpa")
+    with pytest.raises(ValueError, match="block differs from clean history"):
+        hook.activate(mode=HookMode.NOISY, block_index=1, full_prefix=None)
+    with pytest.raises(ValueError, match="requires fused progress-denoise mode"):
+        hook.activate(mode=HookMode.NOISY, block_index=0, full_prefix=None,
+                      fused_previous_video_only=True)
+    with pytest.raises(ValueError, match="fused current history policy"):
+        hook.activate(mode=HookMode.CLEAN_COMMIT, block_index=0, full_prefix=None,
+                      fused_current_recent_blocks=2)
+    with pytest.raises(ValueError, match="denoise step index requires"):
+        hook.activate(mode=HookMode.CLEAN_COMMIT, block_index=0, full_prefix=None,
+                      denoise_step_index=1)
+    hook.activate(mode=HookMode.NOISY, block_index=0, full_prefix=None)
+    with pytest.raises(RuntimeError, match="already active"):
+        hook.activate(mode=HookMode.NOISY, block_index=0, full_prefix=None)
+    hook.deactivate()
+    with pytest.raises(RuntimeError, match="no H3 full-prefix capture is active"):
+        hook.finish_full_prefix_capture()
+    with pytest.raises(ValueError, match="video_rows must be positive"):
+        hook.begin_full_prefix_capture(video_rows=0)
+    fp8 = H3StreamingAttentionHook(cache, attention_backend="flash_attn3_fp8_dynamic")
+    with pytest.raises(ValueError, match="need a dense backend"):
+        fp8.activate(mode=HookMode.FUSED_PROGRESS_DENOISE, block_index=0, full_prefix=None)
+    # a fused forward needs two live documents
+    x = _layout(2, 0, False, seed=80)
+    hook.activate(mode=HookMode.FUSED_PROGRESS_DENOISE, block_index=0, full_prefix=None)
+    with pytest.raises(ValueError, match="target-document count differs"):
+        hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"], value=x["v"],
+             token_tags=x["tags"], commit_mask=x["commit"], cu_seqlens_host=x["cu"])
+    hook.deactivate()

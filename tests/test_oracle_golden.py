@@ -231,3 +231,52 @@ def test_commit_topk_matches_reference() -> None:
         assert selected == list(g[f"selected_{stage}"]), stage
     assert otopk.selected_count(5, 0.5) == 3 and otopk.selected_count(1, 0.1) == 1
     assert otopk.select_commits(np.array([1.0, 1.0, 0.5]), 0.5) == [0, 1]
+
+
+def run_hook_f_oracle():
+    """The FL2AV hook schedule of tests/golden/hook_f.npz through the oracle: per step the
+    output of one layer call, the commit counts and (for the capture) the kept rows."""
+
+    from inputs import HOOK_F_SCHEDULE, hook_f_inputs
+
+    from oracle.hook_f import FL2AVHookOracle
+
+    ora = FL2AVHookOracle(128 ** -0.5)
+    prefix = None
+    results = []
+    for step, (name, live, extra) in enumerate(HOOK_F_SCHEDULE):
+        x = hook_f_inputs(step, live)
+        q, k, v = (torch.from_numpy(x[n]) for n in ("q", "k", "v"))
+        kw = {}
+        mode = {"noisy_prefix": "noisy", "fused_recent": "fused"}.get(name, name)
+        if name == "capture":
+            kw["capture"] = (extra["video_rows"], extra["audio_rows_per_channel"])
+        if name in ("noisy_prefix", "fused_recent"):
+            kw["prefix"] = prefix
+        if name == "fused_recent":
+            ora.retain_sink_and_recent(len(ora.blocks), sink_video_only=True)
+            kw.update(previous_prefix=prefix, previous_video_only=True, use_sink=True,
+                      recent_blocks=extra["fused_current_recent_blocks"])
+        out, captured = ora.call(mode, q, k, v, x["token_tags"], x["cu_seqlens"], **kw)
+        if captured is not None:
+            prefix = captured
+        results.append((out, captured, [len(b[2]) for b in ora.blocks]))
+    return results
+
+
+def test_fl2av_hook_modes_match_reference() -> None:
+    """Every FL2AV hook mode (clean / progress commit, full-prefix capture, noisy over a
+    temporary prefix, fused progress-denoise with and without the recent / sink /
+    previous-video-only policy) restated in the oracle against the reference hook's own
+    outputs (tests/golden/hook_f.npz, bf16 SDPA on CPU): relative L2 <= 1e-2, identical commit
+    ledgers and captured rows."""
+
+    g = load("hook_f.npz")
+    for step, (out, captured, counts) in enumerate(run_hook_f_oracle()):
+        ref = torch.from_numpy(g[f"out_{step}"])
+        err = float((out - ref).norm() / ref.norm())
+        assert err <= 1e-2, (step, err)
+        assert counts == list(g[f"counts_{step}"]), step
+        if captured is not None:
+            assert torch.equal(captured[0].float(), torch.from_numpy(g["prefix_key"]))
+            assert torch.equal(captured[1].float(), torch.from_numpy(g["prefix_value"]))
