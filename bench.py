@@ -1049,6 +1049,158 @@ def run_h3sa(args: argparse.Namespace) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_tp2sp4(args: argparse.Namespace) -> None:
+    """The 1080p FP8 configuration in its TP2 x SP4 layout on 8 GPUs (T/runtime/direct.py:
+    169-190): TP rank t owns 12 of the 24 heads; its Ulysses group {t, t+2, t+4, t+6} trades
+    sequence rows for heads, 3 heads per GPU. Per step and rank: the fused prologue stores Q
+    into the owners' planes and K/V into the owners' bf16 chunk pools over NVLink; a peer
+    barrier; the chunk's K/V rows become one e4m3 part (its own per-head scales) after the
+    four history parts quantised at their commits; Q is quantised per head; one attention
+    launch over the parts (the 35-row pad document attends to itself in bf16); the output
+    all-to-all inside the group (NCCL) and its unpack. Timed with CUDA events, max over the
+    8 ranks. FLOPs: 4 * Nq * (Nh + Nq) * 128 per head."""
+
+    import h3sa
+    from h3sa.kernels import PAGE_ROWS, attention_fwd_fp8_parts, quantize_fp8_rows
+    from h3sa.peer import PeerBarrier, PeerBuffer
+    from h3sa.prologue import qkv_norm_rope_scatter_paged
+    from h3sa.ulysses import build_parallel_context, unpack_o_recv
+
+    world, rank, local = _dist()
+    if world != 8:
+        raise SystemExit("--layout tp2sp4 runs on 8 GPUs (torchrun --nproc-per-node 8)")
+    dev = torch.device("cuda", local)
+    ctx = build_parallel_context(2, 4)
+    group, sp, ur = ctx.ulysses_group, ctx.ulysses_world_size, ctx.ulysses_rank
+    d, heads_tp, nh, nq = 128, 12, 32768, 24480 + 125
+    hl = heads_tp // sp
+    align = 64 * sp // _gcd(64, sp)
+    rows = (nq + align - 1) // align * align
+    tokens = rows // sp
+    g = torch.Generator(device=dev).manual_seed(2000 + rank)
+    merged = torch.randn(tokens, 3 * heads_tp * d, device=dev, generator=g).to(torch.bfloat16)
+    gw = torch.Generator(device=dev).manual_seed(99)
+    wq = (1 + 0.05 * torch.randn(d, device=dev, generator=gw)).to(torch.bfloat16)
+    wk = (1 + 0.05 * torch.randn(d, device=dev, generator=gw)).to(torch.bfloat16)
+    cos_sin = _rope_cache(nh + rows, 96, dev)
+    positions = nh + ur * tokens + torch.arange(tokens, device=dev)
+    pages = rows // PAGE_ROWS + 1
+    table = torch.arange(pages, dtype=torch.int32, device=dev)
+    q_buf = PeerBuffer((rows, hl, d), group)
+    k_buf = PeerBuffer((hl, pages * PAGE_ROWS, d), group)
+    v_buf = PeerBuffer((hl, pages * PAGE_ROWS, d), group)
+    k_buf.tensor.zero_()
+    v_buf.tensor.zero_()
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    peer_barrier = PeerBarrier(group, device_error=err)
+    # e4m3 store: four committed history parts of nh / 4 rows, then the chunk's part
+    parts = [nh // 4] * 4 + [nq]
+    starts, cursor = [], 0
+    for n in parts:
+        starts.append(cursor)
+        cursor = (cursor + n + PAGE_ROWS - 1) // PAGE_ROWS * PAGE_ROWS
+    t8 = torch.arange(cursor // PAGE_ROWS, dtype=torch.int32, device=dev)
+    k8 = torch.zeros(hl, cursor, d, dtype=torch.float8_e4m3fn, device=dev)
+    v8 = torch.zeros_like(k8)
+    ks = torch.empty(len(parts), hl, dtype=torch.float32, device=dev)
+    vs = torch.empty_like(ks)
+    work = torch.empty(2 * hl, dtype=torch.int32, device=dev)
+    block_part = torch.zeros(cursor // PAGE_ROWS, dtype=torch.int32)
+    for i, (s0, n) in enumerate(zip(starts, parts)):
+        for b in range(s0 // PAGE_ROWS, (s0 + n + PAGE_ROWS - 1) // PAGE_ROWS):
+            block_part[b] = i | (min(PAGE_ROWS, s0 + n - b * PAGE_ROWS) << 16)
+    block_part = block_part.to(dev)
+    for i in range(4):
+        hk = torch.randn(parts[i], hl, d, device=dev, generator=g).to(torch.bfloat16)
+        hv = torch.randn(parts[i], hl, d, device=dev, generator=g).to(torch.bfloat16)
+        quantize_fp8_rows([hk, hv], [k8, v8], [ks[i], vs[i]], work, count=parts[i],
+                          dst_start=starts[i], dst_table=t8, zero_tail=True)
+    out = torch.empty(rows, hl, d, dtype=torch.bfloat16, device=dev)
+    orecv = torch.empty(sp, tokens, hl, d, dtype=torch.bfloat16, device=dev)
+    final = torch.empty(tokens, heads_tp, d, dtype=torch.bfloat16, device=dev)
+    P = h3sa.AttentionProblem
+    scale = d ** -0.5
+    phases = ("prologue_scatter", "barrier", "kv_part_quant", "q_quant", "attention",
+              "o_all_to_all", "o_unpack")
+
+    def step(marks=None) -> None:
+        def mark(i):
+            if marks is not None:
+                marks[i].record()
+
+        mark(0)
+        qkv_norm_rope_scatter_paged(merged, wq, wk, cos_sin, positions, 1e-5, q=q_buf,
+                                    key_pool=k_buf, value_pool=v_buf, page_table=table,
+                                    dst_start=0, device_error=err)
+        mark(1)
+        peer_barrier()
+        mark(2)
+        quantize_fp8_rows([k_buf.tensor, v_buf.tensor], [k8, v8], [ks[4], vs[4]], work,
+                          count=nq, src_table=table, dst_start=starts[4], dst_table=t8,
+                          zero_tail=True)
+        mark(3)
+        q8, qs = h3sa.quantize_fp8_e4m3_per_head(q_buf.tensor[:nq].unsqueeze(0))
+        mark(4)
+        attention_fwd_fp8_parts(q8[0], out, k8, v8, t8, [P(0, nq, 0, starts[4] + nq)], scale,
+                                q_scale=qs[0], block_part=block_part, part_k_scale=ks,
+                                part_v_scale=vs, device_error=err)
+        h3sa.attention_fwd(q_buf.tensor, out, k_buf.tensor, v_buf.tensor, table,
+                           [P(nq, rows, nq, rows)], scale, device_error=err)
+        mark(5)
+        torch.distributed.all_to_all_single(orecv, out, group=group)
+        mark(6)
+        unpack_o_recv(orecv, final, world=sp, tokens=tokens, local_heads=hl, head_dim=d)
+        mark(7)
+        # no barrier before the next step's scatter into the peers' planes and pools: a rank
+        # finishes its all-to-all only after every peer has sent, i.e. finished its attention
+
+    for _ in range(args.warmup):
+        step()
+    t0, t1 = torch.cuda.Event(True), torch.cuda.Event(True)
+    per = [[torch.cuda.Event(True) for _ in range(len(phases) + 1)] for _ in range(args.steps)]
+    with ClockSampler(local) as clocks:
+        _barrier(world)
+        clocks.mark_start()
+        t0.record()
+        for i in range(args.steps):
+            step(per[i])
+        t1.record()
+        _barrier(world)
+        clocks.mark_stop()
+    ms = _max_over_ranks(t0.elapsed_time(t1) / args.steps, world)
+    phase_ms = {}
+    for j, name in enumerate(phases):
+        vals = sorted(per[i][j].elapsed_time(per[i][j + 1]) for i in range(args.steps))
+        phase_ms[name] = _max_over_ranks(vals[len(vals) // 2], world)
+    code = int(err.item())
+    flops_gpu = 4.0 * nq * (nh + nq) * d * hl
+    peaks = _peaks()
+    attn_tf = flops_gpu / (phase_ms["attention"] * 1e-3) / 1e12
+    for b in (q_buf, k_buf, v_buf):
+        b.close()
+    peer_barrier.close()
+    if rank == 0:
+        line = {
+            "metric": "chunk attention TFLOP/s (1080p FP8 e4m3, TP2 x SP4, 32k KV cache)",
+            "value": flops_gpu * world / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "e4m3",
+            "data": "synthetic",
+            "config": {"workload": "1080p FP8 chunk: 24480 video + 125 audio queries x [32768 "
+                                   "history (4 e4m3 parts) + 24605 current] keys, 24 heads",
+                       "parallelism": "tp2sp4", "heads_per_gpu": hl, "packed_rows": rows},
+            "per_gpu_tflops": flops_gpu / (ms * 1e-3) / 1e12,
+            "phases_p50_max_over_ranks_ms": phase_ms,
+            "attention_tflops_per_gpu": attn_tf,
+            "roofline": {"bound": "tensor", "peak": 2 * peaks["bf16"],
+                         "frac": attn_tf / (2 * peaks["bf16"]),
+                         "peak_source": "2 x measured bf16 burst (no measured e4m3 GEMM peak)"},
+            "clocks": clocks.summary(),
+            "device_error": code,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1062,6 +1214,8 @@ def main() -> None:
                     help="SP > 1: NCCL all-to-all + layout copies instead of peer stores")
     ap.add_argument("--no-variants", action="store_true",
                     help="skip the kernel-only FP8 1080p, block-sparse 768p and 480p timings")
+    ap.add_argument("--layout", choices=["sp", "tp2sp4"], default="sp",
+                    help="tp2sp4: the 1080p FP8 configuration in its TP2 x SP4 layout (8 GPUs)")
     ap.add_argument("--variant", choices=VARIANTS,
                     help="time only this kernel-only variant on one GPU and print its JSON "
                          "(2 warm-up launches, then --steps launches)")
@@ -1074,6 +1228,8 @@ def main() -> None:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.layout == "tp2sp4":
+        run_tp2sp4(args)
     else:
         run_h3sa(args)
     if torch.distributed.is_initialized():

@@ -46,6 +46,29 @@ class ParallelContext:
             raise ValueError("TP and Ulysses process groups are required")
 
 
+def build_parallel_context(tp_size: int, ulysses_degree: int, *,
+                           backend: str | None = None) -> ParallelContext:
+    """This rank's view of a TP x Ulysses layout over the whole world, built as the reference
+    runtime builds it (T/runtime/direct.py:169-190): global rank = ulysses_rank * tp_size +
+    tp_rank; TP groups are runs of ``tp_size`` consecutive ranks, Ulysses group t holds the
+    ranks t, t + tp_size, t + 2 * tp_size, ... (e.g. {t, t+2, t+4, t+6} for TP2 x SP4).
+    Collective: every rank creates every group, in the same order."""
+
+    dist = torch.distributed
+    world = dist.get_world_size()
+    if tp_size <= 0 or ulysses_degree <= 0 or tp_size * ulysses_degree != world:
+        raise ValueError(f"TP {tp_size} x Ulysses {ulysses_degree} does not cover world {world}")
+    rank = dist.get_rank()
+    tp_groups = [dist.new_group(ranks=[u * tp_size + t for t in range(tp_size)], backend=backend)
+                 for u in range(ulysses_degree)]
+    ulysses_groups = [dist.new_group(ranks=[u * tp_size + t for u in range(ulysses_degree)],
+                                     backend=backend)
+                      for t in range(tp_size)]
+    return ParallelContext(tp_world_size=tp_size, tp_rank=rank % tp_size,
+                           ulysses_world_size=ulysses_degree, ulysses_rank=rank // tp_size,
+                           tp_group=tp_groups[rank // tp_size],
+                           ulysses_group=ulysses_groups[rank % tp_size])
+
 def _require_dist(context: ParallelContext) -> None:
     if not torch.distributed.is_available() or not torch.distributed.is_initialized():
         raise RuntimeError("Ulysses all-to-all requires initialized torch.distributed")
@@ -223,6 +246,7 @@ def merged_qkv_sequence_to_heads(value: torch.Tensor, *, num_heads: int, head_di
 
 __all__ = [
     "ParallelContext",
+    "build_parallel_context",
     "heads_to_sequence",
     "merged_qkv_sequence_to_heads",
     "packed_qkv_sequence_to_heads",
