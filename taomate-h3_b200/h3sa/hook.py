@@ -569,7 +569,13 @@ class H3StreamingAttentionHook:
         n_kv_media = regions[0][3]
         self._launch(layer_name, paged, q_src, out_main, problems, scale, n_kv_media, n_hist,
                      plan, err, exchange)
-        if other_kv:
+        if other_kv and self.backend in FP8_BACKENDS:
+            # every other document is its own one-part e4m3 call in the reference's FP8 backends
+            for a, b, c in other_kv:
+                self._fp8_condition(paged, query, out, AttentionProblem(a, b, c, c + (b - a)),
+                                    scale, err)
+                self.launches += 1
+        elif other_kv:
             probs = [AttentionProblem(a, b, c, c + (b - a)) for a, b, c in other_kv]
             for i in range(0, len(probs), _lib.MAX_PROBLEMS):
                 chunk = probs[i:i + _lib.MAX_PROBLEMS]
@@ -669,9 +675,7 @@ class H3StreamingAttentionHook:
                       scale, q_scale=q_scale.reshape(-1).contiguous(), k_scale=k_scale,
                       v_scale=v_scale, device_error=err)
         out[media.q_lo:media.q_hi].copy_(out_media)
-        # condition rows attend to condition K/V only; that tiny call stays in bf16
-        attention_fwd(q_src, out, paged.key, paged.value, paged.table, [cond], scale,
-                      device_error=err)
+        self._fp8_condition(paged, q_src, out, cond, scale, err)
         self.launches += 2
 
 
@@ -722,10 +726,34 @@ class H3StreamingAttentionHook:
                                 block_part=block_part, part_k_scale=ks, part_v_scale=vs,
                                 device_error=err)
         out[media.q_lo:media.q_hi].copy_(out_media)
-        # condition rows attend to condition K/V only; that small call stays in bf16
-        attention_fwd(q_src, out, paged.key, paged.value, paged.table, [cond], scale,
-                      device_error=err)
+        self._fp8_condition(paged, q_src, out, cond, scale, err)
         self.launches += 2
+
+    def _fp8_condition(self, paged, q_src: torch.Tensor, out: torch.Tensor,
+                       cond: AttentionProblem, scale: float, err: torch.Tensor) -> None:
+        """A one-part call (the condition rows, or another document) in e4m3, as the
+        reference's FP8 backends run it (F/streaming/attention_hook.py:1081-1107): the rows'
+        Q, K and V quantised per head over those rows alone, one attention launch."""
+
+        from .kernels import quantize_fp8_rows
+
+        n_kv, n_q = cond.kv_hi - cond.kv_lo, cond.q_hi - cond.q_lo
+        heads, dim, dev = paged.heads, paged.head_dim, q_src.device
+        pad = (n_kv + PAGE_ROWS - 1) // PAGE_ROWS * PAGE_ROWS
+        k8 = torch.empty(heads, pad, dim, dtype=torch.float8_e4m3fn, device=dev)
+        v8 = torch.empty_like(k8)
+        table = torch.arange(pad // PAGE_ROWS, dtype=torch.int32, device=dev)
+        kv_scale = torch.empty(2, heads, dtype=torch.float32, device=dev)
+        work = torch.empty(2 * heads, dtype=torch.int32, device=dev)
+        quantize_fp8_rows([paged.key, paged.value], [k8, v8], [kv_scale[0], kv_scale[1]], work,
+                          count=n_kv, src_start=cond.kv_lo, src_table=paged.table,
+                          dst_table=table, zero_tail=True, device_error=err)
+        q8, q_scale = quantize_fp8_e4m3_per_head(q_src[cond.q_lo:cond.q_hi].unsqueeze(0))
+        o = torch.empty(n_q, heads, dim, dtype=torch.bfloat16, device=dev)
+        attention_fwd(q8.squeeze(0), o, k8, v8, table, [AttentionProblem(0, n_q, 0, n_kv)], scale,
+                      q_scale=q_scale.reshape(-1).contiguous(), k_scale=kv_scale[0],
+                      v_scale=kv_scale[1], device_error=err)
+        out[cond.q_lo:cond.q_hi].copy_(o)
 
     def _select_commits(self, seg, q_src: torch.Tensor, media: AttentionProblem,
                         err: torch.Tensor) -> list[int] | None:

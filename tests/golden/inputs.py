@@ -92,3 +92,16 @@ def hook_f_inputs(step: int, live: int, heads: int = 2, head_dim: int = 128) -> 
     cu = [0] + [64 * (i + 1) for i in range(live)] + [n]
     return {"q": q, "k": k, "v": v, "token_tags": tags, "commit_mask": (tags == 0) | (tags == 2),
             "cu_seqlens": cu, "scale": head_dim ** -0.5}
+
+
+def hook_topk_inputs(step: int, heads: int = 2, head_dim: int = 128) -> dict:
+    """One call of the commit-level top-k schedule: hook_f_inputs' single-document layout
+    with K (commit steps) or Q (the final call) shifted by a per-step offset row, so the
+    blocks' key summaries score clearly apart against the media queries."""
+
+    x = hook_f_inputs(100 + step, 1, heads, head_dim)
+    rng = np.random.default_rng(2000 + step)
+    offset = 0.5 * rng.standard_normal((1, heads, head_dim)).astype(np.float32)
+    x["k"] = bf16(x["k"] + offset)
+    x["q"] = bf16(x["q"] + offset)
+    return x

@@ -34,6 +34,11 @@ them from the seeds recorded in each fixture. Fixtures:
                  noisy call; layer 0's outputs, the captured prefix and the commit ledger. The
                  hook insists on CUDA tensors: CPU tensors of a subclass that reports is_cuda
                  stand in, and the K/V pair validators are stubbed.
+* hook_topk.npz  the FL2AV hook with its flash_attn3_fp8_segmented_topk backend at density
+                 0.5 over four clean commits, then a noisy call (layer 0 outputs of every
+                 step): FlashAttention-3's FP8 call is replaced by exact attention on the
+                 dequantised e4m3 inputs plus its log-sum-exp, so the reference's own
+                 quantisation, commit-level selection and LSE merge run as written.
 * topk.npz       key summaries of the FL2AV segmented-FP8 CleanAVKVCache
                  (F/streaming/cache.py:836-855) over six commits and after a sink + recent
                  retention, with the commit-level top-k selection of the segmented top-k
@@ -64,11 +69,21 @@ def _import_reference():
 
     stub = types.ModuleType("flash_attn_interface")
 
-    def flash_attn_func(q, k, v, softmax_scale=None, causal=False, num_splits=1):
-        o = torch.nn.functional.scaled_dot_product_attention(
-            q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=softmax_scale,
-            is_causal=causal)
-        return o.transpose(1, 2)
+    def flash_attn_func(q, k, v, softmax_scale=None, causal=False, num_splits=1,
+                        q_descale=None, k_descale=None, v_descale=None):
+        if q_descale is None:
+            o = torch.nn.functional.scaled_dot_product_attention(
+                q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), scale=softmax_scale,
+                is_causal=causal)
+            return o.transpose(1, 2)
+        # FP8 form: e4m3 [B, S, H, D] inputs with fp32 [B, H] descales; exact attention on the
+        # dequantised values, returned with its log-sum-exp [B, H, S] as FA3 does
+        deq = lambda x, s: torch.Tensor(x).float() * torch.Tensor(s).float()[:, None, :, None]  # noqa: E731
+        qf, kf, vf = deq(q, q_descale), deq(k, k_descale), deq(v, v_descale)
+        scores = torch.einsum("bqhd,bkhd->bhqk", qf, kf) * softmax_scale
+        lse = torch.logsumexp(scores, dim=-1)
+        o = torch.einsum("bhqk,bkhd->bqhd", torch.softmax(scores, dim=-1), vf)
+        return o.to(torch.bfloat16), lse
 
     stub.flash_attn_func = flash_attn_func
     sys.modules["flash_attn_interface"] = stub
@@ -401,6 +416,51 @@ def make_hook_f(path: Path) -> None:
         arrays[f"blocks_{step}"] = np.array(cache.committed_blocks)
     np.savez_compressed(path, **arrays)
 
+def make_hook_topk(path: Path) -> None:
+    import torch
+    import digitalhuman_h3.streaming.attention_hook as fhook
+    import digitalhuman_h3.streaming.cache as fcache
+    from inputs import hook_topk_inputs
+
+    fcache._validate_av_pair = lambda pair, contract, *, layer: None
+
+    class CudaFlagged(torch.Tensor):
+        @property
+        def is_cuda(self):
+            return True
+
+    def t(x: np.ndarray, dtype=torch.bfloat16):
+        return torch.from_numpy(x).to(dtype).as_subclass(CudaFlagged)
+
+    class Attn:
+        softmax_scale = 128 ** -0.5
+
+    contract = fcache.KVContract(local_heads=2, head_dim=128)
+    cache = fcache.CleanAVKVCache(contract, segmented_fp8_history=True)
+    hook = fhook.H3StreamingAttentionHook(cache, attention_backend="flash_attn3_fp8_segmented_topk",
+                                          history_kv_dynamic_density=0.5)
+    arrays: dict[str, np.ndarray] = {}
+    for step in range(5):
+        x = hook_topk_inputs(step)
+        commit = step < 4
+        if commit:
+            cache.begin_clean_commit(cache.committed_blocks)
+        mode = fhook.HookMode.CLEAN_COMMIT if commit else fhook.HookMode.NOISY
+        hook.activate(mode=mode, block_index=cache.committed_blocks, full_prefix=None)
+        q, k, v = t(x["q"]), t(x["k"]), t(x["v"])
+        tags, mask = t(x["token_tags"], torch.int64), t(x["commit_mask"], torch.bool)
+        for layer in contract.layer_names:
+            out = hook(attention=Attn(), layer_name=layer, query=q, key=k, value=v,
+                       token_tags=tags, commit_mask=mask, cu_seqlens=None,
+                       cu_seqlens_host=tuple(x["cu_seqlens"]), max_seqlen=64)
+            if layer == contract.layer_names[0]:
+                arrays[f"out_{step}"] = torch.Tensor(out).float().numpy()
+        hook.deactivate()
+        if commit:
+            cache.commit()
+        arrays[f"selected_blocks_{step}"] = np.array(hook.dynamic_block_sparse_selected_blocks)
+    np.savez_compressed(path, **arrays)
+
 # ----------------------------------------------------------------------------- ulysses
 def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import datetime
@@ -493,7 +553,8 @@ def main() -> None:
     makers = {"prologue.npz": make_prologue, "hook_cpu.npz": make_hook, "fp8.npz": make_fp8,
               "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
               "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f,
-              "topk.npz": make_topk, "hook_f.npz": make_hook_f}
+              "topk.npz": make_topk, "hook_f.npz": make_hook_f,
+              "hook_topk.npz": make_hook_topk}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

@@ -183,8 +183,10 @@ def test_hook_fp8_dynamic_matches_dequantised_oracle() -> None:
     ref_media = oatt.attention(deq(x["q"][media])[0].cpu(), deq(k_all)[0].cpu(), deq(v_all)[0].cpu(),
                                Attn.softmax_scale)
     assert rel_l2(out[16:304], ref_media) <= FP8_TOL
-    full = _oracle(x)
-    assert rel_l2(out[:16], full[:16]) <= BF16_TOL
+    # condition rows: their own e4m3 call over the condition rows' Q/K/V
+    ref_cond = oatt.attention(deq(x["q"][cond])[0].cpu(), deq(x["k"][cond])[0].cpu(),
+                              deq(x["v"][cond])[0].cpu(), Attn.softmax_scale)
+    assert rel_l2(out[:16], ref_cond) <= FP8_TOL
 
 
 def test_hook_block_sparse_matches_masked_oracle() -> None:
@@ -295,10 +297,10 @@ def test_hook_fp8_segmented_history_matches_merged_oracle() -> None:
                                        [(ck8, cv8, cks, cvs), *parts, (mk8, mv8, mks, mvs)],
                                        Attn.softmax_scale)
     assert rel_l2(out[16:304], ref) <= FP8_TOL
-    # condition rows see condition K/V only (bf16)
-    ref_cond = oatt.attention(y["q"][cond].float().cpu(), y["k"][cond].float().cpu(),
-                              y["v"][cond].float().cpu(), Attn.softmax_scale)
-    assert rel_l2(out[:16], ref_cond) <= BF16_TOL
+    # condition rows see condition K/V only, in their own e4m3 call
+    ref_cond = oatt.segmented_fp8_attention(y["q"][cond].float().cpu(), [(ck8, cv8, cks, cvs)],
+                                            Attn.softmax_scale)
+    assert rel_l2(out[:16], ref_cond) <= FP8_TOL
 
 
 def test_fl2av_cache_schedule_matches_reference_golden() -> None:
@@ -633,3 +635,46 @@ def test_fl2av_activation_checks_match_reference() -> None:
         hook(attention=Attn(), layer_name="blocks.0.attn", query=x["q"], key=x["k"], value=x["v"],
              token_tags=x["tags"], commit_mask=x["commit"], cu_seqlens_host=x["cu"])
     hook.deactivate()
+
+
+def test_hook_fp8_segmented_topk_matches_reference_hook_golden() -> None:
+    """The top-k segmented backend against the reference FL2AV hook itself
+    (tests/golden/hook_topk.npz: its own e4m3 quantisation, commit-level selection at density
+    0.5 and LSE merge, FlashAttention-3's FP8 call replaced by exact attention on the
+    dequantised inputs) over four clean commits and a noisy call: every step's layer-0 output
+    within the FP8 tolerance, selection counters equal."""
+
+    sys.path.insert(0, str(GOLDEN))
+    from inputs import hook_topk_inputs
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    g = np.load(GOLDEN / "hook_topk.npz")
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128), segmented_fp8_history=True)
+    hook = H3StreamingAttentionHook(cache, attention_backend="flash_attn3_fp8_segmented_topk",
+                                    history_kv_dynamic_density=0.5)
+    t = lambda a, dt=torch.bfloat16: torch.from_numpy(a).to(dt).cuda()  # noqa: E731
+    for step in range(5):
+        x = hook_topk_inputs(step)
+        commit = step < 4
+        if commit:
+            cache.begin_clean_commit(cache.committed_blocks)
+        hook.activate(mode=HookMode.CLEAN_COMMIT if commit else HookMode.NOISY,
+                      block_index=cache.committed_blocks, full_prefix=None)
+        q, k, v = t(x["q"]), t(x["k"]), t(x["v"])
+        tags, mask = t(x["token_tags"], torch.int64), t(x["commit_mask"], torch.bool)
+        for layer in cache.layer_names:
+            out = hook(attention=Attn(), layer_name=layer, query=q, key=k, value=v,
+                       token_tags=tags, commit_mask=mask, cu_seqlens=None,
+                       cu_seqlens_host=tuple(x["cu_seqlens"]), max_seqlen=64)
+            if layer == cache.layer_names[0]:
+                first = out
+        hook.deactivate()
+        hook.check_device_error()
+        if commit:
+            cache.commit()
+        ref = torch.from_numpy(g[f"out_{step}"])
+        assert rel_l2(first[:64], ref[:64]) <= FP8_TOL, step          # the live document
+        assert rel_l2(first[64:], ref[64:]) <= FP8_TOL, step          # the pad document
+        assert hook.dynamic_block_sparse_selected_blocks == int(g[f"selected_blocks_{step}"])
