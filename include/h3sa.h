@@ -226,6 +226,25 @@ H3SA_API int h3sa_segment_row_means(const h3sa_rows* src, const int32_t* segment
 H3SA_API int h3sa_commit_scores(const float* summaries, const float* query_mean,
                                 int32_t num_parts, int32_t heads, double* scores, void* stream);
 
+/* W8A8 projection GEMM (tcgen05 kind::i8, int32 accumulation in TMEM):
+ * out[m, n] = bf16_rn(a_scale[m] * (b_scale[n] * float(sum_k a[m, k] * b[n, k])))
+ * a: int8 [m, k] activations, b: int8 [n, k] weights (both row-major, K contiguous);
+ * a_scale fp32 [m], b_scale fp32 [n]; out bf16 [m, ldo]. k a multiple of 16, n and ldo of 8,
+ * every pointer 16-byte aligned. Replaces vLLM's cutlass_scaled_mm under the reference's W8A8
+ * QKV / FC1 projection (T/inference/w8a8.py:190-221). */
+H3SA_API int h3sa_w8a8_gemm(const void* a, const float* a_scale, const void* b,
+                            const float* b_scale, void* out, int32_t m, int32_t n, int32_t k,
+                            int32_t ldo, int32_t* device_error, void* stream);
+
+/* Per-row int8 quantisation of bf16 rows x [rows, cols] into q int8 [rows, cols] and scale fp32
+ * [rows] (cols a multiple of 8). mode 0 (activations, dynamic per token):
+ * scale = amax / 127, q = clamp(rint(x * (127 / amax)), -128, 127), zero rows give zeros;
+ * mode 1 (weights): scale = max(amax / 127, 1e-12), q = clamp(rint(x / scale), -127, 127).
+ * Replaces scaled_int8_quant of the W8A8 input and _quantize_weight
+ * (T/inference/w8a8.py:56-63, 190-221). */
+H3SA_API int h3sa_quantize_int8_rows(const void* x, void* q, float* scale, int32_t rows,
+                                     int32_t cols, int32_t mode, void* stream);
+
 /* Generic layout permute of 16-byte-aligned records: for every index (i0, i1, i2, i3) of
  * the row-major space dims[4], copy row_bytes from src + sum(i_k * src_strides[k]) to
  * dst + sum(i_k * dst_strides[k]) (strides in bytes, multiples of 16). Serves the Ulysses

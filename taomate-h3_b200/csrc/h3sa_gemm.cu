@@ -1,0 +1,361 @@
+// W8A8 projection GEMM on the sm_100a tensor cores: out[M, N] (bf16) =
+//   a_scale[m] * (b_scale[n] * float(sum_k A[m, k] * B[n, k]))
+// with A int8 [M, K] (activations, one scale per token row) and B int8 [N, K] (weights, one
+// scale per output row), both K-major. This is the arithmetic of the reference's QKV / FC1
+// projection (T/inference/w8a8.py:190-221: dynamic per-token int8 activations, per-row int8
+// weights, CUTLASS scaled_mm into bf16), written for tcgen05:
+//
+// * persistent CTAs, one per SM, walking 128 x 256 output tiles;
+// * warp 0 streams A and B K-slices (128 bytes of K per row, 128-byte swizzle) by TMA into a
+//   4-stage shared-memory ring;
+// * warp 1 issues tcgen05.mma kind::i8 (M 128, N 256, K 32 per instruction) into one of two
+//   TMEM accumulators (2 x 256 int32 columns), so the epilogue of one tile overlaps the MMAs
+//   of the next;
+// * warps 2-5 (one per TMEM lane quadrant) read the int32 accumulators, scale them in the
+//   order above and store bf16 rows.
+//
+// Every wait is bounded (h3sa_ptx.cuh); a wait that gives up records kErrWaitTimeout in the
+// error word and the CTA unwinds.
+#include "h3sa_host.h"
+#include "h3sa_ptx.cuh"
+
+#include <mutex>
+
+namespace h3sa {
+namespace {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBN = 256;
+constexpr int kGemmBK = 128;  // bytes of K per stage (one 128-byte swizzle atom)
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr int kGemmUmmaK = 32;  // int8 K per tcgen05.mma
+constexpr uint32_t kGemmATile = kGemmBM * kGemmBK;  // 16 KB
+constexpr uint32_t kGemmBTile = kGemmBN * kGemmBK;  // 32 KB
+
+struct GemmSmem {
+  uint8_t a[kGemmStages][kGemmATile];  // 1024-byte aligned (tile sizes are multiples)
+  uint8_t b[kGemmStages][kGemmBTile];
+  float b_scale[2][kGemmBN];
+  uint64_t full[kGemmStages];
+  uint64_t empty[kGemmStages];
+  uint64_t acc_full[2];
+  uint64_t acc_empty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+constexpr size_t gemm_smem_bytes() { return sizeof(GemmSmem) + 1024; }
+static_assert(gemm_smem_bytes() <= 232448, "W8A8 GEMM needs more than 227 KB of shared memory");
+
+struct GemmParams {
+  const float* a_scale;  // [M]
+  const float* b_scale;  // [N]
+  __nv_bfloat16* out;    // [M, ldo]
+  int m, n, k;
+  int ldo;
+  int tiles_n, tiles;
+  int* err;
+};
+
+// kind::i8, int32 accumulation, signed A and B, both K-major.
+constexpr uint32_t idesc_s8(int m, int n) {
+  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_ss_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred e, p;\n\t" H3SA_ELECT_PRED
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int* abort_flag = &sm.abort_flag;
+  const int k_steps = (p.k + kGemmBK - 1) / kGemmBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(smem_u32(&sm.full[s]), 1);
+      mbar_init(smem_u32(&sm.empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&sm.acc_full[b]), 1);
+      mbar_init(smem_u32(&sm.acc_empty[b]), 4);  // one arrival per epilogue warp
+    }
+    sm.abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = sm.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < p.tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile / p.tiles_n) * kGemmBM;
+        const int n0 = (tile % p.tiles_n) * kGemmBN;
+        for (int ks = 0; ks < k_steps; ++ks, ++it) {
+          const int s = it % kGemmStages;
+          if (!mbar_wait(smem_u32(&sm.empty[s]), ((it / kGemmStages) & 1) ^ 1, abort_flag, p.err))
+            break;
+          const uint32_t full = smem_u32(&sm.full[s]);
+          mbar_expect_tx(full, kGemmATile + kGemmBTile);
+          tma_load_3d(smem_u32(sm.a[s]), &tmA, full, ks * kGemmBK, m0, 0);
+          tma_load_3d(smem_u32(sm.b[s]), &tmB, full, ks * kGemmBK, n0, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (whole warp)
+    constexpr uint32_t idesc = idesc_s8(kGemmBM, kGemmBN);
+    uint32_t it = 0;
+    int j = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++j) {
+      const int buf = j & 1;
+      if (!mbar_wait(smem_u32(&sm.acc_empty[buf]), ((j >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+      tc_fence_after();
+      const uint32_t d_tmem = tbase + static_cast<uint32_t>(buf * kGemmBN);
+      bool ok = true;
+      for (int ks = 0; ks < k_steps; ++ks, ++it) {
+        const int s = it % kGemmStages;
+        if (!(ok = mbar_wait(smem_u32(&sm.full[s]), (it / kGemmStages) & 1, abort_flag, p.err)))
+          break;
+        tc_fence_after();
+        const uint32_t a_lo = sdesc_lo(smem_u32(sm.a[s]), 16);
+        const uint32_t b_lo = sdesc_lo(smem_u32(sm.b[s]), 16);
+#pragma unroll
+        for (int kk = 0; kk < kGemmBK / kGemmUmmaK; ++kk) {
+          // K advance inside the swizzle atom: 32 bytes = 2 in the address field
+          mma_ss_i8(d_tmem, sdesc_join(a_lo + 2 * kk), sdesc_join(b_lo + 2 * kk), idesc,
+                    (ks | kk) != 0);
+        }
+        tc_commit(smem_u32(&sm.empty[s]));  // the stage is free once these MMAs completed
+      }
+      if (!ok) break;
+      tc_commit(smem_u32(&sm.acc_full[buf]));
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue warps 2..5
+    const int quad = warp & 3;  // TMEM lanes 32 * quad .. 32 * quad + 31
+    const int ep_thread = threadIdx.x - 64;  // 0..127
+    int j = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++j) {
+      const int buf = j & 1;
+      const int m0 = (tile / p.tiles_n) * kGemmBM;
+      const int n0 = (tile % p.tiles_n) * kGemmBN;
+      // this tile's column scales into shared memory (the previous tile of this buffer is done)
+      for (int c = ep_thread; c < kGemmBN; c += 128)
+        sm.b_scale[buf][c] = n0 + c < p.n ? __ldg(p.b_scale + n0 + c) : 0.f;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!mbar_wait(smem_u32(&sm.acc_full[buf]), (j >> 1) & 1, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = m0 + quad * 32 + lane;
+      const float a_s = row < p.m ? __ldg(p.a_scale + row) : 0.f;
+      __nv_bfloat16* orow = p.out + static_cast<size_t>(row) * p.ldo + n0;
+      const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
+                             static_cast<uint32_t>(buf * kGemmBN);
+#pragma unroll 1
+      for (int c = 0; c < kGemmBN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+        tmem_wait_ld();
+        reg_fence32(r);
+        if (row < p.m && n0 + c < p.n) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float x0 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i],
+                                                      __int2float_rn(static_cast<int>(r[2 * i]))));
+            const float x1 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i + 1],
+                                                      __int2float_rn(static_cast<int>(r[2 * i + 1]))));
+            w[i] = pack_bf16x2(x0, x1);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+          if (n0 + c + 32 <= p.n) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          } else {  // ragged last columns: 8-column groups (n is a multiple of 8)
+            for (int q = 0; q < 4 && n0 + c + 8 * q < p.n; ++q)
+              dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.acc_empty[buf]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 512);
+  }
+}
+
+// Per-row int8 quantisation of bf16 rows [rows, cols], one CTA per row:
+// mode 0, the activations (dynamic per-token, as vLLM's dynamic_scaled_int8_quant):
+//   scale = amax / 127, q = clamp(rint(x * (127 / amax)), -128, 127); an all-zero row gives
+//   scale 0 and zeros;
+// mode 1, the weights (T/inference/w8a8.py:56-63):
+//   scale = max(amax / 127, 1e-12), q = clamp(rint(x / scale), -127, 127).
+// rint rounds half to even in both.
+__global__ void __launch_bounds__(256) quantize_int8_rows_kernel(
+    const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scale,
+    int cols, int mode) {
+  const size_t row = blockIdx.x;
+  const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
+  const int chunks = cols / 8;
+  float m = 0.f;
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    const uint4 v = __ldg(src + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      m = fmaxf(m, fabsf(__uint_as_float(w[i] << 16)));
+      m = fmaxf(m, fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  __shared__ float red[8];
+  __shared__ float row_scale, row_mul;
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float amax = red[0];
+    for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+    if (mode == 0) {
+      row_scale = __fdiv_rn(amax, 127.f);
+      row_mul = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
+    } else {
+      row_scale = fmaxf(__fdiv_rn(amax, 127.f), 1.0e-12f);
+      row_mul = 0.f;
+    }
+    scale[row] = row_scale;
+  }
+  __syncthreads();
+  const float sc = row_scale, mul = row_mul;
+  const float lo = mode == 0 ? -128.f : -127.f;
+  uint2* dst = reinterpret_cast<uint2*>(q + row * cols);
+  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
+    const uint4 v = __ldg(src + c);
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+    uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float f = __uint_as_float(i & 1 ? (w[i >> 1] & 0xFFFF0000u) : (w[i >> 1] << 16));
+      const float t = mode == 0 ? __fmul_rn(f, mul) : __fdiv_rn(f, sc);
+      const float r = fminf(fmaxf(rintf(t), lo), 127.f);
+      packed[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * (i & 3));
+    }
+    dst[c] = make_uint2(packed[0], packed[1]);
+  }
+}
+
+}  // namespace
+}  // namespace h3sa
+
+using namespace h3sa;
+
+extern "C" {
+
+int h3sa_w8a8_gemm(const void* a, const float* a_scale, const void* b, const float* b_scale,
+                   void* out, int32_t m, int32_t n, int32_t k, int32_t ldo, int32_t* device_error,
+                   void* stream) {
+  if (!a || !b || !a_scale || !b_scale || !out)
+    return set_error(H3SA_ERR_INVALID, "w8a8_gemm: null operand");
+  if (m < 0 || n <= 0 || k <= 0 || (k % 16) || (n % 8) || ldo < n || (ldo % 8))
+    return set_error(H3SA_ERR_INVALID, "w8a8_gemm: m=%d n=%d k=%d ldo=%d (k must be a multiple "
+                     "of 16, n and ldo of 8)", m, n, k, ldo);
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return set_error(H3SA_ERR_INVALID, "w8a8_gemm: operands must be 16-byte aligned");
+  if (m == 0) return H3SA_OK;
+  CUtensorMap tmA, tmB;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m), 1};
+    const uint64_t strides[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(k) * m};
+    const uint32_t box[3] = {kGemmBK, kGemmBM, 1};
+    int rc = encode_tiled_3d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, dims, strides, box);
+    if (rc) return rc;
+  }
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n), 1};
+    const uint64_t strides[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(k) * n};
+    const uint32_t box[3] = {kGemmBK, kGemmBN, 1};
+    int rc = encode_tiled_3d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, dims, strides, box);
+    if (rc) return rc;
+  }
+  GemmParams prm;
+  prm.a_scale = a_scale;
+  prm.b_scale = b_scale;
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.m = m;
+  prm.n = n;
+  prm.k = k;
+  prm.ldo = ldo;
+  prm.tiles_n = (n + kGemmBN - 1) / kGemmBN;
+  prm.tiles = prm.tiles_n * ((m + kGemmBM - 1) / kGemmBM);
+  prm.err = device_error;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  static std::mutex mu;
+  static bool configured[64] = {};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev < 64 && !configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(gemm_smem_bytes()));
+      if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(w8a8_gemm)", e);
+      configured[dev] = true;
+    }
+  }
+  const int grid = prm.tiles < sms ? prm.tiles : sms;
+  w8a8_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), static_cast<cudaStream_t>(stream)>>>(
+      tmA, tmB, prm);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("w8a8_gemm_kernel launch", e);
+  return H3SA_OK;
+}
+
+int h3sa_quantize_int8_rows(const void* x, void* q, float* scale, int32_t rows, int32_t cols,
+                            int32_t mode, void* stream) {
+  if (!x || !q || !scale || rows < 0 || cols <= 0 || (cols % 8) || (mode != 0 && mode != 1))
+    return set_error(H3SA_ERR_INVALID, "quantize_int8_rows: rows=%d cols=%d mode=%d (cols must "
+                     "be a multiple of 8, mode 0 or 1)", rows, cols, mode);
+  if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 7))
+    return set_error(H3SA_ERR_INVALID, "quantize_int8_rows: unaligned tensors");
+  if (rows == 0) return H3SA_OK;
+  quantize_int8_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<int8_t*>(q), scale, cols, mode);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("quantize_int8_rows launch", e);
+  return H3SA_OK;
+}
+
+}  // extern "C"

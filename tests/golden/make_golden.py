@@ -39,6 +39,9 @@ them from the seeds recorded in each fixture. Fixtures:
                  step): FlashAttention-3's FP8 call is replaced by exact attention on the
                  dequantised e4m3 inputs plus its log-sum-exp, so the reference's own
                  quantisation, commit-level selection and LSE merge run as written.
+* w8a8.npz       the reference's int8 weight quantiser _quantize_weight
+                 (T/inference/w8a8.py:56-63) on a bf16 weight with outliers and an all-zero
+                 row (the 1e-12 scale floor).
 * topk.npz       key summaries of the FL2AV segmented-FP8 CleanAVKVCache
                  (F/streaming/cache.py:836-855) over six commits and after a sink + recent
                  retention, with the commit-level top-k selection of the segmented top-k
@@ -461,6 +464,19 @@ def make_hook_topk(path: Path) -> None:
         arrays[f"selected_blocks_{step}"] = np.array(hook.dynamic_block_sparse_selected_blocks)
     np.savez_compressed(path, **arrays)
 
+def make_w8a8(path: Path) -> None:
+    import torch
+    from taomate_h3.inference.w8a8 import _quantize_weight
+
+    rng = np.random.default_rng(31)
+    w = rng.standard_normal((96, 512)).astype(np.float32) * 0.02
+    w[3, 17] = 0.9          # an outlier sets row 3's scale
+    w[5] = 0.0              # all-zero row: the 1e-12 floor
+    w[7] = np.linspace(-1.27, 1.27, 512, dtype=np.float32)  # exact multiples of the scale
+    wb = bf16(w)
+    q, scale = _quantize_weight(torch.from_numpy(wb).to(torch.bfloat16))
+    np.savez(path, weight=wb, q=q.numpy(), scale=scale.numpy())
+
 # ----------------------------------------------------------------------------- ulysses
 def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import datetime
@@ -554,7 +570,7 @@ def main() -> None:
               "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
               "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f,
               "topk.npz": make_topk, "hook_f.npz": make_hook_f,
-              "hook_topk.npz": make_hook_topk}
+              "hook_topk.npz": make_hook_topk, "w8a8.npz": make_w8a8}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

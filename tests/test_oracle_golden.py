@@ -280,3 +280,24 @@ def test_fl2av_hook_modes_match_reference() -> None:
         if captured is not None:
             assert torch.equal(captured[0].float(), torch.from_numpy(g["prefix_key"]))
             assert torch.equal(captured[1].float(), torch.from_numpy(g["prefix_value"]))
+
+
+def test_w8a8_weight_quantiser_matches_reference() -> None:
+    """The oracle's int8 weight quantiser against the reference's _quantize_weight
+    (tests/golden/w8a8.npz): identical bytes and scales; and the scaled GEMM oracle equals a
+    float64 evaluation of the same products within bf16 rounding."""
+
+    from oracle import w8a8 as ow8
+
+    g = load("w8a8.npz")
+    q, scale = ow8.quantize_weight(g["weight"])
+    assert np.array_equal(q, g["q"]) and np.array_equal(scale, g["scale"])
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal((40, 512)).astype(np.float32)
+    x[4] = 0.0
+    qa, sa = ow8.quantize_activation(x)
+    assert np.all(qa[4] == 0) and sa[4, 0] == 0.0
+    assert qa.min() >= -128 and qa.max() <= 127
+    out = ow8.scaled_mm(qa, sa, q, scale)
+    ref = (qa.astype(np.float64) @ q.astype(np.float64).T) * sa.astype(np.float64) * scale.reshape(1, -1)
+    assert np.allclose(out, ref, rtol=2 ** -7, atol=1e-30)
