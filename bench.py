@@ -436,7 +436,43 @@ def _time_launch(fn, iters: int) -> float:
     return a.elapsed_time(b) / iters
 
 
-VARIANTS = ("fp8", "sparse", "480p", "feeders")
+VARIANTS = ("fp8", "sparse", "480p", "feeders", "w8a8")
+
+
+def w8a8_projection(peaks: dict, iters: int = 20) -> dict:
+    """The W8A8 QKV projection in front of the attention at the 768p SP=8 per-GPU shape: 1568
+    tokens x 5376 hidden -> 9216 (3 x 24 heads x 128), the reference's int8 path
+    (T/inference/w8a8.py:190-221): per-token activation quantisation + scaled int8 GEMM. Timed:
+    the GEMM alone, the whole cutlass_w8a8_linear drop-in, and torch's bf16 matmul (cuBLAS)
+    of the same shape for scale. Ops = 2 * M * N * K. Peak: 2 x the measured bf16 figure
+    (no measured int8 peak; nominal dense int8 4.5 POPS)."""
+
+    from h3sa.w8a8 import cutlass_w8a8_linear, quantize_int8_rows, quantize_weight, w8a8_gemm
+
+    dev = torch.device("cuda")
+    g = torch.Generator(device=dev).manual_seed(13)
+    m, k, n = 1568, 5376, 9216
+    x = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    wq, ws = quantize_weight(w)
+    qa, sa = quantize_int8_rows(x)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    ops = 2.0 * m * n * k
+    ms_gemm = _time_launch(lambda: w8a8_gemm(qa, sa, wq, ws, out), iters)
+    ms_linear = _time_launch(lambda: cutlass_w8a8_linear(x, wq, ws), iters)
+    ms_quant = _time_launch(lambda: quantize_int8_rows(x), iters)
+    wt = w.t()
+    ms_bf16 = _time_launch(lambda: torch.matmul(x, wt), iters)
+    peak = 2 * peaks["bf16"]
+    tops = ops / (ms_gemm * 1e-3) / 1e12
+    return {"w8a8_qkv_768p_sp8_per_gpu": {
+        "m": m, "n": n, "k": k, "gemm_ms": ms_gemm, "gemm_tops": tops,
+        "linear_ms": ms_linear, "activation_quant_ms": ms_quant,
+        "cublas_bf16_ms": ms_bf16, "cublas_bf16_tflops": ops / (ms_bf16 * 1e-3) / 1e12,
+        "speedup_vs_bf16": ms_bf16 / ms_linear,
+        "roofline": {"bound": "tensor", "peak": peak, "frac": tops / peak,
+                     "peak_source": "2 x measured bf16 burst (no measured int8 peak)"},
+        "reference_path_on_b200": "vLLM cutlass_scaled_mm refuses int8 on SM100"}}
 
 
 def feeders(peaks: dict, iters: int = 20) -> dict:
@@ -565,6 +601,8 @@ def _variants(peaks: dict, iters: int = 10, only: str | None = None) -> dict:
     out = {}
     if only == "feeders":
         return {"feeders": feeders(peaks, iters)}
+    if only == "w8a8":
+        return w8a8_projection(peaks, iters)
     for name, fn in (("fp8", _variant_fp8), ("sparse", _variant_sparse), ("480p", _variant_480p)):
         if only in (None, name):
             out.update(fn(peaks, iters, dev, g, pools))

@@ -24,8 +24,11 @@
 namespace h3sa {
 namespace {
 
+#ifndef H3SA_GEMM_BN
+#define H3SA_GEMM_BN 256
+#endif
 constexpr int kGemmBM = 128;
-constexpr int kGemmBN = 256;
+constexpr int kGemmBN = H3SA_GEMM_BN;
 constexpr int kGemmBK = 128;  // bytes of K per stage (one 128-byte swizzle atom)
 constexpr int kGemmStages = 4;
 constexpr int kGemmThreads = 192;
@@ -222,31 +225,60 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // mode 1, the weights (T/inference/w8a8.py:56-63):
 //   scale = max(amax / 127, 1e-12), q = clamp(rint(x / scale), -127, 127).
 // rint rounds half to even in both.
-__global__ void __launch_bounds__(256) quantize_int8_rows_kernel(
+constexpr int kQuantRowThreads = 256;
+constexpr int kQuantRowCached = 4;  // 16-byte chunks a thread keeps in registers (8192 columns)
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+__device__ __forceinline__ float chunk_amax(const uint4& v, float m) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) m = fmaxf(m, fmaxf(fabsf(bf16_lo(w[i])), fabsf(bf16_hi(w[i]))));
+  return m;
+}
+
+__device__ __forceinline__ uint2 chunk_quant(const uint4& v, int mode, float sc, float mul,
+                                             float lo) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float f = (i & 1) ? bf16_hi(w[i >> 1]) : bf16_lo(w[i >> 1]);
+    const float t = mode == 0 ? __fmul_rn(f, mul) : __fdiv_rn(f, sc);
+    const float r = fminf(fmaxf(rintf(t), lo), 127.f);
+    packed[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * (i & 3));
+  }
+  return make_uint2(packed[0], packed[1]);
+}
+
+// Rows of up to kQuantRowThreads * kQuantRowCached * 8 columns are read once (kept in
+// registers between the amax and the quantisation); longer rows are read twice.
+__global__ void __launch_bounds__(kQuantRowThreads) quantize_int8_rows_kernel(
     const __nv_bfloat16* __restrict__ x, int8_t* __restrict__ q, float* __restrict__ scale,
     int cols, int mode) {
   const size_t row = blockIdx.x;
   const uint4* src = reinterpret_cast<const uint4*>(x + row * cols);
   const int chunks = cols / 8;
+  uint4 cache[kQuantRowCached];
   float m = 0.f;
-  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-    const uint4 v = __ldg(src + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      m = fmaxf(m, fabsf(__uint_as_float(w[i] << 16)));
-      m = fmaxf(m, fabsf(__uint_as_float(w[i] & 0xFFFF0000u)));
-    }
+  for (int i = 0; i < kQuantRowCached; ++i) {
+    const int c = threadIdx.x + i * kQuantRowThreads;
+    cache[i] = c < chunks ? __ldg(src + c) : make_uint4(0u, 0u, 0u, 0u);
+    m = chunk_amax(cache[i], m);
   }
+  for (int c = threadIdx.x + kQuantRowCached * kQuantRowThreads; c < chunks; c += kQuantRowThreads)
+    m = chunk_amax(__ldg(src + c), m);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-  __shared__ float red[8];
+  __shared__ float red[kQuantRowThreads / 32];
   __shared__ float row_scale, row_mul;
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
   if (threadIdx.x == 0) {
     float amax = red[0];
-    for (int i = 1; i < 8; ++i) amax = fmaxf(amax, red[i]);
+    for (int i = 1; i < kQuantRowThreads / 32; ++i) amax = fmaxf(amax, red[i]);
     if (mode == 0) {
       row_scale = __fdiv_rn(amax, 127.f);
       row_mul = amax > 0.f ? __fdiv_rn(127.f, amax) : 0.f;
@@ -260,19 +292,13 @@ __global__ void __launch_bounds__(256) quantize_int8_rows_kernel(
   const float sc = row_scale, mul = row_mul;
   const float lo = mode == 0 ? -128.f : -127.f;
   uint2* dst = reinterpret_cast<uint2*>(q + row * cols);
-  for (int c = threadIdx.x; c < chunks; c += blockDim.x) {
-    const uint4 v = __ldg(src + c);
-    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-    uint32_t packed[2] = {0u, 0u};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float f = __uint_as_float(i & 1 ? (w[i >> 1] & 0xFFFF0000u) : (w[i >> 1] << 16));
-      const float t = mode == 0 ? __fmul_rn(f, mul) : __fdiv_rn(f, sc);
-      const float r = fminf(fmaxf(rintf(t), lo), 127.f);
-      packed[i >> 2] |= (static_cast<uint32_t>(static_cast<int>(r)) & 0xFFu) << (8 * (i & 3));
-    }
-    dst[c] = make_uint2(packed[0], packed[1]);
+  for (int i = 0; i < kQuantRowCached; ++i) {
+    const int c = threadIdx.x + i * kQuantRowThreads;
+    if (c < chunks) dst[c] = chunk_quant(cache[i], mode, sc, mul, lo);
   }
+  for (int c = threadIdx.x + kQuantRowCached * kQuantRowThreads; c < chunks; c += kQuantRowThreads)
+    dst[c] = chunk_quant(__ldg(src + c), mode, sc, mul, lo);
 }
 
 }  // namespace
@@ -351,7 +377,7 @@ int h3sa_quantize_int8_rows(const void* x, void* q, float* scale, int32_t rows, 
   if ((reinterpret_cast<uintptr_t>(x) & 15) || (reinterpret_cast<uintptr_t>(q) & 7))
     return set_error(H3SA_ERR_INVALID, "quantize_int8_rows: unaligned tensors");
   if (rows == 0) return H3SA_OK;
-  quantize_int8_rows_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+  quantize_int8_rows_kernel<<<rows, kQuantRowThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const __nv_bfloat16*>(x), static_cast<int8_t*>(q), scale, cols, mode);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("quantize_int8_rows launch", e);
