@@ -236,6 +236,23 @@ H3SA_API int h3sa_w8a8_gemm(const void* a, const float* a_scale, const void* b,
                             const float* b_scale, void* out, int32_t m, int32_t n, int32_t k,
                             int32_t ldo, int32_t* device_error, void* stream);
 
+/* bf16 GEMM on the same tcgen05 kernel (kind::f16, fp32 accumulation in TMEM):
+ * out[m, n] = bf16_rn(sum_k a[m, k] * b[n, k]), a bf16 [m, k], b bf16 [n, k] (K contiguous,
+ * k a multiple of 8, n and ldo of 8, 16-byte aligned). With partial_peers (device array of
+ * `ranks` addresses, each rank's partial buffer [ranks][m][ldo] bf16 mapped here), the tile
+ * is also stored into slot `slot` of every rank's buffer over NVLink: the row-parallel
+ * out_proj's local product with its TP all-reduce exchange fused in (T/model/layers.py:441-443,
+ * T/distributed/linear.py:186-191). out may be NULL then. */
+H3SA_API int h3sa_gemm_bf16(const void* a, const void* b, void* out, int32_t m, int32_t n,
+                            int32_t k, int32_t ldo, const uint64_t* partial_peers, int32_t ranks,
+                            int32_t slot, int32_t* device_error, void* stream);
+
+/* out[m, n] = bf16_rn(sum over t = 0 .. ranks-1 of slots[t][m][n]) (fp32 sum in rank order),
+ * slots bf16 [ranks][m][ldo]: the reduction half of the TP all-reduce after h3sa_gemm_bf16
+ * stored every rank's partial (T/distributed/collectives.py:51-55). */
+H3SA_API int h3sa_tp_reduce(const void* slots, void* out, int32_t m, int32_t n, int32_t ldo,
+                            int32_t ranks, void* stream);
+
 /* Per-row int8 quantisation of bf16 rows x [rows, cols] into q int8 [rows, cols] and scale fp32
  * [rows] (cols a multiple of 8). mode 0 (activations, dynamic per token):
  * scale = amax / 127, q = clamp(rint(x * (127 / amax)), -128, 127), zero rows give zeros;

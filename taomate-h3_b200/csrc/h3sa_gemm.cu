@@ -14,6 +14,12 @@
 // * warps 2-5 (one per TMEM lane quadrant) read the int32 accumulators, scale them in the
 //   order above and store bf16 rows.
 //
+// The same kernel in bf16 (tcgen05 kind::f16, fp32 accumulation) is the row-parallel out_proj
+// of the attention (T/model/layers.py:441-443, T/distributed/linear.py:142-198): its epilogue
+// can store this TP rank's bf16 partial output straight into slot `rank` of every TP rank's
+// partial buffer over NVLink, after which a peer barrier and h3sa_tp_reduce (the slots summed
+// in rank order) replace the TP all-reduce.
+//
 // Every wait is bounded (h3sa_ptx.cuh); a wait that gives up records kErrWaitTimeout in the
 // error word and the CTA unwinds.
 #include "h3sa_host.h"
@@ -52,10 +58,12 @@ constexpr size_t gemm_smem_bytes() { return sizeof(GemmSmem) + 1024; }
 static_assert(gemm_smem_bytes() <= 232448, "W8A8 GEMM needs more than 227 KB of shared memory");
 
 struct GemmParams {
-  const float* a_scale;  // [M]
-  const float* b_scale;  // [N]
-  __nv_bfloat16* out;    // [M, ldo]
-  int m, n, k;
+  const float* a_scale;  // [M] (int8 only)
+  const float* b_scale;  // [N] (int8 only)
+  __nv_bfloat16* out;    // [M, ldo] or null
+  const uint64_t* out_peers;  // bf16 only: partial buffers [ranks][M][ldo] of every TP rank
+  int out_ranks, out_slot;
+  int m, n, k;  // k in elements
   int ldo;
   int tiles_n, tiles;
   int* err;
@@ -76,16 +84,19 @@ __device__ __forceinline__ void mma_ss_i8(uint32_t d_tmem, uint64_t a_desc, uint
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
 
+// kBf16: bf16 operands (kind::f16, fp32 accumulators, no scales); else int8 (kind::i8).
+template <bool kBf16>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    w8a8_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                     const GemmParams p) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const GemmParams p) {
+  constexpr int kElemK = kBf16 ? kGemmBK / 2 : kGemmBK;  // K elements per stage
   extern __shared__ uint8_t smem_raw[];
   GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   volatile int* abort_flag = &sm.abort_flag;
-  const int k_steps = (p.k + kGemmBK - 1) / kGemmBK;
+  const int k_steps = (p.k + kElemK - 1) / kElemK;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kGemmStages; ++s) {
@@ -123,14 +134,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             break;
           const uint32_t full = smem_u32(&sm.full[s]);
           mbar_expect_tx(full, kGemmATile + kGemmBTile);
-          tma_load_3d(smem_u32(sm.a[s]), &tmA, full, ks * kGemmBK, m0, 0);
-          tma_load_3d(smem_u32(sm.b[s]), &tmB, full, ks * kGemmBK, n0, 0);
+          tma_load_3d(smem_u32(sm.a[s]), &tmA, full, ks * kElemK, m0, 0);
+          tma_load_3d(smem_u32(sm.b[s]), &tmB, full, ks * kElemK, n0, 0);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (whole warp)
-    constexpr uint32_t idesc = idesc_s8(kGemmBM, kGemmBN);
+    constexpr uint32_t idesc = kBf16 ? idesc_bf16(kGemmBM, kGemmBN, false)
+                                     : idesc_s8(kGemmBM, kGemmBN);
     uint32_t it = 0;
     int j = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += gridDim.x, ++j) {
@@ -149,8 +161,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < kGemmBK / kGemmUmmaK; ++kk) {
           // K advance inside the swizzle atom: 32 bytes = 2 in the address field
-          mma_ss_i8(d_tmem, sdesc_join(a_lo + 2 * kk), sdesc_join(b_lo + 2 * kk), idesc,
-                    (ks | kk) != 0);
+          if constexpr (kBf16)
+            mma_ss(d_tmem, sdesc_join(a_lo + 2 * kk), sdesc_join(b_lo + 2 * kk), idesc,
+                   (ks | kk) != 0);
+          else
+            mma_ss_i8(d_tmem, sdesc_join(a_lo + 2 * kk), sdesc_join(b_lo + 2 * kk), idesc,
+                      (ks | kk) != 0);
         }
         tc_commit(smem_u32(&sm.empty[s]));  // the stage is free once these MMAs completed
       }
@@ -166,15 +182,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const int buf = j & 1;
       const int m0 = (tile / p.tiles_n) * kGemmBM;
       const int n0 = (tile % p.tiles_n) * kGemmBN;
-      // this tile's column scales into shared memory (the previous tile of this buffer is done)
-      for (int c = ep_thread; c < kGemmBN; c += 128)
-        sm.b_scale[buf][c] = n0 + c < p.n ? __ldg(p.b_scale + n0 + c) : 0.f;
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if constexpr (!kBf16) {
+        // this tile's column scales into shared memory (the previous tile of this buffer is
+        // done: every epilogue warp passed the previous tile's barrier)
+        for (int c = ep_thread; c < kGemmBN; c += 128)
+          sm.b_scale[buf][c] = n0 + c < p.n ? __ldg(p.b_scale + n0 + c) : 0.f;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
       if (!mbar_wait(smem_u32(&sm.acc_full[buf]), (j >> 1) & 1, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = m0 + quad * 32 + lane;
-      const float a_s = row < p.m ? __ldg(p.a_scale + row) : 0.f;
-      __nv_bfloat16* orow = p.out + static_cast<size_t>(row) * p.ldo + n0;
+      const float a_s = (!kBf16 && row < p.m) ? __ldg(p.a_scale + row) : 0.f;
+      const size_t orow_off = (static_cast<size_t>(row) * p.ldo + n0) * sizeof(__nv_bfloat16);
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(buf * kGemmBN);
 #pragma unroll 1
@@ -187,20 +206,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float x0 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i],
-                                                      __int2float_rn(static_cast<int>(r[2 * i]))));
-            const float x1 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i + 1],
-                                                      __int2float_rn(static_cast<int>(r[2 * i + 1]))));
+            float x0, x1;
+            if constexpr (kBf16) {
+              x0 = __uint_as_float(r[2 * i]);
+              x1 = __uint_as_float(r[2 * i + 1]);
+            } else {
+              x0 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i],
+                                            __int2float_rn(static_cast<int>(r[2 * i]))));
+              x1 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i + 1],
+                                            __int2float_rn(static_cast<int>(r[2 * i + 1]))));
+            }
             w[i] = pack_bf16x2(x0, x1);
           }
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
-          if (n0 + c + 32 <= p.n) {
+          // ragged last columns go by 8-column groups (n is a multiple of 8)
+          const int groups = n0 + c + 32 <= p.n ? 4 : (p.n - n0 - c) / 8;
+          const size_t col_off = orow_off + static_cast<size_t>(c) * sizeof(__nv_bfloat16);
+          if (p.out) {
+            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + col_off);
 #pragma unroll
             for (int q = 0; q < 4; ++q)
-              dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-          } else {  // ragged last columns: 8-column groups (n is a multiple of 8)
-            for (int q = 0; q < 4 && n0 + c + 8 * q < p.n; ++q)
-              dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+              if (q < groups) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          }
+          if constexpr (kBf16) {
+            // this rank's partial into its slot of every TP rank's buffer (peer stores)
+            const size_t slot_off = static_cast<size_t>(p.out_slot) * p.m * p.ldo *
+                                    sizeof(__nv_bfloat16);
+            for (int t = 0; t < p.out_ranks; ++t) {
+              uint4* dst = reinterpret_cast<uint4*>(p.out_peers[t] + slot_off + col_off);
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                if (q < groups)
+                  dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+            }
           }
         }
       }
@@ -208,6 +245,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&sm.acc_empty[buf]));
     }
+    // the peer stores are visible to the other GPUs before the barrier that follows
+    if (kBf16 && p.out_ranks > 1) __threadfence_system();
   }
 
   tc_fence_before();
@@ -304,48 +343,34 @@ __global__ void __launch_bounds__(kQuantRowThreads) quantize_int8_rows_kernel(
 }  // namespace
 }  // namespace h3sa
 
-using namespace h3sa;
+namespace h3sa {
+namespace {
 
-extern "C" {
-
-int h3sa_w8a8_gemm(const void* a, const float* a_scale, const void* b, const float* b_scale,
-                   void* out, int32_t m, int32_t n, int32_t k, int32_t ldo, int32_t* device_error,
-                   void* stream) {
-  if (!a || !b || !a_scale || !b_scale || !out)
-    return set_error(H3SA_ERR_INVALID, "w8a8_gemm: null operand");
-  if (m < 0 || n <= 0 || k <= 0 || (k % 16) || (n % 8) || ldo < n || (ldo % 8))
-    return set_error(H3SA_ERR_INVALID, "w8a8_gemm: m=%d n=%d k=%d ldo=%d (k must be a multiple "
-                     "of 16, n and ldo of 8)", m, n, k, ldo);
-  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
-       reinterpret_cast<uintptr_t>(out)) & 15)
-    return set_error(H3SA_ERR_INVALID, "w8a8_gemm: operands must be 16-byte aligned");
-  if (m == 0) return H3SA_OK;
+// A and B row-major with K contiguous, K a multiple of 16 bytes; tcgen05 kind per kBf16.
+template <bool kBf16>
+int launch_gemm(const void* a, const void* b, GemmParams prm, cudaStream_t stream) {
+  const CUtensorMapDataType dt =
+      kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const uint64_t esize = kBf16 ? 2 : 1;
+  const uint32_t box_k = kBf16 ? kGemmBK / 2 : kGemmBK;
+  const uint64_t m = prm.m, n = prm.n, k = prm.k;
   CUtensorMap tmA, tmB;
   {
-    const uint64_t dims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(m), 1};
-    const uint64_t strides[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(k) * m};
-    const uint32_t box[3] = {kGemmBK, kGemmBM, 1};
-    int rc = encode_tiled_3d(&tmA, CU_TENSOR_MAP_DATA_TYPE_UINT8, a, dims, strides, box);
+    const uint64_t dims[3] = {k, m, 1};
+    const uint64_t strides[2] = {k * esize, k * esize * m};
+    const uint32_t box[3] = {box_k, kGemmBM, 1};
+    int rc = encode_tiled_3d(&tmA, dt, a, dims, strides, box);
     if (rc) return rc;
   }
   {
-    const uint64_t dims[3] = {static_cast<uint64_t>(k), static_cast<uint64_t>(n), 1};
-    const uint64_t strides[2] = {static_cast<uint64_t>(k), static_cast<uint64_t>(k) * n};
-    const uint32_t box[3] = {kGemmBK, kGemmBN, 1};
-    int rc = encode_tiled_3d(&tmB, CU_TENSOR_MAP_DATA_TYPE_UINT8, b, dims, strides, box);
+    const uint64_t dims[3] = {k, n, 1};
+    const uint64_t strides[2] = {k * esize, k * esize * n};
+    const uint32_t box[3] = {box_k, kGemmBN, 1};
+    int rc = encode_tiled_3d(&tmB, dt, b, dims, strides, box);
     if (rc) return rc;
   }
-  GemmParams prm;
-  prm.a_scale = a_scale;
-  prm.b_scale = b_scale;
-  prm.out = static_cast<__nv_bfloat16*>(out);
-  prm.m = m;
-  prm.n = n;
-  prm.k = k;
-  prm.ldo = ldo;
-  prm.tiles_n = (n + kGemmBN - 1) / kGemmBN;
-  prm.tiles = prm.tiles_n * ((m + kGemmBM - 1) / kGemmBM);
-  prm.err = device_error;
+  prm.tiles_n = (prm.n + kGemmBN - 1) / kGemmBN;
+  prm.tiles = prm.tiles_n * ((prm.m + kGemmBM - 1) / kGemmBM);
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -354,18 +379,129 @@ int h3sa_w8a8_gemm(const void* a, const float* a_scale, const void* b, const flo
   {
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 64 && !configured[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(w8a8_gemm_kernel,
+      cudaError_t e = cudaFuncSetAttribute(gemm_kernel<kBf16>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(gemm_smem_bytes()));
-      if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(w8a8_gemm)", e);
+      if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
       configured[dev] = true;
     }
   }
   const int grid = prm.tiles < sms ? prm.tiles : sms;
-  w8a8_gemm_kernel<<<grid, kGemmThreads, gemm_smem_bytes(), static_cast<cudaStream_t>(stream)>>>(
-      tmA, tmB, prm);
+  gemm_kernel<kBf16><<<grid, kGemmThreads, gemm_smem_bytes(), stream>>>(tmA, tmB, prm);
   cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return set_cuda_error("w8a8_gemm_kernel launch", e);
+  if (e != cudaSuccess) return set_cuda_error("gemm_kernel launch", e);
+  return H3SA_OK;
+}
+
+// out[i] = bf16(sum over t of float(slots[t][i])) in rank order t = 0, 1, ...
+__global__ void __launch_bounds__(256) tp_reduce_kernel(const __nv_bfloat16* __restrict__ slots,
+                                                        __nv_bfloat16* __restrict__ out, int m,
+                                                        int n, int ldo, int ranks) {
+  const int cpr = n / 8;  // 16-byte chunks per row
+  const long long total = static_cast<long long>(m) * cpr;
+  const size_t slot = static_cast<size_t>(m) * ldo;
+  for (long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;
+       idx += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(idx / cpr);
+    const int c = static_cast<int>(idx - static_cast<long long>(row) * cpr);
+    const size_t off = static_cast<size_t>(row) * ldo + static_cast<size_t>(c) * 8;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    for (int t = 0; t < ranks; ++t) {
+      const uint4 v = __ldcg(reinterpret_cast<const uint4*>(slots + t * slot + off));
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] += __uint_as_float(w[i] << 16);
+        acc[2 * i + 1] += __uint_as_float(w[i] & 0xFFFF0000u);
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + off) = o;
+  }
+}
+
+int check_gemm_args(const void* a, const void* b, const void* out, int32_t m, int32_t n,
+                    int32_t k_bytes, int32_t ldo, const char* name) {
+  if (!a || !b) return set_error(H3SA_ERR_INVALID, "%s: null operand", name);
+  if (m < 0 || n <= 0 || k_bytes <= 0 || (k_bytes % 16) || (n % 8) || ldo < n || (ldo % 8))
+    return set_error(H3SA_ERR_INVALID, "%s: m=%d n=%d k bytes=%d ldo=%d (k bytes must be a "
+                     "multiple of 16, n and ldo of 8)", name, m, n, k_bytes, ldo);
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+       reinterpret_cast<uintptr_t>(out)) & 15)
+    return set_error(H3SA_ERR_INVALID, "%s: operands must be 16-byte aligned", name);
+  return H3SA_OK;
+}
+
+}  // namespace
+}  // namespace h3sa
+
+using namespace h3sa;
+
+extern "C" {
+
+int h3sa_w8a8_gemm(const void* a, const float* a_scale, const void* b, const float* b_scale,
+                   void* out, int32_t m, int32_t n, int32_t k, int32_t ldo, int32_t* device_error,
+                   void* stream) {
+  if (!a_scale || !b_scale || !out) return set_error(H3SA_ERR_INVALID, "w8a8_gemm: null operand");
+  int rc = check_gemm_args(a, b, out, m, n, k, ldo, "w8a8_gemm");
+  if (rc) return rc;
+  if (m == 0) return H3SA_OK;
+  GemmParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.a_scale = a_scale;
+  prm.b_scale = b_scale;
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.m = m;
+  prm.n = n;
+  prm.k = k;
+  prm.ldo = ldo;
+  prm.err = device_error;
+  return launch_gemm<false>(a, b, prm, static_cast<cudaStream_t>(stream));
+}
+
+int h3sa_gemm_bf16(const void* a, const void* b, void* out, int32_t m, int32_t n, int32_t k,
+                   int32_t ldo, const uint64_t* partial_peers, int32_t ranks, int32_t slot,
+                   int32_t* device_error, void* stream) {
+  if (!out && !partial_peers) return set_error(H3SA_ERR_INVALID, "gemm_bf16: no destination");
+  if (partial_peers && (ranks < 1 || slot < 0 || slot >= ranks))
+    return set_error(H3SA_ERR_INVALID, "gemm_bf16: slot %d of %d ranks", slot, ranks);
+  int rc = check_gemm_args(a, b, out, m, n, 2 * k, ldo, "gemm_bf16");
+  if (rc) return rc;
+  if (m == 0) return H3SA_OK;
+  GemmParams prm;
+  memset(&prm, 0, sizeof(prm));
+  prm.out = static_cast<__nv_bfloat16*>(out);
+  prm.out_peers = partial_peers;
+  prm.out_ranks = partial_peers ? ranks : 0;
+  prm.out_slot = slot;
+  prm.m = m;
+  prm.n = n;
+  prm.k = k;
+  prm.ldo = ldo;
+  prm.err = device_error;
+  return launch_gemm<true>(a, b, prm, static_cast<cudaStream_t>(stream));
+}
+
+int h3sa_tp_reduce(const void* slots, void* out, int32_t m, int32_t n, int32_t ldo, int32_t ranks,
+                   void* stream) {
+  if (!slots || !out || m < 0 || n <= 0 || (n % 8) || ldo < n || (ldo % 8) || ranks < 1)
+    return set_error(H3SA_ERR_INVALID, "tp_reduce: m=%d n=%d ldo=%d ranks=%d", m, n, ldo, ranks);
+  if ((reinterpret_cast<uintptr_t>(slots) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return set_error(H3SA_ERR_INVALID, "tp_reduce: tensors must be 16-byte aligned");
+  if (m == 0) return H3SA_OK;
+  const long long work = static_cast<long long>(m) * (n / 8);
+  long long g = (work + 255) / 256;
+  if (g > 148LL * 16) g = 148LL * 16;
+  tp_reduce_kernel<<<static_cast<int>(g), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __nv_bfloat16*>(slots), static_cast<__nv_bfloat16*>(out), m, n, ldo, ranks);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("tp_reduce_kernel launch", e);
   return H3SA_OK;
 }
 

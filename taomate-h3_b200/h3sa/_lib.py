@@ -101,6 +101,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "h3sa_commit_scores": (ctypes.c_int, [_P, _P, _I, _I, _P, _P]),
     "h3sa_w8a8_gemm": (ctypes.c_int, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "h3sa_quantize_int8_rows": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _P]),
+    "h3sa_gemm_bf16": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P, _P]),
+    "h3sa_tp_reduce": (ctypes.c_int, [_P, _P, _I, _I, _I, _I, _P]),
     "h3sa_qkv_norm_rope": (ctypes.c_int, [_P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _F, _P, _P]),
     "h3sa_qkv_norm_rope_pack": (
         ctypes.c_int, [_P, _P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _F, _P, _P]),
