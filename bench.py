@@ -1239,6 +1239,75 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
         print(json.dumps(line), flush=True)
 
 
+def run_out_proj(args: argparse.Namespace) -> None:
+    """The attention's row-parallel out_proj over TP = world ranks (T/model/layers.py:441-443,
+    T/distributed/linear.py:186-191) at the 768p TP2 x SP4 per-rank shape: 3136 sequence rows
+    x (inner 3072 / TP) -> hidden 5376, bias-free. Three forms, each timed over --steps calls
+    after --warmup (CUDA events, max over ranks): the fused PeerRowParallelLinear (partials
+    stored into the peers' slots by the GEMM epilogue, peer barrier, slot reduce); the same
+    tcgen05 GEMM + NCCL all-reduce; cuBLAS (torch.matmul) + NCCL all-reduce, the reference's
+    structure. FLOPs per rank: 2 * rows * hidden * inner / TP."""
+
+    from h3sa.linear import PeerRowParallelLinear, gemm_bf16
+
+    world, rank, local = _dist()
+    if world < 2:
+        raise SystemExit("--layout out_proj runs on 2 or more GPUs (torchrun)")
+    dev = torch.device("cuda", local)
+    rows, inner, hidden = 3136, 3072, 5376
+    loc = inner // world
+    g = torch.Generator(device=dev).manual_seed(10 + rank)
+    x = torch.randn(rows, loc, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(hidden, loc, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    fused = PeerRowParallelLinear(w, rows, device_error=err)
+    wt = w.t()
+    group = torch.distributed.group.WORLD
+
+    def nccl_ours():
+        out = gemm_bf16(x, w)
+        torch.distributed.all_reduce(out, group=group)
+
+    def nccl_cublas():
+        out = torch.matmul(x, wt)
+        torch.distributed.all_reduce(out, group=group)
+
+    def timed(fn) -> float:
+        for _ in range(args.warmup):
+            fn()
+        _barrier(world)
+        a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+        a.record()
+        for _ in range(args.steps):
+            fn()
+        b.record()
+        _barrier(world)
+        return _max_over_ranks(a.elapsed_time(b) / args.steps, world)
+
+    ms_fused = timed(lambda: fused(x))
+    ms_ours = timed(nccl_ours)
+    ms_cublas = timed(nccl_cublas)
+    ms_gemm = timed(lambda: gemm_bf16(x, w))
+    code = int(err.item())
+    torch.cuda.synchronize()
+    _barrier(world)
+    fused.close()
+    flops = 2.0 * rows * hidden * loc
+    if rank == 0:
+        peaks = _peaks()
+        print(json.dumps({
+            "metric": "row-parallel out_proj with TP all-reduce (768p TP2 x SP4 rank shape)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "dtype": "bf16",
+            "config": {"rows": rows, "inner_per_rank": loc, "hidden": hidden, "tp": world},
+            "ms": {"fused_peer_reduce": ms_fused, "tcgen05_gemm_plus_nccl": ms_ours,
+                   "cublas_plus_nccl": ms_cublas, "gemm_alone": ms_gemm},
+            "speedup_vs_cublas_nccl": ms_cublas / ms_fused,
+            "gemm_tflops": flops / (ms_gemm * 1e-3) / 1e12,
+            "gemm_frac_of_bf16_peak": flops / (ms_gemm * 1e-3) / 1e12 / peaks["bf16"],
+            "nvlink_bytes_per_rank": rows * hidden * 2 * (world - 1),
+            "device_error": code}), flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1252,8 +1321,9 @@ def main() -> None:
                     help="SP > 1: NCCL all-to-all + layout copies instead of peer stores")
     ap.add_argument("--no-variants", action="store_true",
                     help="skip the kernel-only FP8 1080p, block-sparse 768p and 480p timings")
-    ap.add_argument("--layout", choices=["sp", "tp2sp4"], default="sp",
-                    help="tp2sp4: the 1080p FP8 configuration in its TP2 x SP4 layout (8 GPUs)")
+    ap.add_argument("--layout", choices=["sp", "tp2sp4", "out_proj"], default="sp",
+                    help="tp2sp4: the 1080p FP8 configuration in its TP2 x SP4 layout (8 GPUs); "
+                         "out_proj: the row-parallel out_proj with its TP all-reduce (TP = GPUs)")
     ap.add_argument("--variant", choices=VARIANTS,
                     help="time only this kernel-only variant on one GPU and print its JSON "
                          "(2 warm-up launches, then --steps launches)")
@@ -1268,6 +1338,8 @@ def main() -> None:
         run_reference(args)
     elif args.layout == "tp2sp4":
         run_tp2sp4(args)
+    elif args.layout == "out_proj":
+        run_out_proj(args)
     else:
         run_h3sa(args)
     if torch.distributed.is_initialized():

@@ -7,12 +7,13 @@
 //
 // * persistent CTAs, one per SM, walking 128 x 256 output tiles;
 // * warp 0 streams A and B K-slices (128 bytes of K per row, 128-byte swizzle) by TMA into a
-//   4-stage shared-memory ring;
+//   4-stage shared-memory ring (3 for bf16);
 // * warp 1 issues tcgen05.mma kind::i8 (M 128, N 256, K 32 per instruction) into one of two
 //   TMEM accumulators (2 x 256 int32 columns), so the epilogue of one tile overlaps the MMAs
 //   of the next;
 // * warps 2-5 (one per TMEM lane quadrant) read the int32 accumulators, scale them in the
-//   order above and store bf16 rows.
+//   order above and store bf16 rows (the bf16 form stages its 32 rows in shared memory and
+//   stores whole 512-byte row segments: full-size packets over NVLink for peer stores).
 //
 // The same kernel in bf16 (tcgen05 kind::f16, fp32 accumulation) is the row-parallel out_proj
 // of the attention (T/model/layers.py:441-443, T/distributed/linear.py:142-198): its epilogue
@@ -30,32 +31,45 @@
 namespace h3sa {
 namespace {
 
-#ifndef H3SA_GEMM_BN
-#define H3SA_GEMM_BN 256
-#endif
 constexpr int kGemmBM = 128;
-constexpr int kGemmBN = H3SA_GEMM_BN;
+constexpr int kGemmBN = 256;  // 32 16-byte chunks per row: one per lane in the row stores
 constexpr int kGemmBK = 128;  // bytes of K per stage (one 128-byte swizzle atom)
-constexpr int kGemmStages = 4;
 constexpr int kGemmThreads = 192;
 constexpr int kGemmUmmaK = 32;  // int8 K per tcgen05.mma
 constexpr uint32_t kGemmATile = kGemmBM * kGemmBK;  // 16 KB
 constexpr uint32_t kGemmBTile = kGemmBN * kGemmBK;  // 32 KB
 
+// int8: 4 stages, each thread stores its own row segments. bf16: 3 stages and a staging area
+// through which the epilogue stores whole rows (the peer stores of the fused TP reduce need
+// full-size NVLink packets; 4 stages and the staging do not fit together).
+template <bool kBf16>
+struct GemmCfg {
+  static constexpr int kStages = kBf16 ? 3 : 4;
+  static constexpr int kStageWarps = kBf16 ? 4 : 1;
+  static constexpr int kStageRows = kBf16 ? 32 : 1;
+};
+
+template <bool kBf16>
 struct GemmSmem {
-  uint8_t a[kGemmStages][kGemmATile];  // 1024-byte aligned (tile sizes are multiples)
-  uint8_t b[kGemmStages][kGemmBTile];
+  using Cfg = GemmCfg<kBf16>;
+  uint8_t a[Cfg::kStages][kGemmATile];  // 1024-byte aligned (tile sizes are multiples)
+  uint8_t b[Cfg::kStages][kGemmBTile];
+  // bf16, per epilogue warp: its 32 rows x kGemmBN bf16 of the tile, 16-byte chunk j of row
+  // r at chunk position j ^ r (conflict-free row-wise writes and lane-wise reads)
+  uint4 stage[Cfg::kStageWarps][Cfg::kStageRows][kGemmBN / 8];
   float b_scale[2][kGemmBN];
-  uint64_t full[kGemmStages];
-  uint64_t empty[kGemmStages];
+  uint64_t full[Cfg::kStages];
+  uint64_t empty[Cfg::kStages];
   uint64_t acc_full[2];
   uint64_t acc_empty[2];
   uint32_t tmem_base;
   int abort_flag;
 };
 
-constexpr size_t gemm_smem_bytes() { return sizeof(GemmSmem) + 1024; }
-static_assert(gemm_smem_bytes() <= 232448, "W8A8 GEMM needs more than 227 KB of shared memory");
+template <bool kBf16>
+constexpr size_t gemm_smem_bytes() { return sizeof(GemmSmem<kBf16>) + 1024; }
+static_assert(gemm_smem_bytes<false>() <= 232448, "int8 GEMM needs more than 227 KB of smem");
+static_assert(gemm_smem_bytes<true>() <= 232448, "bf16 GEMM needs more than 227 KB of smem");
 
 struct GemmParams {
   const float* a_scale;  // [M] (int8 only)
@@ -90,8 +104,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                 const GemmParams p) {
   constexpr int kElemK = kBf16 ? kGemmBK / 2 : kGemmBK;  // K elements per stage
+  constexpr int kGemmStages = GemmCfg<kBf16>::kStages;
   extern __shared__ uint8_t smem_raw[];
-  GemmSmem& sm = *reinterpret_cast<GemmSmem*>(
+  GemmSmem<kBf16>& sm = *reinterpret_cast<GemmSmem<kBf16>*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -193,57 +208,79 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tc_fence_after();
       const int row = m0 + quad * 32 + lane;
       const float a_s = (!kBf16 && row < p.m) ? __ldg(p.a_scale + row) : 0.f;
-      const size_t orow_off = (static_cast<size_t>(row) * p.ldo + n0) * sizeof(__nv_bfloat16);
       const uint32_t t_row = tbase + (static_cast<uint32_t>(quad * 32) << 16) +
                              static_cast<uint32_t>(buf * kGemmBN);
+      if constexpr (kBf16) {
+        uint4 (*stage)[kGemmBN / 8] = sm.stage[quad];
 #pragma unroll 1
-      for (int c = 0; c < kGemmBN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c, r);
-        tmem_wait_ld();
-        reg_fence32(r);
-        if (row < p.m && n0 + c < p.n) {
-          uint32_t w[16];
+        for (int c = 0; c < kGemmBN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c, r);
+          tmem_wait_ld();
+          reg_fence32(r);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            float x0, x1;
-            if constexpr (kBf16) {
-              x0 = __uint_as_float(r[2 * i]);
-              x1 = __uint_as_float(r[2 * i + 1]);
-            } else {
-              x0 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i],
-                                            __int2float_rn(static_cast<int>(r[2 * i]))));
-              x1 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i + 1],
-                                            __int2float_rn(static_cast<int>(r[2 * i + 1]))));
-            }
-            w[i] = pack_bf16x2(x0, x1);
+          for (int q = 0; q < 4; ++q) {
+            uint32_t w[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              w[i] = pack_bf16x2(__uint_as_float(r[8 * q + 2 * i]),
+                                 __uint_as_float(r[8 * q + 2 * i + 1]));
+            stage[lane][(c / 8 + q) ^ lane] = make_uint4(w[0], w[1], w[2], w[3]);
           }
-          // ragged last columns go by 8-column groups (n is a multiple of 8)
-          const int groups = n0 + c + 32 <= p.n ? 4 : (p.n - n0 - c) / 8;
-          const size_t col_off = orow_off + static_cast<size_t>(c) * sizeof(__nv_bfloat16);
-          if (p.out) {
-            uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + col_off);
+        }
+        // the accumulator is in shared memory: the MMAs of tile j + 2 may reuse it
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.acc_empty[buf]));
+        // rows out, a warp per row: lane l carries 16-byte chunk l
+        const size_t slot_off =
+            static_cast<size_t>(p.out_slot) * p.m * p.ldo * sizeof(__nv_bfloat16);
+        const int chunks = min(kGemmBN, p.n - n0) / 8;  // n is a multiple of 8
+        for (int rr = 0; rr < 32; ++rr) {
+          const int grow = m0 + quad * 32 + rr;
+          if (grow >= p.m) break;
+          if (lane < chunks) {
+            const uint4 v = stage[rr][lane ^ rr];
+            const size_t coff = (static_cast<size_t>(grow) * p.ldo + n0) * sizeof(__nv_bfloat16) +
+                                static_cast<size_t>(lane) * 16;
+            if (p.out) *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + coff) = v;
+            // this rank's partial into its slot of every TP rank's buffer (peer stores)
+            for (int t = 0; t < p.out_ranks; ++t)
+              *reinterpret_cast<uint4*>(p.out_peers[t] + slot_off + coff) = v;
+          }
+        }
+        __syncwarp();  // the staging rows are read before the next tile overwrites them
+      } else {
+        __nv_bfloat16* orow = p.out + static_cast<size_t>(row) * p.ldo + n0;
+#pragma unroll 1
+        for (int c = 0; c < kGemmBN; c += 32) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c, r);
+          tmem_wait_ld();
+          reg_fence32(r);
+          if (row < p.m && n0 + c < p.n) {
+            uint32_t w[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float x0 = __fmul_rn(a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i],
+                                                        __int2float_rn(static_cast<int>(r[2 * i]))));
+              const float x1 = __fmul_rn(
+                  a_s, __fmul_rn(sm.b_scale[buf][c + 2 * i + 1],
+                                 __int2float_rn(static_cast<int>(r[2 * i + 1]))));
+              w[i] = pack_bf16x2(x0, x1);
+            }
+            // ragged last columns go by 8-column groups (n is a multiple of 8)
+            const int groups = n0 + c + 32 <= p.n ? 4 : (p.n - n0 - c) / 8;
+            uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               if (q < groups) dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
           }
-          if constexpr (kBf16) {
-            // this rank's partial into its slot of every TP rank's buffer (peer stores)
-            const size_t slot_off = static_cast<size_t>(p.out_slot) * p.m * p.ldo *
-                                    sizeof(__nv_bfloat16);
-            for (int t = 0; t < p.out_ranks; ++t) {
-              uint4* dst = reinterpret_cast<uint4*>(p.out_peers[t] + slot_off + col_off);
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                if (q < groups)
-                  dst[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
-            }
-          }
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.acc_empty[buf]));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sm.acc_empty[buf]));
     }
     // the peer stores are visible to the other GPUs before the barrier that follows
     if (kBf16 && p.out_ranks > 1) __threadfence_system();
@@ -381,13 +418,13 @@ int launch_gemm(const void* a, const void* b, GemmParams prm, cudaStream_t strea
     if (dev < 64 && !configured[dev]) {
       cudaError_t e = cudaFuncSetAttribute(gemm_kernel<kBf16>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(gemm_smem_bytes()));
+                                           static_cast<int>(gemm_smem_bytes<kBf16>()));
       if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(gemm)", e);
       configured[dev] = true;
     }
   }
   const int grid = prm.tiles < sms ? prm.tiles : sms;
-  gemm_kernel<kBf16><<<grid, kGemmThreads, gemm_smem_bytes(), stream>>>(tmA, tmB, prm);
+  gemm_kernel<kBf16><<<grid, kGemmThreads, gemm_smem_bytes<kBf16>(), stream>>>(tmA, tmB, prm);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return set_cuda_error("gemm_kernel launch", e);
   return H3SA_OK;
