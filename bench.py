@@ -1179,7 +1179,7 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
         mark(3)
         q8, qs = h3sa.quantize_fp8_e4m3_per_head(q_buf.tensor[:nq].unsqueeze(0))
         mark(4)
-        attention_fwd_fp8_parts(q8[0], out, k8, v8, t8, [P(0, nq, 0, starts[4] + nq)], scale,
+        attention_fwd_fp8_parts(q8[0], out[:nq], k8, v8, t8, [P(0, nq, 0, starts[4] + nq)], scale,
                                 q_scale=qs[0], block_part=block_part, part_k_scale=ks,
                                 part_v_scale=vs, device_error=err)
         h3sa.attention_fwd(q_buf.tensor, out, k_buf.tensor, v_buf.tensor, table,
