@@ -314,6 +314,38 @@ H3SA_API int h3sa_qkv_norm_rope_scatter_paged(
     const int32_t* page_table, int32_t table_blocks, int32_t dst_start, float eps,
     int32_t* device_error, void* stream);
 
+/* The e4m3 form of the fused prologue: RMSNorm + RoPE + per-head e4m3 quantisation, writing
+ * Q and the chunk's K/V part straight into the owners' e4m3 planes and paged, head-major
+ * caches. Two passes over this rank's merged QKV shard:
+ * 1. h3sa_qkv_norm_rope_amax: amax (uint32 [3][heads], float bits, cleared first) receives
+ *    the max |x| of every plane and head over the rotated rows whose amax_rows flag is set
+ *    (uint8 [tokens], NULL: every row). With world > 1 the caller reduces the words with MAX
+ *    over the Ulysses group (e.g. an NCCL all-reduce of 3 * heads int32).
+ * 2. h3sa_qkv_norm_rope_scatter_fp8: the rows again, quantised with scale = max(amax / 448,
+ *    1e-12) (the arithmetic of h3sa_quantize_fp8_rows: same bytes), Q into peer_q8[owner]
+ *    ([world * tokens, heads / world, 128] e4m3), K / V into the owners' e4m3 pools
+ *    ([heads / world, pool8_pages * 128, 128]) at logical row dst8_start + rank * tokens + t of
+ *    page_table8; this rank's heads' scales into q_scale / k_scale / v_scale (fp32 [heads /
+ *    world]); with peer_key_pool non-NULL the bf16 K / V rows go to the bf16 pools as
+ *    h3sa_qkv_norm_rope_scatter_paged stores them.
+ * Replaces fused_qkv_qk_norm_rope_ (T/inference/fused_kernels.py:805-855), the per-head
+ * quantisation of Q and of the current K / V part (F/inference/fused_kernels.py:823-877 as
+ * called at F/streaming/attention_hook.py:1026-1049), and the exchange and cache append. */
+H3SA_API int h3sa_qkv_norm_rope_amax(const void* qkv, const void* q_weight, const void* k_weight,
+                                     const void* cos_sin, int32_t cache_rows, int32_t rotary,
+                                     const int64_t* positions, int32_t tokens, int32_t heads,
+                                     int32_t head_dim, const uint8_t* amax_rows, uint32_t* amax,
+                                     float eps, int32_t* device_error, void* stream);
+H3SA_API int h3sa_qkv_norm_rope_scatter_fp8(
+    const void* qkv, const void* q_weight, const void* k_weight, const void* cos_sin,
+    int32_t cache_rows, int32_t rotary, const int64_t* positions, int32_t tokens, int32_t heads,
+    int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, const uint64_t* peer_q8,
+    const uint64_t* peer_key_pool8, const uint64_t* peer_value_pool8, int32_t pool8_pages,
+    const int32_t* page_table8, int32_t table8_blocks, int32_t dst8_start, float* q_scale,
+    float* k_scale, float* v_scale, const uint64_t* peer_key_pool, const uint64_t* peer_value_pool,
+    int32_t pool_pages, const int32_t* page_table, int32_t table_blocks, int32_t dst_start,
+    float eps, int32_t* device_error, void* stream);
+
 /* Block-sparse selection policy for h3sa_block_mask. */
 typedef struct h3sa_mask_policy {
   int32_t mode;                   /* 0: history top-k, 1: composite */

@@ -9,6 +9,7 @@
 #include <cstring>
 
 #include "h3sa_attention.cuh"
+#include "h3sa_fp8.cuh"
 #include "h3sa_host.h"
 
 namespace h3sa {
@@ -74,7 +75,7 @@ __global__ void __launch_bounds__(256) kv_copy_kernel(const CopyParams p) {
 }
 
 // ------------------------------------------------------------------ e4m3 quantiser
-constexpr float kFp8Max = 448.0f;
+// (kFp8Max, div_by_scale and quant4: h3sa_fp8.cuh)
 
 // Element offset of (b, s, h, 0); -1 when a page lookup fails.
 __device__ __forceinline__ long long quant_offset(const QuantSpace& q, int b, int s, int h) {
@@ -148,28 +149,6 @@ __global__ void __launch_bounds__(256) quant_finalize_kernel(const float* partia
     for (int i = 1; i < (blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
     scale[blockIdx.x] = fmaxf(__fdiv_rn(r, kFp8Max), 1.0e-12f);
   }
-}
-
-// Correctly rounded x / s from y = RN(1 / s) with two residual corrections: q0 = RN(x * y) is
-// within two ulps of the quotient, one correction q1 = RN(q0 + RN(x - s * q0) * y) makes it
-// faithful, after which the residual x - s * q1 is exact in an FMA and RN(q1 + r1 * y) is the
-// correctly rounded quotient (Markstein's division theorem). Same results as an IEEE division
-// for the normal-range quotients a per-head scale produces.
-__device__ __forceinline__ float div_by_scale(float x, float s, float y) {
-  const float q0 = __fmul_rn(x, y);
-  const float q1 = __fmaf_rn(__fmaf_rn(-s, q0, x), y, q0);
-  return __fmaf_rn(__fmaf_rn(-s, q1, x), y, q1);
-}
-
-__device__ __forceinline__ uint32_t quant4(float a, float b, float c, float d, float s, float y) {
-  a = fminf(fmaxf(div_by_scale(a, s, y), -kFp8Max), kFp8Max);
-  b = fminf(fmaxf(div_by_scale(b, s, y), -kFp8Max), kFp8Max);
-  c = fminf(fmaxf(div_by_scale(c, s, y), -kFp8Max), kFp8Max);
-  d = fminf(fmaxf(div_by_scale(d, s, y), -kFp8Max), kFp8Max);
-  uint16_t lo, hi;
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(lo) : "f"(b), "f"(a));
-  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(hi) : "f"(d), "f"(c));
-  return static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
 }
 
 // One thread per 16 input bytes (8 values) -> 8 output bytes.

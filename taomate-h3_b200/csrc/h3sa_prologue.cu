@@ -17,6 +17,7 @@
 #include <cstring>
 
 #include "h3sa_attention.cuh"
+#include "h3sa_fp8.cuh"
 #include "h3sa_host.h"
 
 namespace h3sa {
@@ -26,6 +27,8 @@ enum RouteMode : int {
   kRouteInPlace = 0,  // Q and K rewritten in the merged input, V untouched (not read)
   kRoutePack = 1,     // all three planes into the Ulysses send layout [W, 3, T, H/W, d]
   kRoutePeers = 2,    // Q into the owner's [W*T, H/W, d] plane, K/V into the owner's paged pools
+  kRouteAmax = 3,     // no stores: per-(plane, head) max |x| of the rotated rows (e4m3 pass 1)
+  kRoutePeersFp8 = 4, // as kRoutePeers with e4m3 rows at the pass-1 scales (e4m3 pass 2)
 };
 
 struct PrologueParams {
@@ -51,6 +54,19 @@ struct PrologueParams {
   int table_blocks;
   int pool_pages;
   int dst_start;
+  // e4m3 passes: per-(plane, head) amax words [3][H] (float bits; pass 1 adds this rank's
+  // rows, pass 2 reads the group's maxima), the token rows pass 1 counts ([T] flags, null: all),
+  // every rank's e4m3 Q plane and paged pools with their page table, and this rank's scales
+  unsigned* amax;
+  const uint8_t* amax_rows;
+  const uint64_t* peer_q8;
+  const uint64_t* peer_k8;
+  const uint64_t* peer_v8;
+  const int* table8;
+  int table8_blocks;
+  int pool8_pages;
+  int dst8_start;
+  float* scale_out[3];  // [H / W] each: this rank's heads
 };
 
 __device__ __forceinline__ float bf16r(float x) {
@@ -80,6 +96,27 @@ __device__ __forceinline__ __nv_bfloat16* dst_row(const PrologueParams& p, int t
   __nv_bfloat16* pool = reinterpret_cast<__nv_bfloat16*>(
       static_cast<uintptr_t>(__ldg((j == 1 ? p.peer_k : p.peer_v) + w)));
   return pool + ((static_cast<size_t>(lh) * p.pool_pages + page) * kBlockN + (logical & 127)) *
+                    kHeadDim;
+}
+
+// e4m3 destination row (128 bytes) of (token t, plane j, head h) for kRoutePeersFp8; nullptr
+// when a page lookup fails.
+__device__ __forceinline__ uint8_t* dst8_row(const PrologueParams& p, int t, int j, int h) {
+  const int hl = p.heads_local;
+  const int w = (h * p.hl_recip) >> 16;
+  const int lh = h - w * hl;
+  const int row = p.rank * p.tokens + t;
+  if (j == 0) {
+    uint8_t* q = reinterpret_cast<uint8_t*>(static_cast<uintptr_t>(__ldg(p.peer_q8 + w)));
+    return q + (static_cast<size_t>(row) * hl + lh) * kHeadDim;
+  }
+  const int logical = p.dst8_start + row;
+  const int blk = logical >> 7;
+  const int page = blk < p.table8_blocks ? __ldg(p.table8 + blk) : -1;
+  if (page < 0 || page >= p.pool8_pages) return nullptr;
+  uint8_t* pool = reinterpret_cast<uint8_t*>(
+      static_cast<uintptr_t>(__ldg((j == 1 ? p.peer_k8 : p.peer_v8) + w)));
+  return pool + ((static_cast<size_t>(lh) * p.pool8_pages + page) * kBlockN + (logical & 127)) *
                     kHeadDim;
 }
 
@@ -187,13 +224,21 @@ struct PipeSmemLayout {
   int total;        // bytes of dynamic shared memory
 };
 
-__host__ __device__ inline PipeSmemLayout pipe_layout(int rows_pt, int rotary) {
+__host__ __device__ inline PipeSmemLayout pipe_layout(int rows_pt, int rotary, int aux_words = 0) {
   PipeSmemLayout l;
   l.slot_bytes = (rows_pt * kHeadDim * 2 + 127) / 128 * 128;
   l.cs_bytes = (rotary * 2 + 15) / 16 * 16;
-  // slots, cos/sin rows, full + empty barriers, per-slot position-valid flags, abort flag
-  l.total = kPipeStages * (l.slot_bytes + l.cs_bytes) + kPipeStages * 2 * 8 + kPipeStages * 4 + 16;
+  // slots, cos/sin rows, full + empty barriers, per-slot position-valid flags, abort flag,
+  // then the e4m3 passes' per-row words (amax, or scale and reciprocal)
+  l.total = kPipeStages * (l.slot_bytes + l.cs_bytes) + kPipeStages * 2 * 8 + kPipeStages * 4 + 16 +
+            aux_words * 4;
   return l;
+}
+
+// aux words of a mode: pass 1 keeps one amax per (plane, head), pass 2 a scale and its
+// reciprocal
+__host__ __device__ inline int pipe_aux_words(int mode, int heads) {
+  return mode == kRouteAmax ? 3 * heads : mode == kRoutePeersFp8 ? 6 * heads : 0;
 }
 
 template <int kMode>
@@ -202,13 +247,14 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
   extern __shared__ __align__(128) uint8_t smem[];
   const int heads = p.heads;
   const int rows_pt = (kMode == kRouteInPlace ? 2 : 3) * heads;
-  const PipeSmemLayout L = pipe_layout(rows_pt, p.rotary);
+  const PipeSmemLayout L = pipe_layout(rows_pt, p.rotary, pipe_aux_words(kMode, heads));
   uint8_t* slots = smem;
   uint8_t* cs_rows = smem + kPipeStages * L.slot_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(cs_rows + kPipeStages * L.cs_bytes);
   uint64_t* empty = full + kPipeStages;
   int* pos_ok = reinterpret_cast<int*>(empty + kPipeStages);
   volatile int* abort_flag = pos_ok + kPipeStages;
+  uint32_t* aux = reinterpret_cast<uint32_t*>(pos_ok + kPipeStages + 4);  // e4m3 passes
   const int t0 = blockIdx.x * tokens_per_cta;
   const int t1 = min(p.tokens, t0 + tokens_per_cta);
   const int n = max(0, t1 - t0);
@@ -287,6 +333,25 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
       wk[i] = f2_pack(fk[2 * i], fk[2 * i + 1]);
     }
   }
+  if constexpr (kMode == kRouteAmax || kMode == kRoutePeersFp8) {
+    // per-(plane, head) words for this CTA: zeroed maxima (pass 1), or the group's scales and
+    // their reciprocals (pass 2: scale = max(amax / 448, 1e-12) as the e4m3 quantisers set it)
+    const int nw = 3 * heads;
+    for (int k = threadIdx.x; k < nw; k += kPipeConsumerWarps * 32) {
+      if constexpr (kMode == kRouteAmax) {
+        aux[k] = 0u;
+      } else {
+        const float sc = fmaxf(__fdiv_rn(__uint_as_float(__ldcg(p.amax + k)), kFp8Max), 1.0e-12f);
+        aux[k] = __float_as_uint(sc);
+        aux[nw + k] = __float_as_uint(__frcp_rn(sc));
+        const int j = k / heads, h = k - j * heads;
+        const int w = (h * p.hl_recip) >> 16;
+        if (blockIdx.x == 0 && w == p.rank && p.scale_out[j])
+          p.scale_out[j][h - w * p.heads_local] = sc;
+      }
+    }
+    asm volatile("bar.sync 1, %0;" ::"n"(kPipeConsumerWarps * 32) : "memory");
+  }
   const int d0 = 8 * sub;
   const bool rotating = d0 < p.rotary;
   const bool low = d0 < half;
@@ -307,6 +372,7 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
       sn[0] = sr.x; sn[1] = sr.y; sn[2] = sr.z; sn[3] = sr.w;
     }
     const uint4* rows = reinterpret_cast<const uint4*>(slots + s * L.slot_bytes);
+    const bool counted = kMode != kRouteAmax || !p.amax_rows || __ldg(p.amax_rows + t) != 0;
     for (int r = hw; r < rows_pt; r += 16) {
       const int j = (r >= heads) + (r >= 2 * heads);
       const int h = r - j * heads;
@@ -315,26 +381,62 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
         if (!pv) continue;
         o = norm_rope_row(o, j == 0 ? wq : wk, p.eps, rotating, low, partner, half_mask, c, sn);
       }
-      __nv_bfloat16* dst = dst_row<kMode>(p, t, j, h);
-      if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
-      else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
+      if constexpr (kMode == kRouteAmax) {
+        if (!counted) continue;
+        float f[8];
+        unpack8(o, f);
+        float m = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) m = fmaxf(m, fabsf(f[e]));
+#pragma unroll
+        for (int x = 8; x > 0; x >>= 1) m = fmaxf(m, __shfl_xor_sync(half_mask, m, x));
+        if (sub == 0) atomicMax(aux + j * heads + h, __float_as_uint(m));
+        continue;
+      } else if constexpr (kMode == kRoutePeersFp8) {
+        const int k = j * heads + h;
+        const float sc = __uint_as_float(aux[k]);
+        const float inv = __uint_as_float(aux[3 * heads + k]);
+        float f[8];
+        unpack8(o, f);
+        const uint2 q8 = make_uint2(quant4(f[0], f[1], f[2], f[3], sc, inv),
+                                    quant4(f[4], f[5], f[6], f[7], sc, inv));
+        uint8_t* d8 = dst8_row(p, t, j, h);
+        if (d8) reinterpret_cast<uint2*>(d8)[sub] = q8;
+        else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
+        if (j == 0 || !p.peer_k) continue;  // bf16 K/V rows too when the caller keeps them
+        __nv_bfloat16* dst = dst_row<kRoutePeers>(p, t, j, h);
+        if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
+        else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
+      } else {
+        __nv_bfloat16* dst = dst_row<kMode>(p, t, j, h);
+        if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
+        else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(&empty[s]));
   }
+  if constexpr (kMode == kRouteAmax) {
+    // this CTA's maxima into the launch's words (non-negative floats order like their bits)
+    asm volatile("bar.sync 1, %0;" ::"n"(kPipeConsumerWarps * 32) : "memory");
+    for (int k = threadIdx.x; k < 3 * heads; k += kPipeConsumerWarps * 32)
+      if (aux[k]) atomicMax(p.amax + k, aux[k]);
+  }
   // stores to other GPUs: visible to them before the kernel is seen as done
-  if (kMode == kRoutePeers && p.world > 1) __threadfence_system();
+  if ((kMode == kRoutePeers || kMode == kRoutePeersFp8) && p.world > 1) __threadfence_system();
 }
 
 static int prologue_launch(const PrologueParams& p, cudaStream_t stream) {
   const int rows_pt = (p.mode == kRouteInPlace ? 2 : 3) * p.heads;
-  const PipeSmemLayout L = pipe_layout(rows_pt, p.rotary);
+  const PipeSmemLayout L = pipe_layout(rows_pt, p.rotary, pipe_aux_words(p.mode, p.heads));
   if (L.total > 227 * 1024)
     return set_error(H3SA_ERR_UNSUPPORTED, "qkv prologue: %d heads need %d bytes of staging",
                      p.heads, L.total);
   auto kernel = p.mode == kRouteInPlace ? qkv_norm_rope_pipe_kernel<kRouteInPlace>
                : p.mode == kRoutePack   ? qkv_norm_rope_pipe_kernel<kRoutePack>
-                                        : qkv_norm_rope_pipe_kernel<kRoutePeers>;
+               : p.mode == kRoutePeers  ? qkv_norm_rope_pipe_kernel<kRoutePeers>
+               : p.mode == kRouteAmax   ? qkv_norm_rope_pipe_kernel<kRouteAmax>
+                                        : qkv_norm_rope_pipe_kernel<kRoutePeersFp8>;
   if (L.total > 48 * 1024) {  // the opt-in applies to the current device
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          L.total);
@@ -487,6 +589,100 @@ int h3sa_qkv_norm_rope_scatter_paged(const void* qkv, const void* q_weight, cons
   p.peer_q = peer_q;
   p.peer_k = peer_key_pool;
   p.peer_v = peer_value_pool;
+  p.page_table = page_table;
+  p.table_blocks = table_blocks;
+  p.pool_pages = pool_pages;
+  p.dst_start = dst_start;
+  return prologue_launch(p, static_cast<cudaStream_t>(stream));
+}
+
+
+int h3sa_qkv_norm_rope_amax(const void* qkv, const void* q_weight, const void* k_weight,
+                            const void* cos_sin, int32_t cache_rows, int32_t rotary,
+                            const int64_t* positions, int32_t tokens, int32_t heads,
+                            int32_t head_dim, const uint8_t* amax_rows, uint32_t* amax, float eps,
+                            int32_t* device_error, void* stream) {
+  int rc = check_prologue(qkv, q_weight, k_weight, cos_sin, cache_rows, rotary, positions, tokens,
+                          heads, head_dim);
+  if (rc) return rc;
+  if (!amax) return set_error(H3SA_ERR_INVALID, "qkv prologue amax: null amax words");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemsetAsync(amax, 0, sizeof(uint32_t) * 3 * heads, st);
+  if (e != cudaSuccess) return set_cuda_error("cudaMemsetAsync(prologue amax)", e);
+  if (tokens == 0) return H3SA_OK;
+  PrologueParams p{};
+  p.src = static_cast<const __nv_bfloat16*>(qkv);
+  p.q_weight = static_cast<const __nv_bfloat16*>(q_weight);
+  p.k_weight = static_cast<const __nv_bfloat16*>(k_weight);
+  p.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin);
+  p.positions = reinterpret_cast<const long long*>(positions);
+  p.tokens = tokens;
+  p.heads = heads;
+  p.rotary = rotary;
+  p.cache_rows = cache_rows;
+  p.world = 1;
+  p.eps = eps;
+  p.err = device_error;
+  p.mode = kRouteAmax;
+  p.amax = amax;
+  p.amax_rows = amax_rows;
+  return prologue_launch(p, st);
+}
+
+int h3sa_qkv_norm_rope_scatter_fp8(
+    const void* qkv, const void* q_weight, const void* k_weight, const void* cos_sin,
+    int32_t cache_rows, int32_t rotary, const int64_t* positions, int32_t tokens, int32_t heads,
+    int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, const uint64_t* peer_q8,
+    const uint64_t* peer_key_pool8, const uint64_t* peer_value_pool8, int32_t pool8_pages,
+    const int32_t* page_table8, int32_t table8_blocks, int32_t dst8_start, float* q_scale,
+    float* k_scale, float* v_scale, const uint64_t* peer_key_pool, const uint64_t* peer_value_pool,
+    int32_t pool_pages, const int32_t* page_table, int32_t table_blocks, int32_t dst_start,
+    float eps, int32_t* device_error, void* stream) {
+  int rc = check_prologue(qkv, q_weight, k_weight, cos_sin, cache_rows, rotary, positions, tokens,
+                          heads, head_dim);
+  if (rc) return rc;
+  if (world <= 0 || heads % world)
+    return set_error(H3SA_ERR_INVALID, "merged QKV heads are not divisible by Ulysses");
+  if (rank < 0 || rank >= world || !amax || !peer_q8 || !peer_key_pool8 || !peer_value_pool8 ||
+      !page_table8 || pool8_pages <= 0 || table8_blocks <= 0 || dst8_start < 0)
+    return set_error(H3SA_ERR_INVALID, "qkv prologue e4m3 scatter: invalid peer or page arguments");
+  const long long end = static_cast<long long>(world) * tokens;
+  if (dst8_start + end > static_cast<long long>(table8_blocks) * kBlockN)
+    return set_error(H3SA_ERR_INVALID, "qkv prologue e4m3 scatter: rows [%d, %lld) exceed the "
+                     "e4m3 page table's %d blocks", dst8_start, dst8_start + end, table8_blocks);
+  const bool keep_bf16 = peer_key_pool != nullptr;
+  if (keep_bf16 && (!peer_value_pool || !page_table || pool_pages <= 0 || table_blocks <= 0 ||
+                    dst_start < 0 || dst_start + end > static_cast<long long>(table_blocks) * kBlockN))
+    return set_error(H3SA_ERR_INVALID, "qkv prologue e4m3 scatter: invalid bf16 pool arguments");
+  if (tokens == 0) return H3SA_OK;
+  PrologueParams p{};
+  p.src = static_cast<const __nv_bfloat16*>(qkv);
+  p.q_weight = static_cast<const __nv_bfloat16*>(q_weight);
+  p.k_weight = static_cast<const __nv_bfloat16*>(k_weight);
+  p.cos_sin = static_cast<const __nv_bfloat16*>(cos_sin);
+  p.positions = reinterpret_cast<const long long*>(positions);
+  p.tokens = tokens;
+  p.heads = heads;
+  p.rotary = rotary;
+  p.cache_rows = cache_rows;
+  p.world = world;
+  p.eps = eps;
+  p.err = device_error;
+  p.mode = kRoutePeersFp8;
+  p.rank = rank;
+  p.amax = const_cast<uint32_t*>(amax);
+  p.peer_q8 = peer_q8;
+  p.peer_k8 = peer_key_pool8;
+  p.peer_v8 = peer_value_pool8;
+  p.table8 = page_table8;
+  p.table8_blocks = table8_blocks;
+  p.pool8_pages = pool8_pages;
+  p.dst8_start = dst8_start;
+  p.scale_out[0] = q_scale;
+  p.scale_out[1] = k_scale;
+  p.scale_out[2] = v_scale;
+  p.peer_k = keep_bf16 ? peer_key_pool : nullptr;
+  p.peer_v = keep_bf16 ? peer_value_pool : nullptr;
   p.page_table = page_table;
   p.table_blocks = table_blocks;
   p.pool_pages = pool_pages;

@@ -112,4 +112,84 @@ def qkv_norm_rope_scatter_paged(qkv: torch.Tensor, q_weight: torch.Tensor, k_wei
          stream_handle(stream))
 
 
-__all__ = ["fused_qkv_qk_norm_rope_", "qkv_norm_rope_pack", "qkv_norm_rope_scatter_paged"]
+def _e4m3_shape(buf) -> tuple[int, ...]:
+    """Shape of a peer / local buffer seen as e4m3 (bf16 buffers hold two e4m3 bytes each)."""
+
+    t = buf.tensor
+    if t.dtype == torch.float8_e4m3fn:
+        return tuple(int(x) for x in t.shape)
+    if t.dtype == torch.bfloat16:
+        return tuple(int(x) for x in t.shape[:-1]) + (2 * int(t.shape[-1]),)
+    raise ValueError("e4m3 destinations must be e4m3 (or bf16-typed byte) buffers")
+
+
+def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
+                              cos_sin_cache: torch.Tensor, positions: torch.Tensor, eps: float,
+                              *, q8, key_pool8, value_pool8, page_table8: torch.Tensor,
+                              dst8_start: int, amax_rows: torch.Tensor | None = None,
+                              group=None, key_pool=None, value_pool=None,
+                              page_table: torch.Tensor | None = None, dst_start: int = 0,
+                              device_error: torch.Tensor | None = None,
+                              stream: torch.cuda.Stream | None = None
+                              ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """The fused RMSNorm + RoPE + per-head e4m3 prologue writing Q and the chunk's K/V part
+    straight into the owners' e4m3 plane and paged caches (two passes: amax, then quantise and
+    store; with more than one rank the maxima are reduced over ``group`` in between).
+
+    ``q8`` / ``key_pool8`` / ``value_pool8``: ``h3sa.peer.PeerBuffer`` / ``LocalBuffer`` of the
+    e4m3 Q plane ``[W*T, H/W, 128]`` and pools ``[H/W, pages * 128, 128]``. ``amax_rows``:
+    uint8 ``[T]`` flags of the rows the scales cover (None: all). With ``key_pool`` /
+    ``value_pool`` (+ ``page_table``, ``dst_start``) the bf16 K/V rows are stored too.
+    Returns this rank's fp32 ``[H/W]`` Q, K and V scales."""
+
+    from .kernels import PAGE_ROWS
+
+    tokens, heads, head_dim, cache, positions = _check(qkv, q_weight, k_weight, cos_sin_cache,
+                                                       positions)
+    world, rank = q8.world, q8.rank
+    if heads % world:
+        raise ValueError("merged QKV heads are not divisible by Ulysses")
+    hl = heads // world
+    if _e4m3_shape(q8) != (world * tokens, hl, head_dim):
+        raise ValueError(f"e4m3 Q plane must be [{world * tokens}, {hl}, {head_dim}]")
+    ks, vs = _e4m3_shape(key_pool8), _e4m3_shape(value_pool8)
+    if ks != vs or len(ks) != 3 or ks[0] != hl or ks[2] != head_dim or ks[1] % PAGE_ROWS:
+        raise ValueError(f"e4m3 KV pools must both be [{hl}, pages * {PAGE_ROWS}, {head_dim}]")
+    if key_pool8.world != world or value_pool8.world != world:
+        raise ValueError("Q plane and KV pools must span the same ranks")
+    if page_table8.dtype != torch.int32 or not page_table8.is_cuda:
+        raise ValueError("page_table8 must be an int32 CUDA tensor")
+    if amax_rows is not None and (amax_rows.dtype != torch.uint8 or amax_rows.numel() != tokens
+                                  or not amax_rows.is_cuda):
+        raise ValueError("amax_rows must be a uint8 CUDA tensor with one flag per token")
+    keep = key_pool is not None
+    if keep:
+        if value_pool is None or page_table is None:
+            raise ValueError("bf16 K/V destinations need both pools and their page table")
+        if (tuple(key_pool.shape) != tuple(value_pool.shape) or key_pool.shape[0] != hl
+                or key_pool.shape[1] % PAGE_ROWS or key_pool.world != world):
+            raise ValueError(f"bf16 KV pools must both be [{hl}, pages * {PAGE_ROWS}, {head_dim}]")
+    dev = qkv.device
+    amax = torch.empty(3 * heads, dtype=torch.int32, device=dev)
+    call("h3sa_qkv_norm_rope_amax", ptr(qkv), ptr(q_weight.contiguous()),
+         ptr(k_weight.contiguous()), ptr(cache), int(cache.shape[0]), int(cache.shape[1]),
+         ptr(positions), tokens, heads, head_dim, ptr(amax_rows), ptr(amax), float(eps),
+         ptr(device_error), stream_handle(stream))
+    if world > 1:  # non-negative floats order like their bits
+        torch.distributed.all_reduce(amax, op=torch.distributed.ReduceOp.MAX, group=group)
+    scales = torch.empty(3, hl, dtype=torch.float32, device=dev)
+    call("h3sa_qkv_norm_rope_scatter_fp8", ptr(qkv), ptr(q_weight.contiguous()),
+         ptr(k_weight.contiguous()), ptr(cache), int(cache.shape[0]), int(cache.shape[1]),
+         ptr(positions), tokens, heads, head_dim, world, rank, ptr(amax), ptr(q8.peer_table),
+         ptr(key_pool8.peer_table), ptr(value_pool8.peer_table), ks[1] // PAGE_ROWS,
+         ptr(page_table8), int(page_table8.numel()), int(dst8_start), ptr(scales[0]),
+         ptr(scales[1]), ptr(scales[2]),
+         ptr(key_pool.peer_table) if keep else None, ptr(value_pool.peer_table) if keep else None,
+         int(key_pool.shape[1]) // PAGE_ROWS if keep else 0, ptr(page_table),
+         int(page_table.numel()) if keep else 0, int(dst_start), float(eps), ptr(device_error),
+         stream_handle(stream))
+    return scales[0], scales[1], scales[2]
+
+
+__all__ = ["fused_qkv_qk_norm_rope_", "qkv_norm_rope_pack", "qkv_norm_rope_scatter_fp8",
+           "qkv_norm_rope_scatter_paged"]

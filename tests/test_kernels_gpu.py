@@ -309,3 +309,60 @@ def test_prologue_scatter_into_cache_matches_oracle(seq: int, heads: int, dst_st
         untouched = np.ones(pool.shape[1], dtype=bool)
         untouched[phys] = False
         assert np.all(host[:, untouched] == fill)
+
+
+@pytest.mark.parametrize("seq,heads,dst_start,masked", [(300, 4, 0, False), (517, 6, 200, True)])
+def test_prologue_scatter_fp8_matches_oracle(seq: int, heads: int, dst_start: int,
+                                             masked: bool) -> None:
+    """The fused RMSNorm + RoPE + e4m3 prologue (amax pass, then quantise-and-store) on one GPU:
+    the scales and the e4m3 bytes of Q and of the K/V part (through a shuffled page table) are
+    the oracle quantiser's on the oracle prologue's rows, the scales covering only the flagged
+    rows; the optional bf16 K/V rows equal the bf16 scatter's."""
+
+    from h3sa.kernels import PAGE_ROWS
+    from h3sa.peer import LocalBuffer
+    from h3sa.prologue import qkv_norm_rope_scatter_fp8
+    from oracle import fp8 as ofp8
+
+    inp, cs = _prologue_case(seq, heads, seed=9)
+    rng = np.random.default_rng(4)
+    pos = rng.integers(0, cs.shape[0], seq)
+    flags = np.ones(seq, np.uint8)
+    if masked:
+        flags[:37] = 0        # e.g. text rows that the media part's scales do not cover
+        flags[-11:] = 0
+    blocks = (dst_start + seq + PAGE_ROWS - 1) // PAGE_ROWS
+    pages = blocks + 2
+    table = torch.from_numpy(rng.permutation(pages)[:blocks].astype(np.int32)).cuda()
+    k8 = torch.zeros(heads, pages * PAGE_ROWS, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    v8 = torch.zeros_like(k8)
+    q8 = torch.zeros(seq, heads, 128, dtype=torch.float8_e4m3fn, device="cuda")
+    kpool = torch.zeros(heads, pages * PAGE_ROWS, 128, dtype=torch.bfloat16, device="cuda")
+    vpool = torch.zeros_like(kpool)
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    qs, ks, vs = qkv_norm_rope_scatter_fp8(
+        _cuda_bf16(inp["qkv"]), _cuda_bf16(inp["q_weight"]), _cuda_bf16(inp["k_weight"]),
+        _cuda_bf16(cs), torch.from_numpy(pos).cuda(), 1e-5, q8=LocalBuffer(q8),
+        key_pool8=LocalBuffer(k8), value_pool8=LocalBuffer(v8), page_table8=table,
+        dst8_start=dst_start, amax_rows=torch.from_numpy(flags).cuda(),
+        key_pool=LocalBuffer(kpool), value_pool=LocalBuffer(vpool), page_table=table,
+        dst_start=dst_start, device_error=err)
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    ref = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, pos, heads, 128,
+                             1e-5).reshape(seq, 3, heads, 128)
+    sel = flags.astype(bool)
+    tab = table.cpu().numpy()
+    logical = dst_start + np.arange(seq)
+    phys = tab[logical // PAGE_ROWS] * PAGE_ROWS + logical % PAGE_ROWS
+    for plane, got_scale, rows_of in ((0, qs, lambda: q8.view(torch.uint8).cpu().numpy()),
+                                      (1, ks, lambda: k8.view(torch.uint8).cpu().numpy()[:, phys].transpose(1, 0, 2)),
+                                      (2, vs, lambda: v8.view(torch.uint8).cpu().numpy()[:, phys].transpose(1, 0, 2))):
+        _, scale = ofp8.quantize_fp8_e4m3_per_head(ref[sel, plane][None])
+        assert np.array_equal(got_scale.cpu().numpy(), scale[0]), plane
+        # every row is quantised with the flagged rows' scales
+        y = np.clip(ref[:, plane] / scale[0][None, :, None], -448.0, 448.0).astype(np.float32)
+        assert np.array_equal(rows_of(), ofp8.e4m3_encode(y)), plane
+    for pool, plane in ((kpool, 1), (vpool, 2)):
+        host = pool.float().cpu().numpy()
+        assert np.array_equal(host[:, phys].transpose(1, 0, 2), ref[:, plane])
