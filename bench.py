@@ -1090,18 +1090,19 @@ def run_h3sa(args: argparse.Namespace) -> None:
 def run_tp2sp4(args: argparse.Namespace) -> None:
     """The 1080p FP8 configuration in its TP2 x SP4 layout on 8 GPUs (T/runtime/direct.py:
     169-190): TP rank t owns 12 of the 24 heads; its Ulysses group {t, t+2, t+4, t+6} trades
-    sequence rows for heads, 3 heads per GPU. Per step and rank: the fused prologue stores Q
-    into the owners' planes and K/V into the owners' bf16 chunk pools over NVLink; a peer
-    barrier; the chunk's K/V rows become one e4m3 part (its own per-head scales) after the
-    four history parts quantised at their commits; Q is quantised per head; one attention
-    launch over the parts (the 35-row pad document attends to itself in bf16); the output
-    all-to-all inside the group (NCCL) and its unpack. Timed with CUDA events, max over the
-    8 ranks. FLOPs: 4 * Nq * (Nh + Nq) * 128 per head."""
+    sequence rows for heads, 3 heads per GPU. Per step and rank: the fused RMSNorm + RoPE +
+    e4m3 prologue (an amax pass over the media rows, the maxima reduced over the group, then Q
+    and the chunk's K/V stored as e4m3 into the owners' plane and stores over NVLink, where
+    the chunk's K/V form one part with its own per-head scales after the four history parts
+    quantised at their commits; bf16 rows kept for the pad document); a peer barrier; one
+    attention launch over the parts (the 35-row pad document attends to itself in bf16); the
+    output all-to-all inside the group (NCCL) and its unpack. Timed with CUDA events, max over
+    the 8 ranks. FLOPs: 4 * Nq * (Nh + Nq) * 128 per head."""
 
     import h3sa
     from h3sa.kernels import PAGE_ROWS, attention_fwd_fp8_parts, quantize_fp8_rows
     from h3sa.peer import PeerBarrier, PeerBuffer
-    from h3sa.prologue import qkv_norm_rope_scatter_paged
+    from h3sa.prologue import qkv_norm_rope_scatter_fp8
     from h3sa.ulysses import build_parallel_context, unpack_o_recv
 
     world, rank, local = _dist()
@@ -1138,8 +1139,17 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
         starts.append(cursor)
         cursor = (cursor + n + PAGE_ROWS - 1) // PAGE_ROWS * PAGE_ROWS
     t8 = torch.arange(cursor // PAGE_ROWS, dtype=torch.int32, device=dev)
-    k8 = torch.zeros(hl, cursor, d, dtype=torch.float8_e4m3fn, device=dev)
-    v8 = torch.zeros_like(k8)
+    # e4m3 stores of every rank of the group (the chunk's part is written by its owner's peers)
+    k8_buf = PeerBuffer((hl, cursor, d // 2), group)
+    v8_buf = PeerBuffer((hl, cursor, d // 2), group)
+    q8_buf = PeerBuffer((rows, hl, d // 2), group)
+    for buf in (k8_buf, v8_buf, q8_buf):
+        buf.tensor.zero_()
+    k8 = k8_buf.tensor.view(torch.float8_e4m3fn)
+    v8 = v8_buf.tensor.view(torch.float8_e4m3fn)
+    q8_plane = q8_buf.tensor.view(torch.float8_e4m3fn)
+    # the scales cover the chunk's media rows, not the pad rows after them
+    amax_rows = ((ur * tokens + torch.arange(tokens, device=dev)) < nq).to(torch.uint8)
     ks = torch.empty(len(parts), hl, dtype=torch.float32, device=dev)
     vs = torch.empty_like(ks)
     work = torch.empty(2 * hl, dtype=torch.int32, device=dev)
@@ -1158,8 +1168,7 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
     final = torch.empty(tokens, heads_tp, d, dtype=torch.bfloat16, device=dev)
     P = h3sa.AttentionProblem
     scale = d ** -0.5
-    phases = ("prologue_scatter", "barrier", "kv_part_quant", "q_quant", "attention",
-              "o_all_to_all", "o_unpack")
+    phases = ("prologue_fp8_scatter", "barrier", "attention", "o_all_to_all", "o_unpack")
 
     def step(marks=None) -> None:
         def mark(i):
@@ -1167,28 +1176,28 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
                 marks[i].record()
 
         mark(0)
-        qkv_norm_rope_scatter_paged(merged, wq, wk, cos_sin, positions, 1e-5, q=q_buf,
-                                    key_pool=k_buf, value_pool=v_buf, page_table=table,
-                                    dst_start=0, device_error=err)
+        # RMSNorm + RoPE + e4m3: amax pass, group max, then Q and the chunk's K/V part as e4m3
+        # into the owners' plane and stores (bf16 rows kept for the pad document)
+        qs, ks_c, vs_c = qkv_norm_rope_scatter_fp8(
+            merged, wq, wk, cos_sin, positions, 1e-5, q8=q8_buf, key_pool8=k8_buf,
+            value_pool8=v8_buf, page_table8=t8, dst8_start=starts[4], amax_rows=amax_rows,
+            group=group, q=q_buf, key_pool=k_buf, value_pool=v_buf, page_table=table,
+            dst_start=0, device_error=err)
+        ks[4].copy_(ks_c)
+        vs[4].copy_(vs_c)
         mark(1)
         peer_barrier()
         mark(2)
-        quantize_fp8_rows([k_buf.tensor, v_buf.tensor], [k8, v8], [ks[4], vs[4]], work,
-                          count=nq, src_table=table, dst_start=starts[4], dst_table=t8,
-                          zero_tail=True)
-        mark(3)
-        q8, qs = h3sa.quantize_fp8_e4m3_per_head(q_buf.tensor[:nq].unsqueeze(0))
-        mark(4)
-        attention_fwd_fp8_parts(q8[0], out[:nq], k8, v8, t8, [P(0, nq, 0, starts[4] + nq)], scale,
-                                q_scale=qs[0], block_part=block_part, part_k_scale=ks,
+        attention_fwd_fp8_parts(q8_plane[:nq], out[:nq], k8, v8, t8, [P(0, nq, 0, starts[4] + nq)],
+                                scale, q_scale=qs, block_part=block_part, part_k_scale=ks,
                                 part_v_scale=vs, device_error=err)
         h3sa.attention_fwd(q_buf.tensor, out, k_buf.tensor, v_buf.tensor, table,
                            [P(nq, rows, nq, rows)], scale, device_error=err)
-        mark(5)
+        mark(3)
         torch.distributed.all_to_all_single(orecv, out, group=group)
-        mark(6)
+        mark(4)
         unpack_o_recv(orecv, final, world=sp, tokens=tokens, local_heads=hl, head_dim=d)
-        mark(7)
+        mark(5)
         # no barrier before the next step's scatter into the peers' planes and pools: a rank
         # finishes its all-to-all only after every peer has sent, i.e. finished its attention
 
@@ -1214,7 +1223,7 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
     flops_gpu = 4.0 * nq * (nh + nq) * d * hl
     peaks = _peaks()
     attn_tf = flops_gpu / (phase_ms["attention"] * 1e-3) / 1e12
-    for b in (q_buf, k_buf, v_buf):
+    for b in (q_buf, k_buf, v_buf, q8_buf, k8_buf, v8_buf):
         b.close()
     peer_barrier.close()
     if rank == 0:

@@ -326,8 +326,8 @@ H3SA_API int h3sa_qkv_norm_rope_scatter_paged(
  *    ([world * tokens, heads / world, 128] e4m3), K / V into the owners' e4m3 pools
  *    ([heads / world, pool8_pages * 128, 128]) at logical row dst8_start + rank * tokens + t of
  *    page_table8; this rank's heads' scales into q_scale / k_scale / v_scale (fp32 [heads /
- *    world]); with peer_key_pool non-NULL the bf16 K / V rows go to the bf16 pools as
- *    h3sa_qkv_norm_rope_scatter_paged stores them.
+ *    world]); with peer_q / peer_key_pool non-NULL the bf16 Q / K / V rows go to the bf16
+ *    plane and pools as h3sa_qkv_norm_rope_scatter_paged stores them.
  * Replaces fused_qkv_qk_norm_rope_ (T/inference/fused_kernels.py:805-855), the per-head
  * quantisation of Q and of the current K / V part (F/inference/fused_kernels.py:823-877 as
  * called at F/streaming/attention_hook.py:1026-1049), and the exchange and cache append. */
@@ -342,9 +342,9 @@ H3SA_API int h3sa_qkv_norm_rope_scatter_fp8(
     int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, const uint64_t* peer_q8,
     const uint64_t* peer_key_pool8, const uint64_t* peer_value_pool8, int32_t pool8_pages,
     const int32_t* page_table8, int32_t table8_blocks, int32_t dst8_start, float* q_scale,
-    float* k_scale, float* v_scale, const uint64_t* peer_key_pool, const uint64_t* peer_value_pool,
-    int32_t pool_pages, const int32_t* page_table, int32_t table_blocks, int32_t dst_start,
-    float eps, int32_t* device_error, void* stream);
+    float* k_scale, float* v_scale, const uint64_t* peer_q, const uint64_t* peer_key_pool,
+    const uint64_t* peer_value_pool, int32_t pool_pages, const int32_t* page_table,
+    int32_t table_blocks, int32_t dst_start, float eps, int32_t* device_error, void* stream);
 
 /* Block-sparse selection policy for h3sa_block_mask. */
 typedef struct h3sa_mask_policy {

@@ -403,7 +403,8 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
         uint8_t* d8 = dst8_row(p, t, j, h);
         if (d8) reinterpret_cast<uint2*>(d8)[sub] = q8;
         else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
-        if (j == 0 || !p.peer_k) continue;  // bf16 K/V rows too when the caller keeps them
+        // bf16 rows too where the caller keeps them (Q plane; K/V pools)
+        if (j == 0 ? !p.peer_q : !p.peer_k) continue;
         __nv_bfloat16* dst = dst_row<kRoutePeers>(p, t, j, h);
         if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
         else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
@@ -635,9 +636,9 @@ int h3sa_qkv_norm_rope_scatter_fp8(
     int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, const uint64_t* peer_q8,
     const uint64_t* peer_key_pool8, const uint64_t* peer_value_pool8, int32_t pool8_pages,
     const int32_t* page_table8, int32_t table8_blocks, int32_t dst8_start, float* q_scale,
-    float* k_scale, float* v_scale, const uint64_t* peer_key_pool, const uint64_t* peer_value_pool,
-    int32_t pool_pages, const int32_t* page_table, int32_t table_blocks, int32_t dst_start,
-    float eps, int32_t* device_error, void* stream) {
+    float* k_scale, float* v_scale, const uint64_t* peer_q, const uint64_t* peer_key_pool,
+    const uint64_t* peer_value_pool, int32_t pool_pages, const int32_t* page_table,
+    int32_t table_blocks, int32_t dst_start, float eps, int32_t* device_error, void* stream) {
   int rc = check_prologue(qkv, q_weight, k_weight, cos_sin, cache_rows, rotary, positions, tokens,
                           heads, head_dim);
   if (rc) return rc;
@@ -681,6 +682,7 @@ int h3sa_qkv_norm_rope_scatter_fp8(
   p.scale_out[0] = q_scale;
   p.scale_out[1] = k_scale;
   p.scale_out[2] = v_scale;
+  p.peer_q = peer_q;
   p.peer_k = keep_bf16 ? peer_key_pool : nullptr;
   p.peer_v = keep_bf16 ? peer_value_pool : nullptr;
   p.page_table = page_table;

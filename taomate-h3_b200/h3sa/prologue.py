@@ -127,7 +127,7 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
                               cos_sin_cache: torch.Tensor, positions: torch.Tensor, eps: float,
                               *, q8, key_pool8, value_pool8, page_table8: torch.Tensor,
                               dst8_start: int, amax_rows: torch.Tensor | None = None,
-                              group=None, key_pool=None, value_pool=None,
+                              group=None, q=None, key_pool=None, value_pool=None,
                               page_table: torch.Tensor | None = None, dst_start: int = 0,
                               device_error: torch.Tensor | None = None,
                               stream: torch.cuda.Stream | None = None
@@ -138,8 +138,9 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
 
     ``q8`` / ``key_pool8`` / ``value_pool8``: ``h3sa.peer.PeerBuffer`` / ``LocalBuffer`` of the
     e4m3 Q plane ``[W*T, H/W, 128]`` and pools ``[H/W, pages * 128, 128]``. ``amax_rows``:
-    uint8 ``[T]`` flags of the rows the scales cover (None: all). With ``key_pool`` /
-    ``value_pool`` (+ ``page_table``, ``dst_start``) the bf16 K/V rows are stored too.
+    uint8 ``[T]`` flags of the rows the scales cover (None: all). With ``q`` (the bf16 plane)
+    and ``key_pool`` / ``value_pool`` (+ ``page_table``, ``dst_start``) the bf16 rows are stored
+    too.
     Returns this rank's fp32 ``[H/W]`` Q, K and V scales."""
 
     from .kernels import PAGE_ROWS
@@ -169,6 +170,8 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
         if (tuple(key_pool.shape) != tuple(value_pool.shape) or key_pool.shape[0] != hl
                 or key_pool.shape[1] % PAGE_ROWS or key_pool.world != world):
             raise ValueError(f"bf16 KV pools must both be [{hl}, pages * {PAGE_ROWS}, {head_dim}]")
+    if q is not None and (tuple(q.shape) != (world * tokens, hl, head_dim) or q.world != world):
+        raise ValueError(f"bf16 Q plane must be [{world * tokens}, {hl}, {head_dim}]")
     dev = qkv.device
     amax = torch.empty(3 * heads, dtype=torch.int32, device=dev)
     call("h3sa_qkv_norm_rope_amax", ptr(qkv), ptr(q_weight.contiguous()),
@@ -183,7 +186,7 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
          ptr(positions), tokens, heads, head_dim, world, rank, ptr(amax), ptr(q8.peer_table),
          ptr(key_pool8.peer_table), ptr(value_pool8.peer_table), ks[1] // PAGE_ROWS,
          ptr(page_table8), int(page_table8.numel()), int(dst8_start), ptr(scales[0]),
-         ptr(scales[1]), ptr(scales[2]),
+         ptr(scales[1]), ptr(scales[2]), ptr(q.peer_table) if q is not None else None,
          ptr(key_pool.peer_table) if keep else None, ptr(value_pool.peer_table) if keep else None,
          int(key_pool.shape[1]) // PAGE_ROWS if keep else 0, ptr(page_table),
          int(page_table.numel()) if keep else 0, int(dst_start), float(eps), ptr(device_error),

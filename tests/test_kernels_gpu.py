@@ -339,18 +339,20 @@ def test_prologue_scatter_fp8_matches_oracle(seq: int, heads: int, dst_start: in
     q8 = torch.zeros(seq, heads, 128, dtype=torch.float8_e4m3fn, device="cuda")
     kpool = torch.zeros(heads, pages * PAGE_ROWS, 128, dtype=torch.bfloat16, device="cuda")
     vpool = torch.zeros_like(kpool)
+    qbf = torch.zeros(seq, heads, 128, dtype=torch.bfloat16, device="cuda")
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
     qs, ks, vs = qkv_norm_rope_scatter_fp8(
         _cuda_bf16(inp["qkv"]), _cuda_bf16(inp["q_weight"]), _cuda_bf16(inp["k_weight"]),
         _cuda_bf16(cs), torch.from_numpy(pos).cuda(), 1e-5, q8=LocalBuffer(q8),
         key_pool8=LocalBuffer(k8), value_pool8=LocalBuffer(v8), page_table8=table,
         dst8_start=dst_start, amax_rows=torch.from_numpy(flags).cuda(),
-        key_pool=LocalBuffer(kpool), value_pool=LocalBuffer(vpool), page_table=table,
-        dst_start=dst_start, device_error=err)
+        q=LocalBuffer(qbf), key_pool=LocalBuffer(kpool), value_pool=LocalBuffer(vpool),
+        page_table=table, dst_start=dst_start, device_error=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     ref = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, pos, heads, 128,
                              1e-5).reshape(seq, 3, heads, 128)
+    assert np.array_equal(qbf.float().cpu().numpy(), ref[:, 0])
     sel = flags.astype(bool)
     tab = table.cpu().numpy()
     logical = dst_start + np.arange(seq)

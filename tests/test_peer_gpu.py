@@ -14,6 +14,7 @@ from __future__ import annotations
 import sys
 from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -152,9 +153,36 @@ def _worker(rank: int, world: int, rendezvous: str) -> None:
             assert torch.equal(q_peer.tensor, q_ref2), "fused prologue: q plane differs"
             assert torch.equal(k_peer.tensor, k_ref2), "fused prologue: key cache differs"
             assert torch.equal(v_peer.tensor, v_ref2), "fused prologue: value cache differs"
+        # the e4m3 form: scales over the whole chunk (every rank's rows, maxima reduced over the
+        # group), Q and the chunk's K/V as e4m3 into the owners' plane and caches
+        from h3sa.prologue import qkv_norm_rope_scatter_fp8
+        from oracle import fp8 as ofp8
+
+        q8_peer = PeerBuffer((rows, hl, d // 2))
+        k8_peer = PeerBuffer((hl, pages * PAGE_ROWS, d // 2))
+        v8_peer = PeerBuffer((hl, pages * PAGE_ROWS, d // 2))
+        for buf in (q8_peer, k8_peer, v8_peer):
+            buf.tensor.zero_()
+        peer_barrier()
+        scales = qkv_norm_rope_scatter_fp8(merged, wq, wk, cos_sin, positions, 1e-5, q8=q8_peer,
+                                           key_pool8=k8_peer, value_pool8=v8_peer,
+                                           page_table8=table, dst8_start=hist, device_error=err)
+        peer_barrier()
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        chunk = slice(hist, hist + rows)
+        for plane, ref_rows, buf in ((0, q_ref2, q8_peer),
+                                     (1, k_ref2[:, chunk].transpose(0, 1), k8_peer),
+                                     (2, v_ref2[:, chunk].transpose(0, 1), v8_peer)):
+            want, scale = ofp8.quantize_fp8_e4m3_per_head(ref_rows.float().cpu().numpy()[None])
+            assert np.array_equal(scales[plane].cpu().numpy(), scale[0]), plane
+            got = buf.tensor.view(torch.uint8)
+            if plane:
+                got = got[:, chunk].transpose(0, 1)
+            assert np.array_equal(got.cpu().numpy(), want[0]), plane
         barrier()
         torch.cuda.synchronize()
-        for buf in (qkv_peer, out_peer, q_peer, k_peer, v_peer):
+        for buf in (qkv_peer, out_peer, q_peer, k_peer, v_peer, q8_peer, k8_peer, v8_peer):
             buf.close()
         peer_barrier.close()
     finally:
