@@ -1101,7 +1101,7 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
 
     import h3sa
     from h3sa.kernels import PAGE_ROWS, attention_fwd_fp8_parts, quantize_fp8_rows
-    from h3sa.peer import PeerBarrier, PeerBuffer
+    from h3sa.peer import PeerBarrier, PeerBuffer, PeerGroupMax
     from h3sa.prologue import qkv_norm_rope_scatter_fp8
     from h3sa.ulysses import build_parallel_context, unpack_o_recv
 
@@ -1132,6 +1132,7 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
     v_buf.tensor.zero_()
     err = torch.zeros(1, dtype=torch.int32, device=dev)
     peer_barrier = PeerBarrier(group, device_error=err)
+    group_max = PeerGroupMax(3 * heads_tp, group, device_error=err)
     # e4m3 store: four committed history parts of nh / 4 rows, then the chunk's part
     parts = [nh // 4] * 4 + [nq]
     starts, cursor = [], 0
@@ -1176,13 +1177,14 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
                 marks[i].record()
 
         mark(0)
-        # RMSNorm + RoPE + e4m3: amax pass, group max, then Q and the chunk's K/V part as e4m3
-        # into the owners' plane and stores (bf16 rows kept for the pad document)
+        # RMSNorm + RoPE + e4m3: amax pass, group max over peer memory, then Q and the chunk's
+        # K/V part as e4m3 into the owners' plane and stores (bf16 rows only for the pad
+        # document, the rows the scales do not cover)
         qs, ks_c, vs_c = qkv_norm_rope_scatter_fp8(
             merged, wq, wk, cos_sin, positions, 1e-5, q8=q8_buf, key_pool8=k8_buf,
             value_pool8=v8_buf, page_table8=t8, dst8_start=starts[4], amax_rows=amax_rows,
-            group=group, q=q_buf, key_pool=k_buf, value_pool=v_buf, page_table=table,
-            dst_start=0, device_error=err)
+            peer_max=group_max, q=q_buf, key_pool=k_buf, value_pool=v_buf, page_table=table,
+            dst_start=0, bf16_unflagged_only=True, device_error=err)
         ks[4].copy_(ks_c)
         vs[4].copy_(vs_c)
         mark(1)
@@ -1223,8 +1225,11 @@ def run_tp2sp4(args: argparse.Namespace) -> None:
     flops_gpu = 4.0 * nq * (nh + nq) * d * hl
     peaks = _peaks()
     attn_tf = flops_gpu / (phase_ms["attention"] * 1e-3) / 1e12
+    torch.cuda.synchronize()
+    _barrier(world)
     for b in (q_buf, k_buf, v_buf, q8_buf, k8_buf, v8_buf):
         b.close()
+    group_max.close()
     peer_barrier.close()
     if rank == 0:
         line = {

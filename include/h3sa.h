@@ -320,15 +320,26 @@ H3SA_API int h3sa_qkv_norm_rope_scatter_paged(
  * 1. h3sa_qkv_norm_rope_amax: amax (uint32 [3][heads], float bits, cleared first) receives
  *    the max |x| of every plane and head over the rotated rows whose amax_rows flag is set
  *    (uint8 [tokens], NULL: every row). With world > 1 the caller reduces the words with MAX
- *    over the Ulysses group (e.g. an NCCL all-reduce of 3 * heads int32).
+ *    over the Ulysses group: an NCCL all-reduce of 3 * heads int32, or h3sa_publish_words
+ *    into every rank's [world][3 * heads] slots followed by a peer barrier, pass 2 then
+ *    taking the maximum over amax_sets = world sets.
  * 2. h3sa_qkv_norm_rope_scatter_fp8: the rows again, quantised with scale = max(amax / 448,
  *    1e-12) (the arithmetic of h3sa_quantize_fp8_rows: same bytes), Q into peer_q8[owner]
  *    ([world * tokens, heads / world, 128] e4m3), K / V into the owners' e4m3 pools
  *    ([heads / world, pool8_pages * 128, 128]) at logical row dst8_start + rank * tokens + t of
  *    page_table8; this rank's heads' scales into q_scale / k_scale / v_scale (fp32 [heads /
  *    world]); with peer_q / peer_key_pool non-NULL the bf16 Q / K / V rows go to the bf16
- *    plane and pools as h3sa_qkv_norm_rope_scatter_paged stores them.
- * Replaces fused_qkv_qk_norm_rope_ (T/inference/fused_kernels.py:805-855), the per-head
+ *    plane and pools as h3sa_qkv_norm_rope_scatter_paged stores them (with
+ *    bf16_unflagged_only, only the rows whose amax_rows flag is 0). amax holds amax_sets
+ *    consecutive [3][heads] sets whose maximum is used. */
+/* Copies `count` words into slot `rank` of every rank's [world][count] slot array
+ * (peer_slots: device array of the `world` arrays' addresses), visible to the other GPUs when
+ * the kernel completes: the group maximum of the e4m3 prologue over peer memory. No reference
+ * counterpart (it replaces a small all-reduce). */
+H3SA_API int h3sa_publish_words(const uint32_t* words, const uint64_t* peer_slots, int32_t world,
+                                int32_t rank, int32_t count, void* stream);
+/* The two passes of the e4m3 prologue described above. Together they replace
+ * fused_qkv_qk_norm_rope_ (T/inference/fused_kernels.py:805-855), the per-head
  * quantisation of Q and of the current K / V part (F/inference/fused_kernels.py:823-877 as
  * called at F/streaming/attention_hook.py:1026-1049), and the exchange and cache append. */
 H3SA_API int h3sa_qkv_norm_rope_amax(const void* qkv, const void* q_weight, const void* k_weight,
@@ -339,7 +350,8 @@ H3SA_API int h3sa_qkv_norm_rope_amax(const void* qkv, const void* q_weight, cons
 H3SA_API int h3sa_qkv_norm_rope_scatter_fp8(
     const void* qkv, const void* q_weight, const void* k_weight, const void* cos_sin,
     int32_t cache_rows, int32_t rotary, const int64_t* positions, int32_t tokens, int32_t heads,
-    int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, const uint64_t* peer_q8,
+    int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, int32_t amax_sets,
+    const uint8_t* amax_rows, int32_t bf16_unflagged_only, const uint64_t* peer_q8,
     const uint64_t* peer_key_pool8, const uint64_t* peer_value_pool8, int32_t pool8_pages,
     const int32_t* page_table8, int32_t table8_blocks, int32_t dst8_start, float* q_scale,
     float* k_scale, float* v_scale, const uint64_t* peer_q, const uint64_t* peer_key_pool,

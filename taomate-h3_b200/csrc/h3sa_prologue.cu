@@ -58,7 +58,9 @@ struct PrologueParams {
   // rows, pass 2 reads the group's maxima), the token rows pass 1 counts ([T] flags, null: all),
   // every rank's e4m3 Q plane and paged pools with their page table, and this rank's scales
   unsigned* amax;
+  int amax_sets;             // pass 2: maxima over this many [3][H] sets of words
   const uint8_t* amax_rows;
+  int bf16_unflagged_only;   // pass 2: bf16 copies only of the rows amax_rows leaves out
   const uint64_t* peer_q8;
   const uint64_t* peer_k8;
   const uint64_t* peer_v8;
@@ -341,7 +343,9 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
       if constexpr (kMode == kRouteAmax) {
         aux[k] = 0u;
       } else {
-        const float sc = fmaxf(__fdiv_rn(__uint_as_float(__ldcg(p.amax + k)), kFp8Max), 1.0e-12f);
+        unsigned a = 0u;
+        for (int g = 0; g < p.amax_sets; ++g) a = max(a, __ldcg(p.amax + g * nw + k));
+        const float sc = fmaxf(__fdiv_rn(__uint_as_float(a), kFp8Max), 1.0e-12f);
         aux[k] = __float_as_uint(sc);
         aux[nw + k] = __float_as_uint(__frcp_rn(sc));
         const int j = k / heads, h = k - j * heads;
@@ -372,7 +376,7 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
       sn[0] = sr.x; sn[1] = sr.y; sn[2] = sr.z; sn[3] = sr.w;
     }
     const uint4* rows = reinterpret_cast<const uint4*>(slots + s * L.slot_bytes);
-    const bool counted = kMode != kRouteAmax || !p.amax_rows || __ldg(p.amax_rows + t) != 0;
+    const bool counted = !p.amax_rows || __ldg(p.amax_rows + t) != 0;
     for (int r = hw; r < rows_pt; r += 16) {
       const int j = (r >= heads) + (r >= 2 * heads);
       const int h = r - j * heads;
@@ -403,8 +407,9 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
         uint8_t* d8 = dst8_row(p, t, j, h);
         if (d8) reinterpret_cast<uint2*>(d8)[sub] = q8;
         else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
-        // bf16 rows too where the caller keeps them (Q plane; K/V pools)
-        if (j == 0 ? !p.peer_q : !p.peer_k) continue;
+        // bf16 rows too where the caller keeps them (Q plane; K/V pools), optionally only the
+        // rows the e4m3 scales leave out
+        if ((j == 0 ? !p.peer_q : !p.peer_k) || (p.bf16_unflagged_only && counted)) continue;
         __nv_bfloat16* dst = dst_row<kRoutePeers>(p, t, j, h);
         if (dst) reinterpret_cast<uint4*>(dst)[sub] = o;
         else if (sub == 0 && p.err) atomicOr(p.err, kErrBadPage);
@@ -425,6 +430,17 @@ __global__ void __launch_bounds__(kPipeThreads, 3) qkv_norm_rope_pipe_kernel(con
   }
   // stores to other GPUs: visible to them before the kernel is seen as done
   if ((kMode == kRoutePeers || kMode == kRoutePeersFp8) && p.world > 1) __threadfence_system();
+}
+
+// CTA t copies `count` words into slot `rank` of rank t's [world][count] slot array (peer
+// stores), then makes them visible beyond this GPU before the kernel completes.
+__global__ void __launch_bounds__(256) publish_words_kernel(const uint32_t* words,
+                                                            const uint64_t* peer_slots, int rank,
+                                                            int count) {
+  uint32_t* dst = reinterpret_cast<uint32_t*>(static_cast<uintptr_t>(__ldg(peer_slots + blockIdx.x))) +
+                  static_cast<size_t>(rank) * count;
+  for (int i = threadIdx.x; i < count; i += blockDim.x) dst[i] = __ldcg(words + i);
+  __threadfence_system();
 }
 
 static int prologue_launch(const PrologueParams& p, cudaStream_t stream) {
@@ -630,10 +646,23 @@ int h3sa_qkv_norm_rope_amax(const void* qkv, const void* q_weight, const void* k
   return prologue_launch(p, st);
 }
 
+int h3sa_publish_words(const uint32_t* words, const uint64_t* peer_slots, int32_t world,
+                       int32_t rank, int32_t count, void* stream) {
+  if (!words || !peer_slots || world < 1 || rank < 0 || rank >= world || count < 0)
+    return set_error(H3SA_ERR_INVALID, "publish_words: invalid arguments");
+  if (count == 0) return H3SA_OK;
+  publish_words_kernel<<<world, 256, 0, static_cast<cudaStream_t>(stream)>>>(words, peer_slots,
+                                                                             rank, count);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_cuda_error("publish_words launch", e);
+  return H3SA_OK;
+}
+
 int h3sa_qkv_norm_rope_scatter_fp8(
     const void* qkv, const void* q_weight, const void* k_weight, const void* cos_sin,
     int32_t cache_rows, int32_t rotary, const int64_t* positions, int32_t tokens, int32_t heads,
-    int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, const uint64_t* peer_q8,
+    int32_t head_dim, int32_t world, int32_t rank, const uint32_t* amax, int32_t amax_sets,
+    const uint8_t* amax_rows, int32_t bf16_unflagged_only, const uint64_t* peer_q8,
     const uint64_t* peer_key_pool8, const uint64_t* peer_value_pool8, int32_t pool8_pages,
     const int32_t* page_table8, int32_t table8_blocks, int32_t dst8_start, float* q_scale,
     float* k_scale, float* v_scale, const uint64_t* peer_q, const uint64_t* peer_key_pool,
@@ -644,6 +673,11 @@ int h3sa_qkv_norm_rope_scatter_fp8(
   if (rc) return rc;
   if (world <= 0 || heads % world)
     return set_error(H3SA_ERR_INVALID, "merged QKV heads are not divisible by Ulysses");
+  if (amax_sets < 1 || amax_sets > world)
+    return set_error(H3SA_ERR_INVALID, "qkv prologue e4m3 scatter: %d amax sets for %d ranks",
+                     amax_sets, world);
+  if (bf16_unflagged_only && !amax_rows)
+    return set_error(H3SA_ERR_INVALID, "qkv prologue e4m3 scatter: unflagged bf16 rows need flags");
   if (rank < 0 || rank >= world || !amax || !peer_q8 || !peer_key_pool8 || !peer_value_pool8 ||
       !page_table8 || pool8_pages <= 0 || table8_blocks <= 0 || dst8_start < 0)
     return set_error(H3SA_ERR_INVALID, "qkv prologue e4m3 scatter: invalid peer or page arguments");
@@ -672,6 +706,9 @@ int h3sa_qkv_norm_rope_scatter_fp8(
   p.mode = kRoutePeersFp8;
   p.rank = rank;
   p.amax = const_cast<uint32_t*>(amax);
+  p.amax_sets = amax_sets;
+  p.amax_rows = amax_rows;
+  p.bf16_unflagged_only = bf16_unflagged_only ? 1 : 0;
   p.peer_q8 = peer_q8;
   p.peer_k8 = peer_key_pool8;
   p.peer_v8 = peer_value_pool8;

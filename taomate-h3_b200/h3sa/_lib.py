@@ -112,8 +112,9 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "h3sa_qkv_norm_rope_amax": (
         ctypes.c_int, [_P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _P, _P, _F, _P, _P]),
     "h3sa_qkv_norm_rope_scatter_fp8": (
-        ctypes.c_int, [_P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _P, _P, _P, _I, _P, _I,
-                       _I, _P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _F, _P, _P]),
+        ctypes.c_int, [_P, _P, _P, _P, _I, _I, _P, _I, _I, _I, _I, _I, _P, _I, _P, _I, _P, _P, _P,
+                       _I, _P, _I, _I, _P, _P, _P, _P, _P, _P, _I, _P, _I, _I, _F, _P, _P]),
+    "h3sa_publish_words": (ctypes.c_int, [_P, _P, _I, _I, _I, _P]),
     "h3sa_block_mask": (
         ctypes.c_int,
         [_P, _I, _I, _I, _I, _I, _P, _I, _P, _I, ctypes.POINTER(MaskPolicy), _P, _P, _I, _P, _P],

@@ -131,6 +131,44 @@ class PeerBarrier:
         self.flags.close()
 
 
+class PeerGroupMax:
+    """Maximum over the group's ranks of a small vector of non-negative int32 words, over peer
+    memory: each rank stores its words into its slot of every rank's slot array
+    (``h3sa_publish_words``), one peer barrier, and every rank then holds all ranks' words
+    (the consumer takes the maximum). Two slot sets alternate, so a set is rewritten only
+    after every rank has passed the barrier of the call in between. Collective to construct."""
+
+    def __init__(self, count: int, group=None, device_error: torch.Tensor | None = None) -> None:
+        import torch.distributed as dist
+
+        self.count = int(count)
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.slots = PeerBuffer((2, self.world, 2 * self.count), group)  # int32 words
+        self.slots.tensor.zero_()
+        self.barrier = PeerBarrier(group, device_error=device_error)
+        set_bytes = self.world * self.count * 4
+        self._tables = [torch.tensor([a + s * set_bytes for a in self.slots.addresses],
+                                     dtype=torch.int64, device="cuda") for s in range(2)]
+        self._calls = 0
+
+    def __call__(self, words: torch.Tensor, stream: torch.cuda.Stream | None = None) -> torch.Tensor:
+        """int32 ``[world * count]``: every rank's words (rank-major), once all have arrived."""
+
+        if words.dtype != torch.int32 or words.numel() != self.count or not words.is_cuda:
+            raise ValueError(f"PeerGroupMax takes {self.count} int32 CUDA words")
+        s = self._calls & 1
+        self._calls += 1
+        call("h3sa_publish_words", ptr(words), ptr(self._tables[s]), self.world, self.rank,
+             self.count, stream_handle(stream))
+        self.barrier(stream)
+        return self.slots.tensor[s].view(torch.int32).reshape(-1)
+
+    def close(self) -> None:
+        self.barrier.close()
+        self.slots.close()
+
+
 def barrier(group=None, flag: torch.Tensor | None = None) -> None:
     """Stream-ordered barrier: a one-element all-reduce. Kernels enqueued after it on any rank
     start after every rank's kernels enqueued before it have finished."""
@@ -236,5 +274,5 @@ def attention_fwd_scatter(
          out.rank * heads, ptr(device_error), stream_handle(stream))
 
 
-__all__ = ["LocalBuffer", "PeerBarrier", "PeerBuffer", "attention_fwd_scatter", "barrier", "scatter_qkv",
+__all__ = ["LocalBuffer", "PeerBarrier", "PeerBuffer", "PeerGroupMax", "attention_fwd_scatter", "barrier", "scatter_qkv",
            "scatter_qkv_paged"]

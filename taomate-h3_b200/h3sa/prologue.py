@@ -127,8 +127,9 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
                               cos_sin_cache: torch.Tensor, positions: torch.Tensor, eps: float,
                               *, q8, key_pool8, value_pool8, page_table8: torch.Tensor,
                               dst8_start: int, amax_rows: torch.Tensor | None = None,
-                              group=None, q=None, key_pool=None, value_pool=None,
-                              page_table: torch.Tensor | None = None, dst_start: int = 0,
+                              group=None, peer_max=None, q=None, key_pool=None,
+                              value_pool=None, page_table: torch.Tensor | None = None,
+                              dst_start: int = 0, bf16_unflagged_only: bool = False,
                               device_error: torch.Tensor | None = None,
                               stream: torch.cuda.Stream | None = None
                               ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
@@ -140,8 +141,10 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
     e4m3 Q plane ``[W*T, H/W, 128]`` and pools ``[H/W, pages * 128, 128]``. ``amax_rows``:
     uint8 ``[T]`` flags of the rows the scales cover (None: all). With ``q`` (the bf16 plane)
     and ``key_pool`` / ``value_pool`` (+ ``page_table``, ``dst_start``) the bf16 rows are stored
-    too.
-    Returns this rank's fp32 ``[H/W]`` Q, K and V scales."""
+    too (only the unflagged ones with ``bf16_unflagged_only``). With more than one rank the
+    maxima are reduced over ``group`` by NCCL, or over peer memory with ``peer_max`` (an
+    ``h3sa.peer.PeerGroupMax`` of 3 * heads words). Returns this rank's fp32 ``[H/W]`` Q, K
+    and V scales."""
 
     from .kernels import PAGE_ROWS
 
@@ -172,18 +175,26 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
             raise ValueError(f"bf16 KV pools must both be [{hl}, pages * {PAGE_ROWS}, {head_dim}]")
     if q is not None and (tuple(q.shape) != (world * tokens, hl, head_dim) or q.world != world):
         raise ValueError(f"bf16 Q plane must be [{world * tokens}, {hl}, {head_dim}]")
+    if bf16_unflagged_only and amax_rows is None:
+        raise ValueError("bf16_unflagged_only needs amax_rows")
+    if peer_max is not None and (peer_max.count != 3 * heads or peer_max.world != world):
+        raise ValueError(f"peer_max must carry {3 * heads} words over {world} ranks")
     dev = qkv.device
     amax = torch.empty(3 * heads, dtype=torch.int32, device=dev)
     call("h3sa_qkv_norm_rope_amax", ptr(qkv), ptr(q_weight.contiguous()),
          ptr(k_weight.contiguous()), ptr(cache), int(cache.shape[0]), int(cache.shape[1]),
          ptr(positions), tokens, heads, head_dim, ptr(amax_rows), ptr(amax), float(eps),
          ptr(device_error), stream_handle(stream))
-    if world > 1:  # non-negative floats order like their bits
+    sets, words = 1, amax
+    if world > 1 and peer_max is not None:
+        words, sets = peer_max(amax), world
+    elif world > 1:  # non-negative floats order like their bits
         torch.distributed.all_reduce(amax, op=torch.distributed.ReduceOp.MAX, group=group)
     scales = torch.empty(3, hl, dtype=torch.float32, device=dev)
     call("h3sa_qkv_norm_rope_scatter_fp8", ptr(qkv), ptr(q_weight.contiguous()),
          ptr(k_weight.contiguous()), ptr(cache), int(cache.shape[0]), int(cache.shape[1]),
-         ptr(positions), tokens, heads, head_dim, world, rank, ptr(amax), ptr(q8.peer_table),
+         ptr(positions), tokens, heads, head_dim, world, rank, ptr(words), sets, ptr(amax_rows),
+         1 if bf16_unflagged_only else 0, ptr(q8.peer_table),
          ptr(key_pool8.peer_table), ptr(value_pool8.peer_table), ks[1] // PAGE_ROWS,
          ptr(page_table8), int(page_table8.numel()), int(dst8_start), ptr(scales[0]),
          ptr(scales[1]), ptr(scales[2]), ptr(q.peer_table) if q is not None else None,

@@ -311,13 +311,16 @@ def test_prologue_scatter_into_cache_matches_oracle(seq: int, heads: int, dst_st
         assert np.all(host[:, untouched] == fill)
 
 
-@pytest.mark.parametrize("seq,heads,dst_start,masked", [(300, 4, 0, False), (517, 6, 200, True)])
+@pytest.mark.parametrize("seq,heads,dst_start,masked,unflagged_only",
+                         [(300, 4, 0, False, False), (517, 6, 200, True, False),
+                          (517, 6, 200, True, True)])
 def test_prologue_scatter_fp8_matches_oracle(seq: int, heads: int, dst_start: int,
-                                             masked: bool) -> None:
+                                             masked: bool, unflagged_only: bool) -> None:
     """The fused RMSNorm + RoPE + e4m3 prologue (amax pass, then quantise-and-store) on one GPU:
     the scales and the e4m3 bytes of Q and of the K/V part (through a shuffled page table) are
     the oracle quantiser's on the oracle prologue's rows, the scales covering only the flagged
-    rows; the optional bf16 K/V rows equal the bf16 scatter's."""
+    rows; the optional bf16 rows equal the bf16 scatter's (only the unflagged ones, the flagged
+    ones left untouched, when asked)."""
 
     from h3sa.kernels import PAGE_ROWS
     from h3sa.peer import LocalBuffer
@@ -347,13 +350,17 @@ def test_prologue_scatter_fp8_matches_oracle(seq: int, heads: int, dst_start: in
         key_pool8=LocalBuffer(k8), value_pool8=LocalBuffer(v8), page_table8=table,
         dst8_start=dst_start, amax_rows=torch.from_numpy(flags).cuda(),
         q=LocalBuffer(qbf), key_pool=LocalBuffer(kpool), value_pool=LocalBuffer(vpool),
-        page_table=table, dst_start=dst_start, device_error=err)
+        page_table=table, dst_start=dst_start, bf16_unflagged_only=unflagged_only,
+        device_error=err)
     torch.cuda.synchronize()
     assert int(err.item()) == 0
     ref = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, pos, heads, 128,
                              1e-5).reshape(seq, 3, heads, 128)
-    assert np.array_equal(qbf.float().cpu().numpy(), ref[:, 0])
     sel = flags.astype(bool)
+    bf16_rows = ~sel if unflagged_only else np.ones(seq, dtype=bool)
+    host_q = qbf.float().cpu().numpy()
+    assert np.array_equal(host_q[bf16_rows], ref[bf16_rows, 0])
+    assert np.all(host_q[~bf16_rows] == 0)
     tab = table.cpu().numpy()
     logical = dst_start + np.arange(seq)
     phys = tab[logical // PAGE_ROWS] * PAGE_ROWS + logical % PAGE_ROWS
@@ -366,5 +373,6 @@ def test_prologue_scatter_fp8_matches_oracle(seq: int, heads: int, dst_start: in
         y = np.clip(ref[:, plane] / scale[0][None, :, None], -448.0, 448.0).astype(np.float32)
         assert np.array_equal(rows_of(), ofp8.e4m3_encode(y)), plane
     for pool, plane in ((kpool, 1), (vpool, 2)):
-        host = pool.float().cpu().numpy()
-        assert np.array_equal(host[:, phys].transpose(1, 0, 2), ref[:, plane])
+        host = pool.float().cpu().numpy()[:, phys].transpose(1, 0, 2)
+        assert np.array_equal(host[bf16_rows], ref[bf16_rows, plane])
+        assert np.all(host[~bf16_rows] == 0)

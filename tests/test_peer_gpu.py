@@ -180,10 +180,32 @@ def _worker(rank: int, world: int, rendezvous: str) -> None:
             if plane:
                 got = got[:, chunk].transpose(0, 1)
             assert np.array_equal(got.cpu().numpy(), want[0]), plane
+        # the group maximum over peer memory instead of NCCL, three calls (both slot sets and
+        # a reuse): the same scales and bytes
+        from h3sa.peer import PeerGroupMax
+
+        group_max = PeerGroupMax(3 * heads, device_error=err)
+        first = [b.tensor.clone() for b in (q8_peer, k8_peer, v8_peer)]
+        for _ in range(3):
+            for buf in (q8_peer, k8_peer, v8_peer):
+                buf.tensor.zero_()
+            peer_barrier()
+            again = qkv_norm_rope_scatter_fp8(merged, wq, wk, cos_sin, positions, 1e-5,
+                                              q8=q8_peer, key_pool8=k8_peer, value_pool8=v8_peer,
+                                              page_table8=table, dst8_start=hist,
+                                              peer_max=group_max, device_error=err)
+            peer_barrier()
+            torch.cuda.synchronize()
+            assert int(err.item()) == 0
+            for a, b in zip(scales, again):
+                assert torch.equal(a, b), "peer group max: scales differ"
+            for a, b in zip(first, (q8_peer, k8_peer, v8_peer)):
+                assert torch.equal(a, b.tensor), "peer group max: e4m3 bytes differ"
         barrier()
         torch.cuda.synchronize()
         for buf in (qkv_peer, out_peer, q_peer, k_peer, v_peer, q8_peer, k8_peer, v8_peer):
             buf.close()
+        group_max.close()
         peer_barrier.close()
     finally:
         torch.distributed.barrier()
