@@ -105,3 +105,23 @@ def hook_topk_inputs(step: int, heads: int = 2, head_dim: int = 128) -> dict:
     x["k"] = bf16(x["k"] + offset)
     x["q"] = bf16(x["q"] + offset)
     return x
+
+
+# SOL-Attn cases: (query rows, key rows, heads, tau, sink tokens)
+SOL_CASES = ((150, 700, 2, 0.5, 200), (64, 1283, 1, 1.0, 0), (200, 640, 3, -0.5, 130))
+
+
+def sol_inputs(case: int, head_dim: int = 128) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """bf16-exact float32 query / key / value [N, H, D] with block-clustered keys (each 64-row
+    key block drawn around its own centre), so that the routing keeps some blocks and not
+    others."""
+
+    nq, nk, heads, _, _ = SOL_CASES[case]
+    rng = np.random.default_rng(700 + case)
+    kb = (nk + 63) // 64
+    centre = rng.standard_normal((kb, heads, head_dim)).astype(np.float32)
+    k = 0.6 * rng.standard_normal((nk, heads, head_dim)).astype(np.float32)
+    k += np.repeat(centre, 64, axis=0)[:nk]
+    q = rng.standard_normal((nq, heads, head_dim)).astype(np.float32)
+    v = rng.standard_normal((nk, heads, head_dim)).astype(np.float32)
+    return bf16(q), bf16(k), bf16(v)

@@ -42,6 +42,9 @@ them from the seeds recorded in each fixture. Fixtures:
 * w8a8.npz       the reference's int8 weight quantiser _quantize_weight
                  (T/inference/w8a8.py:56-63) on a bf16 weight with outliers and an all-zero
                  row (the 1e-12 scale floor).
+* sol.npz        the SOL-Attn rectangular adapter (F/inference/sol_attention.py:366-598),
+                 its Triton kernels run by Triton's CPU interpreter with float32 buffers, on
+                 three block-clustered cases: outputs and the four telemetry counts.
 * topk.npz       key summaries of the FL2AV segmented-FP8 CleanAVKVCache
                  (F/streaming/cache.py:836-855) over six commits and after a sink + recent
                  retention, with the commit-level top-k selection of the segmented top-k
@@ -478,6 +481,39 @@ def make_w8a8(path: Path) -> None:
     np.savez(path, weight=wb, q=q.numpy(), scale=scale.numpy())
 
 # ----------------------------------------------------------------------------- ulysses
+def make_sol(path: Path) -> None:
+    """The reference SOL-Attn adapter (F/inference/sol_attention.py:366-598) through Triton's
+    CPU interpreter. The interpreter mishandles bf16 buffers, so the run keeps every buffer
+    in float32 (torch.bfloat16 stands for float32 during the call): the summaries and the
+    probabilities are not rounded to bf16, the output still is (its tl.bfloat16 cast)."""
+
+    import subprocess
+
+    code = (
+        "import os, sys, numpy as np\n"
+        "os.environ['TRITON_INTERPRET'] = '1'\n"
+        f"sys.path.insert(0, {str(REF / 'src' / 'taomate-fl2av' / 'src')!r})\n"
+        f"sys.path.insert(0, {str(HERE)!r})\n"
+        "import torch\n"
+        "from digitalhuman_h3.inference.sol_attention import sol_attn_rectangular\n"
+        "from inputs import SOL_CASES, sol_inputs\n"
+        "out = {}\n"
+        "for c, (nq, nk, h, tau, sink) in enumerate(SOL_CASES):\n"
+        "    q, k, v = (torch.from_numpy(a) for a in sol_inputs(c))\n"
+        "    tel = torch.zeros(4, dtype=torch.int64)\n"
+        "    saved, torch.bfloat16 = torch.bfloat16, torch.float32\n"
+        "    try:\n"
+        "        o = sol_attn_rectangular(q, k, v, scale=128 ** -0.5, tau=tau, sink_tokens=sink,\n"
+        "                                 telemetry_counts=tel)\n"
+        "    finally:\n"
+        "        torch.bfloat16 = saved\n"
+        "    out[f'out{c}'] = (o.numpy().view(np.uint32) >> 16).astype(np.uint16)  # bf16 bits\n"
+        "    out[f'telemetry{c}'] = tel.numpy()\n"
+        f"np.savez({str(path)!r}, **out)\n"
+    )
+    subprocess.run([sys.executable, "-c", code], check=True)
+
+
 def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import datetime
 
@@ -570,7 +606,7 @@ def main() -> None:
               "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
               "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f,
               "topk.npz": make_topk, "hook_f.npz": make_hook_f,
-              "hook_topk.npz": make_hook_topk, "w8a8.npz": make_w8a8}
+              "hook_topk.npz": make_hook_topk, "w8a8.npz": make_w8a8, "sol.npz": make_sol}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

@@ -301,3 +301,27 @@ def test_w8a8_weight_quantiser_matches_reference() -> None:
     out = ow8.scaled_mm(qa, sa, q, scale)
     ref = (qa.astype(np.float64) @ q.astype(np.float64).T) * sa.astype(np.float64) * scale.reshape(1, -1)
     assert np.allclose(out, ref, rtol=2 ** -7, atol=1e-30)
+
+
+def test_sol_attention_matches_reference() -> None:
+    """The SOL-Attn oracle against the reference adapter run by Triton's CPU interpreter with
+    float32 buffers (tests/golden/make_golden.py): the four routing counts are equal, and the
+    outputs are equal after the interpreter's bf16 cast, which truncates (a GPU rounds to
+    nearest): at most one bf16 unit apart, in a handful of elements."""
+
+    from inputs import SOL_CASES, sol_inputs
+
+    from oracle import sol_attention as osol
+
+    g = load("sol.npz")
+    for c, (_, _, _, tau, sink) in enumerate(SOL_CASES):
+        q, k, v = (torch.from_numpy(a) for a in sol_inputs(c))
+        out, _, margin, tele = osol.sol_attn_rectangular(q, k, v, scale=128 ** -0.5, tau=tau,
+                                                         sink_tokens=sink,
+                                                         summary_dtype=torch.float32)
+        assert tele.tolist() == g[f"telemetry{c}"].tolist(), c
+        assert float(margin.abs().min()) > 1e-4, c  # no routing decision is a near tie
+        want = bf16_from_bits(g[f"out{c}"])
+        got = bf16_from_bits(out.numpy().view(np.uint32) >> 16)  # truncated, as the interpreter
+        ulps = ulp_distance_bf16(got, want)
+        assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3, (c, ulps.max(), (ulps > 0).mean())
