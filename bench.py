@@ -436,7 +436,7 @@ def _time_launch(fn, iters: int) -> float:
     return a.elapsed_time(b) / iters
 
 
-VARIANTS = ("fp8", "sparse", "480p", "feeders", "w8a8")
+VARIANTS = ("fp8", "sparse", "480p", "feeders", "w8a8", "sol")
 
 
 def w8a8_projection(peaks: dict, iters: int = 20) -> dict:
@@ -603,6 +603,8 @@ def _variants(peaks: dict, iters: int = 10, only: str | None = None) -> dict:
         return {"feeders": feeders(peaks, iters)}
     if only == "w8a8":
         return w8a8_projection(peaks, iters)
+    if only == "sol":
+        return _variant_sol(peaks, iters, dev, g)
     for name, fn in (("fp8", _variant_fp8), ("sparse", _variant_sparse), ("480p", _variant_480p)):
         if only in (None, name):
             out.update(fn(peaks, iters, dev, g, pools))
@@ -761,6 +763,76 @@ def _variant_sparse(peaks: dict, iters: int, dev: torch.device, g: torch.Generat
         "ms": ms, "tflops_on_kept_blocks": tf, "kept_block_fraction": density, "heads": heads,
         "queries": nq, "keys": nk,
         "roofline": {"bound": "tensor", "peak": peaks["bf16"], "frac": tf / peaks["bf16"]}}
+    return out
+
+
+def _variant_sol(peaks: dict, iters: int, dev: torch.device, g: torch.Generator) -> dict:
+    """SOL-Attn at 768p (12509 media queries; keys = the chunk's 12509 rows as the exact sink,
+    then 16384 history rows routed, tau 1.0 as the FL2AV runtime's default), for the SP=8
+    per-GPU shape (3 heads) and one GPU (24 heads), against this repo's dense kernel over the
+    same keys. Keys are drawn around per-64-row-block centres (N(0,1) centres, N(0, 0.6^2)
+    rows) so that the routing has something to select. `mma_tflops` counts the tensor-core
+    work the attention kernel issues (per item: S = Q K^T and O += P V at M = 128, N / K = 64);
+    `dense_equiv_tflops` counts the dense attention the call replaces."""
+
+    import h3sa
+    from h3sa.kernels import PAGE_ROWS
+    from h3sa.sol_attention import sol_attn_rectangular
+
+    d = CFG["head_dim"]
+    nq, nh = CFG["video"] + CFG["audio"], CFG["history"]
+    nk = nq + nh
+    kb = (nk + 63) // 64
+    out = {}
+    for heads in (3, 24):
+        q = torch.randn(nq, heads, d, device=dev, generator=g).to(torch.bfloat16)
+        centre = torch.randn(kb, heads, d, device=dev, generator=g)
+        k = (0.6 * torch.randn(nk, heads, d, device=dev, generator=g)
+             + centre.repeat_interleave(64, 0)[:nk]).to(torch.bfloat16)
+        v = torch.randn(nk, heads, d, device=dev, generator=g).to(torch.bfloat16)
+        qb = (nq + 63) // 64
+        mask = torch.empty(heads, qb, (kb + 31) // 32, dtype=torch.int32, device=dev)
+        tele = torch.zeros(4, dtype=torch.int64, device=dev)
+        sol_attn_rectangular(q, k, v, scale=d ** -0.5, tau=1.0, sink_tokens=nq,
+                             telemetry_counts=tele, exact_blocks=mask)
+        ms = _time_launch(lambda: sol_attn_rectangular(q, k, v, scale=d ** -0.5, tau=1.0,
+                                                       sink_tokens=nq, exact_blocks=mask), iters)
+        # items per (128-row tile, head): chunks holding an approximate block for either half,
+        # plus the union of the two halves' exact blocks
+        bits = ((mask.view(torch.int32).unsqueeze(-1) >> torch.arange(32, device=dev)) & 1)
+        bits = bits.reshape(heads, qb, -1)[:, :, :kb].bool()
+        exist = torch.ones(heads, qb + qb % 2, 1, dtype=torch.bool, device=dev)
+        if qb % 2:  # the last tile's second half has no query block: no items of its own
+            bits = torch.cat((bits, torch.zeros_like(bits[:, :1])), 1)
+            exist[:, -1] = False
+        ex = bits.reshape(heads, -1, 2, kb)
+        union = ex.any(2)
+        approx_any = ((~ex) & exist.reshape(heads, -1, 2, 1)).any(2)
+        chunks = torch.nn.functional.pad(approx_any, (0, (-kb) % 64)).reshape(heads, -1, (kb + 63) // 64, 64).any(-1)
+        items = int(union.sum().item()) + int(chunks.sum().item())
+        mma_flops = items * 4.0 * 128 * 64 * d
+        dense_flops = 4.0 * nq * nk * d * heads
+        t = tele.tolist()
+        pages = (nk + PAGE_ROWS - 1) // PAGE_ROWS
+        table = torch.arange(pages, dtype=torch.int32, device=dev)
+        kp = torch.zeros(heads, pages * PAGE_ROWS, d, dtype=torch.bfloat16, device=dev)
+        vp = torch.zeros_like(kp)
+        h3sa.kv_copy_rows([k, v], [kp, vp], count=nk, dst_table=table)
+        o = torch.empty(nq, heads, d, dtype=torch.bfloat16, device=dev)
+        probs = [h3sa.AttentionProblem(0, nq, 0, nk)]
+        dense_ms = _time_launch(lambda: h3sa.attention_fwd(q, o, kp, vp, table, probs, d ** -0.5),
+                                iters)
+        mma_tf = mma_flops / (ms * 1e-3) / 1e12
+        out[f"sol_768p_{heads}h"] = {
+            "ms": ms, "dense_kernel_ms": dense_ms, "speedup_vs_dense": dense_ms / ms,
+            "routed_fraction": t[0] / max(1, t[2]), "exact_fraction": t[1] / max(1, t[3]),
+            "items": items, "mma_tflops": mma_tf,
+            "dense_equiv_tflops": dense_flops / (ms * 1e-3) / 1e12, "heads": heads,
+            "queries": nq, "keys": nk, "sink_tokens": nq, "tau": 1.0,
+            "roofline": {"bound": "tensor", "peak": peaks["bf16"], "frac": mma_tf / peaks["bf16"],
+                         "note": "whole call (summaries, statistics, routing, attention)"}}
+        del kp, vp, k, v, q
+        torch.cuda.empty_cache()
     return out
 
 

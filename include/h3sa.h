@@ -226,6 +226,28 @@ H3SA_API int h3sa_segment_row_means(const h3sa_rows* src, const int32_t* segment
 H3SA_API int h3sa_commit_scores(const float* summaries, const float* query_mean,
                                 int32_t num_parts, int32_t heads, double* scores, void* stream);
 
+/* Rectangular SOL-Attn: query [query_tokens, heads, 128] bf16 against one packed K/V
+ * sequence key / value [key_tokens, heads, 128] bf16, cut into 64-row blocks. The first
+ * ceil(sink_tokens / 64) key blocks are exact for every query; the rest are routed per 64-row
+ * query block and head: exact when the block's mean proxy score (query rows . key centroid,
+ * times softmax_scale * log2(e)) exceeds mu + tau * sqrt(var + 1e-6), mu and var the proxy
+ * score's mean and diagonal variance over the key centroids; every other block enters the
+ * softmax through its centroid, weighted by its row count, with its V sum as value. Scratch
+ * and side outputs, all device memory: key_centroids and value_sums bf16
+ * [ceil(key_tokens / 64), heads, 128]; key_stats fp32 [heads, 2, 128]; exact_blocks uint32
+ * [heads, ceil(query_tokens / 64), ceil(key_blocks / 32)] (bit b of a query block's words =
+ * key block b is exact); telemetry int64 [4] or NULL, to which the launch adds the counts of
+ * routed, exact, routable and candidate blocks. out bf16 [query_tokens, heads, 128]. Up to
+ * 4096 key blocks (262144 key rows); every pointer 16-byte aligned. Replaces
+ * sol_attn_rectangular without a static summary cache (F/inference/sol_attention.py:366-598),
+ * the FL2AV hook's sol_attn backend call (F/streaming/attention_hook.py:909-991). */
+H3SA_API int h3sa_sol_attention(const void* query, int32_t query_tokens, const void* key,
+                                const void* value, int32_t key_tokens, int32_t heads,
+                                int32_t head_dim, float softmax_scale, float tau,
+                                int32_t sink_tokens, void* key_centroids, void* value_sums,
+                                float* key_stats, uint32_t* exact_blocks, int64_t* telemetry,
+                                void* out, int32_t* device_error, void* stream);
+
 /* W8A8 projection GEMM (tcgen05 kind::i8, int32 accumulation in TMEM):
  * out[m, n] = bf16_rn(a_scale[m] * (b_scale[n] * float(sum_k a[m, k] * b[n, k])))
  * a: int8 [m, k] activations, b: int8 [n, k] weights (both row-major, K contiguous);

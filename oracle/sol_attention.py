@@ -38,13 +38,16 @@ def _blocks(n: int) -> int:
 
 
 def summaries(x: torch.Tensor, *, mean: bool, dtype: torch.dtype) -> torch.Tensor:
-    """Per 64-row block sums (or means) of ``x`` [N, H, D] in float32, rounded to ``dtype``."""
+    """Per 64-row block sums (or means) of ``x`` [N, H, D], float32 added in row order, rounded
+    to ``dtype``."""
 
     n = x.shape[0]
     out = []
     for b in range(_blocks(n)):
         rows = x[b * BLOCK:(b + 1) * BLOCK].float()
-        s = rows.sum(0)
+        s = rows[0].clone()
+        for r in range(1, rows.shape[0]):
+            s = s + rows[r]
         if mean:
             s = s / float(rows.shape[0])
         out.append(s)
@@ -99,7 +102,6 @@ def sol_attn_rectangular(query: torch.Tensor, key: torch.Tensor, value: torch.Te
     for qb in range(qb_n):
         r0, r1 = qb * BLOCK, min(nq, (qb + 1) * BLOCK)
         for h in range(heads):
-            q = q32[r0:r1, h].double()
             ex = route[qb, h]
             key_rows = torch.cat([torch.arange(b * BLOCK, min(nk, (b + 1) * BLOCK))
                                   for b in range(kb_n) if bool(ex[b])] or [torch.zeros(0, dtype=torch.long)])
@@ -119,7 +121,6 @@ def sol_attn_rectangular(query: torch.Tensor, key: torch.Tensor, value: torch.Te
             pp = p_proxy.float().to(summary_dtype).double()
             num = pe @ v32[key_rows, h].double() + pp @ vs[approx, h].double()
             out[r0:r1, h] = (num / den[:, None]).float()
-            del q
     return out, route, margin, tele
 
 

@@ -99,6 +99,8 @@ SIGNATURES: dict[str, tuple[object, list[object]]] = {
     "h3sa_segment_row_means": (
         ctypes.c_int, [ctypes.POINTER(Rows), _P, _I, _I, _I, _P, _P, _P, _P]),
     "h3sa_commit_scores": (ctypes.c_int, [_P, _P, _I, _I, _P, _P]),
+    "h3sa_sol_attention": (
+        ctypes.c_int, [_P, _I, _P, _P, _I, _I, _I, _F, _F, _I, _P, _P, _P, _P, _P, _P, _P, _P]),
     "h3sa_w8a8_gemm": (ctypes.c_int, [_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P]),
     "h3sa_quantize_int8_rows": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _P]),
     "h3sa_gemm_bf16": (ctypes.c_int, [_P, _P, _P, _I, _I, _I, _I, _P, _I, _I, _P, _P]),
