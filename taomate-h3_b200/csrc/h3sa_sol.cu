@@ -55,22 +55,45 @@ struct SolParams {
   int* err;
 };
 
-// grid (kb, heads), 128 threads: thread d sums dim d of the block's rows in row order.
+__device__ __forceinline__ void add_bf16x8(float (&acc)[8], const uint4 w) {
+  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    acc[2 * e] += __uint_as_float(ws[e] << 16);
+    acc[2 * e + 1] += __uint_as_float(ws[e] & 0xFFFF0000u);
+  }
+}
+
+// grid ceil(kb * heads / 8), 128 threads: 16 threads per (key block, head), each summing 8 dims
+// (one 16-byte load per row) over the block's rows in row order.
 __global__ void __launch_bounds__(128) sol_summaries_kernel(const SolParams p) {
-  const int b = blockIdx.x, h = blockIdx.y, d = threadIdx.x;
+  const int pair = blockIdx.x * 8 + (threadIdx.x >> 4);
+  if (pair >= p.kb * p.heads) return;
+  const int b = pair / p.heads, h = pair - b * p.heads, c = threadIdx.x & 15;
   const int r0 = b * kSolRows;
   const int n = min(kSolRows, p.nk - r0);
-  float sk = 0.f, sv = 0.f;
-  const size_t stride = static_cast<size_t>(p.heads) * kHeadDim;
-  const size_t base = (static_cast<size_t>(r0) * p.heads + h) * kHeadDim + d;
-#pragma unroll 8
+  const size_t stride = static_cast<size_t>(p.heads) * kHeadDim / 8;  // in uint4
+  const size_t base = ((static_cast<size_t>(r0) * p.heads + h) * kHeadDim) / 8 + c;
+  const uint4* k = reinterpret_cast<const uint4*>(p.k) + base;
+  const uint4* v = reinterpret_cast<const uint4*>(p.v) + base;
+  float sk[8] = {}, sv[8] = {};
+#pragma unroll 4
   for (int r = 0; r < n; ++r) {
-    sk += __bfloat162float(p.k[base + r * stride]);
-    sv += __bfloat162float(p.v[base + r * stride]);
+    add_bf16x8(sk, __ldg(k + r * stride));
+    add_bf16x8(sv, __ldg(v + r * stride));
   }
-  const size_t o = (static_cast<size_t>(b) * p.heads + h) * kHeadDim + d;
-  p.kc[o] = __float2bfloat16_rn(sk / static_cast<float>(n));
-  p.vs[o] = __float2bfloat16_rn(sv);
+  const float inv_n = static_cast<float>(n);
+  uint4 ok, ov;
+  uint32_t* pk = &ok.x;
+  uint32_t* pv = &ov.x;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    pk[e] = pack_bf16x2(sk[2 * e] / inv_n, sk[2 * e + 1] / inv_n);
+    pv[e] = pack_bf16x2(sv[2 * e], sv[2 * e + 1]);
+  }
+  const size_t o = ((static_cast<size_t>(b) * p.heads + h) * kHeadDim) / 8 + c;
+  reinterpret_cast<uint4*>(p.kc)[o] = ok;
+  reinterpret_cast<uint4*>(p.vs)[o] = ov;
 }
 
 // grid heads, 128 threads: mean, then the mean squared deviation, of dim d over the centroids.
@@ -104,17 +127,19 @@ __global__ void __launch_bounds__(kSolThreads) sol_route_kernel(const SolParams 
   const int nqb = min(kSolRouteQBlocks, p.qb - qb0);
   const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const size_t stride = static_cast<size_t>(p.heads) * kHeadDim;
-  {
-    const int d = t & (kHeadDim - 1);
-    for (int j = t >> 7; j < nqb; j += kSolThreads / kHeadDim) {
-      const int r0 = (qb0 + j) * kSolRows;
-      const int n = min(kSolRows, p.nq - r0);
-      const __nv_bfloat16* src = p.q + (static_cast<size_t>(r0) * p.heads + h) * kHeadDim + d;
-      float s = 0.f;
-#pragma unroll 8
-      for (int r = 0; r < n; ++r) s += __bfloat162float(src[r * stride]);
-      cs[j][d] = s;
-    }
+  if (t < 16 * kSolRouteQBlocks && (t >> 4) < nqb) {
+    // 16 threads per query block, 8 dims each, rows added in order
+    const int j = t >> 4, c = t & 15;
+    const int r0 = (qb0 + j) * kSolRows;
+    const int n = min(kSolRows, p.nq - r0);
+    const uint4* src = reinterpret_cast<const uint4*>(p.q) +
+                       ((static_cast<size_t>(r0) * p.heads + h) * kHeadDim) / 8 + c;
+    float acc[8] = {};
+#pragma unroll 1
+    for (int r = 0; r < n; ++r) add_bf16x8(acc, __ldg(src + r * (stride / 8)));
+    float4* dst = reinterpret_cast<float4*>(&cs[j][8 * c]);
+    dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
   }
   __syncthreads();
   if (warp < nqb) {
@@ -448,44 +473,71 @@ __global__ void __launch_bounds__(kSolThreads, 2)
       }
       if (!(ok = mbar_wait(smem_u32(&sm.s_full[i & 1]), (i >> 1) & 1, abort_flag, p.err))) break;
       tc_fence_after();
-      const uint32_t tS = tbase + static_cast<uint32_t>(i & 1) * 64u + lane_off;
-      uint32_t r0[32], r1[32];
-      tmem_ld32(tS, r0);
-      tmem_ld32(tS + 32u, r1);
-      tmem_wait_ld();
-      reg_fence32(r0);
-      reg_fence32(r1);
-      float s[64];
-      const uint32_t vlo = static_cast<uint32_t>(vm), vhi = static_cast<uint32_t>(vm >> 32);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        s[j] = ((vlo >> j) & 1u) ? __uint_as_float(r0[j]) * p.sl2 : -INFINITY;
-        s[32 + j] = ((vhi >> j) & 1u) ? __uint_as_float(r1[j]) * p.sl2 : -INFINITY;
-      }
-      float mx = s[0];
-#pragma unroll
-      for (int j = 1; j < 64; ++j) mx = fmaxf(mx, s[j]);
-      const bool need = mx > m_used + kSolRescale || (m_used == -INFINITY && mx > -INFINITY);
-      const float m_new = need ? mx : m_used;
-      const float alpha = (need && m_used > -INFINITY) ? fast_exp2(m_used - m_new) : 1.0f;
-      const bool any_need = i > 0 && __any_sync(0xffffffffu, need && m_used > -INFINITY);
-      l_sum *= alpha;
-      m_used = m_new;
-      const float bias = m_used == -INFINITY ? 0.f : -m_used;
+      // a warp's 32 rows lie in one half, so `vm` is warp-uniform: a warp whose query block
+      // takes nothing from this item only writes zero P
+      const bool live = vm != 0ull;
+      bool need = false;
+      float alpha = 1.0f;
       uint32_t pk[32];
-      float sum = 0.f;
+      if (live) {
+        const uint32_t tS = tbase + static_cast<uint32_t>(i & 1) * 64u + lane_off;
+        uint32_t r[64];
+        tmem_ld32(tS, *reinterpret_cast<uint32_t(*)[32]>(r));
+        tmem_ld32(tS + 32u, *reinterpret_cast<uint32_t(*)[32]>(r + 32));
+        tmem_wait_ld();
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(r));
+        reg_fence32(*reinterpret_cast<uint32_t(*)[32]>(r + 32));
+        if (vm != ~0ull) {
+          const uint32_t vlo = static_cast<uint32_t>(vm), vhi = static_cast<uint32_t>(vm >> 32);
 #pragma unroll
-      for (int j = 0; j < 64; j += 2) {
-        const float p0 = fast_exp2(s[j] + bias);
-        const float p1 = fast_exp2(s[j + 1] + bias);
-        sum += p0 + p1;
-        pk[j / 2] = pack_bf16x2(p0, p1);
-        if (approx && jl >= 0) {  // the partial last block: its weight is its row count
-          if (j == jl) sum += p0 * static_cast<float>(last_len - 64) * (1.0f / 64.0f);
-          if (j + 1 == jl) sum += p1 * static_cast<float>(last_len - 64) * (1.0f / 64.0f);
+          for (int j = 0; j < 32; ++j) {
+            if (!((vlo >> j) & 1u)) r[j] = 0xFF800000u;  // -inf
+            if (!((vhi >> j) & 1u)) r[32 + j] = 0xFF800000u;
+          }
         }
+        float m0 = __uint_as_float(r[0]), m1 = __uint_as_float(r[1]);
+#pragma unroll
+        for (int j = 2; j < 64; j += 4) {
+          m0 = fmax3(m0, __uint_as_float(r[j]), __uint_as_float(r[j + 2]));
+          m1 = fmax3(m1, __uint_as_float(r[j + 1]), __uint_as_float(r[j + 3]));
+        }
+        const float mx = fmaxf(m0, m1) * p.sl2;  // the scale is positive
+        need = mx > m_used + kSolRescale || (m_used == -INFINITY && mx > -INFINITY);
+        const float m_new = need ? mx : m_used;
+        alpha = (need && m_used > -INFINITY) ? fast_exp2(m_used - m_new) : 1.0f;
+        l_sum *= alpha;
+        m_used = m_new;
+        const float bias = m_used == -INFINITY ? 0.f : -m_used;
+        const uint64_t sl2x2 = f2_pack(p.sl2, p.sl2), bias2 = f2_pack(bias, bias);
+        uint64_t sum2 = f2_pack(0.f, 0.f);
+#pragma unroll
+        for (int j = 0; j < 64; j += 2) {
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), sl2x2, bias2),
+                    x0, x1);
+          const float p0 = fast_exp2(x0), p1 = fast_exp2(x1);
+          sum2 = f2_add(sum2, f2_pack(p0, p1));
+          pk[j / 2] = pack_bf16x2(p0, p1);
+        }
+        float sa, sb;
+        f2_unpack(sum2, sa, sb);
+        float sum = sa + sb;
+        if (approx) {  // every block's weight is its row count; only the last may be short
+          sum *= 64.0f;
+          if (jl >= 0) {
+            float rj = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 64; ++j)
+              if (j == jl) rj = __uint_as_float(r[j]);
+            sum += fast_exp2(fmaf(rj, p.sl2, bias)) * static_cast<float>(last_len - 64);
+          }
+        }
+        l_sum += sum;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) pk[j] = 0u;
       }
-      l_sum += approx ? 64.0f * sum : sum;
+      const bool any_need = i > 0 && __any_sync(0xffffffffu, need && alpha != 1.0f);
       if (any_need) {
         // PV(i - 1) has finished (S(i) completed after it); rescale this row's O
         if (!(ok = mbar_wait(smem_u32(&sm.pv_done), (i - 1) & 1, abort_flag, p.err))) break;
@@ -614,7 +666,7 @@ extern "C" int h3sa_sol_attention(const void* query, int32_t query_tokens, const
     e = cudaFuncSetAttribute(sol_attention_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                              100);
   if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(sol attention)", e);
-  sol_summaries_kernel<<<dim3(kb, heads), 128, 0, st>>>(p);
+  sol_summaries_kernel<<<(kb * heads + 7) / 8, 128, 0, st>>>(p);
   sol_key_stats_kernel<<<heads, 128, 0, st>>>(p);
   sol_route_kernel<<<dim3((p.qb + kSolRouteQBlocks - 1) / kSolRouteQBlocks, heads), kSolThreads,
                      0, st>>>(p);
