@@ -31,10 +31,13 @@ bf16), ``"flash_attn3_fp8_dynamic"`` (per-call per-head e4m3 Q/K/V,
 F/streaming/attention_hook.py:1081-1098), ``"flash_attn3_fp8_segmented"`` (e4m3 history
 parts quantised once at commit, :1015-1066), ``"flash_attn3_fp8_segmented_topk"`` (the same
 over the committed blocks whose key summaries score highest against the media queries,
-:1256-1302) and ``"flex_dynamic_blocksparse"`` (history block top-k,
-F/inference/dynamic_block_sparse.py:50-172). The e4m3 and block-sparse backends run the
+:1256-1302), ``"flex_dynamic_blocksparse"`` (history block top-k,
+F/inference/dynamic_block_sparse.py:50-172) and ``"sol_attn"`` (rectangular SOL-Attn routing
+of the history video, F/streaming/attention_hook.py:909-991, 1361-1492: dense in the commit
+and capture modes, the first ``sol_attn_dense_layers`` layers and the first
+``sol_attn_dense_denoise_steps`` denoise steps). The e4m3 and block-sparse backends run the
 NOISY / CLEAN_COMMIT / PROGRESS_COMMIT modes without a temporary prefix; fused forwards,
-prefix captures and temporary prefixes run on the dense backends.
+prefix captures and temporary prefixes run on the dense and SOL backends.
 """
 
 from __future__ import annotations
@@ -57,6 +60,7 @@ FP8_BACKENDS = ("flash_attn3_fp8_dynamic", "flash_attn3_fp8_segmented",
                 "flash_attn3_fp8_segmented_topk")
 SEGMENTED_BACKENDS = ("flash_attn3_fp8_segmented", "flash_attn3_fp8_segmented_topk")
 SPARSE_BACKENDS = ("flex_dynamic_blocksparse",)
+SOL_BACKENDS = ("sol_attn",)
 
 
 class HookMode(str, Enum):
@@ -188,14 +192,32 @@ class H3StreamingAttentionHook:
 
     def __init__(self, cache: CleanAVKVCache, *, backend: str = "flash_attn_3",
                  history_density: float = 0.5, attention_backend: str | None = None,
-                 history_kv_dynamic_density: float | None = None) -> None:
+                 history_kv_dynamic_density: float | None = None, sol_attn_tau: float = 1.0,
+                 sol_attn_thresh_type: str = "diag", sol_attn_dense_layers: int = 2,
+                 sol_attn_dense_denoise_steps: int = 1,
+                 sol_attn_route_current_video: bool = False,
+                 sol_attn_static_summary_cache: bool = False) -> None:
         # the FL2AV constructor's names for the same two knobs (F/streaming/attention_hook.py:377-394)
         if attention_backend is not None:
             backend = attention_backend
         if history_kv_dynamic_density is not None:
             history_density = history_kv_dynamic_density
-        if backend not in DENSE_BACKENDS + FP8_BACKENDS + SPARSE_BACKENDS:
+        if backend not in DENSE_BACKENDS + FP8_BACKENDS + SPARSE_BACKENDS + SOL_BACKENDS:
             raise ValueError(f"unsupported H3 streaming attention backend: {backend}")
+        # SOL-Attn knobs (F/streaming/attention_hook.py:387-434)
+        self.sol_attn_tau = float(sol_attn_tau)
+        if sol_attn_thresh_type != "diag":
+            raise ValueError("SOL-Attn rectangular adapter supports only diag thresholding")
+        self.sol_attn_thresh_type = sol_attn_thresh_type
+        self.sol_attn_dense_layers = int(sol_attn_dense_layers)
+        self.sol_attn_dense_denoise_steps = int(sol_attn_dense_denoise_steps)
+        self.sol_attn_route_current_video = bool(sol_attn_route_current_video)
+        self.sol_attn_static_summary_cache = bool(sol_attn_static_summary_cache)
+        self.sol_attn_kernel_calls = 0
+        self.sol_attn_dense_calls = 0
+        self.sol_attn_query_tokens = 0
+        self.sol_attn_key_tokens = 0
+        self._sol_attn_density_counts: torch.Tensor | None = None
         if not 0.0 < history_density <= 1.0:
             raise ValueError("dynamic history KV density must be in (0, 1]")
         self.cache = cache
@@ -233,6 +255,39 @@ class H3StreamingAttentionHook:
         # (last_output_exchanged tells the caller whether that happened).
         self.output_exchange = None
         self.last_output_exchanged = False
+
+    def sol_attn_receipt(self) -> dict[str, object] | None:
+        """Counters of the SOL-Attn backend (F/streaming/attention_hook.py:496-552); the
+        routing counts come from the device telemetry of every SOL call."""
+
+        if self.backend not in SOL_BACKENDS:
+            return None
+        counts = ([0, 0, 0, 0] if self._sol_attn_density_counts is None
+                  else [int(x) for x in self._sol_attn_density_counts.detach().cpu().tolist()])
+        selected, exact, routable, candidate = counts
+        return {
+            "backend": "h3sa_sm100a_sol_attn_rectangular",
+            "tau": self.sol_attn_tau,
+            "thresh_type": self.sol_attn_thresh_type,
+            "dense_layers": self.sol_attn_dense_layers,
+            "dense_denoise_steps": self.sol_attn_dense_denoise_steps,
+            "route_current_video": self.sol_attn_route_current_video,
+            "static_summary_cache": self.sol_attn_static_summary_cache,
+            "kernel_calls": self.sol_attn_kernel_calls,
+            "dense_calls": self.sol_attn_dense_calls,
+            "query_tokens": self.sol_attn_query_tokens,
+            "key_tokens": self.sol_attn_key_tokens,
+            "route_selected_blocks": selected,
+            "exact_blocks": exact,
+            "routable_blocks": routable,
+            "candidate_blocks": candidate,
+            "selected_density": None if routable == 0 else selected / routable,
+            "exact_density": None if candidate == 0 else exact / candidate,
+            "history_policy": (
+                "rectangular_exact_condition_prefix_audio_sparse_current_and_history_video"
+                if self.sol_attn_route_current_video
+                else "rectangular_exact_condition_current_prefix_audio_sparse_history_video"),
+        }
 
     def receipt(self) -> dict[str, object]:
         return {
@@ -306,7 +361,7 @@ class H3StreamingAttentionHook:
         self._phase_index = phase_index
 
     def _require_dense_for(self, extras: bool) -> None:
-        if extras and self.backend not in DENSE_BACKENDS:
+        if extras and self.backend not in DENSE_BACKENDS + SOL_BACKENDS:
             raise ValueError(f"the {self.backend} backend runs NOISY, CLEAN_COMMIT and "
                              "PROGRESS_COMMIT without a temporary prefix; fused forwards, "
                              "prefix captures and temporary prefixes need a dense backend")
@@ -560,15 +615,26 @@ class H3StreamingAttentionHook:
                                              sparse=self.backend in SPARSE_BACKENDS))
             problems.append(AttentionProblem(cq[0], cq[1], c_start, c_start + (cq[1] - cq[0])))
         out_main = out if gathered is None else torch.empty_like(gathered)
+        # SOL-Attn backend: the media rows of the document(s) it routes go through
+        # h3sa_sol_attention instead of the dense launch
+        sol_docs = self._sol_documents(layer_name, fused)
         # rows stored straight into the owners' sequence shards when the output rows are the
         # query rows (no gather) and the launch is bf16
         exchange = self.output_exchange
-        if exchange is not None and (gathered is not None or self.backend in FP8_BACKENDS):
+        if exchange is not None and (gathered is not None or self.backend in FP8_BACKENDS
+                                     or sol_docs):
             exchange = None
         self.last_output_exchanged = exchange is not None
         n_kv_media = regions[0][3]
-        self._launch(layer_name, paged, q_src, out_main, problems, scale, n_kv_media, n_hist,
-                     plan, err, exchange)
+        dense_problems = [pr for i, pr in enumerate(problems)
+                          if not (i % 2 == 0 and i // 2 in sol_docs)]
+        self._launch(layer_name, paged, q_src, out_main, dense_problems, scale, n_kv_media,
+                     n_hist, plan, err, exchange)
+        if self.backend in SOL_BACKENDS:
+            self.sol_attn_dense_calls += len(dense_problems)
+        for d in sol_docs:
+            self._sol_media(paged, plan, d, regions[d], q_src, q_ranges[2 * d], out_main, scale,
+                            fused, token_tags, layer_name, err)
         if other_kv and self.backend in FP8_BACKENDS:
             # every other document is its own one-part e4m3 call in the reference's FP8 backends
             for a, b, c in other_kv:
@@ -607,6 +673,143 @@ class H3StreamingAttentionHook:
                                       commit_indices=plan.docs[0].media.host.to(
                                           token_tags.device, torch.long))
         return out
+
+    # ------------------------------------------------------------------ SOL-Attn
+    def _sol_documents(self, layer_name: str, fused: bool) -> list[int]:
+        """Live documents (positions in the plan) whose media rows are routed this call: none
+        in the commit and capture modes, in the first ``sol_attn_dense_denoise_steps`` denoise
+        steps or the first ``sol_attn_dense_layers`` layers; in a fused forward only the
+        current document (F/streaming/attention_hook.py:909-929, 1487)."""
+
+        if self.backend not in SOL_BACKENDS:
+            return []
+        if self.mode in (HookMode.CLEAN_COMMIT, HookMode.PROGRESS_COMMIT,
+                         HookMode.FULL_PREFIX_CAPTURE):
+            return []
+        if (self._denoise_step_index is not None
+                and self._denoise_step_index < self.sol_attn_dense_denoise_steps):
+            return []
+        if int(layer_name.split(".")[1]) < self.sol_attn_dense_layers:
+            return []
+        return [1] if fused else [0]
+
+    def _sol_history_rows(self, fused_current: bool) -> tuple[list[int], list[int]]:
+        """Logical history rows split into audio and video, block by block, over the blocks
+        the SOL call sees (F/streaming/cache.py:439-499)."""
+
+        cache = self.cache
+        retained = cache.retained_blocks
+        if retained == 0:
+            return [], []
+        recent_blocks = self.fused_current_recent_blocks
+        if fused_current and recent_blocks is not None:
+            recent = max(0, recent_blocks - 1)
+            if self.fused_current_use_sink:
+                blocks = (0, *range(max(1, retained - recent), retained))
+            else:
+                blocks = tuple(range(max(0, retained - recent), retained))
+        else:
+            blocks = tuple(range(retained))
+        offsets = cache._block_offsets()
+        tags = cache.commit_token_tags()
+        audio: list[int] = []
+        video: list[int] = []
+        for b in blocks:
+            for r, tag in enumerate(tags[b]):
+                if tag == AUDIO_TOKEN_TAG:
+                    audio.append(offsets[b] + r)
+                elif tag == VIDEO_TOKEN_TAG:
+                    video.append(offsets[b] + r)
+        return audio, video
+
+    def _sol_media(self, paged, plan: _DocumentPlan, d: int, region: tuple[int, int, int, int],
+                   q_src: torch.Tensor, q_range: tuple[int, int], out: torch.Tensor,
+                   scale: float, fused: bool, token_tags: torch.Tensor, layer_name: str,
+                   err: torch.Tensor) -> None:
+        """One live document's media rows through SOL-Attn. The K/V sequence is gathered from
+        the page sequence in the reference's part order: exact parts [condition, current
+        media, temporary prefix, previous document's media, audio history] as the sink, then
+        the video history routed; with ``sol_attn_route_current_video`` the current video
+        moves from the sink to the routed part and the audio queries attend densely
+        (F/streaming/attention_hook.py:1379-1492)."""
+
+        from .sol_attention import sol_attn_rectangular
+
+        kv_start, first, c_start, end = region
+        doc = plan.docs[d]
+        n_media, n_cond = doc.media.n, doc.cond.n
+        transient = self._transient(layer_name, d, fused)
+        n_prefix = 0 if transient is None else int(transient.key.shape[0])
+        media_rows = list(range(first, first + n_media))
+        cond_rows = list(range(c_start, c_start + n_cond))
+        prefix_rows = list(range(c_start + n_cond, c_start + n_cond + n_prefix))
+        prev_rows: list[int] = []
+        if fused and d == 1 and plan.previous_media is not None:
+            at = c_start + n_cond + n_prefix
+            prev_rows = list(range(at, at + plan.previous_media.n))
+        audio_hist, video_hist = self._sol_history_rows(fused_current=fused and d == 1)
+        device = q_src.device
+        lo, hi = q_range
+        route_video = self.sol_attn_route_current_video and not fused
+        if route_video:
+            tags = token_tags.detach().to("cpu")[doc.media.host].tolist()
+            cur_audio = [media_rows[i] for i, t in enumerate(tags) if t == AUDIO_TOKEN_TAG]
+            cur_video = [media_rows[i] for i, t in enumerate(tags) if t == VIDEO_TOKEN_TAG]
+            exact = cond_rows + cur_audio + prefix_rows + audio_hist
+            routed = cur_video + video_hist
+            q_audio = [i for i, t in enumerate(tags) if t == AUDIO_TOKEN_TAG]
+            q_video = [i for i, t in enumerate(tags) if t == VIDEO_TOKEN_TAG]
+        else:
+            exact = cond_rows + media_rows + prefix_rows + prev_rows + audio_hist
+            routed = video_hist
+            q_audio, q_video = [], None
+        rows = exact + routed
+        index = torch.tensor(rows, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
+        heads = q_src.shape[1]
+        k = torch.empty(len(rows), heads, q_src.shape[2], dtype=q_src.dtype, device=device)
+        v = torch.empty_like(k)
+        kv_copy_rows([paged.key, paged.value], [k, v], count=len(rows), src_table=paged.table,
+                     src_index=index, device_error=err)
+        if self._sol_attn_density_counts is None or self._sol_attn_density_counts.device != device:
+            self._sol_attn_density_counts = torch.zeros(4, dtype=torch.int64, device=device)
+
+        def subset(positions: list[int]):
+            idx = torch.tensor([lo + i for i in positions], dtype=torch.int32).pin_memory().to(
+                device, non_blocking=True)
+            qs = torch.empty(len(positions), *q_src.shape[1:], dtype=q_src.dtype, device=device)
+            kv_copy_rows([q_src], [qs], count=len(positions), src_index=idx)
+            return qs, idx
+
+        if q_video is None:
+            o = sol_attn_rectangular(q_src[lo:hi], k, v, scale=scale, tau=self.sol_attn_tau,
+                                     sink_tokens=len(exact),
+                                     telemetry_counts=self._sol_attn_density_counts,
+                                     device_error=err)
+            out[lo:hi].copy_(o)
+            n_sol = hi - lo
+        else:
+            if q_audio:
+                qa, ia = subset(q_audio)
+                oa = torch.empty_like(qa)
+                attention_fwd(qa, oa, paged.key, paged.value, paged.table,
+                              [AttentionProblem(0, len(q_audio), kv_start, end)], scale,
+                              device_error=err)
+                kv_copy_rows([oa], [out], count=len(q_audio), dst_index=ia)
+                self.sol_attn_dense_calls += 1
+                self.launches += 1
+            n_sol = len(q_video)
+            if q_video:
+                qv, iv = subset(q_video)
+                ov = sol_attn_rectangular(qv, k, v, scale=scale, tau=self.sol_attn_tau,
+                                          sink_tokens=len(exact),
+                                          telemetry_counts=self._sol_attn_density_counts,
+                                          device_error=err)
+                kv_copy_rows([ov], [out], count=n_sol, dst_index=iv)
+        if n_sol:
+            self.sol_attn_kernel_calls += 1
+            self.sol_attn_query_tokens += n_sol
+            self.sol_attn_key_tokens += len(rows)
+            self.launches += 1
 
     def _capture(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,
                  token_tags: torch.Tensor, commit_mask: torch.Tensor) -> None:
