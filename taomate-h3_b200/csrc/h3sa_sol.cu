@@ -56,12 +56,14 @@ struct SolParams {
 };
 
 __device__ __forceinline__ void add_bf16x8(float (&acc)[8], const uint4 w) {
-  const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    acc[2 * e] += __uint_as_float(ws[e] << 16);
-    acc[2 * e + 1] += __uint_as_float(ws[e] & 0xFFFF0000u);
-  }
+  acc[0] += __uint_as_float(w.x << 16);
+  acc[1] += __uint_as_float(w.x & 0xFFFF0000u);
+  acc[2] += __uint_as_float(w.y << 16);
+  acc[3] += __uint_as_float(w.y & 0xFFFF0000u);
+  acc[4] += __uint_as_float(w.z << 16);
+  acc[5] += __uint_as_float(w.z & 0xFFFF0000u);
+  acc[6] += __uint_as_float(w.w << 16);
+  acc[7] += __uint_as_float(w.w & 0xFFFF0000u);
 }
 
 // grid ceil(kb * heads / 8), 128 threads: 16 threads per (key block, head), each summing 8 dims
@@ -77,40 +79,50 @@ __global__ void __launch_bounds__(128) sol_summaries_kernel(const SolParams p) {
   const uint4* k = reinterpret_cast<const uint4*>(p.k) + base;
   const uint4* v = reinterpret_cast<const uint4*>(p.v) + base;
   float sk[8] = {}, sv[8] = {};
-#pragma unroll 4
+#pragma unroll 8
   for (int r = 0; r < n; ++r) {
     add_bf16x8(sk, __ldg(k + r * stride));
     add_bf16x8(sv, __ldg(v + r * stride));
   }
-  const float inv_n = static_cast<float>(n);
-  uint4 ok, ov;
-  uint32_t* pk = &ok.x;
-  uint32_t* pv = &ov.x;
-#pragma unroll
-  for (int e = 0; e < 4; ++e) {
-    pk[e] = pack_bf16x2(sk[2 * e] / inv_n, sk[2 * e + 1] / inv_n);
-    pv[e] = pack_bf16x2(sv[2 * e], sv[2 * e + 1]);
-  }
+  const float fn = static_cast<float>(n);
   const size_t o = ((static_cast<size_t>(b) * p.heads + h) * kHeadDim) / 8 + c;
-  reinterpret_cast<uint4*>(p.kc)[o] = ok;
-  reinterpret_cast<uint4*>(p.vs)[o] = ov;
+  reinterpret_cast<uint4*>(p.kc)[o] =
+      make_uint4(pack_bf16x2(sk[0] / fn, sk[1] / fn), pack_bf16x2(sk[2] / fn, sk[3] / fn),
+                 pack_bf16x2(sk[4] / fn, sk[5] / fn), pack_bf16x2(sk[6] / fn, sk[7] / fn));
+  reinterpret_cast<uint4*>(p.vs)[o] =
+      make_uint4(pack_bf16x2(sv[0], sv[1]), pack_bf16x2(sv[2], sv[3]), pack_bf16x2(sv[4], sv[5]),
+                 pack_bf16x2(sv[6], sv[7]));
 }
 
-// grid heads, 128 threads: mean, then the mean squared deviation, of dim d over the centroids.
-__global__ void __launch_bounds__(128) sol_key_stats_kernel(const SolParams p) {
-  const int h = blockIdx.x, d = threadIdx.x;
+// grid heads, 512 threads: dim d = t % 128, block group g = t / 128 takes blocks g, g + 4, ...;
+// the four groups' partial sums are added in group order, first for the mean, then for the
+// mean squared deviation.
+__global__ void __launch_bounds__(512) sol_key_stats_kernel(const SolParams p) {
+  __shared__ float part[4][kHeadDim];
+  const int h = blockIdx.x, d = threadIdx.x & (kHeadDim - 1), g = threadIdx.x >> 7;
   const size_t stride = static_cast<size_t>(p.heads) * kHeadDim;
   const __nv_bfloat16* c = p.kc + static_cast<size_t>(h) * kHeadDim + d;
   float s = 0.f;
-  for (int b = 0; b < p.kb; ++b) s += __bfloat162float(c[b * stride]);
-  const float mean = s / static_cast<float>(p.kb);
+#pragma unroll 8
+  for (int b = g; b < p.kb; b += 4) s += __bfloat162float(c[b * stride]);
+  part[g][d] = s;
+  __syncthreads();
+  const float mean = ((part[0][d] + part[1][d]) + (part[2][d] + part[3][d])) /
+                     static_cast<float>(p.kb);
+  __syncthreads();
   float s2 = 0.f;
-  for (int b = 0; b < p.kb; ++b) {
+#pragma unroll 8
+  for (int b = g; b < p.kb; b += 4) {
     const float x = __bfloat162float(c[b * stride]) - mean;
     s2 += x * x;
   }
-  p.stats[(h * 2 + 0) * kHeadDim + d] = mean;
-  p.stats[(h * 2 + 1) * kHeadDim + d] = s2 / static_cast<float>(p.kb);
+  part[g][d] = s2;
+  __syncthreads();
+  if (g == 0) {
+    p.stats[(h * 2 + 0) * kHeadDim + d] = mean;
+    p.stats[(h * 2 + 1) * kHeadDim + d] =
+        ((part[0][d] + part[1][d]) + (part[2][d] + part[3][d])) / static_cast<float>(p.kb);
+  }
 }
 
 // grid (ceil(qb / 8), heads), 256 threads. The query blocks' column sums (fp32, row order) go
@@ -135,7 +147,7 @@ __global__ void __launch_bounds__(kSolThreads) sol_route_kernel(const SolParams 
     const uint4* src = reinterpret_cast<const uint4*>(p.q) +
                        ((static_cast<size_t>(r0) * p.heads + h) * kHeadDim) / 8 + c;
     float acc[8] = {};
-#pragma unroll 1
+#pragma unroll 8
     for (int r = 0; r < n; ++r) add_bf16x8(acc, __ldg(src + r * (stride / 8)));
     float4* dst = reinterpret_cast<float4*>(&cs[j][8 * c]);
     dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
@@ -176,13 +188,8 @@ __global__ void __launch_bounds__(kSolThreads) sol_route_kernel(const SolParams 
 #pragma unroll 2
       for (int c = 0; c < kHeadDim / 8; ++c) {
         const uint4 w = __ldg(row + c);
-        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-        float x[8];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          x[2 * e] = __uint_as_float(ws[e] << 16);
-          x[2 * e + 1] = __uint_as_float(ws[e] & 0xFFFF0000u);
-        }
+        float x[8] = {};
+        add_bf16x8(x, w);
 #pragma unroll
         for (int q = 0; q < kSolRouteQBlocks; ++q) {
           const float4 a = *reinterpret_cast<const float4*>(&cs[q][8 * c]);
@@ -667,7 +674,7 @@ extern "C" int h3sa_sol_attention(const void* query, int32_t query_tokens, const
                              100);
   if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(sol attention)", e);
   sol_summaries_kernel<<<(kb * heads + 7) / 8, 128, 0, st>>>(p);
-  sol_key_stats_kernel<<<heads, 128, 0, st>>>(p);
+  sol_key_stats_kernel<<<heads, 512, 0, st>>>(p);
   sol_route_kernel<<<dim3((p.qb + kSolRouteQBlocks - 1) / kSolRouteQBlocks, heads), kSolThreads,
                      0, st>>>(p);
   const int tiles = (query_tokens + kBlockM - 1) / kBlockM;
