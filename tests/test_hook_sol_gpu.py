@@ -9,7 +9,10 @@ rows with block-clustered keys; then NOISY calls:
   counts one SOL call with the oracle's routing counts;
 * with ``sol_attn_route_current_video`` the current video moves into the routed part and the
   audio queries attend densely (:1379-1451);
-* in a dense layer the media rows equal dense attention over the same keys.
+* in a dense layer the media rows equal dense attention over the same keys;
+* a fused progress-denoise forward with the sink + recent policy routes the current
+  document over [condition, media, previous document's media, audio history] exact and the
+  policy's video history (F/streaming/cache.py:477-499), the previous document dense.
 
 The inputs are seeded so that no routing decision lies within 5e-5 (log2 units) of its
 threshold, far above the fp32 noise of the scores (~1e-6).
@@ -155,3 +158,77 @@ def test_hook_sol_rejects_other_thresholds() -> None:
     cache = CleanAVKVCache(KVContract(local_heads=HEADS, head_dim=128), layer_names=("blocks.0.attn",))
     with pytest.raises(ValueError, match="diag"):
         H3StreamingAttentionHook(cache, attention_backend="sol_attn", sol_attn_thresh_type="full")
+
+
+def _fused_inputs(seed: int):
+    rng = np.random.default_rng(seed)
+    history = [_document(rng, rng.standard_normal((5, HEADS, 128))) for _ in range(3)]
+    a = _document(rng, rng.standard_normal((5, HEADS, 128)))
+    b = _document(rng, rng.standard_normal((5, HEADS, 128)))
+    # the packed call: document A (previous, committed by this forward), document B, a pad
+    cat = lambda key: torch.cat((a[key][:304], b[key][:304], b[key][304:]))  # noqa: E731
+    y = {key: cat(key) for key in ("q", "k", "v", "tags", "commit")}
+    y["cu"] = (0, 304, 608, 624)
+    return history, a, b, y
+
+
+def _fused_oracle_parts(history: list[dict], a: dict, b: dict):
+    """Document B's SOL parts in a fused forward with the sink + one recent block policy:
+    [condition, current media, previous document's media, audio history of blocks 0 and 2]
+    exact, the video history of blocks 0 and 2 routed (F/streaming/cache.py:477-499)."""
+
+    seen = [history[0], history[2]]
+    exact = [(b["k"][:16], b["v"][:16]), (b["k"][16:304], b["v"][16:304]),
+             (a["k"][16:304], a["v"][16:304]), *[(d["k"][16:48], d["v"][16:48]) for d in seen]]
+    routed = [(d["k"][48:304], d["v"][48:304]) for d in seen]
+    k = torch.cat([p[0] for p in exact + routed]).float()
+    v = torch.cat([p[1] for p in exact + routed]).float()
+    return k, v, sum(int(p[0].shape[0]) for p in exact)
+
+
+FUSED_SEED = 31
+
+
+def test_hook_sol_fused_progress_denoise() -> None:
+    """FUSED_PROGRESS_DENOISE with fused_current_use_sink / fused_current_recent_blocks: the
+    previous document attends densely to its condition, the whole history and its media; the
+    current one through SOL over the parts above; the previous document is committed."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    layer = "blocks.2.attn"
+    history, a, b, y = _fused_inputs(FUSED_SEED)
+    k, v, sink = _fused_oracle_parts(history, a, b)
+    qb = b["q"][16:304].float()
+    want, _, margin, _ = osol.sol_attn_rectangular(qb, k, v, scale=SCALE, tau=TAU,
+                                                   sink_tokens=sink)
+    assert float(margin.abs().min()) > 5e-5
+
+    cache = CleanAVKVCache(KVContract(local_heads=HEADS, head_dim=128), layer_names=(layer,))
+    hook = H3StreamingAttentionHook(cache, attention_backend="sol_attn", sol_attn_tau=TAU)
+    for i, x in enumerate(history):
+        cache.begin_clean_commit(cache.committed_blocks)
+        hook.activate(mode=HookMode.CLEAN_COMMIT, block_index=i)
+        hook(attention=Attn(), layer_name=layer, query=x["q"].cuda(), key=x["k"].cuda(),
+             value=x["v"].cuda(), token_tags=x["tags"].cuda(), commit_mask=x["commit"].cuda(),
+             cu_seqlens_host=x["cu"])
+        hook.deactivate()
+        cache.commit()
+    cache.begin_clean_commit(cache.committed_blocks)
+    hook.activate(mode=HookMode.FUSED_PROGRESS_DENOISE, block_index=3, denoise_step_index=1,
+                  fused_current_use_sink=True, fused_current_recent_blocks=2)
+    out = hook(attention=Attn(), layer_name=layer, query=y["q"].cuda(), key=y["k"].cuda(),
+               value=y["v"].cuda(), token_tags=y["tags"].cuda(), commit_mask=y["commit"].cuda(),
+               cu_seqlens_host=y["cu"]).float().cpu()
+    hook.deactivate()
+    cache.commit()
+    hook.check_device_error()
+    assert hook.sol_attn_kernel_calls == 1
+    assert _rel(out[320:608], want) <= 1e-2
+    hk = torch.cat([d["k"][16:304] for d in history])
+    hv = torch.cat([d["v"][16:304] for d in history])
+    ka = torch.cat((a["k"][:16], hk, a["k"][16:304]))
+    va = torch.cat((a["v"][:16], hv, a["v"][16:304]))
+    assert _rel(out[16:304], _dense(a["q"][16:304], ka, va)) <= 1e-2
+    assert cache.committed_blocks == 4 and cache.commit_token_counts[-1] == 288
