@@ -436,7 +436,7 @@ def _time_launch(fn, iters: int) -> float:
     return a.elapsed_time(b) / iters
 
 
-VARIANTS = ("fp8", "sparse", "480p", "feeders", "w8a8", "sol")
+VARIANTS = ("fp8", "sparse", "480p", "feeders", "w8a8", "sol", "sol_hook")
 
 
 def w8a8_projection(peaks: dict, iters: int = 20) -> dict:
@@ -605,6 +605,8 @@ def _variants(peaks: dict, iters: int = 10, only: str | None = None) -> dict:
         return w8a8_projection(peaks, iters)
     if only == "sol":
         return _variant_sol(peaks, iters, dev, g)
+    if only == "sol_hook":
+        return {"sol_768p_hook_24h": _sol_hook(dev, g, iters)}
     for name, fn in (("fp8", _variant_fp8), ("sparse", _variant_sparse), ("480p", _variant_480p)):
         if only in (None, name):
             out.update(fn(peaks, iters, dev, g, pools))
@@ -833,7 +835,60 @@ def _variant_sol(peaks: dict, iters: int, dev: torch.device, g: torch.Generator)
                          "note": "whole call (summaries, statistics, routing, attention)"}}
         del kp, vp, k, v, q
         torch.cuda.empty_cache()
+    out["sol_768p_hook_24h"] = _sol_hook(dev, g, iters)
     return out
+
+
+def _sol_hook(dev: torch.device, g: torch.Generator, iters: int) -> dict:
+    """The drop-in path at 768p on one GPU (24 heads): a NOISY call of the hook at a routed
+    layer with the `sol_attn` backend (K/V gathered in the reference's part order, SOL over
+    the history video, condition rows dense) against the same call with the dense backend.
+    History: 4 committed blocks of 125 audio + 3971 video rows; the call: 64 text, 125 audio,
+    12384 video rows."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    heads, d, layer = 24, CFG["head_dim"], "blocks.2.attn"
+    block_tags = tuple([2] * 125 + [0] * 3971)
+    n_text, n_audio, n_video = 64, CFG["audio"], CFG["video"]
+    seq = n_text + n_audio + n_video
+    tags = torch.tensor([1] * n_text + [2] * n_audio + [0] * n_video, device=dev)
+    commit = tags != 1
+    q = torch.randn(seq, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    k = torch.randn(seq, heads, d, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(seq, heads, d, device=dev, generator=g).to(torch.bfloat16)
+
+    class Attn:
+        softmax_scale = d ** -0.5
+
+    res = {}
+    for backend in ("sol_attn", "sdpa"):
+        cache = CleanAVKVCache(KVContract(local_heads=heads, head_dim=d), layer_names=(layer,))
+        paged = cache.layer(layer, dev)
+        n_hist = 4 * len(block_tags)
+        centre = torch.randn((n_hist + 63) // 64, heads, d, device=dev, generator=g)
+        hk = (0.6 * torch.randn(n_hist, heads, d, device=dev, generator=g)
+              + centre.repeat_interleave(64, 0)[:n_hist]).to(torch.bfloat16)
+        hv = torch.randn(n_hist, heads, d, device=dev, generator=g).to(torch.bfloat16)
+        paged.write(hk, hv, start=0, count=n_hist)
+        paged.history_rows = n_hist
+        for _ in range(4):
+            cache._commit_token_counts.append(len(block_tags))
+            cache._commit_token_tags.append(block_tags)
+        hook = H3StreamingAttentionHook(cache, attention_backend=backend)
+        hook.activate(HookMode.NOISY)
+        call = lambda: hook(attention=Attn(), layer_name=layer, query=q, key=k, value=v,  # noqa: E731
+                            token_tags=tags, commit_mask=commit, cu_seqlens_host=(0, seq))
+        res[backend] = _time_launch(call, iters)
+        hook.deactivate()
+        hook.check_device_error()
+        del cache, paged, hk, hv
+        torch.cuda.empty_cache()
+    return {"sol_ms": res["sol_attn"], "dense_ms": res["sdpa"],
+            "speedup": res["sdpa"] / res["sol_attn"], "heads": heads, "queries": seq,
+            "history": 4 * len(block_tags), "tau": 1.0,
+            "note": "whole hook call: K/V gather, SOL (or dense) attention, condition rows"}
 
 
 def _variant_480p(peaks: dict, iters: int, dev: torch.device, g: torch.Generator, pools) -> dict:

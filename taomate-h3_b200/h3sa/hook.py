@@ -693,34 +693,42 @@ class H3StreamingAttentionHook:
             return []
         return [1] if fused else [0]
 
-    def _sol_history_rows(self, fused_current: bool) -> tuple[list[int], list[int]]:
-        """Logical history rows split into audio and video, block by block, over the blocks
-        the SOL call sees (F/streaming/cache.py:439-499)."""
+    def _sol_history_rows(self, fused_current: bool,
+                          device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+        """Logical history rows (int32 device tensors) split into audio and video, block by
+        block, over the blocks the SOL call sees (F/streaming/cache.py:439-499). Built once
+        per history state and policy, then shared by every layer's call."""
 
         cache = self.cache
         retained = cache.retained_blocks
-        if retained == 0:
-            return [], []
         recent_blocks = self.fused_current_recent_blocks
+        counts = tuple(cache.commit_token_counts)
         if fused_current and recent_blocks is not None:
             recent = max(0, recent_blocks - 1)
             if self.fused_current_use_sink:
-                blocks = (0, *range(max(1, retained - recent), retained))
+                blocks = (0, *range(max(1, retained - recent), retained)) if retained else ()
             else:
                 blocks = tuple(range(max(0, retained - recent), retained))
         else:
             blocks = tuple(range(retained))
-        offsets = cache._block_offsets()
         tags = cache.commit_token_tags()
-        audio: list[int] = []
-        video: list[int] = []
+        # a block's tag tuple is replaced whenever its rows change (retention, audio drop)
+        key = (cache.committed_blocks, counts, blocks, tuple(id(tags[b]) for b in blocks),
+               str(device))
+        hit = getattr(self, "_sol_history_cache", None)
+        if hit is not None and hit[0] == key:
+            return hit[2]
+        offsets = cache._block_offsets()
+        audio, video = [], []
         for b in blocks:
-            for r, tag in enumerate(tags[b]):
-                if tag == AUDIO_TOKEN_TAG:
-                    audio.append(offsets[b] + r)
-                elif tag == VIDEO_TOKEN_TAG:
-                    video.append(offsets[b] + r)
-        return audio, video
+            t = torch.tensor(tags[b], dtype=torch.int64)
+            audio.append(torch.nonzero(t == AUDIO_TOKEN_TAG).flatten() + offsets[b])
+            video.append(torch.nonzero(t == VIDEO_TOKEN_TAG).flatten() + offsets[b])
+        empty = torch.zeros(0, dtype=torch.int64)
+        split = tuple((torch.cat(x) if x else empty).to(torch.int32).pin_memory().to(
+            device, non_blocking=True) for x in (audio, video))
+        self._sol_history_cache = (key, [tags[b] for b in blocks], split)  # keeps the ids alive
+        return split
 
     def _sol_media(self, paged, plan: _DocumentPlan, d: int, region: tuple[int, int, int, int],
                    q_src: torch.Tensor, q_range: tuple[int, int], out: torch.Tensor,
@@ -740,35 +748,38 @@ class H3StreamingAttentionHook:
         n_media, n_cond = doc.media.n, doc.cond.n
         transient = self._transient(layer_name, d, fused)
         n_prefix = 0 if transient is None else int(transient.key.shape[0])
-        media_rows = list(range(first, first + n_media))
-        cond_rows = list(range(c_start, c_start + n_cond))
-        prefix_rows = list(range(c_start + n_cond, c_start + n_cond + n_prefix))
-        prev_rows: list[int] = []
-        if fused and d == 1 and plan.previous_media is not None:
-            at = c_start + n_cond + n_prefix
-            prev_rows = list(range(at, at + plan.previous_media.n))
-        audio_hist, video_hist = self._sol_history_rows(fused_current=fused and d == 1)
+        n_prev = plan.previous_media.n if (fused and d == 1 and plan.previous_media is not None) else 0
         device = q_src.device
+
+        def span(a: int, n: int) -> torch.Tensor:
+            return torch.arange(a, a + n, dtype=torch.int32, device=device)
+
+        media_rows = span(first, n_media)
+        cond_rows = span(c_start, n_cond)
+        prefix_rows = span(c_start + n_cond, n_prefix)
+        prev_rows = span(c_start + n_cond + n_prefix, n_prev)
+        audio_hist, video_hist = self._sol_history_rows(fused and d == 1, device)
         lo, hi = q_range
         route_video = self.sol_attn_route_current_video and not fused
         if route_video:
-            tags = token_tags.detach().to("cpu")[doc.media.host].tolist()
-            cur_audio = [media_rows[i] for i, t in enumerate(tags) if t == AUDIO_TOKEN_TAG]
-            cur_video = [media_rows[i] for i, t in enumerate(tags) if t == VIDEO_TOKEN_TAG]
-            exact = cond_rows + cur_audio + prefix_rows + audio_hist
-            routed = cur_video + video_hist
-            q_audio = [i for i, t in enumerate(tags) if t == AUDIO_TOKEN_TAG]
-            q_video = [i for i, t in enumerate(tags) if t == VIDEO_TOKEN_TAG]
+            tags = token_tags.detach().to("cpu")[doc.media.host]
+            q_audio = torch.nonzero(tags == AUDIO_TOKEN_TAG).flatten().tolist()
+            q_video = torch.nonzero(tags == VIDEO_TOKEN_TAG).flatten().tolist()
+            cur_audio = media_rows[torch.tensor(q_audio, dtype=torch.long, device=device)]
+            cur_video = media_rows[torch.tensor(q_video, dtype=torch.long, device=device)]
+            exact = (cond_rows, cur_audio, prefix_rows, audio_hist)
+            routed = (cur_video, video_hist)
         else:
-            exact = cond_rows + media_rows + prefix_rows + prev_rows + audio_hist
-            routed = video_hist
+            exact = (cond_rows, media_rows, prefix_rows, prev_rows, audio_hist)
+            routed = (video_hist,)
             q_audio, q_video = [], None
-        rows = exact + routed
-        index = torch.tensor(rows, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
+        n_exact = sum(int(t.numel()) for t in exact)
+        index = torch.cat(exact + routed)
+        n_rows = int(index.numel())
         heads = q_src.shape[1]
-        k = torch.empty(len(rows), heads, q_src.shape[2], dtype=q_src.dtype, device=device)
+        k = torch.empty(n_rows, heads, q_src.shape[2], dtype=q_src.dtype, device=device)
         v = torch.empty_like(k)
-        kv_copy_rows([paged.key, paged.value], [k, v], count=len(rows), src_table=paged.table,
+        kv_copy_rows([paged.key, paged.value], [k, v], count=n_rows, src_table=paged.table,
                      src_index=index, device_error=err)
         if self._sol_attn_density_counts is None or self._sol_attn_density_counts.device != device:
             self._sol_attn_density_counts = torch.zeros(4, dtype=torch.int64, device=device)
@@ -781,11 +792,10 @@ class H3StreamingAttentionHook:
             return qs, idx
 
         if q_video is None:
-            o = sol_attn_rectangular(q_src[lo:hi], k, v, scale=scale, tau=self.sol_attn_tau,
-                                     sink_tokens=len(exact),
-                                     telemetry_counts=self._sol_attn_density_counts,
-                                     device_error=err)
-            out[lo:hi].copy_(o)
+            sol_attn_rectangular(q_src[lo:hi], k, v, scale=scale, tau=self.sol_attn_tau,
+                                 sink_tokens=n_exact,
+                                 telemetry_counts=self._sol_attn_density_counts,
+                                 out=out[lo:hi], device_error=err)
             n_sol = hi - lo
         else:
             if q_audio:
@@ -801,14 +811,14 @@ class H3StreamingAttentionHook:
             if q_video:
                 qv, iv = subset(q_video)
                 ov = sol_attn_rectangular(qv, k, v, scale=scale, tau=self.sol_attn_tau,
-                                          sink_tokens=len(exact),
+                                          sink_tokens=n_exact,
                                           telemetry_counts=self._sol_attn_density_counts,
                                           device_error=err)
                 kv_copy_rows([ov], [out], count=n_sol, dst_index=iv)
         if n_sol:
             self.sol_attn_kernel_calls += 1
             self.sol_attn_query_tokens += n_sol
-            self.sol_attn_key_tokens += len(rows)
+            self.sol_attn_key_tokens += n_rows
             self.launches += 1
 
     def _capture(self, layer_name: str, key: torch.Tensor, value: torch.Tensor,

@@ -55,6 +55,7 @@ def sol_attn_rectangular(query: torch.Tensor, key: torch.Tensor, value: torch.Te
                          telemetry_counts: torch.Tensor | None = None,
                          return_receipt: bool = False,
                          exact_blocks: torch.Tensor | None = None,
+                         out: torch.Tensor | None = None,
                          device_error: torch.Tensor | None = None,
                          stream: torch.cuda.Stream | None = None):
     """SOL-Attn of ``query`` [Nq, H, 128] over ``key`` / ``value`` [Nk, H, 128] (bf16, CUDA):
@@ -62,9 +63,10 @@ def sol_attn_rectangular(query: torch.Tensor, key: torch.Tensor, value: torch.Te
     (F/inference/sol_attention.py:366-598). ``telemetry_counts``: int64 CUDA [4] to which the
     routed, exact, routable and candidate block counts are added. ``exact_blocks``: optional
     int32 CUDA [H, ceil(Nq / 64), ceil(ceil(Nk / 64) / 32)] that receives the exact-block
-    bitmask. Returns the bf16 output (and the receipt with ``return_receipt``)."""
+    bitmask. ``out``: optional contiguous bf16 CUDA tensor shaped like ``query`` that receives
+    the result. Returns the bf16 output (and the receipt with ``return_receipt``)."""
 
-    _require_cuda(telemetry_counts, exact_blocks, device_error)
+    _require_cuda(telemetry_counts, exact_blocks, out, device_error)
     for name, t in (("query", query), ("key", key), ("value", value)):
         if not t.is_cuda:
             raise RuntimeError("h3sa kernels require CUDA tensors")
@@ -93,7 +95,10 @@ def sol_attn_rectangular(query: torch.Tensor, key: torch.Tensor, value: torch.Te
     centroids = torch.empty(kb, heads, HEAD_DIM, dtype=torch.bfloat16, device=query.device)
     value_sums = torch.empty_like(centroids)
     stats = torch.empty(heads, 2, HEAD_DIM, dtype=torch.float32, device=query.device)
-    out = torch.empty_like(q)
+    if out is None:
+        out = torch.empty_like(q)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != tuple(query.shape):
+        raise RuntimeError("sol_attn_rectangular: out must be bf16 shaped like the query")
     call("h3sa_sol_attention", ptr(q), nq, ptr(k), ptr(v), nk, heads, HEAD_DIM, float(scale),
          float(tau), int(sink_tokens), ptr(centroids), ptr(value_sums), ptr(stats),
          ptr(exact_blocks), ptr(telemetry_counts), ptr(out), ptr(device_error),
