@@ -856,6 +856,36 @@ class CleanAVKVCache:
                     ordinal += 1
         return rows
 
+    def history_for_attention_rows(self, *, fused_current: bool, recent_full_blocks: int,
+                                   older_video_stride: int, use_sink: bool = False,
+                                   recent_blocks: int | None = None) -> list[int] | None:
+        """Logical rows of ``history_for_attention`` (None: no history)."""
+
+        retained = self.retained_blocks
+        if fused_current and recent_blocks is not None:
+            retained_recent = max(0, recent_blocks - 1)
+            count = min(retained, (1 if use_sink and retained else 0) + retained_recent)
+            recent_full_blocks = max(0, recent_full_blocks - 1)
+        else:
+            count = retained
+        return self.attention_history_rows(count=count, recent_full_blocks=recent_full_blocks,
+                                           older_video_stride=older_video_stride,
+                                           preserve_sink=use_sink)
+
+    def history_for_attention(self, layer_name: str, *, fused_current: bool,
+                              recent_full_blocks: int, older_video_stride: int,
+                              use_sink: bool = False,
+                              recent_blocks: int | None = None) -> AVKV | None:
+        """History for dense-recent / sparse-older attention: every block, or in a fused
+        forward's current document the sink and recent window, with the older blocks' video
+        rows strided (F/streaming/cache.py:409-437)."""
+
+        _validate_layer_name(layer_name, self.layer_names)
+        rows = self.history_for_attention_rows(
+            fused_current=fused_current, recent_full_blocks=recent_full_blocks,
+            older_video_stride=older_video_stride, use_sink=use_sink, recent_blocks=recent_blocks)
+        return None if not rows else self._rows_view(layer_name, rows)
+
     def attention_history(self, layer_name: str, *, count: int, recent_full_blocks: int,
                           older_video_stride: int, preserve_sink: bool = False) -> AVKV | None:
         """Dense recent blocks and structured-sparse older video rows (every audio row and

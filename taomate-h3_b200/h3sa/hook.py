@@ -196,7 +196,11 @@ class H3StreamingAttentionHook:
                  sol_attn_thresh_type: str = "diag", sol_attn_dense_layers: int = 2,
                  sol_attn_dense_denoise_steps: int = 1,
                  sol_attn_route_current_video: bool = False,
-                 sol_attn_static_summary_cache: bool = False) -> None:
+                 sol_attn_static_summary_cache: bool = False,
+                 history_kv_recent_full_blocks: int = 5, history_kv_older_video_stride: int = 1,
+                 current_video_kv_stride: int = 1,
+                 dense_current_document_when_empty: bool = False,
+                 direct_sage_kv_workspace: bool = False) -> None:
         # the FL2AV constructor's names for the same two knobs (F/streaming/attention_hook.py:377-394)
         if attention_backend is not None:
             backend = attention_backend
@@ -220,6 +224,25 @@ class H3StreamingAttentionHook:
         self._sol_attn_density_counts: torch.Tensor | None = None
         if not 0.0 < history_density <= 1.0:
             raise ValueError("dynamic history KV density must be in (0, 1]")
+        # the FL2AV history / current-video policies (F/streaming/attention_hook.py:382-441)
+        if current_video_kv_stride < 1:
+            raise ValueError("current video KV stride must be positive")
+        if history_kv_recent_full_blocks < 0 or history_kv_older_video_stride < 1:
+            raise ValueError("invalid H3 attention-history policy")
+        if direct_sage_kv_workspace:
+            raise ValueError("Direct dense K/V workspace requires SageAttention")
+        if dense_current_document_when_empty and current_video_kv_stride != 1:
+            raise ValueError(
+                "dense current-document compatibility requires current video KV stride 1")
+        if ((history_kv_older_video_stride > 1 or current_video_kv_stride > 1)
+                and backend not in DENSE_BACKENDS + SOL_BACKENDS):
+            raise ValueError(f"the {backend} backend reads the whole history and every current "
+                             "row; strided history or current video needs a dense or SOL backend")
+        self.history_kv_recent_full_blocks = int(history_kv_recent_full_blocks)
+        self.history_kv_older_video_stride = int(history_kv_older_video_stride)
+        self.current_video_kv_stride = int(current_video_kv_stride)
+        self.dense_current_document_when_empty = bool(dense_current_document_when_empty)
+        self.direct_sage_kv_workspace = False
         self.cache = cache
         self.backend = backend
         self.history_density = float(history_density)
@@ -557,6 +580,23 @@ class H3StreamingAttentionHook:
             paged.write(pair.key.contiguous(), pair.value.contiguous(), start=cursor, count=n)
             cursor += n
 
+        sparse_history = self.history_kv_older_video_stride > 1
+        video_stride = self.current_video_kv_stride
+        # doc -> (first row, rows, media positions) of its strided current media keys
+        selected_media: dict[int, tuple[int, int, torch.Tensor]] = {}
+
+        def copy_rows(rows: list[int]) -> None:
+            nonlocal cursor
+            if not rows:
+                return
+            index = torch.tensor(rows, dtype=torch.int32).pin_memory().to(
+                query.device, non_blocking=True)
+            paged.reserve(cursor + len(rows))
+            kv_copy_rows([paged.key, paged.value], [paged.key, paged.value], count=len(rows),
+                         src_table=paged.table, dst_table=paged.table, src_index=index,
+                         dst_start=cursor)
+            cursor += len(rows)
+
         for position, doc in enumerate(plan.docs):
             first = cursor
             put_rows(doc.media)
@@ -565,21 +605,51 @@ class H3StreamingAttentionHook:
             transient = self._transient(layer_name, position, fused)
             if transient is not None:
                 put_dense(transient)
+            # the persistent history this document's media see, appended as a row view when
+            # it is not the whole history in place: the fused current document's view, a
+            # strided older history, or any history once the current video is strided
+            view: list[int] | None = None
+            own_view = False
             if fused and position == 1:
                 assert plan.previous_media is not None
                 if plan.previous_media.n:
                     put_rows(plan.previous_media)
-                view = self.cache.history_for_fused_current_rows(
-                    use_sink=bool(self.fused_current_use_sink),
-                    recent_blocks=self.fused_current_recent_blocks)
-                if view:
-                    index = torch.tensor(view, dtype=torch.int32).pin_memory().to(
-                        query.device, non_blocking=True)
-                    paged.reserve(cursor + len(view))
-                    kv_copy_rows([paged.key, paged.value], [paged.key, paged.value],
-                                 count=len(view), src_table=paged.table, dst_table=paged.table,
-                                 src_index=index, dst_start=cursor)
-                    cursor += len(view)
+                policy = ({} if self.fused_current_recent_blocks is None else
+                          {"use_sink": bool(self.fused_current_use_sink),
+                           "recent_blocks": self.fused_current_recent_blocks})
+                if sparse_history:
+                    view = self.cache.history_for_attention_rows(
+                        fused_current=True, recent_full_blocks=self.history_kv_recent_full_blocks,
+                        older_video_stride=self.history_kv_older_video_stride, **policy)
+                else:
+                    view = self.cache.history_for_fused_current_rows(
+                        use_sink=bool(self.fused_current_use_sink),
+                        recent_blocks=self.fused_current_recent_blocks)
+                own_view = True
+            elif not capture and (sparse_history or video_stride > 1):
+                if sparse_history:
+                    view = self.cache.history_for_attention_rows(
+                        fused_current=False, recent_full_blocks=self.history_kv_recent_full_blocks,
+                        older_video_stride=self.history_kv_older_video_stride)
+                else:
+                    view = list(range(n_hist))
+                own_view = True
+            if view:
+                copy_rows(view)
+            if video_stride > 1:
+                # every committed audio row and every video_stride-th committed video row of
+                # the document (F/streaming/attention_hook.py:219-236)
+                tags_media = token_tags.detach().to("cpu")[doc.media.host]
+                video_pos = torch.nonzero(tags_media == VIDEO_TOKEN_TAG).flatten()
+                keep = torch.ones(doc.media.n, dtype=torch.bool)
+                keep[video_pos] = False
+                keep[video_pos[::video_stride]] = True
+                sel_first = cursor
+                kept = torch.nonzero(keep).flatten()
+                copy_rows((kept + first).tolist())
+                selected_media[position] = (sel_first, cursor - sel_first, kept)
+                kv_start = c_start  # skips the unstrided media rows
+            elif own_view:
                 kv_start = first
             else:
                 # the first document's media see the persistent history (none while capturing)
@@ -608,12 +678,22 @@ class H3StreamingAttentionHook:
                 q_ranges.append((at, at + r.n))
                 at += r.n
             q_src = gathered
+        # the first packed document with nothing before it: its condition rows see the whole
+        # document too (F/streaming/attention_hook.py:1308-1316)
+        whole_document = (self.dense_current_document_when_empty
+                          and self.mode is HookMode.NOISY and self.block_index == 0
+                          and n_hist == 0 and self._transient(layer_name, 0, fused) is None
+                          and not fused)
         problems = []
         for d, (kv_start, m_start, c_start, end) in enumerate(regions):
             mq, cq = q_ranges[2 * d], q_ranges[2 * d + 1]
             problems.append(AttentionProblem(mq[0], mq[1], kv_start, end,
                                              sparse=self.backend in SPARSE_BACKENDS))
-            problems.append(AttentionProblem(cq[0], cq[1], c_start, c_start + (cq[1] - cq[0])))
+            if whole_document:
+                problems.append(AttentionProblem(cq[0], cq[1], kv_start, end))
+            else:
+                problems.append(AttentionProblem(cq[0], cq[1], c_start,
+                                                 c_start + (cq[1] - cq[0])))
         out_main = out if gathered is None else torch.empty_like(gathered)
         # SOL-Attn backend: the media rows of the document(s) it routes go through
         # h3sa_sol_attention instead of the dense launch
@@ -634,7 +714,7 @@ class H3StreamingAttentionHook:
             self.sol_attn_dense_calls += len(dense_problems)
         for d in sol_docs:
             self._sol_media(paged, plan, d, regions[d], q_src, q_ranges[2 * d], out_main, scale,
-                            fused, token_tags, layer_name, err)
+                            fused, token_tags, layer_name, err, selected_media.get(d))
         if other_kv and self.backend in FP8_BACKENDS:
             # every other document is its own one-part e4m3 call in the reference's FP8 backends
             for a, b, c in other_kv:
@@ -733,7 +813,8 @@ class H3StreamingAttentionHook:
     def _sol_media(self, paged, plan: _DocumentPlan, d: int, region: tuple[int, int, int, int],
                    q_src: torch.Tensor, q_range: tuple[int, int], out: torch.Tensor,
                    scale: float, fused: bool, token_tags: torch.Tensor, layer_name: str,
-                   err: torch.Tensor) -> None:
+                   err: torch.Tensor,
+                   selected: tuple[int, int, torch.Tensor] | None = None) -> None:
         """One live document's media rows through SOL-Attn. The K/V sequence is gathered from
         the page sequence in the reference's part order: exact parts [condition, current
         media, temporary prefix, previous document's media, audio history] as the sink, then
@@ -754,7 +835,9 @@ class H3StreamingAttentionHook:
         def span(a: int, n: int) -> torch.Tensor:
             return torch.arange(a, a + n, dtype=torch.int32, device=device)
 
-        media_rows = span(first, n_media)
+        # the current media keys: every media row, or the strided copy with
+        # current_video_kv_stride > 1 (the reference's current_media_key)
+        media_rows = span(first, n_media) if selected is None else span(selected[0], selected[1])
         cond_rows = span(c_start, n_cond)
         prefix_rows = span(c_start + n_cond, n_prefix)
         prev_rows = span(c_start + n_cond + n_prefix, n_prev)
@@ -765,8 +848,10 @@ class H3StreamingAttentionHook:
             tags = token_tags.detach().to("cpu")[doc.media.host]
             q_audio = torch.nonzero(tags == AUDIO_TOKEN_TAG).flatten().tolist()
             q_video = torch.nonzero(tags == VIDEO_TOKEN_TAG).flatten().tolist()
-            cur_audio = media_rows[torch.tensor(q_audio, dtype=torch.long, device=device)]
-            cur_video = media_rows[torch.tensor(q_video, dtype=torch.long, device=device)]
+            key_tags = tags if selected is None else tags[selected[2]]
+            k_audio = torch.nonzero(key_tags == AUDIO_TOKEN_TAG).flatten().to(device)
+            k_video = torch.nonzero(key_tags == VIDEO_TOKEN_TAG).flatten().to(device)
+            cur_audio, cur_video = media_rows[k_audio], media_rows[k_video]
             exact = (cond_rows, cur_audio, prefix_rows, audio_hist)
             routed = (cur_video, video_hist)
         else:

@@ -78,6 +78,19 @@ HOOK_F_SCHEDULE = (
 )
 
 
+# FL2AV hook history / current-video policies and their schedule
+HOOK_F_POLICY = {"history_kv_older_video_stride": 3, "history_kv_recent_full_blocks": 1,
+                 "current_video_kv_stride": 2}
+HOOK_F_POLICY_SCHEDULE = (
+    ("clean_commit", 1, {}),
+    ("clean_commit", 1, {}),
+    ("clean_commit", 1, {}),
+    ("noisy", 1, {"denoise_step_index": 1}),
+    ("fused", 2, {"fused_current_use_sink": True, "fused_current_recent_blocks": 2}),
+    ("noisy", 1, {}),
+)
+
+
 def hook_f_inputs(step: int, live: int, heads: int = 2, head_dim: int = 128) -> dict:
     """One packed call of the FL2AV hook schedule: ``live`` documents of [8 text | 4 + 4
     audio | 48 video] rows each, then an 8-row pad document; q/k RMS-normalised, bf16."""

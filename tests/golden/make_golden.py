@@ -34,6 +34,9 @@ them from the seeds recorded in each fixture. Fixtures:
                  noisy call; layer 0's outputs, the captured prefix and the commit ledger. The
                  hook insists on CUDA tensors: CPU tensors of a subclass that reports is_cuda
                  stand in, and the K/V pair validators are stubbed.
+* hook_f_policy.npz the FL2AV hook (sdpa backend) with strided older history, strided
+                 current video keys and, separately, dense_current_document_when_empty:
+                 layer 0's outputs and the commit counts of every step.
 * hook_topk.npz  the FL2AV hook with its flash_attn3_fp8_segmented_topk backend at density
                  0.5 over four clean commits, then a noisy call (layer 0 outputs of every
                  step): FlashAttention-3's FP8 call is replaced by exact attention on the
@@ -422,6 +425,67 @@ def make_hook_f(path: Path) -> None:
         arrays[f"blocks_{step}"] = np.array(cache.committed_blocks)
     np.savez_compressed(path, **arrays)
 
+def make_hook_f_policy(path: Path) -> None:
+    """The FL2AV hook's history and current-video policies: strided older history
+    (history_kv_older_video_stride, history_kv_recent_full_blocks), strided current video
+    keys (current_video_kv_stride) through commits, noisy and fused calls; and the
+    dense_current_document_when_empty rule on a first call with no history."""
+
+    import torch
+    import digitalhuman_h3.streaming.attention_hook as fhook
+    import digitalhuman_h3.streaming.cache as fcache
+    from inputs import HOOK_F_POLICY, HOOK_F_POLICY_SCHEDULE, hook_f_inputs
+
+    fcache._validate_av_pair = lambda pair, contract, *, layer: None
+    fcache._validate_video_pair = lambda pair, contract, *, layer: None
+
+    class CudaFlagged(torch.Tensor):
+        @property
+        def is_cuda(self):
+            return True
+
+    def t(x: np.ndarray, dtype=torch.bfloat16):
+        return torch.from_numpy(x).to(dtype).as_subclass(CudaFlagged)
+
+    class Attn:
+        softmax_scale = 128 ** -0.5
+
+    modes = {"clean_commit": fhook.HookMode.CLEAN_COMMIT, "noisy": fhook.HookMode.NOISY,
+             "fused": fhook.HookMode.FUSED_PROGRESS_DENOISE}
+    contract = fcache.KVContract(local_heads=2, head_dim=128)
+    arrays: dict[str, np.ndarray] = {}
+
+    def run(hook, cache, step, name, live, extra, key):
+        x = hook_f_inputs(100 + step, live)
+        mode = modes[name]
+        commit = mode is not fhook.HookMode.NOISY
+        if commit:
+            cache.begin_clean_commit(cache.committed_blocks)
+        hook.activate(mode=mode, block_index=cache.committed_blocks, full_prefix=None, **extra)
+        q, k, v = t(x["q"]), t(x["k"]), t(x["v"])
+        tags, mask = t(x["token_tags"], torch.int64), t(x["commit_mask"], torch.bool)
+        for layer in contract.layer_names:
+            out = hook(attention=Attn(), layer_name=layer, query=q, key=k, value=v,
+                       token_tags=tags, commit_mask=mask, cu_seqlens=None,
+                       cu_seqlens_host=tuple(x["cu_seqlens"]), max_seqlen=64)
+            if layer == contract.layer_names[0]:
+                arrays[key] = torch.Tensor(out).float().numpy()
+        hook.deactivate()
+        if commit:
+            cache.commit()
+
+    cache = fcache.CleanAVKVCache(contract)
+    hook = fhook.H3StreamingAttentionHook(cache, attention_backend="sdpa", **HOOK_F_POLICY)
+    for step, (name, live, extra) in enumerate(HOOK_F_POLICY_SCHEDULE):
+        run(hook, cache, step, name, live, extra, f"out_{step}")
+        arrays[f"counts_{step}"] = np.array(cache.commit_token_counts, dtype=np.int64)
+    cache = fcache.CleanAVKVCache(contract)
+    hook = fhook.H3StreamingAttentionHook(cache, attention_backend="sdpa",
+                                          dense_current_document_when_empty=True)
+    run(hook, cache, 50, "noisy", 1, {}, "whole_out")
+    np.savez_compressed(path, **arrays)
+
+
 def make_hook_topk(path: Path) -> None:
     import torch
     import digitalhuman_h3.streaming.attention_hook as fhook
@@ -606,7 +670,8 @@ def main() -> None:
               "mask.npz": make_mask, "cache.npz": make_cache, "ulysses.npz": make_ulysses,
               "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f,
               "topk.npz": make_topk, "hook_f.npz": make_hook_f,
-              "hook_topk.npz": make_hook_topk, "w8a8.npz": make_w8a8, "sol.npz": make_sol}
+              "hook_topk.npz": make_hook_topk, "w8a8.npz": make_w8a8, "sol.npz": make_sol,
+              "hook_f_policy.npz": make_hook_f_policy}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

@@ -678,3 +678,65 @@ def test_hook_fp8_segmented_topk_matches_reference_hook_golden() -> None:
         assert rel_l2(first[:64], ref[:64]) <= FP8_TOL, step          # the live document
         assert rel_l2(first[64:], ref[64:]) <= FP8_TOL, step          # the pad document
         assert hook.dynamic_block_sparse_selected_blocks == int(g[f"selected_blocks_{step}"])
+
+
+def test_fl2av_hook_policies_match_reference_golden() -> None:
+    """The FL2AV hook's strided older history (history_kv_older_video_stride,
+    history_kv_recent_full_blocks) and strided current video keys (current_video_kv_stride)
+    through commits, noisy and fused calls, and dense_current_document_when_empty on a first
+    call with no history, replaying tests/golden/hook_f_policy.npz (the reference hook's own
+    outputs). A hook without the policies gives measurably different outputs."""
+
+    sys.path.insert(0, str(GOLDEN))
+    from inputs import HOOK_F_POLICY, HOOK_F_POLICY_SCHEDULE, hook_f_inputs
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    g = np.load(GOLDEN / "hook_f_policy.npz")
+    modes = {"clean_commit": HookMode.CLEAN_COMMIT, "noisy": HookMode.NOISY,
+             "fused": HookMode.FUSED_PROGRESS_DENOISE}
+    t = lambda a, dt=torch.bfloat16: torch.from_numpy(a).to(dt).cuda()  # noqa: E731
+
+    def run(hook, cache, step, name, live, extra):
+        x = hook_f_inputs(100 + step, live)
+        mode = modes[name]
+        commit = mode is not HookMode.NOISY
+        if commit:
+            cache.begin_clean_commit(cache.committed_blocks)
+        hook.activate(mode=mode, block_index=cache.committed_blocks, full_prefix=None, **extra)
+        q, k, v = t(x["q"]), t(x["k"]), t(x["v"])
+        tags, mask = t(x["token_tags"], torch.int64), t(x["commit_mask"], torch.bool)
+        first = None
+        for layer in cache.layer_names:
+            out = hook(attention=Attn(), layer_name=layer, query=q, key=k, value=v,
+                       token_tags=tags, commit_mask=mask, cu_seqlens=None,
+                       cu_seqlens_host=tuple(x["cu_seqlens"]), max_seqlen=64)
+            if first is None:
+                first = out
+        hook.check_device_error()
+        hook.deactivate()
+        if commit:
+            cache.commit()
+        return first
+
+    caches = [CleanAVKVCache(KVContract(local_heads=2, head_dim=128)) for _ in range(2)]
+    hooks = [H3StreamingAttentionHook(caches[0], attention_backend="sdpa", **HOOK_F_POLICY),
+             H3StreamingAttentionHook(caches[1], attention_backend="sdpa")]
+    for step, (name, live, extra) in enumerate(HOOK_F_POLICY_SCHEDULE):
+        out = run(hooks[0], caches[0], step, name, live, extra)
+        plain = run(hooks[1], caches[1], step, name, live, extra)
+        want = torch.from_numpy(g[f"out_{step}"])
+        assert rel_l2(out, want) <= BF16_TOL, (step, name)
+        assert list(caches[0].commit_token_counts) == list(g[f"counts_{step}"]), step
+        if step > 0:  # with history or strided current keys the policies change the result
+            assert rel_l2(plain, want) > 2 * BF16_TOL, (step, name)
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128))
+    hook = H3StreamingAttentionHook(cache, attention_backend="sdpa",
+                                    dense_current_document_when_empty=True)
+    whole = run(hook, cache, 50, "noisy", 1, {})
+    assert rel_l2(whole, torch.from_numpy(g["whole_out"])) <= BF16_TOL
+    plain_hook = H3StreamingAttentionHook(CleanAVKVCache(KVContract(local_heads=2, head_dim=128)),
+                                          attention_backend="sdpa")
+    plain = run(plain_hook, plain_hook.cache, 50, "noisy", 1, {})
+    assert rel_l2(plain, torch.from_numpy(g["whole_out"])) > 2 * BF16_TOL
