@@ -312,6 +312,16 @@ class H3StreamingAttentionHook:
                 else "rectangular_exact_condition_current_prefix_audio_sparse_history_video"),
         }
 
+    def sage_attn_receipt(self) -> dict[str, object] | None:
+        """The SageAttention backend is not built here (an sm90 library): always None."""
+
+        return None
+
+    def attention_backend_receipt(self) -> dict[str, object] | None:
+        """The alternative backend's receipt (F/streaming/attention_hook.py:574-575)."""
+
+        return self.sol_attn_receipt() or self.sage_attn_receipt()
+
     def receipt(self) -> dict[str, object]:
         return {
             "backend": f"h3sa_sm100a_{self.backend}",

@@ -131,6 +131,7 @@ def test_hook_sol_routes_history_video() -> None:
     assert receipt["key_tokens"] == k.shape[0]
     assert [receipt[n] for n in ("route_selected_blocks", "exact_blocks", "routable_blocks",
                                  "candidate_blocks")] == tele.tolist()
+    assert hook.attention_backend_receipt() == receipt and hook.sage_attn_receipt() is None
     # a dense layer: the media rows see the same keys densely
     out0 = _noisy(hook, "blocks.0.attn", y)
     assert hook.sol_attn_kernel_calls == 1
