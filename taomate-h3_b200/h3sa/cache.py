@@ -19,6 +19,7 @@ kernel launch per layer (T/streaming/cache.py:246-284 selects the same rows).
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Sequence
 
 import torch
 
@@ -757,6 +758,65 @@ class CleanAVKVCache:
         views = (self._rows_view(layer_name, list(range(offsets[i], offsets[i + 1])))
                  for i in range(len(self._commit_token_counts)))
         return tuple(v for v in views if v is not None)
+
+    def sink_and_recent_history_blocks(self, layer_name: str,
+                                       recent_count: int) -> tuple[AVKV, ...]:
+        """Block 0 plus the newest ``recent_count`` other blocks, one copy per block
+        (F/streaming/cache.py:325-342)."""
+
+        if isinstance(recent_count, bool) or not isinstance(recent_count, int) or recent_count < 0:
+            raise ValueError("recent H3 history count must be non-negative")
+        blocks = self.history_blocks(layer_name)
+        if not blocks:
+            return ()
+        return (blocks[0], *blocks[max(1, len(blocks) - recent_count):])
+
+    def history_modality_parts_rows(self, block_indices: Sequence[int]
+                                    ) -> tuple[list[list[int]], list[list[int]]]:
+        """Logical rows of ``history_modality_parts``: per selected block its audio rows and
+        its video rows (blocks without rows of a kind contribute no part)."""
+
+        self._require_valid()
+        offsets = self._block_offsets()
+        audio: list[list[int]] = []
+        video: list[list[int]] = []
+        for b in block_indices:
+            start, tags = offsets[b], self._commit_token_tags[b]
+            for tag, parts in ((AUDIO_TOKEN_TAG, audio), (VIDEO_TOKEN_TAG, video)):
+                rows = [start + i for i, t in enumerate(tags) if t == tag]
+                if rows:
+                    parts.append(rows)
+        return audio, video
+
+    def history_modality_parts(self, layer_name: str, block_indices: Sequence[int]
+                               ) -> tuple[tuple[tuple[torch.Tensor, torch.Tensor], ...],
+                                          tuple[tuple[torch.Tensor, torch.Tensor], ...]]:
+        """The selected blocks' history as exact audio and routable video (key, value) parts
+        for SOL-Attn (F/streaming/cache.py:439-475)."""
+
+        _validate_layer_name(layer_name, self.layer_names)
+        audio, video = self.history_modality_parts_rows(block_indices)
+        views = lambda parts: tuple((v.key, v.value) for v in  # noqa: E731
+                                    (self._rows_view(layer_name, rows) for rows in parts))
+        return views(audio), views(video)
+
+    def sol_history_modality_parts(self, layer_name: str, *, fused_current: bool,
+                                   use_sink: bool = False, recent_blocks: int | None = None):
+        """``history_modality_parts`` over every retained block, or in a fused forward's
+        current document the sink and recent window (F/streaming/cache.py:477-499)."""
+
+        retained = self.retained_blocks
+        if retained == 0:
+            return (), ()
+        if fused_current and recent_blocks is not None:
+            recent = max(0, recent_blocks - 1)
+            if use_sink:
+                blocks = (0, *range(max(1, retained - recent), retained))
+            else:
+                blocks = tuple(range(max(0, retained - recent), retained))
+        else:
+            blocks = tuple(range(retained))
+        return self.history_modality_parts(layer_name, blocks)
 
     def recent_history(self, layer_name: str, count: int) -> AVKV | None:
         """The newest ``count`` blocks (F/streaming/cache.py:287-300)."""

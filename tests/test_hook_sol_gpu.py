@@ -132,6 +132,13 @@ def test_hook_sol_routes_history_video() -> None:
     assert [receipt[n] for n in ("route_selected_blocks", "exact_blocks", "routable_blocks",
                                  "candidate_blocks")] == tele.tolist()
     assert hook.attention_backend_receipt() == receipt and hook.sage_attn_receipt() is None
+    # the cache's SOL history split: per block its audio rows and its video rows
+    audio_parts, video_parts = hook.cache.sol_history_modality_parts("blocks.2.attn",
+                                                                     fused_current=False)
+    assert len(audio_parts) == 4 and len(video_parts) == 4
+    for (ak, av), (vk, vv), d in zip(audio_parts, video_parts, history):
+        assert torch.equal(ak.cpu(), d["k"][16:48]) and torch.equal(av.cpu(), d["v"][16:48])
+        assert torch.equal(vk.cpu(), d["k"][48:304]) and torch.equal(vv.cpu(), d["v"][48:304])
     # a dense layer: the media rows see the same keys densely
     out0 = _noisy(hook, "blocks.0.attn", y)
     assert hook.sol_attn_kernel_calls == 1

@@ -502,3 +502,21 @@ def test_snapshot_header_checks_run_before_device_work(tmp_path) -> None:
     with pytest.raises(ValueError, match="contract"):
         snapshot.load_cache(write("c.h3kv", header, data),
                             contract=KVContract(local_heads=4, head_dim=128))
+
+
+def test_sol_history_modality_rows() -> None:
+    """The SOL history split (F/streaming/cache.py:439-499) on the row bookkeeping alone: per
+    selected block its audio rows, then its video rows; a fused current document's sink +
+    recent window."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128), layer_names=("blocks.0.attn",))
+    for tags in ((2, 2, 0, 0, 0), (0, 0, 0), (2, 0, 2, 0)):
+        cache._commit_token_counts.append(len(tags))
+        cache._commit_token_tags.append(tags)
+    audio, video = cache.history_modality_parts_rows((0, 1, 2))
+    assert audio == [[0, 1], [8, 10]]
+    assert video == [[2, 3, 4], [5, 6, 7], [9, 11]]
+    audio, video = cache.history_modality_parts_rows((0, 2))
+    assert audio == [[0, 1], [8, 10]] and video == [[2, 3, 4], [9, 11]]
