@@ -142,6 +142,31 @@ def unpack_o_recv(recv: torch.Tensor, out: torch.Tensor, *, world: int, tokens: 
                      src, dst, rb)
 
 
+def qkv_send_layout(value: torch.Tensor, *, num_heads: int, head_dim: int,
+                    world_size: int) -> torch.Tensor:
+    """The FL2AV send layout (F/distributed/ulysses_layout.py:26-37): merged QKV
+    ``[T, 3 * H * d]`` -> ``[W, 3, T, ceil(H / W), d]`` with the missing heads of the last
+    shards zero."""
+
+    tokens = int(value.shape[0])
+    hl = -(-num_heads // world_size)
+    out = torch.empty(world_size, 3, tokens, hl, head_dim, dtype=value.dtype, device=value.device)
+    pack_qkv_send(value.contiguous(), out, world=world_size, num_heads=num_heads,
+                  head_dim=head_dim)
+    return out
+
+
+def attention_receive_layout(value: torch.Tensor, *, num_heads: int) -> torch.Tensor:
+    """The FL2AV receive layout (F/distributed/ulysses_layout.py:54-60): head shards
+    ``[W, T, Hl, d]`` -> ``[T, H, d]``, the zero padding dropped."""
+
+    world, tokens, local, dim = (int(x) for x in value.shape)
+    out = torch.empty(tokens, num_heads, dim, dtype=value.dtype, device=value.device)
+    unpack_o_recv(value.contiguous(), out, world=world, tokens=tokens, local_heads=local,
+                  head_dim=dim, num_heads=num_heads)
+    return out
+
+
 def _all_to_all_swap(value: torch.Tensor, *, world_size: int, group: object,
                      sequence_to_heads: bool, num_heads: int | None = None) -> torch.Tensor:
     """Swap sequence and head shards with one all-to-all (T/distributed/ulysses.py:10-55)."""
@@ -246,6 +271,8 @@ def merged_qkv_sequence_to_heads(value: torch.Tensor, *, num_heads: int, head_di
 
 __all__ = [
     "ParallelContext",
+    "attention_receive_layout",
+    "qkv_send_layout",
     "build_parallel_context",
     "heads_to_sequence",
     "merged_qkv_sequence_to_heads",

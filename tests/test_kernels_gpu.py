@@ -245,6 +245,16 @@ def test_ulysses_layouts_vs_oracle(heads: int, world: int) -> None:
         unpack_o_recv(recv, o, world=world, tokens=tokens, local_heads=hl, head_dim=d,
                       num_heads=heads)
         assert np.array_equal(o.float().cpu().numpy(), expect_o[r])
+    # the FL2AV-named allocating forms of the same two layouts
+    from h3sa.ulysses import attention_receive_layout, qkv_send_layout
+
+    send0 = qkv_send_layout(_cuda_bf16(mb[0]), num_heads=heads, head_dim=d, world_size=world)
+    padded = torch.zeros_like(sends[0])
+    pack_qkv_send(_cuda_bf16(mb[0]), padded, world=world, num_heads=heads, head_dim=d)
+    assert torch.equal(send0, padded)
+    recv = torch.stack([outs[s].view(world, tokens, hl, d)[0] for s in range(world)])
+    assert np.array_equal(attention_receive_layout(recv, num_heads=heads).float().cpu().numpy(),
+                          expect_o[0])
 
 
 def test_kv_copy_rows_index_and_bounds() -> None:
