@@ -520,3 +520,29 @@ def test_sol_history_modality_rows() -> None:
     assert video == [[2, 3, 4], [5, 6, 7], [9, 11]]
     audio, video = cache.history_modality_parts_rows((0, 2))
     assert audio == [[0, 1], [8, 10]] and video == [[2, 3, 4], [9, 11]]
+
+
+def test_sol_attention_argument_validation() -> None:
+    """h3sa_sol_attention refuses bad sizes, scales and pointers before touching the device."""
+
+    lib = _lib()
+    L = lib.LIB
+    A = 1 << 20  # a 16-byte aligned stand-in address, never dereferenced
+
+    def call(**over):
+        a = dict(q=A, nq=100, k=A, v=A, nk=1000, heads=2, hd=128, scale=0.088, tau=1.0, sink=64,
+                 kc=A, vs=A, stats=A, mask=A, tele=None, out=A)
+        a.update(over)
+        return L.h3sa_sol_attention(a["q"], a["nq"], a["k"], a["v"], a["nk"], a["heads"], a["hd"],
+                                    ctypes.c_float(a["scale"]), ctypes.c_float(a["tau"]), a["sink"],
+                                    a["kc"], a["vs"], a["stats"], a["mask"], a["tele"], a["out"],
+                                    None, None)
+
+    assert call(hd=64) == lib.H3SA_ERR_UNSUPPORTED and "head_dim 128" in lib.last_error()
+    assert call(nk=4096 * 64 + 1) == lib.H3SA_ERR_UNSUPPORTED and "exceed" in lib.last_error()
+    for bad in (dict(nq=0), dict(nk=0), dict(heads=0), dict(sink=-1)):
+        assert call(**bad) == lib.H3SA_ERR_INVALID, bad
+    assert call(scale=0.0) == lib.H3SA_ERR_INVALID and "scale" in lib.last_error()
+    assert call(tau=float("nan")) == lib.H3SA_ERR_INVALID
+    assert call(kc=None) == lib.H3SA_ERR_INVALID and "null" in lib.last_error()
+    assert call(out=A + 8) == lib.H3SA_ERR_INVALID and "aligned" in lib.last_error()
