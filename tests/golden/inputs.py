@@ -138,3 +138,27 @@ def sol_inputs(case: int, head_dim: int = 128) -> tuple[np.ndarray, np.ndarray, 
     q = rng.standard_normal((nq, heads, head_dim)).astype(np.float32)
     v = rng.standard_normal((nk, heads, head_dim)).astype(np.float32)
     return bf16(q), bf16(k), bf16(v)
+
+
+def sol_hook_document(rng: np.random.Generator, heads: int = 2, head_dim: int = 128) -> dict:
+    """One packed call for the hook's SOL backend: 16 text, 32 audio, 256 video rows and a
+    16-row pad document, keys clustered around a centre per 64 rows (bf16-exact float32)."""
+
+    centre = rng.standard_normal((5, heads, head_dim))
+    tags = np.full(320, -1, np.int64)
+    tags[:16] = 1
+    tags[16:48] = 2
+    tags[48:304] = 0
+    k = 0.7 * rng.standard_normal((320, heads, head_dim)) + np.repeat(centre, 64, axis=0)[:320]
+    return {"q": bf16(rng.standard_normal((320, heads, head_dim)).astype(np.float32)),
+            "k": bf16(k.astype(np.float32)),
+            "v": bf16(rng.standard_normal((320, heads, head_dim)).astype(np.float32)),
+            "token_tags": tags, "commit_mask": (tags == 0) | (tags == 2), "cu_seqlens": [0, 304, 320]}
+
+
+def sol_hook_inputs(seed: int = 5) -> tuple[list[dict], dict]:
+    """Three committed documents and the noisy call of the SOL hook fixture."""
+
+    rng = np.random.default_rng(seed)
+    docs = [sol_hook_document(rng) for _ in range(4)]
+    return docs[:3], docs[3]

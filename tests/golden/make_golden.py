@@ -37,6 +37,9 @@ them from the seeds recorded in each fixture. Fixtures:
 * hook_f_policy.npz the FL2AV hook (sdpa backend) with strided older history, strided
                  current video keys and, separately, dense_current_document_when_empty:
                  layer 0's outputs and the commit counts of every step.
+* hook_sol.npz   the FL2AV hook with its sol_attn backend (tests/golden/make_hook_sol.py):
+                 layer 0 and layer 2 outputs of a noisy call over three commits, default and
+                 route-current-video policies, the adapter in Triton's CPU interpreter.
 * hook_topk.npz  the FL2AV hook with its flash_attn3_fp8_segmented_topk backend at density
                  0.5 over four clean commits, then a noisy call (layer 0 outputs of every
                  step): FlashAttention-3's FP8 call is replaced by exact attention on the
@@ -578,6 +581,15 @@ def make_sol(path: Path) -> None:
     subprocess.run([sys.executable, "-c", code], check=True)
 
 
+def make_hook_sol(path: Path) -> None:
+    """The FL2AV hook's sol_attn backend (tests/golden/make_hook_sol.py, own process)."""
+
+    import subprocess
+
+    subprocess.run([sys.executable, str(HERE / "make_hook_sol.py"), str(path)], check=True,
+                   cwd=HERE)
+
+
 def _ulysses_worker(rank: int, world: int, port: int, out_dir: str) -> None:
     import datetime
 
@@ -671,7 +683,7 @@ def main() -> None:
               "ulysses_pad.npz": make_ulysses_pad, "cache_f.npz": make_cache_f,
               "topk.npz": make_topk, "hook_f.npz": make_hook_f,
               "hook_topk.npz": make_hook_topk, "w8a8.npz": make_w8a8, "sol.npz": make_sol,
-              "hook_f_policy.npz": make_hook_f_policy}
+              "hook_f_policy.npz": make_hook_f_policy, "hook_sol.npz": make_hook_sol}
     wanted = sys.argv[1:] or list(makers)  # optional: only the named fixtures
     for name, fn in makers.items():
         if name not in wanted:

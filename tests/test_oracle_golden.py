@@ -325,3 +325,50 @@ def test_sol_attention_matches_reference() -> None:
         got = bf16_from_bits(out.numpy().view(np.uint32) >> 16)  # truncated, as the interpreter
         ulps = ulp_distance_bf16(got, want)
         assert ulps.max() <= 1 and (ulps > 0).mean() < 1e-3, (c, ulps.max(), (ulps > 0).mean())
+
+
+@pytest.mark.parametrize("route_video", [False, True])
+def test_hook_sol_composition_matches_reference_hook(route_video: bool) -> None:
+    """The part order the hook's sol_attn backend uses (and its GPU tests check against):
+    the SOL oracle over [condition, current media (audio only when the current video is
+    routed), audio history] as the sink and [current video,] video history routed equals the
+    reference FL2AV hook's own sol_attn output (tests/golden/hook_sol.npz, adapter in Triton's
+    CPU interpreter with float32 buffers, its bf16 cast truncating): rel-L2 <= 5e-3, under
+    0.1 % of elements apart after truncation. Layer 0 (a dense layer) is dense attention over
+    the same keys, and the reference counted one SOL call per routed layer."""
+
+    from inputs import sol_hook_inputs
+
+    from oracle import sol_attention as osol
+
+    g = load("hook_sol.npz")
+    history, y = sol_hook_inputs()
+    T = torch.from_numpy
+    audio = [(T(d["k"][16:48]), T(d["v"][16:48])) for d in history]
+    video = [(T(d["k"][48:304]), T(d["v"][48:304])) for d in history]
+    yk, yv = T(y["k"]), T(y["v"])
+    if route_video:
+        exact = [(yk[:16], yv[:16]), (yk[16:48], yv[16:48]), *audio]
+        routed = [(yk[48:304], yv[48:304]), *video]
+        rows = slice(48, 304)
+    else:
+        exact = [(yk[:16], yv[:16]), (yk[16:304], yv[16:304]), *audio]
+        routed = video
+        rows = slice(16, 304)
+    k = torch.cat([p[0] for p in exact + routed])
+    v = torch.cat([p[1] for p in exact + routed])
+    out, _, margin, _ = osol.sol_attn_rectangular(T(y["q"][rows]), k, v, scale=128 ** -0.5,
+                                                  tau=0.5, sink_tokens=sum(p[0].shape[0] for p in exact),
+                                                  summary_dtype=torch.float32)
+    assert float(margin.abs().min()) > 1e-4
+    name = "route_video" if route_video else "default"
+    got = torch.from_numpy(bf16_from_bits(g[f"{name}_2"]))[rows]
+    assert float((got - out).norm() / out.norm()) <= 5e-3
+    trunc = torch.from_numpy(bf16_from_bits(out.numpy().view(np.uint32) >> 16))
+    assert float((got != trunc).float().mean()) < 1e-3
+    q = T(y["q"][16:304])
+    p = torch.softmax(torch.einsum("qhd,khd->hqk", q, k) * 128 ** -0.5, -1)
+    dense = torch.einsum("hqk,khd->qhd", p, v)
+    got0 = torch.from_numpy(bf16_from_bits(g[f"{name}_0"]))[16:304]
+    assert float((got0 - dense).norm() / dense.norm()) <= 1e-2
+    assert int(g[f"{name}_calls"][0]) == 48  # layers 2..49 routed, 0 and 1 dense
