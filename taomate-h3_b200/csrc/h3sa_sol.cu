@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(kSolThreads) sol_route_kernel(const SolParams 
 //   approximate chunk c (bit 15 set): centroids / value sums of key blocks [64c, 64c + 64),
 //     with one 64-bit mask per half of the rows (valid, not exact for that query block);
 //   exact key block b (bits 0-11): its 64 K/V rows, bits 12 / 13 = exact for rows 0-63 / 64-127.
-// Two CTAs share an SM (106 KB of shared memory and 256 TMEM columns each), so one CTA's
+// Two CTAs share an SM (107 KB of shared memory and 256 TMEM columns each), so one CTA's
 // softmax runs while the other's MMAs do. Warp roles: warp 0 lane 0 TMA (Q once, then per
 // item the K tile into a 2-stage ring freed when its S MMA completes, and the V tile into a
 // 2-stage ring freed when its P V MMA completes); warp 1 MMA issue (S = Q K^T, M = 128, N = 64, into one of two TMEM S buffers;
