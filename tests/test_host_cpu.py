@@ -546,3 +546,41 @@ def test_sol_attention_argument_validation() -> None:
     assert call(tau=float("nan")) == lib.H3SA_ERR_INVALID
     assert call(kc=None) == lib.H3SA_ERR_INVALID and "null" in lib.last_error()
     assert call(out=A + 8) == lib.H3SA_ERR_INVALID and "aligned" in lib.last_error()
+
+
+def test_hook_sol_dense_rules() -> None:
+    """Which calls the sol_attn backend routes (F/streaming/attention_hook.py:909-929): none in
+    the commit and capture modes, the first sol_attn_dense_layers layers or the first
+    sol_attn_dense_denoise_steps denoise steps; in a fused forward the current document only."""
+
+    from h3sa.cache import CleanAVKVCache, KVContract
+    from h3sa.hook import H3StreamingAttentionHook, HookMode
+
+    cache = CleanAVKVCache(KVContract(local_heads=2, head_dim=128), layer_names=("blocks.0.attn",))
+    hook = H3StreamingAttentionHook(cache, attention_backend="sol_attn", sol_attn_dense_layers=2,
+                                    sol_attn_dense_denoise_steps=1)
+    hook.activate(mode=HookMode.NOISY, block_index=0, full_prefix=None, denoise_step_index=1)
+    assert hook._sol_documents("blocks.2.attn", False) == [0]
+    assert hook._sol_documents("blocks.1.attn", False) == []
+    hook.deactivate()
+    hook.activate(mode=HookMode.NOISY, block_index=0, full_prefix=None, denoise_step_index=0)
+    assert hook._sol_documents("blocks.9.attn", False) == []
+    hook.deactivate()
+    hook.activate(mode=HookMode.CLEAN_COMMIT, block_index=0, full_prefix=None)
+    assert hook._sol_documents("blocks.9.attn", False) == []
+    hook.deactivate()
+    hook.activate(HookMode.NOISY)  # the T form: no denoise step index
+    assert hook._sol_documents("blocks.9.attn", False) == [0]
+    assert hook._sol_documents("blocks.9.attn", True) == [1]
+    hook.deactivate()
+    dense = H3StreamingAttentionHook(cache, attention_backend="sdpa")
+    dense.activate(HookMode.NOISY)
+    assert dense._sol_documents("blocks.9.attn", False) == [] and dense.sol_attn_receipt() is None
+    with pytest.raises(ValueError, match="stride"):
+        H3StreamingAttentionHook(cache, attention_backend="flash_attn3_fp8_dynamic",
+                                 current_video_kv_stride=2)
+    with pytest.raises(ValueError, match="SageAttention"):
+        H3StreamingAttentionHook(cache, direct_sage_kv_workspace=True)
+    with pytest.raises(ValueError, match="stride 1"):
+        H3StreamingAttentionHook(cache, dense_current_document_when_empty=True,
+                                 current_video_kv_stride=2)
