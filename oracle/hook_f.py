@@ -14,6 +14,11 @@ attention_hook.py) with its cache (F/streaming/cache.py), one layer, fp32 SDPA:
   (F/streaming/cache.py:368-407) and the previous document's media rows (video only on
   request, :239-251); the previous document's media rows are the commit (:1579-1590).
 
+The history / current-video policies of the FL2AV hook constructor are restated too:
+strided older history (``history_for_attention``, F/streaming/cache.py:409-437, 501-575),
+strided current video keys (F/streaming/attention_hook.py:219-236) and the whole first
+document (:1308-1336).
+
 The history is kept as dense per-block K/V with their token tags, the way the reference's
 cache ledger does (F/streaming/cache.py:199-262, 964-995).
 """
@@ -42,7 +47,7 @@ class FL2AVHookOracle:
         return (torch.cat([b[0] for b in blocks]), torch.cat([b[1] for b in blocks]))
 
     def history(self):
-        return self._cat(self.blocks)
+        return self._cat(self.blocks)  # (key, value) of every block, oldest first
 
     def fused_current_history(self, use_sink: bool, recent_blocks: int | None):
         if recent_blocks is None:
@@ -62,6 +67,52 @@ class FL2AVHookOracle:
         else:
             sink = self.blocks[0]
         return self._cat([sink] + self.blocks[start:])
+
+    def attention_history(self, count: int, recent_full_blocks: int, older_video_stride: int,
+                          preserve_sink: bool = False):
+        """Dense newest ``recent_full_blocks`` blocks and the older blocks' audio rows plus
+        every ``older_video_stride``-th video row, over the newest ``count`` blocks or block
+        0 plus the newest ``count - 1`` (F/streaming/cache.py:501-575)."""
+
+        n = len(self.blocks)
+        if n == 0 or count <= 0:
+            return None
+        if preserve_sink:
+            chosen = [0, *range(max(1, n - max(0, count - 1)), n)]
+        else:
+            chosen = list(range(max(0, n - count), n))
+        dense = older_video_stride == 1 or recent_full_blocks >= len(chosen)
+        dense_start = max(0, len(chosen) - recent_full_blocks)
+        parts = []
+        for position, b in enumerate(chosen):
+            k, v, tags = self.blocks[b]
+            if dense or position >= dense_start:
+                parts.append((k, v, tags))
+                continue
+            keep, ordinal = [], 0
+            for i, tag in enumerate(tags):
+                if tag == AUDIO:
+                    keep.append(i)
+                elif tag == VIDEO:
+                    if ordinal % older_video_stride == 0:
+                        keep.append(i)
+                    ordinal += 1
+            parts.append((k[keep], v[keep], [tags[i] for i in keep]))
+        return self._cat(parts)
+
+    def history_for_attention(self, fused_current: bool, recent_full_blocks: int,
+                              older_video_stride: int, use_sink: bool = False,
+                              recent_blocks: int | None = None):
+        """F/streaming/cache.py:409-437."""
+
+        retained = len(self.blocks)
+        if fused_current and recent_blocks is not None:
+            count = min(retained, (1 if use_sink and retained else 0) + max(0, recent_blocks - 1))
+            recent_full_blocks = max(0, recent_full_blocks - 1)
+        else:
+            count = retained
+        return self.attention_history(count, recent_full_blocks, older_video_stride,
+                                      preserve_sink=use_sink)
 
     def retain_sink_and_recent(self, recent_count: int, sink_video_only: bool = True) -> None:
         self.sink_video_only = bool(sink_video_only)
@@ -83,9 +134,16 @@ class FL2AVHookOracle:
     def call(self, mode: str, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
              tags: Sequence[int], cu: Sequence[int], *, prefix=None, previous_prefix=None,
              previous_video_only: bool = False, use_sink: bool | None = None,
-             recent_blocks: int | None = None, capture: tuple[int, int | None] | None = None):
+             recent_blocks: int | None = None, capture: tuple[int, int | None] | None = None,
+             older_video_stride: int = 1, recent_full_blocks: int = 5, video_stride: int = 1,
+             whole_first_document: bool = False):
         """Output rows of one layer call; commits (or returns the captured rows) as the mode
-        says. ``prefix`` / ``previous_prefix``: (key, value) pairs."""
+        says. ``prefix`` / ``previous_prefix``: (key, value) pairs. ``older_video_stride`` /
+        ``recent_full_blocks``: the strided-history policy; ``video_stride``: the current
+        media keys keep every audio row and every ``video_stride``-th video row
+        (F/streaming/attention_hook.py:219-236, 831-850, 1147-1200);
+        ``whole_first_document``: a noisy call with nothing before the document lets its
+        condition rows see the whole document (:1308-1336)."""
 
         tags_t = torch.as_tensor(list(tags))
         commit = (tags_t == VIDEO) | (tags_t == AUDIO)
@@ -109,19 +167,40 @@ class FL2AVHookOracle:
             else:
                 transient = prefix
             extra = []
+            sparse = older_video_stride > 1
             if fused and index == live[-1]:
                 pa, pb = bounds[live[0]]
                 prev = torch.arange(pa, pb)[commit[pa:pb]]
                 if previous_video_only:
                     prev = prev[tags_t[prev] == VIDEO]
-                persistent = self.fused_current_history(bool(use_sink), recent_blocks)
+                if sparse:
+                    policy = ({} if recent_blocks is None else
+                              {"use_sink": bool(use_sink), "recent_blocks": recent_blocks})
+                    persistent = self.history_for_attention(True, recent_full_blocks,
+                                                            older_video_stride, **policy)
+                else:
+                    persistent = self.fused_current_history(bool(use_sink), recent_blocks)
                 extra = [p for p in (transient, persistent) if p is not None]
                 extra.append((k[prev], v[prev]))
             else:
-                persistent = None if mode == "capture" else self.history()
+                if mode == "capture":
+                    persistent = None
+                elif sparse:
+                    persistent = self.history_for_attention(False, recent_full_blocks,
+                                                            older_video_stride)
+                else:
+                    persistent = self.history()
                 extra = [p for p in (transient, persistent) if p is not None]
-            out[cond] = sdpa_from_kv_parts(q[cond], [(k[cond], v[cond])], self.scale)
-            parts = [(k[cond], v[cond]), *extra, (k[media], v[media])]
+            current = media
+            if video_stride > 1:
+                video_rows = media[tags_t[media] == VIDEO]
+                keep = set(media[tags_t[media] != VIDEO].tolist()) | set(video_rows[::video_stride].tolist())
+                current = torch.tensor(sorted(keep), dtype=torch.long)
+            whole = (whole_first_document and mode == "noisy" and not self.blocks
+                     and transient is None and not fused)
+            cond_parts = [(k[cond], v[cond])] + ([(k[media], v[media])] if whole else [])
+            out[cond] = sdpa_from_kv_parts(q[cond], cond_parts, self.scale)
+            parts = [(k[cond], v[cond]), *extra, (k[current], v[current])]
             out[media] = sdpa_from_kv_parts(q[media], parts, self.scale)
         captured = None
         if mode == "capture":

@@ -372,3 +372,41 @@ def test_hook_sol_composition_matches_reference_hook(route_video: bool) -> None:
     got0 = torch.from_numpy(bf16_from_bits(g[f"{name}_0"]))[16:304]
     assert float((got0 - dense).norm() / dense.norm()) <= 1e-2
     assert int(g[f"{name}_calls"][0]) == 48  # layers 2..49 routed, 0 and 1 dense
+
+
+def test_fl2av_hook_policies_match_reference() -> None:
+    """The oracle's strided older history, strided current video keys and whole first
+    document against the reference hook's own outputs (tests/golden/hook_f_policy.npz, bf16
+    SDPA on CPU): relative L2 <= 1e-2 per step, identical commit ledgers; without the
+    policies the oracle's outputs differ measurably."""
+
+    from inputs import HOOK_F_POLICY, HOOK_F_POLICY_SCHEDULE, hook_f_inputs
+
+    from oracle.hook_f import FL2AVHookOracle
+
+    g = load("hook_f_policy.npz")
+    policy = {"older_video_stride": HOOK_F_POLICY["history_kv_older_video_stride"],
+              "recent_full_blocks": HOOK_F_POLICY["history_kv_recent_full_blocks"],
+              "video_stride": HOOK_F_POLICY["current_video_kv_stride"]}
+    oracles = (FL2AVHookOracle(128 ** -0.5), FL2AVHookOracle(128 ** -0.5))
+    for step, (name, live, extra) in enumerate(HOOK_F_POLICY_SCHEDULE):
+        x = hook_f_inputs(100 + step, live)
+        q, k, v = (torch.from_numpy(x[n]) for n in ("q", "k", "v"))
+        kw = {}
+        if name == "fused":
+            kw = {"use_sink": extra["fused_current_use_sink"],
+                  "recent_blocks": extra["fused_current_recent_blocks"]}
+        out, _ = oracles[0].call(name, q, k, v, x["token_tags"], x["cu_seqlens"], **kw, **policy)
+        plain, _ = oracles[1].call(name, q, k, v, x["token_tags"], x["cu_seqlens"], **kw)
+        ref = torch.from_numpy(g[f"out_{step}"])
+        assert float((out - ref).norm() / ref.norm()) <= 1e-2, (step, name)
+        assert float((plain - ref).norm() / ref.norm()) > 2e-2, (step, name)
+        assert [len(b[2]) for b in oracles[0].blocks] == list(g[f"counts_{step}"]), step
+    x = hook_f_inputs(150, 1)
+    q, k, v = (torch.from_numpy(x[n]) for n in ("q", "k", "v"))
+    ref = torch.from_numpy(g["whole_out"])
+    whole, _ = FL2AVHookOracle(128 ** -0.5).call("noisy", q, k, v, x["token_tags"], x["cu_seqlens"],
+                                                 whole_first_document=True)
+    plain, _ = FL2AVHookOracle(128 ** -0.5).call("noisy", q, k, v, x["token_tags"], x["cu_seqlens"])
+    assert float((whole - ref).norm() / ref.norm()) <= 1e-2
+    assert float((plain - ref).norm() / ref.norm()) > 2e-2
