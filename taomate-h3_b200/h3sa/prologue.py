@@ -52,6 +52,34 @@ def fused_qkv_qk_norm_rope_(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight:
     return qkv
 
 
+def fused_qk_norm_rope(value: torch.Tensor, weight: torch.Tensor, cos: torch.Tensor,
+                       sin: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm + rotate-half RoPE of one of Q or K, out of place (T/inference/fused_kernels.py:
+    775-802, used by the processor when the merged prologue is off, T/model/layers.py:390-398).
+
+    ``value`` ``[T, H, d]`` bf16 (any strides), ``cos`` / ``sin`` ``[T, rotary]`` per token
+    with duplicated halves, as the processor builds them from the cos/sin cache. Runs the
+    merged prologue kernel (same arithmetic and bf16 rounding points) on a ``[T, 3, H, d]``
+    staging copy whose Q plane is ``value``; returns a contiguous ``[T, H, d]`` bf16 tensor."""
+
+    if value.ndim != 3:
+        raise ValueError("SOL QKNorm/RoPE takes [tokens, heads, head_dim]")
+    tokens, heads, head_dim = (int(x) for x in value.shape)
+    rotary = int(cos.shape[-1])
+    if rotary > head_dim or rotary % 2:
+        raise ValueError("SOL QKNorm/RoPE requires an even rotary span within a head")
+    if tuple(cos.shape) != (tokens, rotary) or tuple(sin.shape) != (tokens, rotary):
+        raise ValueError("SOL QKNorm/RoPE needs one cos/sin row per token")
+    half = rotary // 2
+    merged = torch.zeros(tokens, 3, heads, head_dim, dtype=torch.bfloat16, device=value.device)
+    merged[:, 0].copy_(value)
+    cache = torch.cat((cos[:, :half], sin[:, :half]), dim=-1).to(torch.bfloat16).contiguous()
+    positions = torch.arange(tokens, device=value.device)
+    w = weight.to(torch.bfloat16).contiguous()
+    fused_qkv_qk_norm_rope_(merged.view(tokens, 3 * heads * head_dim), w, w, cache, positions, eps)
+    return merged[:, 0].contiguous()
+
+
 def qkv_norm_rope_pack(qkv: torch.Tensor, q_weight: torch.Tensor, k_weight: torch.Tensor,
                        cos_sin_cache: torch.Tensor, positions: torch.Tensor, eps: float, *,
                        world: int, send: torch.Tensor | None = None) -> torch.Tensor:
@@ -205,5 +233,5 @@ def qkv_norm_rope_scatter_fp8(qkv: torch.Tensor, q_weight: torch.Tensor, k_weigh
     return scales[0], scales[1], scales[2]
 
 
-__all__ = ["fused_qkv_qk_norm_rope_", "qkv_norm_rope_pack", "qkv_norm_rope_scatter_fp8",
+__all__ = ["fused_qk_norm_rope", "fused_qkv_qk_norm_rope_", "qkv_norm_rope_pack", "qkv_norm_rope_scatter_fp8",
            "qkv_norm_rope_scatter_paged"]

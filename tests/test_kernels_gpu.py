@@ -197,6 +197,30 @@ def test_prologue_bit_exact_vs_oracle_and_golden() -> None:
         assert np.all(diff <= np.abs(gold) * 2.0 ** -7 + 1e-30)
 
 
+def test_unmerged_qk_norm_rope_matches_oracle() -> None:
+    """fused_qk_norm_rope (one of Q or K, out of place, per-token cos/sin with duplicated
+    halves as the processor builds them) equals the oracle prologue's Q plane bit for bit,
+    on a strided view of a merged projection."""
+
+    from h3sa.prologue import fused_qk_norm_rope
+
+    seq, heads = 200, 4
+    inp, cs = _prologue_case(seq, heads, seed=17)
+    pos = np.random.default_rng(2).integers(0, cs.shape[0], seq)
+    half = cs.shape[1] // 2
+    sel = cs[pos]
+    cos = np.concatenate((sel[:, :half], sel[:, :half]), -1)
+    sin = np.concatenate((sel[:, half:], sel[:, half:]), -1)
+    merged = _cuda_bf16(inp["qkv"])
+    q_view = merged.view(seq, 3, heads, 128)[:, 0]  # a strided view, as qkv.split gives
+    out = fused_qk_norm_rope(q_view, _cuda_bf16(inp["q_weight"]), _cuda_bf16(cos), _cuda_bf16(sin),
+                             1e-5)
+    ref = opro.qkv_norm_rope(inp["qkv"], inp["q_weight"], inp["k_weight"], cs, pos, heads, 128,
+                             1e-5).reshape(seq, 3, heads, 128)
+    assert out.is_contiguous() and np.array_equal(out.float().cpu().numpy(), ref[:, 0])
+    assert torch.equal(merged, _cuda_bf16(inp["qkv"]))  # the input is not modified
+
+
 @pytest.mark.parametrize("world", [2, 4])
 def test_prologue_pack_matches_oracle_send_layout(world: int) -> None:
     from h3sa.prologue import qkv_norm_rope_pack
