@@ -280,8 +280,10 @@ class H3StreamingAttentionHook:
         self.last_output_exchanged = False
 
     def sol_attn_receipt(self) -> dict[str, object] | None:
-        """Counters of the SOL-Attn backend (F/streaming/attention_hook.py:496-552); the
-        routing counts come from the device telemetry of every SOL call."""
+        """Counters of the SOL-Attn backend, with the reference's keys
+        (F/streaming/attention_hook.py:496-552). The routing counts come from the device
+        telemetry of every SOL call (always collected here); the summaries are rebuilt on
+        every call, so the static summary cache counters stay zero."""
 
         if self.backend not in SOL_BACKENDS:
             return None
@@ -296,10 +298,16 @@ class H3StreamingAttentionHook:
             "dense_denoise_steps": self.sol_attn_dense_denoise_steps,
             "route_current_video": self.sol_attn_route_current_video,
             "static_summary_cache": self.sol_attn_static_summary_cache,
+            "density_telemetry_enabled": True,
             "kernel_calls": self.sol_attn_kernel_calls,
             "dense_calls": self.sol_attn_dense_calls,
             "query_tokens": self.sol_attn_query_tokens,
             "key_tokens": self.sol_attn_key_tokens,
+            "static_cache_hits": 0,
+            "static_cache_misses": 0,
+            "static_summary_reused_blocks": 0,
+            "static_summary_built_blocks": 0,
+            "dynamic_or_boundary_summary_blocks": 0,
             "route_selected_blocks": selected,
             "exact_blocks": exact,
             "routable_blocks": routable,
